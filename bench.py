@@ -1,0 +1,458 @@
+"""bench.py -- decode-path throughput on B200 (driver contract: one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
+
+Workloads (synthetic seeded inputs of the stated shapes):
+  decode2b  config 4: 2B-shape hybrid decoder, batch 1, greedy decode tokens/s (default)
+  mlp       config 1: SwiGLU MLP 2048 -> 6144 -> 2048, Q4_K, batch 1
+  attention config 2: GQA decode 16q/4kv, head_dim 256, fp16 KV, history --history (default 32768)
+  lmhead    config 3: vocabulary readout 151936 x 2048 Q6_K, batch 1, logits + argmax
+At N > 1 (torchrun, one process per GPU, NCCL) every rank runs the same
+workload on its own GPU (replicas: the decode of one sequence does not shard),
+the time is the max over ranks and `value` is the whole-job aggregate.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "ray-tracing-attention_b200"))
+sys.path.insert(0, str(ROOT))
+
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+L2_BYTES = 126 * 2 ** 20
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]), "source": "measured"}
+    return dict(PEAKS_FALLBACK, source="fallback")
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi sampling of SM clock and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------ distributed
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    import torch
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ------------------------------------------------------------- workloads
+class Workload:
+    """One step of the hot path over one batch of synthetic input."""
+    name = ""
+    metric = ""
+    unit = ""
+    dtype = ""
+    launches_per_step = 0
+    dominant = ""
+
+    def step(self, i: int): ...
+    def dominant_launch(self, i: int): ...
+    def dominant_bytes(self) -> float: ...
+    def units_per_step(self) -> float: ...
+    def e2e_step(self, i: int): ...
+    def e2e_bytes(self): ...
+    def config(self) -> dict: ...
+    def cpu_baseline(self, budget_s: float) -> dict: ...
+
+
+def _rotations(footprint: int) -> int:
+    return max(1, -(-2 * L2_BYTES // max(footprint, 1)))
+
+
+class MLPWorkload(Workload):
+    name, metric, unit, dtype, dominant = ("mlp", "SwiGLU MLP decode steps/s (Q4_K, 2048-6144-2048)", "steps/s",
+                                           "q4k-int8mma-f32acc", "gemv_kernel<Q4_K> gate+up (SwiGLU)")
+    D, F = 2048, 6144
+    launches_per_step = 2
+
+    def __init__(self, seed=20261110):
+        import torch
+        from rta_b200 import ops
+        self.ops, self.torch = ops, torch
+        per = 3 * self.F * self.D // 256 * 144
+        self.copies = _rotations(per)
+        self.w = [[ops.synthetic_blocks(12, self.F, self.D, seed + 3 * c + j) for j in range(2)] +
+                  [ops.synthetic_blocks(12, self.D, self.F, seed + 3 * c + 2)] for c in range(self.copies)]
+        self.x = ops.synthetic_normal(self.D, seed + 999)
+        self.act = torch.empty(1, self.F, device="cuda")
+        self.y = torch.empty(1, self.D, device="cuda")
+        self.hx = torch.empty(self.D, dtype=torch.float32).pin_memory()
+        self.hx.copy_(self.x.cpu())
+        self.hy = torch.empty(self.D, dtype=torch.float32).pin_memory()
+
+    def step(self, i):
+        w = self.w[i % self.copies]
+        self.ops.mlp_swiglu(12, w[0], w[1], w[2], self.D, self.F, self.x, y=self.y, act=self.act)
+
+    def dominant_launch(self, i):
+        w = self.w[i % self.copies]
+        self.ops.gemv(12, w[0], self.F, self.D, self.x, y=self.act)  # one 6144x2048 Q4_K GEMV
+
+    def dominant_bytes(self):
+        return self.F * self.D // 256 * 144 + self.D * 4 + self.F * 4
+
+    def units_per_step(self):
+        return 1.0
+
+    def e2e_step(self, i):
+        x = self.x
+        x.copy_(self.hx, non_blocking=True)
+        self.step(i)
+        self.hy.copy_(self.y.view(-1), non_blocking=True)
+
+    def e2e_bytes(self):
+        return self.D * 4, self.D * 4
+
+    def algorithmic_bytes_step(self):
+        return 3 * self.F * self.D // 256 * 144 + 2 * self.D * 4 + 2 * self.F * 4
+
+    def config(self):
+        return {"workload": "config1_swiglu_mlp_b1", "hidden": self.D, "intermediate": self.F, "format": "Q4_K",
+                "batch": 1, "l2": f"rotating {self.copies} weight copies (> L2 per pass)"}
+
+    def cpu_baseline(self, budget_s):
+        from oracle import oracle
+        rng = np.random.default_rng(0)
+        mats = [oracle.quantize(12, rng.normal(0, 0.02, n).astype(np.float32))
+                for n in (self.F * self.D, self.F * self.D, self.D * self.F)]
+        x = rng.normal(0, 1, (1, self.D)).astype(np.float32)
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < budget_s or n == 0:
+            oracle.mlp(12, *mats, self.D, self.F, x)
+            n += 1
+        dt = time.perf_counter() - t0
+        return {"value": n / dt, "unit": self.unit, "cores": oracle.threads(), "kind": "port",
+                "sample": f"{n} full config-1 MLP steps (C restatement of resident_math.comp op 2, OpenMP)"}
+
+
+class LMHeadWorkload(Workload):
+    name, metric, unit, dtype, dominant = ("lmhead", "vocabulary readout tokens/s (151936x2048 Q6_K, logits+argmax)",
+                                           "tokens/s", "q6k-int8mma-f32acc", "gemv_kernel<Q6_K> readout + argmax")
+    V, D = 151936, 2048
+    launches_per_step = 2
+
+    def __init__(self, seed=31):
+        import torch
+        from rta_b200 import ops
+        self.ops, self.torch = ops, torch
+        self.w = ops.synthetic_blocks(14, self.V, self.D, seed)
+        self.x = ops.synthetic_normal(self.D, seed + 1)
+        self.ws = torch.empty(4096, dtype=torch.uint8, device="cuda")
+        self.hx = torch.empty(self.D, dtype=torch.float32).pin_memory()
+        self.hx.copy_(self.x.cpu())
+        self.harg = torch.empty(1, dtype=torch.int32).pin_memory()
+
+    def step(self, i):
+        self.last = self.ops.readout(14, self.w, self.V, self.D, self.x, logits=True, workspace=self.ws)
+
+    dominant_launch = step
+
+    def dominant_bytes(self):
+        return self.V * self.D // 256 * 210 + self.D * 4 + self.V * 4
+
+    def units_per_step(self):
+        return 1.0
+
+    def e2e_step(self, i):
+        self.x.copy_(self.hx, non_blocking=True)
+        self.step(i)
+        self.harg.copy_(self.last[1], non_blocking=True)
+
+    def e2e_bytes(self):
+        return self.D * 4, 4
+
+    def algorithmic_bytes_step(self):
+        return self.dominant_bytes()
+
+    def config(self):
+        return {"workload": "config3_lmhead_b1", "vocab": self.V, "hidden": self.D, "format": "Q6_K", "batch": 1,
+                "l2": "weights 255 MB > L2"}
+
+    def cpu_baseline(self, budget_s):
+        from oracle import oracle
+        rng = np.random.default_rng(0)
+        W = oracle.quantize(14, rng.normal(0, 0.02, self.V * self.D).astype(np.float32))
+        x = rng.normal(0, 1, (1, self.D)).astype(np.float32)
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < budget_s or n == 0:
+            oracle.lmhead(14, W, self.V, self.D, x, want_logits=True)
+            n += 1
+        dt = time.perf_counter() - t0
+        return {"value": n / dt, "unit": self.unit, "cores": oracle.threads(), "kind": "port",
+                "sample": f"{n} full readouts (C restatement of resident_math.comp ops 16/17/23, OpenMP)"}
+
+
+class AttentionWorkload(Workload):
+    name, metric, unit, dtype, dominant = ("attention", "GQA decode attention steps/s (16q/4kv, d 256, fp16 KV)",
+                                           "steps/s", "f16-mma-f32acc", "attention_split_kernel")
+    launches_per_step = 2
+
+    def __init__(self, history=32768, seed=5):
+        import torch
+        from rta_b200 import ops
+        self.ops, self.torch = ops, torch
+        self.L = history
+        kv_bytes = 2 * self.L * 4 * 256 * 2
+        self.copies = _rotations(kv_bytes)
+        g = torch.Generator(device="cuda").manual_seed(seed)
+        self.k = [torch.randn(self.L, 4, 256, device="cuda", generator=g).half() for _ in range(self.copies)]
+        self.v = [torch.randn(self.L, 4, 256, device="cuda", generator=g).half() for _ in range(self.copies)]
+        self.q = torch.randn(16, 256, device="cuda", generator=g)
+        self.splits = ops._lib.load().rta_attention_default_splits(self.L, 4)
+        self.ws = ops.attention_workspace(16, 4, 256, self.splits)
+        self.hq = torch.empty(16 * 256, dtype=torch.float32).pin_memory()
+        self.hq.copy_(self.q.view(-1).cpu())
+        self.hout = torch.empty(16 * 256, dtype=torch.float32).pin_memory()
+
+    def step(self, i):
+        c = i % self.copies
+        self.last = self.ops.attention_decode_f16(self.q, self.k[c], self.v[c], self.L - 1, self.L, 4, 1,
+                                                  splits=self.splits, workspace=self.ws, phys=False)
+
+    dominant_launch = step
+
+    def dominant_bytes(self):
+        return 2 * self.L * 4 * 256 * 2 + 2 * 16 * 256 * 4
+
+    def units_per_step(self):
+        return 1.0
+
+    def e2e_step(self, i):
+        self.q.view(-1).copy_(self.hq, non_blocking=True)
+        self.step(i)
+        self.hout.copy_(self.last[0].view(-1), non_blocking=True)
+
+    def e2e_bytes(self):
+        return 16 * 256 * 4, 16 * 256 * 4
+
+    def algorithmic_bytes_step(self):
+        return self.dominant_bytes()
+
+    def config(self):
+        return {"workload": f"config2_gqa_decode_L{self.L}", "history": self.L, "q_heads": 16, "kv_heads": 4,
+                "head_dim": 256, "kv": "fp16", "splits": self.splits,
+                "l2": f"rotating {self.copies} KV copies (> L2 per pass)" if self.copies > 1 else "KV > L2"}
+
+    def cpu_baseline(self, budget_s):
+        from oracle import oracle
+        rng = np.random.default_rng(0)
+        L = min(self.L, 8192)
+        q = rng.normal(0, 1, (1, 16, 256)).astype(np.float32)
+        k = rng.normal(0, 1, (L, 4, 256)).astype(np.float16).astype(np.float32)
+        v = rng.normal(0, 1, (L, 4, 256)).astype(np.float16).astype(np.float32)
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < budget_s or n == 0:
+            oracle.attention(q, k, v, None, L - 1, 0, L, False)
+            n += 1
+        dt = time.perf_counter() - t0
+        return {"value": n / dt * (L / self.L), "unit": self.unit, "cores": oracle.threads(), "kind": "port",
+                "sample": f"{n} decode steps at L={L}, scaled to L={self.L} by history length "
+                          "(C restatement of the S_t/R_t detector, OpenMP over heads)"}
+
+
+WORKLOADS = {"mlp": MLPWorkload, "lmhead": LMHeadWorkload, "attention": AttentionWorkload}
+
+
+# ----------------------------------------------------------------- timing
+def time_steps(fn, steps, warmup, world):
+    import torch
+    for i in range(warmup):
+        fn(i)
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for i in range(steps):
+        fn(warmup + i)
+    stop.record()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(stop)
+    barrier(world)
+    return max_over_ranks(ms, world)
+
+
+def run_ours(args, world, rank, local):
+    import torch
+    wl = WORKLOADS[args.workload](**({"history": args.history} if args.workload == "attention" else {}))
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        ms = time_steps(wl.step, args.steps, args.warmup, world)
+    ms_step = ms / args.steps
+    value = wl.units_per_step() * world / (ms_step / 1e3)
+    # dominant kernel alone, CUDA events on the launching (current) stream
+    dom_ms = time_steps(wl.dominant_launch, args.steps, args.warmup, world) / args.steps
+    pk = peaks()
+    achieved = wl.dominant_bytes() / (dom_ms / 1e3) / 1e9
+    e2e_ms = time_steps(wl.e2e_step, args.steps, args.warmup, world) / args.steps
+    h2d, d2h = wl.e2e_bytes()
+    line = {
+        "metric": wl.metric, "value": value, "unit": wl.unit, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic (seeded, BASELINE shapes)",
+        "config": dict(wl.config(), parallelism=f"replicas x{world}" if world > 1 else "single GPU"),
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / pk["hbm_gbs"], "traffic": None, "kernel": wl.dominant,
+                     "algorithmic_bytes": wl.dominant_bytes(), "kernel_ms": dom_ms,
+                     "peak_source": f"{pk['source']} hbm_gbs (burst copy)"},
+        "e2e": {"value": wl.units_per_step() * world / (e2e_ms / 1e3), "unit": wl.unit,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "api": "rta_b200.ops -> librta_cuda.so C-ABI"},
+        "gpu_launches": wl.launches_per_step * args.steps,
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = wl.cpu_baseline(args.cpu_budget)
+    return line
+
+
+def run_reference(args, world, rank):
+    """Reference arm: the reference's CPU path for this workload (the oracle port of
+    its shader math; the Vulkan path cannot run here), rank 0 only."""
+    if rank != 0:
+        return None
+    cls = WORKLOADS[args.workload]
+    wl = cls.__new__(cls)
+    if args.workload == "attention":
+        wl.L = args.history
+    budget = max(1.0, args.cpu_budget / max(args.steps, 1))
+    vals = []
+    for _ in range(args.warmup + args.steps):
+        vals.append(wl.cpu_baseline(budget))
+    vals = vals[args.warmup:]
+    v = float(np.median([b["value"] for b in vals]))
+    base = dict(vals[-1], value=v)
+    cfg = {"mlp": {"workload": "config1_swiglu_mlp_b1"}, "lmhead": {"workload": "config3_lmhead_b1"},
+           "attention": {"workload": f"config2_gqa_decode_L{args.history}"}}[args.workload]
+    return {"impl": "reference", "metric": cls.metric, "value": v, "unit": cls.unit, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "dtype": "f32",
+            "data": "synthetic (seeded, BASELINE shapes)", "config": cfg,
+            "cpu_baseline": base, "e2e": {"value": v, "unit": cls.unit, "h2d_bytes_per_step": 0,
+                                          "d2h_bytes_per_step": 0},
+            "note": "reference Vulkan ray-query worker unavailable on this box (no graphics stack, no RT cores); "
+                    "timed its CPU path: the C restatement of its shader math"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="lmhead")
+    ap.add_argument("--history", type=int, default=32768)
+    ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        line = run_reference(args, world, rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+    world, rank, local = dist_setup(args.gpus)
+    line = run_ours(args, world, rank, local)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,37 @@
+// attention.h -- parameters of the split-K decode attention (attention.cu).
+#pragma once
+#include <cuda_fp16.h>
+#include <cstddef>
+#include <cstdint>
+
+namespace rta {
+
+struct AttnParams {
+  const float* q = nullptr;      // [nseq][heads][hd] fp32 (normed, rotated)
+  size_t q_seq_stride = 0;       // floats between sequences
+  const __half* k = nullptr;     // key cache base (fp16)
+  const __half* v = nullptr;     // value cache base (fp16)
+  size_t seq_stride = 0;         // halves between sequences' caches
+  size_t kv_stride = 0;          // halves between KV heads
+  size_t pos_stride = 0;         // halves between ring slots
+  uint32_t heads = 16, kvh = 4, hd = 256;
+  uint32_t capacity = 0;         // ring slots (position p lives in slot p % capacity)
+  uint32_t history_start = 0;    // oldest age present
+  uint32_t t = 0;                // current absolute time (used when pos == nullptr)
+  const uint32_t* pos = nullptr; // [nseq] device-side current times (graph replay)
+  const float* gate = nullptr;   // [nseq][heads][hd] or null
+  float* out = nullptr;          // [nseq][heads][hd]
+  size_t out_seq_stride = 0;
+  uint32_t rotary_out = 0;       // >0: write outputs in original (un-paired) axis order
+  float* phys = nullptr;         // [nseq][heads][2] = (m + 20, Z) or null
+  float* part_m = nullptr;       // split records [nseq][kvh][nsplit][4]
+  float* part_z = nullptr;
+  float* part_o = nullptr;       // [nseq][kvh][nsplit][4][hd]
+  uint32_t* err = nullptr;
+};
+
+size_t attention_smem_bytes();
+cudaError_t launch_attention(const AttnParams& p, uint32_t nsplit, uint32_t nseq, bool pdl, cudaStream_t s);
+uint32_t attention_default_splits(uint32_t history, uint32_t kvh, int sms);
+
+}  // namespace rta

@@ -1,0 +1,230 @@
+// capi.cu -- extern "C" boundary of librta_cuda.so (declared in include/rta.h).
+//
+// Operators validate their arguments, launch the sm_100a kernels and translate
+// CUDA failures into rta_status codes with a thread-local message; nothing
+// here aborts the process.  There is no host fallback: every operator runs
+// its CUDA kernel or returns an error.
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "../../include/rta.h"
+#include "attention.h"
+#include "rta_internal.h"
+
+namespace {
+thread_local std::string g_last_error = "no error";
+
+rta_status fail(rta_status code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+rta_status cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return RTA_OK;
+  return fail(RTA_E_CUDA, std::string(what) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")");
+}
+cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+bool quant_format(int f) { return f == RTA_Q4_K || f == RTA_Q6_K; }
+
+constexpr size_t kErrBytes = 256;  // device error word + padding at the head of every workspace
+
+__global__ void readout_finish_kernel(const unsigned long long* keys, uint32_t batch, uint32_t vocab,
+                                      uint32_t* argmax, float* best, uint32_t* err) {
+  const uint32_t b = threadIdx.x;
+  if (b >= batch) return;
+  const unsigned long long k = keys[b];
+  const uint32_t id = ~static_cast<uint32_t>(k & 0xffffffffull);
+  if (k == 0ull || id >= vocab) {
+    if (err) atomicOr(err, RTA_DEVERR_TOKEN);
+    argmax[b] = 0xffffffffu;
+    if (best) best[b] = -INFINITY;
+    return;
+  }
+  argmax[b] = id;
+  if (best) best[b] = rta::float_from_order_key(static_cast<uint32_t>(k >> 32));
+}
+}  // namespace
+
+extern "C" {
+
+const char* rta_last_error(void) { return g_last_error.c_str(); }
+const char* rta_version(void) { return "rta_cuda sm_100a"; }
+
+rta_status rta_quantize(int format, const float* src, size_t nblocks, void* dst, void* stream) {
+  if (!quant_format(format) || (nblocks && (!src || !dst))) return fail(RTA_E_ARG, "rta_quantize: bad arguments");
+  return cuda_status(rta::launch_quantize(format, src, nblocks, static_cast<uint8_t*>(dst), as_stream(stream)),
+                     "rta_quantize");
+}
+
+rta_status rta_synthetic_blocks(int format, uint64_t seed, float sigma, uint64_t first_block, size_t nblocks,
+                                void* dst, void* stream) {
+  if (!quant_format(format) || (nblocks && !dst)) return fail(RTA_E_ARG, "rta_synthetic_blocks: bad arguments");
+  return cuda_status(rta::launch_random_quantize(format, seed, sigma, first_block, nblocks,
+                                                 static_cast<uint8_t*>(dst), as_stream(stream)),
+                     "rta_synthetic_blocks");
+}
+
+rta_status rta_synthetic_normal(uint64_t seed, float sigma, float mean, size_t n, float* dst, void* stream) {
+  if (n && !dst) return fail(RTA_E_ARG, "rta_synthetic_normal: null destination");
+  return cuda_status(rta::launch_random_normal(seed, sigma, mean, n, dst, as_stream(stream)), "rta_synthetic_normal");
+}
+
+rta_status rta_dequantize(int format, const void* blocks, size_t nblocks, float* dst, void* stream) {
+  if (!quant_format(format) || (nblocks && (!blocks || !dst))) return fail(RTA_E_ARG, "rta_dequantize: bad arguments");
+  return cuda_status(rta::launch_dequantize(format, static_cast<const uint8_t*>(blocks), nblocks, dst,
+                                            as_stream(stream)),
+                     "rta_dequantize");
+}
+
+rta_status rta_gemv(int format, const void* w, uint32_t rows, uint32_t cols, const float* x, uint32_t batch,
+                    float* y, int accumulate, void* stream) {
+  if (!quant_format(format) || !w || !x || !y || rows == 0 || rows % 16 || cols == 0 || cols % 256 || batch == 0 ||
+      batch > rta::kMaxBatch)
+    return fail(RTA_E_ARG, "rta_gemv: format must be Q4_K/Q6_K, rows % 16 == 0, cols % 256 == 0, 1 <= batch <= 32");
+  rta::GemvArgs a;
+  a.fmt = format;
+  a.w0 = static_cast<const uint8_t*>(w);
+  a.rows = rows;
+  a.cols = cols;
+  a.x = x;
+  a.x_stride = cols;
+  a.batch = batch;
+  a.epilogue = accumulate ? rta::kAccumulate : rta::kStore;
+  a.y = y;
+  a.y_stride = rows;
+  return cuda_status(rta::launch_gemv(a, as_stream(stream)), "rta_gemv");
+}
+
+rta_status rta_mlp_swiglu(int format, const void* wg, const void* wu, const void* wd, uint32_t hidden,
+                          uint32_t middle, const float* x, uint32_t batch, float* act, float* y, int accumulate,
+                          void* stream) {
+  if (!quant_format(format) || !wg || !wu || !wd || !x || !act || !y || hidden % 256 || middle % 256 || !hidden ||
+      !middle || batch == 0 || batch > rta::kMaxBatch)
+    return fail(RTA_E_ARG, "rta_mlp_swiglu: bad arguments (hidden, middle multiples of 256; 1 <= batch <= 32)");
+  rta::GemvArgs g;
+  g.fmt = format;
+  g.w0 = static_cast<const uint8_t*>(wg);
+  g.w1 = static_cast<const uint8_t*>(wu);
+  g.rows = middle;
+  g.cols = hidden;
+  g.x = x;
+  g.x_stride = hidden;
+  g.batch = batch;
+  g.epilogue = rta::kSwiGLU;
+  g.y = act;
+  g.y_stride = middle;
+  rta_status st = cuda_status(rta::launch_gemv(g, as_stream(stream)), "rta_mlp_swiglu(gate/up)");
+  if (st != RTA_OK) return st;
+  rta::GemvArgs d;
+  d.fmt = format;
+  d.w0 = static_cast<const uint8_t*>(wd);
+  d.rows = hidden;
+  d.cols = middle;
+  d.x = act;
+  d.x_stride = middle;
+  d.batch = batch;
+  d.epilogue = accumulate ? rta::kAccumulate : rta::kStore;
+  d.y = y;
+  d.y_stride = hidden;
+  d.pdl = true;
+  return cuda_status(rta::launch_gemv(d, as_stream(stream)), "rta_mlp_swiglu(down)");
+}
+
+size_t rta_readout_workspace_bytes(uint32_t batch) { return kErrBytes + 8ull * (batch ? batch : 1); }
+
+rta_status rta_readout(int format, const void* w, uint32_t vocab, uint32_t hidden, const float* x, uint32_t batch,
+                       float* logits, uint32_t* argmax, float* best, void* workspace, void* stream) {
+  if (!quant_format(format) || !w || !x || !argmax || !workspace || vocab == 0 || vocab % 16 || hidden % 256 ||
+      hidden == 0 || batch == 0 || batch > 8)
+    return fail(RTA_E_ARG, "rta_readout: bad arguments (vocab % 16 == 0, hidden % 256 == 0, 1 <= batch <= 8)");
+  cudaStream_t s = as_stream(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  uint32_t* err = reinterpret_cast<uint32_t*>(ws);
+  auto* keys = reinterpret_cast<unsigned long long*>(ws + kErrBytes);
+  rta_status st = cuda_status(cudaMemsetAsync(ws, 0, rta_readout_workspace_bytes(batch), s), "rta_readout(memset)");
+  if (st != RTA_OK) return st;
+  rta::GemvArgs a;
+  a.fmt = format;
+  a.w0 = static_cast<const uint8_t*>(w);
+  a.rows = vocab;
+  a.cols = hidden;
+  a.x = x;
+  a.x_stride = hidden;
+  a.batch = batch;
+  a.epilogue = rta::kStore;
+  a.y = logits;
+  a.y_stride = vocab;
+  a.argmax = keys;
+  a.err = err;
+  st = cuda_status(rta::launch_gemv(a, s), "rta_readout");
+  if (st != RTA_OK) return st;
+  readout_finish_kernel<<<1, 32, 0, s>>>(keys, batch, vocab, argmax, best, err);
+  return cuda_status(cudaGetLastError(), "rta_readout(finish)");
+}
+
+size_t rta_attention_workspace_bytes(uint32_t heads, uint32_t kv_heads, uint32_t head_dim, uint32_t splits) {
+  (void)kv_heads;
+  const size_t recs = static_cast<size_t>(heads) * (splits ? splits : 1);
+  return kErrBytes + recs * 4 * 2 + recs * head_dim * 4 + 64;
+}
+
+uint32_t rta_attention_default_splits(uint32_t history, uint32_t kv_heads) {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return rta::attention_default_splits(history, kv_heads, sms);
+}
+
+rta_status rta_attention_decode_f16(const float* q, const void* k, const void* v, uint32_t time, uint32_t capacity,
+                                    uint32_t heads, uint32_t kv_heads, uint32_t head_dim, uint32_t pos_stride,
+                                    uint32_t kv_stride, const float* gate, float* out, float* phys, uint32_t splits,
+                                    void* workspace, size_t workspace_bytes, void* stream) {
+  if (!q || !k || !v || !out || !workspace || head_dim != 256 || kv_heads == 0 || heads != 4 * kv_heads ||
+      capacity == 0 || splits == 0)
+    return fail(RTA_E_ARG, "rta_attention_decode_f16: head_dim 256, heads == 4*kv_heads, capacity and splits > 0");
+  if (workspace_bytes < rta_attention_workspace_bytes(heads, kv_heads, head_dim, splits))
+    return fail(RTA_E_ARG, "rta_attention_decode_f16: workspace too small");
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  const size_t recs = static_cast<size_t>(heads) * splits;
+  rta::AttnParams p;
+  p.q = q;
+  p.q_seq_stride = static_cast<size_t>(heads) * head_dim;
+  p.k = static_cast<const __half*>(k);
+  p.v = static_cast<const __half*>(v);
+  p.seq_stride = 0;
+  p.kv_stride = static_cast<size_t>(kv_stride) * head_dim;
+  p.pos_stride = static_cast<size_t>(pos_stride) * head_dim;
+  p.heads = heads;
+  p.kvh = kv_heads;
+  p.hd = head_dim;
+  p.capacity = capacity;
+  p.history_start = 0;
+  p.t = time;
+  p.gate = gate;
+  p.out = out;
+  p.out_seq_stride = static_cast<size_t>(heads) * head_dim;
+  p.phys = phys;
+  p.err = reinterpret_cast<uint32_t*>(ws);
+  p.part_m = reinterpret_cast<float*>(ws + kErrBytes);
+  p.part_z = p.part_m + recs;
+  p.part_o = p.part_z + recs;
+  cudaStream_t s = as_stream(stream);
+  rta_status st = cuda_status(cudaMemsetAsync(ws, 0, 4, s), "rta_attention_decode_f16(memset)");
+  if (st != RTA_OK) return st;
+  return cuda_status(rta::launch_attention(p, splits, 1, false, s), "rta_attention_decode_f16");
+}
+
+rta_status rta_workspace_error(const void* workspace, size_t workspace_bytes, void* stream, uint32_t* error_word) {
+  if (!workspace || workspace_bytes < 4 || !error_word) return fail(RTA_E_ARG, "rta_workspace_error: bad arguments");
+  uint32_t w = 0;
+  cudaStream_t s = as_stream(stream);
+  rta_status st = cuda_status(cudaMemcpyAsync(&w, workspace, 4, cudaMemcpyDeviceToHost, s), "rta_workspace_error");
+  if (st != RTA_OK) return st;
+  st = cuda_status(cudaStreamSynchronize(s), "rta_workspace_error(sync)");
+  if (st != RTA_OK) return st;
+  *error_word = w;
+  if (w & RTA_DEVERR_TIMEOUT) return fail(RTA_E_TIMEOUT, "device-side wait exceeded its bound");
+  if (w) return fail(RTA_E_DEVICE_CHECK, "device error word " + std::to_string(w));
+  return RTA_OK;
+}
+
+}  // extern "C"

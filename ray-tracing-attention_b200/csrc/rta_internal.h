@@ -1,0 +1,63 @@
+// rta_internal.h -- internal C++ interface between the CUDA kernels, the
+// decode engine and the C-ABI layer (capi.cu).  Not installed; the public
+// boundary is include/rta.h.
+#pragma once
+#include <cuda_runtime.h>
+#include <cstddef>
+#include <cstdint>
+
+#include "rta_device.cuh"
+
+namespace rta {
+
+constexpr int kF32 = 0, kF16 = 1, kBF16 = 30, kQ4K = 12, kQ6K = 14;  // export.py FORMATS codes
+constexpr uint32_t kQ4KBytes = 144, kQ6KBytes = 210;
+constexpr uint32_t kMaxBatch = 32;  // GEMV batch rows per launch (mma slices of 4)
+
+inline uint32_t block_bytes(int fmt) { return fmt == kQ4K ? kQ4KBytes : kQ6KBytes; }
+
+// ---------------------------------------------------------------- quant.cu
+cudaError_t launch_quantize(int fmt, const float* src, size_t nblocks, uint8_t* dst, cudaStream_t s);
+cudaError_t launch_random_quantize(int fmt, uint64_t seed, float sigma, uint64_t first_block, size_t nblocks,
+                                   uint8_t* dst, cudaStream_t s);
+cudaError_t launch_random_normal(uint64_t seed, float sigma, float mean, size_t n, float* dst, cudaStream_t s);
+cudaError_t launch_dequantize(int fmt, const uint8_t* src, size_t nblocks, float* dst, cudaStream_t s);
+
+// ----------------------------------------------------------------- gemv.cu
+// Activation prologue applied (per CTA) before the int16 activation split.
+enum Prologue : int {
+  kPlain = 0,      // x as given
+  kRmsNorm = 1,    // x * inversesqrt(mean(x^2) + eps) * norm_w
+  kHeadGate = 2,   // per 128-wide head: x * inversesqrt(mean_head(x^2)+eps) * norm_w * z * sigmoid(z)
+  kSigmoidGate = 3 // x * sigmoid(z)
+};
+enum Epilogue : int {
+  kStore = 0,      // y = W x
+  kAccumulate = 1, // y += W x  (residual stream)
+  kSwiGLU = 2      // y = swiglu(W0 x, W1 x)
+};
+struct GemvArgs {
+  int fmt = kQ4K;             // kQ4K or kQ6K
+  const uint8_t* w0 = nullptr;
+  const uint8_t* w1 = nullptr;  // second matrix (SwiGLU up); same shape as w0
+  uint32_t rows = 0, cols = 0;  // output rows (multiple of 16), input cols (multiple of 256)
+  const float* x = nullptr;
+  uint32_t x_stride = 0, batch = 1;
+  int prologue = kPlain;
+  const float* norm_w = nullptr;
+  float eps = 1e-6f;
+  const float* z = nullptr;     // gate input for kHeadGate / kSigmoidGate, same stride as x
+  int epilogue = kStore;
+  float* y = nullptr;
+  uint32_t y_stride = 0;
+  // optional argmax over the rows of batch row b (vocabulary readout):
+  unsigned long long* argmax = nullptr;  // [batch] packed (order key, ~id); null = none
+  uint32_t* err = nullptr;               // device error word (may be null)
+  bool pdl = false;                      // launch with programmatic stream serialization
+};
+cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t s);
+// Dense F32 GEMV for the tiny recurrent alpha/beta projections.
+cudaError_t launch_gemv_f32(const float* W, uint32_t rows, uint32_t cols, const float* x, uint32_t x_stride,
+                            uint32_t batch, float* y, uint32_t y_stride, cudaStream_t s);
+
+}  // namespace rta
