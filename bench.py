@@ -42,7 +42,8 @@ def peaks():
 
 # ---------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi sampling of SM clock and throttle reasons during the timed region."""
+    """nvidia-smi sampling of SM clock and throttle reasons during the timed region
+    (written to a file by nvidia-smi itself: a pipe would be block-buffered)."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -52,29 +53,31 @@ class ClockSampler:
         self.gpu = gpu_index
         self.proc = None
         self.lines: list[str] = []
+        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"rta_clocks_{os.getpid()}_{gpu_index}.csv"
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
+                                          "--format=csv,noheader,nounits", "-lms", "50", "-f", str(self.path)],
+                                         stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)  # let the first sample land before the timed region starts
         except (OSError, FileNotFoundError):
             self.proc = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
     def __exit__(self, *exc):
         if self.proc is not None:
+            time.sleep(0.1)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
+            try:
+                self.lines = self.path.read_text().splitlines()
+                self.path.unlink()
+            except OSError:
+                self.lines = []
 
     def summary(self):
         sm, mx, reasons = [], None, set()
@@ -180,10 +183,10 @@ class MLPWorkload(Workload):
 
     def dominant_launch(self, i):
         w = self.w[i % self.copies]
-        self.ops.gemv(12, w[0], self.F, self.D, self.x, y=self.act)  # one 6144x2048 Q4_K GEMV
+        self.ops.gemv_swiglu(12, w[0], w[1], self.F, self.D, self.x, act=self.act)  # gate+up, 2 x 6144x2048
 
     def dominant_bytes(self):
-        return self.F * self.D // 256 * 144 + self.D * 4 + self.F * 4
+        return 2 * self.F * self.D // 256 * 144 + self.D * 4 + self.F * 4
 
     def units_per_step(self):
         return 1.0
@@ -348,20 +351,43 @@ WORKLOADS = {"mlp": MLPWorkload, "lmhead": LMHeadWorkload, "attention": Attentio
 
 
 # ----------------------------------------------------------------- timing
-def time_steps(fn, steps, warmup, world):
+def time_steps(fn, steps, warmup, world, graph=True, min_seconds=0.0):
+    """W warm-up steps, then EXACTLY `steps` steps timed with CUDA events on the
+    launching stream between barrier + synchronize, max over ranks.  With
+    graph=True the K steps are captured once into a CUDA graph and the timed
+    region is one replay (device throughput without host launch overhead);
+    graph=False times eager public-API calls.  min_seconds repeats the timed
+    region (same K steps each time) and reports the per-replay mean, so the
+    clock sampler sees the load."""
     import torch
     for i in range(warmup):
         fn(i)
     torch.cuda.synchronize()
+    g = None
+    if graph:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for i in range(steps):
+                fn(warmup + i)
+        g.replay()  # untimed: first replay uploads the graph
+        torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps, t0 = 0, time.perf_counter()
     start.record()
-    for i in range(steps):
-        fn(warmup + i)
+    while True:
+        if g is not None:
+            g.replay()
+        else:
+            for i in range(steps):
+                fn(warmup + i)
+        reps += 1
+        if time.perf_counter() - t0 >= min_seconds:
+            break
     stop.record()
     torch.cuda.synchronize()
-    ms = start.elapsed_time(stop)
+    ms = start.elapsed_time(stop) / reps
     barrier(world)
     return max_over_ranks(ms, world)
 
@@ -371,14 +397,14 @@ def run_ours(args, world, rank, local):
     wl = WORKLOADS[args.workload](**({"history": args.history} if args.workload == "attention" else {}))
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
-        ms = time_steps(wl.step, args.steps, args.warmup, world)
+        ms = time_steps(wl.step, args.steps, args.warmup, world, min_seconds=args.min_seconds)
     ms_step = ms / args.steps
     value = wl.units_per_step() * world / (ms_step / 1e3)
     # dominant kernel alone, CUDA events on the launching (current) stream
     dom_ms = time_steps(wl.dominant_launch, args.steps, args.warmup, world) / args.steps
     pk = peaks()
     achieved = wl.dominant_bytes() / (dom_ms / 1e3) / 1e9
-    e2e_ms = time_steps(wl.e2e_step, args.steps, args.warmup, world) / args.steps
+    e2e_ms = time_steps(wl.e2e_step, args.steps, args.warmup, world, graph=False) / args.steps
     h2d, d2h = wl.e2e_bytes()
     line = {
         "metric": wl.metric, "value": value, "unit": wl.unit, "n_gpus": world, "steps": args.steps,
@@ -435,6 +461,8 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="lmhead")
     ap.add_argument("--history", type=int, default=32768)
     ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--min-seconds", type=float, default=1.0,
+                    help="repeat the timed K-step region for at least this long (clock sampling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)

@@ -78,6 +78,12 @@ RTA_API rta_status rta_dequantize(int format, const void* blocks, size_t nblocks
 RTA_API rta_status rta_gemv(int format, const void* w, uint32_t rows, uint32_t cols, const float* x, uint32_t batch,
                     float* y, int accumulate, void* stream);
 
+/* Fused gate+up projection with the SwiGLU epilogue (op 2 kind 3,
+ * ray_tracing/native/shaders/resident_math.comp:54,58,71):
+ * act[b][r] = swiglu(Wg[r] . x[b], Wu[r] . x[b]), rows % 16 == 0, cols % 256 == 0. */
+RTA_API rta_status rta_gemv_swiglu(int format, const void* w_gate, const void* w_up, uint32_t rows, uint32_t cols,
+                                   const float* x, uint32_t batch, float* act, void* stream);
+
 /* SwiGLU MLP: act = swiglu(Wg x, Wu x) [batch][middle]; y (+)= Wd act [batch][hidden].
  * swiglu(g,u) = sign(g)sign(u)|g||u|sigmoid(g).  Replaces executeMLP
  * (optical_resident.cpp:484-491: op 2 kind 3 then kind 4). */

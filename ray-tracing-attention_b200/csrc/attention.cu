@@ -314,9 +314,17 @@ cudaError_t launch_attention(const AttnParams& p, uint32_t nsplit, uint32_t nseq
       p.kv_stride % 8 || p.seq_stride % 8)
     return cudaErrorMisalignedAddress;
   const size_t smem = attention_smem_bytes();
-  cudaError_t e = cudaFuncSetAttribute(attention_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(smem));
-  if (e != cudaSuccess) return e;
+  static bool attr_set[64] = {false};  // one-time per-device kernel setup, off the per-launch path
+  cudaError_t e = cudaSuccess;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!attr_set[dev]) {
+    e = cudaFuncSetAttribute(attention_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;

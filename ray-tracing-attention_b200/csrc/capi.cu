@@ -95,6 +95,26 @@ rta_status rta_gemv(int format, const void* w, uint32_t rows, uint32_t cols, con
   return cuda_status(rta::launch_gemv(a, as_stream(stream)), "rta_gemv");
 }
 
+rta_status rta_gemv_swiglu(int format, const void* wg, const void* wu, uint32_t rows, uint32_t cols, const float* x,
+                           uint32_t batch, float* act, void* stream) {
+  if (!quant_format(format) || !wg || !wu || !x || !act || rows == 0 || rows % 16 || cols == 0 || cols % 256 ||
+      batch == 0 || batch > rta::kMaxBatch)
+    return fail(RTA_E_ARG, "rta_gemv_swiglu: rows % 16 == 0, cols % 256 == 0, 1 <= batch <= 32");
+  rta::GemvArgs g;
+  g.fmt = format;
+  g.w0 = static_cast<const uint8_t*>(wg);
+  g.w1 = static_cast<const uint8_t*>(wu);
+  g.rows = rows;
+  g.cols = cols;
+  g.x = x;
+  g.x_stride = cols;
+  g.batch = batch;
+  g.epilogue = rta::kSwiGLU;
+  g.y = act;
+  g.y_stride = rows;
+  return cuda_status(rta::launch_gemv(g, as_stream(stream)), "rta_gemv_swiglu");
+}
+
 rta_status rta_mlp_swiglu(int format, const void* wg, const void* wu, const void* wd, uint32_t hidden,
                           uint32_t middle, const float* x, uint32_t batch, float* act, float* y, int accumulate,
                           void* stream) {

@@ -285,22 +285,21 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const Params p) {
             scr[pair] = d * static_cast<float>(static_cast<int8_t>(bk[192 + grp]));
           }
           __syncwarp();
-          const uint8_t* base = stage + kb * 210u;
-          const uint32_t rowg = g * chunk, rowg8 = (g + 8u) * chunk;
+          const uint32_t rowg = g * chunk + kb * 210u, rowg8 = (g + 8u) * chunk + kb * 210u;
 #pragma unroll
           for (uint32_t part = 0; part < 2u; ++part) {
             uint32_t ql[2][4], qh[2][2];
 #pragma unroll
             for (uint32_t q = 0; q < 4u; ++q) {
               const uint32_t off = part * 64u + 16u * q + 4u * t;
-              ql[0][q] = lds_u32_unaligned(base, rowg + off);
-              ql[1][q] = lds_u32_unaligned(base, rowg8 + off);
+              ql[0][q] = lds_u32_unaligned(stage, rowg + off);
+              ql[1][q] = lds_u32_unaligned(stage, rowg8 + off);
             }
 #pragma unroll
             for (uint32_t q = 0; q < 2u; ++q) {
               const uint32_t off = 128u + part * 32u + 16u * q + 4u * t;
-              qh[0][q] = lds_u32_unaligned(base, rowg + off);
-              qh[1][q] = lds_u32_unaligned(base, rowg8 + off);
+              qh[0][q] = lds_u32_unaligned(stage, rowg + off);
+              qh[1][q] = lds_u32_unaligned(stage, rowg8 + off);
             }
 #pragma unroll
             for (uint32_t jj = 0; jj < 8u; ++jj) {
@@ -445,14 +444,38 @@ cudaError_t launch_t(const GemvArgs& a, Params p, cudaStream_t s) {
   p.off_red = carve(max(red_floats * 4u, static_cast<uint32_t>(kThreads * 8)), 16);
   p.off_misc = carve(128, 16);
   const uint32_t smem = off;
-  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return e;
-  int dev = 0, sms = 0, per_sm = 0;
+  // One-time kernel setup and occupancy per (kernel instance, smem size): these
+  // queries cost microseconds and must stay off the per-launch path.
+  // (function attributes are per device: index the cache by device ordinal)
+  static int max_smem_set[64] = {0};
+  static uint32_t cached_smem[8] = {0};
+  static int cached_grid[8] = {0};
+  static int sms = 0;
+  cudaError_t e = cudaSuccess;
+  int dev = 0;
   cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, smem);
-  if (e != cudaSuccess) return e;
-  if (per_sm < 1) return cudaErrorInvalidConfiguration;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!max_smem_set[dev]) {
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return e;
+    max_smem_set[dev] = 1;
+  }
+  if (smem > 227u * 1024u) return cudaErrorInvalidConfiguration;
+  int per_sm = 0;
+  for (int i = 0; i < 8; ++i)
+    if (cached_smem[i] == smem) per_sm = cached_grid[i];
+  if (per_sm == 0) {
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, smem);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) return cudaErrorInvalidConfiguration;
+    for (int i = 0; i < 8; ++i)
+      if (cached_smem[i] == 0) {
+        cached_smem[i] = smem;
+        cached_grid[i] = per_sm;
+        break;
+      }
+  }
   const uint32_t tiles = a.rows / kTileRows;
   const uint32_t grid = min(tiles, static_cast<uint32_t>(per_sm * sms));
   cudaLaunchConfig_t cfg = {};

@@ -12,7 +12,11 @@
 namespace rta {
 
 __device__ __forceinline__ float round_half(float v) { return __half2float(__float2half_rn(v)); }
-__device__ __forceinline__ float clampf_(float v, float lo, float hi) { return fminf(fmaxf(v, lo), hi); }
+// GLSL max(x,y) = x < y ? y : x, min(x,y) = y < x ? y : x: the operand order
+// fixes the sign of zero results (fmaxf/fminf leave it unspecified).
+__device__ __forceinline__ float gmax(float a, float b) { return a < b ? b : a; }
+__device__ __forceinline__ float gmin(float a, float b) { return b < a ? b : a; }
+__device__ __forceinline__ float clampf_(float v, float lo, float hi) { return gmin(gmax(v, lo), hi); }
 __device__ __forceinline__ void put_half(uint8_t* p, float v) {
   const unsigned short h = __half_as_ushort(__float2half_rn(v));
   p[0] = static_cast<uint8_t>(h);
@@ -20,22 +24,22 @@ __device__ __forceinline__ void put_half(uint8_t* p, float v) {
 }
 
 __device__ void quant_q4k_block(const float* v, uint8_t* out) {
-  float gscale[8], gmin[8];
+  float gscale[8], gminv[8];
   uint32_t sc[8], mn[8];
   for (int g = 0; g < 8; ++g) {
     float lo = 0.f, hi = 0.f;
     for (int i = 0; i < 32; ++i) {
       const float x = v[g * 32 + i];
-      lo = fminf(lo, x);
-      hi = fmaxf(hi, x);
+      lo = gmin(lo, x);
+      hi = gmax(hi, x);
     }
     gscale[g] = __fdiv_rn(__fsub_rn(hi, lo), 15.0f);
-    gmin[g] = -lo;
+    gminv[g] = -lo;
   }
   float maxD = 0.f, maxMin = 0.f;
   for (int g = 0; g < 8; ++g) {
-    maxD = fmaxf(maxD, gscale[g]);
-    maxMin = fmaxf(maxMin, gmin[g]);
+    maxD = gmax(maxD, gscale[g]);
+    maxMin = gmax(maxMin, gminv[g]);
   }
   const float d = round_half(__fdiv_rn(maxD, 63.0f));
   const float dm = round_half(__fdiv_rn(maxMin, 63.0f));
@@ -44,8 +48,8 @@ __device__ void quant_q4k_block(const float* v, uint8_t* out) {
   put_half(blk, d);
   put_half(blk + 2, dm);
   for (int g = 0; g < 8; ++g) {
-    sc[g] = static_cast<uint32_t>(clampf_(roundf(__fdiv_rn(gscale[g], fmaxf(d, 1e-30f))), 0.f, 63.f));
-    mn[g] = static_cast<uint32_t>(clampf_(roundf(__fdiv_rn(gmin[g], fmaxf(dm, 1e-30f))), 0.f, 63.f));
+    sc[g] = static_cast<uint32_t>(clampf_(roundf(__fdiv_rn(gscale[g], gmax(d, 1e-30f))), 0.f, 63.f));
+    mn[g] = static_cast<uint32_t>(clampf_(roundf(__fdiv_rn(gminv[g], gmax(dm, 1e-30f))), 0.f, 63.f));
   }
   for (int g = 0; g < 4; ++g) {
     blk[4 + g] = static_cast<uint8_t>(sc[g] | ((sc[g + 4] >> 4) << 6));
@@ -57,7 +61,7 @@ __device__ void quant_q4k_block(const float* v, uint8_t* out) {
     const float offset = __fmul_rn(dm, static_cast<float>(mn[g]));
     const float step = __fmul_rn(d, static_cast<float>(sc[g]));
     const uint32_t q = static_cast<uint32_t>(
-        clampf_(roundf(__fdiv_rn(__fadd_rn(v[i], offset), fmaxf(step, 1e-30f))), 0.f, 15.f));
+        clampf_(roundf(__fdiv_rn(__fadd_rn(v[i], offset), gmax(step, 1e-30f))), 0.f, 15.f));
     blk[16 + (i / 64u) * 32u + i % 32u] |= static_cast<uint8_t>(q << ((i % 64u) / 32u * 4u));
   }
   for (int i = 0; i < 144; ++i) out[i] = blk[i];
@@ -67,24 +71,24 @@ __device__ void quant_q6k_block(const float* v, uint8_t* out) {
   float gscale[16];
   for (int g = 0; g < 16; ++g) {
     float hi = 0.f;
-    for (int i = 0; i < 16; ++i) hi = fmaxf(hi, fabsf(v[g * 16 + i]));
+    for (int i = 0; i < 16; ++i) hi = gmax(hi, fabsf(v[g * 16 + i]));
     gscale[g] = __fdiv_rn(hi, 31.0f);
   }
   float maxD = 0.f;
-  for (int g = 0; g < 16; ++g) maxD = fmaxf(maxD, gscale[g]);
+  for (int g = 0; g < 16; ++g) maxD = gmax(maxD, gscale[g]);
   const float d = round_half(__fdiv_rn(maxD, 127.0f));
   uint8_t blk[210];
   for (int i = 0; i < 210; ++i) blk[i] = 0;
   put_half(blk + 208, d);
   uint32_t sc[16];
   for (int g = 0; g < 16; ++g) {
-    sc[g] = static_cast<uint32_t>(clampf_(roundf(__fdiv_rn(gscale[g], fmaxf(d, 1e-30f))), 0.f, 127.f));
+    sc[g] = static_cast<uint32_t>(clampf_(roundf(__fdiv_rn(gscale[g], gmax(d, 1e-30f))), 0.f, 127.f));
     blk[192 + g] = static_cast<uint8_t>(sc[g]);
   }
   for (uint32_t i = 0; i < 256u; ++i) {
     const float step = __fmul_rn(d, static_cast<float>(sc[i / 16u]));
     const uint32_t q = static_cast<uint32_t>(
-        static_cast<int>(clampf_(roundf(__fdiv_rn(v[i], fmaxf(step, 1e-30f))), -32.f, 31.f)) + 32);
+        static_cast<int>(clampf_(roundf(__fdiv_rn(v[i], gmax(step, 1e-30f))), -32.f, 31.f)) + 32);
     const uint32_t part = i / 128u, within = i % 128u;
     blk[part * 64u + within % 64u] |= static_cast<uint8_t>((q & 15u) << ((within / 64u) * 4u));
     blk[128u + part * 32u + within % 32u] |= static_cast<uint8_t>((q >> 4) << ((within / 32u) * 2u));

@@ -136,8 +136,9 @@ __device__ __forceinline__ float warp_max(float v) {
   for (int m = 16; m >= 1; m >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, m));
   return v;
 }
-// Load 4 bytes at a 2-byte aligned shared address (Q6_K blocks are 210 bytes,
-// so odd blocks of a row start 2 bytes off a word boundary).
+// Load 4 bytes at byte offset `byte_off` from a 4-byte aligned shared base
+// (Q6_K blocks are 210 bytes, so odd blocks of a row start 2 bytes off a word
+// boundary).  `base` itself must be word aligned.
 __device__ __forceinline__ uint32_t lds_u32_unaligned(const uint8_t* base, uint32_t byte_off) {
   const uint32_t* w = reinterpret_cast<const uint32_t*>(base + (byte_off & ~3u));
   const uint32_t lo = w[0];

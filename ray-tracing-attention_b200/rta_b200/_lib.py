@@ -35,6 +35,7 @@ _SIGNATURES = {
     "rta_synthetic_normal": (c_i32, [c_u64, c_f, c_f, c_sz, c_p, c_p]),
     "rta_dequantize": (c_i32, [c_i32, c_p, c_sz, c_p, c_p]),
     "rta_gemv": (c_i32, [c_i32, c_p, c_u32, c_u32, c_p, c_u32, c_p, c_i32, c_p]),
+    "rta_gemv_swiglu": (c_i32, [c_i32, c_p, c_p, c_u32, c_u32, c_p, c_u32, c_p, c_p]),
     "rta_mlp_swiglu": (c_i32, [c_i32, c_p, c_p, c_p, c_u32, c_u32, c_p, c_u32, c_p, c_p, c_i32, c_p]),
     "rta_readout_workspace_bytes": (c_sz, [c_u32]),
     "rta_readout": (c_i32, [c_i32, c_p, c_u32, c_u32, c_p, c_u32, c_p, c_p, c_p, c_p, c_p]),

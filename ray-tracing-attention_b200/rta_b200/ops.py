@@ -74,6 +74,13 @@ def gemv(fmt: int, w: torch.Tensor, rows: int, cols: int, x: torch.Tensor, y: to
     return y
 
 
+def gemv_swiglu(fmt: int, wg, wu, rows: int, cols: int, x: torch.Tensor, act: torch.Tensor | None = None):
+    x = x.reshape(-1, cols)
+    act = torch.empty(x.shape[0], rows, dtype=torch.float32, device=x.device) if act is None else act
+    check(_lib.load().rta_gemv_swiglu(fmt, _ptr(wg), _ptr(wu), rows, cols, _ptr(x), x.shape[0], _ptr(act), _stream()))
+    return act
+
+
 def mlp_swiglu(fmt: int, wg, wu, wd, hidden: int, middle: int, x: torch.Tensor, y: torch.Tensor | None = None,
                act: torch.Tensor | None = None, accumulate: bool = False):
     x = x.reshape(-1, hidden)
@@ -132,5 +139,5 @@ def workspace_error(workspace: torch.Tensor) -> int:
     return int(word.value)
 
 
-__all__ = ["quantize", "dequantize", "synthetic_blocks", "synthetic_normal", "gemv", "mlp_swiglu", "readout",
+__all__ = ["quantize", "dequantize", "synthetic_blocks", "synthetic_normal", "gemv", "gemv_swiglu", "mlp_swiglu", "readout",
            "attention_decode_f16", "attention_workspace", "workspace_error", "Q4_K", "Q6_K", "BLOCK_BYTES"]
