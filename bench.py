@@ -347,7 +347,159 @@ class AttentionWorkload(Workload):
                           "(C restatement of the S_t/R_t detector, OpenMP over heads)"}
 
 
-WORKLOADS = {"mlp": MLPWorkload, "lmhead": LMHeadWorkload, "attention": AttentionWorkload}
+class DecodeWorkload(Workload):
+    """2B-shape hybrid (24 layers, 3:1 recurrent:full), batch 1,
+    prompt 512 random ids, then greedy decode.  A step is one decode token."""
+    name, metric, unit, dtype, dominant = ("decode2b", "decode tokens/s (2B-shape hybrid, batch 1)", "tokens/s",
+                                           "q4k/q6k-int8mma, f16-kv, f32 state",
+                                           "gemv_kernel<Q6_K> vocabulary readout + argmax")
+    prompt_len = 512
+
+    def __init__(self, seed=20261201):
+        import torch
+        from rta_b200 import assets, ops
+        from rta_b200.model import ResidentModel
+        self.ops, self.torch, self.assets = ops, torch, assets
+        self.spec = assets.spec_2b()
+        self.seed = seed
+        self.model = ResidentModel.synthetic(self.spec, seed, capacity=2048)
+        self.prompt = np.random.default_rng(seed).integers(0, self.spec.vocabulary_size, self.prompt_len)
+        self.model.prefill(self.prompt)
+        self.launches_per_step = self.model.resources()["kernels_per_decode_step"]
+        # the dominant kernel in isolation: same readout shape on its own weights
+        self.lm_w = ops.synthetic_blocks(14, self.spec.vocabulary_size, self.spec.hidden_size, seed + 7)
+        self.lm_x = ops.synthetic_normal(self.spec.hidden_size, seed + 8)
+        self.lm_ws = torch.empty(4096, dtype=torch.uint8, device="cuda")
+
+    def decode(self, k):
+        ids = self.model.generate(k)
+        return self.model.last_gpu_ms, ids
+
+    def dominant_launch(self, i):
+        self.ops.readout(14, self.lm_w, self.spec.vocabulary_size, self.spec.hidden_size, self.lm_x, logits=False,
+                         workspace=self.lm_ws)
+
+    def dominant_bytes(self):
+        return self.spec.vocabulary_size * self.spec.hidden_size // 256 * 210 + self.spec.hidden_size * 4
+
+    def step_bytes(self, position):
+        """Algorithmic HBM bytes of one decode token at `position` (weights once, fp16 KV, recurrent state)."""
+        lay = self.model.layout
+        weights = sum(t.nbytes for t in lay.matrices) + lay.basis[1].nbytes + self.spec.hidden_size * 210 // 256
+        kv = len(self.spec.full_layers) * min(position + 1, 2048) * self.spec.kv_width * 2 * 2
+        rec = len(self.spec.recurrent_layers) * self.spec.state_heads * 128 * 128 * 4 * 2
+        return weights + kv + rec
+
+    def units_per_step(self):
+        return 1.0
+
+    def config(self):
+        return {"workload": "config4_2b_hybrid_decode_b1", "layers": self.spec.depth, "pattern": "rec,rec,rec,full",
+                "hidden": self.spec.hidden_size, "intermediate": self.spec.middle_size,
+                "vocab": self.spec.vocabulary_size, "q_heads": 16, "kv_heads": 4, "head_dim": 256,
+                "rotary_dim": self.spec.rotary_dim, "state_heads": self.spec.state_heads,
+                "state_key_heads": self.spec.state_key_heads, "formats": "Q4_K matrices, Q6_K embedding + LM head",
+                "kv_cache": "fp16", "prompt": self.prompt_len, "batch": 1, "tied_embeddings": False,
+                "l2": "per-token weight stream 1.1 GB > L2"}
+
+    def cpu_baseline(self, budget_s):
+        from oracle import oracle
+        from oracle.model import OracleModel
+        from rta_b200 import assets
+        spec = assets.spec_2b()
+        lay = assets.plan(spec, self.seed)
+        params, mats, basis = host_payloads(lay, self.seed)
+        ref = OracleModel(spec, params, mats, basis, 2048)
+        t0 = time.perf_counter()
+        ref.prefill(np.random.default_rng(self.seed).integers(0, spec.vocabulary_size, 4))
+        n = 0
+        while time.perf_counter() - t0 < budget_s or n == 0:
+            tok, _ = ref.readout()
+            ref.forward(tok)
+            n += 1
+        dt = time.perf_counter() - t0
+        return {"value": (n + 4) / dt, "unit": self.unit, "cores": oracle.threads(), "kind": "port",
+                "sample": f"4 prompt + {n} greedy tokens of a 2B-shape model (random valid Q4_K/Q6_K blocks) "
+                          "through the model oracle (C restatement of the reference shader math, OpenMP)"}
+
+
+def host_payloads(layout, seed):
+    """Host-side payloads of the layout's shapes with random valid packed blocks
+    (no GPU kernels involved: the CPU arms time the reference's CPU path only)."""
+    rng = np.random.default_rng(seed)
+    mats = np.zeros(layout.matrix_words * 4, np.uint8)
+    basis = np.zeros(layout.basis_words * 4, np.uint8)
+    for i, t in enumerate(layout.matrices + layout.basis):
+        buf = mats if i < len(layout.matrices) else basis
+        if t.fmt == 0:
+            buf[t.offset:t.offset + t.nbytes] = rng.normal(0, 0.02, t.rows * t.cols).astype(np.float32).view(np.uint8)
+            continue
+        bs = 144 if t.fmt == 12 else 210
+        nb = t.rows * t.cols // 256
+        blk = rng.integers(0, 256, (nb, bs), dtype=np.uint8)
+        d = rng.uniform(1e-4, 6e-4, nb).astype(np.float16).view(np.uint8).reshape(nb, 2)
+        if t.fmt == 12:
+            blk[:, 0:2] = d
+            blk[:, 2:4] = rng.uniform(1e-4, 6e-4, nb).astype(np.float16).view(np.uint8).reshape(nb, 2)
+        else:
+            blk[:, 208:210] = d
+        buf[t.offset:t.offset + t.nbytes] = blk.reshape(-1)
+    return layout.params(), mats, basis
+
+
+WORKLOADS = {"mlp": MLPWorkload, "lmhead": LMHeadWorkload, "attention": AttentionWorkload,
+             "decode2b": DecodeWorkload}
+
+
+def run_decode(args, world, rank, local):
+    """Decode: `value` = K tokens generated in one public-API call (device-side
+    graph replays, GPU time by CUDA events on the engine stream); `e2e` = K calls
+    of generate(1) (host round trip per token: control H2D, ids D2H)."""
+    import torch
+    wl = DecodeWorkload()
+    wl.decode(args.warmup)                       # warm-up tokens
+    torch.cuda.synchronize()
+    barrier(world)
+    with ClockSampler(local) as clk:
+        reps, ms_total, t0 = 0, 0.0, time.perf_counter()
+        while True:
+            ms, ids = wl.decode(args.steps)
+            ms_total += ms
+            reps += 1
+            if time.perf_counter() - t0 >= args.min_seconds or reps >= 64:
+                break
+    ms_step = max_over_ranks(ms_total / reps, world) / args.steps
+    barrier(world)
+    dom_ms = time_steps(wl.dominant_launch, args.steps, args.warmup, world) / args.steps
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        wl.model.generate(1)
+    e2e_s = (time.perf_counter() - t0) / args.steps
+    e2e_s = max_over_ranks(e2e_s * 1e3, world) / 1e3
+    pos = wl.model.state()[1]
+    pk = peaks()
+    achieved = wl.dominant_bytes() / (dom_ms / 1e3) / 1e9
+    step_gbs = wl.step_bytes(pos) / (ms_step / 1e3) / 1e9
+    line = {
+        "metric": wl.metric, "value": world / (ms_step / 1e3), "unit": wl.unit, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic (seeded random init, prompt ids)",
+        "config": dict(wl.config(), parallelism=f"replicas x{world}" if world > 1 else "single GPU"),
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / pk["hbm_gbs"], "traffic": None, "kernel": wl.dominant,
+                     "algorithmic_bytes": wl.dominant_bytes(), "kernel_ms": dom_ms,
+                     "peak_source": f"{pk['source']} hbm_gbs (burst copy)",
+                     "step_algorithmic_bytes": wl.step_bytes(pos), "step_achieved_gbs": step_gbs,
+                     "step_frac": step_gbs / pk["hbm_gbs"]},
+        "e2e": {"value": world / e2e_s, "unit": wl.unit, "h2d_bytes_per_step": 16, "d2h_bytes_per_step": 4,
+                "api": "ResidentModel.generate(1) -> rta_model_generate (C-ABI)"},
+        "gpu_launches": wl.launches_per_step * args.steps,
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = wl.cpu_baseline(args.cpu_budget)
+    return line
 
 
 # ----------------------------------------------------------------- timing
@@ -430,10 +582,14 @@ def run_reference(args, world, rank):
     its shader math; the Vulkan path cannot run here), rank 0 only."""
     if rank != 0:
         return None
+    if args.workload == "decode2b":
+        return run_reference_decode(args, world)
     cls = WORKLOADS[args.workload]
     wl = cls.__new__(cls)
     if args.workload == "attention":
         wl.L = args.history
+    if args.workload == "decode2b":
+        wl.seed = 20261201
     budget = max(1.0, args.cpu_budget / max(args.steps, 1))
     vals = []
     for _ in range(args.warmup + args.steps):
@@ -442,12 +598,43 @@ def run_reference(args, world, rank):
     v = float(np.median([b["value"] for b in vals]))
     base = dict(vals[-1], value=v)
     cfg = {"mlp": {"workload": "config1_swiglu_mlp_b1"}, "lmhead": {"workload": "config3_lmhead_b1"},
-           "attention": {"workload": f"config2_gqa_decode_L{args.history}"}}[args.workload]
+           "attention": {"workload": f"config2_gqa_decode_L{args.history}"},
+           "decode2b": {"workload": "config4_2b_hybrid_decode_b1"}}[args.workload]
     return {"impl": "reference", "metric": cls.metric, "value": v, "unit": cls.unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "dtype": "f32",
             "data": "synthetic (seeded, BASELINE shapes)", "config": cfg,
             "cpu_baseline": base, "e2e": {"value": v, "unit": cls.unit, "h2d_bytes_per_step": 0,
                                           "d2h_bytes_per_step": 0},
+            "note": "reference Vulkan ray-query worker unavailable on this box (no graphics stack, no RT cores); "
+                    "timed its CPU path: the C restatement of its shader math"}
+
+
+def run_reference_decode(args, world):
+    """The 2B decode through the model oracle on all host cores: one model build,
+    W warm-up tokens, then min(K, 16) timed tokens (a bounded sample)."""
+    from oracle import oracle
+    from oracle.model import OracleModel
+    from rta_b200 import assets
+    spec = assets.spec_2b()
+    lay = assets.plan(spec, 20261201)
+    params, mats, basis = host_payloads(lay, 20261201)
+    ref = OracleModel(spec, params, mats, basis, 2048)
+    ref.prefill(np.random.default_rng(1).integers(0, spec.vocabulary_size, 4))
+    for _ in range(min(args.warmup, 3)):
+        ref.forward(ref.readout()[0])
+    n = max(1, min(args.steps, 16))
+    t0 = time.perf_counter()
+    for _ in range(n):
+        ref.forward(ref.readout()[0])
+    v = n / (time.perf_counter() - t0)
+    base = {"value": v, "unit": "tokens/s", "cores": oracle.threads(), "kind": "port",
+            "sample": f"{n} greedy tokens after a 4-token prompt of a 2B-shape model (random valid Q4_K/Q6_K "
+                      "blocks) through the model oracle, the C restatement of the reference shader math (OpenMP)"}
+    return {"impl": "reference", "metric": DecodeWorkload.metric, "value": v, "unit": "tokens/s", "n_gpus": world,
+            "steps": n, "warmup": min(args.warmup, 3), "higher_is_better": True, "dtype": "f32",
+            "data": "synthetic (seeded random init, prompt ids)",
+            "config": {"workload": "config4_2b_hybrid_decode_b1"}, "cpu_baseline": base,
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "note": "reference Vulkan ray-query worker unavailable on this box (no graphics stack, no RT cores); "
                     "timed its CPU path: the C restatement of its shader math"}
 
@@ -458,7 +645,7 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="lmhead")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="decode2b")
     ap.add_argument("--history", type=int, default=32768)
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--min-seconds", type=float, default=1.0,
@@ -474,7 +661,7 @@ def main():
             print(json.dumps(line), flush=True)
         return
     world, rank, local = dist_setup(args.gpus)
-    line = run_ours(args, world, rank, local)
+    line = run_decode(args, world, rank, local) if args.workload == "decode2b" else run_ours(args, world, rank, local)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -121,6 +121,66 @@ RTA_API rta_status rta_attention_decode_f16(const float* q, const void* k, const
  * (0 = clean); synchronizes `stream`. */
 RTA_API rta_status rta_workspace_error(const void* workspace, size_t workspace_bytes, void* stream, uint32_t* error_word);
 
+
+/* ------------------------------------------------------------ 2. resident model */
+
+/* Model geometry: the fields of the compiler's ModelSpec
+ * (ray_tracing/compiler/spec.py:9-26), normally read from model.json.
+ * layer_kinds[l] = 1 for a full-attention layer, 2 for a recurrent layer. */
+typedef struct rta_model_spec {
+  uint32_t hidden_size, middle_size, vocabulary_size, depth;
+  uint32_t attention_heads, kv_heads, attention_head_dim, rotary_dim;
+  uint32_t state_heads, state_key_heads, state_head_dim;
+  uint32_t attention_gate, qk_norm;
+  float rope_theta, norm_epsilon;
+  uint8_t layer_kinds[256];
+} rta_model_spec;
+
+typedef struct rta_model rta_model;
+
+/* Text of the last rta_model_* error on this thread. */
+RTA_API const char* rta_model_last_error(void);
+
+/* Open a model from the exporter's payloads (ray_tracing/compiler/export.py:136-138):
+ * params = the parameter words of optical_model.bin (after its 44-byte header),
+ * matrices = geometry_weights.bin, basis = vocabulary.bin after its 16-byte
+ * header.  Pointers may be host or device memory; the handle copies them to
+ * `device` and owns all device memory from then on.  Replaces the worker
+ * constructor Resident::Resident (optical_resident.cpp:118-220). */
+RTA_API rta_status rta_model_open(const rta_model_spec* spec, const uint32_t* params, size_t n_params,
+                                  const void* matrices, size_t matrix_bytes, const void* basis, size_t basis_bytes,
+                                  uint32_t capacity, int device, rta_model** out);
+/* Same, reading the three payload files. */
+RTA_API rta_status rta_model_open_files(const rta_model_spec* spec, const char* optical_model_bin,
+                                        const char* geometry_bin, const char* vocabulary_bin, uint32_t capacity,
+                                        int device, rta_model** out);
+RTA_API void rta_model_close(rta_model* model);
+
+/* Prefill a fresh sequence with n prompt ids (positions 0..n-1); stops[2] are
+ * the stop ids of the following generate calls.  Worker op 1
+ * (Resident::prefill, optical_resident.cpp:609-712). */
+RTA_API rta_status rta_model_prefill(rta_model* model, const uint32_t* ids, uint32_t n, const uint32_t stops[2],
+                                     double* gpu_ms);
+/* Greedy decode of up to `count` tokens (readout -> argmax -> embedding ->
+ * layers per token), stopping after a stop id.  Worker op 2
+ * (Resident::generatePacket, optical_resident.cpp:760-871). */
+RTA_API rta_status rta_model_generate(rta_model* model, uint32_t count, uint32_t* ids, uint32_t* n_out,
+                                      double* gpu_ms);
+/* MLP diagnostic, worker op 6 (mlpCheck, optical_resident.cpp:922-949):
+ * y = W_down swiglu(W_gate x, W_up x), rows 1..32, host buffers. */
+RTA_API rta_status rta_model_mlp(rta_model* model, uint32_t layer, const float* x, uint32_t rows, float* y,
+                                 float* act);
+/* Vocabulary diagnostic, worker op 4 (wordCheck, optical_resident.cpp:889-906):
+ * argmax (ties -> lowest id) of the readout of `hidden`; logits may be NULL. */
+RTA_API rta_status rta_model_vocabulary(rta_model* model, const float* hidden, float* logits, uint32_t* argmax,
+                                        float* best);
+/* Current residual state (hidden_size floats) and absolute position. */
+RTA_API rta_status rta_model_state(rta_model* model, float* state, uint32_t* position);
+/* Resource counters, worker op 8: payload bytes, derived layer bytes, KV bytes,
+ * recurrent state bytes, capacity, attention splits, kernels per decode step,
+ * kernels per prefill step, position. */
+RTA_API rta_status rta_model_resources(rta_model* model, uint64_t* out, size_t n);
+
 #ifdef __cplusplus
 }
 #endif

@@ -55,6 +55,7 @@ def lib():
             "rta_oracle_head_norm": (None, [p, p, u32, u32, f]),
             "rta_oracle_sigmoid": (f, [f]),
             "rta_oracle_threads": (i32, []),
+            "rta_oracle_inv_freq": (None, [f, u32, u32, p]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(_lib, name)
@@ -167,6 +168,12 @@ def head_norm(v, w, heads: int, hd: int, eps: float):
     v = _c(v, np.float32).copy()
     lib().rta_oracle_head_norm(_p(v), _p(_c(w, np.float32)), heads, hd, eps)
     return v
+
+
+def inv_freq(theta: float, rotary: int, hd: int) -> np.ndarray:
+    out = np.zeros(hd // 2, np.float32)
+    lib().rta_oracle_inv_freq(theta, rotary, hd, _p(out))
+    return out
 
 
 def sigmoid(x: float) -> float:

@@ -77,6 +77,7 @@ __global__ void __launch_bounds__(kThreads) attention_split_kernel(const AttnPar
   __syncthreads();
   pdl_wait();
   pdl_launch_dependents();
+  if (p.running && *p.running == 0u) return;
 
   uint32_t t, lo, n;
   window(p, z, t, lo, n);
@@ -275,6 +276,7 @@ __global__ void __launch_bounds__(kThreads) attention_split_kernel(const AttnPar
 __global__ void __launch_bounds__(kHD) attention_merge_kernel(const AttnParams p, uint32_t nsplit) {
   pdl_wait();
   pdl_launch_dependents();
+  if (p.running && *p.running == 0u) return;
   const uint32_t head = blockIdx.x, z = blockIdx.y, d = threadIdx.x;
   const uint32_t kv = head / kGroup, h = head % kGroup;
   const size_t rec0 = (static_cast<size_t>(z) * p.kvh + kv) * nsplit;

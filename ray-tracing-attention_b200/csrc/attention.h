@@ -28,6 +28,7 @@ struct AttnParams {
   float* part_z = nullptr;
   float* part_o = nullptr;       // [nseq][kvh][nsplit][4][hd]
   uint32_t* err = nullptr;
+  const uint32_t* running = nullptr;  // optional: 0 -> skip (generation stopped)
 };
 
 size_t attention_smem_bytes();

@@ -1,0 +1,857 @@
+// engine.cu -- the resident decode engine behind the rta_model_* C-ABI.
+//
+// It owns one model on one GPU: the exporter's three payloads
+// (optical_model.bin parameters, geometry_weights.bin matrices and
+// vocabulary.bin rows; ray_tracing/compiler/export.py:51-150) copied to HBM,
+// load-time row gathers that turn the reference's row modes 1/2/3
+// (resident_quant.glsl:21-27) into plain row-major matrices, fp16 K/V rings,
+// recurrent states, and two CUDA graphs: one decode step (readout -> argmax ->
+// embedding -> layers, the per-token loop of Resident::generatePacket,
+// optical_resident.cpp:825-828) and one prefill step (prompt token ->
+// embedding -> layers).  Positions, the running flag and emitted ids live in a
+// device control block, so the graphs replay unchanged step after step.
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "../../include/rta.h"
+#include "attention.h"
+#include "layers.h"
+#include "rta_internal.h"
+
+namespace rta {
+namespace {
+
+thread_local std::string g_model_error = "no error";
+
+struct Failure {
+  rta_status code;
+  std::string msg;
+};
+#define RTA_CUDA(call)                                                                                     \
+  do {                                                                                                     \
+    cudaError_t e_ = (call);                                                                               \
+    if (e_ != cudaSuccess) throw ::rta::Failure{RTA_E_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_)}; \
+  } while (0)
+
+inline void require(bool ok, const std::string& msg, rta_status code = RTA_E_ASSET) {
+  if (!ok) throw Failure{code, msg};
+}
+
+template <class T>
+struct DevBuf {
+  T* p = nullptr;
+  size_t n = 0;
+  void alloc(size_t count) {
+    n = count;
+    RTA_CUDA(cudaMalloc(&p, std::max<size_t>(1, count) * sizeof(T)));
+  }
+  void zero(cudaStream_t s) { RTA_CUDA(cudaMemsetAsync(p, 0, std::max<size_t>(1, n) * sizeof(T), s)); }
+  ~DevBuf() {
+    if (p) cudaFree(p);
+  }
+};
+
+struct Layer {
+  bool full = true;
+  uint32_t fi = 0, ri = 0;
+  const float* attn_norm = nullptr;
+  const float* post_norm = nullptr;
+  // full attention
+  DevBuf<uint8_t> qkvg;  // [q | k | v | gate] rows, internal (rotary-paired) order
+  int qkvg_fmt = kQ4K;
+  uint32_t qkvg_rows = 0;
+  bool gated = false;
+  const uint8_t* o = nullptr;
+  int o_fmt = kQ4K;
+  uint32_t rotary_out = 0;  // o_proj mode 4: un-pair the attention output
+  const float* qnorm = nullptr;
+  const float* knorm = nullptr;
+  // recurrent
+  DevBuf<uint8_t> inproj;  // [q (K) | k (K) | v (S) | z (S)]
+  int inproj_fmt = kQ4K;
+  uint32_t inproj_rows = 0;
+  const uint8_t* out = nullptr;
+  int out_fmt = kQ4K;
+  const float *wa = nullptr, *wb = nullptr, *a_log = nullptr, *dt_bias = nullptr, *conv_w = nullptr,
+              *ssm_norm = nullptr;
+  // MLP
+  const uint8_t *gate = nullptr, *up = nullptr, *down = nullptr;
+  int mlp_fmt = kQ4K, down_fmt = kQ4K;
+};
+
+struct Engine {
+  rta_model_spec spec{};
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  uint32_t capacity = 0, nsplit = 1;
+  std::vector<uint32_t> hp;  // host copy of the parameter words
+  DevBuf<uint32_t> params;
+  DevBuf<uint8_t> matrices, basis;
+  std::vector<std::unique_ptr<Layer>> layers;
+  uint32_t n_full = 0, n_rec = 0;
+  const uint8_t* lm = nullptr;
+  int lm_fmt = kQ6K;
+  const uint8_t* embed = nullptr;
+  int embed_fmt = kQ6K;
+  const float* out_norm = nullptr;
+  // activations
+  DevBuf<float> state, proj, qproc, att, gdn, act, inv_freq, part_m, part_z, part_o, scratch_x, scratch_y;
+  DevBuf<__half> kcache, vcache;
+  DevBuf<float> rec, conv;
+  DevBuf<Control> ctrl;
+  DevBuf<uint32_t> prompt;
+  Control* ctrl_host = nullptr;  // pinned mirror
+  cudaGraphExec_t g_decode = nullptr, g_prefill = nullptr;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  uint32_t stops[2] = {0xffffffffu, 0xffffffffu};
+  uint32_t position = 0;
+  uint32_t kernels_per_decode = 0, kernels_per_prefill = 0;
+  double last_gpu_ms = 0.0;
+  uint64_t payload_bytes = 0;
+
+  uint32_t D() const { return spec.hidden_size; }
+  uint32_t Q() const { return spec.attention_heads * spec.attention_head_dim; }
+  uint32_t KVW() const { return spec.kv_heads * spec.attention_head_dim; }
+  uint32_t S() const { return spec.state_heads * spec.state_head_dim; }
+  uint32_t K() const { return spec.state_key_heads * 128u; }
+
+  ~Engine() {
+    if (g_decode) cudaGraphExecDestroy(g_decode);
+    if (g_prefill) cudaGraphExecDestroy(g_prefill);
+    if (ev0) cudaEventDestroy(ev0);
+    if (ev1) cudaEventDestroy(ev1);
+    if (ctrl_host) cudaFreeHost(ctrl_host);
+    if (stream) cudaStreamDestroy(stream);
+  }
+
+  uint32_t word(size_t i) const {
+    require(i < hp.size(), "parameter index out of range: " + std::to_string(i));
+    return hp[i];
+  }
+  const float* pf(uint32_t off, size_t count) const {
+    require(static_cast<size_t>(off) + count <= hp.size(), "parameter tensor out of range");
+    return reinterpret_cast<const float*>(params.p + off);
+  }
+  // descriptor i (0 q, 1 k, 2 o, 3 gate, 4 down, 5 up, 6 attn-gate/z, 8 v) of layer l
+  struct Desc {
+    const uint8_t* ptr;
+    int fmt, mode;
+  };
+  Desc desc(uint32_t l, uint32_t i, size_t rows, size_t cols) const {
+    const uint32_t base = 32u + l * 64u;
+    const uint32_t field = i == 8u ? base + 32u : base + 9u + 2u * i;
+    const uint32_t at = word(base + 27u) + word(field), meta = word(field + 1u);
+    Desc d{matrices.p + static_cast<size_t>(at) * 4u, static_cast<int>(meta & 255u), static_cast<int>(meta >> 8)};
+    size_t bytes = 0;
+    if (d.fmt == kQ4K || d.fmt == kQ6K) bytes = rows * cols / 256 * block_bytes(d.fmt);
+    else if (d.fmt == kF32) bytes = rows * cols * 4;
+    else throw Failure{RTA_E_ASSET, "layer " + std::to_string(l) + " descriptor " + std::to_string(i) +
+                                        ": coefficient format " + std::to_string(d.fmt) + " not supported"};
+    require(static_cast<size_t>(at) * 4u + bytes <= matrices.n, "matrix descriptor beyond geometry_weights");
+    return d;
+  }
+  uint32_t orig_axis(uint32_t a) const {
+    const uint32_t R = spec.rotary_dim;
+    return a < R ? (a % 2u) * (R / 2u) + a / 2u : a;
+  }
+  uint32_t src_row(int mode, uint32_t r) const {
+    const uint32_t hd = spec.attention_head_dim;
+    switch (mode) {
+      case 1: return (r / hd) * (2u * hd) + orig_axis(r % hd);
+      case 2: return (r / hd) * (2u * hd) + hd + orig_axis(r % hd);
+      case 3: return (r / hd) * hd + orig_axis(r % hd);
+      case 5: return r % (spec.state_key_heads * 128u);
+      default: return r;
+    }
+  }
+  void gather(uint8_t* dst, const Desc& d, uint32_t rows, uint32_t row_bytes, int mode) {
+    std::vector<uint32_t> map(rows);
+    for (uint32_t r = 0; r < rows; ++r) map[r] = src_row(mode, r);
+    DevBuf<uint32_t> dmap;
+    dmap.alloc(rows);
+    RTA_CUDA(cudaMemcpyAsync(dmap.p, map.data(), rows * 4u, cudaMemcpyHostToDevice, stream));
+    RTA_CUDA(launch_gather_rows(d.ptr, dmap.p, rows, row_bytes, dst, stream));
+    RTA_CUDA(cudaStreamSynchronize(stream));
+  }
+
+  void load(const rta_model_spec& sp, const uint32_t* prm, size_t n_params, const void* mat, size_t matrix_bytes,
+            const void* bas, size_t basis_bytes, uint32_t cap, int dev) {
+    spec = sp;
+    device = dev;
+    require(spec.depth >= 1 && spec.depth <= 256, "depth must be 1..256", RTA_E_ARG);
+    require(spec.hidden_size % 256 == 0 && spec.middle_size % 256 == 0, "hidden/middle must be multiples of 256",
+            RTA_E_ARG);
+    require(spec.attention_head_dim == 256 && spec.attention_heads == 4 * spec.kv_heads,
+            "this build serves head_dim 256 with 4 query heads per KV head", RTA_E_ARG);
+    require(spec.state_head_dim == 128 && spec.state_heads % std::max(1u, spec.state_key_heads) == 0,
+            "recurrent heads must be 128 wide", RTA_E_ARG);
+    require(spec.rotary_dim % 2 == 0 && spec.rotary_dim <= spec.attention_head_dim, "bad rotary_dim", RTA_E_ARG);
+    require(cap >= 1, "capacity must be positive", RTA_E_ARG);
+    capacity = cap;
+    RTA_CUDA(cudaSetDevice(device));
+    RTA_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+    RTA_CUDA(cudaEventCreate(&ev0));
+    RTA_CUDA(cudaEventCreate(&ev1));
+    hp.assign(prm, prm + n_params);
+    require(n_params >= 32 + 64ull * spec.depth, "parameter table too short");
+    require(hp[0] == spec.depth && hp[2] == spec.middle_size, "parameter header does not match the model spec");
+    params.alloc(n_params);
+    RTA_CUDA(cudaMemcpyAsync(params.p, prm, n_params * 4, cudaMemcpyDefault, stream));
+    matrices.alloc(matrix_bytes);
+    RTA_CUDA(cudaMemcpyAsync(matrices.p, mat, matrix_bytes, cudaMemcpyDefault, stream));
+    basis.alloc(basis_bytes);
+    RTA_CUDA(cudaMemcpyAsync(basis.p, bas, basis_bytes, cudaMemcpyDefault, stream));
+    RTA_CUDA(cudaStreamSynchronize(stream));
+    payload_bytes = n_params * 4ull + matrix_bytes + basis_bytes;
+
+    const uint32_t D = this->D(), hd = spec.attention_head_dim;
+    out_norm = pf(word(4), D);
+    embed_fmt = static_cast<int>(word(13));
+    lm_fmt = static_cast<int>(word(15));
+    require((embed_fmt == kQ4K || embed_fmt == kQ6K) && (lm_fmt == kQ4K || lm_fmt == kQ6K),
+            "token embedding and output rows must be Q4_K or Q6_K");
+    const size_t row_e = D / 256 * block_bytes(embed_fmt), row_l = D / 256 * block_bytes(lm_fmt);
+    require(static_cast<size_t>(word(14)) * 4 + row_e * spec.vocabulary_size <= basis_bytes, "token_embd out of range");
+    require(static_cast<size_t>(word(16)) * 4 + row_l * spec.vocabulary_size <= basis_bytes, "output rows out of range");
+    require(spec.vocabulary_size % 16 == 0, "vocabulary must be a multiple of 16 rows");
+    embed = basis.p + static_cast<size_t>(word(14)) * 4;
+    lm = basis.p + static_cast<size_t>(word(16)) * 4;
+
+    for (uint32_t l = 0; l < spec.depth; ++l) {
+      auto L = std::make_unique<Layer>();
+      const uint32_t base = 32u + l * 64u;
+      L->full = word(base + 26u) == 1u;
+      require(L->full == (spec.layer_kinds[l] == 1), "layer kind disagrees with the parameter table");
+      L->attn_norm = pf(word(base), D);
+      L->post_norm = pf(word(base + 1u), D);
+      if (L->full) {
+        L->fi = n_full++;
+        const uint32_t Qw = Q(), KV = KVW();
+        L->gated = spec.attention_gate != 0;
+        Desc dq = desc(l, 0, static_cast<size_t>(Qw) * (L->gated ? 2 : 1), D);
+        Desc dk = desc(l, 1, KV, D), dv = desc(l, 8, KV, D);
+        Desc dg = L->gated ? desc(l, 6, static_cast<size_t>(Qw) * 2, D) : dq;
+        require(dq.fmt == dk.fmt && dq.fmt == dv.fmt && (dq.fmt == kQ4K || dq.fmt == kQ6K),
+                "q/k/v projections must share one packed format");
+        L->qkvg_fmt = dq.fmt;
+        const uint32_t rb = D / 256 * block_bytes(dq.fmt);
+        L->qkvg_rows = Qw + 2 * KV + (L->gated ? Qw : 0);
+        L->qkvg.alloc(static_cast<size_t>(L->qkvg_rows) * rb);
+        gather(L->qkvg.p, dq, Qw, rb, dq.mode);
+        gather(L->qkvg.p + static_cast<size_t>(Qw) * rb, dk, KV, rb, dk.mode);
+        gather(L->qkvg.p + static_cast<size_t>(Qw + KV) * rb, dv, KV, rb, dv.mode);
+        if (L->gated) gather(L->qkvg.p + static_cast<size_t>(Qw + 2 * KV) * rb, dg, Qw, rb, dg.mode);
+        Desc dO = desc(l, 2, D, Qw);
+        L->o = dO.ptr;
+        L->o_fmt = dO.fmt;
+        L->rotary_out = dO.mode == 4 ? spec.rotary_dim : 0u;
+        L->qnorm = pf(word(base + 24u), Qw);
+        L->knorm = pf(word(base + 25u), Qw);
+        require(word(base + 29u) == spec.rotary_dim, "per-layer rotary_dim disagrees with the spec");
+      } else {
+        L->ri = n_rec++;
+        const uint32_t Kw = K(), Sw = S(), H = spec.state_heads;
+        Desc dqkv = desc(l, 0, 2ull * Kw + Sw, D);
+        Desc dz = desc(l, 6, Sw, D);
+        require(dqkv.fmt == dz.fmt && (dqkv.fmt == kQ4K || dqkv.fmt == kQ6K),
+                "recurrent qkv and gate projections must share one packed format");
+        const uint32_t rb = D / 256 * block_bytes(dqkv.fmt);
+        L->inproj_fmt = dqkv.fmt;
+        L->inproj_rows = 2 * Kw + 2 * Sw;
+        L->inproj.alloc(static_cast<size_t>(L->inproj_rows) * rb);
+        RTA_CUDA(cudaMemcpyAsync(L->inproj.p, dqkv.ptr, static_cast<size_t>(2 * Kw + Sw) * rb,
+                                 cudaMemcpyDeviceToDevice, stream));
+        RTA_CUDA(cudaMemcpyAsync(L->inproj.p + static_cast<size_t>(2 * Kw + Sw) * rb, dz.ptr,
+                                 static_cast<size_t>(Sw) * rb, cudaMemcpyDeviceToDevice, stream));
+        Desc dO = desc(l, 2, D, Sw);
+        L->out = dO.ptr;
+        L->out_fmt = dO.fmt;
+        const uint32_t at_b = word(base + 27u) + word(base + 35u), at_a = word(base + 27u) + word(base + 36u);
+        require((word(base + 39u) & 255u) == kF32 && (word(base + 40u) & 255u) == kF32,
+                "recurrent alpha/beta projections must be F32 in this build");
+        require((static_cast<size_t>(std::max(at_a, at_b)) * 4 + static_cast<size_t>(H) * D * 4) <= matrices.n,
+                "alpha/beta beyond geometry_weights");
+        L->wa = reinterpret_cast<const float*>(matrices.p + static_cast<size_t>(at_a) * 4);
+        L->wb = reinterpret_cast<const float*>(matrices.p + static_cast<size_t>(at_b) * 4);
+        L->dt_bias = pf(word(base + 37u), H);
+        L->a_log = pf(word(base + 38u), H);
+        L->conv_w = pf(word(base + 34u), 3ull * Sw * 4);
+        L->ssm_norm = pf(word(base + 31u), Sw);
+      }
+      Desc dg = desc(l, 3, spec.middle_size, D), du = desc(l, 5, spec.middle_size, D),
+           dd = desc(l, 4, D, spec.middle_size);
+      require(dg.fmt == du.fmt && (dg.fmt == kQ4K || dg.fmt == kQ6K) && (dd.fmt == kQ4K || dd.fmt == kQ6K),
+              "MLP projections must be Q4_K / Q6_K (gate and up alike)");
+      L->gate = dg.ptr;
+      L->up = du.ptr;
+      L->down = dd.ptr;
+      L->mlp_fmt = dg.fmt;
+      L->down_fmt = dd.fmt;
+      layers.push_back(std::move(L));
+    }
+    RTA_CUDA(cudaStreamSynchronize(stream));
+
+    // activations and state
+    const uint32_t projw = std::max(Q() + 2 * KVW() + Q(), 2 * K() + 2 * S());
+    state.alloc(D);
+    proj.alloc(projw);
+    qproc.alloc(Q());
+    att.alloc(Q());
+    gdn.alloc(std::max(1u, S()));
+    act.alloc(spec.middle_size);
+    scratch_x.alloc(32ull * std::max(D, spec.middle_size));
+    scratch_y.alloc(32ull * std::max(D, spec.middle_size));
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    nsplit = std::max(1u, std::min(static_cast<uint32_t>(sms) / spec.kv_heads, capacity / 256u));
+    const size_t recs = static_cast<size_t>(spec.kv_heads) * nsplit * 4;
+    part_m.alloc(recs);
+    part_z.alloc(recs);
+    part_o.alloc(recs * hd);
+    kcache.alloc(static_cast<size_t>(std::max(1u, n_full)) * spec.kv_heads * capacity * hd);
+    vcache.alloc(kcache.n);
+    rec.alloc(static_cast<size_t>(std::max(1u, n_rec)) * spec.state_heads * 128 * 128);
+    conv.alloc(static_cast<size_t>(std::max(1u, n_rec)) * 2 * 3 * S() * 3);
+    ctrl.alloc(1);
+    prompt.alloc(capacity);
+    RTA_CUDA(cudaMallocHost(&ctrl_host, sizeof(Control)));
+    std::vector<float> freq(hd / 2, 0.f);
+    for (uint32_t p = 0; p < spec.rotary_dim / 2u; ++p)
+      freq[p] = std::pow(spec.rope_theta, -static_cast<float>(p) / static_cast<float>(spec.rotary_dim / 2u));
+    inv_freq.alloc(hd / 2);
+    RTA_CUDA(cudaMemcpyAsync(inv_freq.p, freq.data(), freq.size() * 4, cudaMemcpyHostToDevice, stream));
+    reset_sequence();
+    capture();
+  }
+
+  void reset_sequence() {
+    ctrl.zero(stream);
+    rec.zero(stream);
+    conv.zero(stream);
+    state.zero(stream);
+    position = 0;
+    RTA_CUDA(cudaStreamSynchronize(stream));
+  }
+
+  // ---------------------------------------------------------- step recording
+  uint32_t record_step(bool decode) {
+    const cudaStream_t s = stream;
+    uint32_t n = 0;
+    Control* c = ctrl.p;
+    const uint32_t* running = &c->running;
+    const uint32_t D = this->D(), F = spec.middle_size, hd = spec.attention_head_dim;
+    if (decode) {
+      GemvArgs r;
+      r.fmt = lm_fmt;
+      r.w0 = lm;
+      r.rows = spec.vocabulary_size;
+      r.cols = D;
+      r.x = state.p;
+      r.prologue = kRmsNorm;
+      r.norm_w = out_norm;
+      r.eps = spec.norm_epsilon;
+      r.argmax = &c->argkey;
+      r.err = &c->err;
+      r.running = running;
+      r.pdl = true;
+      RTA_CUDA(launch_gemv(r, s));
+      ++n;
+    }
+    EmbedParams e;
+    e.table = embed;
+    e.fmt = embed_fmt;
+    e.D = D;
+    e.row_bytes = D / 256 * block_bytes(embed_fmt);
+    e.vocab = spec.vocabulary_size;
+    e.ctrl = c;
+    e.prompt = prompt.p;
+    e.mode = decode ? kEmbedDecode : kEmbedPrefill;
+    e.state = state.p;
+    RTA_CUDA(launch_embed(e, s, true));
+    ++n;
+    for (auto& Lp : layers) {
+      Layer& L = *Lp;
+      if (L.full) {
+        GemvArgs g;
+        g.fmt = L.qkvg_fmt;
+        g.w0 = L.qkvg.p;
+        g.rows = L.qkvg_rows;
+        g.cols = D;
+        g.x = state.p;
+        g.prologue = kRmsNorm;
+        g.norm_w = L.attn_norm;
+        g.eps = spec.norm_epsilon;
+        g.y = proj.p;
+        g.running = running;
+        g.err = &c->err;
+        g.pdl = true;
+        RTA_CUDA(launch_gemv(g, s));
+        PrepParams pp;
+        pp.qkvg = proj.p;
+        pp.qnorm = L.qnorm;
+        pp.knorm = L.knorm;
+        pp.inv_freq = inv_freq.p;
+        pp.eps = spec.norm_epsilon;
+        pp.heads = spec.attention_heads;
+        pp.kvh = spec.kv_heads;
+        pp.hd = hd;
+        pp.group = spec.attention_heads / spec.kv_heads;
+        pp.rotary = spec.rotary_dim;
+        pp.qk_norm = spec.qk_norm;
+        pp.q_width = Q();
+        pp.kv_width = KVW();
+        pp.qout = qproc.p;
+        const size_t layer_kv = static_cast<size_t>(spec.kv_heads) * capacity * hd;
+        pp.kcache = kcache.p + L.fi * layer_kv;
+        pp.vcache = vcache.p + L.fi * layer_kv;
+        pp.capacity = capacity;
+        pp.pos = &c->pos_cur;
+        pp.running = running;
+        RTA_CUDA(launch_attn_prep(pp, s, true));
+        AttnParams ap;
+        ap.q = qproc.p;
+        ap.k = pp.kcache;
+        ap.v = pp.vcache;
+        ap.kv_stride = static_cast<size_t>(capacity) * hd;
+        ap.pos_stride = hd;
+        ap.heads = spec.attention_heads;
+        ap.kvh = spec.kv_heads;
+        ap.hd = hd;
+        ap.capacity = capacity;
+        ap.pos = &c->pos_cur;
+        ap.gate = L.gated ? proj.p + Q() + 2 * KVW() : nullptr;
+        ap.out = att.p;
+        ap.rotary_out = L.rotary_out;
+        ap.part_m = part_m.p;
+        ap.part_z = part_z.p;
+        ap.part_o = part_o.p;
+        ap.err = &c->err;
+        ap.running = running;
+        RTA_CUDA(launch_attention(ap, nsplit, 1, true, s));
+        GemvArgs o;
+        o.fmt = L.o_fmt;
+        o.w0 = L.o;
+        o.rows = D;
+        o.cols = Q();
+        o.x = att.p;
+        o.epilogue = kAccumulate;
+        o.y = state.p;
+        o.running = running;
+        o.err = &c->err;
+        o.pdl = true;
+        RTA_CUDA(launch_gemv(o, s));
+        n += 5;
+      } else {
+        GemvArgs g;
+        g.fmt = L.inproj_fmt;
+        g.w0 = L.inproj.p;
+        g.rows = L.inproj_rows;
+        g.cols = D;
+        g.x = state.p;
+        g.prologue = kRmsNorm;
+        g.norm_w = L.attn_norm;
+        g.eps = spec.norm_epsilon;
+        g.y = proj.p;
+        g.running = running;
+        g.err = &c->err;
+        g.pdl = true;
+        RTA_CUDA(launch_gemv(g, s));
+        GdnParams gp;
+        gp.x = state.p;
+        gp.attn_norm = L.attn_norm;
+        gp.eps = spec.norm_epsilon;
+        gp.wa = L.wa;
+        gp.wb = L.wb;
+        gp.a_log = L.a_log;
+        gp.dt_bias = L.dt_bias;
+        gp.proj = proj.p;
+        gp.conv_w = L.conv_w;
+        gp.conv_state = conv.p + static_cast<size_t>(L.ri) * 2 * 3 * S() * 3;
+        gp.rec = rec.p + static_cast<size_t>(L.ri) * spec.state_heads * 128 * 128;
+        gp.out = gdn.p;
+        gp.D = D;
+        gp.H = spec.state_heads;
+        gp.KH = spec.state_key_heads;
+        gp.pos = &c->pos_cur;
+        gp.running = running;
+        RTA_CUDA(launch_gdn(gp, s, true));
+        GemvArgs o;
+        o.fmt = L.out_fmt;
+        o.w0 = L.out;
+        o.rows = D;
+        o.cols = S();
+        o.x = gdn.p;
+        o.prologue = kHeadGate;
+        o.z = proj.p + 2 * K() + S();
+        o.norm_w = L.ssm_norm;
+        o.eps = spec.norm_epsilon;
+        o.epilogue = kAccumulate;
+        o.y = state.p;
+        o.running = running;
+        o.err = &c->err;
+        o.pdl = true;
+        RTA_CUDA(launch_gemv(o, s));
+        n += 3;
+      }
+      GemvArgs gu;
+      gu.fmt = L.mlp_fmt;
+      gu.w0 = L.gate;
+      gu.w1 = L.up;
+      gu.rows = F;
+      gu.cols = D;
+      gu.x = state.p;
+      gu.prologue = kRmsNorm;
+      gu.norm_w = L.post_norm;
+      gu.eps = spec.norm_epsilon;
+      gu.epilogue = kSwiGLU;
+      gu.y = act.p;
+      gu.running = running;
+      gu.err = &c->err;
+      gu.pdl = true;
+      RTA_CUDA(launch_gemv(gu, s));
+      GemvArgs dn;
+      dn.fmt = L.down_fmt;
+      dn.w0 = L.down;
+      dn.rows = D;
+      dn.cols = F;
+      dn.x = act.p;
+      dn.epilogue = kAccumulate;
+      dn.y = state.p;
+      dn.running = running;
+      dn.err = &c->err;
+      dn.pdl = true;
+      RTA_CUDA(launch_gemv(dn, s));
+      n += 2;
+    }
+    return n;
+  }
+
+  void capture() {
+    for (int mode = 0; mode < 2; ++mode) {
+      cudaGraph_t graph = nullptr;
+      RTA_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeRelaxed));
+      uint32_t n = 0;
+      try {
+        n = record_step(mode == 1);
+      } catch (...) {
+        cudaStreamEndCapture(stream, &graph);
+        if (graph) cudaGraphDestroy(graph);
+        throw;
+      }
+      RTA_CUDA(cudaStreamEndCapture(stream, &graph));
+      cudaGraphExec_t exec = nullptr;
+      const cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
+      cudaGraphDestroy(graph);
+      RTA_CUDA(e);
+      if (mode == 1) {
+        g_decode = exec;
+        kernels_per_decode = n;
+      } else {
+        g_prefill = exec;
+        kernels_per_prefill = n;
+      }
+    }
+  }
+
+  void read_control() {
+    RTA_CUDA(cudaMemcpyAsync(ctrl_host, ctrl.p, sizeof(Control), cudaMemcpyDeviceToHost, stream));
+    RTA_CUDA(cudaStreamSynchronize(stream));
+    if (ctrl_host->err & RTA_DEVERR_TIMEOUT) throw Failure{RTA_E_TIMEOUT, "device-side wait exceeded its bound"};
+    if (ctrl_host->err)
+      throw Failure{RTA_E_DEVICE_CHECK, "device error word " + std::to_string(ctrl_host->err)};
+  }
+
+  void prefill(const uint32_t* ids, uint32_t n, const uint32_t st[2]) {
+    require(n >= 1 && n <= capacity, "prefill length must be 1..capacity", RTA_E_ARG);
+    for (uint32_t i = 0; i < n; ++i) require(ids[i] < spec.vocabulary_size, "token id beyond the vocabulary", RTA_E_ARG);
+    stops[0] = st ? st[0] : 0xffffffffu;
+    stops[1] = st ? st[1] : 0xffffffffu;
+    reset_sequence();
+    RTA_CUDA(cudaMemcpyAsync(prompt.p, ids, n * 4ull, cudaMemcpyHostToDevice, stream));
+    Control init{};
+    init.running = 1u;
+    init.stops[0] = stops[0];
+    init.stops[1] = stops[1];
+    RTA_CUDA(cudaMemcpyAsync(ctrl.p, &init, offsetof(Control, ids), cudaMemcpyHostToDevice, stream));
+    RTA_CUDA(cudaEventRecord(ev0, stream));
+    for (uint32_t i = 0; i < n; ++i) RTA_CUDA(cudaGraphLaunch(g_prefill, stream));
+    RTA_CUDA(cudaEventRecord(ev1, stream));
+    read_control();
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, ev0, ev1);
+    last_gpu_ms = ms;
+    position = ctrl_host->pos_next;
+  }
+
+  void generate(uint32_t count, uint32_t* ids_out, uint32_t* n_out) {
+    require(count >= 1 && count <= kMaxOut, "generate count must be 1..4096", RTA_E_ARG);
+    require(position > 0, "prefill before generate", RTA_E_STATE);
+    // running = 1, n_out = 0 (the pinned mirror holds the rest of the control block)
+    ctrl_host->running = 1u;
+    ctrl_host->n_out = 0u;
+    ctrl_host->stops[0] = stops[0];
+    ctrl_host->stops[1] = stops[1];
+    RTA_CUDA(cudaMemcpyAsync(&ctrl.p->running, &ctrl_host->running, 8, cudaMemcpyHostToDevice, stream));
+    RTA_CUDA(cudaMemcpyAsync(&ctrl.p->stops, &ctrl_host->stops, 8, cudaMemcpyHostToDevice, stream));
+    RTA_CUDA(cudaEventRecord(ev0, stream));
+    for (uint32_t i = 0; i < count; ++i) RTA_CUDA(cudaGraphLaunch(g_decode, stream));
+    RTA_CUDA(cudaEventRecord(ev1, stream));
+    read_control();
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, ev0, ev1);
+    last_gpu_ms = ms;
+    const uint32_t got = std::min(ctrl_host->n_out, count);
+    if (ids_out) std::memcpy(ids_out, ctrl_host->ids, got * 4ull);
+    if (n_out) *n_out = got;
+    position = ctrl_host->pos_next;
+  }
+
+  void mlp(uint32_t layer, const float* x, uint32_t rows, float* y, float* a) {
+    require(layer < spec.depth, "layer out of range", RTA_E_ARG);
+    require(rows >= 1 && rows <= 32, "MLP check supports 1..32 rows", RTA_E_ARG);
+    const uint32_t D = this->D(), F = spec.middle_size;
+    for (size_t i = 0; i < static_cast<size_t>(rows) * D; ++i)
+      require(std::isfinite(x[i]), "MLP input must be finite", RTA_E_ARG);
+    Layer& L = *layers[layer];
+    RTA_CUDA(cudaMemcpyAsync(scratch_x.p, x, static_cast<size_t>(rows) * D * 4, cudaMemcpyHostToDevice, stream));
+    for (uint32_t r0 = 0; r0 < rows; r0 += 8) {  // 8-row launches keep the activation tables in shared memory
+      const uint32_t nb = std::min(8u, rows - r0);
+      GemvArgs gu;
+      gu.fmt = L.mlp_fmt;
+      gu.w0 = L.gate;
+      gu.w1 = L.up;
+      gu.rows = F;
+      gu.cols = D;
+      gu.x = scratch_x.p + static_cast<size_t>(r0) * D;
+      gu.x_stride = D;
+      gu.batch = nb;
+      gu.epilogue = kSwiGLU;
+      gu.y = scratch_y.p + static_cast<size_t>(r0) * F;
+      gu.y_stride = F;
+      RTA_CUDA(launch_gemv(gu, stream));
+    }
+    RTA_CUDA(cudaMemcpyAsync(a, scratch_y.p, static_cast<size_t>(rows) * F * 4, cudaMemcpyDeviceToHost, stream));
+    for (uint32_t r0 = 0; r0 < rows; r0 += 8) {
+      const uint32_t nb = std::min(8u, rows - r0);
+      GemvArgs dn;
+      dn.fmt = L.down_fmt;
+      dn.w0 = L.down;
+      dn.rows = D;
+      dn.cols = F;
+      dn.x = scratch_y.p + static_cast<size_t>(r0) * F;
+      dn.x_stride = F;
+      dn.batch = nb;
+      dn.y = scratch_x.p + static_cast<size_t>(r0) * D;  // x no longer needed
+      dn.y_stride = D;
+      RTA_CUDA(launch_gemv(dn, stream));
+    }
+    RTA_CUDA(cudaMemcpyAsync(y, scratch_x.p, static_cast<size_t>(rows) * D * 4, cudaMemcpyDeviceToHost, stream));
+    RTA_CUDA(cudaStreamSynchronize(stream));
+  }
+
+  void vocabulary(const float* hidden, float* logits, uint32_t* argmax, float* best) {
+    const uint32_t D = this->D(), V = spec.vocabulary_size;
+    for (uint32_t i = 0; i < D; ++i) require(std::isfinite(hidden[i]), "vocabulary input must be finite", RTA_E_ARG);
+    RTA_CUDA(cudaMemcpyAsync(scratch_x.p, hidden, D * 4ull, cudaMemcpyHostToDevice, stream));
+    unsigned long long* key = reinterpret_cast<unsigned long long*>(scratch_y.p);
+    RTA_CUDA(cudaMemsetAsync(key, 0, 8, stream));
+    DevBuf<float> lg;
+    if (logits) lg.alloc(V);
+    GemvArgs r;
+    r.fmt = lm_fmt;
+    r.w0 = lm;
+    r.rows = V;
+    r.cols = D;
+    r.x = scratch_x.p;
+    r.y = logits ? lg.p : nullptr;
+    r.argmax = key;
+    RTA_CUDA(launch_gemv(r, stream));
+    unsigned long long k = 0;
+    RTA_CUDA(cudaMemcpyAsync(&k, key, 8, cudaMemcpyDeviceToHost, stream));
+    if (logits) RTA_CUDA(cudaMemcpyAsync(logits, lg.p, V * 4ull, cudaMemcpyDeviceToHost, stream));
+    RTA_CUDA(cudaStreamSynchronize(stream));
+    const uint32_t id = ~static_cast<uint32_t>(k & 0xffffffffu);
+    require(k != 0 && id < V, "readout produced no valid row", RTA_E_DEVICE_CHECK);
+    *argmax = id;
+    if (best) {
+      const uint32_t ok = static_cast<uint32_t>(k >> 32);
+      const uint32_t bits = (ok & 0x80000000u) ? (ok & 0x7fffffffu) : ~ok;
+      std::memcpy(best, &bits, 4);
+    }
+  }
+};
+
+rta_status fail_model(const Failure& f) {
+  g_model_error = f.msg;
+  return f.code;
+}
+
+bool read_file(const std::string& path, std::vector<char>& out) {
+  std::ifstream f(path, std::ios::binary | std::ios::ate);
+  if (!f) return false;
+  const std::streamsize n = f.tellg();
+  f.seekg(0);
+  out.resize(static_cast<size_t>(n));
+  return static_cast<bool>(f.read(out.data(), n));
+}
+
+}  // namespace
+}  // namespace rta
+
+struct rta_model {
+  rta::Engine engine;
+};
+
+extern "C" {
+
+const char* rta_model_last_error(void) { return rta::g_model_error.c_str(); }
+
+rta_status rta_model_open(const rta_model_spec* spec, const uint32_t* params, size_t n_params, const void* matrices,
+                          size_t matrix_bytes, const void* basis, size_t basis_bytes, uint32_t capacity, int device,
+                          rta_model** out) {
+  if (!spec || !params || !matrices || !basis || !out) {
+    rta::g_model_error = "rta_model_open: null argument";
+    return RTA_E_ARG;
+  }
+  *out = nullptr;
+  auto* m = new (std::nothrow) rta_model;
+  if (!m) return RTA_E_CUDA;
+  try {
+    m->engine.load(*spec, params, n_params, matrices, matrix_bytes, basis, basis_bytes, capacity, device);
+  } catch (const rta::Failure& f) {
+    delete m;
+    return rta::fail_model(f);
+  }
+  *out = m;
+  return RTA_OK;
+}
+
+rta_status rta_model_open_files(const rta_model_spec* spec, const char* optical_model_bin, const char* geometry_bin,
+                                const char* vocabulary_bin, uint32_t capacity, int device, rta_model** out) {
+  if (!spec || !optical_model_bin || !geometry_bin || !vocabulary_bin || !out) {
+    rta::g_model_error = "rta_model_open_files: null argument";
+    return RTA_E_ARG;
+  }
+  std::vector<char> model, geo, voc;
+  if (!rta::read_file(optical_model_bin, model) || !rta::read_file(geometry_bin, geo) ||
+      !rta::read_file(vocabulary_bin, voc)) {
+    rta::g_model_error = "cannot read the model payload files";
+    return RTA_E_ASSET;
+  }
+  // optical_model.bin: 'RTRES004' + <9I d, depth, depth, middle, V, 4, n_params, matrix_words, 0> + params
+  if (model.size() < 44 || std::memcmp(model.data(), "RTRES004", 8) != 0) {
+    rta::g_model_error = "optical_model.bin: bad magic";
+    return RTA_E_ASSET;
+  }
+  uint32_t hdr[9];
+  std::memcpy(hdr, model.data() + 8, sizeof hdr);
+  if (hdr[0] != spec->hidden_size || hdr[1] != spec->depth || hdr[3] != spec->middle_size ||
+      hdr[4] != spec->vocabulary_size || model.size() < 44 + static_cast<size_t>(hdr[6]) * 4 ||
+      geo.size() < static_cast<size_t>(hdr[7]) * 4) {
+    rta::g_model_error = "optical_model.bin header does not match the model spec or the payload sizes";
+    return RTA_E_ASSET;
+  }
+  // vocabulary.bin: 'RTBASQ01' + <2I V, D> + raw rows
+  uint32_t vh[2];
+  if (voc.size() < 16 || std::memcmp(voc.data(), "RTBASQ01", 8) != 0) {
+    rta::g_model_error = "vocabulary.bin: bad magic";
+    return RTA_E_ASSET;
+  }
+  std::memcpy(vh, voc.data() + 8, 8);
+  if (vh[0] != spec->vocabulary_size || vh[1] != spec->hidden_size) {
+    rta::g_model_error = "vocabulary.bin header does not match the model spec";
+    return RTA_E_ASSET;
+  }
+  return rta_model_open(spec, reinterpret_cast<const uint32_t*>(model.data() + 44), hdr[6], geo.data(),
+                        static_cast<size_t>(hdr[7]) * 4, voc.data() + 16, voc.size() - 16, capacity, device, out);
+}
+
+void rta_model_close(rta_model* m) { delete m; }
+
+rta_status rta_model_prefill(rta_model* m, const uint32_t* ids, uint32_t n, const uint32_t stops[2], double* gpu_ms) {
+  if (!m || !ids) return RTA_E_ARG;
+  try {
+    cudaSetDevice(m->engine.device);
+    m->engine.prefill(ids, n, stops);
+    if (gpu_ms) *gpu_ms = m->engine.last_gpu_ms;
+  } catch (const rta::Failure& f) {
+    return rta::fail_model(f);
+  }
+  return RTA_OK;
+}
+
+rta_status rta_model_generate(rta_model* m, uint32_t count, uint32_t* ids, uint32_t* n_out, double* gpu_ms) {
+  if (!m) return RTA_E_ARG;
+  try {
+    cudaSetDevice(m->engine.device);
+    m->engine.generate(count, ids, n_out);
+    if (gpu_ms) *gpu_ms = m->engine.last_gpu_ms;
+  } catch (const rta::Failure& f) {
+    return rta::fail_model(f);
+  }
+  return RTA_OK;
+}
+
+rta_status rta_model_mlp(rta_model* m, uint32_t layer, const float* x, uint32_t rows, float* y, float* act) {
+  if (!m || !x || !y || !act) return RTA_E_ARG;
+  try {
+    cudaSetDevice(m->engine.device);
+    m->engine.mlp(layer, x, rows, y, act);
+  } catch (const rta::Failure& f) {
+    return rta::fail_model(f);
+  }
+  return RTA_OK;
+}
+
+rta_status rta_model_vocabulary(rta_model* m, const float* hidden, float* logits, uint32_t* argmax, float* best) {
+  if (!m || !hidden || !argmax) return RTA_E_ARG;
+  try {
+    cudaSetDevice(m->engine.device);
+    m->engine.vocabulary(hidden, logits, argmax, best);
+  } catch (const rta::Failure& f) {
+    return rta::fail_model(f);
+  }
+  return RTA_OK;
+}
+
+rta_status rta_model_state(rta_model* m, float* state, uint32_t* position) {
+  if (!m || !state) return RTA_E_ARG;
+  try {
+    cudaSetDevice(m->engine.device);
+    RTA_CUDA(cudaMemcpyAsync(state, m->engine.state.p, m->engine.D() * 4ull, cudaMemcpyDeviceToHost,
+                             m->engine.stream));
+    RTA_CUDA(cudaStreamSynchronize(m->engine.stream));
+    if (position) *position = m->engine.position;
+  } catch (const rta::Failure& f) {
+    return rta::fail_model(f);
+  }
+  return RTA_OK;
+}
+
+rta_status rta_model_resources(rta_model* m, uint64_t* out, size_t n) {
+  if (!m || !out) return RTA_E_ARG;
+  const rta::Engine& e = m->engine;
+  size_t layer_bytes = 0;
+  for (auto& L : e.layers) layer_bytes += L->qkvg.n + L->inproj.n;
+  const uint64_t v[] = {
+      e.payload_bytes,
+      layer_bytes,
+      e.kcache.n * 2ull + e.vcache.n * 2ull,
+      e.rec.n * 4ull + e.conv.n * 4ull,
+      e.capacity,
+      e.nsplit,
+      e.kernels_per_decode,
+      e.kernels_per_prefill,
+      e.position,
+  };
+  for (size_t i = 0; i < n && i < sizeof(v) / sizeof(v[0]); ++i) out[i] = v[i];
+  return RTA_OK;
+}
+
+}  // extern "C"

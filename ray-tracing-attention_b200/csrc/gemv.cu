@@ -48,6 +48,7 @@ struct Params {
   uint32_t y_stride;
   unsigned long long* argmax;
   uint32_t* err;
+  const uint32_t* running;
   // shared-memory carve (byte offsets from the dynamic base)
   uint32_t off_bar, off_xq, off_xsc, off_scr, off_red, off_misc;
 };
@@ -184,6 +185,12 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const Params p) {
 
   pdl_wait();                 // activations (and residual target) are now visible
   pdl_launch_dependents();    // let the next kernel start streaming its weights
+  if (p.running && *p.running == 0u) {
+    // generation stopped: drain the stages already in flight and leave
+    if (threadIdx.x == 0)
+      for (uint32_t j = 0; j < issued; ++j) (void)mbar_wait(&bars[j % p.nstage], (j / p.nstage) & 1u, nullptr);
+    return;
+  }
   prepare_x<NSL>(p, smem);
 
   const uint32_t* xq = reinterpret_cast<const uint32_t*>(smem + p.off_xq);
@@ -530,6 +537,7 @@ cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t s) {
   p.y_stride = a.y_stride ? a.y_stride : a.rows;
   p.argmax = a.argmax;
   p.err = a.err;
+  p.running = a.running;
   const uint32_t nsl = (a.batch + 3) / 4;
   if (a.fmt == kQ4K) {
     if (nsl == 1) return launch_t<kQ4K, 1>(a, p, s);

@@ -1,0 +1,77 @@
+// layers.h -- parameter blocks of the per-token kernels in layers.cu.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace rta {
+
+constexpr uint32_t kMaxOut = 4096;  // token ids kept per generate call
+
+// Device-resident control block of one sequence (the role of the reference's
+// control[] words: token, count, running flag, stop ids, error word).
+struct Control {
+  unsigned long long argkey;    // packed (order key, ~id) written by the readout's atomicMax
+  unsigned long long best_key;  // last consumed key (winner value)
+  uint32_t pos_next;            // next absolute position to process
+  uint32_t pos_cur;             // position processed by the current step
+  uint32_t running;             // 1 while generating (0 after a stop id / error)
+  uint32_t n_out;               // ids emitted by this generate call
+  uint32_t stops[2];
+  uint32_t err;
+  uint32_t pad;
+  uint32_t ids[kMaxOut];
+};
+
+enum EmbedMode : int { kEmbedPrefill = 0, kEmbedDecode = 1 };
+struct EmbedParams {
+  const uint8_t* table = nullptr;  // token_embd rows (Q4_K / Q6_K)
+  int fmt = 14;
+  uint32_t D = 0, row_bytes = 0, vocab = 0;
+  Control* ctrl = nullptr;
+  const uint32_t* prompt = nullptr;  // prefill ids by absolute position
+  int mode = kEmbedDecode;
+  float* state = nullptr;
+};
+
+struct PrepParams {
+  const float* qkvg = nullptr;   // [q (heads*hd) | k (kvh*hd) | v (kvh*hd) | gate]
+  const float* qnorm = nullptr;  // [heads][hd]
+  const float* knorm = nullptr;  // [heads][hd] (tiled per query head)
+  const float* inv_freq = nullptr;
+  float eps = 1e-6f;
+  uint32_t heads = 16, kvh = 4, hd = 256, group = 4, rotary = 0, qk_norm = 1;
+  uint32_t q_width = 0, kv_width = 0;
+  float* qout = nullptr;
+  __half* kcache = nullptr;  // this layer: [kvh][capacity][hd]
+  __half* vcache = nullptr;
+  uint32_t capacity = 0;
+  const uint32_t* pos = nullptr;
+  const uint32_t* running = nullptr;
+};
+
+struct GdnParams {
+  const float* x = nullptr;          // residual stream [D] (input of the layer)
+  const float* attn_norm = nullptr;  // [D]
+  float eps = 1e-6f;
+  const float* wa = nullptr;         // [H][D] alpha projection (F32)
+  const float* wb = nullptr;         // [H][D] beta projection (F32)
+  const float* a_log = nullptr;      // [H]
+  const float* dt_bias = nullptr;    // [H]
+  const float* proj = nullptr;       // [q (K) | k (K) | v (S) | z (S)] raw projections
+  const float* conv_w = nullptr;     // [3S][4]
+  float* conv_state = nullptr;       // [2][3S][3] double-buffered by position parity
+  float* rec = nullptr;              // [H][128][128] (value, key)
+  float* out = nullptr;              // [S] detector output (before the gated norm)
+  uint32_t D = 0, H = 0, KH = 0;
+  const uint32_t* pos = nullptr;
+  const uint32_t* running = nullptr;
+};
+
+cudaError_t launch_embed(const EmbedParams& p, cudaStream_t s, bool pdl);
+cudaError_t launch_attn_prep(const PrepParams& p, cudaStream_t s, bool pdl);
+cudaError_t launch_gdn(const GdnParams& p, cudaStream_t s, bool pdl);
+cudaError_t launch_gather_rows(const uint8_t* src, const uint32_t* map, uint32_t rows, uint32_t row_bytes,
+                               uint8_t* dst, cudaStream_t s);
+
+}  // namespace rta

@@ -53,6 +53,7 @@ struct GemvArgs {
   // optional argmax over the rows of batch row b (vocabulary readout):
   unsigned long long* argmax = nullptr;  // [batch] packed (order key, ~id); null = none
   uint32_t* err = nullptr;               // device error word (may be null)
+  const uint32_t* running = nullptr;     // optional device flag: 0 -> skip (generation stopped)
   bool pdl = false;                      // launch with programmatic stream serialization
 };
 cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t s);

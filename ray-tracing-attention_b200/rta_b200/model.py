@@ -1,0 +1,188 @@
+"""ResidentModel: Python handle over the rta_model_* C-ABI (one model, one GPU)."""
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+import numpy as np
+
+from . import _lib, assets
+
+
+class ModelSpecC(ctypes.Structure):
+    """Mirror of rta_model_spec (include/rta.h)."""
+    _fields_ = [("hidden_size", ctypes.c_uint32), ("middle_size", ctypes.c_uint32),
+                ("vocabulary_size", ctypes.c_uint32), ("depth", ctypes.c_uint32),
+                ("attention_heads", ctypes.c_uint32), ("kv_heads", ctypes.c_uint32),
+                ("attention_head_dim", ctypes.c_uint32), ("rotary_dim", ctypes.c_uint32),
+                ("state_heads", ctypes.c_uint32), ("state_key_heads", ctypes.c_uint32),
+                ("state_head_dim", ctypes.c_uint32), ("attention_gate", ctypes.c_uint32),
+                ("qk_norm", ctypes.c_uint32), ("rope_theta", ctypes.c_float), ("norm_epsilon", ctypes.c_float),
+                ("layer_kinds", ctypes.c_uint8 * 256)]
+
+    @classmethod
+    def from_spec(cls, s: assets.Spec) -> "ModelSpecC":
+        c = cls(s.hidden_size, s.middle_size, s.vocabulary_size, s.depth, s.attention_heads, s.kv_heads,
+                s.attention_head_dim, s.rotary_dim, s.state_heads, s.state_key_heads, s.state_head_dim,
+                int(s.attention_gate), int(s.qk_norm), float(s.rope_theta), float(s.norm_epsilon))
+        for i, k in enumerate(s.layer_types):
+            c.layer_kinds[i] = 1 if k == "full" else 2
+        return c
+
+
+_P, _U32, _SZ, _I = ctypes.c_void_p, ctypes.c_uint32, ctypes.c_size_t, ctypes.c_int
+_SIGS = {
+    "rta_model_last_error": (ctypes.c_char_p, []),
+    "rta_model_open": (_I, [ctypes.POINTER(ModelSpecC), _P, _SZ, _P, _SZ, _P, _SZ, _U32, _I, ctypes.POINTER(_P)]),
+    "rta_model_open_files": (_I, [ctypes.POINTER(ModelSpecC), ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p,
+                                  _U32, _I, ctypes.POINTER(_P)]),
+    "rta_model_close": (None, [_P]),
+    "rta_model_prefill": (_I, [_P, _P, _U32, _P, ctypes.POINTER(ctypes.c_double)]),
+    "rta_model_generate": (_I, [_P, _U32, _P, ctypes.POINTER(_U32), ctypes.POINTER(ctypes.c_double)]),
+    "rta_model_mlp": (_I, [_P, _U32, _P, _U32, _P, _P]),
+    "rta_model_vocabulary": (_I, [_P, _P, _P, ctypes.POINTER(_U32), ctypes.POINTER(ctypes.c_float)]),
+    "rta_model_state": (_I, [_P, _P, ctypes.POINTER(_U32)]),
+    "rta_model_resources": (_I, [_P, _P, _SZ]),
+}
+RESOURCE_NAMES = ("payload_bytes", "derived_layer_bytes", "history_bytes", "recurrent_state_bytes", "capacity",
+                  "attention_splits", "kernels_per_decode_step", "kernels_per_prefill_step", "position")
+
+
+def _lib_model():
+    lib = _lib.load()
+    if not getattr(lib, "_model_sigs", False):
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(lib, name)
+            fn.restype, fn.argtypes = res, args
+        lib._model_sigs = True
+    return lib
+
+
+def _check(status: int):
+    if status != 0:
+        raise _lib.RtaError(status, _lib_model().rta_model_last_error().decode(errors="replace"))
+
+
+def _np_ptr(a: np.ndarray):
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+class ResidentModel:
+    """One resident model on one GPU (prefill / generate / mlp / vocabulary)."""
+
+    def __init__(self, handle, spec: assets.Spec, capacity: int, device: int):
+        self._h = handle
+        self.spec = spec
+        self.capacity = capacity
+        self.device = device
+        self.last_gpu_ms = 0.0
+
+    # ---------------------------------------------------------------- open
+    @classmethod
+    def from_payloads(cls, spec: assets.Spec, params, matrices, basis, capacity: int, device: int = 0):
+        """params: uint32 numpy; matrices/basis: uint8 numpy (host) or torch CUDA tensors (device)."""
+        lib = _lib_model()
+        params = np.ascontiguousarray(params, np.uint32)
+
+        def addr(buf):
+            if isinstance(buf, np.ndarray):
+                b = np.ascontiguousarray(buf, np.uint8)
+                return _np_ptr(b), b.nbytes, b
+            return ctypes.c_void_p(buf.data_ptr()), buf.numel() * buf.element_size(), buf
+        mp, mb, mkeep = addr(matrices)
+        bp, bb, bkeep = addr(basis)
+        cs = ModelSpecC.from_spec(spec)
+        h = ctypes.c_void_p()
+        _check(lib.rta_model_open(ctypes.byref(cs), _np_ptr(params), params.size, mp, mb, bp, bb, capacity, device,
+                                  ctypes.byref(h)))
+        del mkeep, bkeep
+        return cls(h, spec, capacity, device)
+
+    @classmethod
+    def from_directory(cls, directory, capacity: int, device: int = 0):
+        directory = Path(directory)
+        import json
+        spec = assets.Spec.from_dict(json.loads((directory / "model.json").read_text())["model_spec"])
+        lib = _lib_model()
+        cs = ModelSpecC.from_spec(spec)
+        h = ctypes.c_void_p()
+        _check(lib.rta_model_open_files(ctypes.byref(cs), str(directory / "optical_model.bin").encode(),
+                                        str(directory / "geometry_weights.bin").encode(),
+                                        str(directory / "vocabulary.bin").encode(), capacity, device,
+                                        ctypes.byref(h)))
+        return cls(h, spec, capacity, device)
+
+    @classmethod
+    def synthetic(cls, spec: assets.Spec, seed: int = 0, capacity: int = 1024, device: int = 0):
+        """Random-init model of `spec` generated on the GPU (payloads in the exporter's layout)."""
+        import torch
+        torch.cuda.set_device(device)
+        layout = assets.plan(spec, seed)
+        mats, basis = assets.generate_device(layout, seed)
+        model = cls.from_payloads(spec, layout.params(), mats, basis, capacity, device)
+        model.layout = layout
+        del mats, basis
+        torch.cuda.empty_cache()
+        return model
+
+    # ----------------------------------------------------------- operations
+    def close(self):
+        if self._h is not None:
+            _lib_model().rta_model_close(self._h)
+            self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def prefill(self, ids, stops=()):
+        ids = np.ascontiguousarray(ids, np.uint32)
+        st = (list(stops)[:2] + [0xFFFFFFFF] * 2)[:2]
+        st = np.array(st, np.uint32)
+        ms = ctypes.c_double(0)
+        _check(_lib_model().rta_model_prefill(self._h, _np_ptr(ids), ids.size, _np_ptr(st), ctypes.byref(ms)))
+        self.last_gpu_ms = ms.value
+        return ms.value
+
+    def generate(self, count: int):
+        out = np.zeros(count, np.uint32)
+        n = ctypes.c_uint32(0)
+        ms = ctypes.c_double(0)
+        _check(_lib_model().rta_model_generate(self._h, count, _np_ptr(out), ctypes.byref(n), ctypes.byref(ms)))
+        self.last_gpu_ms = ms.value
+        return out[:n.value].copy()
+
+    def mlp(self, x, layer: int):
+        x = np.ascontiguousarray(x, np.float32).reshape(-1, self.spec.hidden_size)
+        y = np.zeros_like(x)
+        act = np.zeros((x.shape[0], self.spec.middle_size), np.float32)
+        _check(_lib_model().rta_model_mlp(self._h, layer, _np_ptr(x), x.shape[0], _np_ptr(y), _np_ptr(act)))
+        return y, act
+
+    def vocabulary(self, hidden, logits: bool = False):
+        h = np.ascontiguousarray(hidden, np.float32).reshape(self.spec.hidden_size)
+        lg = np.zeros(self.spec.vocabulary_size, np.float32) if logits else None
+        arg = ctypes.c_uint32(0)
+        best = ctypes.c_float(0)
+        _check(_lib_model().rta_model_vocabulary(self._h, _np_ptr(h), _np_ptr(lg) if lg is not None else None,
+                                                 ctypes.byref(arg), ctypes.byref(best)))
+        return int(arg.value), float(best.value), lg
+
+    def state(self):
+        s = np.zeros(self.spec.hidden_size, np.float32)
+        pos = ctypes.c_uint32(0)
+        _check(_lib_model().rta_model_state(self._h, _np_ptr(s), ctypes.byref(pos)))
+        return s, int(pos.value)
+
+    def resources(self):
+        out = np.zeros(len(RESOURCE_NAMES), np.uint64)
+        _check(_lib_model().rta_model_resources(self._h, _np_ptr(out), out.size))
+        return dict(zip(RESOURCE_NAMES, map(int, out)))
