@@ -145,14 +145,18 @@ __global__ void __launch_bounds__(kThreads) attention_split_kernel(const AttnPar
     }
     const uint32_t st = smem_u32(smem + s * kStageBytes);
     // S^T[pos][col] = K[pos] . Q[col]
-    float sacc[4] = {0.f, 0.f, 0.f, 0.f};
+    // four independent accumulators break the 16-deep MMA dependency chain
+    float sp[4][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
     for (int kk = 0; kk < 16; ++kk) {
       uint32_t a0, a1, a2, a3;
       const uint32_t addr = st + (lane & 15) * kRowBytes + (kk * 16 + (lane >> 4) * 8) * 2;
       ldsm_x4(addr, a0, a1, a2, a3);
-      mma_f16(sacc, a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
+      mma_f16(sp[kk & 3], a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
     }
+    float sacc[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) sacc[i] = (sp[0][i] + sp[1][i]) + (sp[2][i] + sp[3][i]);
     // hi + lo columns -> full score; lanes t4 and t4^2 end up with the same values.
     float sc[4];
 #pragma unroll

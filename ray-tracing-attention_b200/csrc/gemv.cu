@@ -9,26 +9,34 @@
 // B200 design:
 //  * Weights stream HBM -> shared memory through the bulk-copy (TMA) engine:
 //    a stage is 16 consecutive rows x up to 8 blocks (2048 coefficients), one
-//    cp.async.bulk per row, NSTAGE stages in flight per CTA, mbarrier
-//    completion with bounded waits.  Under programmatic dependent launch the
-//    first stages are issued before griddepcontrol.wait, so weight streaming
-//    overlaps the tail of the kernel that produces x.
-//  * Products are exact integers: the packed 4/6-bit codes are the u8 A
-//    operand of mma.sync (m16n8k32 for a 32-wide Q4_K group, m16n8k16 for a
+//    cp.async.bulk per row, 3-4 stages in flight per CTA, 2 CTAs per SM,
+//    mbarrier completion with bounded waits.  Under programmatic dependent
+//    launch the first stages (and the norm weights) are requested before
+//    griddepcontrol.wait, so weight streaming overlaps the tail of the kernel
+//    that produces x.
+//  * Each of the 8 warps owns one 256-coefficient block of the stage.
+//    Products are exact integers: the packed 4/6-bit codes are the u8 A
+//    operand of mma.sync (m16n8k32 per 32-wide Q4_K group, m16n8k16 per
 //    16-wide Q6_K group) and the activation is split per 32-group into
-//    x ~= xs * (256*H + L) with H, L signed bytes (|X| <= 32639), the s8 B
-//    operand (columns = (H, L) x 4 batch rows).  Group scales d*sc, the
-//    dmin*m offset and the Q6_K -32 offset are applied in fp32 per group.
-//    The activation split keeps |relative error| <= 1.5e-5 per element.
+//    x ~= xs * (256*H + L) with H, L signed bytes (|X| <= 32639): the s8 B
+//    operand (columns = (H, L) x 4 batch rows).  Per (row, group) the block
+//    scale and xs fold into one fp32 coefficient; the Q4_K dmin*m offset and
+//    the Q6_K -32 offset fold into one per-row bias per block.  The activation
+//    split keeps |relative error| <= 1.5e-5 per element.
+//  * The activation prologue (RMSNorm, per-head gated norm, sigmoid gate) reads
+//    x once with coalesced 16-byte loads into registers; no dependent global
+//    load sits inside a loop.
 #include "rta_internal.h"
 
 namespace rta {
 namespace {
 
-constexpr int kThreads = 128;
-constexpr int kWarps = 4;
+constexpr int kThreads = 256;
+constexpr int kWarps = 8;
 constexpr int kTileRows = 16;
 constexpr int kStageBlocks = 8;
+constexpr int kMaxChunks = 16;        // float4 chunks of x per thread: cols <= 16384
+constexpr int kPass = 4;              // chunks held in registers per pass (normed inputs: cols <= 4096)
 constexpr float kXLevels = 32639.0f;  // 127*256 + 127: keeps H in [-127, 127]
 
 struct Params {
@@ -58,81 +66,124 @@ struct Fmt;
 template <>
 struct Fmt<kQ4K> {
   static constexpr uint32_t kBytes = 144;
+  static constexpr uint32_t kGroups = 8;
 };
 template <>
 struct Fmt<kQ6K> {
   static constexpr uint32_t kBytes = 210;
+  static constexpr uint32_t kGroups = 16;
 };
 
-__device__ __forceinline__ float block_sum(float v, float* red4) {
+__device__ __forceinline__ float block_sum(float v, float* red8) {
   v = warp_sum(v);
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
   __syncthreads();
-  if (l == 0) red4[w] = v;
+  if (l == 0) red8[w] = v;
   __syncthreads();
-  return red4[0] + ((red4[1] + red4[2]) + red4[3]);
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < kWarps; ++i) s += red8[i];
+  return s;
 }
 
-// Build the int16-split activation tables in shared memory.
-//   xq  : [xgroup][slice][half][ncol][4 words]   (B fragments, zero padded)
-//   xsc : [batch][xgroup] float4(xs, sum X first 16, sum X last 16, 0)
+// Activation prologue: x (and z, norm weights) -> int16 split tables in shared memory.
+//   xq  : [xgroup][slice][half][ncol][4 words]   (mma B fragments)
+//   xsc : [batch][xgroup] float4(xs, sum X first 16, sum X last 16, xs * sum X)
+// Thread i owns float4 chunks i, i+256, ...; 8 consecutive chunks form one
+// 32-coefficient group (8 consecutive lanes), 32 chunks one 128-wide head.
 template <int NSL>
-__device__ void prepare_x(const Params& p, uint8_t* smem) {
+__device__ void prepare_x(const Params& p, uint8_t* smem, const float4 (&wv)[kPass]) {
   uint32_t* xq = reinterpret_cast<uint32_t*>(smem + p.off_xq);
   float4* xsc = reinterpret_cast<float4*>(smem + p.off_xsc);
-  float* misc = reinterpret_cast<float*>(smem + p.off_misc);
-  const uint32_t G = p.cols / 32u;
-  const uint32_t words = G * NSL * 2u * p.ncol * 4u;
-  for (uint32_t i = threadIdx.x; i < words; i += kThreads) xq[i] = 0u;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* red8 = reinterpret_cast<float*>(smem + p.off_misc);
+  const uint32_t G = p.cols / 32u, nchunk = p.cols / 4u;
+  const uint32_t tid = threadIdx.x;
+  if (p.ncol > 2u * p.batch || NSL > 1) {
+    const uint32_t words = G * NSL * 2u * p.ncol * 4u;
+    for (uint32_t i = tid; i < words; i += kThreads) xq[i] = 0u;
+    __syncthreads();
+  }
+  const uint32_t npass = (nchunk + kPass * kThreads - 1) / (kPass * kThreads);
   for (uint32_t b = 0; b < p.batch; ++b) {
-    const float* xr = p.x + static_cast<size_t>(b) * p.x_stride;
-    const float* zr = p.z ? p.z + static_cast<size_t>(b) * p.x_stride : nullptr;
-    float inv = 1.f;
-    if (p.prologue == kRmsNorm) {
-      float s = 0.f;
-      for (uint32_t c = threadIdx.x; c < p.cols; c += kThreads) s += xr[c] * xr[c];
-      const float total = block_sum(s, misc);
-      inv = rsqrtf(total / static_cast<float>(p.cols) + p.eps);
-    }
-    __syncthreads();  // xq zero-fill and misc reuse complete
-    for (uint32_t g = warp; g < G; g += kWarps) {
-      const uint32_t c = g * 32u + lane;
-      float v = xr[c];
-      if (p.prologue == kRmsNorm) {
-        v = v * inv * p.norm_w[c];
-      } else if (p.prologue == kHeadGate) {
-        // per 128-wide head RMS: the 4 groups of a head are 4 consecutive g.
-        const uint32_t head0 = (c / 128u) * 128u;
-        float s = 0.f;
-        for (uint32_t k = lane; k < 128u; k += 32u) s += xr[head0 + k] * xr[head0 + k];
-        s = warp_sum(s);
-        const float hinv = rsqrtf(s / 128.0f + p.eps);
-        const float gz = zr[c];
-        v = v * (((hinv * p.norm_w[c]) * gz) * detector_sigmoid(gz));
-      } else if (p.prologue == kSigmoidGate) {
-        v = v * detector_sigmoid(zr[c]);
-      }
-      const float amax = warp_max(fabsf(v));
-      int X = 0;
-      float xs = 0.f;
-      if (amax > 0.f) {
-        X = __float2int_rn(v * (kXLevels / amax));
-        X = max(-32639, min(32639, X));
-        xs = amax / kXLevels;
-      }
-      const int L = static_cast<int>(static_cast<int8_t>(X & 0xff));
-      const int H = (X - L) >> 8;
-      float sx = static_cast<float>(X);
+    const float4* xr = reinterpret_cast<const float4*>(p.x + static_cast<size_t>(b) * p.x_stride);
+    const float4* zr = p.z ? reinterpret_cast<const float4*>(p.z + static_cast<size_t>(b) * p.x_stride) : nullptr;
+    for (uint32_t pass = 0; pass < npass; ++pass) {
+      float4 xv[kPass], zv[kPass];
 #pragma unroll
-      for (int m = 8; m >= 1; m >>= 1) sx += __shfl_xor_sync(0xffffffffu, sx, m);
-      const float sx_other = __shfl_xor_sync(0xffffffffu, sx, 16);
-      const uint32_t sl = b / 4u, colH = 2u * (b % 4u), half = static_cast<uint32_t>(lane) / 16u;
-      const uint32_t t = (static_cast<uint32_t>(lane) % 16u) / 4u, byte = static_cast<uint32_t>(lane) % 4u;
-      uint8_t* base = reinterpret_cast<uint8_t*>(xq + (((g * NSL + sl) * 2u + half) * p.ncol) * 4u);
-      base[(colH * 4u + t) * 4u + byte] = static_cast<uint8_t>(H & 0xff);
-      base[((colH + 1u) * 4u + t) * 4u + byte] = static_cast<uint8_t>(L & 0xff);
-      if (lane == 0) xsc[b * G + g] = make_float4(xs, sx, sx_other, 0.f);
+      for (int i = 0; i < kPass; ++i) {
+        const uint32_t c = tid + (pass * kPass + i) * kThreads;
+        xv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        zv[i] = xv[i];
+        if (c < nchunk) {
+          xv[i] = xr[c];
+          if (zr) zv[i] = zr[c];
+        }
+      }
+      float inv = 1.f;
+      if (p.prologue == kRmsNorm) {  // single pass: cols <= kPass * 4 * kThreads
+        float s = 0.f;
+#pragma unroll
+        for (int i = 0; i < kPass; ++i)
+          s += xv[i].x * xv[i].x + xv[i].y * xv[i].y + xv[i].z * xv[i].z + xv[i].w * xv[i].w;
+        inv = rsqrtf(block_sum(s, red8) / static_cast<float>(p.cols) + p.eps);
+      }
+#pragma unroll
+      for (int i = 0; i < kPass; ++i) {
+        const uint32_t ci = (pass * kPass + i) * kThreads;
+        if (ci >= nchunk) break;  // uniform across the CTA
+        const uint32_t c = tid + ci;
+        float v[4] = {xv[i].x, xv[i].y, xv[i].z, xv[i].w};
+        if (p.prologue == kRmsNorm) {
+          const float w4[4] = {wv[i].x, wv[i].y, wv[i].z, wv[i].w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) v[e] = v[e] * inv * w4[e];
+        } else if (p.prologue == kHeadGate) {
+          // one 128-wide head = the 32 chunks of this warp in this iteration
+          float s = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
+          s = warp_sum(s);
+          const float hinv = rsqrtf(s / 128.0f + p.eps);
+          const float w4[4] = {wv[i].x, wv[i].y, wv[i].z, wv[i].w};
+          const float z4[4] = {zv[i].x, zv[i].y, zv[i].z, zv[i].w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) v[e] = v[e] * (((hinv * w4[e]) * z4[e]) * detector_sigmoid(z4[e]));
+        } else if (p.prologue == kSigmoidGate) {
+          const float z4[4] = {zv[i].x, zv[i].y, zv[i].z, zv[i].w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) v[e] = v[e] * detector_sigmoid(z4[e]);
+        }
+        float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+        const float scale = amax > 0.f ? kXLevels / amax : 0.f;
+        uint32_t hw = 0u, lw = 0u;
+        int sx = 0;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          int X = __float2int_rn(v[e] * scale);
+          X = max(-32639, min(32639, X));
+          const int L = static_cast<int>(static_cast<int8_t>(X & 0xff));
+          const int H = (X - L) >> 8;
+          hw |= (static_cast<uint32_t>(H) & 0xffu) << (8 * e);
+          lw |= (static_cast<uint32_t>(L) & 0xffu) << (8 * e);
+          sx += X;
+        }
+        sx += __shfl_xor_sync(0xffffffffu, sx, 1);
+        sx += __shfl_xor_sync(0xffffffffu, sx, 2);  // 16-element half sums
+        const int sx_hi = __shfl_xor_sync(0xffffffffu, sx, 4);
+        if (c < nchunk) {
+          const uint32_t g = c / 8u, k8 = c % 8u, half = k8 / 4u, t = k8 % 4u;
+          const uint32_t sl = b / 4u, colH = 2u * (b % 4u);
+          uint32_t* base = xq + (((g * NSL + sl) * 2u + half) * p.ncol) * 4u;
+          base[colH * 4u + t] = hw;
+          base[(colH + 1u) * 4u + t] = lw;
+          if (k8 == 0u) {
+            const float xs = amax / kXLevels;
+            xsc[b * G + g] = make_float4(xs, static_cast<float>(sx), static_cast<float>(sx_hi),
+                                         xs * static_cast<float>(sx + sx_hi));
+          }
+        }
+      }
     }
   }
   __syncthreads();
@@ -145,17 +196,19 @@ __device__ __forceinline__ const uint8_t* stage_src(const Params& p, uint32_t ti
          static_cast<size_t>(kst) * kStageBlocks * Fmt<FMT>::kBytes;
 }
 
-template <int FMT, int NSL>
-__global__ void __launch_bounds__(kThreads) gemv_kernel(const Params p) {
+// ONE: batch == 1 (xs folded into the per-(row, group) coefficients).
+template <int FMT, int NSL, bool ONE>
+__global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const Params p) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.off_bar);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t g = static_cast<uint32_t>(lane) >> 2, t = static_cast<uint32_t>(lane) & 3u;
   const uint32_t tiles = p.rows / kTileRows;
-  const uint32_t ipt = p.nmat * p.ks;  // iterations (stages) per tile
+  const uint32_t ipt = p.nmat * p.ks;  // stages per tile
   const uint32_t my_tiles = blockIdx.x < tiles ? (tiles - 1u - blockIdx.x) / gridDim.x + 1u : 0u;
   const uint32_t total = my_tiles * ipt;
   volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + p.off_misc + 64);
+  constexpr uint32_t NG = Fmt<FMT>::kGroups;
 
   if (threadIdx.x == 0) {
     for (uint32_t s = 0; s < p.nstage; ++s) mbar_init(&bars[s], 1);
@@ -165,8 +218,7 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const Params p) {
   __syncthreads();
   const uint64_t policy = evict_first_policy();
 
-  auto issue = [&](uint32_t it) {
-    // warp 0 only
+  auto issue = [&](uint32_t it) {  // warp 0 only
     const uint32_t s = it % p.nstage;
     const uint32_t tile = blockIdx.x + (it / ipt) * gridDim.x;
     const uint32_t r = it % ipt, mat = r / p.ks, kst = r % p.ks;
@@ -183,19 +235,29 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const Params p) {
   if (warp == 0)
     for (uint32_t it = 0; it < issued; ++it) issue(it);
 
+  // norm weights are constant: read them before waiting on the producer
+  float4 wv[kPass];
+#pragma unroll
+  for (int i = 0; i < kPass; ++i) wv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (p.prologue == kRmsNorm || p.prologue == kHeadGate) {
+    const float4* w4 = reinterpret_cast<const float4*>(p.norm_w);
+#pragma unroll
+    for (int i = 0; i < kPass; ++i)
+      if (threadIdx.x + i * kThreads < p.cols / 4u) wv[i] = w4[threadIdx.x + i * kThreads];
+  }
+
   pdl_wait();                 // activations (and residual target) are now visible
   pdl_launch_dependents();    // let the next kernel start streaming its weights
   if (p.running && *p.running == 0u) {
-    // generation stopped: drain the stages already in flight and leave
-    if (threadIdx.x == 0)
+    if (threadIdx.x == 0)  // generation stopped: drain the stages in flight and leave
       for (uint32_t j = 0; j < issued; ++j) (void)mbar_wait(&bars[j % p.nstage], (j / p.nstage) & 1u, nullptr);
     return;
   }
-  prepare_x<NSL>(p, smem);
+  prepare_x<NSL>(p, smem, wv);
 
   const uint32_t* xq = reinterpret_cast<const uint32_t*>(smem + p.off_xq);
   const float4* xsc = reinterpret_cast<const float4*>(smem + p.off_xsc);
-  float* scr = reinterpret_cast<float*>(smem + p.off_scr) + warp * 512;
+  float* scr = reinterpret_cast<float*>(smem + p.off_scr) + warp * (kTileRows * 16 * 2 + kTileRows);
   float* red = reinterpret_cast<float*>(smem + p.off_red);
   const uint32_t G = p.cols / 32u;
   const uint32_t redsz = kWarps * 2u * kTileRows * p.batch;  // one buffer (per parity)
@@ -218,47 +280,90 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const Params p) {
     const uint32_t nb = min(static_cast<uint32_t>(kStageBlocks), p.kb_total - kst * kStageBlocks);
     const uint32_t chunk = nb * Fmt<FMT>::kBytes;
     const uint8_t* stage = smem + s * p.stage_bytes;
+    const uint32_t kb = static_cast<uint32_t>(warp);
 
-    if (ok) {
-      for (uint32_t kb = warp; kb < nb; kb += kWarps) {
-        const uint32_t xg0 = (kst * kStageBlocks + kb) * 8u;  // first x-group of this block
+    if (ok && kb < nb) {
+      const uint32_t xg0 = (kst * kStageBlocks + kb) * 8u;  // first x-group of this block
+      // ---- per (row, group) scales of this block: lane -> row lane/2, half the groups
+      {
+        const uint32_t row = static_cast<uint32_t>(lane) >> 1, gh = (static_cast<uint32_t>(lane) & 1u) * (NG / 2u);
+        const uint8_t* bk = stage + row * chunk + kb * Fmt<FMT>::kBytes;
+        float bias = 0.f;
         if constexpr (FMT == kQ4K) {
-          // scales of the 16 rows x 8 groups of this block -> (d*sc, dmin*m)
+          const float d = half_bits_to_float(bk[0] | (bk[1] << 8));
+          const float dmin = half_bits_to_float(bk[2] | (bk[3] << 8));
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const uint32_t pair = lane + 32u * i, row = pair >> 3, grp = pair & 7u;
-            const uint8_t* h = stage + row * chunk + kb * 144u;
-            const float d = half_bits_to_float(h[0] | (h[1] << 8));
-            const float dmin = half_bits_to_float(h[2] | (h[3] << 8));
+          for (uint32_t q = 0; q < NG / 2u; ++q) {
+            const uint32_t grp = gh + q;
             uint32_t sc, mn;
             if (grp < 4u) {
-              sc = h[4 + grp] & 63u;
-              mn = h[8 + grp] & 63u;
+              sc = bk[4 + grp] & 63u;
+              mn = bk[8 + grp] & 63u;
             } else {
-              const uint32_t q = grp - 4u, mixed = h[12 + q];
-              sc = (mixed & 15u) | ((static_cast<uint32_t>(h[4 + q]) >> 6) << 4);
-              mn = (mixed >> 4) | ((static_cast<uint32_t>(h[8 + q]) >> 6) << 4);
+              const uint32_t u = grp - 4u, mixed = bk[12 + u];
+              sc = (mixed & 15u) | ((static_cast<uint32_t>(bk[4 + u]) >> 6) << 4);
+              mn = (mixed >> 4) | ((static_cast<uint32_t>(bk[8 + u]) >> 6) << 4);
             }
-            scr[2 * pair] = d * static_cast<float>(sc);
-            scr[2 * pair + 1] = dmin * static_cast<float>(mn);
+            const float dsc = d * static_cast<float>(sc), dmm = dmin * static_cast<float>(mn);
+            if constexpr (ONE) {
+              const float4 xv = xsc[xg0 + grp];
+              scr[row * NG + grp] = dsc * xv.x;
+              bias += dmm * xv.w;
+            } else {
+              scr[2 * (row * NG + grp)] = dsc;
+              scr[2 * (row * NG + grp) + 1] = dmm;
+            }
           }
-          __syncwarp();
-          const uint8_t* rg = stage + g * chunk + kb * 144u + 16u;
-          const uint8_t* rg8 = stage + (g + 8u) * chunk + kb * 144u + 16u;
+        } else {
+          const float d = half_bits_to_float(bk[208] | (bk[209] << 8));
 #pragma unroll
-          for (uint32_t pch = 0; pch < 4u; ++pch) {
-            const uint32_t w0 = *reinterpret_cast<const uint32_t*>(rg + 32u * pch + 4u * t);
-            const uint32_t w2 = *reinterpret_cast<const uint32_t*>(rg + 32u * pch + 16u + 4u * t);
-            const uint32_t w1 = *reinterpret_cast<const uint32_t*>(rg8 + 32u * pch + 4u * t);
-            const uint32_t w3 = *reinterpret_cast<const uint32_t*>(rg8 + 32u * pch + 16u + 4u * t);
+          for (uint32_t q = 0; q < NG / 2u; ++q) {
+            const uint32_t grp = gh + q;
+            const float dsc = d * static_cast<float>(static_cast<int8_t>(bk[192 + grp]));
+            if constexpr (ONE) {
+              const float4 xv = xsc[xg0 + grp / 2u];
+              const float coef = dsc * xv.x;
+              scr[row * NG + grp] = coef;
+              bias += 32.0f * coef * ((grp & 1u) ? xv.z : xv.y);
+            } else {
+              scr[row * NG + grp] = dsc;
+            }
+          }
+        }
+        if constexpr (ONE) {
+          bias += __shfl_xor_sync(0xffffffffu, bias, 1);
+          if ((lane & 1) == 0) scr[kTileRows * NG * 2 + row] = bias;
+        }
+      }
+      __syncwarp();
+
+      if constexpr (FMT == kQ4K) {
+        const uint8_t* rg = stage + g * chunk + kb * 144u + 16u;
+        const uint8_t* rg8 = stage + (g + 8u) * chunk + kb * 144u + 16u;
 #pragma unroll
-            for (uint32_t nib = 0; nib < 2u; ++nib) {
-              const uint32_t grp = 2u * pch + nib, sh = 4u * nib;
-              const uint32_t a0 = (w0 >> sh) & 0x0f0f0f0fu, a1 = (w1 >> sh) & 0x0f0f0f0fu;
-              const uint32_t a2 = (w2 >> sh) & 0x0f0f0f0fu, a3 = (w3 >> sh) & 0x0f0f0f0fu;
-              const uint32_t xg = xg0 + grp;
-              const float2 sA = *reinterpret_cast<const float2*>(scr + 2 * (g * 8u + grp));
-              const float2 sB = *reinterpret_cast<const float2*>(scr + 2 * ((g + 8u) * 8u + grp));
+        for (uint32_t pch = 0; pch < 4u; ++pch) {
+          const uint32_t w0 = *reinterpret_cast<const uint32_t*>(rg + 32u * pch + 4u * t);
+          const uint32_t w2 = *reinterpret_cast<const uint32_t*>(rg + 32u * pch + 16u + 4u * t);
+          const uint32_t w1 = *reinterpret_cast<const uint32_t*>(rg8 + 32u * pch + 4u * t);
+          const uint32_t w3 = *reinterpret_cast<const uint32_t*>(rg8 + 32u * pch + 16u + 4u * t);
+#pragma unroll
+          for (uint32_t nib = 0; nib < 2u; ++nib) {
+            const uint32_t grp = 2u * pch + nib, sh = 4u * nib;
+            const uint32_t a0 = (w0 >> sh) & 0x0f0f0f0fu, a1 = (w1 >> sh) & 0x0f0f0f0fu;
+            const uint32_t a2 = (w2 >> sh) & 0x0f0f0f0fu, a3 = (w3 >> sh) & 0x0f0f0f0fu;
+            const uint32_t xg = xg0 + grp;
+            if constexpr (ONE) {
+              const uint32_t* xw = xq + (xg * 2u) * 8u;
+              const uint32_t b0 = g < 2u ? xw[g * 4u + t] : 0u, b1 = g < 2u ? xw[8u + g * 4u + t] : 0u;
+              int c[4] = {0, 0, 0, 0};
+              mma_u8s8_k32(c, a0, a1, a2, a3, b0, b1);
+              if (t == 0u) {
+                acc[mat][0][0] += scr[g * NG + grp] * static_cast<float>(c[0] * 256 + c[1]);
+                acc[mat][0][1] += scr[(g + 8u) * NG + grp] * static_cast<float>(c[2] * 256 + c[3]);
+              }
+            } else {
+              const float2 sA = *reinterpret_cast<const float2*>(scr + 2 * (g * NG + grp));
+              const float2 sB = *reinterpret_cast<const float2*>(scr + 2 * ((g + 8u) * NG + grp));
 #pragma unroll
               for (int sl = 0; sl < NSL; ++sl) {
                 const uint32_t* xw = xq + ((xg * NSL + sl) * 2u) * p.ncol * 4u;
@@ -273,48 +378,46 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const Params p) {
                 if (b < p.batch) {
                   const float4 xv = xsc[b * G + xg];
                   const float sx = xv.y + xv.z;
-                  const float dot0 = static_cast<float>(c[0] * 256 + c[1]);
-                  const float dot1 = static_cast<float>(c[2] * 256 + c[3]);
-                  acc[mat][sl][0] += xv.x * (sA.x * dot0 - sA.y * sx);
-                  acc[mat][sl][1] += xv.x * (sB.x * dot1 - sB.y * sx);
+                  acc[mat][sl][0] += xv.x * (sA.x * static_cast<float>(c[0] * 256 + c[1]) - sA.y * sx);
+                  acc[mat][sl][1] += xv.x * (sB.x * static_cast<float>(c[2] * 256 + c[3]) - sB.y * sx);
                 }
               }
             }
           }
-          __syncwarp();
-        } else {
-          // Q6_K: d * int8 scale per (row, 16-group)
+        }
+      } else {
+        const uint32_t rowg = g * chunk + kb * 210u, rowg8 = (g + 8u) * chunk + kb * 210u;
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const uint32_t pair = lane + 32u * i, row = pair >> 4, grp = pair & 15u;
-            const uint8_t* bk = stage + row * chunk + kb * 210u;
-            const float d = half_bits_to_float(bk[208] | (bk[209] << 8));
-            scr[pair] = d * static_cast<float>(static_cast<int8_t>(bk[192 + grp]));
+        for (uint32_t part = 0; part < 2u; ++part) {
+          uint32_t ql[2][4], qh[2][2];
+#pragma unroll
+          for (uint32_t q = 0; q < 4u; ++q) {
+            const uint32_t off = part * 64u + 16u * q + 4u * t;
+            ql[0][q] = lds_u32_unaligned(stage, rowg + off);
+            ql[1][q] = lds_u32_unaligned(stage, rowg8 + off);
           }
-          __syncwarp();
-          const uint32_t rowg = g * chunk + kb * 210u, rowg8 = (g + 8u) * chunk + kb * 210u;
 #pragma unroll
-          for (uint32_t part = 0; part < 2u; ++part) {
-            uint32_t ql[2][4], qh[2][2];
+          for (uint32_t q = 0; q < 2u; ++q) {
+            const uint32_t off = 128u + part * 32u + 16u * q + 4u * t;
+            qh[0][q] = lds_u32_unaligned(stage, rowg + off);
+            qh[1][q] = lds_u32_unaligned(stage, rowg8 + off);
+          }
 #pragma unroll
-            for (uint32_t q = 0; q < 4u; ++q) {
-              const uint32_t off = part * 64u + 16u * q + 4u * t;
-              ql[0][q] = lds_u32_unaligned(stage, rowg + off);
-              ql[1][q] = lds_u32_unaligned(stage, rowg8 + off);
-            }
-#pragma unroll
-            for (uint32_t q = 0; q < 2u; ++q) {
-              const uint32_t off = 128u + part * 32u + 16u * q + 4u * t;
-              qh[0][q] = lds_u32_unaligned(stage, rowg + off);
-              qh[1][q] = lds_u32_unaligned(stage, rowg8 + off);
-            }
-#pragma unroll
-            for (uint32_t jj = 0; jj < 8u; ++jj) {
-              const uint32_t grp = part * 8u + jj, ns = (jj / 4u) * 4u, hs = (jj / 2u) * 2u;
-              const uint32_t a0 = ((ql[0][jj % 4u] >> ns) & 0x0f0f0f0fu) | (((qh[0][jj % 2u] >> hs) & 0x03030303u) << 4);
-              const uint32_t a1 = ((ql[1][jj % 4u] >> ns) & 0x0f0f0f0fu) | (((qh[1][jj % 2u] >> hs) & 0x03030303u) << 4);
-              const uint32_t xg = xg0 + grp / 2u, half = grp & 1u;
-              const float dA = scr[g * 16u + grp], dB = scr[(g + 8u) * 16u + grp];
+          for (uint32_t jj = 0; jj < 8u; ++jj) {
+            const uint32_t grp = part * 8u + jj, ns = (jj / 4u) * 4u, hs = (jj / 2u) * 2u;
+            const uint32_t a0 = ((ql[0][jj % 4u] >> ns) & 0x0f0f0f0fu) | (((qh[0][jj % 2u] >> hs) & 0x03030303u) << 4);
+            const uint32_t a1 = ((ql[1][jj % 4u] >> ns) & 0x0f0f0f0fu) | (((qh[1][jj % 2u] >> hs) & 0x03030303u) << 4);
+            const uint32_t xg = xg0 + grp / 2u, half = grp & 1u;
+            if constexpr (ONE) {
+              const uint32_t b0 = g < 2u ? xq[((xg * 2u + half) * 2u + g) * 4u + t] : 0u;
+              int c[4] = {0, 0, 0, 0};
+              mma_u8s8_k16(c, a0, a1, b0);
+              if (t == 0u) {
+                acc[mat][0][0] += scr[g * NG + grp] * static_cast<float>(c[0] * 256 + c[1]);
+                acc[mat][0][1] += scr[(g + 8u) * NG + grp] * static_cast<float>(c[2] * 256 + c[3]);
+              }
+            } else {
+              const float dA = scr[g * NG + grp], dB = scr[(g + 8u) * NG + grp];
 #pragma unroll
               for (int sl = 0; sl < NSL; ++sl) {
                 const uint32_t* xw = xq + ((xg * NSL + sl) * 2u + half) * p.ncol * 4u;
@@ -325,17 +428,21 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const Params p) {
                 if (b < p.batch) {
                   const float4 xv = xsc[b * G + xg];
                   const float sx32 = 32.0f * (half ? xv.z : xv.y);
-                  const float dot0 = static_cast<float>(c[0] * 256 + c[1]) - sx32;
-                  const float dot1 = static_cast<float>(c[2] * 256 + c[3]) - sx32;
-                  acc[mat][sl][0] += xv.x * (dA * dot0);
-                  acc[mat][sl][1] += xv.x * (dB * dot1);
+                  acc[mat][sl][0] += xv.x * (dA * (static_cast<float>(c[0] * 256 + c[1]) - sx32));
+                  acc[mat][sl][1] += xv.x * (dB * (static_cast<float>(c[2] * 256 + c[3]) - sx32));
                 }
               }
             }
           }
-          __syncwarp();
         }
       }
+      if constexpr (ONE) {
+        if (t == 0u) {
+          acc[mat][0][0] -= scr[kTileRows * NG * 2 + g];
+          acc[mat][0][1] -= scr[kTileRows * NG * 2 + g + 8u];
+        }
+      }
+      __syncwarp();
     }
 
     const bool tile_end = (r == ipt - 1u);
@@ -366,28 +473,28 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const Params p) {
       issued = it + p.nstage + 1u;
     }
     if (tile_end)
-    for (uint32_t idx = threadIdx.x; idx < kTileRows * p.batch; idx += kThreads) {
-      const uint32_t row = idx % kTileRows, b = idx / kTileRows;
-      float v[2] = {0.f, 0.f};
-      for (uint32_t m = 0; m < p.nmat; ++m)
-        for (int w = 0; w < kWarps; ++w) v[m] += redbuf[((w * 2 + m) * kTileRows + row) * p.batch + b];
-      const uint32_t R = tile * kTileRows + row;
-      float* yp = p.y ? p.y + static_cast<size_t>(b) * p.y_stride + R : nullptr;
-      if (p.epilogue == kSwiGLU) {
-        const float gv = v[0], uv = v[1];
-        const float amp = fabsf(gv) * fabsf(uv) * detector_sigmoid(gv);
-        const float sgn = (gv > 0.f ? 1.f : gv < 0.f ? -1.f : 0.f) * (uv > 0.f ? 1.f : uv < 0.f ? -1.f : 0.f);
-        *yp = sgn * amp;
-      } else if (p.epilogue == kAccumulate) {
-        *yp += v[0];
-      } else if (yp) {
-        *yp = v[0];
+      for (uint32_t idx = threadIdx.x; idx < kTileRows * p.batch; idx += kThreads) {
+        const uint32_t row = idx % kTileRows, b = idx / kTileRows;
+        float v[2] = {0.f, 0.f};
+        for (uint32_t m = 0; m < p.nmat; ++m)
+          for (int w = 0; w < kWarps; ++w) v[m] += redbuf[((w * 2 + m) * kTileRows + row) * p.batch + b];
+        const uint32_t R = tile * kTileRows + row;
+        float* yp = p.y ? p.y + static_cast<size_t>(b) * p.y_stride + R : nullptr;
+        if (p.epilogue == kSwiGLU) {
+          const float gv = v[0], uv = v[1];
+          const float amp = fabsf(gv) * fabsf(uv) * detector_sigmoid(gv);
+          const float sgn = (gv > 0.f ? 1.f : gv < 0.f ? -1.f : 0.f) * (uv > 0.f ? 1.f : uv < 0.f ? -1.f : 0.f);
+          *yp = sgn * amp;
+        } else if (p.epilogue == kAccumulate) {
+          *yp += v[0];
+        } else if (yp) {
+          *yp = v[0];
+        }
+        if (p.argmax) {
+          const unsigned long long key = pack_argmax(v[0], R);
+          best = key > best ? key : best;
+        }
       }
-      if (p.argmax) {
-        const unsigned long long key = pack_argmax(v[0], R);
-        best = key > best ? key : best;
-      }
-    }
   }
 
   if (aborted) {
@@ -426,13 +533,13 @@ __global__ void gemv_f32_kernel(const float* __restrict__ W, uint32_t rows, uint
   if (lane == 0) y[b * y_stride + r] = s;
 }
 
-template <int FMT, int NSL>
+template <int FMT, int NSL, bool ONE>
 cudaError_t launch_t(const GemvArgs& a, Params p, cudaStream_t s) {
-  auto kernel = gemv_kernel<FMT, NSL>;
+  auto kernel = gemv_kernel<FMT, NSL, ONE>;
   const uint32_t bytes = Fmt<FMT>::kBytes;
   p.stage_bytes = kTileRows * kStageBlocks * bytes;
-  p.nstage = 4;
-  p.ncol = (a.batch == 1u && NSL == 1) ? 2u : 8u;
+  p.nstage = FMT == kQ4K ? 4u : 3u;
+  p.ncol = ONE ? 2u : 8u;
   const uint32_t G = a.cols / 32u;
   uint32_t off = 0;
   auto carve = [&](uint32_t sz, uint32_t align) {
@@ -441,19 +548,18 @@ cudaError_t launch_t(const GemvArgs& a, Params p, cudaStream_t s) {
     off += sz;
     return at;
   };
-  const uint32_t off_stage = carve(p.nstage * p.stage_bytes, 128);
-  (void)off_stage;
+  carve(p.nstage * p.stage_bytes, 128);
   p.off_bar = carve(8 * p.nstage, 8);
   p.off_xq = carve(G * NSL * 2 * p.ncol * 16, 16);
   p.off_xsc = carve(a.batch * G * 16, 16);
-  p.off_scr = carve(kWarps * 512 * 4, 16);
+  p.off_scr = carve(kWarps * (kTileRows * 16 * 2 + kTileRows) * 4, 16);
   const uint32_t red_floats = 2 * kWarps * 2 * kTileRows * a.batch;
   p.off_red = carve(max(red_floats * 4u, static_cast<uint32_t>(kThreads * 8)), 16);
   p.off_misc = carve(128, 16);
   const uint32_t smem = off;
   // One-time kernel setup and occupancy per (kernel instance, smem size): these
-  // queries cost microseconds and must stay off the per-launch path.
-  // (function attributes are per device: index the cache by device ordinal)
+  // queries cost microseconds and must stay off the per-launch path
+  // (function attributes are per device: index the cache by device ordinal).
   static int max_smem_set[64] = {0};
   static uint32_t cached_smem[8] = {0};
   static int cached_grid[8] = {0};
@@ -502,10 +608,8 @@ cudaError_t launch_t(const GemvArgs& a, Params p, cudaStream_t s) {
 
 cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t s) {
   if ((a.fmt != kQ4K && a.fmt != kQ6K) || !a.w0 || !a.x || a.rows == 0 || a.rows % kTileRows ||
-      a.cols == 0 || a.cols % 256 || a.batch == 0 || a.batch > kMaxBatch)
+      a.cols == 0 || a.cols % 256 || a.cols > 4u * kThreads * kMaxChunks || a.batch == 0 || a.batch > kMaxBatch)
     return cudaErrorInvalidValue;
-  if (a.fmt == kQ6K && (a.cols / 256) % kStageBlocks && a.cols / 256 > static_cast<uint32_t>(kStageBlocks))
-    return cudaErrorInvalidValue;  // Q6_K row chunks must stay 16-byte aligned
   if (a.epilogue == kSwiGLU && !a.w1) return cudaErrorInvalidValue;
   if (a.epilogue != kSwiGLU && a.w1) return cudaErrorInvalidValue;
   if (!a.y && !a.argmax) return cudaErrorInvalidValue;
@@ -513,9 +617,14 @@ cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t s) {
   if ((a.prologue == kHeadGate || a.prologue == kSigmoidGate) && !a.z) return cudaErrorInvalidValue;
   if ((a.prologue == kRmsNorm || a.prologue == kHeadGate) && !a.norm_w) return cudaErrorInvalidValue;
   if (a.prologue == kHeadGate && a.cols % 128) return cudaErrorInvalidValue;
+  if ((a.prologue == kRmsNorm || a.prologue == kHeadGate) && a.cols > 4u * kThreads * kPass)
+    return cudaErrorInvalidValue;  // normed inputs are held in registers in one pass
   const uint32_t row_bytes = a.cols / 256 * block_bytes(a.fmt);
-  if (row_bytes % 16 || reinterpret_cast<uintptr_t>(a.w0) % 16 || reinterpret_cast<uintptr_t>(a.w1) % 16)
-    return cudaErrorMisalignedAddress;
+  const uint32_t x_stride = a.x_stride ? a.x_stride : a.cols;
+  if (row_bytes % 16 || reinterpret_cast<uintptr_t>(a.w0) % 16 || reinterpret_cast<uintptr_t>(a.w1) % 16 ||
+      reinterpret_cast<uintptr_t>(a.x) % 16 || reinterpret_cast<uintptr_t>(a.z) % 16 ||
+      reinterpret_cast<uintptr_t>(a.norm_w) % 16 || x_stride % 4)
+    return cudaErrorMisalignedAddress;  // rows, activations and norm weights are read as 16-byte vectors
   Params p = {};
   p.w[0] = a.w0;
   p.w[1] = a.w1;
@@ -526,7 +635,7 @@ cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t s) {
   p.row_bytes = row_bytes;
   p.ks = (p.kb_total + kStageBlocks - 1) / kStageBlocks;
   p.x = a.x;
-  p.x_stride = a.x_stride ? a.x_stride : a.cols;
+  p.x_stride = x_stride;
   p.batch = a.batch;
   p.prologue = a.prologue;
   p.norm_w = a.norm_w;
@@ -540,13 +649,15 @@ cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t s) {
   p.running = a.running;
   const uint32_t nsl = (a.batch + 3) / 4;
   if (a.fmt == kQ4K) {
-    if (nsl == 1) return launch_t<kQ4K, 1>(a, p, s);
-    if (nsl == 2) return launch_t<kQ4K, 2>(a, p, s);
-    return launch_t<kQ4K, 8>(a, p, s);
+    if (a.batch == 1) return launch_t<kQ4K, 1, true>(a, p, s);
+    if (nsl == 1) return launch_t<kQ4K, 1, false>(a, p, s);
+    if (nsl == 2) return launch_t<kQ4K, 2, false>(a, p, s);
+    return launch_t<kQ4K, 8, false>(a, p, s);
   }
-  if (nsl == 1) return launch_t<kQ6K, 1>(a, p, s);
-  if (nsl == 2) return launch_t<kQ6K, 2>(a, p, s);
-  return launch_t<kQ6K, 8>(a, p, s);
+  if (a.batch == 1) return launch_t<kQ6K, 1, true>(a, p, s);
+  if (nsl == 1) return launch_t<kQ6K, 1, false>(a, p, s);
+  if (nsl == 2) return launch_t<kQ6K, 2, false>(a, p, s);
+  return launch_t<kQ6K, 8, false>(a, p, s);
 }
 
 cudaError_t launch_gemv_f32(const float* W, uint32_t rows, uint32_t cols, const float* x, uint32_t x_stride,
