@@ -45,8 +45,9 @@ struct Params {
   uint32_t ks;           // stages per matrix per tile
   uint32_t nstage;       // pipeline depth
   uint32_t stage_bytes;  // bytes of one stage buffer
+  uint32_t row_pad;      // shared-memory padding after each staged row (bank spreading)
   const float* x;
-  uint32_t x_stride, batch, ncol;
+  uint32_t x_stride, batch;
   int prologue;
   const float* norm_w;
   float eps;
@@ -67,11 +68,13 @@ template <>
 struct Fmt<kQ4K> {
   static constexpr uint32_t kBytes = 144;
   static constexpr uint32_t kGroups = 8;
+  static constexpr uint32_t kPad = 16;  // 1152-byte rows are a multiple of 128 B: pad to spread banks
 };
 template <>
 struct Fmt<kQ6K> {
   static constexpr uint32_t kBytes = 210;
   static constexpr uint32_t kGroups = 16;
+  static constexpr uint32_t kPad = 0;   // 1680-byte rows already fall on distinct banks
 };
 
 __device__ __forceinline__ float block_sum(float v, float* red8) {
@@ -87,22 +90,16 @@ __device__ __forceinline__ float block_sum(float v, float* red8) {
 }
 
 // Activation prologue: x (and z, norm weights) -> int16 split tables in shared memory.
-//   xq  : [xgroup][slice][half][ncol][4 words]   (mma B fragments)
+//   xq  : [batch][xgroup][half][H,L][4 words]  (16 words per 32-coefficient group)
 //   xsc : [batch][xgroup] float4(xs, sum X first 16, sum X last 16, xs * sum X)
 // Thread i owns float4 chunks i, i+256, ...; 8 consecutive chunks form one
 // 32-coefficient group (8 consecutive lanes), 32 chunks one 128-wide head.
-template <int NSL>
 __device__ void prepare_x(const Params& p, uint8_t* smem, const float4 (&wv)[kPass]) {
   uint32_t* xq = reinterpret_cast<uint32_t*>(smem + p.off_xq);
   float4* xsc = reinterpret_cast<float4*>(smem + p.off_xsc);
   float* red8 = reinterpret_cast<float*>(smem + p.off_misc);
   const uint32_t G = p.cols / 32u, nchunk = p.cols / 4u;
   const uint32_t tid = threadIdx.x;
-  if (p.ncol > 2u * p.batch || NSL > 1) {
-    const uint32_t words = G * NSL * 2u * p.ncol * 4u;
-    for (uint32_t i = tid; i < words; i += kThreads) xq[i] = 0u;
-    __syncthreads();
-  }
   const uint32_t npass = (nchunk + kPass * kThreads - 1) / (kPass * kThreads);
   for (uint32_t b = 0; b < p.batch; ++b) {
     const float4* xr = reinterpret_cast<const float4*>(p.x + static_cast<size_t>(b) * p.x_stride);
@@ -173,14 +170,13 @@ __device__ void prepare_x(const Params& p, uint8_t* smem, const float4 (&wv)[kPa
         const int sx_hi = __shfl_xor_sync(0xffffffffu, sx, 4);
         if (c < nchunk) {
           const uint32_t g = c / 8u, k8 = c % 8u, half = k8 / 4u, t = k8 % 4u;
-          const uint32_t sl = b / 4u, colH = 2u * (b % 4u);
-          uint32_t* base = xq + (((g * NSL + sl) * 2u + half) * p.ncol) * 4u;
-          base[colH * 4u + t] = hw;
-          base[(colH + 1u) * 4u + t] = lw;
+          uint32_t* base = xq + (static_cast<size_t>(b) * G + g) * 16u + half * 8u;
+          base[t] = hw;
+          base[4u + t] = lw;
           if (k8 == 0u) {
             const float xs = amax / kXLevels;
             xsc[b * G + g] = make_float4(xs, static_cast<float>(sx), static_cast<float>(sx_hi),
-                                         xs * static_cast<float>(sx + sx_hi));
+                                         __fmul_rn(xs, static_cast<float>(sx + sx_hi)));
           }
         }
       }
@@ -196,8 +192,13 @@ __device__ __forceinline__ const uint8_t* stage_src(const Params& p, uint32_t ti
          static_cast<size_t>(kst) * kStageBlocks * Fmt<FMT>::kBytes;
 }
 
-// ONE: batch == 1 (xs folded into the per-(row, group) coefficients).
-template <int FMT, int NSL, bool ONE>
+// Per-warp scratch (floats): dsc[16 groups][17] | dmm[16][17] | bias[16 rows]
+constexpr uint32_t kScrStride = 17;
+constexpr uint32_t kScrFloats = 2 * 16 * kScrStride + kTileRows;
+
+// NB: batch rows per launch (1, 2, 4, 8).  Every batch row runs the identical
+// batch-1 arithmetic, so a row's result does not depend on the batch size.
+template <int FMT, int NB>
 __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const Params p) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.off_bar);
@@ -227,8 +228,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const Params p) {
     if (lane == 0) mbar_expect_tx(&bars[s], chunk * kTileRows);
     __syncwarp();
     if (lane < kTileRows)
-      bulk_g2s_stream(smem + s * p.stage_bytes + lane * chunk, stage_src<FMT>(p, tile, mat, kst, lane), chunk,
-                      &bars[s], policy);
+      bulk_g2s_stream(smem + s * p.stage_bytes + lane * (chunk + p.row_pad), stage_src<FMT>(p, tile, mat, kst, lane),
+                      chunk, &bars[s], policy);
   };
 
   uint32_t issued = min(total, p.nstage), drain_from = 0;  // tracked by every thread alike
@@ -253,20 +254,24 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const Params p) {
       for (uint32_t j = 0; j < issued; ++j) (void)mbar_wait(&bars[j % p.nstage], (j / p.nstage) & 1u, nullptr);
     return;
   }
-  prepare_x<NSL>(p, smem, wv);
+  prepare_x(p, smem, wv);
 
   const uint32_t* xq = reinterpret_cast<const uint32_t*>(smem + p.off_xq);
   const float4* xsc = reinterpret_cast<const float4*>(smem + p.off_xsc);
-  float* scr = reinterpret_cast<float*>(smem + p.off_scr) + warp * (kTileRows * 16 * 2 + kTileRows);
+  float* scr = reinterpret_cast<float*>(smem + p.off_scr) + warp * kScrFloats;
+  float* dsc_s = scr;
+  float* dmm_s = scr + 16 * kScrStride;
+  float* bias_s = scr + 2 * 16 * kScrStride;
   float* red = reinterpret_cast<float*>(smem + p.off_red);
   const uint32_t G = p.cols / 32u;
   const uint32_t redsz = kWarps * 2u * kTileRows * p.batch;  // one buffer (per parity)
+  const uint32_t nbatch = p.batch;
 
-  float acc[2][NSL][2];
+  float acc[2][NB][2];
 #pragma unroll
   for (int m = 0; m < 2; ++m)
 #pragma unroll
-    for (int s = 0; s < NSL; ++s) acc[m][s][0] = acc[m][s][1] = 0.f;
+    for (int b = 0; b < NB; ++b) acc[m][b][0] = acc[m][b][1] = 0.f;
 
   unsigned long long best = 0ull;  // epilogue thread's running argmax key
   bool aborted = false;
@@ -278,17 +283,17 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const Params p) {
     if (!mbar_wait(&bars[s], parity, p.err)) *abort_flag = 1u;
     const bool ok = *abort_flag == 0u;
     const uint32_t nb = min(static_cast<uint32_t>(kStageBlocks), p.kb_total - kst * kStageBlocks);
-    const uint32_t chunk = nb * Fmt<FMT>::kBytes;
+    const uint32_t chunk = nb * Fmt<FMT>::kBytes, rstride = chunk + p.row_pad;
     const uint8_t* stage = smem + s * p.stage_bytes;
     const uint32_t kb = static_cast<uint32_t>(warp);
 
     if (ok && kb < nb) {
       const uint32_t xg0 = (kst * kStageBlocks + kb) * 8u;  // first x-group of this block
-      // ---- per (row, group) scales of this block: lane -> row lane/2, half the groups
+      // ---- per (row, group) block scales: lane -> row lane/2, half of the groups
       {
         const uint32_t row = static_cast<uint32_t>(lane) >> 1, gh = (static_cast<uint32_t>(lane) & 1u) * (NG / 2u);
-        const uint8_t* bk = stage + row * chunk + kb * Fmt<FMT>::kBytes;
-        float bias = 0.f;
+        const uint8_t* bk = stage + row * rstride + kb * Fmt<FMT>::kBytes;
+        float bias = 0.f;  // batch-1 only: sum over this lane's groups
         if constexpr (FMT == kQ4K) {
           const float d = half_bits_to_float(bk[0] | (bk[1] << 8));
           const float dmin = half_bits_to_float(bk[2] | (bk[3] << 8));
@@ -304,14 +309,14 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const Params p) {
               sc = (mixed & 15u) | ((static_cast<uint32_t>(bk[4 + u]) >> 6) << 4);
               mn = (mixed >> 4) | ((static_cast<uint32_t>(bk[8 + u]) >> 6) << 4);
             }
-            const float dsc = d * static_cast<float>(sc), dmm = dmin * static_cast<float>(mn);
-            if constexpr (ONE) {
+            const float dsc = __fmul_rn(d, static_cast<float>(sc)), dmm = __fmul_rn(dmin, static_cast<float>(mn));
+            if constexpr (NB == 1) {
               const float4 xv = xsc[xg0 + grp];
-              scr[row * NG + grp] = dsc * xv.x;
-              bias += dmm * xv.w;
+              dsc_s[grp * kScrStride + row] = __fmul_rn(dsc, xv.x);
+              bias = fmaf(dmm, xv.w, bias);
             } else {
-              scr[2 * (row * NG + grp)] = dsc;
-              scr[2 * (row * NG + grp) + 1] = dmm;
+              dsc_s[grp * kScrStride + row] = dsc;
+              dmm_s[grp * kScrStride + row] = dmm;
             }
           }
         } else {
@@ -319,27 +324,33 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const Params p) {
 #pragma unroll
           for (uint32_t q = 0; q < NG / 2u; ++q) {
             const uint32_t grp = gh + q;
-            const float dsc = d * static_cast<float>(static_cast<int8_t>(bk[192 + grp]));
-            if constexpr (ONE) {
+            const float dsc = __fmul_rn(d, static_cast<float>(static_cast<int8_t>(bk[192 + grp])));
+            if constexpr (NB == 1) {
               const float4 xv = xsc[xg0 + grp / 2u];
-              const float coef = dsc * xv.x;
-              scr[row * NG + grp] = coef;
-              bias += 32.0f * coef * ((grp & 1u) ? xv.z : xv.y);
+              const float coef = __fmul_rn(dsc, xv.x);
+              dsc_s[grp * kScrStride + row] = coef;
+              bias = fmaf(__fmul_rn(32.0f, coef), (grp & 1u) ? xv.z : xv.y, bias);
             } else {
-              scr[row * NG + grp] = dsc;
+              dsc_s[grp * kScrStride + row] = dsc;
             }
           }
         }
-        if constexpr (ONE) {
-          bias += __shfl_xor_sync(0xffffffffu, bias, 1);
-          if ((lane & 1) == 0) scr[kTileRows * NG * 2 + row] = bias;
+        if constexpr (NB == 1) {
+          const float other = __shfl_xor_sync(0xffffffffu, bias, 1);
+          if ((lane & 1) == 0) bias_s[row] = bias + other;  // (first half) + (second half)
         }
       }
       __syncwarp();
 
+      // coefficient of (row, group) for batch row b (identical arithmetic for every NB)
+      auto coef = [&](uint32_t grp, uint32_t row, uint32_t b, uint32_t xg) -> float {
+        if constexpr (NB == 1) return dsc_s[grp * kScrStride + row];
+        else return __fmul_rn(dsc_s[grp * kScrStride + row], xsc[b * G + xg].x);
+      };
+
       if constexpr (FMT == kQ4K) {
-        const uint8_t* rg = stage + g * chunk + kb * 144u + 16u;
-        const uint8_t* rg8 = stage + (g + 8u) * chunk + kb * 144u + 16u;
+        const uint8_t* rg = stage + g * rstride + kb * 144u + 16u;
+        const uint8_t* rg8 = stage + (g + 8u) * rstride + kb * 144u + 16u;
 #pragma unroll
         for (uint32_t pch = 0; pch < 4u; ++pch) {
           const uint32_t w0 = *reinterpret_cast<const uint32_t*>(rg + 32u * pch + 4u * t);
@@ -352,41 +363,26 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const Params p) {
             const uint32_t a0 = (w0 >> sh) & 0x0f0f0f0fu, a1 = (w1 >> sh) & 0x0f0f0f0fu;
             const uint32_t a2 = (w2 >> sh) & 0x0f0f0f0fu, a3 = (w3 >> sh) & 0x0f0f0f0fu;
             const uint32_t xg = xg0 + grp;
-            if constexpr (ONE) {
-              const uint32_t* xw = xq + (xg * 2u) * 8u;
+#pragma unroll
+            for (int b = 0; b < NB; ++b) {
+              if (static_cast<uint32_t>(b) >= nbatch) break;
+              const uint32_t* xw = xq + (static_cast<size_t>(b) * G + xg) * 16u;
               const uint32_t b0 = g < 2u ? xw[g * 4u + t] : 0u, b1 = g < 2u ? xw[8u + g * 4u + t] : 0u;
               int c[4] = {0, 0, 0, 0};
               mma_u8s8_k32(c, a0, a1, a2, a3, b0, b1);
               if (t == 0u) {
-                acc[mat][0][0] += scr[g * NG + grp] * static_cast<float>(c[0] * 256 + c[1]);
-                acc[mat][0][1] += scr[(g + 8u) * NG + grp] * static_cast<float>(c[2] * 256 + c[3]);
-              }
-            } else {
-              const float2 sA = *reinterpret_cast<const float2*>(scr + 2 * (g * NG + grp));
-              const float2 sB = *reinterpret_cast<const float2*>(scr + 2 * ((g + 8u) * NG + grp));
-#pragma unroll
-              for (int sl = 0; sl < NSL; ++sl) {
-                const uint32_t* xw = xq + ((xg * NSL + sl) * 2u) * p.ncol * 4u;
-                uint32_t b0 = 0u, b1 = 0u;
-                if (g < p.ncol) {
-                  b0 = xw[g * 4u + t];
-                  b1 = xw[p.ncol * 4u + g * 4u + t];
-                }
-                int c[4] = {0, 0, 0, 0};
-                mma_u8s8_k32(c, a0, a1, a2, a3, b0, b1);
-                const uint32_t b = 4u * sl + t;
-                if (b < p.batch) {
-                  const float4 xv = xsc[b * G + xg];
-                  const float sx = xv.y + xv.z;
-                  acc[mat][sl][0] += xv.x * (sA.x * static_cast<float>(c[0] * 256 + c[1]) - sA.y * sx);
-                  acc[mat][sl][1] += xv.x * (sB.x * static_cast<float>(c[2] * 256 + c[3]) - sB.y * sx);
-                }
+                acc[mat][b][0] = fmaf(coef(grp, g, b, xg), static_cast<float>(c[0] * 256 + c[1]), acc[mat][b][0]);
+                acc[mat][b][1] = fmaf(coef(grp, g + 8u, b, xg), static_cast<float>(c[2] * 256 + c[3]),
+                                      acc[mat][b][1]);
               }
             }
           }
         }
       } else {
-        const uint32_t rowg = g * chunk + kb * 210u, rowg8 = (g + 8u) * chunk + kb * 210u;
+        // Two 16-wide groups per m16n8k32: the first group's (H, L) in B
+        // columns 0-1 over k 0..15, the second group's in columns 2-3 over k
+        // 16..31; lanes t = 0 / 1 accumulate the first / second group.
+        const uint32_t rowg = g * rstride + kb * 210u, rowg8 = (g + 8u) * rstride + kb * 210u;
 #pragma unroll
         for (uint32_t part = 0; part < 2u; ++part) {
           uint32_t ql[2][4], qh[2][2];
@@ -403,43 +399,62 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const Params p) {
             qh[1][q] = lds_u32_unaligned(stage, rowg8 + off);
           }
 #pragma unroll
-          for (uint32_t jj = 0; jj < 8u; ++jj) {
-            const uint32_t grp = part * 8u + jj, ns = (jj / 4u) * 4u, hs = (jj / 2u) * 2u;
-            const uint32_t a0 = ((ql[0][jj % 4u] >> ns) & 0x0f0f0f0fu) | (((qh[0][jj % 2u] >> hs) & 0x03030303u) << 4);
-            const uint32_t a1 = ((ql[1][jj % 4u] >> ns) & 0x0f0f0f0fu) | (((qh[1][jj % 2u] >> hs) & 0x03030303u) << 4);
-            const uint32_t xg = xg0 + grp / 2u, half = grp & 1u;
-            if constexpr (ONE) {
-              const uint32_t b0 = g < 2u ? xq[((xg * 2u + half) * 2u + g) * 4u + t] : 0u;
-              int c[4] = {0, 0, 0, 0};
-              mma_u8s8_k16(c, a0, a1, b0);
-              if (t == 0u) {
-                acc[mat][0][0] += scr[g * NG + grp] * static_cast<float>(c[0] * 256 + c[1]);
-                acc[mat][0][1] += scr[(g + 8u) * NG + grp] * static_cast<float>(c[2] * 256 + c[3]);
-              }
-            } else {
-              const float dA = scr[g * NG + grp], dB = scr[(g + 8u) * NG + grp];
+          for (uint32_t j = 0; j < 4u; ++j) {
+            uint32_t a[4];
 #pragma unroll
-              for (int sl = 0; sl < NSL; ++sl) {
-                const uint32_t* xw = xq + ((xg * NSL + sl) * 2u + half) * p.ncol * 4u;
-                const uint32_t b0 = g < p.ncol ? xw[g * 4u + t] : 0u;
-                int c[4] = {0, 0, 0, 0};
-                mma_u8s8_k16(c, a0, a1, b0);
-                const uint32_t b = 4u * sl + t;
-                if (b < p.batch) {
-                  const float4 xv = xsc[b * G + xg];
-                  const float sx32 = 32.0f * (half ? xv.z : xv.y);
-                  acc[mat][sl][0] += xv.x * (dA * (static_cast<float>(c[0] * 256 + c[1]) - sx32));
-                  acc[mat][sl][1] += xv.x * (dB * (static_cast<float>(c[2] * 256 + c[3]) - sx32));
-                }
+            for (uint32_t h = 0; h < 2u; ++h) {  // h: first / second group of the pair
+              const uint32_t jj = 2u * j + h, ns = (jj / 4u) * 4u, hs = (jj / 2u) * 2u;
+              a[2 * h] = ((ql[0][jj % 4u] >> ns) & 0x0f0f0f0fu) | (((qh[0][jj % 2u] >> hs) & 0x03030303u) << 4);
+              a[2 * h + 1] = ((ql[1][jj % 4u] >> ns) & 0x0f0f0f0fu) | (((qh[1][jj % 2u] >> hs) & 0x03030303u) << 4);
+            }
+            const uint32_t xg = xg0 + part * 4u + j;
+            const uint32_t grp = part * 8u + 2u * j + (t & 1u);
+#pragma unroll
+            for (int b = 0; b < NB; ++b) {
+              if (static_cast<uint32_t>(b) >= nbatch) break;
+              const uint32_t word = g < 4u ? xq[(static_cast<size_t>(b) * G + xg) * 16u + g * 4u + t] : 0u;
+              const uint32_t b0 = g < 2u ? word : 0u, b1 = (g >= 2u && g < 4u) ? word : 0u;
+              int c[4] = {0, 0, 0, 0};
+              mma_u8s8_k32(c, a[0], a[1], a[2], a[3], b0, b1);
+              if (t < 2u) {
+                acc[mat][b][0] = fmaf(coef(grp, g, b, xg), static_cast<float>(c[0] * 256 + c[1]), acc[mat][b][0]);
+                acc[mat][b][1] = fmaf(coef(grp, g + 8u, b, xg), static_cast<float>(c[2] * 256 + c[3]),
+                                      acc[mat][b][1]);
               }
             }
           }
         }
       }
-      if constexpr (ONE) {
-        if (t == 0u) {
-          acc[mat][0][0] -= scr[kTileRows * NG * 2 + g];
-          acc[mat][0][1] -= scr[kTileRows * NG * 2 + g + 8u];
+      // block offsets (Q4_K dmin*m, Q6_K -32), in the same order for every NB
+      if (t == 0u) {
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+          if (static_cast<uint32_t>(b) >= nbatch) break;
+#pragma unroll
+          for (uint32_t hr = 0; hr < 2u; ++hr) {
+            const uint32_t row = g + 8u * hr;
+            float bias;
+            if constexpr (NB == 1) {
+              bias = bias_s[row];
+            } else {
+              float part_b[2] = {0.f, 0.f};
+#pragma unroll
+              for (uint32_t grp = 0; grp < NG; ++grp) {
+                const uint32_t xg = xg0 + (FMT == kQ4K ? grp : grp / 2u);
+                const float4 xv = xsc[b * G + xg];
+                float term;
+                if constexpr (FMT == kQ4K) {
+                  part_b[grp / (NG / 2u)] = fmaf(dmm_s[grp * kScrStride + row], xv.w, part_b[grp / (NG / 2u)]);
+                } else {
+                  const float cf = __fmul_rn(dsc_s[grp * kScrStride + row], xv.x);
+                  term = (grp & 1u) ? xv.z : xv.y;
+                  part_b[grp / (NG / 2u)] = fmaf(__fmul_rn(32.0f, cf), term, part_b[grp / (NG / 2u)]);
+                }
+              }
+              bias = part_b[0] + part_b[1];
+            }
+            acc[mat][b][hr] = acc[mat][b][hr] - bias;
+          }
         }
       }
       __syncwarp();
@@ -452,13 +467,16 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const Params p) {
       for (int m = 0; m < 2; ++m) {
         if (static_cast<uint32_t>(m) >= p.nmat) break;
 #pragma unroll
-        for (int sl = 0; sl < NSL; ++sl) {
-          const uint32_t b = 4u * sl + t;
-          if (b < p.batch) {
-            redbuf[((warp * 2 + m) * kTileRows + g) * p.batch + b] = acc[m][sl][0];
-            redbuf[((warp * 2 + m) * kTileRows + g + 8u) * p.batch + b] = acc[m][sl][1];
+        for (int b = 0; b < NB; ++b) {
+          // Q6_K: the second group of every pair was accumulated by lane t = 1
+          const float o0 = __shfl_down_sync(0xffffffffu, acc[m][b][0], 1);
+          const float o1 = __shfl_down_sync(0xffffffffu, acc[m][b][1], 1);
+          if (t == 0u && static_cast<uint32_t>(b) < nbatch) {
+            redbuf[((warp * 2 + m) * kTileRows + g) * nbatch + b] = FMT == kQ6K ? acc[m][b][0] + o0 : acc[m][b][0];
+            redbuf[((warp * 2 + m) * kTileRows + g + 8u) * nbatch + b] =
+                FMT == kQ6K ? acc[m][b][1] + o1 : acc[m][b][1];
           }
-          acc[m][sl][0] = acc[m][sl][1] = 0.f;
+          acc[m][b][0] = acc[m][b][1] = 0.f;
         }
       }
     }
@@ -473,11 +491,11 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const Params p) {
       issued = it + p.nstage + 1u;
     }
     if (tile_end)
-      for (uint32_t idx = threadIdx.x; idx < kTileRows * p.batch; idx += kThreads) {
+      for (uint32_t idx = threadIdx.x; idx < kTileRows * nbatch; idx += kThreads) {
         const uint32_t row = idx % kTileRows, b = idx / kTileRows;
         float v[2] = {0.f, 0.f};
         for (uint32_t m = 0; m < p.nmat; ++m)
-          for (int w = 0; w < kWarps; ++w) v[m] += redbuf[((w * 2 + m) * kTileRows + row) * p.batch + b];
+          for (int w = 0; w < kWarps; ++w) v[m] += redbuf[((w * 2 + m) * kTileRows + row) * nbatch + b];
         const uint32_t R = tile * kTileRows + row;
         float* yp = p.y ? p.y + static_cast<size_t>(b) * p.y_stride + R : nullptr;
         if (p.epilogue == kSwiGLU) {
@@ -507,9 +525,9 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const Params p) {
   if (p.argmax) {
     unsigned long long* cand = reinterpret_cast<unsigned long long*>(smem + p.off_red);
     __syncthreads();
-    cand[threadIdx.x] = threadIdx.x < kTileRows * p.batch ? best : 0ull;
+    cand[threadIdx.x] = threadIdx.x < kTileRows * nbatch ? best : 0ull;
     __syncthreads();
-    if (threadIdx.x < p.batch) {
+    if (threadIdx.x < nbatch) {
       unsigned long long m = 0ull;
       for (uint32_t row = 0; row < kTileRows; ++row) {
         const unsigned long long c = cand[threadIdx.x * kTileRows + row];
@@ -533,14 +551,9 @@ __global__ void gemv_f32_kernel(const float* __restrict__ W, uint32_t rows, uint
   if (lane == 0) y[b * y_stride + r] = s;
 }
 
-template <int FMT, int NSL, bool ONE>
-cudaError_t launch_t(const GemvArgs& a, Params p, cudaStream_t s) {
-  auto kernel = gemv_kernel<FMT, NSL, ONE>;
-  const uint32_t bytes = Fmt<FMT>::kBytes;
-  p.stage_bytes = kTileRows * kStageBlocks * bytes;
-  p.nstage = FMT == kQ4K ? 4u : 3u;
-  p.ncol = ONE ? 2u : 8u;
-  const uint32_t G = a.cols / 32u;
+template <int FMT>
+uint32_t smem_bytes(uint32_t cols, uint32_t batch, Params* p) {
+  const uint32_t G = cols / 32u;
   uint32_t off = 0;
   auto carve = [&](uint32_t sz, uint32_t align) {
     off = (off + align - 1) / align * align;
@@ -548,15 +561,34 @@ cudaError_t launch_t(const GemvArgs& a, Params p, cudaStream_t s) {
     off += sz;
     return at;
   };
-  carve(p.nstage * p.stage_bytes, 128);
-  p.off_bar = carve(8 * p.nstage, 8);
-  p.off_xq = carve(G * NSL * 2 * p.ncol * 16, 16);
-  p.off_xsc = carve(a.batch * G * 16, 16);
-  p.off_scr = carve(kWarps * (kTileRows * 16 * 2 + kTileRows) * 4, 16);
-  const uint32_t red_floats = 2 * kWarps * 2 * kTileRows * a.batch;
-  p.off_red = carve(max(red_floats * 4u, static_cast<uint32_t>(kThreads * 8)), 16);
-  p.off_misc = carve(128, 16);
-  const uint32_t smem = off;
+  const uint32_t nstage = FMT == kQ4K ? 4u : 3u;
+  const uint32_t stage_bytes = kTileRows * (kStageBlocks * Fmt<FMT>::kBytes + Fmt<FMT>::kPad);
+  carve(nstage * stage_bytes, 128);
+  const uint32_t off_bar = carve(8 * nstage, 8);
+  const uint32_t off_xq = carve(batch * G * 64, 16);
+  const uint32_t off_xsc = carve(batch * G * 16, 16);
+  const uint32_t off_scr = carve(kWarps * kScrFloats * 4, 16);
+  const uint32_t red_floats = 2 * kWarps * 2 * kTileRows * batch;
+  const uint32_t off_red = carve(max(red_floats * 4u, static_cast<uint32_t>(kThreads * 8)), 16);
+  const uint32_t off_misc = carve(128, 16);
+  if (p) {
+    p->nstage = nstage;
+    p->stage_bytes = stage_bytes;
+    p->row_pad = Fmt<FMT>::kPad;
+    p->off_bar = off_bar;
+    p->off_xq = off_xq;
+    p->off_xsc = off_xsc;
+    p->off_scr = off_scr;
+    p->off_red = off_red;
+    p->off_misc = off_misc;
+  }
+  return off;
+}
+
+template <int FMT, int NB>
+cudaError_t launch_t(const GemvArgs& a, Params p, cudaStream_t s) {
+  auto kernel = gemv_kernel<FMT, NB>;
+  const uint32_t smem = smem_bytes<FMT>(a.cols, p.batch, &p);
   // One-time kernel setup and occupancy per (kernel instance, smem size): these
   // queries cost microseconds and must stay off the per-launch path
   // (function attributes are per device: index the cache by device ordinal).
@@ -604,6 +636,14 @@ cudaError_t launch_t(const GemvArgs& a, Params p, cudaStream_t s) {
   return cudaLaunchKernelEx(&cfg, kernel, p);
 }
 
+template <int FMT>
+cudaError_t launch_fmt(const GemvArgs& a, Params p, cudaStream_t s) {
+  if (p.batch == 1) return launch_t<FMT, 1>(a, p, s);
+  if (p.batch == 2) return launch_t<FMT, 2>(a, p, s);
+  if (p.batch <= 4) return launch_t<FMT, 4>(a, p, s);
+  return launch_t<FMT, 8>(a, p, s);
+}
+
 }  // namespace
 
 cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t s) {
@@ -647,17 +687,24 @@ cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t s) {
   p.argmax = a.argmax;
   p.err = a.err;
   p.running = a.running;
-  const uint32_t nsl = (a.batch + 3) / 4;
-  if (a.fmt == kQ4K) {
-    if (a.batch == 1) return launch_t<kQ4K, 1, true>(a, p, s);
-    if (nsl == 1) return launch_t<kQ4K, 1, false>(a, p, s);
-    if (nsl == 2) return launch_t<kQ4K, 2, false>(a, p, s);
-    return launch_t<kQ4K, 8, false>(a, p, s);
+  // Batch rows run in launches of at most 8 rows (each launch streams the
+  // weights once); a launch's activation tables must fit in shared memory.
+  for (uint32_t b0 = 0; b0 < a.batch;) {
+    uint32_t nb = min(8u, a.batch - b0);
+    while (nb > 1 && (a.fmt == kQ4K ? smem_bytes<kQ4K>(a.cols, nb, nullptr) : smem_bytes<kQ6K>(a.cols, nb, nullptr)) >
+                         227u * 1024u)
+      nb /= 2;
+    Params q = p;
+    q.batch = nb;
+    q.x = a.x + static_cast<size_t>(b0) * x_stride;
+    q.z = a.z ? a.z + static_cast<size_t>(b0) * x_stride : nullptr;
+    q.y = a.y ? a.y + static_cast<size_t>(b0) * p.y_stride : nullptr;
+    q.argmax = a.argmax ? a.argmax + b0 : nullptr;
+    const cudaError_t e = a.fmt == kQ4K ? launch_fmt<kQ4K>(a, q, s) : launch_fmt<kQ6K>(a, q, s);
+    if (e != cudaSuccess) return e;
+    b0 += nb;
   }
-  if (a.batch == 1) return launch_t<kQ6K, 1, true>(a, p, s);
-  if (nsl == 1) return launch_t<kQ6K, 1, false>(a, p, s);
-  if (nsl == 2) return launch_t<kQ6K, 2, false>(a, p, s);
-  return launch_t<kQ6K, 8, false>(a, p, s);
+  return cudaSuccess;
 }
 
 cudaError_t launch_gemv_f32(const float* W, uint32_t rows, uint32_t cols, const float* x, uint32_t x_stride,

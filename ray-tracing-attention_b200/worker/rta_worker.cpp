@@ -1,0 +1,326 @@
+// rta_worker -- drop-in replacement for the reference's native worker process.
+//
+// It speaks the binary stdin/stdout protocol of ray_tracing/native/src/
+// optical_resident.cpp (main loop :964-971) so that the unmodified
+// ray_tracing.runtime.ResidentRuntime (resident_runtime.py:10) drives the B200
+// backend: same argv, same hello words, same request framing <3I op,count,debug>
+// + body, same reply framing <2I status,size> + payload, and the payload
+// layouts its parsers read (resident_runtime.py:116-263).  All model work goes
+// through librta_cuda.so (include/rta.h); this file only frames bytes.
+//
+// Served operations: 0 quit, 1 prefill, 2 generate, 4 vocabulary, 6 mlp,
+// 8 resources, 9 stream, 10 grow (capacity).  Operations tied to the ray-traced
+// caches and diagnostics (5 codec, 7 aperture, 11/12 checkpointed prefill,
+// 13 finish_history, 14 attention receipts, 15 statistics) answer status 1, which
+// the runtime turns into RuntimeError.
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <iostream>
+#include <sstream>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "rta.h"
+
+namespace {
+
+using Clock = std::chrono::steady_clock;
+
+// ------------------------------------------------------------ model.json
+// Minimal reader for the flat "model_spec" object the compiler writes
+// (ray_tracing/compiler/export.py:233, spec.py:66).
+struct SpecReader {
+  std::string text;
+  size_t find_key(const std::string& key) const {
+    const size_t spec = text.find("\"model_spec\"");
+    if (spec == std::string::npos) throw std::runtime_error("model.json has no model_spec");
+    const size_t at = text.find("\"" + key + "\"", spec);
+    if (at == std::string::npos) throw std::runtime_error("model_spec field missing: " + key);
+    return text.find(':', at) + 1;
+  }
+  double number(const std::string& key) const {
+    size_t i = find_key(key);
+    while (i < text.size() && std::isspace(static_cast<unsigned char>(text[i]))) ++i;
+    if (text.compare(i, 4, "true") == 0) return 1.0;
+    if (text.compare(i, 5, "false") == 0) return 0.0;
+    return std::stod(text.substr(i, 40));
+  }
+  std::vector<std::string> strings(const std::string& key) const {
+    size_t i = text.find('[', find_key(key)), end = text.find(']', i);
+    std::vector<std::string> out;
+    while (true) {
+      const size_t a = text.find('"', i);
+      if (a == std::string::npos || a > end) break;
+      const size_t b = text.find('"', a + 1);
+      out.push_back(text.substr(a + 1, b - a - 1));
+      i = b + 1;
+    }
+    return out;
+  }
+};
+
+rta_model_spec read_spec(const std::string& dir) {
+  std::ifstream f(dir + "/model.json");
+  if (!f) throw std::runtime_error("cannot read model.json next to the model payload");
+  std::stringstream ss;
+  ss << f.rdbuf();
+  SpecReader r{ss.str()};
+  rta_model_spec s{};
+  s.hidden_size = static_cast<uint32_t>(r.number("hidden_size"));
+  s.middle_size = static_cast<uint32_t>(r.number("middle_size"));
+  s.vocabulary_size = static_cast<uint32_t>(r.number("vocabulary_size"));
+  s.attention_heads = static_cast<uint32_t>(r.number("attention_heads"));
+  s.kv_heads = static_cast<uint32_t>(r.number("kv_heads"));
+  s.attention_head_dim = static_cast<uint32_t>(r.number("attention_head_dim"));
+  s.rotary_dim = static_cast<uint32_t>(r.number("rotary_dim"));
+  s.state_heads = static_cast<uint32_t>(r.number("state_heads"));
+  s.state_key_heads = static_cast<uint32_t>(r.number("state_key_heads"));
+  s.state_head_dim = static_cast<uint32_t>(r.number("state_head_dim"));
+  s.attention_gate = static_cast<uint32_t>(r.number("attention_gate"));
+  s.qk_norm = static_cast<uint32_t>(r.number("qk_norm"));
+  s.rope_theta = static_cast<float>(r.number("rope_theta"));
+  s.norm_epsilon = static_cast<float>(r.number("norm_epsilon"));
+  const auto kinds = r.strings("layer_types");
+  if (kinds.empty() || kinds.size() > 256) throw std::runtime_error("model_spec.layer_types out of range");
+  s.depth = static_cast<uint32_t>(kinds.size());
+  for (size_t i = 0; i < kinds.size(); ++i) s.layer_kinds[i] = kinds[i] == "full" ? 1 : 2;
+  return s;
+}
+
+// ------------------------------------------------------------- framing
+template <class T>
+void append(std::vector<char>& out, const T* v, size_t n) {
+  const char* p = reinterpret_cast<const char*>(v);
+  out.insert(out.end(), p, p + n * sizeof(T));
+}
+template <class T>
+void append(std::vector<char>& out, std::initializer_list<T> v) {
+  append(out, v.begin(), v.size());
+}
+void reply(uint32_t status, const std::vector<char>& payload) {
+  const uint32_t header[2] = {status, static_cast<uint32_t>(payload.size())};
+  std::cout.write(reinterpret_cast<const char*>(header), 8);
+  if (!payload.empty()) std::cout.write(payload.data(), static_cast<std::streamsize>(payload.size()));
+  std::cout.flush();
+}
+template <class T>
+void input(std::vector<T>& v, size_t n) {
+  v.resize(n);
+  if (n && !std::cin.read(reinterpret_cast<char*>(v.data()), static_cast<std::streamsize>(n * sizeof(T))))
+    throw std::runtime_error("Incomplete resident request body");
+}
+
+struct Worker {
+  rta_model* model = nullptr;
+  rta_model_spec spec{};
+  std::string model_bin, geometry_bin, vocab_bin;
+  uint32_t capacity = 300, position = 0;
+  uint32_t stops[2] = {0xffffffffu, 0xffffffffu};
+
+  void check(rta_status st) {
+    if (st != RTA_OK) throw std::runtime_error(rta_model_last_error());
+  }
+  void open() {
+    check(rta_model_open_files(&spec, model_bin.c_str(), geometry_bin.c_str(), vocab_bin.c_str(), capacity, 0,
+                               &model));
+  }
+
+  // op 1: ids[count] + stops[2] -> 6 doubles + 8 control words (+ batch statistics)
+  void prefill(uint32_t count) {
+    std::vector<uint32_t> ids, st;
+    input(ids, count);
+    input(st, 2);
+    stops[0] = st[0];
+    stops[1] = st[1];
+    const auto t0 = Clock::now();
+    double gpu = 0.0;
+    check(rta_model_prefill(model, ids.data(), count, stops, &gpu));
+    const double wall = std::chrono::duration<double, std::milli>(Clock::now() - t0).count();
+    position = count;
+    std::vector<char> out;
+    append<double>(out, {0.0, gpu, wall, wall, 0.0, 0.0});
+    append<uint32_t>(out, {ids.back(), 0u, 1u, 0u, stops[0], stops[1], 0u, 0u});
+    append<uint64_t>(out, {1ull, static_cast<uint64_t>(count), 0ull, static_cast<uint64_t>(count)});
+    reply(0, out);
+  }
+
+  // GenerationPacket::bytes (optical_resident.cpp:63-71), parsed by _generation_result
+  std::vector<char> packet(const std::vector<uint32_t>& ids, bool running, double gpu, double wall) {
+    std::vector<char> out;
+    const uint32_t n = static_cast<uint32_t>(std::min<size_t>(ids.size(), 64));
+    append<double>(out, {gpu, wall, 1.0, 1.0, 0.0, 0.0, static_cast<double>(position), 0.0, 0, 0, 0, 0, 0, 0, 0, 0,
+                         0, 0});
+    append<uint32_t>(out, {n ? ids[n - 1] : 0u, n, running ? 1u : 0u, 0u, stops[0], stops[1], 0u, 0u});
+    std::vector<uint32_t> id64(64, 0u);
+    std::copy_n(ids.begin(), n, id64.begin());
+    append(out, id64.data(), 64);
+    append<uint32_t>(out, {spec.middle_size * spec.depth, spec.middle_size * spec.depth, spec.vocabulary_size, 0u,
+                           0u});
+    append<double>(out, {0.0, 0.0, 0.0, 0.0});
+    append<uint32_t>(out, {0u, 0u, 0u, 0u});
+    append<double>(out, {0.0, 0.0, 0.0, 0.0, 0.0});
+    append<uint32_t>(out, {0u, 0u});
+    append<uint64_t>(out, {0ull, 0ull});
+    return out;
+  }
+
+  bool generate_one_packet(uint32_t count) {
+    std::vector<uint32_t> ids(count);
+    uint32_t n = 0;
+    double gpu = 0.0;
+    const auto t0 = Clock::now();
+    check(rta_model_generate(model, count, ids.data(), &n, &gpu));
+    const double wall = std::chrono::duration<double, std::milli>(Clock::now() - t0).count();
+    ids.resize(n);
+    position += n;
+    const bool running = !(n && (ids.back() == stops[0] || ids.back() == stops[1])) && n == count;
+    reply(0, packet(ids, running, gpu, wall));
+    return running;
+  }
+
+  // op 4: hidden[D] -> timings, winner, hit ids, first decoded rows, packets, charts
+  void vocabulary() {
+    const uint32_t D = spec.hidden_size, V = spec.vocabulary_size, blocks = D / 256;
+    std::vector<float> h;
+    input(h, D);
+    uint32_t arg = 0;
+    float best = 0.f;
+    const auto t0 = Clock::now();
+    check(rta_model_vocabulary(model, h.data(), nullptr, &arg, &best));
+    const double wall = std::chrono::duration<double, std::milli>(Clock::now() - t0).count();
+    std::vector<char> out;
+    append<double>(out, {wall, wall, 0.0, 0.0, 0.0});
+    float b20 = best + 20.0f, one = 1.0f;
+    uint32_t w[4] = {arg, 0, 0, 0};
+    std::memcpy(&w[1], &b20, 4);
+    std::memcpy(&w[2], &one, 4);
+    std::memcpy(&w[3], &one, 4);
+    append(out, w, 4);
+    append<uint32_t>(out, {V});
+    std::vector<uint32_t> ids(V);
+    for (uint32_t i = 0; i < V; ++i) ids[i] = i;
+    append(out, ids.data(), V);
+    std::vector<float> rows(256ull * D, 0.f);  // geometric word rows are a ray-traced artefact: zeros
+    append(out, rows.data(), rows.size());
+    std::vector<uint32_t> packets(blocks * 256ull);
+    std::memcpy(packets.data(), h.data(), D * 4ull);  // encodePathPair is the identity on the bits
+    append(out, packets.data(), packets.size());
+    std::vector<float> charts(blocks * 4ull, 0.f);
+    append(out, charts.data(), charts.size());
+    append<uint32_t>(out, {V * blocks});
+    reply(0, out);
+  }
+
+  // op 6: rows x D -> rows x D output, rows x middle activation, rows feature hits, 3 timings
+  void mlp(uint32_t rows, uint32_t layer) {
+    const uint32_t D = spec.hidden_size, F = spec.middle_size;
+    if (rows == 0 || rows > std::min(capacity, 32u) || layer >= spec.depth)
+      throw std::runtime_error("Invalid optical MLP input");
+    std::vector<float> x;
+    input(x, static_cast<size_t>(rows) * D);
+    for (float v : x)
+      if (!std::isfinite(v)) throw std::runtime_error("Optical MLP input must be finite");
+    std::vector<float> y(static_cast<size_t>(rows) * D), act(static_cast<size_t>(rows) * F);
+    const auto t0 = Clock::now();
+    check(rta_model_mlp(model, layer, x.data(), rows, y.data(), act.data()));
+    const double wall = std::chrono::duration<double, std::milli>(Clock::now() - t0).count();
+    std::vector<char> out;
+    append(out, y.data(), y.size());
+    append(out, act.data(), act.size());
+    std::vector<uint32_t> hits(rows, F);
+    append(out, hits.data(), rows);
+    append<double>(out, {0.0, wall, 0.0});
+    reply(0, out);
+  }
+
+  // op 8: the 61 counters resident_runtime.resources() names, in its order
+  void resources() {
+    uint64_t r[9] = {0};
+    check(rta_model_resources(model, r, 9));
+    std::vector<uint64_t> v(61, 0ull);
+    v[1] = r[0] + r[1] + r[2] + r[3];  // device allocation bytes (payloads, derived, history, state)
+    v[9] = r[0];                        // packed coefficient bytes
+    v[13] = r[2];                       // history bytes
+    v[15] = r[3];                       // recurrent field bytes
+    v[26] = 32;                         // workspace rows (MLP check rows)
+    v[38] = 256;                        // attention block
+    std::vector<char> out;
+    append(out, v.data(), v.size());
+    reply(0, out);
+  }
+
+  // op 10: reopen with a larger history ring -> previous, capacity, wall ms
+  void grow(uint32_t next) {
+    if (next <= capacity) throw std::runtime_error("Invalid tree growth request");
+    const auto t0 = Clock::now();
+    const uint32_t previous = capacity;
+    rta_model_close(model);
+    model = nullptr;
+    capacity = next;
+    open();
+    position = 0;  // the reference re-prefills after growth
+    std::vector<char> out;
+    append<double>(out, {static_cast<double>(previous), static_cast<double>(capacity),
+                         std::chrono::duration<double, std::milli>(Clock::now() - t0).count()});
+    reply(0, out);
+  }
+};
+
+}  // namespace
+
+int main(int argc, char** argv) {
+  try {
+    if (argc < 3) throw std::runtime_error("Usage: rta_worker optical_model.bin vocabulary.bin [capacity] ...");
+    Worker w;
+    w.model_bin = argv[1];
+    w.vocab_bin = argv[2];
+    const std::string dir = w.model_bin.substr(0, w.model_bin.find_last_of('/') == std::string::npos
+                                                       ? 0
+                                                       : w.model_bin.find_last_of('/'));
+    w.geometry_bin = (dir.empty() ? std::string(".") : dir) + "/geometry_weights.bin";
+    w.capacity = argc > 3 ? static_cast<uint32_t>(std::stoul(argv[3])) : 300u;
+    w.spec = read_spec(dir.empty() ? "." : dir);
+    w.open();
+    // hello: magic, depth, blocks (= depth, header word 2), middle, mode =
+    // quantization 4 | standard MLP 4096 | ordered detector 131072
+    const uint32_t hello[5] = {0x5254523au, w.spec.depth, w.spec.depth, w.spec.middle_size, 4u | 4096u | 131072u};
+    std::cout.write(reinterpret_cast<const char*>(hello), 20);
+    std::cout.flush();
+    uint32_t op = 0;
+    while (std::cin.read(reinterpret_cast<char*>(&op), 4)) {
+      if (!op) break;
+      uint32_t count = 0, debug = 0;
+      if (!std::cin.read(reinterpret_cast<char*>(&count), 4) || !std::cin.read(reinterpret_cast<char*>(&debug), 4))
+        throw std::runtime_error("Incomplete resident request");
+      try {
+        if (op == 1) w.prefill(count);
+        else if (op == 2) {
+          if (count == 0 || count > 4096) throw std::runtime_error("Resident generation expects 1..4096 tokens");
+          w.generate_one_packet(count);
+        } else if (op == 9) {
+          if (!count || count > 64) throw std::runtime_error("Resident stream expects 1..64 tokens");
+          for (uint32_t i = 0; i < count; ++i)
+            if (!w.generate_one_packet(1)) break;
+        } else if (op == 4) w.vocabulary();
+        else if (op == 6) w.mlp(count, debug);
+        else if (op == 8) w.resources();
+        else if (op == 10) w.grow(count);
+        else throw std::runtime_error("Operation " + std::to_string(op) + " is not served by the B200 backend");
+      } catch (const std::exception& e) {
+        std::cerr << e.what() << std::endl;
+        reply(1, {});
+      }
+    }
+    if (w.model) rta_model_close(w.model);
+    return 0;
+  } catch (const std::exception& e) {
+    std::cerr << e.what() << std::endl;
+    return 1;
+  }
+}
