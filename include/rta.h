@@ -117,6 +117,25 @@ RTA_API rta_status rta_attention_decode_f16(const float* q, const void* k, const
                                     uint32_t kv_stride, const float* gate, float* out, float* phys, uint32_t splits,
                                     void* workspace, size_t workspace_bytes, void* stream);
 
+/* Allocation-free variant of rta_attention_decode_f16 (no counterpart in the
+ * reference; it exists for callers that may not allocate device memory while
+ * decoding, e.g. inside another framework's allocator or a latency-critical
+ * serving loop).  The split records live in a fixed array inside the library's
+ * device image (about 1 MiB per GPU that loads the library, held until the
+ * process exits) instead of a caller workspace, so heads * splits must not
+ * exceed 1024 (RTA_E_ARG otherwise).  The call allocates and frees nothing.
+ * The first call on a device looks up the array's device address (set-up); make
+ * that first call before any stream capture.  All calls share the array: calls
+ * that overlap on the GPU (different streams, or different threads on one
+ * device) race and must be serialised by the caller.  device_error: optional
+ * caller-owned device word, zeroed by the call, that receives the device error
+ * bits (timeouts, non-finite output). */
+RTA_API rta_status rta_attention_decode_f16_noalloc(const float* q, const void* k, const void* v, uint32_t time,
+                                                    uint32_t capacity, uint32_t heads, uint32_t kv_heads,
+                                                    uint32_t head_dim, uint32_t pos_stride, uint32_t kv_stride,
+                                                    const float* gate, float* out, float* phys, uint32_t splits,
+                                                    uint32_t* device_error, void* stream);
+
 /* Device error word of the last operator call that had a workspace
  * (0 = clean); synchronizes `stream`. */
 RTA_API rta_status rta_workspace_error(const void* workspace, size_t workspace_bytes, void* stream, uint32_t* error_word);

@@ -16,6 +16,10 @@
 // m16n8k16 f16 MMA: columns 0-3 hold fp16(q) and columns 4-7 the fp16
 // residual q - fp16(q), so scores carry ~22 significant bits; P is split the
 // same way for the P*V MMA.  Accumulation is fp32 throughout.
+#include <mutex>
+#include <string>
+
+#include "../../include/rta.h"
 #include "rta_internal.h"
 #include "attention.h"
 
@@ -361,3 +365,102 @@ uint32_t attention_default_splits(uint32_t history, uint32_t kvh, int sms) {
 }
 
 }  // namespace rta
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of the decode attention.
+//
+// Some callers cannot allocate device memory at the moment they decode: a
+// serving loop that runs under another framework's caching allocator (which
+// owns every byte of the GPU and forbids a foreign cudaMalloc), code that must
+// not trigger cudaMalloc's implicit device synchronisation on a latency-critical
+// path, or an embedding that has no place to keep a per-call workspace.  For
+// them the split records live in one fixed array in this library's device
+// image instead of a caller workspace: every GPU that loads the library keeps
+// it (about 1 MiB) until the process exits, and every call shares it.
+namespace rta {
+namespace {
+constexpr uint32_t kStaticRecords = 1024;  // (query heads) x (splits) records at most
+constexpr size_t kStaticFloats = kStaticRecords * (2 + kHD);
+static __device__ __align__(256) float g_attention_scratch[kStaticFloats];
+std::mutex g_scratch_mutex;
+float* g_scratch_addr[64] = {nullptr};  // device address of the array, per device ordinal
+}  // namespace
+}  // namespace rta
+
+extern "C" rta_status rta_attention_decode_f16_noalloc(const float* q, const void* k, const void* v, uint32_t time,
+                                                       uint32_t capacity, uint32_t heads, uint32_t kv_heads,
+                                                       uint32_t head_dim, uint32_t pos_stride, uint32_t kv_stride,
+                                                       const float* gate, float* out, float* phys, uint32_t splits,
+                                                       uint32_t* device_error, void* stream) {
+  using namespace rta;
+  if (!q || !k || !v || !out || head_dim != kHD || kv_heads == 0 || heads != 4 * kv_heads || capacity == 0 ||
+      splits == 0) {
+    set_last_error("rta_attention_decode_f16_noalloc: head_dim 256, heads == 4*kv_heads, capacity and splits > 0");
+    return RTA_E_ARG;
+  }
+  if (static_cast<size_t>(heads) * splits > kStaticRecords) {
+    set_last_error("rta_attention_decode_f16_noalloc: heads * splits = " +
+                   std::to_string(static_cast<size_t>(heads) * splits) + " exceeds the static scratch limit of " +
+                   std::to_string(kStaticRecords) + " records");
+    return RTA_E_ARG;
+  }
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+    set_last_error("rta_attention_decode_f16_noalloc: no current CUDA device");
+    return RTA_E_CUDA;
+  }
+  float* scratch = nullptr;
+  {
+    // One-time set-up per device, with that device current: the array's name is
+    // only a host-side stand-in, the kernel needs its device address.
+    std::lock_guard<std::mutex> lock(g_scratch_mutex);
+    if (!g_scratch_addr[dev]) {
+      void* addr = nullptr;
+      e = cudaGetSymbolAddress(&addr, g_attention_scratch);
+      if (e != cudaSuccess || !addr) {
+        set_last_error(std::string("rta_attention_decode_f16_noalloc: cudaGetSymbolAddress: ") +
+                       cudaGetErrorString(e));
+        return RTA_E_CUDA;
+      }
+      g_scratch_addr[dev] = static_cast<float*>(addr);
+    }
+    scratch = g_scratch_addr[dev];
+  }
+  const size_t recs = static_cast<size_t>(heads) * splits;
+  AttnParams p;
+  p.q = q;
+  p.q_seq_stride = static_cast<size_t>(heads) * head_dim;
+  p.k = static_cast<const __half*>(k);
+  p.v = static_cast<const __half*>(v);
+  p.kv_stride = static_cast<size_t>(kv_stride) * head_dim;
+  p.pos_stride = static_cast<size_t>(pos_stride) * head_dim;
+  p.heads = heads;
+  p.kvh = kv_heads;
+  p.hd = head_dim;
+  p.capacity = capacity;
+  p.t = time;
+  p.gate = gate;
+  p.out = out;
+  p.out_seq_stride = static_cast<size_t>(heads) * head_dim;
+  p.phys = phys;
+  p.err = device_error;
+  p.part_m = scratch;
+  p.part_z = scratch + recs;
+  p.part_o = scratch + 2 * recs;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (device_error) {
+    e = cudaMemsetAsync(device_error, 0, 4, s);
+    if (e != cudaSuccess) {
+      set_last_error(std::string("rta_attention_decode_f16_noalloc: ") + cudaGetErrorString(e));
+      return RTA_E_CUDA;
+    }
+  }
+  e = launch_attention(p, splits, 1, false, s);
+  if (e != cudaSuccess) {
+    set_last_error(std::string("rta_attention_decode_f16_noalloc: ") + cudaGetErrorName(e) + " (" +
+                   cudaGetErrorString(e) + ")");
+    return RTA_E_CUDA;
+  }
+  return RTA_OK;
+}

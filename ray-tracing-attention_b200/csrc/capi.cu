@@ -45,6 +45,10 @@ __global__ void readout_finish_kernel(const unsigned long long* keys, uint32_t b
 }
 }  // namespace
 
+namespace rta {
+void set_last_error(const std::string& msg) { g_last_error = msg; }
+}  // namespace rta
+
 extern "C" {
 
 const char* rta_last_error(void) { return g_last_error.c_str(); }

@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 #include <cstddef>
 #include <cstdint>
+#include <string>
 
 #include "rta_device.cuh"
 
@@ -15,6 +16,9 @@ constexpr uint32_t kQ4KBytes = 144, kQ6KBytes = 210;
 constexpr uint32_t kMaxBatch = 32;  // GEMV batch rows per launch (mma slices of 4)
 
 inline uint32_t block_bytes(int fmt) { return fmt == kQ4K ? kQ4KBytes : kQ6KBytes; }
+
+// Record the thread-local text returned by rta_last_error() (capi.cu).
+void set_last_error(const std::string& msg);
 
 // ---------------------------------------------------------------- quant.cu
 cudaError_t launch_quantize(int fmt, const float* src, size_t nblocks, uint8_t* dst, cudaStream_t s);
