@@ -158,7 +158,7 @@ def _rotations(footprint: int) -> int:
 
 class MLPWorkload(Workload):
     name, metric, unit, dtype, dominant = ("mlp", "SwiGLU MLP decode steps/s (Q4_K, 2048-6144-2048)", "steps/s",
-                                           "q4k-int8mma-f32acc", "gemv_kernel<Q4_K> gate+up (SwiGLU)")
+                                           "q4k-int8mma-f32acc", "gemv_tiled_kernel<Q4_K> gate+up (SwiGLU)")
     D, F = 2048, 6144
     launches_per_step = 2
 
@@ -168,8 +168,12 @@ class MLPWorkload(Workload):
         self.ops, self.torch = ops, torch
         per = 3 * self.F * self.D // 256 * 144
         self.copies = _rotations(per)
-        self.w = [[ops.synthetic_blocks(12, self.F, self.D, seed + 3 * c + j) for j in range(2)] +
-                  [ops.synthetic_blocks(12, self.D, self.F, seed + 3 * c + 2)] for c in range(self.copies)]
+        # weights re-laid once into the tiled GEMV order, as the engine does at load
+        tile = lambda w, r, c: ops.tile_weights(12, w, r, c)[1]
+        self.w = [[tile(ops.synthetic_blocks(12, self.F, self.D, seed + 3 * c + j), self.F, self.D) for j in range(2)] +
+                  [tile(ops.synthetic_blocks(12, self.D, self.F, seed + 3 * c + 2), self.D, self.F)]
+                  for c in range(self.copies)]
+        self.fmt = ops.TILED[12]
         self.x = ops.synthetic_normal(self.D, seed + 999)
         self.act = torch.empty(1, self.F, device="cuda")
         self.y = torch.empty(1, self.D, device="cuda")
@@ -179,11 +183,11 @@ class MLPWorkload(Workload):
 
     def step(self, i):
         w = self.w[i % self.copies]
-        self.ops.mlp_swiglu(12, w[0], w[1], w[2], self.D, self.F, self.x, y=self.y, act=self.act)
+        self.ops.mlp_swiglu(self.fmt, w[0], w[1], w[2], self.D, self.F, self.x, y=self.y, act=self.act)
 
     def dominant_launch(self, i):
         w = self.w[i % self.copies]
-        self.ops.gemv_swiglu(12, w[0], w[1], self.F, self.D, self.x, act=self.act)  # gate+up, 2 x 6144x2048
+        self.ops.gemv_swiglu(self.fmt, w[0], w[1], self.F, self.D, self.x, act=self.act)  # gate+up, 2 x 6144x2048
 
     def dominant_bytes(self):
         return 2 * self.F * self.D // 256 * 144 + self.D * 4 + self.F * 4
@@ -205,7 +209,8 @@ class MLPWorkload(Workload):
 
     def config(self):
         return {"workload": "config1_swiglu_mlp_b1", "hidden": self.D, "intermediate": self.F, "format": "Q4_K",
-                "batch": 1, "l2": f"rotating {self.copies} weight copies (> L2 per pass)"}
+                "layout": "tiled (rta_tile_weights, once before timing)", "batch": 1,
+                "l2": f"rotating {self.copies} weight copies (> L2 per pass)"}
 
     def cpu_baseline(self, budget_s):
         from oracle import oracle
@@ -224,7 +229,7 @@ class MLPWorkload(Workload):
 
 class LMHeadWorkload(Workload):
     name, metric, unit, dtype, dominant = ("lmhead", "vocabulary readout tokens/s (151936x2048 Q6_K, logits+argmax)",
-                                           "tokens/s", "q6k-int8mma-f32acc", "gemv_kernel<Q6_K> readout + argmax")
+                                           "tokens/s", "q6k-int8mma-f32acc", "gemv_tiled_kernel<Q6_K> readout + argmax")
     V, D = 151936, 2048
     launches_per_step = 2
 
@@ -232,7 +237,7 @@ class LMHeadWorkload(Workload):
         import torch
         from rta_b200 import ops
         self.ops, self.torch = ops, torch
-        self.w = ops.synthetic_blocks(14, self.V, self.D, seed)
+        self.fmt, self.w = ops.tile_weights(14, ops.synthetic_blocks(14, self.V, self.D, seed), self.V, self.D)
         self.x = ops.synthetic_normal(self.D, seed + 1)
         self.ws = torch.empty(4096, dtype=torch.uint8, device="cuda")
         self.hx = torch.empty(self.D, dtype=torch.float32).pin_memory()
@@ -240,7 +245,7 @@ class LMHeadWorkload(Workload):
         self.harg = torch.empty(1, dtype=torch.int32).pin_memory()
 
     def step(self, i):
-        self.last = self.ops.readout(14, self.w, self.V, self.D, self.x, logits=True, workspace=self.ws)
+        self.last = self.ops.readout(self.fmt, self.w, self.V, self.D, self.x, logits=True, workspace=self.ws)
 
     dominant_launch = step
 
@@ -262,8 +267,8 @@ class LMHeadWorkload(Workload):
         return self.dominant_bytes()
 
     def config(self):
-        return {"workload": "config3_lmhead_b1", "vocab": self.V, "hidden": self.D, "format": "Q6_K", "batch": 1,
-                "l2": "weights 255 MB > L2"}
+        return {"workload": "config3_lmhead_b1", "vocab": self.V, "hidden": self.D, "format": "Q6_K",
+                "layout": "tiled (rta_tile_weights, once before timing)", "batch": 1, "l2": "weights 255 MB > L2"}
 
     def cpu_baseline(self, budget_s):
         from oracle import oracle
@@ -352,10 +357,9 @@ class DecodeWorkload(Workload):
     prompt 512 random ids, then greedy decode.  A step is one decode token."""
     name, metric, unit, dtype, dominant = ("decode2b", "decode tokens/s (2B-shape hybrid, batch 1)", "tokens/s",
                                            "q4k/q6k-int8mma, f16-kv, f32 state",
-                                           "gemv_kernel<Q6_K> vocabulary readout + argmax")
-    prompt_len = 512
-
-    def __init__(self, seed=20261201):
+                                           "gemv_tiled_kernel<Q6_K> vocabulary readout + argmax")
+    def __init__(self, seed=20261201, prompt_len=512):
+        self.prompt_len = prompt_len
         import torch
         from rta_b200 import assets, ops
         from rta_b200.model import ResidentModel
@@ -367,7 +371,9 @@ class DecodeWorkload(Workload):
         self.model.prefill(self.prompt)
         self.launches_per_step = self.model.resources()["kernels_per_decode_step"]
         # the dominant kernel in isolation: same readout shape on its own weights
-        self.lm_w = ops.synthetic_blocks(14, self.spec.vocabulary_size, self.spec.hidden_size, seed + 7)
+        self.lm_fmt, self.lm_w = ops.tile_weights(
+            14, ops.synthetic_blocks(14, self.spec.vocabulary_size, self.spec.hidden_size, seed + 7),
+            self.spec.vocabulary_size, self.spec.hidden_size)
         self.lm_x = ops.synthetic_normal(self.spec.hidden_size, seed + 8)
         self.lm_ws = torch.empty(4096, dtype=torch.uint8, device="cuda")
 
@@ -376,7 +382,7 @@ class DecodeWorkload(Workload):
         return self.model.last_gpu_ms, ids
 
     def dominant_launch(self, i):
-        self.ops.readout(14, self.lm_w, self.spec.vocabulary_size, self.spec.hidden_size, self.lm_x, logits=False,
+        self.ops.readout(self.lm_fmt, self.lm_w, self.spec.vocabulary_size, self.spec.hidden_size, self.lm_x, logits=False,
                          workspace=self.lm_ws)
 
     def dominant_bytes(self):
@@ -456,7 +462,7 @@ def run_decode(args, world, rank, local):
     graph replays, GPU time by CUDA events on the engine stream); `e2e` = K calls
     of generate(1) (host round trip per token: control H2D, ids D2H)."""
     import torch
-    wl = DecodeWorkload()
+    wl = DecodeWorkload(prompt_len=args.prompt)
     wl.decode(args.warmup)                       # warm-up tokens
     torch.cuda.synchronize()
     barrier(world)
@@ -651,6 +657,8 @@ def main():
     ap.add_argument("--min-seconds", type=float, default=1.0,
                     help="repeat the timed K-step region for at least this long (clock sampling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--prompt", type=int, default=512,
+                    help="decode2b: prompt length before the timed tokens (short prompts keep profiler runs small)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":

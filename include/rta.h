@@ -47,6 +47,11 @@ enum {
   RTA_E_STATE = 6         /* call not valid in the handle's current state */
 };
 enum { RTA_F32 = 0, RTA_F16 = 1, RTA_BF16 = 30, RTA_Q4_K = 12, RTA_Q6_K = 14 };
+/* Tiled re-layouts of Q4_K / Q6_K matrices made by rta_tile_weights: the same
+ * bytes in the order the decode GEMV streams them.  Codes of this library (no
+ * counterpart in the exporter's format table); accepted by the GEMV operators
+ * (rta_gemv, rta_gemv_swiglu, rta_mlp_swiglu, rta_readout) in place of 12 / 14. */
+enum { RTA_Q4_K_TILED = 112, RTA_Q6_K_TILED = 114 };
 
 /* Text of the last error raised on this thread (never NULL). */
 RTA_API const char* rta_last_error(void);
@@ -71,6 +76,16 @@ RTA_API rta_status rta_synthetic_normal(uint64_t seed, float sigma, float mean, 
 /* Decode packed blocks to fp32, bit-exact with ggufValue
  * (ray_tracing/native/shaders/resident_quant.glsl:6-20). */
 RTA_API rta_status rta_dequantize(int format, const void* blocks, size_t nblocks, float* dst, void* stream);
+
+/* Re-lay a row-major [rows x cols] Q4_K / Q6_K matrix (rows % 16 == 0,
+ * cols % 256 == 0) into the tiled order of RTA_Q4_K_TILED / RTA_Q6_K_TILED:
+ * for each 16-row tile and 256-column block the 16 blocks become one
+ * contiguous tile, codes in tensor-core fragment order.  dst (same byte size,
+ * 16-byte aligned) must not overlap src.  The engine applies this once to
+ * every resident matrix at load (the reference keeps its payloads in GGUF
+ * order, optical_resident.cpp:139-153). */
+RTA_API rta_status rta_tile_weights(int format, const void* src, uint32_t rows, uint32_t cols, void* dst,
+                                    void* stream);
 
 /* y[b][r] (+)= sum_c W[r][c] x[b][c]; W Q4_K or Q6_K row-major, rows % 16 == 0,
  * cols % 256 == 0, 1 <= batch <= 32.  Replaces op 2 of

@@ -25,6 +25,7 @@ rta_status cuda_status(cudaError_t e, const char* what) {
 }
 cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
 bool quant_format(int f) { return f == RTA_Q4_K || f == RTA_Q6_K; }
+bool gemv_format(int f) { return quant_format(f) || f == RTA_Q4_K_TILED || f == RTA_Q6_K_TILED; }
 
 constexpr size_t kErrBytes = 256;  // device error word + padding at the head of every workspace
 
@@ -80,9 +81,20 @@ rta_status rta_dequantize(int format, const void* blocks, size_t nblocks, float*
                      "rta_dequantize");
 }
 
+rta_status rta_tile_weights(int format, const void* src, uint32_t rows, uint32_t cols, void* dst, void* stream) {
+  if (!quant_format(format) || !src || !dst || rows == 0 || rows % 16 || cols == 0 || cols % 256)
+    return fail(RTA_E_ARG, "rta_tile_weights: format must be Q4_K/Q6_K, rows % 16 == 0, cols % 256 == 0");
+  const size_t bytes = static_cast<size_t>(rows) * (cols / 256) * rta::block_bytes(format);
+  const uintptr_t a = reinterpret_cast<uintptr_t>(src), b = reinterpret_cast<uintptr_t>(dst);
+  if (a < b + bytes && b < a + bytes) return fail(RTA_E_ARG, "rta_tile_weights: dst overlaps src");
+  return cuda_status(rta::launch_tile_weights(format, static_cast<const uint8_t*>(src), rows, cols,
+                                              static_cast<uint8_t*>(dst), as_stream(stream)),
+                     "rta_tile_weights");
+}
+
 rta_status rta_gemv(int format, const void* w, uint32_t rows, uint32_t cols, const float* x, uint32_t batch,
                     float* y, int accumulate, void* stream) {
-  if (!quant_format(format) || !w || !x || !y || rows == 0 || rows % 16 || cols == 0 || cols % 256 || batch == 0 ||
+  if (!gemv_format(format) || !w || !x || !y || rows == 0 || rows % 16 || cols == 0 || cols % 256 || batch == 0 ||
       batch > rta::kMaxBatch)
     return fail(RTA_E_ARG, "rta_gemv: format must be Q4_K/Q6_K, rows % 16 == 0, cols % 256 == 0, 1 <= batch <= 32");
   rta::GemvArgs a;
@@ -101,7 +113,7 @@ rta_status rta_gemv(int format, const void* w, uint32_t rows, uint32_t cols, con
 
 rta_status rta_gemv_swiglu(int format, const void* wg, const void* wu, uint32_t rows, uint32_t cols, const float* x,
                            uint32_t batch, float* act, void* stream) {
-  if (!quant_format(format) || !wg || !wu || !x || !act || rows == 0 || rows % 16 || cols == 0 || cols % 256 ||
+  if (!gemv_format(format) || !wg || !wu || !x || !act || rows == 0 || rows % 16 || cols == 0 || cols % 256 ||
       batch == 0 || batch > rta::kMaxBatch)
     return fail(RTA_E_ARG, "rta_gemv_swiglu: rows % 16 == 0, cols % 256 == 0, 1 <= batch <= 32");
   rta::GemvArgs g;
@@ -122,7 +134,7 @@ rta_status rta_gemv_swiglu(int format, const void* wg, const void* wu, uint32_t 
 rta_status rta_mlp_swiglu(int format, const void* wg, const void* wu, const void* wd, uint32_t hidden,
                           uint32_t middle, const float* x, uint32_t batch, float* act, float* y, int accumulate,
                           void* stream) {
-  if (!quant_format(format) || !wg || !wu || !wd || !x || !act || !y || hidden % 256 || middle % 256 || !hidden ||
+  if (!gemv_format(format) || !wg || !wu || !wd || !x || !act || !y || hidden % 256 || middle % 256 || !hidden ||
       !middle || batch == 0 || batch > rta::kMaxBatch)
     return fail(RTA_E_ARG, "rta_mlp_swiglu: bad arguments (hidden, middle multiples of 256; 1 <= batch <= 32)");
   rta::GemvArgs g;
@@ -158,7 +170,7 @@ size_t rta_readout_workspace_bytes(uint32_t batch) { return kErrBytes + 8ull * (
 
 rta_status rta_readout(int format, const void* w, uint32_t vocab, uint32_t hidden, const float* x, uint32_t batch,
                        float* logits, uint32_t* argmax, float* best, void* workspace, void* stream) {
-  if (!quant_format(format) || !w || !x || !argmax || !workspace || vocab == 0 || vocab % 16 || hidden % 256 ||
+  if (!gemv_format(format) || !w || !x || !argmax || !workspace || vocab == 0 || vocab % 16 || hidden % 256 ||
       hidden == 0 || batch == 0 || batch > 8)
     return fail(RTA_E_ARG, "rta_readout: bad arguments (vocab % 16 == 0, hidden % 256 == 0, 1 <= batch <= 8)");
   cudaStream_t s = as_stream(stream);

@@ -97,6 +97,7 @@ struct Engine {
   uint32_t n_full = 0, n_rec = 0;
   const uint8_t* lm = nullptr;
   int lm_fmt = kQ6K;
+  DevBuf<uint8_t> lm_tiled;  // the LM head in tiled order (its GGUF rows may double as the embedding)
   const uint8_t* embed = nullptr;
   int embed_fmt = kQ6K;
   const float* out_norm = nullptr;
@@ -177,6 +178,61 @@ struct Engine {
     dmap.alloc(rows);
     RTA_CUDA(cudaMemcpyAsync(dmap.p, map.data(), rows * 4u, cudaMemcpyHostToDevice, stream));
     RTA_CUDA(launch_gather_rows(d.ptr, dmap.p, rows, row_bytes, dst, stream));
+    RTA_CUDA(cudaStreamSynchronize(stream));
+  }
+
+  // Re-lay every GEMV matrix once into the tiled order (same bytes; see
+  // launch_tile_weights): layer matrices in place through a scratch buffer,
+  // the LM head into its own buffer.  Fails on projections sharing bytes.
+  void tile_matrices() {
+    const uint32_t D = this->D(), F = spec.middle_size;
+    struct Job {
+      uint8_t* p;
+      int fmt;           // packed format of the payload (Q4_K / Q6_K)
+      int* tiled_field;  // format field switched to the tiled code afterwards (null: shared with another job)
+      uint32_t rows, cols;
+    };
+    std::vector<Job> jobs;
+    auto mut = [](const uint8_t* q) { return const_cast<uint8_t*>(q); };
+    for (auto& Lp : layers) {
+      Layer& L = *Lp;
+      if (L.full) {
+        jobs.push_back({L.qkvg.p, L.qkvg_fmt, &L.qkvg_fmt, L.qkvg_rows, D});
+        jobs.push_back({mut(L.o), L.o_fmt, &L.o_fmt, D, Q()});
+      } else {
+        jobs.push_back({L.inproj.p, L.inproj_fmt, &L.inproj_fmt, L.inproj_rows, D});
+        jobs.push_back({mut(L.out), L.out_fmt, &L.out_fmt, D, S()});
+      }
+      jobs.push_back({mut(L.gate), L.mlp_fmt, &L.mlp_fmt, F, D});
+      jobs.push_back({mut(L.up), L.mlp_fmt, nullptr, F, D});  // up shares the gate's format field
+      jobs.push_back({mut(L.down), L.down_fmt, &L.down_fmt, D, F});
+    }
+    std::vector<std::pair<uintptr_t, size_t>> spans;
+    size_t need = 0;
+    for (const Job& j : jobs) {
+      const size_t bytes = static_cast<size_t>(j.rows) * (j.cols / 256) * block_bytes(j.fmt);
+      const uintptr_t a = reinterpret_cast<uintptr_t>(j.p);
+      for (const auto& d : spans)
+        require(!(a < d.first + d.second && d.first < a + bytes),
+                "two projections share payload bytes; the tiled re-layout needs distinct matrices");
+      require(a % 16 == 0, "projection payload not 16-byte aligned");
+      spans.push_back({a, bytes});
+      need = std::max(need, bytes);
+    }
+    DevBuf<uint8_t> tmp;
+    tmp.alloc(need);
+    for (const Job& j : jobs) {
+      const size_t bytes = static_cast<size_t>(j.rows) * (j.cols / 256) * block_bytes(j.fmt);
+      RTA_CUDA(launch_tile_weights(j.fmt, j.p, j.rows, j.cols, tmp.p, stream));
+      RTA_CUDA(cudaMemcpyAsync(j.p, tmp.p, bytes, cudaMemcpyDeviceToDevice, stream));
+    }
+    for (const Job& j : jobs)
+      if (j.tiled_field) *j.tiled_field = j.fmt + kTiledOffset;
+    const size_t lm_bytes = static_cast<size_t>(spec.vocabulary_size) * (D / 256) * block_bytes(lm_fmt);
+    lm_tiled.alloc(lm_bytes);
+    RTA_CUDA(launch_tile_weights(lm_fmt, lm, spec.vocabulary_size, D, lm_tiled.p, stream));
+    lm = lm_tiled.p;
+    lm_fmt += kTiledOffset;
     RTA_CUDA(cudaStreamSynchronize(stream));
   }
 
@@ -296,6 +352,7 @@ struct Engine {
       layers.push_back(std::move(L));
     }
     RTA_CUDA(cudaStreamSynchronize(stream));
+    tile_matrices();
 
     // activations and state
     const uint32_t projw = std::max(Q() + 2 * KVW() + Q(), 2 * K() + 2 * S());
@@ -839,6 +896,7 @@ rta_status rta_model_resources(rta_model* m, uint64_t* out, size_t n) {
   const rta::Engine& e = m->engine;
   size_t layer_bytes = 0;
   for (auto& L : e.layers) layer_bytes += L->qkvg.n + L->inproj.n;
+  layer_bytes += e.lm_tiled.n;
   const uint64_t v[] = {
       e.payload_bytes,
       layer_bytes,

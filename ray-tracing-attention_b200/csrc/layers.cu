@@ -149,7 +149,14 @@ __global__ void __launch_bounds__(256) attn_prep_kernel(PrepParams p) {
 // RMS-normed layer input; 4-tap causal conv + SiLU; L2-normalised q, k; and the
 // gated delta rule s <- s*decay; r = k.s; s += k*(v - r)*beta; o = (q/sqrt(128)).s
 // on a [128 value x 128 key] fp32 state per head.  Grid (head, value slice).
-constexpr uint32_t kGdnRows = 32;  // value rows per CTA (8 warps x 4)
+//
+// Latency layout: the kernel is a short chain of dependent steps, so everything
+// that does not depend on the preceding kernels (this CTA's state rows, the
+// gate / norm / conv weights, the conv history) is requested before
+// griddepcontrol.wait -- state rows into registers, the rest into L2 -- and the
+// block reductions carry several values per barrier.
+constexpr uint32_t kGdnRows = 16;                 // value rows per CTA
+constexpr uint32_t kGdnRowsPerWarp = kGdnRows / 8u;
 
 __device__ __forceinline__ float signed_product_sum(float a0, float a1, float a2, float a3, float b0, float b1,
                                                     float b2, float b3) {
@@ -166,97 +173,151 @@ __device__ __forceinline__ float signed_product_sum(float a0, float a1, float a2
   return warp_sum(P) - warp_sum(M);
 }
 
+// Sum of N values over the 256 threads; `red` holds 8*N floats and is used by
+// this call only (one barrier).
+template <int N>
+__device__ __forceinline__ void block_sums(float (&v)[N], float* red) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) v[i] = warp_sum(v[i]);
+  const uint32_t w = threadIdx.x >> 5;
+  if ((threadIdx.x & 31u) == 0u)
+#pragma unroll
+    for (int i = 0; i < N; ++i) red[w * N + i] = v[i];
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s += red[j * N + i];
+    v[i] = s;
+  }
+}
+
+__device__ __forceinline__ void prefetch_l2(const void* ptr) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr));
+}
+
 __global__ void __launch_bounds__(256) gdn_kernel(GdnParams p) {
+  __shared__ float red1[8], red2[16], red3[16];
+  __shared__ float qn[128], kn[128], vv[kGdnRows];
+  const uint32_t h = blockIdx.x, slice = blockIdx.y, tid = threadIdx.x;
+  const uint32_t HD = 128u, S = p.H * HD, K = p.KH * HD, kh = h % p.KH;
+  const uint32_t warp = tid >> 5, lane = tid & 31u;
+
+  // ---- independent of the preceding kernels: state rows, weights, conv history
+  float* st = p.rec + static_cast<size_t>(h) * HD * HD;
+  float2 s0[kGdnRowsPerWarp], s1[kGdnRowsPerWarp];
+#pragma unroll
+  for (uint32_t i = 0; i < kGdnRowsPerWarp; ++i) {
+    const float* row = st + static_cast<size_t>(slice * kGdnRows + warp * kGdnRowsPerWarp + i) * HD;
+    s0[i] = *reinterpret_cast<const float2*>(row + 2 * lane);   // lane owns keys (2l, 2l+1) and
+    s1[i] = *reinterpret_cast<const float2*>(row + 2 * lane + 64);  // (2l+64, 2l+65), as op 21
+  }
+  for (uint32_t c = tid * 32u; c < p.D; c += 256u * 32u) {  // one 128-byte line per thread
+    prefetch_l2(p.wa + static_cast<size_t>(h) * p.D + c);
+    prefetch_l2(p.wb + static_cast<size_t>(h) * p.D + c);
+    prefetch_l2(p.attn_norm + c);
+  }
+  // The conv history is double-buffered by position parity; the position is
+  // written by this step's embed kernel, so both buffers are read here and the
+  // choice is made after the wait.
+  const size_t buf = static_cast<size_t>(3u) * S * 3u;
+  // this thread's conv channel: q (tid < 128) or k (tid >= 128), plus v rows for tid < kGdnRows
+  const uint32_t qk_coord = tid < 128u ? h * HD + tid : S + h * HD + (tid - 128u);
+  const uint32_t v_coord = 2u * S + h * HD + slice * kGdnRows + (tid % kGdnRows);
+  const float4 wq = *reinterpret_cast<const float4*>(p.conv_w + static_cast<size_t>(qk_coord) * 4u);
+  float pq[2][3], pv[2][3] = {{0.f, 0.f, 0.f}, {0.f, 0.f, 0.f}};
+#pragma unroll
+  for (int b = 0; b < 2; ++b)
+#pragma unroll
+    for (int j = 0; j < 3; ++j) pq[b][j] = p.conv_state[b * buf + qk_coord * 3u + j];
+  float4 wv = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (tid < kGdnRows) {
+    wv = *reinterpret_cast<const float4*>(p.conv_w + static_cast<size_t>(v_coord) * 4u);
+#pragma unroll
+    for (int b = 0; b < 2; ++b)
+#pragma unroll
+      for (int j = 0; j < 3; ++j) pv[b][j] = p.conv_state[b * buf + v_coord * 3u + j];
+  }
+  const float a_log = p.a_log[h], dt_bias = p.dt_bias[h];
+
   pdl_wait();
   pdl_launch_dependents();
   if (p.running && *p.running == 0u) return;
-  __shared__ float red[16];
-  __shared__ float qn[128], kn[128], vv[kGdnRows];
-  __shared__ float gates[2];
-  const uint32_t h = blockIdx.x, slice = blockIdx.y, tid = threadIdx.x;
-  const uint32_t HD = 128u, S = p.H * HD, K = p.KH * HD, kh = h % p.KH;
   const uint32_t par = (*p.pos) & 1u;
-  const float* past = p.conv_state + static_cast<size_t>(par) * 3u * S * 3u;
-  float* next = p.conv_state + static_cast<size_t>(par ^ 1u) * 3u * S * 3u;
+  float* next = p.conv_state + (par ^ 1u) * buf;
+  const float pq0 = par ? pq[1][0] : pq[0][0], pq1 = par ? pq[1][1] : pq[0][1], pq2 = par ? pq[1][2] : pq[0][2];
+  const float pv0 = par ? pv[1][0] : pv[0][0], pv1 = par ? pv[1][1] : pv[0][1], pv2 = par ? pv[1][2] : pv[0][2];
 
-  // gates: a, b = (rmsnorm(x) * attn_norm) . W_alpha[h], W_beta[h]
-  float ss = 0.f;
-  for (uint32_t c = tid; c < p.D; c += blockDim.x) ss += p.x[c] * p.x[c];
-  const float inv = rsqrtf(block_sum256(ss, red) / static_cast<float>(p.D) + p.eps);
-  float a = 0.f, b = 0.f;
-  for (uint32_t c = tid; c < p.D; c += blockDim.x) {
+  // ---- op 18 gates: a, b = (rmsnorm(x) * attn_norm) . W_alpha[h], W_beta[h]
+  float ss[1] = {0.f};
+  for (uint32_t c = tid; c < p.D; c += 256u) ss[0] += p.x[c] * p.x[c];
+  const float raw_q = p.proj[tid < 128u ? kh * HD + tid : K + kh * HD + (tid - 128u)];
+  const float raw_v = tid < kGdnRows ? p.proj[2u * K + h * HD + slice * kGdnRows + tid] : 0.f;
+  block_sums<1>(ss, red1);
+  const float inv = rsqrtf(ss[0] / static_cast<float>(p.D) + p.eps);
+  float ab[2] = {0.f, 0.f};
+  for (uint32_t c = tid; c < p.D; c += 256u) {
     const float xn = p.x[c] * inv * p.attn_norm[c];
-    a += xn * p.wa[static_cast<size_t>(h) * p.D + c];
-    b += xn * p.wb[static_cast<size_t>(h) * p.D + c];
-  }
-  a = block_sum256(a, red);
-  b = block_sum256(b, red);
-  if (tid == 0) {
-    gates[0] = expf(-expf(p.a_log[h]) * softplus(a + p.dt_bias[h]));
-    gates[1] = detector_sigmoid(b);
+    ab[0] += xn * p.wa[static_cast<size_t>(h) * p.D + c];
+    ab[1] += xn * p.wb[static_cast<size_t>(h) * p.D + c];
   }
 
-  // causal conv + SiLU for q, k (128 each) and this slice's v channels
-  auto conv = [&](uint32_t coord, float raw, bool write) {
-    const float* w = p.conv_w + static_cast<size_t>(coord) * 4u;
-    const float* pc = past + static_cast<size_t>(coord) * 3u;
+  // ---- op 19: causal conv + SiLU (independent of the gates)
+  auto conv = [](float4 w, float c0, float c1, float c2, float raw) {
     float signal = 0.f;
-    signal = signal + pc[0] * w[0];
-    signal = signal + pc[1] * w[1];
-    signal = signal + pc[2] * w[2];
-    signal = signal + raw * w[3];
-    if (write) {
-      float* nc = next + static_cast<size_t>(coord) * 3u;
-      nc[0] = pc[1];
-      nc[1] = pc[2];
-      nc[2] = raw;
-    }
+    signal = signal + c0 * w.x;
+    signal = signal + c1 * w.y;
+    signal = signal + c2 * w.z;
+    signal = signal + raw * w.w;
     return signal * detector_sigmoid(signal);
   };
-  if (tid < 128u) {
-    qn[tid] = conv(h * HD + tid, p.proj[kh * HD + tid], slice == 0);
-  } else {
-    const uint32_t c = tid - 128u;
-    kn[c] = conv(S + h * HD + c, p.proj[K + kh * HD + c], slice == 0);
+  const float f = conv(wq, pq0, pq1, pq2, raw_q);
+  if (slice == 0u) {
+    float* nc = next + static_cast<size_t>(qk_coord) * 3u;
+    nc[0] = pq1;
+    nc[1] = pq2;
+    nc[2] = raw_q;
   }
   if (tid < kGdnRows) {
-    const uint32_t c = slice * kGdnRows + tid;
-    vv[tid] = conv(2u * S + h * HD + c, p.proj[2u * K + h * HD + c], true);
+    vv[tid] = conv(wv, pv0, pv1, pv2, raw_v);
+    float* nc = next + static_cast<size_t>(v_coord) * 3u;
+    nc[0] = pv1;
+    nc[1] = pv2;
+    nc[2] = raw_v;
   }
+  block_sums<2>(ab, red2);
+  const float decay = expf(-expf(a_log) * softplus(ab[0] + dt_bias));
+  const float beta = detector_sigmoid(ab[1]);
+
+  // ---- op 20: L2 norms, q * inversesqrt(sum q^2 + eps), same for k
+  float qk2[2] = {tid < 128u ? f * f : 0.f, tid >= 128u ? f * f : 0.f};
+  block_sums<2>(qk2, red3);
+  if (tid < 128u) qn[tid] = (f * rsqrtf(qk2[0] + p.eps)) / sqrtf(128.0f);
+  else kn[tid - 128u] = f * rsqrtf(qk2[1] + p.eps);
   __syncthreads();
-  // L2 norms (op 20): q * inversesqrt(sum q^2 + eps), same for k
-  const float qv = tid < 128u ? qn[tid] : 0.f, kv = tid < 128u ? kn[tid] : 0.f;
-  const float qs = rsqrtf(block_sum256(qv * qv, red) + p.eps);
-  const float ks = rsqrtf(block_sum256(kv * kv, red) + p.eps);
-  if (tid < 128u) {
-    qn[tid] = (qv * qs) / sqrtf(128.0f);
-    kn[tid] = kv * ks;
-  }
-  __syncthreads();
-  const float decay = gates[0], beta = gates[1];
-  const uint32_t warp = tid >> 5, lane = tid & 31u;
-  // lane owns keys (2l, 2l+1) and (2l+64, 2l+65), as fieldPair of op 21
+
+  // ---- op 21: gated delta rule on this warp's value rows
   const float k0 = kn[2 * lane], k1 = kn[2 * lane + 1], k2 = kn[2 * lane + 64], k3 = kn[2 * lane + 65];
   const float q0 = qn[2 * lane], q1 = qn[2 * lane + 1], q2 = qn[2 * lane + 64], q3 = qn[2 * lane + 65];
-  float* st = p.rec + static_cast<size_t>(h) * HD * HD;
-  for (uint32_t i = 0; i < kGdnRows / 8u; ++i) {
-    const uint32_t r = warp * (kGdnRows / 8u) + i, v = slice * kGdnRows + r;
-    float* row = st + static_cast<size_t>(v) * HD;
-    float2 s0 = *reinterpret_cast<float2*>(row + 2 * lane);
-    float2 s1 = *reinterpret_cast<float2*>(row + 2 * lane + 64);
-    s0.x *= decay;
-    s0.y *= decay;
-    s1.x *= decay;
-    s1.y *= decay;
-    const float received = signed_product_sum(k0, k1, k2, k3, s0.x, s0.y, s1.x, s1.y);
+#pragma unroll
+  for (uint32_t i = 0; i < kGdnRowsPerWarp; ++i) {
+    const uint32_t r = warp * kGdnRowsPerWarp + i, v = slice * kGdnRows + r;
+    float2 a = s0[i], b = s1[i];
+    a.x *= decay;
+    a.y *= decay;
+    b.x *= decay;
+    b.y *= decay;
+    const float received = signed_product_sum(k0, k1, k2, k3, a.x, a.y, b.x, b.y);
     const float delta = (vv[r] - received) * beta;
-    s0.x += k0 * delta;
-    s0.y += k1 * delta;
-    s1.x += k2 * delta;
-    s1.y += k3 * delta;
-    const float o = signed_product_sum(q0, q1, q2, q3, s0.x, s0.y, s1.x, s1.y);
-    *reinterpret_cast<float2*>(row + 2 * lane) = s0;
-    *reinterpret_cast<float2*>(row + 2 * lane + 64) = s1;
+    a.x += k0 * delta;
+    a.y += k1 * delta;
+    b.x += k2 * delta;
+    b.y += k3 * delta;
+    const float o = signed_product_sum(q0, q1, q2, q3, a.x, a.y, b.x, b.y);
+    float* row = st + static_cast<size_t>(v) * HD;
+    *reinterpret_cast<float2*>(row + 2 * lane) = a;
+    *reinterpret_cast<float2*>(row + 2 * lane + 64) = b;
     if (lane == 0) p.out[h * HD + v] = o;
   }
 }

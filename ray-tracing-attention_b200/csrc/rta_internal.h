@@ -12,10 +12,13 @@
 namespace rta {
 
 constexpr int kF32 = 0, kF16 = 1, kBF16 = 30, kQ4K = 12, kQ6K = 14;  // export.py FORMATS codes
+// Tiled re-layouts of Q4_K / Q6_K matrices (same bytes, GEMV-friendly order;
+// see launch_tile_weights).  Codes of this library, not of the exporter.
+constexpr int kTiledOffset = 100, kQ4KTiled = kQ4K + kTiledOffset, kQ6KTiled = kQ6K + kTiledOffset;
 constexpr uint32_t kQ4KBytes = 144, kQ6KBytes = 210;
 constexpr uint32_t kMaxBatch = 32;  // GEMV batch rows per launch (mma slices of 4)
 
-inline uint32_t block_bytes(int fmt) { return fmt == kQ4K ? kQ4KBytes : kQ6KBytes; }
+inline uint32_t block_bytes(int fmt) { return fmt == kQ4K || fmt == kQ4KTiled ? kQ4KBytes : kQ6KBytes; }
 
 // Record the thread-local text returned by rta_last_error() (capi.cu).
 void set_last_error(const std::string& msg);
@@ -61,6 +64,10 @@ struct GemvArgs {
   bool pdl = false;                      // launch with programmatic stream serialization
 };
 cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t s);
+// Re-lay a [rows x cols] Q4_K / Q6_K matrix (rows % 16 == 0) out of GGUF row
+// order into the tiled order the kTiled formats name (dst != src, same size).
+cudaError_t launch_tile_weights(int fmt, const uint8_t* src, uint32_t rows, uint32_t cols, uint8_t* dst,
+                                cudaStream_t s);
 // Dense F32 GEMV for the tiny recurrent alpha/beta projections.
 cudaError_t launch_gemv_f32(const float* W, uint32_t rows, uint32_t cols, const float* x, uint32_t x_stride,
                             uint32_t batch, float* y, uint32_t y_stride, cudaStream_t s);

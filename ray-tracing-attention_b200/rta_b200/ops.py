@@ -9,7 +9,7 @@ from __future__ import annotations
 import torch
 
 from . import _lib
-from ._lib import BLOCK_BYTES, Q4_K, Q6_K, check
+from ._lib import BLOCK_BYTES, Q4_K, Q6_K, TILED, check
 
 
 def _stream():
@@ -63,6 +63,14 @@ def dequantize(fmt: int, blocks: torch.Tensor) -> torch.Tensor:
     out = torch.empty(nb * 256, dtype=torch.float32, device=blocks.device)
     check(_lib.load().rta_dequantize(fmt, _ptr(blocks), nb, _ptr(out), _stream()))
     return out
+
+
+def tile_weights(fmt: int, w: torch.Tensor, rows: int, cols: int) -> tuple[int, torch.Tensor]:
+    """Re-lay a row-major Q4_K / Q6_K matrix into the tiled GEMV order.
+    Returns (tiled format code, tiled bytes); the input is left unchanged."""
+    out = torch.empty_like(w)
+    check(_lib.load().rta_tile_weights(fmt, _ptr(w), rows, cols, _ptr(out), _stream()))
+    return TILED[fmt], out
 
 
 def gemv(fmt: int, w: torch.Tensor, rows: int, cols: int, x: torch.Tensor, y: torch.Tensor | None = None,
