@@ -161,6 +161,9 @@ class MLPWorkload(Workload):
                                            "q4k-int8mma-f32acc", "gemv_tiled_kernel<Q4_K> gate+up (SwiGLU)")
     D, F = 2048, 6144
     launches_per_step = 2
+    # dram__bytes_read.sum + dram__bytes_write.sum of one gate+up launch, from one
+    # ncu capture (profiles/gemv_tiled_q4k_mlp_2048_6144.md)
+    traffic = 14.23e6
 
     def __init__(self, seed=20261110):
         import torch
@@ -232,6 +235,9 @@ class LMHeadWorkload(Workload):
                                            "tokens/s", "q6k-int8mma-f32acc", "gemv_tiled_kernel<Q6_K> readout + argmax")
     V, D = 151936, 2048
     launches_per_step = 2
+    # dram read + write of one readout launch with logits, from one ncu capture
+    # (profiles/gemv_tiled_q6k_readout_151936x2048.md)
+    traffic = 255.36e6 + 3.69e6
 
     def __init__(self, seed=31):
         import torch
@@ -493,7 +499,7 @@ def run_decode(args, world, rank, local):
         "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic (seeded random init, prompt ids)",
         "config": dict(wl.config(), parallelism=f"replicas x{world}" if world > 1 else "single GPU"),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                     "frac": achieved / pk["hbm_gbs"], "traffic": None, "kernel": wl.dominant,
+                     "frac": achieved / pk["hbm_gbs"], "traffic": getattr(wl, "traffic", None), "kernel": wl.dominant,
                      "algorithmic_bytes": wl.dominant_bytes(), "kernel_ms": dom_ms,
                      "peak_source": f"{pk['source']} hbm_gbs (burst copy)",
                      "step_algorithmic_bytes": wl.step_bytes(pos), "step_achieved_gbs": step_gbs,
@@ -570,7 +576,7 @@ def run_ours(args, world, rank, local):
         "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic (seeded, BASELINE shapes)",
         "config": dict(wl.config(), parallelism=f"replicas x{world}" if world > 1 else "single GPU"),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                     "frac": achieved / pk["hbm_gbs"], "traffic": None, "kernel": wl.dominant,
+                     "frac": achieved / pk["hbm_gbs"], "traffic": getattr(wl, "traffic", None), "kernel": wl.dominant,
                      "algorithmic_bytes": wl.dominant_bytes(), "kernel_ms": dom_ms,
                      "peak_source": f"{pk['source']} hbm_gbs (burst copy)"},
         "e2e": {"value": wl.units_per_step() * world / (e2e_ms / 1e3), "unit": wl.unit,
