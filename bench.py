@@ -127,7 +127,8 @@ def max_over_ranks(v: float, world: int) -> float:
         return v
     import torch
     import torch.distributed as dist
-    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 
@@ -459,8 +460,137 @@ def host_payloads(layout, seed):
     return layout.params(), mats, basis
 
 
+class RaggedBatchWorkload:
+    """9B-shape hybrid (32 layers 3:1, D 4096, F 12288), a ragged batch of
+    64 sequences with seeded histories U[128, 8192], sharded by sequence over the ranks
+    (weights replicated, no collective on the data path).  A step is one decode token
+    for every sequence of the job."""
+    name, metric, unit, dtype = ("ragged9b", "decode tokens/s (9B-shape hybrid, ragged batch of 64 sequences)",
+                                 "tokens/s", "q4k/q6k-int8mma, f16-kv, f32 state")
+    dominant = "gemv_tiled_kernel<Q6_K> vocabulary readout + argmax (rank batch, <= 8 rows per launch)"
+    seed = 20261205
+
+
 WORKLOADS = {"mlp": MLPWorkload, "lmhead": LMHeadWorkload, "attention": AttentionWorkload,
-             "decode2b": DecodeWorkload}
+             "decode2b": DecodeWorkload, "ragged9b": RaggedBatchWorkload}
+
+
+def ragged_step_bytes(spec, layout, lengths, capacity):
+    """Algorithmic HBM bytes of one ragged-batch step on one rank: weights once,
+    one embedding row per sequence, every visible fp16 K/V position, and the
+    recurrent state read and written."""
+    seqs = len(lengths)
+    weights = sum(t.nbytes for t in layout.matrices) + layout.basis[1].nbytes
+    emb = seqs * spec.hidden_size * 210 // 256
+    kv = sum(min(int(n) + 1, capacity) for n in lengths) * len(spec.full_layers) * spec.kv_width * 2 * 2
+    rec = seqs * len(spec.recurrent_layers) * spec.state_heads * 128 * 128 * 4 * 2
+    return weights + emb + kv + rec
+
+
+def run_ragged(args, world, rank, local):
+    """Config 5 on `world` GPUs: every rank decodes its shard of the 64 sequences;
+    `value` = 64 tokens per step / the slowest rank's step time (CUDA events around
+    K graph replays); `e2e` = K public-API calls of one step each."""
+    import torch
+    from rta_b200 import assets, ops, sharding
+    from rta_b200.model import ResidentModel
+    wl = RaggedBatchWorkload
+    spec = assets.spec_9b()
+    lengths = sharding.config5_histories(wl.seed)
+    shards = sharding.shard_sequences(lengths, world)
+    mine = lengths[shards[rank]]
+    capacity = (int(lengths.max()) + 256 + 255) // 256 * 256
+    model = ResidentModel.synthetic(spec, wl.seed, capacity=capacity, device=local, sequences=len(mine))
+    model.seed_history(mine, seed=wl.seed + 1)
+    model.generate_batch(args.warmup)
+    torch.cuda.synchronize()
+    barrier(world)
+    with ClockSampler(local) as clk:
+        reps, ms_total, t0 = 0, 0.0, time.perf_counter()
+        while True:
+            model.generate_batch(args.steps)
+            ms_total += model.last_gpu_ms
+            reps += 1
+            if time.perf_counter() - t0 >= args.min_seconds or reps >= 64:
+                break
+    ms_step = max_over_ranks(ms_total / reps, world) / args.steps
+    res = model.resources()
+    torch.cuda.synchronize()
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        model.generate_batch(1)
+    e2e_s = max_over_ranks((time.perf_counter() - t0) * 1e3, world) / 1e3 / args.steps
+    positions = mine + args.warmup + args.steps * (reps + 1)
+    step_bytes = ragged_step_bytes(spec, model.layout, positions, capacity)
+    layout = model.layout
+    model.close()
+    torch.cuda.empty_cache()
+    # dominant kernel alone: the 9B readout at this rank's launch batch
+    rows = min(8, len(mine))
+    lm_fmt, lm_w = ops.tile_weights(14, ops.synthetic_blocks(14, spec.vocabulary_size, spec.hidden_size, wl.seed + 7),
+                                    spec.vocabulary_size, spec.hidden_size)
+    lm_x = ops.synthetic_normal(rows * spec.hidden_size, wl.seed + 8).reshape(rows, spec.hidden_size)
+    lm_ws = torch.empty(4096, dtype=torch.uint8, device="cuda")
+    dom = lambda i: ops.readout(lm_fmt, lm_w, spec.vocabulary_size, spec.hidden_size, lm_x, logits=False,
+                                workspace=lm_ws)
+    dom_ms = time_steps(dom, args.steps, args.warmup, world) / args.steps
+    dom_bytes = spec.vocabulary_size * spec.hidden_size // 256 * 210 + rows * spec.hidden_size * 4
+    pk = peaks()
+    achieved = dom_bytes / (dom_ms / 1e3) / 1e9
+    step_gbs = step_bytes / (ms_step / 1e3) / 1e9
+    total = int(lengths.size)
+    line = {
+        "metric": wl.metric, "value": total / (ms_step / 1e3), "unit": wl.unit, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": wl.dtype,
+        "data": "synthetic (seeded random init; seeded K/V, recurrent state and residual histories)",
+        "config": {"workload": "config5_9b_ragged_batch64", "layers": spec.depth, "pattern": "rec,rec,rec,full",
+                   "hidden": spec.hidden_size, "intermediate": spec.middle_size, "vocab": spec.vocabulary_size,
+                   "q_heads": 16, "kv_heads": 4, "head_dim": 256, "state_heads": spec.state_heads,
+                   "state_key_heads": spec.state_key_heads, "sequences": total,
+                   "history": "U[128, 8192] seeded", "sequences_per_rank": [len(x) for x in shards],
+                   "capacity": capacity, "kv_cache": "fp16",
+                   "parallelism": f"sequence-sharded x{world}, weights replicated" if world > 1 else "single GPU",
+                   "l2": "per-step weight stream 4 GB > L2"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / pk["hbm_gbs"], "traffic": None, "kernel": wl.dominant,
+                     "algorithmic_bytes": dom_bytes, "kernel_ms": dom_ms,
+                     "peak_source": f"{pk['source']} hbm_gbs (burst copy)",
+                     "step_algorithmic_bytes_rank": step_bytes, "step_achieved_gbs_rank": step_gbs,
+                     "step_frac": step_gbs / pk["hbm_gbs"]},
+        "e2e": {"value": total / e2e_s, "unit": wl.unit, "h2d_bytes_per_step": 48 * len(mine),
+                "d2h_bytes_per_step": 52 * len(mine),
+                "api": "ResidentModel.generate_batch(1) -> rta_model_generate_batch (C-ABI)"},
+        "gpu_launches": res["kernels_per_decode_step"] * args.steps,
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = ragged_cpu_baseline(args.cpu_budget)
+    return line
+
+
+def ragged_cpu_baseline(budget_s, tokens=None):
+    """The 9B model oracle on the host cores: one sequence, a 2-token prompt, then
+    greedy tokens until the budget is spent (at least one).  The CPU port decodes
+    the 64 sequences one after another, so its aggregate rate equals this rate."""
+    from oracle import oracle
+    from oracle.model import OracleModel
+    from rta_b200 import assets
+    spec = assets.spec_9b()
+    lay = assets.plan(spec, RaggedBatchWorkload.seed)
+    params, mats, basis = host_payloads(lay, RaggedBatchWorkload.seed)
+    ref = OracleModel(spec, params, mats, basis, 256)
+    ref.prefill(np.random.default_rng(3).integers(0, spec.vocabulary_size, 2))
+    n, t0 = 0, time.perf_counter()
+    while n == 0 or (time.perf_counter() - t0 < budget_s and (tokens is None or n < tokens)):
+        ref.forward(ref.readout()[0])
+        n += 1
+    v = n / (time.perf_counter() - t0)
+    return {"value": v, "unit": "tokens/s", "cores": oracle.threads(), "kind": "port",
+            "sample": f"{n} greedy tokens of one sequence after a 2-token prompt, 9B-shape model (random valid "
+                      "Q4_K/Q6_K blocks), model oracle = C restatement of the reference shader math (OpenMP); "
+                      "sequences are decoded one after another on the CPU"}
 
 
 def run_decode(args, world, rank, local):
@@ -504,7 +634,7 @@ def run_decode(args, world, rank, local):
                      "peak_source": f"{pk['source']} hbm_gbs (burst copy)",
                      "step_algorithmic_bytes": wl.step_bytes(pos), "step_achieved_gbs": step_gbs,
                      "step_frac": step_gbs / pk["hbm_gbs"]},
-        "e2e": {"value": world / e2e_s, "unit": wl.unit, "h2d_bytes_per_step": 16, "d2h_bytes_per_step": 4,
+        "e2e": {"value": world / e2e_s, "unit": wl.unit, "h2d_bytes_per_step": 48, "d2h_bytes_per_step": 52,
                 "api": "ResidentModel.generate(1) -> rta_model_generate (C-ABI)"},
         "gpu_launches": wl.launches_per_step * args.steps,
         "clocks": clk.summary(),
@@ -596,6 +726,16 @@ def run_reference(args, world, rank):
         return None
     if args.workload == "decode2b":
         return run_reference_decode(args, world)
+    if args.workload == "ragged9b":
+        base = ragged_cpu_baseline(args.cpu_budget, tokens=max(1, args.steps))
+        v = base["value"]
+        return {"impl": "reference", "metric": RaggedBatchWorkload.metric, "value": v, "unit": "tokens/s",
+                "n_gpus": world, "steps": args.steps, "warmup": 0, "higher_is_better": True, "dtype": "f32",
+                "data": "synthetic (seeded random init)", "config": {"workload": "config5_9b_ragged_batch64"},
+                "cpu_baseline": base, "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                                              "d2h_bytes_per_step": 0},
+                "note": "reference Vulkan ray-query worker unavailable on this box (no graphics stack, no RT "
+                        "cores); timed its CPU path: the C restatement of its shader math"}
     cls = WORKLOADS[args.workload]
     wl = cls.__new__(cls)
     if args.workload == "attention":
@@ -675,7 +815,12 @@ def main():
             print(json.dumps(line), flush=True)
         return
     world, rank, local = dist_setup(args.gpus)
-    line = run_decode(args, world, rank, local) if args.workload == "decode2b" else run_ours(args, world, rank, local)
+    if args.workload == "decode2b":
+        line = run_decode(args, world, rank, local)
+    elif args.workload == "ragged9b":
+        line = run_ragged(args, world, rank, local)
+    else:
+        line = run_ours(args, world, rank, local)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

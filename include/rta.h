@@ -190,6 +190,31 @@ RTA_API rta_status rta_model_open_files(const rta_model_spec* spec, const char* 
                                         int device, rta_model** out);
 RTA_API void rta_model_close(rta_model* model);
 
+/* A handle that decodes `sequences` independent sequences side by side (the
+ * ragged multi-sequence batch of BASELINE config 5): one decode step produces
+ * one token for every running sequence, each with its own history ring,
+ * recurrent state, position and stop state, the GEMVs streaming the weights
+ * once per up-to-8 sequences.  No reference counterpart: the reference worker
+ * serves one sequence per process (optical_resident.cpp:964-971).  The
+ * single-sequence calls (rta_model_prefill / rta_model_generate) require
+ * sequences == 1. */
+RTA_API rta_status rta_model_open_batch(const rta_model_spec* spec, const uint32_t* params, size_t n_params,
+                                        const void* matrices, size_t matrix_bytes, const void* basis,
+                                        size_t basis_bytes, uint32_t capacity, uint32_t sequences, int device,
+                                        rta_model** out);
+/* Prefill every sequence: ids[z * stride + i], i < lengths[z] (0 = idle
+ * sequence); the sequences advance in lockstep, a shorter prompt sits out the
+ * remaining steps. */
+RTA_API rta_status rta_model_prefill_batch(rta_model* model, const uint32_t* ids, const uint32_t* lengths,
+                                           uint32_t stride, const uint32_t stops[2], double* gpu_ms);
+/* Throughput runs: fill every history slot, recurrent state and residual row
+ * with seeded values and resume sequence z at position lengths[z]. */
+RTA_API rta_status rta_model_seed_history(rta_model* model, const uint32_t* lengths, uint64_t seed);
+/* `count` greedy tokens for every sequence with a history: ids[z * count + i],
+ * n_out[z] tokens each (a sequence stops alone at a stop id). */
+RTA_API rta_status rta_model_generate_batch(rta_model* model, uint32_t count, uint32_t* ids, uint32_t* n_out,
+                                            double* gpu_ms);
+
 /* Prefill a fresh sequence with n prompt ids (positions 0..n-1); stops[2] are
  * the stop ids of the following generate calls.  Worker op 1
  * (Resident::prefill, optical_resident.cpp:609-712). */
@@ -208,11 +233,11 @@ RTA_API rta_status rta_model_mlp(rta_model* model, uint32_t layer, const float* 
  * argmax (ties -> lowest id) of the readout of `hidden`; logits may be NULL. */
 RTA_API rta_status rta_model_vocabulary(rta_model* model, const float* hidden, float* logits, uint32_t* argmax,
                                         float* best);
-/* Current residual state (hidden_size floats) and absolute position. */
+/* Current residual state (hidden_size floats) and absolute position (sequence 0). */
 RTA_API rta_status rta_model_state(rta_model* model, float* state, uint32_t* position);
 /* Resource counters, worker op 8: payload bytes, derived layer bytes, KV bytes,
  * recurrent state bytes, capacity, attention splits, kernels per decode step,
- * kernels per prefill step, position. */
+ * kernels per prefill step, position, sequences. */
 RTA_API rta_status rta_model_resources(rta_model* model, uint64_t* out, size_t n);
 
 #ifdef __cplusplus

@@ -59,7 +59,7 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
 
 // Visible window of sequence z at absolute time t: ages [lo, t].
 __device__ __forceinline__ void window(const AttnParams& p, uint32_t z, uint32_t& t, uint32_t& lo, uint32_t& n) {
-  t = p.pos ? p.pos[z] : p.t;
+  t = p.pos ? p.pos[z * p.ctrl_step] : p.t;
   const uint32_t cap = p.capacity;
   lo = t + 1u >= cap ? t + 1u - cap : 0u;
   if (lo < p.history_start) lo = p.history_start;
@@ -81,7 +81,7 @@ __global__ void __launch_bounds__(kThreads) attention_split_kernel(const AttnPar
   __syncthreads();
   pdl_wait();
   pdl_launch_dependents();
-  if (p.running && *p.running == 0u) return;
+  if (p.running && p.running[blockIdx.z * p.ctrl_step] == 0u) return;
 
   uint32_t t, lo, n;
   window(p, z, t, lo, n);
@@ -284,8 +284,8 @@ __global__ void __launch_bounds__(kThreads) attention_split_kernel(const AttnPar
 __global__ void __launch_bounds__(kHD) attention_merge_kernel(const AttnParams p, uint32_t nsplit) {
   pdl_wait();
   pdl_launch_dependents();
-  if (p.running && *p.running == 0u) return;
   const uint32_t head = blockIdx.x, z = blockIdx.y, d = threadIdx.x;
+  if (p.running && p.running[z * p.ctrl_step] == 0u) return;
   const uint32_t kv = head / kGroup, h = head % kGroup;
   const size_t rec0 = (static_cast<size_t>(z) * p.kvh + kv) * nsplit;
   float m = -INFINITY;
@@ -300,8 +300,7 @@ __global__ void __launch_bounds__(kHD) attention_merge_kernel(const AttnParams p
       os += p.part_o[((rec0 + s) * kGroup + h) * kHD + d] * e;
     }
   float v = os / fmaxf(zs, 1e-30f);
-  const size_t at = static_cast<size_t>(z) * p.out_seq_stride + static_cast<size_t>(head) * kHD + d;
-  if (p.gate) v *= detector_sigmoid(p.gate[at]);
+  if (p.gate) v *= detector_sigmoid(p.gate[static_cast<size_t>(z) * p.gate_seq_stride + static_cast<size_t>(head) * kHD + d]);
   uint32_t od = d;
   if (p.rotary_out && d < p.rotary_out) od = (d % 2u) * (p.rotary_out / 2u) + d / 2u;  // original axis order
   p.out[static_cast<size_t>(z) * p.out_seq_stride + static_cast<size_t>(head) * kHD + od] = v;

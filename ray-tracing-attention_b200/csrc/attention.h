@@ -18,8 +18,10 @@ struct AttnParams {
   uint32_t capacity = 0;         // ring slots (position p lives in slot p % capacity)
   uint32_t history_start = 0;    // oldest age present
   uint32_t t = 0;                // current absolute time (used when pos == nullptr)
-  const uint32_t* pos = nullptr; // [nseq] device-side current times (graph replay)
-  const float* gate = nullptr;   // [nseq][heads][hd] or null
+  const uint32_t* pos = nullptr; // device-side current times (graph replay): sequence z reads pos[z * ctrl_step]
+  uint32_t ctrl_step = 1;        // u32 elements between sequences' pos / running words
+  const float* gate = nullptr;   // [nseq] x ([heads][hd] at gate_seq_stride) or null
+  size_t gate_seq_stride = 0;
   float* out = nullptr;          // [nseq][heads][hd]
   size_t out_seq_stride = 0;
   uint32_t rotary_out = 0;       // >0: write outputs in original (un-paired) axis order
@@ -28,7 +30,7 @@ struct AttnParams {
   float* part_z = nullptr;
   float* part_o = nullptr;       // [nseq][kvh][nsplit][4][hd]
   uint32_t* err = nullptr;
-  const uint32_t* running = nullptr;  // optional: 0 -> skip (generation stopped)
+  const uint32_t* running = nullptr;  // optional: sequence z skipped when running[z * ctrl_step] == 0
 };
 
 size_t attention_smem_bytes();

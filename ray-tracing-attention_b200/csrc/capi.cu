@@ -27,6 +27,7 @@ cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
 bool quant_format(int f) { return f == RTA_Q4_K || f == RTA_Q6_K; }
 bool gemv_format(int f) { return quant_format(f) || f == RTA_Q4_K_TILED || f == RTA_Q6_K_TILED; }
 
+constexpr uint32_t kApiMaxBatch = 32;  // batch rows accepted by the GEMV operators (rta.h)
 constexpr size_t kErrBytes = 256;  // device error word + padding at the head of every workspace
 
 __global__ void readout_finish_kernel(const unsigned long long* keys, uint32_t batch, uint32_t vocab,
@@ -95,7 +96,7 @@ rta_status rta_tile_weights(int format, const void* src, uint32_t rows, uint32_t
 rta_status rta_gemv(int format, const void* w, uint32_t rows, uint32_t cols, const float* x, uint32_t batch,
                     float* y, int accumulate, void* stream) {
   if (!gemv_format(format) || !w || !x || !y || rows == 0 || rows % 16 || cols == 0 || cols % 256 || batch == 0 ||
-      batch > rta::kMaxBatch)
+      batch > kApiMaxBatch)
     return fail(RTA_E_ARG, "rta_gemv: format must be Q4_K/Q6_K, rows % 16 == 0, cols % 256 == 0, 1 <= batch <= 32");
   rta::GemvArgs a;
   a.fmt = format;
@@ -114,7 +115,7 @@ rta_status rta_gemv(int format, const void* w, uint32_t rows, uint32_t cols, con
 rta_status rta_gemv_swiglu(int format, const void* wg, const void* wu, uint32_t rows, uint32_t cols, const float* x,
                            uint32_t batch, float* act, void* stream) {
   if (!gemv_format(format) || !wg || !wu || !x || !act || rows == 0 || rows % 16 || cols == 0 || cols % 256 ||
-      batch == 0 || batch > rta::kMaxBatch)
+      batch == 0 || batch > kApiMaxBatch)
     return fail(RTA_E_ARG, "rta_gemv_swiglu: rows % 16 == 0, cols % 256 == 0, 1 <= batch <= 32");
   rta::GemvArgs g;
   g.fmt = format;
@@ -135,7 +136,7 @@ rta_status rta_mlp_swiglu(int format, const void* wg, const void* wu, const void
                           uint32_t middle, const float* x, uint32_t batch, float* act, float* y, int accumulate,
                           void* stream) {
   if (!gemv_format(format) || !wg || !wu || !wd || !x || !act || !y || hidden % 256 || middle % 256 || !hidden ||
-      !middle || batch == 0 || batch > rta::kMaxBatch)
+      !middle || batch == 0 || batch > kApiMaxBatch)
     return fail(RTA_E_ARG, "rta_mlp_swiglu: bad arguments (hidden, middle multiples of 256; 1 <= batch <= 32)");
   rta::GemvArgs g;
   g.fmt = format;

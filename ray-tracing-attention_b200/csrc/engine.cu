@@ -90,6 +90,8 @@ struct Engine {
   int device = 0;
   cudaStream_t stream = nullptr;
   uint32_t capacity = 0, nsplit = 1;
+  uint32_t nseq = 1;   // sequences decoded side by side (one token each per step)
+  uint32_t projw = 0;  // floats of one sequence's projection row
   std::vector<uint32_t> hp;  // host copy of the parameter words
   DevBuf<uint32_t> params;
   DevBuf<uint8_t> matrices, basis;
@@ -107,11 +109,12 @@ struct Engine {
   DevBuf<float> rec, conv;
   DevBuf<Control> ctrl;
   DevBuf<uint32_t> prompt;
-  Control* ctrl_host = nullptr;  // pinned mirror
+  Control* ctrl_host = nullptr;  // pinned mirror [nseq]
   cudaGraphExec_t g_decode = nullptr, g_prefill = nullptr;
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
   uint32_t stops[2] = {0xffffffffu, 0xffffffffu};
-  uint32_t position = 0;
+  uint32_t position = 0;          // sequence 0's next position (single-sequence API)
+  std::vector<uint32_t> positions;  // next position per sequence
   uint32_t kernels_per_decode = 0, kernels_per_prefill = 0;
   double last_gpu_ms = 0.0;
   uint64_t payload_bytes = 0;
@@ -237,9 +240,11 @@ struct Engine {
   }
 
   void load(const rta_model_spec& sp, const uint32_t* prm, size_t n_params, const void* mat, size_t matrix_bytes,
-            const void* bas, size_t basis_bytes, uint32_t cap, int dev) {
+            const void* bas, size_t basis_bytes, uint32_t cap, uint32_t sequences, int dev) {
     spec = sp;
     device = dev;
+    require(sequences >= 1 && sequences <= 256, "sequences must be 1..256", RTA_E_ARG);
+    nseq = sequences;
     require(spec.depth >= 1 && spec.depth <= 256, "depth must be 1..256", RTA_E_ARG);
     require(spec.hidden_size % 256 == 0 && spec.middle_size % 256 == 0, "hidden/middle must be multiples of 256",
             RTA_E_ARG);
@@ -354,30 +359,33 @@ struct Engine {
     RTA_CUDA(cudaStreamSynchronize(stream));
     tile_matrices();
 
-    // activations and state
-    const uint32_t projw = std::max(Q() + 2 * KVW() + Q(), 2 * K() + 2 * S());
-    state.alloc(D);
-    proj.alloc(projw);
-    qproc.alloc(Q());
-    att.alloc(Q());
-    gdn.alloc(std::max(1u, S()));
-    act.alloc(spec.middle_size);
+    // activations and state, one row per sequence
+    projw = std::max(Q() + 2 * KVW() + Q(), 2 * K() + 2 * S());
+    projw = (projw + 3u) / 4u * 4u;  // 16-byte aligned rows
+    state.alloc(static_cast<size_t>(nseq) * D);
+    proj.alloc(static_cast<size_t>(nseq) * projw);
+    qproc.alloc(static_cast<size_t>(nseq) * Q());
+    att.alloc(static_cast<size_t>(nseq) * Q());
+    gdn.alloc(static_cast<size_t>(nseq) * std::max(1u, S()));
+    act.alloc(static_cast<size_t>(nseq) * spec.middle_size);
     scratch_x.alloc(32ull * std::max(D, spec.middle_size));
     scratch_y.alloc(32ull * std::max(D, spec.middle_size));
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
     nsplit = std::max(1u, std::min(static_cast<uint32_t>(sms) / spec.kv_heads, capacity / 256u));
-    const size_t recs = static_cast<size_t>(spec.kv_heads) * nsplit * 4;
+    const size_t recs = static_cast<size_t>(nseq) * spec.kv_heads * nsplit * 4;
     part_m.alloc(recs);
     part_z.alloc(recs);
     part_o.alloc(recs * hd);
-    kcache.alloc(static_cast<size_t>(std::max(1u, n_full)) * spec.kv_heads * capacity * hd);
+    // [layer][sequence] x per-sequence blocks
+    kcache.alloc(static_cast<size_t>(std::max(1u, n_full)) * nseq * spec.kv_heads * capacity * hd);
     vcache.alloc(kcache.n);
-    rec.alloc(static_cast<size_t>(std::max(1u, n_rec)) * spec.state_heads * 128 * 128);
-    conv.alloc(static_cast<size_t>(std::max(1u, n_rec)) * 2 * 3 * S() * 3);
-    ctrl.alloc(1);
-    prompt.alloc(capacity);
-    RTA_CUDA(cudaMallocHost(&ctrl_host, sizeof(Control)));
+    rec.alloc(static_cast<size_t>(std::max(1u, n_rec)) * nseq * spec.state_heads * 128 * 128);
+    conv.alloc(static_cast<size_t>(std::max(1u, n_rec)) * nseq * 2 * 3 * S() * 3);
+    ctrl.alloc(nseq);
+    prompt.alloc(static_cast<size_t>(nseq) * capacity);
+    positions.assign(nseq, 0u);
+    RTA_CUDA(cudaMallocHost(&ctrl_host, sizeof(Control) * nseq));
     std::vector<float> freq(hd / 2, 0.f);
     for (uint32_t p = 0; p < spec.rotary_dim / 2u; ++p)
       freq[p] = std::pow(spec.rope_theta, -static_cast<float>(p) / static_cast<float>(spec.rotary_dim / 2u));
@@ -393,6 +401,7 @@ struct Engine {
     conv.zero(stream);
     state.zero(stream);
     position = 0;
+    std::fill(positions.begin(), positions.end(), 0u);
     RTA_CUDA(cudaStreamSynchronize(stream));
   }
 
@@ -403,6 +412,8 @@ struct Engine {
     Control* c = ctrl.p;
     const uint32_t* running = &c->running;
     const uint32_t D = this->D(), F = spec.middle_size, hd = spec.attention_head_dim;
+    const uint32_t cstep = static_cast<uint32_t>(sizeof(Control) / 4);  // u32 between sequences' control words
+    static_assert(sizeof(Control) % 8 == 0, "control blocks must keep 8-byte alignment");
     if (decode) {
       GemvArgs r;
       r.fmt = lm_fmt;
@@ -413,9 +424,13 @@ struct Engine {
       r.prologue = kRmsNorm;
       r.norm_w = out_norm;
       r.eps = spec.norm_epsilon;
+      r.batch = nseq;
+      r.x_stride = D;
       r.argmax = &c->argkey;
+      r.argmax_step = static_cast<uint32_t>(sizeof(Control) / 8);
       r.err = &c->err;
       r.running = running;
+      r.running_step = cstep;
       r.pdl = true;
       RTA_CUDA(launch_gemv(r, s));
       ++n;
@@ -428,6 +443,8 @@ struct Engine {
     e.vocab = spec.vocabulary_size;
     e.ctrl = c;
     e.prompt = prompt.p;
+    e.prompt_stride = capacity;
+    e.nseq = nseq;
     e.mode = decode ? kEmbedDecode : kEmbedPrefill;
     e.state = state.p;
     RTA_CUDA(launch_embed(e, s, true));
@@ -445,7 +462,11 @@ struct Engine {
         g.norm_w = L.attn_norm;
         g.eps = spec.norm_epsilon;
         g.y = proj.p;
+        g.batch = nseq;
+        g.x_stride = D;
+        g.y_stride = projw;
         g.running = running;
+        g.running_step = cstep;
         g.err = &c->err;
         g.pdl = true;
         RTA_CUDA(launch_gemv(g, s));
@@ -464,17 +485,23 @@ struct Engine {
         pp.q_width = Q();
         pp.kv_width = KVW();
         pp.qout = qproc.p;
-        const size_t layer_kv = static_cast<size_t>(spec.kv_heads) * capacity * hd;
+        const size_t seq_kv = static_cast<size_t>(spec.kv_heads) * capacity * hd;
+        const size_t layer_kv = seq_kv * nseq;
         pp.kcache = kcache.p + L.fi * layer_kv;
         pp.vcache = vcache.p + L.fi * layer_kv;
         pp.capacity = capacity;
         pp.pos = &c->pos_cur;
         pp.running = running;
+        pp.nseq = nseq;
+        pp.ctrl_step = cstep;
+        pp.qkvg_seq = projw;
         RTA_CUDA(launch_attn_prep(pp, s, true));
         AttnParams ap;
         ap.q = qproc.p;
         ap.k = pp.kcache;
         ap.v = pp.vcache;
+        ap.q_seq_stride = Q();
+        ap.seq_stride = seq_kv;
         ap.kv_stride = static_cast<size_t>(capacity) * hd;
         ap.pos_stride = hd;
         ap.heads = spec.attention_heads;
@@ -482,15 +509,18 @@ struct Engine {
         ap.hd = hd;
         ap.capacity = capacity;
         ap.pos = &c->pos_cur;
+        ap.ctrl_step = cstep;
         ap.gate = L.gated ? proj.p + Q() + 2 * KVW() : nullptr;
+        ap.gate_seq_stride = projw;
         ap.out = att.p;
+        ap.out_seq_stride = Q();
         ap.rotary_out = L.rotary_out;
         ap.part_m = part_m.p;
         ap.part_z = part_z.p;
         ap.part_o = part_o.p;
         ap.err = &c->err;
         ap.running = running;
-        RTA_CUDA(launch_attention(ap, nsplit, 1, true, s));
+        RTA_CUDA(launch_attention(ap, nsplit, nseq, true, s));
         GemvArgs o;
         o.fmt = L.o_fmt;
         o.w0 = L.o;
@@ -499,7 +529,11 @@ struct Engine {
         o.x = att.p;
         o.epilogue = kAccumulate;
         o.y = state.p;
+        o.batch = nseq;
+        o.x_stride = Q();
+        o.y_stride = D;
         o.running = running;
+        o.running_step = cstep;
         o.err = &c->err;
         o.pdl = true;
         RTA_CUDA(launch_gemv(o, s));
@@ -515,7 +549,11 @@ struct Engine {
         g.norm_w = L.attn_norm;
         g.eps = spec.norm_epsilon;
         g.y = proj.p;
+        g.batch = nseq;
+        g.x_stride = D;
+        g.y_stride = projw;
         g.running = running;
+        g.running_step = cstep;
         g.err = &c->err;
         g.pdl = true;
         RTA_CUDA(launch_gemv(g, s));
@@ -529,8 +567,13 @@ struct Engine {
         gp.dt_bias = L.dt_bias;
         gp.proj = proj.p;
         gp.conv_w = L.conv_w;
-        gp.conv_state = conv.p + static_cast<size_t>(L.ri) * 2 * 3 * S() * 3;
-        gp.rec = rec.p + static_cast<size_t>(L.ri) * spec.state_heads * 128 * 128;
+        gp.conv_seq = static_cast<size_t>(2) * 3 * S() * 3;
+        gp.rec_seq = static_cast<size_t>(spec.state_heads) * 128 * 128;
+        gp.conv_state = conv.p + static_cast<size_t>(L.ri) * nseq * gp.conv_seq;
+        gp.rec = rec.p + static_cast<size_t>(L.ri) * nseq * gp.rec_seq;
+        gp.proj_seq = projw;
+        gp.nseq = nseq;
+        gp.ctrl_step = cstep;
         gp.out = gdn.p;
         gp.D = D;
         gp.H = spec.state_heads;
@@ -544,13 +587,18 @@ struct Engine {
         o.rows = D;
         o.cols = S();
         o.x = gdn.p;
+        o.x_stride = S();
+        o.batch = nseq;
         o.prologue = kHeadGate;
         o.z = proj.p + 2 * K() + S();
+        o.z_stride = projw;
         o.norm_w = L.ssm_norm;
         o.eps = spec.norm_epsilon;
         o.epilogue = kAccumulate;
         o.y = state.p;
+        o.y_stride = D;
         o.running = running;
+        o.running_step = cstep;
         o.err = &c->err;
         o.pdl = true;
         RTA_CUDA(launch_gemv(o, s));
@@ -568,7 +616,11 @@ struct Engine {
       gu.eps = spec.norm_epsilon;
       gu.epilogue = kSwiGLU;
       gu.y = act.p;
+      gu.batch = nseq;
+      gu.x_stride = D;
+      gu.y_stride = F;
       gu.running = running;
+      gu.running_step = cstep;
       gu.err = &c->err;
       gu.pdl = true;
       RTA_CUDA(launch_gemv(gu, s));
@@ -580,7 +632,11 @@ struct Engine {
       dn.x = act.p;
       dn.epilogue = kAccumulate;
       dn.y = state.p;
+      dn.batch = nseq;
+      dn.x_stride = F;
+      dn.y_stride = D;
       dn.running = running;
+      dn.running_step = cstep;
       dn.err = &c->err;
       dn.pdl = true;
       RTA_CUDA(launch_gemv(dn, s));
@@ -602,6 +658,9 @@ struct Engine {
         throw;
       }
       RTA_CUDA(cudaStreamEndCapture(stream, &graph));
+      size_t nodes = 0;
+      cudaGraphGetNodes(graph, nullptr, &nodes);  // launches per replay (batched GEMVs may split)
+      n = static_cast<uint32_t>(nodes);
       cudaGraphExec_t exec = nullptr;
       const cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
       cudaGraphDestroy(graph);
@@ -616,57 +675,123 @@ struct Engine {
     }
   }
 
-  void read_control() {
-    RTA_CUDA(cudaMemcpyAsync(ctrl_host, ctrl.p, sizeof(Control), cudaMemcpyDeviceToHost, stream));
+  // Copy the control blocks back (header plus the first `ids` emitted ids of
+  // every sequence) and surface device-side errors.
+  void read_control(uint32_t ids = 0) {
+    const size_t width = offsetof(Control, ids) + 4ull * std::min(ids, kMaxOut);
+    RTA_CUDA(cudaMemcpy2DAsync(ctrl_host, sizeof(Control), ctrl.p, sizeof(Control), width, nseq,
+                               cudaMemcpyDeviceToHost, stream));
     RTA_CUDA(cudaStreamSynchronize(stream));
-    if (ctrl_host->err & RTA_DEVERR_TIMEOUT) throw Failure{RTA_E_TIMEOUT, "device-side wait exceeded its bound"};
-    if (ctrl_host->err)
-      throw Failure{RTA_E_DEVICE_CHECK, "device error word " + std::to_string(ctrl_host->err)};
+    uint32_t err = 0;
+    for (uint32_t z = 0; z < nseq; ++z) {
+      err |= ctrl_host[z].err;
+      positions[z] = ctrl_host[z].pos_next;
+    }
+    position = positions[0];
+    if (err & RTA_DEVERR_TIMEOUT) throw Failure{RTA_E_TIMEOUT, "device-side wait exceeded its bound"};
+    if (err) throw Failure{RTA_E_DEVICE_CHECK, "device error word " + std::to_string(err)};
+  }
+  void write_headers() {
+    RTA_CUDA(cudaMemcpy2DAsync(ctrl.p, sizeof(Control), ctrl_host, sizeof(Control), offsetof(Control, ids), nseq,
+                               cudaMemcpyHostToDevice, stream));
   }
 
-  void prefill(const uint32_t* ids, uint32_t n, const uint32_t st[2]) {
-    require(n >= 1 && n <= capacity, "prefill length must be 1..capacity", RTA_E_ARG);
-    for (uint32_t i = 0; i < n; ++i) require(ids[i] < spec.vocabulary_size, "token id beyond the vocabulary", RTA_E_ARG);
+  // Prefill every sequence in lockstep: replay i feeds prompt id i of each
+  // sequence that has one; a sequence with a shorter prompt sits out the rest.
+  void prefill_batch(const uint32_t* ids, const uint32_t* lengths, uint32_t stride, const uint32_t st[2]) {
+    uint32_t longest = 0;
+    for (uint32_t z = 0; z < nseq; ++z) {
+      require(lengths[z] <= capacity && lengths[z] <= stride, "prefill length must be at most capacity", RTA_E_ARG);
+      for (uint32_t i = 0; i < lengths[z]; ++i)
+        require(ids[static_cast<size_t>(z) * stride + i] < spec.vocabulary_size, "token id beyond the vocabulary",
+                RTA_E_ARG);
+      longest = std::max(longest, lengths[z]);
+    }
+    require(longest >= 1, "prefill needs at least one prompt id", RTA_E_ARG);
     stops[0] = st ? st[0] : 0xffffffffu;
     stops[1] = st ? st[1] : 0xffffffffu;
     reset_sequence();
-    RTA_CUDA(cudaMemcpyAsync(prompt.p, ids, n * 4ull, cudaMemcpyHostToDevice, stream));
-    Control init{};
-    init.running = 1u;
-    init.stops[0] = stops[0];
-    init.stops[1] = stops[1];
-    RTA_CUDA(cudaMemcpyAsync(ctrl.p, &init, offsetof(Control, ids), cudaMemcpyHostToDevice, stream));
+    std::vector<uint32_t> rows(static_cast<size_t>(nseq) * capacity, 0u);
+    for (uint32_t z = 0; z < nseq; ++z)
+      std::copy_n(ids + static_cast<size_t>(z) * stride, lengths[z], rows.begin() + static_cast<size_t>(z) * capacity);
+    RTA_CUDA(cudaMemcpyAsync(prompt.p, rows.data(), rows.size() * 4ull, cudaMemcpyHostToDevice, stream));
+    std::memset(ctrl_host, 0, sizeof(Control) * nseq);
+    for (uint32_t z = 0; z < nseq; ++z) {
+      ctrl_host[z].running = lengths[z] > 0 ? 1u : 0u;
+      ctrl_host[z].prompt_len = lengths[z];
+      ctrl_host[z].stops[0] = stops[0];
+      ctrl_host[z].stops[1] = stops[1];
+    }
+    write_headers();
     RTA_CUDA(cudaEventRecord(ev0, stream));
-    for (uint32_t i = 0; i < n; ++i) RTA_CUDA(cudaGraphLaunch(g_prefill, stream));
+    for (uint32_t i = 0; i < longest; ++i) RTA_CUDA(cudaGraphLaunch(g_prefill, stream));
     RTA_CUDA(cudaEventRecord(ev1, stream));
     read_control();
     float ms = 0.f;
     cudaEventElapsedTime(&ms, ev0, ev1);
     last_gpu_ms = ms;
-    position = ctrl_host->pos_next;
   }
 
-  void generate(uint32_t count, uint32_t* ids_out, uint32_t* n_out) {
+  void prefill(const uint32_t* ids, uint32_t n, const uint32_t st[2]) {
+    require(nseq == 1, "this handle decodes several sequences: use the batch prefill", RTA_E_STATE);
+    require(n >= 1 && n <= capacity, "prefill length must be 1..capacity", RTA_E_ARG);
+    prefill_batch(ids, &n, n, st);
+  }
+
+  // Synthetic histories for throughput runs: every ring slot, recurrent state,
+  // conv history and residual row is filled with seeded values and sequence z
+  // resumes at position lengths[z] (as if it had been prefilled that far).
+  void seed_history(const uint32_t* lengths, uint64_t seed) {
+    for (uint32_t z = 0; z < nseq; ++z) require(lengths[z] >= 1, "history lengths must be positive", RTA_E_ARG);
+    reset_sequence();
+    RTA_CUDA(launch_random_normal_half(seed, 1.0f, kcache.n, kcache.p, stream));
+    RTA_CUDA(launch_random_normal_half(seed + 1, 1.0f, vcache.n, vcache.p, stream));
+    RTA_CUDA(launch_random_normal(seed + 2, 0.02f, 0.0f, rec.n, rec.p, stream));
+    RTA_CUDA(launch_random_normal(seed + 3, 1.0f, 0.0f, conv.n, conv.p, stream));
+    RTA_CUDA(launch_random_normal(seed + 4, 1.0f, 0.0f, state.n, state.p, stream));
+    std::memset(ctrl_host, 0, sizeof(Control) * nseq);
+    for (uint32_t z = 0; z < nseq; ++z) {
+      ctrl_host[z].pos_next = lengths[z];
+      ctrl_host[z].pos_cur = lengths[z] - 1u;
+      ctrl_host[z].stops[0] = ctrl_host[z].stops[1] = 0xffffffffu;
+    }
+    stops[0] = stops[1] = 0xffffffffu;
+    write_headers();
+    read_control();
+  }
+
+  // `count` greedy tokens for every sequence that has a history; a sequence
+  // stops on its own at a stop id.  ids_out: [nseq][count].
+  void generate_batch(uint32_t count, uint32_t* ids_out, uint32_t* n_out) {
     require(count >= 1 && count <= kMaxOut, "generate count must be 1..4096", RTA_E_ARG);
-    require(position > 0, "prefill before generate", RTA_E_STATE);
-    // running = 1, n_out = 0 (the pinned mirror holds the rest of the control block)
-    ctrl_host->running = 1u;
-    ctrl_host->n_out = 0u;
-    ctrl_host->stops[0] = stops[0];
-    ctrl_host->stops[1] = stops[1];
-    RTA_CUDA(cudaMemcpyAsync(&ctrl.p->running, &ctrl_host->running, 8, cudaMemcpyHostToDevice, stream));
-    RTA_CUDA(cudaMemcpyAsync(&ctrl.p->stops, &ctrl_host->stops, 8, cudaMemcpyHostToDevice, stream));
+    bool any = false;
+    for (uint32_t z = 0; z < nseq; ++z) {
+      ctrl_host[z].running = positions[z] > 0 ? 1u : 0u;
+      ctrl_host[z].n_out = 0u;
+      ctrl_host[z].stops[0] = stops[0];
+      ctrl_host[z].stops[1] = stops[1];
+      any = any || positions[z] > 0;
+    }
+    require(any, "prefill before generate", RTA_E_STATE);
+    write_headers();
     RTA_CUDA(cudaEventRecord(ev0, stream));
     for (uint32_t i = 0; i < count; ++i) RTA_CUDA(cudaGraphLaunch(g_decode, stream));
     RTA_CUDA(cudaEventRecord(ev1, stream));
-    read_control();
+    read_control(count);
     float ms = 0.f;
     cudaEventElapsedTime(&ms, ev0, ev1);
     last_gpu_ms = ms;
-    const uint32_t got = std::min(ctrl_host->n_out, count);
-    if (ids_out) std::memcpy(ids_out, ctrl_host->ids, got * 4ull);
-    if (n_out) *n_out = got;
-    position = ctrl_host->pos_next;
+    for (uint32_t z = 0; z < nseq; ++z) {
+      const uint32_t got = std::min(ctrl_host[z].n_out, count);
+      if (ids_out) std::memcpy(ids_out + static_cast<size_t>(z) * count, ctrl_host[z].ids, got * 4ull);
+      if (n_out) n_out[z] = got;
+    }
+  }
+
+  void generate(uint32_t count, uint32_t* ids_out, uint32_t* n_out) {
+    require(nseq == 1, "this handle decodes several sequences: use the batch generate", RTA_E_STATE);
+    require(position > 0, "prefill before generate", RTA_E_STATE);
+    generate_batch(count, ids_out, n_out);
   }
 
   void mlp(uint32_t layer, const float* x, uint32_t rows, float* y, float* a) {
@@ -769,9 +894,9 @@ extern "C" {
 
 const char* rta_model_last_error(void) { return rta::g_model_error.c_str(); }
 
-rta_status rta_model_open(const rta_model_spec* spec, const uint32_t* params, size_t n_params, const void* matrices,
-                          size_t matrix_bytes, const void* basis, size_t basis_bytes, uint32_t capacity, int device,
-                          rta_model** out) {
+rta_status rta_model_open_batch(const rta_model_spec* spec, const uint32_t* params, size_t n_params,
+                                const void* matrices, size_t matrix_bytes, const void* basis, size_t basis_bytes,
+                                uint32_t capacity, uint32_t sequences, int device, rta_model** out) {
   if (!spec || !params || !matrices || !basis || !out) {
     rta::g_model_error = "rta_model_open: null argument";
     return RTA_E_ARG;
@@ -780,13 +905,20 @@ rta_status rta_model_open(const rta_model_spec* spec, const uint32_t* params, si
   auto* m = new (std::nothrow) rta_model;
   if (!m) return RTA_E_CUDA;
   try {
-    m->engine.load(*spec, params, n_params, matrices, matrix_bytes, basis, basis_bytes, capacity, device);
+    m->engine.load(*spec, params, n_params, matrices, matrix_bytes, basis, basis_bytes, capacity, sequences, device);
   } catch (const rta::Failure& f) {
     delete m;
     return rta::fail_model(f);
   }
   *out = m;
   return RTA_OK;
+}
+
+rta_status rta_model_open(const rta_model_spec* spec, const uint32_t* params, size_t n_params, const void* matrices,
+                          size_t matrix_bytes, const void* basis, size_t basis_bytes, uint32_t capacity, int device,
+                          rta_model** out) {
+  return rta_model_open_batch(spec, params, n_params, matrices, matrix_bytes, basis, basis_bytes, capacity, 1u, device,
+                              out);
 }
 
 rta_status rta_model_open_files(const rta_model_spec* spec, const char* optical_model_bin, const char* geometry_bin,
@@ -855,6 +987,42 @@ rta_status rta_model_generate(rta_model* m, uint32_t count, uint32_t* ids, uint3
   return RTA_OK;
 }
 
+rta_status rta_model_prefill_batch(rta_model* m, const uint32_t* ids, const uint32_t* lengths, uint32_t stride,
+                                   const uint32_t stops[2], double* gpu_ms) {
+  if (!m || !ids || !lengths) return RTA_E_ARG;
+  try {
+    cudaSetDevice(m->engine.device);
+    m->engine.prefill_batch(ids, lengths, stride, stops);
+    if (gpu_ms) *gpu_ms = m->engine.last_gpu_ms;
+  } catch (const rta::Failure& f) {
+    return rta::fail_model(f);
+  }
+  return RTA_OK;
+}
+
+rta_status rta_model_seed_history(rta_model* m, const uint32_t* lengths, uint64_t seed) {
+  if (!m || !lengths) return RTA_E_ARG;
+  try {
+    cudaSetDevice(m->engine.device);
+    m->engine.seed_history(lengths, seed);
+  } catch (const rta::Failure& f) {
+    return rta::fail_model(f);
+  }
+  return RTA_OK;
+}
+
+rta_status rta_model_generate_batch(rta_model* m, uint32_t count, uint32_t* ids, uint32_t* n_out, double* gpu_ms) {
+  if (!m) return RTA_E_ARG;
+  try {
+    cudaSetDevice(m->engine.device);
+    m->engine.generate_batch(count, ids, n_out);
+    if (gpu_ms) *gpu_ms = m->engine.last_gpu_ms;
+  } catch (const rta::Failure& f) {
+    return rta::fail_model(f);
+  }
+  return RTA_OK;
+}
+
 rta_status rta_model_mlp(rta_model* m, uint32_t layer, const float* x, uint32_t rows, float* y, float* act) {
   if (!m || !x || !y || !act) return RTA_E_ARG;
   try {
@@ -907,6 +1075,7 @@ rta_status rta_model_resources(rta_model* m, uint64_t* out, size_t n) {
       e.kernels_per_decode,
       e.kernels_per_prefill,
       e.position,
+      e.nseq,
   };
   for (size_t i = 0; i < n && i < sizeof(v) / sizeof(v[0]); ++i) out[i] = v[i];
   return RTA_OK;

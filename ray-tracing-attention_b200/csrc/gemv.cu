@@ -53,12 +53,14 @@ struct Params {
   const float* norm_w;
   float eps;
   const float* z;
+  uint32_t z_stride;
   int epilogue;
   float* y;
   uint32_t y_stride;
   unsigned long long* argmax;
   uint32_t* err;
   const uint32_t* running;
+  uint32_t run_step, arg_step;  // elements between batch rows' running flags / argmax keys
   // shared-memory carve (byte offsets from the dynamic base)
   uint32_t off_bar, off_xq, off_xsc, off_scr, off_red, off_misc;
 };
@@ -104,7 +106,7 @@ __device__ void prepare_x(const Params& p, uint8_t* smem, const float4 (&wv)[kPa
   const uint32_t npass = (nchunk + kPass * kThreads - 1) / (kPass * kThreads);
   for (uint32_t b = 0; b < p.batch; ++b) {
     const float4* xr = reinterpret_cast<const float4*>(p.x + static_cast<size_t>(b) * p.x_stride);
-    const float4* zr = p.z ? reinterpret_cast<const float4*>(p.z + static_cast<size_t>(b) * p.x_stride) : nullptr;
+    const float4* zr = p.z ? reinterpret_cast<const float4*>(p.z + static_cast<size_t>(b) * p.z_stride) : nullptr;
     for (uint32_t pass = 0; pass < npass; ++pass) {
       float4 xv[kPass], zv[kPass];
 #pragma unroll
@@ -216,6 +218,14 @@ struct StageCursor {
   }
 };
 
+// True while at least one batch row of the launch is still generating.
+__device__ __forceinline__ bool any_running(const Params& p) {
+  if (!p.running) return true;
+  for (uint32_t b = 0; b < p.batch; ++b)
+    if (p.running[b * p.run_step] != 0u) return true;
+  return false;
+}
+
 // Per-warp scratch (floats): dsc[16 groups][17] | dmm[16][17] | bias[16 rows]
 constexpr uint32_t kScrStride = 17;
 constexpr uint32_t kScrFloats = 2 * 16 * kScrStride + kTileRows;
@@ -273,7 +283,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const Params p) {
 
   pdl_wait();                 // activations (and residual target) are now visible
   pdl_launch_dependents();    // let the next kernel start streaming its weights
-  if (p.running && *p.running == 0u) {
+  if (!any_running(p)) {
     if (threadIdx.x == 0)  // generation stopped: drain the stages in flight and leave
       for (uint32_t j = 0; j < issued; ++j) (void)mbar_wait(&bars[j % p.nstage], (j / p.nstage) & 1u, nullptr);
     return;
@@ -528,6 +538,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const Params p) {
           for (int w = 0; w < kWarps; ++w) v[m] += redbuf[((w * 2 + m) * kTileRows + row) * nbatch + b];
         }
         const uint32_t R = tile * kTileRows + row;
+        if (p.running && p.running[b * p.run_step] == 0u) continue;  // this batch row has stopped
         float* yp = p.y ? p.y + static_cast<size_t>(b) * p.y_stride + R : nullptr;
         if (p.epilogue == kSwiGLU) {
           const float gv = v[0], uv = v[1];
@@ -564,7 +575,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const Params p) {
         const unsigned long long c = cand[threadIdx.x * kTileRows + row];
         m = c > m ? c : m;
       }
-      if (m) atomicMax(p.argmax + threadIdx.x, m);
+      if (m) atomicMax(p.argmax + static_cast<size_t>(threadIdx.x) * p.arg_step, m);
     }
   }
 }
@@ -755,7 +766,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_tiled_kernel(const Params p)
 
   pdl_wait();                 // activations (and residual target) are now visible
   pdl_launch_dependents();    // let the next kernel start streaming its weights
-  if (p.running && *p.running == 0u) {
+  if (!any_running(p)) {
     if (threadIdx.x == 0)  // generation stopped: drain the stages in flight and leave
       for (uint32_t j = 0; j < issued; ++j) (void)mbar_wait(&bars[j % p.nstage], (j / p.nstage) & 1u, nullptr);
     return;
@@ -943,6 +954,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_tiled_kernel(const Params p)
           for (int w = 0; w < kWarps; ++w) v[m] += redbuf[((w * 2 + m) * kTileRows + row) * nbatch + b];
         }
         const uint32_t R = tile * kTileRows + row;
+        if (p.running && p.running[b * p.run_step] == 0u) continue;  // this batch row has stopped
         float* yp = p.y ? p.y + static_cast<size_t>(b) * p.y_stride + R : nullptr;
         if (p.epilogue == kSwiGLU) {
           const float gv = v[0], uv = v[1];
@@ -979,7 +991,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_tiled_kernel(const Params p)
         const unsigned long long c = cand[threadIdx.x * kTileRows + row];
         m = c > m ? c : m;
       }
-      if (m) atomicMax(p.argmax + threadIdx.x, m);
+      if (m) atomicMax(p.argmax + static_cast<size_t>(threadIdx.x) * p.arg_step, m);
     }
   }
 }
@@ -1107,7 +1119,6 @@ cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t s) {
   if (a.epilogue == kSwiGLU && !a.w1) return cudaErrorInvalidValue;
   if (a.epilogue != kSwiGLU && a.w1) return cudaErrorInvalidValue;
   if (!a.y && !a.argmax) return cudaErrorInvalidValue;
-  if (a.argmax && a.batch * kTileRows > static_cast<uint32_t>(kThreads)) return cudaErrorInvalidValue;
   if ((a.prologue == kHeadGate || a.prologue == kSigmoidGate) && !a.z) return cudaErrorInvalidValue;
   if ((a.prologue == kRmsNorm || a.prologue == kHeadGate) && !a.norm_w) return cudaErrorInvalidValue;
   if (a.prologue == kHeadGate && a.cols % 128) return cudaErrorInvalidValue;
@@ -1117,7 +1128,7 @@ cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t s) {
   const uint32_t x_stride = a.x_stride ? a.x_stride : a.cols;
   if ((!tiled && row_bytes % 16) || reinterpret_cast<uintptr_t>(a.w0) % 16 || reinterpret_cast<uintptr_t>(a.w1) % 16 ||
       reinterpret_cast<uintptr_t>(a.x) % 16 || reinterpret_cast<uintptr_t>(a.z) % 16 ||
-      reinterpret_cast<uintptr_t>(a.norm_w) % 16 || x_stride % 4)
+      reinterpret_cast<uintptr_t>(a.norm_w) % 16 || x_stride % 4 || a.z_stride % 4)
     return cudaErrorMisalignedAddress;  // rows, activations and norm weights are read as 16-byte vectors
   Params p = {};
   p.w[0] = a.w0;
@@ -1135,12 +1146,15 @@ cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t s) {
   p.norm_w = a.norm_w;
   p.eps = a.eps;
   p.z = a.z;
+  p.z_stride = a.z_stride ? a.z_stride : x_stride;
   p.epilogue = a.epilogue;
   p.y = a.y;
   p.y_stride = a.y_stride ? a.y_stride : a.rows;
   p.argmax = a.argmax;
   p.err = a.err;
   p.running = a.running;
+  p.run_step = a.running_step ? a.running_step : 1u;
+  p.arg_step = a.argmax_step ? a.argmax_step : 1u;
   // Batch rows run in launches of at most 8 rows (each launch streams the
   // weights once); a launch's activation tables must fit in shared memory.
   for (uint32_t b0 = 0; b0 < a.batch;) {
@@ -1153,9 +1167,10 @@ cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t s) {
     Params q = p;
     q.batch = nb;
     q.x = a.x + static_cast<size_t>(b0) * x_stride;
-    q.z = a.z ? a.z + static_cast<size_t>(b0) * x_stride : nullptr;
+    q.z = a.z ? a.z + static_cast<size_t>(b0) * p.z_stride : nullptr;
     q.y = a.y ? a.y + static_cast<size_t>(b0) * p.y_stride : nullptr;
-    q.argmax = a.argmax ? a.argmax + b0 : nullptr;
+    q.argmax = a.argmax ? a.argmax + static_cast<size_t>(b0) * p.arg_step : nullptr;
+    q.running = a.running ? a.running + static_cast<size_t>(b0) * p.run_step : nullptr;
     const cudaError_t e = tiled ? (fmt == kQ4K ? launch_fmt<kQ4K, true>(a, q, s) : launch_fmt<kQ6K, true>(a, q, s))
                                 : (fmt == kQ4K ? launch_fmt<kQ4K, false>(a, q, s) : launch_fmt<kQ6K, false>(a, q, s));
     if (e != cudaSuccess) return e;

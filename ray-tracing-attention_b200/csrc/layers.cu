@@ -56,33 +56,45 @@ __global__ void __launch_bounds__(256) embed_kernel(EmbedParams p) {
   pdl_wait();
   pdl_launch_dependents();
   __shared__ uint32_t token_s, go_s;
-  Control* c = p.ctrl;
+  const uint32_t z = blockIdx.x;  // sequence
+  Control* c = p.ctrl + z;
   if (threadIdx.x == 0) {
+    // every control word this step needs, read at once (one round trip)
+    const unsigned long long key = c->argkey;
+    const uint32_t running = c->running, n_out = c->n_out, pos_next = c->pos_next;
+    const uint32_t stop0 = c->stops[0], stop1 = c->stops[1];
     uint32_t token = 0xffffffffu, go = 0u;
     if (p.mode == kEmbedDecode) {
-      if (c->running) {
-        const unsigned long long key = c->argkey;
+      if (running) {
         c->argkey = 0ull;
         token = ~static_cast<uint32_t>(key & 0xffffffffull);
         if (key == 0ull || token >= p.vocab) {
           atomicOr(&c->err, RTA_DEVERR_TOKEN);
           c->running = 0u;
         } else {
-          if (c->n_out < kMaxOut) c->ids[c->n_out] = token;
-          c->n_out += 1u;
+          if (n_out < kMaxOut) c->ids[n_out] = token;
+          c->n_out = n_out + 1u;
           c->best_key = key;
-          if (token == c->stops[0] || token == c->stops[1]) c->running = 0u;
+          if (token == stop0 || token == stop1) c->running = 0u;
           else go = 1u;
         }
       }
     } else {
-      token = p.prompt[c->pos_next];
-      go = token < p.vocab ? 1u : 0u;
-      if (!go) atomicOr(&c->err, RTA_DEVERR_TOKEN);
+      // a sequence whose prompt is consumed sits out the remaining prefill steps
+      if (running && pos_next < c->prompt_len) {
+        token = p.prompt[static_cast<size_t>(z) * p.prompt_stride + pos_next];
+        go = token < p.vocab ? 1u : 0u;
+        if (!go) {
+          atomicOr(&c->err, RTA_DEVERR_TOKEN);
+          c->running = 0u;
+        }
+      } else if (running) {
+        c->running = 0u;
+      }
     }
     if (go) {
-      c->pos_cur = c->pos_next;
-      c->pos_next += 1u;
+      c->pos_cur = pos_next;
+      c->pos_next = pos_next + 1u;
     }
     token_s = token;
     go_s = go;
@@ -91,9 +103,10 @@ __global__ void __launch_bounds__(256) embed_kernel(EmbedParams p) {
   if (!go_s) return;
   const uint8_t* row = p.table + static_cast<size_t>(token_s) * p.row_bytes;
   const uint32_t bb = p.fmt == kQ4K ? 144u : 210u;
+  float* state = p.state + static_cast<size_t>(z) * p.D;
   for (uint32_t i = threadIdx.x; i < p.D; i += blockDim.x) {
     const uint8_t* blk = row + (i / 256u) * bb;
-    p.state[i] = p.fmt == kQ4K ? q4k_row_value(blk, i % 256u) : q6k_row_value(blk, i % 256u);
+    state[i] = p.fmt == kQ4K ? q4k_row_value(blk, i % 256u) : q6k_row_value(blk, i % 256u);
   }
 }
 
@@ -105,14 +118,16 @@ __global__ void __launch_bounds__(256) embed_kernel(EmbedParams p) {
 __global__ void __launch_bounds__(256) attn_prep_kernel(PrepParams p) {
   pdl_wait();
   pdl_launch_dependents();
-  if (p.running && *p.running == 0u) return;
+  const uint32_t z = blockIdx.y;  // sequence
+  if (p.running && p.running[z * p.ctrl_step] == 0u) return;
   __shared__ float red[16];
   __shared__ float xs[256];
   const uint32_t d = threadIdx.x, hd = p.hd;
-  const uint32_t pos = *p.pos;
+  const uint32_t pos = p.pos[z * p.ctrl_step];
   const bool is_q = blockIdx.x < p.heads;
   const uint32_t head = is_q ? blockIdx.x : blockIdx.x - p.heads;
-  const float* src = is_q ? p.qkvg + head * hd : p.qkvg + p.q_width + head * hd;
+  const float* qkvg = p.qkvg + z * p.qkvg_seq;
+  const float* src = is_q ? qkvg + head * hd : qkvg + p.q_width + head * hd;
   float x = d < hd ? src[d] : 0.f;
   if (p.qk_norm) {
     const float ss = block_sum256(x * x, red);
@@ -133,12 +148,12 @@ __global__ void __launch_bounds__(256) attn_prep_kernel(PrepParams p) {
   }
   if (d >= hd) return;
   if (is_q) {
-    p.qout[head * hd + d] = x;
+    p.qout[(static_cast<size_t>(z) * p.heads + head) * hd + d] = x;
   } else {
     const size_t slot = static_cast<size_t>(pos % p.capacity);
-    const size_t at = (static_cast<size_t>(head) * p.capacity + slot) * hd + d;
+    const size_t at = ((static_cast<size_t>(z) * p.kvh + head) * p.capacity + slot) * hd + d;
     p.kcache[at] = __float2half_rn(x);
-    const float v = p.qkvg[p.q_width + p.kv_width + head * hd + d];
+    const float v = qkvg[p.q_width + p.kv_width + head * hd + d];
     p.vcache[at] = __float2half_rn(v);
   }
 }
@@ -200,12 +215,15 @@ __device__ __forceinline__ void prefetch_l2(const void* ptr) {
 __global__ void __launch_bounds__(256) gdn_kernel(GdnParams p) {
   __shared__ float red1[8], red2[16], red3[16];
   __shared__ float qn[128], kn[128], vv[kGdnRows];
-  const uint32_t h = blockIdx.x, slice = blockIdx.y, tid = threadIdx.x;
+  const uint32_t h = blockIdx.x, slice = blockIdx.y, z = blockIdx.z, tid = threadIdx.x;
   const uint32_t HD = 128u, S = p.H * HD, K = p.KH * HD, kh = h % p.KH;
   const uint32_t warp = tid >> 5, lane = tid & 31u;
+  const float* x_seq = p.x + static_cast<size_t>(z) * p.D;
+  const float* proj = p.proj + z * p.proj_seq;
+  float* conv_state = p.conv_state + z * p.conv_seq;
 
   // ---- independent of the preceding kernels: state rows, weights, conv history
-  float* st = p.rec + static_cast<size_t>(h) * HD * HD;
+  float* st = p.rec + z * p.rec_seq + static_cast<size_t>(h) * HD * HD;
   float2 s0[kGdnRowsPerWarp], s1[kGdnRowsPerWarp];
 #pragma unroll
   for (uint32_t i = 0; i < kGdnRowsPerWarp; ++i) {
@@ -230,35 +248,35 @@ __global__ void __launch_bounds__(256) gdn_kernel(GdnParams p) {
 #pragma unroll
   for (int b = 0; b < 2; ++b)
 #pragma unroll
-    for (int j = 0; j < 3; ++j) pq[b][j] = p.conv_state[b * buf + qk_coord * 3u + j];
+    for (int j = 0; j < 3; ++j) pq[b][j] = conv_state[b * buf + qk_coord * 3u + j];
   float4 wv = make_float4(0.f, 0.f, 0.f, 0.f);
   if (tid < kGdnRows) {
     wv = *reinterpret_cast<const float4*>(p.conv_w + static_cast<size_t>(v_coord) * 4u);
 #pragma unroll
     for (int b = 0; b < 2; ++b)
 #pragma unroll
-      for (int j = 0; j < 3; ++j) pv[b][j] = p.conv_state[b * buf + v_coord * 3u + j];
+      for (int j = 0; j < 3; ++j) pv[b][j] = conv_state[b * buf + v_coord * 3u + j];
   }
   const float a_log = p.a_log[h], dt_bias = p.dt_bias[h];
 
   pdl_wait();
   pdl_launch_dependents();
-  if (p.running && *p.running == 0u) return;
-  const uint32_t par = (*p.pos) & 1u;
-  float* next = p.conv_state + (par ^ 1u) * buf;
+  if (p.running && p.running[z * p.ctrl_step] == 0u) return;
+  const uint32_t par = p.pos[z * p.ctrl_step] & 1u;
+  float* next = conv_state + (par ^ 1u) * buf;
   const float pq0 = par ? pq[1][0] : pq[0][0], pq1 = par ? pq[1][1] : pq[0][1], pq2 = par ? pq[1][2] : pq[0][2];
   const float pv0 = par ? pv[1][0] : pv[0][0], pv1 = par ? pv[1][1] : pv[0][1], pv2 = par ? pv[1][2] : pv[0][2];
 
   // ---- op 18 gates: a, b = (rmsnorm(x) * attn_norm) . W_alpha[h], W_beta[h]
   float ss[1] = {0.f};
-  for (uint32_t c = tid; c < p.D; c += 256u) ss[0] += p.x[c] * p.x[c];
-  const float raw_q = p.proj[tid < 128u ? kh * HD + tid : K + kh * HD + (tid - 128u)];
-  const float raw_v = tid < kGdnRows ? p.proj[2u * K + h * HD + slice * kGdnRows + tid] : 0.f;
+  for (uint32_t c = tid; c < p.D; c += 256u) ss[0] += x_seq[c] * x_seq[c];
+  const float raw_q = proj[tid < 128u ? kh * HD + tid : K + kh * HD + (tid - 128u)];
+  const float raw_v = tid < kGdnRows ? proj[2u * K + h * HD + slice * kGdnRows + tid] : 0.f;
   block_sums<1>(ss, red1);
   const float inv = rsqrtf(ss[0] / static_cast<float>(p.D) + p.eps);
   float ab[2] = {0.f, 0.f};
   for (uint32_t c = tid; c < p.D; c += 256u) {
-    const float xn = p.x[c] * inv * p.attn_norm[c];
+    const float xn = x_seq[c] * inv * p.attn_norm[c];
     ab[0] += xn * p.wa[static_cast<size_t>(h) * p.D + c];
     ab[1] += xn * p.wb[static_cast<size_t>(h) * p.D + c];
   }
@@ -318,7 +336,7 @@ __global__ void __launch_bounds__(256) gdn_kernel(GdnParams p) {
     float* row = st + static_cast<size_t>(v) * HD;
     *reinterpret_cast<float2*>(row + 2 * lane) = a;
     *reinterpret_cast<float2*>(row + 2 * lane + 64) = b;
-    if (lane == 0) p.out[h * HD + v] = o;
+    if (lane == 0) p.out[static_cast<size_t>(z) * S + h * HD + v] = o;
   }
 }
 
@@ -349,17 +367,18 @@ cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, void** args, cudaS
 
 cudaError_t launch_embed(const EmbedParams& p, cudaStream_t s, bool pdl) {
   void* args[] = {const_cast<EmbedParams*>(&p)};
-  return launch_pdl(reinterpret_cast<const void*>(embed_kernel), dim3(1), dim3(256), args, s, pdl);
+  return launch_pdl(reinterpret_cast<const void*>(embed_kernel), dim3(p.nseq), dim3(256), args, s, pdl);
 }
 cudaError_t launch_attn_prep(const PrepParams& p, cudaStream_t s, bool pdl) {
   if (p.hd > 256) return cudaErrorInvalidValue;
   void* args[] = {const_cast<PrepParams*>(&p)};
-  return launch_pdl(reinterpret_cast<const void*>(attn_prep_kernel), dim3(p.heads + p.kvh), dim3(256), args, s, pdl);
+  return launch_pdl(reinterpret_cast<const void*>(attn_prep_kernel), dim3(p.heads + p.kvh, p.nseq), dim3(256), args, s,
+                    pdl);
 }
 cudaError_t launch_gdn(const GdnParams& p, cudaStream_t s, bool pdl) {
   void* args[] = {const_cast<GdnParams*>(&p)};
-  return launch_pdl(reinterpret_cast<const void*>(gdn_kernel), dim3(p.H, 128u / kGdnRows), dim3(256), args, s,
-                    pdl);
+  return launch_pdl(reinterpret_cast<const void*>(gdn_kernel), dim3(p.H, 128u / kGdnRows, p.nseq), dim3(256), args,
+                    s, pdl);
 }
 cudaError_t launch_gather_rows(const uint8_t* src, const uint32_t* map, uint32_t rows, uint32_t row_bytes,
                                uint8_t* dst, cudaStream_t s) {

@@ -19,7 +19,7 @@ struct Control {
   uint32_t n_out;               // ids emitted by this generate call
   uint32_t stops[2];
   uint32_t err;
-  uint32_t pad;
+  uint32_t prompt_len;          // prefill: prompt ids of this sequence
   uint32_t ids[kMaxOut];
 };
 
@@ -28,10 +28,12 @@ struct EmbedParams {
   const uint8_t* table = nullptr;  // token_embd rows (Q4_K / Q6_K)
   int fmt = 14;
   uint32_t D = 0, row_bytes = 0, vocab = 0;
-  Control* ctrl = nullptr;
-  const uint32_t* prompt = nullptr;  // prefill ids by absolute position
+  Control* ctrl = nullptr;           // [nseq] control blocks
+  const uint32_t* prompt = nullptr;  // [nseq][prompt_stride] prefill ids by absolute position
+  uint32_t prompt_stride = 0;
   int mode = kEmbedDecode;
-  float* state = nullptr;
+  float* state = nullptr;            // [nseq][D]
+  uint32_t nseq = 1;
 };
 
 struct PrepParams {
@@ -43,11 +45,13 @@ struct PrepParams {
   uint32_t heads = 16, kvh = 4, hd = 256, group = 4, rotary = 0, qk_norm = 1;
   uint32_t q_width = 0, kv_width = 0;
   float* qout = nullptr;
-  __half* kcache = nullptr;  // this layer: [kvh][capacity][hd]
+  __half* kcache = nullptr;  // this layer: [nseq][kvh][capacity][hd]
   __half* vcache = nullptr;
   uint32_t capacity = 0;
-  const uint32_t* pos = nullptr;
-  const uint32_t* running = nullptr;
+  const uint32_t* pos = nullptr;      // sequence z reads pos[z * ctrl_step]
+  const uint32_t* running = nullptr;  // likewise
+  uint32_t nseq = 1, ctrl_step = 0;
+  size_t qkvg_seq = 0;                // floats between sequences' projections
 };
 
 struct GdnParams {
@@ -64,8 +68,11 @@ struct GdnParams {
   float* rec = nullptr;              // [H][128][128] (value, key)
   float* out = nullptr;              // [S] detector output (before the gated norm)
   uint32_t D = 0, H = 0, KH = 0;
-  const uint32_t* pos = nullptr;
-  const uint32_t* running = nullptr;
+  const uint32_t* pos = nullptr;      // sequence z reads pos[z * ctrl_step]
+  const uint32_t* running = nullptr;  // likewise
+  uint32_t nseq = 1, ctrl_step = 0;
+  size_t proj_seq = 0;                // floats between sequences' projections
+  size_t conv_seq = 0, rec_seq = 0;   // floats between sequences' conv history / recurrent state
 };
 
 cudaError_t launch_embed(const EmbedParams& p, cudaStream_t s, bool pdl);

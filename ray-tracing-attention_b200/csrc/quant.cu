@@ -7,6 +7,8 @@
 // so no multiply-add is contracted and results match the CPU restatement bit
 // for bit.  The dequantizer is ggufValue (resident_quant.glsl:10-19):
 // (d*sc)*q - dmin*m and (d*scale)*(q6-32).
+#include <algorithm>
+
 #include "rta_internal.h"
 
 namespace rta {
@@ -136,6 +138,13 @@ __global__ void random_normal_kernel(uint64_t seed, float sigma, float mean, siz
   if (i < n) dst[i] = mean + sigma * synthetic_normal(seed, i);
 }
 
+// fp16 variant (synthetic K/V histories); grid-stride for multi-GB rings
+__global__ void random_normal_half_kernel(uint64_t seed, float sigma, size_t n, __half* __restrict__ dst) {
+  for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x)
+    dst[i] = __float2half_rn(sigma * synthetic_normal(seed, i));
+}
+
 __device__ __forceinline__ float q4k_value(const uint8_t* b, uint32_t index) {
   const uint32_t group = index / 32u;
   uint32_t sc, mn;
@@ -185,6 +194,12 @@ cudaError_t launch_random_quantize(int fmt, uint64_t seed, float sigma, uint64_t
 cudaError_t launch_random_normal(uint64_t seed, float sigma, float mean, size_t n, float* dst, cudaStream_t s) {
   if (n == 0) return cudaSuccess;
   random_normal_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(seed, sigma, mean, n, dst);
+  return cudaGetLastError();
+}
+cudaError_t launch_random_normal_half(uint64_t seed, float sigma, size_t n, __half* dst, cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  const size_t blocks = std::min<size_t>((n + 255) / 256, 148u * 64u);
+  random_normal_half_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(seed, sigma, n, dst);
   return cudaGetLastError();
 }
 cudaError_t launch_dequantize(int fmt, const uint8_t* src, size_t nblocks, float* dst, cudaStream_t s) {

@@ -2,6 +2,7 @@
 // decode engine and the C-ABI layer (capi.cu).  Not installed; the public
 // boundary is include/rta.h.
 #pragma once
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <cstddef>
 #include <cstdint>
@@ -16,7 +17,7 @@ constexpr int kF32 = 0, kF16 = 1, kBF16 = 30, kQ4K = 12, kQ6K = 14;  // export.p
 // see launch_tile_weights).  Codes of this library, not of the exporter.
 constexpr int kTiledOffset = 100, kQ4KTiled = kQ4K + kTiledOffset, kQ6KTiled = kQ6K + kTiledOffset;
 constexpr uint32_t kQ4KBytes = 144, kQ6KBytes = 210;
-constexpr uint32_t kMaxBatch = 32;  // GEMV batch rows per launch (mma slices of 4)
+constexpr uint32_t kMaxBatch = 256;  // GEMV batch rows per call (run as launches of up to 8 rows)
 
 inline uint32_t block_bytes(int fmt) { return fmt == kQ4K || fmt == kQ4KTiled ? kQ4KBytes : kQ6KBytes; }
 
@@ -28,6 +29,7 @@ cudaError_t launch_quantize(int fmt, const float* src, size_t nblocks, uint8_t* 
 cudaError_t launch_random_quantize(int fmt, uint64_t seed, float sigma, uint64_t first_block, size_t nblocks,
                                    uint8_t* dst, cudaStream_t s);
 cudaError_t launch_random_normal(uint64_t seed, float sigma, float mean, size_t n, float* dst, cudaStream_t s);
+cudaError_t launch_random_normal_half(uint64_t seed, float sigma, size_t n, __half* dst, cudaStream_t s);
 cudaError_t launch_dequantize(int fmt, const uint8_t* src, size_t nblocks, float* dst, cudaStream_t s);
 
 // ----------------------------------------------------------------- gemv.cu
@@ -53,14 +55,17 @@ struct GemvArgs {
   int prologue = kPlain;
   const float* norm_w = nullptr;
   float eps = 1e-6f;
-  const float* z = nullptr;     // gate input for kHeadGate / kSigmoidGate, same stride as x
+  const float* z = nullptr;     // gate input for kHeadGate / kSigmoidGate
+  uint32_t z_stride = 0;        // floats between batch rows of z (0: x_stride)
   int epilogue = kStore;
   float* y = nullptr;
   uint32_t y_stride = 0;
   // optional argmax over the rows of batch row b (vocabulary readout):
   unsigned long long* argmax = nullptr;  // [batch] packed (order key, ~id); null = none
+  uint32_t argmax_step = 1;              // u64 elements between batch rows' argmax keys
   uint32_t* err = nullptr;               // device error word (may be null)
-  const uint32_t* running = nullptr;     // optional device flag: 0 -> skip (generation stopped)
+  const uint32_t* running = nullptr;     // optional per-row device flags: 0 -> that row is skipped
+  uint32_t running_step = 1;             // u32 elements between batch rows' flags
   bool pdl = false;                      // launch with programmatic stream serialization
 };
 cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t s);

@@ -34,6 +34,11 @@ _P, _U32, _SZ, _I = ctypes.c_void_p, ctypes.c_uint32, ctypes.c_size_t, ctypes.c_
 _SIGS = {
     "rta_model_last_error": (ctypes.c_char_p, []),
     "rta_model_open": (_I, [ctypes.POINTER(ModelSpecC), _P, _SZ, _P, _SZ, _P, _SZ, _U32, _I, ctypes.POINTER(_P)]),
+    "rta_model_open_batch": (_I, [ctypes.POINTER(ModelSpecC), _P, _SZ, _P, _SZ, _P, _SZ, _U32, _U32, _I,
+                                  ctypes.POINTER(_P)]),
+    "rta_model_prefill_batch": (_I, [_P, _P, _P, _U32, _P, ctypes.POINTER(ctypes.c_double)]),
+    "rta_model_seed_history": (_I, [_P, _P, ctypes.c_uint64]),
+    "rta_model_generate_batch": (_I, [_P, _U32, _P, _P, ctypes.POINTER(ctypes.c_double)]),
     "rta_model_open_files": (_I, [ctypes.POINTER(ModelSpecC), ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p,
                                   _U32, _I, ctypes.POINTER(_P)]),
     "rta_model_close": (None, [_P]),
@@ -45,7 +50,8 @@ _SIGS = {
     "rta_model_resources": (_I, [_P, _P, _SZ]),
 }
 RESOURCE_NAMES = ("payload_bytes", "derived_layer_bytes", "history_bytes", "recurrent_state_bytes", "capacity",
-                  "attention_splits", "kernels_per_decode_step", "kernels_per_prefill_step", "position")
+                  "attention_splits", "kernels_per_decode_step", "kernels_per_prefill_step", "position",
+                  "sequences")
 
 
 def _lib_model():
@@ -68,18 +74,22 @@ def _np_ptr(a: np.ndarray):
 
 
 class ResidentModel:
-    """One resident model on one GPU (prefill / generate / mlp / vocabulary)."""
+    """One resident model on one GPU (prefill / generate / mlp / vocabulary).
+    With sequences > 1 the handle decodes that many sequences side by side
+    (prefill_batch / seed_history / generate_batch)."""
 
-    def __init__(self, handle, spec: assets.Spec, capacity: int, device: int):
+    def __init__(self, handle, spec: assets.Spec, capacity: int, device: int, sequences: int = 1):
         self._h = handle
         self.spec = spec
         self.capacity = capacity
         self.device = device
+        self.sequences = sequences
         self.last_gpu_ms = 0.0
 
     # ---------------------------------------------------------------- open
     @classmethod
-    def from_payloads(cls, spec: assets.Spec, params, matrices, basis, capacity: int, device: int = 0):
+    def from_payloads(cls, spec: assets.Spec, params, matrices, basis, capacity: int, device: int = 0,
+                      sequences: int = 1):
         """params: uint32 numpy; matrices/basis: uint8 numpy (host) or torch CUDA tensors (device)."""
         lib = _lib_model()
         params = np.ascontiguousarray(params, np.uint32)
@@ -93,10 +103,10 @@ class ResidentModel:
         bp, bb, bkeep = addr(basis)
         cs = ModelSpecC.from_spec(spec)
         h = ctypes.c_void_p()
-        _check(lib.rta_model_open(ctypes.byref(cs), _np_ptr(params), params.size, mp, mb, bp, bb, capacity, device,
-                                  ctypes.byref(h)))
+        _check(lib.rta_model_open_batch(ctypes.byref(cs), _np_ptr(params), params.size, mp, mb, bp, bb, capacity,
+                                        sequences, device, ctypes.byref(h)))
         del mkeep, bkeep
-        return cls(h, spec, capacity, device)
+        return cls(h, spec, capacity, device, sequences)
 
     @classmethod
     def from_directory(cls, directory, capacity: int, device: int = 0):
@@ -113,13 +123,14 @@ class ResidentModel:
         return cls(h, spec, capacity, device)
 
     @classmethod
-    def synthetic(cls, spec: assets.Spec, seed: int = 0, capacity: int = 1024, device: int = 0):
+    def synthetic(cls, spec: assets.Spec, seed: int = 0, capacity: int = 1024, device: int = 0,
+                  sequences: int = 1):
         """Random-init model of `spec` generated on the GPU (payloads in the exporter's layout)."""
         import torch
         torch.cuda.set_device(device)
         layout = assets.plan(spec, seed)
         mats, basis = assets.generate_device(layout, seed)
-        model = cls.from_payloads(spec, layout.params(), mats, basis, capacity, device)
+        model = cls.from_payloads(spec, layout.params(), mats, basis, capacity, device, sequences)
         model.layout = layout
         del mats, basis
         torch.cuda.empty_cache()
@@ -159,6 +170,38 @@ class ResidentModel:
         _check(_lib_model().rta_model_generate(self._h, count, _np_ptr(out), ctypes.byref(n), ctypes.byref(ms)))
         self.last_gpu_ms = ms.value
         return out[:n.value].copy()
+
+    # ------------------------------------------------------ several sequences
+    def prefill_batch(self, prompts, stops=()):
+        """prompts: one id sequence per handle sequence (empty = idle)."""
+        if len(prompts) != self.sequences:
+            raise ValueError("one prompt per sequence")
+        lengths = np.array([len(p) for p in prompts], np.uint32)
+        stride = max(1, int(lengths.max()))
+        ids = np.zeros((self.sequences, stride), np.uint32)
+        for z, p in enumerate(prompts):
+            ids[z, :len(p)] = np.asarray(p, np.uint32)
+        st = np.array((list(stops)[:2] + [0xFFFFFFFF] * 2)[:2], np.uint32)
+        ms = ctypes.c_double(0)
+        _check(_lib_model().rta_model_prefill_batch(self._h, _np_ptr(ids), _np_ptr(lengths), stride, _np_ptr(st),
+                                                    ctypes.byref(ms)))
+        self.last_gpu_ms = ms.value
+        return ms.value
+
+    def seed_history(self, lengths, seed: int = 0):
+        lengths = np.ascontiguousarray(lengths, np.uint32)
+        if lengths.size != self.sequences:
+            raise ValueError("one history length per sequence")
+        _check(_lib_model().rta_model_seed_history(self._h, _np_ptr(lengths), seed))
+
+    def generate_batch(self, count: int):
+        """Returns one id array per sequence (shorter where a stop id ended it)."""
+        out = np.zeros((self.sequences, count), np.uint32)
+        n = np.zeros(self.sequences, np.uint32)
+        ms = ctypes.c_double(0)
+        _check(_lib_model().rta_model_generate_batch(self._h, count, _np_ptr(out), _np_ptr(n), ctypes.byref(ms)))
+        self.last_gpu_ms = ms.value
+        return [out[z, :n[z]].copy() for z in range(self.sequences)]
 
     def mlp(self, x, layer: int):
         x = np.ascontiguousarray(x, np.float32).reshape(-1, self.spec.hidden_size)
