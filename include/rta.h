@@ -184,10 +184,24 @@ RTA_API const char* rta_model_last_error(void);
 RTA_API rta_status rta_model_open(const rta_model_spec* spec, const uint32_t* params, size_t n_params,
                                   const void* matrices, size_t matrix_bytes, const void* basis, size_t basis_bytes,
                                   uint32_t capacity, int device, rta_model** out);
+/* Model flags. */
+enum {
+  /* Keep the attention history as the reference's packets (per position kv_heads
+   * Q4_K key blocks then kv_heads Q6_K value blocks, 1416 B at 4 x 256;
+   * resident_history_quant.glsl:9-41) instead of fp16 K/V. */
+  RTA_MODEL_PACKET_HISTORY = 1
+};
+RTA_API rta_status rta_model_open_ex(const rta_model_spec* spec, const uint32_t* params, size_t n_params,
+                                     const void* matrices, size_t matrix_bytes, const void* basis, size_t basis_bytes,
+                                     uint32_t capacity, uint32_t sequences, uint32_t flags, int device,
+                                     rta_model** out);
 /* Same, reading the three payload files. */
 RTA_API rta_status rta_model_open_files(const rta_model_spec* spec, const char* optical_model_bin,
                                         const char* geometry_bin, const char* vocabulary_bin, uint32_t capacity,
                                         int device, rta_model** out);
+RTA_API rta_status rta_model_open_files_ex(const rta_model_spec* spec, const char* optical_model_bin,
+                                           const char* geometry_bin, const char* vocabulary_bin, uint32_t capacity,
+                                           uint32_t sequences, uint32_t flags, int device, rta_model** out);
 RTA_API void rta_model_close(rta_model* model);
 
 /* A handle that decodes `sequences` independent sequences side by side (the
@@ -225,6 +239,27 @@ RTA_API rta_status rta_model_prefill(rta_model* model, const uint32_t* ids, uint
  * (Resident::generatePacket, optical_resident.cpp:760-871). */
 RTA_API rta_status rta_model_generate(rta_model* model, uint32_t count, uint32_t* ids, uint32_t* n_out,
                                       double* gpu_ms);
+/* Full-attention diagnostic, worker op 14 (attentionCheck,
+ * resident_attention_runtime.inl:646-753): layer must be a full-attention
+ * layer; q, gate [rows][heads][head_dim] (rotated), k, v [count][kv_heads][head_dim]
+ * compact history of ages history_start .. history_start+count-1; query row r
+ * sits at time query_start + r.  Outputs: out [rows][heads][head_dim] (gated
+ * when the model is), phys [rows][heads][2] = (m + 20, Z), the history packets
+ * [count][packet bytes], and dense receipts [n_records][head_dim + 8 + block/32]
+ * (m, Z, count, work counters, flags, coverage bits, U) in the order row, group
+ * of `block` positions newest first, head.  block: 128, 256 or 512. */
+RTA_API rta_status rta_model_attention(rta_model* model, uint32_t layer, const float* q, const float* k,
+                                       const float* v, const float* gate, uint32_t rows, uint32_t count,
+                                       uint32_t query_start, uint32_t history_start, uint32_t block, float* out,
+                                       float* phys, uint8_t* packets, uint32_t* receipts, uint32_t* n_records,
+                                       double* gpu_ms);
+/* Test hook of a packet-history handle: the last step's last full-attention
+ * layer for sequence `seq` -- q [heads][head_dim] after QK-norm and RoPE, its
+ * gate row, the detector output in o-projection axis order -- and that layer's
+ * visible history packets, oldest first ([*n_positions][packet bytes]; size the
+ * buffer for capacity rows).  No reference counterpart. */
+RTA_API rta_status rta_model_debug_attention(rta_model* model, uint32_t seq, float* q, float* gate, float* att,
+                                             uint8_t* packets, uint32_t* n_positions);
 /* MLP diagnostic, worker op 6 (mlpCheck, optical_resident.cpp:922-949):
  * y = W_down swiglu(W_gate x, W_up x), rows 1..32, host buffers. */
 RTA_API rta_status rta_model_mlp(rta_model* model, uint32_t layer, const float* x, uint32_t rows, float* y,

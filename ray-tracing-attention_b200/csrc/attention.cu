@@ -22,6 +22,7 @@
 #include "../../include/rta.h"
 #include "rta_internal.h"
 #include "attention.h"
+#include "packets.cuh"
 
 namespace rta {
 namespace {
@@ -279,6 +280,212 @@ __global__ void __launch_bounds__(kThreads) attention_split_kernel(const AttnPar
   }
 }
 
+
+// ------------------------------------------------------------ packet history
+// The same split-K detector over the reference's own history format: K as
+// Q4_K and V as Q6_K blocks per (position, KV head).  Every K/V value is
+// decoded exactly as ggufValue does ((d*sc)*q - dmin*m, (d*scale)*(q6-32);
+// resident_quant.glsl:10-19) and all arithmetic is fp32 on the CUDA cores:
+// at 4 query heads per KV head the 1416-byte packet rows, not the FMAs, bound
+// the kernel.
+//
+// Lanes own dimensions.  Scores: lane l decodes the 4 code bytes 16+4l..19+4l
+// of a key block (dims 64p+4(l%8)+j and 64p+32+4(l%8)+j, p = l/8), so a warp
+// reads each key block with one coalesced 128-byte load; eight positions' 4-head
+// partial dots are folded across the warp by a 31-step transpose-reduction
+// after which lane L holds (position L/4, head L%4).  Values: lane l owns dims
+// 32k+l (ql bytes l, 32+l, 64+l, 96+l; qh bytes 128+l, 160+l).
+__device__ __forceinline__ void q4k_group_scale(const uint8_t* hb, uint32_t grp, float d, float dmin, float& dsc,
+                                                float& dmm) {
+  uint32_t sc, mn;
+  if (grp < 4u) {
+    sc = hb[4 + grp] & 63u;
+    mn = hb[8 + grp] & 63u;
+  } else {
+    const uint32_t u = grp - 4u, mixed = hb[12 + u];
+    sc = (mixed & 15u) | ((static_cast<uint32_t>(hb[4 + u]) >> 6) << 4);
+    mn = (mixed >> 4) | ((static_cast<uint32_t>(hb[8 + u]) >> 6) << 4);
+  }
+  dsc = d * static_cast<float>(sc);    // exact (11 + 6 bits)
+  dmm = dmin * static_cast<float>(mn);
+}
+
+__global__ void __launch_bounds__(kThreads) attention_packet_split_kernel(const AttnParams p) {
+  __shared__ float cm[kWarps][kGroup], cz[kWarps][kGroup];
+  __shared__ float co[kWarps][kGroup][kHD];
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+  const uint32_t split = blockIdx.x, kv = blockIdx.y, z = blockIdx.z;
+  pdl_wait();
+  pdl_launch_dependents();
+  if (p.running && p.running[z * p.ctrl_step] == 0u) return;
+
+  uint32_t t, lo, n;
+  window(p, z, t, lo, n);
+  uint32_t first, last;  // ages [first, last)
+  if (p.group_block) {   // newest-first groups of group_block positions
+    const uint64_t top = static_cast<uint64_t>(t) + 1u, off = static_cast<uint64_t>(split) * p.group_block;
+    last = top > off ? static_cast<uint32_t>(top - off) : 0u;
+    if (last < lo) last = lo;
+    first = last > lo + p.group_block ? last - p.group_block : lo;
+  } else {
+    uint32_t chunk = (n + gridDim.x - 1u) / gridDim.x;
+    chunk = (chunk + 63u) / 64u * 64u;
+    if (chunk < 64u) chunk = 64u;
+    first = lo + split * chunk;
+    last = min(t + 1u, first + chunk);
+    if (first > last) first = last;
+  }
+  const uint8_t* rows = p.packets + static_cast<size_t>(z) * p.packet_seq_stride;
+  const uint32_t vbase = p.kvh * kPacketKeyBytes + kv * kPacketValueBytes;
+
+  // this lane's query values in the key layout: qk[h][j] dims 64p+4(l%8)+j, qk[h][4+j] = +32
+  const uint32_t pk = lane / 8u, kcol = 4u * (lane % 8u);
+  float qk[kGroup][8];
+#pragma unroll
+  for (uint32_t h = 0; h < kGroup; ++h) {
+    const float* qh = p.q + static_cast<size_t>(z) * p.q_seq_stride + static_cast<size_t>(kv * kGroup + h) * kHD;
+#pragma unroll
+    for (uint32_t j = 0; j < 4u; ++j) {
+      qk[h][j] = qh[64u * pk + kcol + j];
+      qk[h][4u + j] = qh[64u * pk + 32u + kcol + j];
+    }
+  }
+  float o[kGroup][8];
+#pragma unroll
+  for (uint32_t h = 0; h < kGroup; ++h)
+#pragma unroll
+    for (uint32_t k = 0; k < 8u; ++k) o[h][k] = 0.f;
+  float m_run[kGroup], z_run[kGroup];
+#pragma unroll
+  for (uint32_t h = 0; h < kGroup; ++h) {
+    m_run[h] = -INFINITY;
+    z_run[h] = 0.f;
+  }
+  const float inv_scale = 1.0f / 16.0f;  // 1/sqrt(256), applied after the dot like the reference
+
+  for (uint32_t g0 = first + 8u * warp; g0 < last; g0 += 8u * kWarps) {
+    // ---- scores of positions g0..g0+7 (partial over this lane's 8 dims)
+    float part[32];
+#pragma unroll
+    for (uint32_t pi = 0; pi < 8u; ++pi) {
+      const uint32_t age = g0 + pi < last ? g0 + pi : last - 1u;  // finite filler, masked below
+      const uint8_t* kb = rows + static_cast<size_t>((age - p.packet_base) % p.capacity) * p.packet_stride +
+                          kv * kPacketKeyBytes;
+      const uint32_t hd0 = *reinterpret_cast<const uint32_t*>(kb);
+      const uint32_t code = *reinterpret_cast<const uint32_t*>(kb + 16u + 4u * lane);
+      const float d = half_bits_to_float(hd0 & 0xffffu), dmin = half_bits_to_float(hd0 >> 16);
+      float dsc0, dmm0, dsc1, dmm1;
+      q4k_group_scale(kb, 2u * pk, d, dmin, dsc0, dmm0);
+      q4k_group_scale(kb, 2u * pk + 1u, d, dmin, dsc1, dmm1);
+      float kval[8];
+#pragma unroll
+      for (uint32_t j = 0; j < 4u; ++j) {
+        kval[j] = fmaf(dsc0, static_cast<float>((code >> (8u * j)) & 15u), -dmm0);
+        kval[4u + j] = fmaf(dsc1, static_cast<float>((code >> (8u * j + 4u)) & 15u), -dmm1);
+      }
+#pragma unroll
+      for (uint32_t h = 0; h < kGroup; ++h) {
+        float acc = 0.f;
+#pragma unroll
+        for (uint32_t j = 0; j < 8u; ++j) acc = fmaf(qk[h][j], kval[j], acc);
+        part[pi * 4u + h] = acc;
+      }
+    }
+    // transpose-reduction: lane L ends with the full dot of (position L/4, head L%4)
+#pragma unroll
+    for (uint32_t w = 16u, cnt = 16u; w >= 1u; w >>= 1, cnt >>= 1) {
+      const bool upper = (lane & w) != 0u;
+#pragma unroll
+      for (uint32_t i = 0; i < cnt; ++i) {
+        const float keep = upper ? part[i + cnt] : part[i];
+        const float send = upper ? part[i] : part[i + cnt];
+        part[i] = keep + __shfl_xor_sync(0xffffffffu, send, w);
+      }
+    }
+    const uint32_t my_pos = lane >> 2, my_head = lane & 3u;
+    const float sc = g0 + my_pos < last ? part[0] * inv_scale : -INFINITY;
+    // ---- online max / normaliser per head (lanes with equal lane%4 share a head)
+    float mx = sc;
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+    float m_new[kGroup], keep[kGroup];
+#pragma unroll
+    for (uint32_t h = 0; h < kGroup; ++h) {
+      m_new[h] = fmaxf(m_run[h], __shfl_sync(0xffffffffu, mx, h));
+      keep[h] = m_new[h] == -INFINITY ? 1.f : expf(m_run[h] - m_new[h]);
+    }
+    const float m_sel = my_head == 0u ? m_new[0] : my_head == 1u ? m_new[1] : my_head == 2u ? m_new[2] : m_new[3];
+    const float pr = (sc == -INFINITY || m_sel == -INFINITY) ? 0.f : expf(sc - m_sel);
+    float ps = pr;
+    ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+    ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+    ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+#pragma unroll
+    for (uint32_t h = 0; h < kGroup; ++h) {
+      z_run[h] = z_run[h] * keep[h] + __shfl_sync(0xffffffffu, ps, h);
+      m_run[h] = m_new[h];
+#pragma unroll
+      for (uint32_t k = 0; k < 8u; ++k) o[h][k] *= keep[h];
+    }
+    // ---- weighted values
+#pragma unroll
+    for (uint32_t pi = 0; pi < 8u; ++pi) {
+      if (g0 + pi >= last) break;  // uniform across the warp
+      float w[kGroup];
+#pragma unroll
+      for (uint32_t h = 0; h < kGroup; ++h) w[h] = __shfl_sync(0xffffffffu, pr, pi * 4u + h);
+      const uint8_t* vb =
+          rows + static_cast<size_t>((g0 + pi - p.packet_base) % p.capacity) * p.packet_stride + vbase;
+      const float d = half_bits_to_float(vb[208] | (vb[209] << 8));
+      const uint32_t ql[4] = {vb[lane], vb[32u + lane], vb[64u + lane], vb[96u + lane]};
+      const uint32_t qh[2] = {vb[128u + lane], vb[160u + lane]};
+#pragma unroll
+      for (uint32_t k = 0; k < 8u; ++k) {  // dim 32k + lane: part k/4, ql byte 64(k/4) + 32(k%2) + l
+        const uint32_t part_ = k / 4u;
+        const uint32_t lo4 = (ql[2u * part_ + (k % 2u)] >> (4u * ((k % 4u) / 2u))) & 15u;
+        const uint32_t hi2 = (qh[part_] >> (2u * (k % 4u))) & 3u;
+        const int scale = static_cast<int>(static_cast<int8_t>(vb[192u + 2u * k + (lane >> 4)]));
+        const float v = (d * static_cast<float>(scale)) * static_cast<float>(static_cast<int>(lo4 | (hi2 << 4)) - 32);
+#pragma unroll
+        for (uint32_t h = 0; h < kGroup; ++h) o[h][k] = fmaf(w[h], v, o[h][k]);
+      }
+    }
+  }
+
+  // ---- combine the four warps and publish this split's record
+  if (lane == 0) {
+#pragma unroll
+    for (uint32_t h = 0; h < kGroup; ++h) {
+      cm[warp][h] = m_run[h];
+      cz[warp][h] = z_run[h];
+    }
+  }
+#pragma unroll
+  for (uint32_t h = 0; h < kGroup; ++h)
+#pragma unroll
+    for (uint32_t k = 0; k < 8u; ++k) co[warp][h][32u * k + lane] = o[h][k];
+  __syncthreads();
+  const size_t rec = (static_cast<size_t>(z) * p.kvh + kv) * gridDim.x + split;
+  for (uint32_t i = threadIdx.x; i < kGroup * kHD; i += kThreads) {
+    const uint32_t h = i / kHD, dd = i % kHD;
+    float m = -INFINITY;
+    for (uint32_t w = 0; w < kWarps; ++w) m = fmaxf(m, cm[w][h]);
+    float zs = 0.f, os = 0.f;
+    if (m != -INFINITY)
+      for (uint32_t w = 0; w < kWarps; ++w) {
+        const float e = cm[w][h] == -INFINITY ? 0.f : expf(cm[w][h] - m);
+        zs += cz[w][h] * e;
+        os += co[w][h][dd] * e;
+      }
+    p.part_o[(rec * kGroup + h) * kHD + dd] = os;
+    if (dd == 0) {
+      p.part_m[rec * kGroup + h] = m;
+      p.part_z[rec * kGroup + h] = zs;
+    }
+  }
+}
+
 // Merge the split records of every (sequence, head): m = max m_s,
 // Z = sum Z_s e^(m_s-m), U = sum U_s e^(m_s-m), out = U/max(Z,1e-30)*gate.
 __global__ void __launch_bounds__(kHD) attention_merge_kernel(const AttnParams p, uint32_t nsplit) {
@@ -315,10 +522,41 @@ __global__ void __launch_bounds__(kHD) attention_merge_kernel(const AttnParams p
 
 size_t attention_smem_bytes() { return kStages * kStageBytes + 128 + kWarps * 8 * kTile * 2; }
 
+cudaError_t launch_attention_merge(const AttnParams& p, uint32_t nsplit, uint32_t nseq, bool pdl, cudaStream_t s) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.heads, nseq);
+  cfg.blockDim = dim3(kHD);
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, attention_merge_kernel, p, nsplit);
+}
+
 cudaError_t launch_attention(const AttnParams& p, uint32_t nsplit, uint32_t nseq, bool pdl, cudaStream_t s) {
-  if (p.hd != kHD || p.heads != p.kvh * kGroup || !p.q || !p.k || !p.v || !p.out || !p.part_m || !p.part_z ||
-      !p.part_o || nsplit == 0 || nseq == 0 || p.capacity == 0)
+  if (p.hd != kHD || p.heads != p.kvh * kGroup || !p.q || !p.out || !p.part_m || !p.part_z || !p.part_o ||
+      nsplit == 0 || nseq == 0 || p.capacity == 0)
     return cudaErrorInvalidValue;
+  if (p.packets) {  // the reference's packet history
+    if (p.packet_stride != packet_bytes(p.kvh) || p.packet_stride % 8 || p.packet_seq_stride % 8 ||
+        reinterpret_cast<uintptr_t>(p.packets) % 8)
+      return cudaErrorMisalignedAddress;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(nsplit, p.kvh, nseq);
+    cfg.blockDim = dim3(kThreads);
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, attention_packet_split_kernel, p);
+    if (e != cudaSuccess) return e;
+    return launch_attention_merge(p, nsplit, nseq, pdl, s);
+  }
+  if (!p.k || !p.v) return cudaErrorInvalidValue;
   if (reinterpret_cast<uintptr_t>(p.k) % 16 || reinterpret_cast<uintptr_t>(p.v) % 16 || p.pos_stride % 8 ||
       p.kv_stride % 8 || p.seq_stride % 8)
     return cudaErrorMisalignedAddress;
@@ -346,13 +584,7 @@ cudaError_t launch_attention(const AttnParams& p, uint32_t nsplit, uint32_t nseq
   cfg.numAttrs = 1;
   e = cudaLaunchKernelEx(&cfg, attention_split_kernel, p);
   if (e != cudaSuccess) return e;
-  cudaLaunchConfig_t cfg2 = {};
-  cfg2.gridDim = dim3(p.heads, nseq);
-  cfg2.blockDim = dim3(kHD);
-  cfg2.stream = s;
-  cfg2.attrs = attr;
-  cfg2.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg2, attention_merge_kernel, p, nsplit);
+  return launch_attention_merge(p, nsplit, nseq, pdl, s);
 }
 
 uint32_t attention_default_splits(uint32_t history, uint32_t kvh, int sms) {

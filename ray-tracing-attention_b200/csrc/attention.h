@@ -31,6 +31,16 @@ struct AttnParams {
   float* part_o = nullptr;       // [nseq][kvh][nsplit][4][hd]
   uint32_t* err = nullptr;
   const uint32_t* running = nullptr;  // optional: sequence z skipped when running[z * ctrl_step] == 0
+  // History packets instead of fp16 K/V (the reference's format): per position
+  // kvh Q4_K key blocks then kvh Q6_K value blocks; age a lives in packet row
+  // (a - packet_base) % capacity, rows packet_stride bytes apart, sequences
+  // packet_seq_stride bytes apart.
+  const uint8_t* packets = nullptr;
+  size_t packet_seq_stride = 0;
+  uint32_t packet_stride = 0, packet_base = 0;
+  // 0: splits cut the visible window into equal chunks; > 0: split g covers the
+  // g-th newest group of `group_block` positions (the reference's receipt groups).
+  uint32_t group_block = 0;
 };
 
 size_t attention_smem_bytes();

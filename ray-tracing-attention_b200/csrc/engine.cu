@@ -22,6 +22,7 @@
 #include "../../include/rta.h"
 #include "attention.h"
 #include "layers.h"
+#include "packets.cuh"
 #include "rta_internal.h"
 
 namespace rta {
@@ -106,6 +107,9 @@ struct Engine {
   // activations
   DevBuf<float> state, proj, qproc, att, gdn, act, inv_freq, part_m, part_z, part_o, scratch_x, scratch_y;
   DevBuf<__half> kcache, vcache;
+  bool packet_history = false;  // the reference's history packets instead of fp16 K/V
+  DevBuf<uint8_t> pring;        // [full layer][sequence][capacity][packet_bytes(kvh)]
+  uint32_t pbytes = 0;
   DevBuf<float> rec, conv;
   DevBuf<Control> ctrl;
   DevBuf<uint32_t> prompt;
@@ -240,9 +244,11 @@ struct Engine {
   }
 
   void load(const rta_model_spec& sp, const uint32_t* prm, size_t n_params, const void* mat, size_t matrix_bytes,
-            const void* bas, size_t basis_bytes, uint32_t cap, uint32_t sequences, int dev) {
+            const void* bas, size_t basis_bytes, uint32_t cap, uint32_t sequences, uint32_t flags, int dev) {
     spec = sp;
     device = dev;
+    require((flags & ~static_cast<uint32_t>(RTA_MODEL_PACKET_HISTORY)) == 0, "unknown model flags", RTA_E_ARG);
+    packet_history = (flags & RTA_MODEL_PACKET_HISTORY) != 0;
     require(sequences >= 1 && sequences <= 256, "sequences must be 1..256", RTA_E_ARG);
     nseq = sequences;
     require(spec.depth >= 1 && spec.depth <= 256, "depth must be 1..256", RTA_E_ARG);
@@ -378,8 +384,15 @@ struct Engine {
     part_z.alloc(recs);
     part_o.alloc(recs * hd);
     // [layer][sequence] x per-sequence blocks
-    kcache.alloc(static_cast<size_t>(std::max(1u, n_full)) * nseq * spec.kv_heads * capacity * hd);
-    vcache.alloc(kcache.n);
+    pbytes = packet_bytes(spec.kv_heads);
+    if (packet_history) {
+      pring.alloc(static_cast<size_t>(std::max(1u, n_full)) * nseq * capacity * pbytes);
+      kcache.alloc(1);
+      vcache.alloc(1);
+    } else {
+      kcache.alloc(static_cast<size_t>(std::max(1u, n_full)) * nseq * spec.kv_heads * capacity * hd);
+      vcache.alloc(kcache.n);
+    }
     rec.alloc(static_cast<size_t>(std::max(1u, n_rec)) * nseq * spec.state_heads * 128 * 128);
     conv.alloc(static_cast<size_t>(std::max(1u, n_rec)) * nseq * 2 * 3 * S() * 3);
     ctrl.alloc(nseq);
@@ -495,6 +508,8 @@ struct Engine {
         pp.nseq = nseq;
         pp.ctrl_step = cstep;
         pp.qkvg_seq = projw;
+        const size_t layer_pkt = static_cast<size_t>(nseq) * capacity * pbytes;
+        if (packet_history) pp.packets = pring.p + L.fi * layer_pkt;
         RTA_CUDA(launch_attn_prep(pp, s, true));
         AttnParams ap;
         ap.q = qproc.p;
@@ -502,6 +517,11 @@ struct Engine {
         ap.v = pp.vcache;
         ap.q_seq_stride = Q();
         ap.seq_stride = seq_kv;
+        if (packet_history) {
+          ap.packets = pp.packets;
+          ap.packet_seq_stride = static_cast<size_t>(capacity) * pbytes;
+          ap.packet_stride = pbytes;
+        }
         ap.kv_stride = static_cast<size_t>(capacity) * hd;
         ap.pos_stride = hd;
         ap.heads = spec.attention_heads;
@@ -744,8 +764,12 @@ struct Engine {
   void seed_history(const uint32_t* lengths, uint64_t seed) {
     for (uint32_t z = 0; z < nseq; ++z) require(lengths[z] >= 1, "history lengths must be positive", RTA_E_ARG);
     reset_sequence();
-    RTA_CUDA(launch_random_normal_half(seed, 1.0f, kcache.n, kcache.p, stream));
-    RTA_CUDA(launch_random_normal_half(seed + 1, 1.0f, vcache.n, vcache.p, stream));
+    if (packet_history) {
+      RTA_CUDA(launch_random_packets(seed, pring.n / pbytes, spec.kv_heads, pring.p, stream));
+    } else {
+      RTA_CUDA(launch_random_normal_half(seed, 1.0f, kcache.n, kcache.p, stream));
+      RTA_CUDA(launch_random_normal_half(seed + 1, 1.0f, vcache.n, vcache.p, stream));
+    }
     RTA_CUDA(launch_random_normal(seed + 2, 0.02f, 0.0f, rec.n, rec.p, stream));
     RTA_CUDA(launch_random_normal(seed + 3, 1.0f, 0.0f, conv.n, conv.p, stream));
     RTA_CUDA(launch_random_normal(seed + 4, 1.0f, 0.0f, state.n, state.p, stream));
@@ -792,6 +816,170 @@ struct Engine {
     require(nseq == 1, "this handle decodes several sequences: use the batch generate", RTA_E_STATE);
     require(position > 0, "prefill before generate", RTA_E_STATE);
     generate_batch(count, ids_out, n_out);
+  }
+
+  // Worker op 14 (attentionCheck, resident_attention_runtime.inl:646-753): the
+  // full-attention detector of one full layer over a supplied causal history.
+  // K/V rows are packed into the reference's history packets (returned), the
+  // detector runs over the packets with one split per newest-first group of
+  // `block` positions, and every (row, group, head) record becomes one dense
+  // receipt (verify_attention_receipts.py:140-203 reads them).
+  void attention_check(uint32_t layer, const float* q, const float* k, const float* v, const float* gate,
+                       uint32_t rows, uint32_t count, uint32_t query_start, uint32_t history_start, uint32_t block,
+                       float* out, float* phys, uint8_t* packets_out, uint32_t* receipts, uint32_t* n_records,
+                       double* timing) {
+    const uint32_t H = spec.attention_heads, KVH = spec.kv_heads, hd = spec.attention_head_dim;
+    require(layer < spec.depth && layers[layer]->full, "attention diagnostic needs a full-attention layer", RTA_E_ARG);
+    require(rows >= 1 && rows <= 32 && count >= 1 && count <= capacity, "attention rows 1..32, count 1..capacity",
+            RTA_E_ARG);
+    require(query_start >= history_start &&
+                static_cast<uint64_t>(query_start) + rows <= static_cast<uint64_t>(history_start) + count,
+            "query times must lie inside the supplied causal history", RTA_E_ARG);
+    require(block == 128 || block == 256 || block == 512, "attention block must be 128, 256 or 512", RTA_E_ARG);
+    const size_t nq = static_cast<size_t>(rows) * H * hd, nk = static_cast<size_t>(count) * KVH * hd;
+    for (size_t i = 0; i < nq; ++i)
+      require(std::isfinite(q[i]) && std::isfinite(gate[i]), "attention values must be finite", RTA_E_ARG);
+    for (size_t i = 0; i < nk; ++i)
+      require(std::isfinite(k[i]) && std::isfinite(v[i]), "attention values must be finite", RTA_E_ARG);
+    // visible positions and receipt groups per row
+    std::vector<uint32_t> visible(rows), times(rows);
+    uint32_t groups = 0, records = 0;
+    for (uint32_t r = 0; r < rows; ++r) {
+      times[r] = query_start + r;
+      visible[r] = std::min(times[r] - history_start + 1u, capacity);
+      const uint32_t g = (visible[r] + block - 1u) / block;
+      groups = std::max(groups, g);
+      records += g * H;
+    }
+    DevBuf<float> dq, dk, dv, dg, dout, dphys, pm, pz, po;
+    DevBuf<uint8_t> dpk;
+    DevBuf<uint32_t> dt, derr;
+    dq.alloc(nq);
+    dg.alloc(nq);
+    dk.alloc(nk);
+    dv.alloc(nk);
+    dout.alloc(nq);
+    dphys.alloc(static_cast<size_t>(rows) * H * 2);
+    const size_t recs = static_cast<size_t>(rows) * KVH * groups * 4;
+    pm.alloc(recs);
+    pz.alloc(recs);
+    po.alloc(recs * hd);
+    dpk.alloc(static_cast<size_t>(count) * pbytes);
+    dt.alloc(rows);
+    derr.alloc(1);
+    derr.zero(stream);
+    RTA_CUDA(cudaMemcpyAsync(dq.p, q, nq * 4, cudaMemcpyHostToDevice, stream));
+    RTA_CUDA(cudaMemcpyAsync(dg.p, gate, nq * 4, cudaMemcpyHostToDevice, stream));
+    RTA_CUDA(cudaMemcpyAsync(dk.p, k, nk * 4, cudaMemcpyHostToDevice, stream));
+    RTA_CUDA(cudaMemcpyAsync(dv.p, v, nk * 4, cudaMemcpyHostToDevice, stream));
+    RTA_CUDA(cudaMemcpyAsync(dt.p, times.data(), rows * 4ull, cudaMemcpyHostToDevice, stream));
+    RTA_CUDA(cudaEventRecord(ev0, stream));
+    RTA_CUDA(launch_pack_history(dk.p, dv.p, count, KVH, dpk.p, stream));
+    AttnParams ap;
+    ap.q = dq.p;
+    ap.q_seq_stride = static_cast<size_t>(H) * hd;
+    ap.heads = H;
+    ap.kvh = KVH;
+    ap.hd = hd;
+    ap.capacity = capacity;
+    ap.history_start = history_start;
+    ap.pos = dt.p;
+    ap.ctrl_step = 1;
+    ap.gate = spec.attention_gate ? dg.p : nullptr;
+    ap.gate_seq_stride = static_cast<size_t>(H) * hd;
+    ap.out = dout.p;
+    ap.out_seq_stride = static_cast<size_t>(H) * hd;
+    ap.phys = dphys.p;
+    ap.part_m = pm.p;
+    ap.part_z = pz.p;
+    ap.part_o = po.p;
+    ap.err = derr.p;
+    ap.packets = dpk.p;
+    ap.packet_seq_stride = 0;  // every row reads the same supplied history
+    ap.packet_stride = pbytes;
+    ap.packet_base = history_start;
+    ap.group_block = block;
+    RTA_CUDA(launch_attention(ap, groups, rows, false, stream));
+    RTA_CUDA(cudaEventRecord(ev1, stream));
+    std::vector<float> hm(recs), hz(recs), ho(recs * hd);
+    RTA_CUDA(cudaMemcpyAsync(out, dout.p, nq * 4, cudaMemcpyDeviceToHost, stream));
+    RTA_CUDA(cudaMemcpyAsync(phys, dphys.p, static_cast<size_t>(rows) * H * 8, cudaMemcpyDeviceToHost, stream));
+    RTA_CUDA(cudaMemcpyAsync(packets_out, dpk.p, static_cast<size_t>(count) * pbytes, cudaMemcpyDeviceToHost,
+                             stream));
+    RTA_CUDA(cudaMemcpyAsync(hm.data(), pm.p, recs * 4, cudaMemcpyDeviceToHost, stream));
+    RTA_CUDA(cudaMemcpyAsync(hz.data(), pz.p, recs * 4, cudaMemcpyDeviceToHost, stream));
+    RTA_CUDA(cudaMemcpyAsync(ho.data(), po.p, recs * hd * 4, cudaMemcpyDeviceToHost, stream));
+    uint32_t err = 0;
+    RTA_CUDA(cudaMemcpyAsync(&err, derr.p, 4, cudaMemcpyDeviceToHost, stream));
+    RTA_CUDA(cudaStreamSynchronize(stream));
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, ev0, ev1);
+    if (timing) timing[0] = ms;
+    require(err == 0, "attention diagnostic device error " + std::to_string(err), RTA_E_DEVICE_CHECK);
+    // dense receipts in the reference's order: row, group (newest first), head
+    const uint32_t words = block / 32u, stride = hd + 8u + words;
+    size_t at = 0;
+    for (uint32_t r = 0; r < rows; ++r) {
+      const uint32_t ng = (visible[r] + block - 1u) / block;
+      for (uint32_t g = 0; g < ng; ++g) {
+        const uint32_t cnt = std::min(block, visible[r] - g * block);
+        for (uint32_t h = 0; h < H; ++h) {
+          const uint32_t kv = h / (H / KVH), hq = h % (H / KVH);
+          const size_t rec = ((static_cast<size_t>(r) * KVH + kv) * groups + g) * 4 + hq;
+          uint32_t* w = receipts + at * stride;
+          const float m = hm[rec], zz = hz[rec];
+          bool finite = std::isfinite(m) && std::isfinite(zz);
+          for (uint32_t d = 0; d < hd; ++d) finite = finite && std::isfinite(ho[rec * hd + d]);
+          std::memcpy(&w[0], &m, 4);
+          std::memcpy(&w[1], &zz, 4);
+          w[2] = cnt;          // positions in the group
+          w[3] = cnt;          // exponentials: one per position
+          w[4] = cnt;          // value rows accumulated one by one (no vector grouping)
+          w[5] = cnt;          // weight contributions
+          // history-traversal counter of the reference's record (head 0 carries
+          // it): 2 + one per 16-position tile, the tiling this kernel also uses
+          w[6] = h == 0 ? 2u + (cnt + 15u) / 16u : 0u;
+          w[7] = finite ? 3u : 1u;  // bit 0: verified, bit 1: finite
+          for (uint32_t i = 0; i < words; ++i) {
+            const uint32_t bits = std::min(32u, cnt > 32u * i ? cnt - 32u * i : 0u);
+            w[8 + i] = bits == 32u ? 0xffffffffu : (1u << bits) - 1u;
+          }
+          std::memcpy(&w[8 + words], &ho[rec * hd], hd * 4ull);
+          ++at;
+        }
+      }
+    }
+    if (n_records) *n_records = records;
+  }
+
+  // Inputs and output of the last full-attention layer of the last step for
+  // sequence z (q after QK-norm and RoPE, the gate row, the detector output in
+  // o-projection axis order) and that layer's visible history packets, oldest
+  // first: what a test needs to recompute the layer's attention independently.
+  uint32_t debug_attention(uint32_t z, float* q, float* gate, float* att, uint8_t* packets) {
+    require(packet_history, "needs a packet-history handle", RTA_E_STATE);
+    require(z < nseq && positions[z] > 0, "sequence has no history", RTA_E_ARG);
+    uint32_t fi = 0;
+    bool any = false;
+    for (auto& L : layers)
+      if (L->full) {
+        fi = L->fi;
+        any = true;
+      }
+    require(any, "model has no full-attention layer", RTA_E_STATE);
+    const uint32_t t = positions[z] - 1u, n = std::min(t + 1u, capacity), lo = t + 1u - n;
+    RTA_CUDA(cudaMemcpyAsync(q, qproc.p + static_cast<size_t>(z) * Q(), Q() * 4ull, cudaMemcpyDeviceToHost, stream));
+    RTA_CUDA(cudaMemcpyAsync(gate, proj.p + static_cast<size_t>(z) * projw + Q() + 2 * KVW(), Q() * 4ull,
+                             cudaMemcpyDeviceToHost, stream));
+    RTA_CUDA(cudaMemcpyAsync(att, this->att.p + static_cast<size_t>(z) * Q(), Q() * 4ull, cudaMemcpyDeviceToHost,
+                             stream));
+    const uint8_t* ring = pring.p + (static_cast<size_t>(fi) * nseq + z) * capacity * pbytes;
+    for (uint32_t i = 0; i < n; ++i)
+      RTA_CUDA(cudaMemcpyAsync(packets + static_cast<size_t>(i) * pbytes,
+                               ring + static_cast<size_t>((lo + i) % capacity) * pbytes, pbytes,
+                               cudaMemcpyDeviceToHost, stream));
+    RTA_CUDA(cudaStreamSynchronize(stream));
+    return n;
   }
 
   void mlp(uint32_t layer, const float* x, uint32_t rows, float* y, float* a) {
@@ -894,9 +1082,9 @@ extern "C" {
 
 const char* rta_model_last_error(void) { return rta::g_model_error.c_str(); }
 
-rta_status rta_model_open_batch(const rta_model_spec* spec, const uint32_t* params, size_t n_params,
-                                const void* matrices, size_t matrix_bytes, const void* basis, size_t basis_bytes,
-                                uint32_t capacity, uint32_t sequences, int device, rta_model** out) {
+rta_status rta_model_open_ex(const rta_model_spec* spec, const uint32_t* params, size_t n_params,
+                             const void* matrices, size_t matrix_bytes, const void* basis, size_t basis_bytes,
+                             uint32_t capacity, uint32_t sequences, uint32_t flags, int device, rta_model** out) {
   if (!spec || !params || !matrices || !basis || !out) {
     rta::g_model_error = "rta_model_open: null argument";
     return RTA_E_ARG;
@@ -905,13 +1093,21 @@ rta_status rta_model_open_batch(const rta_model_spec* spec, const uint32_t* para
   auto* m = new (std::nothrow) rta_model;
   if (!m) return RTA_E_CUDA;
   try {
-    m->engine.load(*spec, params, n_params, matrices, matrix_bytes, basis, basis_bytes, capacity, sequences, device);
+    m->engine.load(*spec, params, n_params, matrices, matrix_bytes, basis, basis_bytes, capacity, sequences, flags,
+                   device);
   } catch (const rta::Failure& f) {
     delete m;
     return rta::fail_model(f);
   }
   *out = m;
   return RTA_OK;
+}
+
+rta_status rta_model_open_batch(const rta_model_spec* spec, const uint32_t* params, size_t n_params,
+                                const void* matrices, size_t matrix_bytes, const void* basis, size_t basis_bytes,
+                                uint32_t capacity, uint32_t sequences, int device, rta_model** out) {
+  return rta_model_open_ex(spec, params, n_params, matrices, matrix_bytes, basis, basis_bytes, capacity, sequences, 0u,
+                           device, out);
 }
 
 rta_status rta_model_open(const rta_model_spec* spec, const uint32_t* params, size_t n_params, const void* matrices,
@@ -923,6 +1119,12 @@ rta_status rta_model_open(const rta_model_spec* spec, const uint32_t* params, si
 
 rta_status rta_model_open_files(const rta_model_spec* spec, const char* optical_model_bin, const char* geometry_bin,
                                 const char* vocabulary_bin, uint32_t capacity, int device, rta_model** out) {
+  return rta_model_open_files_ex(spec, optical_model_bin, geometry_bin, vocabulary_bin, capacity, 1u, 0u, device, out);
+}
+
+rta_status rta_model_open_files_ex(const rta_model_spec* spec, const char* optical_model_bin,
+                                   const char* geometry_bin, const char* vocabulary_bin, uint32_t capacity,
+                                   uint32_t sequences, uint32_t flags, int device, rta_model** out) {
   if (!spec || !optical_model_bin || !geometry_bin || !vocabulary_bin || !out) {
     rta::g_model_error = "rta_model_open_files: null argument";
     return RTA_E_ARG;
@@ -957,8 +1159,9 @@ rta_status rta_model_open_files(const rta_model_spec* spec, const char* optical_
     rta::g_model_error = "vocabulary.bin header does not match the model spec";
     return RTA_E_ASSET;
   }
-  return rta_model_open(spec, reinterpret_cast<const uint32_t*>(model.data() + 44), hdr[6], geo.data(),
-                        static_cast<size_t>(hdr[7]) * 4, voc.data() + 16, voc.size() - 16, capacity, device, out);
+  return rta_model_open_ex(spec, reinterpret_cast<const uint32_t*>(model.data() + 44), hdr[6], geo.data(),
+                           static_cast<size_t>(hdr[7]) * 4, voc.data() + 16, voc.size() - 16, capacity, sequences,
+                           flags, device, out);
 }
 
 void rta_model_close(rta_model* m) { delete m; }
@@ -1023,6 +1226,34 @@ rta_status rta_model_generate_batch(rta_model* m, uint32_t count, uint32_t* ids,
   return RTA_OK;
 }
 
+rta_status rta_model_attention(rta_model* m, uint32_t layer, const float* q, const float* k, const float* v,
+                               const float* gate, uint32_t rows, uint32_t count, uint32_t query_start,
+                               uint32_t history_start, uint32_t block, float* out, float* phys, uint8_t* packets,
+                               uint32_t* receipts, uint32_t* n_records, double* gpu_ms) {
+  if (!m || !q || !k || !v || !gate || !out || !phys || !packets || !receipts) return RTA_E_ARG;
+  try {
+    cudaSetDevice(m->engine.device);
+    m->engine.attention_check(layer, q, k, v, gate, rows, count, query_start, history_start, block, out, phys,
+                              packets, receipts, n_records, gpu_ms);
+  } catch (const rta::Failure& f) {
+    return rta::fail_model(f);
+  }
+  return RTA_OK;
+}
+
+rta_status rta_model_debug_attention(rta_model* m, uint32_t seq, float* q, float* gate, float* att,
+                                     uint8_t* packets, uint32_t* n_positions) {
+  if (!m || !q || !gate || !att || !packets) return RTA_E_ARG;
+  try {
+    cudaSetDevice(m->engine.device);
+    const uint32_t n = m->engine.debug_attention(seq, q, gate, att, packets);
+    if (n_positions) *n_positions = n;
+  } catch (const rta::Failure& f) {
+    return rta::fail_model(f);
+  }
+  return RTA_OK;
+}
+
 rta_status rta_model_mlp(rta_model* m, uint32_t layer, const float* x, uint32_t rows, float* y, float* act) {
   if (!m || !x || !y || !act) return RTA_E_ARG;
   try {
@@ -1068,7 +1299,7 @@ rta_status rta_model_resources(rta_model* m, uint64_t* out, size_t n) {
   const uint64_t v[] = {
       e.payload_bytes,
       layer_bytes,
-      e.kcache.n * 2ull + e.vcache.n * 2ull,
+      e.packet_history ? e.pring.n : e.kcache.n * 2ull + e.vcache.n * 2ull,
       e.rec.n * 4ull + e.conv.n * 4ull,
       e.capacity,
       e.nsplit,

@@ -2,6 +2,7 @@
 // the GEMVs: token readout->embedding control, QK-norm + RoPE + history append
 // for full-attention layers, and the fused recurrent (gated delta rule) layer.
 #include "layers.h"
+#include "packets.cuh"
 #include "rta_internal.h"
 
 namespace rta {
@@ -145,6 +146,15 @@ __global__ void __launch_bounds__(256) attn_prep_kernel(PrepParams p) {
     sincosf(phase, &sn, &cs);
     const float a = xs[d & ~1u], b = xs[d | 1u];
     x = (d & 1u) ? a * sn + b * cs : a * cs - b * sn;
+  }
+  if (p.packets && !is_q) {  // op 34: pack this KV head's K (Q4_K) and V (Q6_K) into the position's packet
+    __shared__ PackScratch sh;
+    const size_t row = static_cast<size_t>(z) * p.capacity + pos % p.capacity;
+    uint8_t* pkt = p.packets + row * packet_bytes(p.kvh);
+    pack_q4k_block(x, pkt + head * kPacketKeyBytes, sh);
+    pack_q6k_block(qkvg[p.q_width + p.kv_width + head * hd + d],
+                   pkt + p.kvh * kPacketKeyBytes + head * kPacketValueBytes, sh);
+    return;
   }
   if (d >= hd) return;
   if (is_q) {
@@ -370,7 +380,7 @@ cudaError_t launch_embed(const EmbedParams& p, cudaStream_t s, bool pdl) {
   return launch_pdl(reinterpret_cast<const void*>(embed_kernel), dim3(p.nseq), dim3(256), args, s, pdl);
 }
 cudaError_t launch_attn_prep(const PrepParams& p, cudaStream_t s, bool pdl) {
-  if (p.hd > 256) return cudaErrorInvalidValue;
+  if (p.hd > 256 || (p.packets && p.hd != 256)) return cudaErrorInvalidValue;  // a packet block is 256 values
   void* args[] = {const_cast<PrepParams*>(&p)};
   return launch_pdl(reinterpret_cast<const void*>(attn_prep_kernel), dim3(p.heads + p.kvh, p.nseq), dim3(256), args, s,
                     pdl);

@@ -52,6 +52,9 @@ struct PrepParams {
   const uint32_t* running = nullptr;  // likewise
   uint32_t nseq = 1, ctrl_step = 0;
   size_t qkvg_seq = 0;                // floats between sequences' projections
+  // non-null: append the reference's history packet (kvh Q4_K keys + kvh Q6_K
+  // values, packet_bytes(kvh) per position) to this ring instead of fp16 K/V
+  uint8_t* packets = nullptr;         // this layer: [nseq][capacity][packet]
 };
 
 struct GdnParams {

@@ -9,6 +9,7 @@
 // (d*sc)*q - dmin*m and (d*scale)*(q6-32).
 #include <algorithm>
 
+#include "packets.cuh"
 #include "rta_internal.h"
 
 namespace rta {
@@ -98,14 +99,6 @@ __device__ void quant_q6k_block(const float* v, uint8_t* out) {
   for (int i = 0; i < 210; ++i) out[i] = blk[i];
 }
 
-__global__ void quantize_kernel(int fmt, const float* __restrict__ src, size_t nblocks, uint8_t* __restrict__ dst) {
-  const size_t b = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (b >= nblocks) return;
-  float v[256];
-  for (int i = 0; i < 256; ++i) v[i] = src[b * 256 + i];
-  if (fmt == kQ4K) quant_q4k_block(v, dst + b * kQ4KBytes);
-  else quant_q6k_block(v, dst + b * kQ6KBytes);
-}
 
 // Counter-based N(0, sigma) source for synthetic weights: splitmix64 of
 // (seed, element index) -> two uniforms -> Box-Muller.
@@ -179,9 +172,64 @@ __global__ void dequantize_kernel(int fmt, const uint8_t* __restrict__ src, size
   dst[i] = fmt == kQ4K ? q4k_value(src + blk * kQ4KBytes, j) : q6k_value(src + blk * kQ6KBytes, j);
 }
 
+// One 256-thread CTA per block (the packet quantizer of packets.cuh, also used
+// by the decode step to pack history); grid-stride over blocks.
+__global__ void __launch_bounds__(256) quantize_cta_kernel(int fmt, const float* __restrict__ src, size_t nblocks,
+                                                           uint8_t* __restrict__ dst) {
+  __shared__ PackScratch sh;
+  for (size_t b = blockIdx.x; b < nblocks; b += gridDim.x) {
+    const float x = src[b * 256 + threadIdx.x];
+    if (fmt == kQ4K) pack_q4k_block(x, dst + b * kQ4KBytes, sh);
+    else pack_q6k_block(x, dst + b * kQ6KBytes, sh);
+  }
+}
+
+// History packets of `rows` positions from fp32 K and V rows [row][kvh][256]:
+// CTA (row, j) packs key head j (j < kvh) or value head j - kvh.
+__global__ void __launch_bounds__(256) pack_history_kernel(const float* __restrict__ k, const float* __restrict__ v,
+                                                           uint32_t kvh, uint8_t* __restrict__ dst) {
+  __shared__ PackScratch sh;
+  const uint32_t row = blockIdx.x, j = blockIdx.y;
+  uint8_t* pkt = dst + static_cast<size_t>(row) * packet_bytes(kvh);
+  if (j < kvh) pack_q4k_block(k[(static_cast<size_t>(row) * kvh + j) * 256 + threadIdx.x], pkt + j * kPacketKeyBytes, sh);
+  else
+    pack_q6k_block(v[(static_cast<size_t>(row) * kvh + (j - kvh)) * 256 + threadIdx.x],
+                   pkt + kvh * kPacketKeyBytes + (j - kvh) * kPacketValueBytes, sh);
+}
+
+// Seeded history packets (throughput runs): values N(0, 1) per block, packed.
+__global__ void __launch_bounds__(256) random_packets_kernel(uint64_t seed, size_t rows, uint32_t kvh,
+                                                             uint8_t* __restrict__ dst) {
+  __shared__ PackScratch sh;
+  const size_t blocks = rows * 2u * kvh;
+  for (size_t b = blockIdx.x; b < blocks; b += gridDim.x) {
+    const size_t row = b / (2u * kvh);
+    const uint32_t j = static_cast<uint32_t>(b % (2u * kvh));
+    const float x = synthetic_normal(seed, b * 256 + threadIdx.x);
+    uint8_t* pkt = dst + row * packet_bytes(kvh);
+    if (j < kvh) pack_q4k_block(x, pkt + j * kPacketKeyBytes, sh);
+    else pack_q6k_block(x, pkt + kvh * kPacketKeyBytes + (j - kvh) * kPacketValueBytes, sh);
+  }
+}
+
+cudaError_t launch_pack_history(const float* k, const float* v, uint32_t rows, uint32_t kvh, uint8_t* dst,
+                                cudaStream_t s) {
+  if (rows == 0) return cudaSuccess;
+  if (!k || !v || !dst || kvh == 0) return cudaErrorInvalidValue;
+  pack_history_kernel<<<dim3(rows, 2 * kvh), 256, 0, s>>>(k, v, kvh, dst);
+  return cudaGetLastError();
+}
+cudaError_t launch_random_packets(uint64_t seed, size_t rows, uint32_t kvh, uint8_t* dst, cudaStream_t s) {
+  if (rows == 0) return cudaSuccess;
+  const size_t grid = std::min<size_t>(rows * 2u * kvh, 148u * 16u);
+  random_packets_kernel<<<static_cast<unsigned>(grid), 256, 0, s>>>(seed, rows, kvh, dst);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_quantize(int fmt, const float* src, size_t nblocks, uint8_t* dst, cudaStream_t s) {
   if (nblocks == 0) return cudaSuccess;
-  quantize_kernel<<<static_cast<unsigned>((nblocks + 127) / 128), 128, 0, s>>>(fmt, src, nblocks, dst);
+  const size_t grid = std::min<size_t>(nblocks, 148u * 16u);
+  quantize_cta_kernel<<<static_cast<unsigned>(grid), 256, 0, s>>>(fmt, src, nblocks, dst);
   return cudaGetLastError();
 }
 cudaError_t launch_random_quantize(int fmt, uint64_t seed, float sigma, uint64_t first_block, size_t nblocks,

@@ -31,6 +31,11 @@ cudaError_t launch_random_quantize(int fmt, uint64_t seed, float sigma, uint64_t
 cudaError_t launch_random_normal(uint64_t seed, float sigma, float mean, size_t n, float* dst, cudaStream_t s);
 cudaError_t launch_random_normal_half(uint64_t seed, float sigma, size_t n, __half* dst, cudaStream_t s);
 cudaError_t launch_dequantize(int fmt, const uint8_t* src, size_t nblocks, float* dst, cudaStream_t s);
+// History packets (kvh Q4_K keys + kvh Q6_K values per position) from fp32
+// K / V rows [rows][kvh][256], and seeded random packets for throughput runs.
+cudaError_t launch_pack_history(const float* k, const float* v, uint32_t rows, uint32_t kvh, uint8_t* dst,
+                                cudaStream_t s);
+cudaError_t launch_random_packets(uint64_t seed, size_t rows, uint32_t kvh, uint8_t* dst, cudaStream_t s);
 
 // ----------------------------------------------------------------- gemv.cu
 // Activation prologue applied (per CTA) before the int16 activation split.

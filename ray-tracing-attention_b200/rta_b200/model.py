@@ -36,6 +36,11 @@ _SIGS = {
     "rta_model_open": (_I, [ctypes.POINTER(ModelSpecC), _P, _SZ, _P, _SZ, _P, _SZ, _U32, _I, ctypes.POINTER(_P)]),
     "rta_model_open_batch": (_I, [ctypes.POINTER(ModelSpecC), _P, _SZ, _P, _SZ, _P, _SZ, _U32, _U32, _I,
                                   ctypes.POINTER(_P)]),
+    "rta_model_open_ex": (_I, [ctypes.POINTER(ModelSpecC), _P, _SZ, _P, _SZ, _P, _SZ, _U32, _U32, _U32, _I,
+                               ctypes.POINTER(_P)]),
+    "rta_model_attention": (_I, [_P, _U32, _P, _P, _P, _P, _U32, _U32, _U32, _U32, _U32, _P, _P, _P, _P,
+                                 ctypes.POINTER(_U32), ctypes.POINTER(ctypes.c_double)]),
+    "rta_model_debug_attention": (_I, [_P, _U32, _P, _P, _P, _P, ctypes.POINTER(_U32)]),
     "rta_model_prefill_batch": (_I, [_P, _P, _P, _U32, _P, ctypes.POINTER(ctypes.c_double)]),
     "rta_model_seed_history": (_I, [_P, _P, ctypes.c_uint64]),
     "rta_model_generate_batch": (_I, [_P, _U32, _P, _P, ctypes.POINTER(ctypes.c_double)]),
@@ -49,6 +54,7 @@ _SIGS = {
     "rta_model_state": (_I, [_P, _P, ctypes.POINTER(_U32)]),
     "rta_model_resources": (_I, [_P, _P, _SZ]),
 }
+PACKET_HISTORY = 1  # RTA_MODEL_PACKET_HISTORY
 RESOURCE_NAMES = ("payload_bytes", "derived_layer_bytes", "history_bytes", "recurrent_state_bytes", "capacity",
                   "attention_splits", "kernels_per_decode_step", "kernels_per_prefill_step", "position",
                   "sequences")
@@ -89,7 +95,8 @@ class ResidentModel:
     # ---------------------------------------------------------------- open
     @classmethod
     def from_payloads(cls, spec: assets.Spec, params, matrices, basis, capacity: int, device: int = 0,
-                      sequences: int = 1):
+                      sequences: int = 1, history: str = "fp16"):
+        """history: "fp16" K/V rings, or "packet" (the reference's Q4_K/Q6_K history packets)."""
         """params: uint32 numpy; matrices/basis: uint8 numpy (host) or torch CUDA tensors (device)."""
         lib = _lib_model()
         params = np.ascontiguousarray(params, np.uint32)
@@ -103,10 +110,15 @@ class ResidentModel:
         bp, bb, bkeep = addr(basis)
         cs = ModelSpecC.from_spec(spec)
         h = ctypes.c_void_p()
-        _check(lib.rta_model_open_batch(ctypes.byref(cs), _np_ptr(params), params.size, mp, mb, bp, bb, capacity,
-                                        sequences, device, ctypes.byref(h)))
+        if history not in ("fp16", "packet"):
+            raise ValueError("history must be 'fp16' or 'packet'")
+        flags = PACKET_HISTORY if history == "packet" else 0
+        _check(lib.rta_model_open_ex(ctypes.byref(cs), _np_ptr(params), params.size, mp, mb, bp, bb, capacity,
+                                     sequences, flags, device, ctypes.byref(h)))
         del mkeep, bkeep
-        return cls(h, spec, capacity, device, sequences)
+        model = cls(h, spec, capacity, device, sequences)
+        model.history = history
+        return model
 
     @classmethod
     def from_directory(cls, directory, capacity: int, device: int = 0):
@@ -124,13 +136,13 @@ class ResidentModel:
 
     @classmethod
     def synthetic(cls, spec: assets.Spec, seed: int = 0, capacity: int = 1024, device: int = 0,
-                  sequences: int = 1):
+                  sequences: int = 1, history: str = "fp16"):
         """Random-init model of `spec` generated on the GPU (payloads in the exporter's layout)."""
         import torch
         torch.cuda.set_device(device)
         layout = assets.plan(spec, seed)
         mats, basis = assets.generate_device(layout, seed)
-        model = cls.from_payloads(spec, layout.params(), mats, basis, capacity, device, sequences)
+        model = cls.from_payloads(spec, layout.params(), mats, basis, capacity, device, sequences, history)
         model.layout = layout
         del mats, basis
         torch.cuda.empty_cache()
@@ -202,6 +214,53 @@ class ResidentModel:
         _check(_lib_model().rta_model_generate_batch(self._h, count, _np_ptr(out), _np_ptr(n), ctypes.byref(ms)))
         self.last_gpu_ms = ms.value
         return [out[z, :n[z]].copy() for z in range(self.sequences)]
+
+    def attention(self, query, keys, values, gate=None, *, layer=None, query_start=None, history_start=0,
+                  block=128):
+        """Full-attention diagnostic (worker op 14): the detector of a full layer over a
+        supplied compact history; returns output, physical, history_packets and dense
+        receipts shaped like ResidentRuntime.attention's result."""
+        s = self.spec
+        H, KVH, hd = s.attention_heads, s.kv_heads, s.attention_head_dim
+        q = np.ascontiguousarray(query, np.float32).reshape(-1, H, hd)
+        k = np.ascontiguousarray(keys, np.float32).reshape(-1, KVH, hd)
+        v = np.ascontiguousarray(values, np.float32).reshape(-1, KVH, hd)
+        g = np.zeros_like(q) if gate is None else np.ascontiguousarray(gate, np.float32).reshape(q.shape)
+        if layer is None:
+            layer = s.full_layers[0]
+        if query_start is None:
+            query_start = history_start + len(k) - len(q)
+        rows, count = len(q), len(k)
+        vis = [min(query_start - history_start + r + 1, self.capacity) for r in range(rows)]
+        records = H * sum((n + block - 1) // block for n in vis)
+        stride = hd + 8 + block // 32
+        out = np.zeros((rows, H, hd), np.float32)
+        phys = np.zeros((rows, H, 2), np.float32)
+        pbytes = KVH * (144 + 210)
+        packets = np.zeros((count, pbytes), np.uint8)
+        receipts = np.zeros((records, stride), np.uint32)
+        n = ctypes.c_uint32(0)
+        ms = ctypes.c_double(0)
+        _check(_lib_model().rta_model_attention(self._h, layer, _np_ptr(q), _np_ptr(k), _np_ptr(v), _np_ptr(g), rows,
+                                                count, query_start, history_start, block, _np_ptr(out),
+                                                _np_ptr(phys), _np_ptr(packets), _np_ptr(receipts), ctypes.byref(n),
+                                                ctypes.byref(ms)))
+        assert n.value == records
+        return dict(output=out, physical=phys, history_packets=packets, receipts=receipts, block=block,
+                    stride=stride, query_start=query_start, history_start=history_start, gpu_ms=ms.value,
+                    legacy_available=history_start == 0)
+
+    def debug_attention(self, seq: int = 0):
+        """Test hook (packet history): q, gate, detector output of the last full layer of the
+        last step and that layer's visible history packets, oldest first."""
+        s = self.spec
+        Q = s.attention_heads * s.attention_head_dim
+        q, gate, att = (np.zeros(Q, np.float32) for _ in range(3))
+        packets = np.zeros((self.capacity, s.kv_heads * (144 + 210)), np.uint8)
+        n = ctypes.c_uint32(0)
+        _check(_lib_model().rta_model_debug_attention(self._h, seq, _np_ptr(q), _np_ptr(gate), _np_ptr(att),
+                                                      _np_ptr(packets), ctypes.byref(n)))
+        return q, gate, att, packets[:n.value].copy()
 
     def mlp(self, x, layer: int):
         x = np.ascontiguousarray(x, np.float32).reshape(-1, self.spec.hidden_size)

@@ -9,15 +9,17 @@
 // through librta_cuda.so (include/rta.h); this file only frames bytes.
 //
 // Served operations: 0 quit, 1 prefill, 2 generate, 4 vocabulary, 6 mlp,
-// 8 resources, 9 stream, 10 grow (capacity).  Operations tied to the ray-traced
-// caches and diagnostics (5 codec, 7 aperture, 11/12 checkpointed prefill,
-// 13 finish_history, 14 attention receipts, 15 statistics) answer status 1, which
-// the runtime turns into RuntimeError.
+// 8 resources, 9 stream, 10 grow (capacity), 14 full-attention diagnostic
+// (dense receipts).  The attention history is kept in the reference's packet
+// format.  Operations tied to the ray-traced caches and statistics (5 codec,
+// 7 aperture, 11/12 checkpointed prefill, 13 finish_history, 15 statistics)
+// answer status 1, which the runtime turns into RuntimeError.
 #include <algorithm>
 #include <chrono>
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <fstream>
 #include <iostream>
@@ -122,13 +124,15 @@ struct Worker {
   std::string model_bin, geometry_bin, vocab_bin;
   uint32_t capacity = 300, position = 0;
   uint32_t stops[2] = {0xffffffffu, 0xffffffffu};
+  uint32_t block = 128;  // RT_ATTENTION_BLOCK: receipt group size (128, 256 or 512)
 
   void check(rta_status st) {
     if (st != RTA_OK) throw std::runtime_error(rta_model_last_error());
   }
   void open() {
-    check(rta_model_open_files(&spec, model_bin.c_str(), geometry_bin.c_str(), vocab_bin.c_str(), capacity, 0,
-                               &model));
+    // the reference's history format: Q4_K key / Q6_K value packets
+    check(rta_model_open_files_ex(&spec, model_bin.c_str(), geometry_bin.c_str(), vocab_bin.c_str(), capacity, 1u,
+                                  RTA_MODEL_PACKET_HISTORY, 0, &model));
   }
 
   // op 1: ids[count] + stops[2] -> 6 doubles + 8 control words (+ batch statistics)
@@ -239,6 +243,48 @@ struct Worker {
     reply(0, out);
   }
 
+  // op 14 (attentionCheck, resident_attention_runtime.inl:646-753): rows of rotated
+  // q + compact K/V history + gate -> outputs, physical, history packets, receipts
+  void attention(uint32_t rows, uint32_t layer) {
+    uint32_t hdr[4];
+    if (!std::cin.read(reinterpret_cast<char*>(hdr), sizeof hdr)) throw std::runtime_error("Incomplete attention header");
+    const uint32_t count = hdr[0], query_start = hdr[1], history_start = hdr[2];
+    const uint32_t H = spec.attention_heads, KVH = spec.kv_heads, hd = spec.attention_head_dim;
+    if (!rows || rows > 32 || !count || hdr[3] || layer >= spec.depth || spec.layer_kinds[layer] != 1)
+      throw std::runtime_error("Invalid full-attention diagnostic shape or causal domain");
+    std::vector<float> q, k, v, gate;
+    input(q, static_cast<size_t>(rows) * H * hd);
+    input(k, static_cast<size_t>(count) * KVH * hd);
+    input(v, static_cast<size_t>(count) * KVH * hd);
+    input(gate, static_cast<size_t>(rows) * H * hd);
+    uint32_t records = 0;
+    for (uint32_t r = 0; r < rows; ++r)
+      records += H * ((std::min(query_start - history_start + r + 1u, capacity) + block - 1u) / block);
+    const uint32_t stride = hd + 8u + block / 32u, pbytes = KVH * (144u + 210u);
+    std::vector<float> out(q.size()), phys(static_cast<size_t>(rows) * H * 2);
+    std::vector<uint8_t> packets(static_cast<size_t>(count) * pbytes);
+    std::vector<uint32_t> receipts(static_cast<size_t>(records) * stride);
+    uint32_t n = 0;
+    double gpu = 0.0;
+    const auto t0 = Clock::now();
+    check(rta_model_attention(model, layer, q.data(), k.data(), v.data(), gate.data(), rows, count, query_start,
+                              history_start, block, out.data(), phys.data(), packets.data(), receipts.data(), &n,
+                              &gpu));
+    const double wall = std::chrono::duration<double, std::milli>(Clock::now() - t0).count();
+    if (n != records) throw std::runtime_error("Full-attention diagnostic record count mismatch");
+    const uint32_t legacy = history_start == 0u ? 1u : 0u;
+    std::vector<char> o;
+    append<uint32_t>(o, {0x41545231u, rows, count, H, KVH, hd, pbytes, block, stride, records, legacy, 0u});
+    append<double>(o, {gpu, 0.0, 0.0, wall});
+    append(o, out.data(), out.size());
+    append(o, phys.data(), phys.size());
+    append(o, out.data(), out.size());    // legacy output: this backend has one detector
+    append(o, phys.data(), phys.size());
+    append(o, packets.data(), packets.size());
+    append(o, receipts.data(), receipts.size());
+    reply(0, o);
+  }
+
   // op 8: the 61 counters resident_runtime.resources() names, in its order
   void resources() {
     uint64_t r[9] = {0};
@@ -249,7 +295,7 @@ struct Worker {
     v[13] = r[2];                       // history bytes
     v[15] = r[3];                       // recurrent field bytes
     v[26] = 32;                         // workspace rows (MLP check rows)
-    v[38] = 256;                        // attention block
+    v[38] = block;                      // attention block
     std::vector<char> out;
     append(out, v.data(), v.size());
     reply(0, out);
@@ -286,6 +332,11 @@ int main(int argc, char** argv) {
     w.geometry_bin = (dir.empty() ? std::string(".") : dir) + "/geometry_weights.bin";
     w.capacity = argc > 3 ? static_cast<uint32_t>(std::stoul(argv[3])) : 300u;
     w.spec = read_spec(dir.empty() ? "." : dir);
+    if (const char* b = std::getenv("RT_ATTENTION_BLOCK")) {
+      w.block = static_cast<uint32_t>(std::strtoul(b, nullptr, 10));
+      if (w.block != 128 && w.block != 256 && w.block != 512)
+        throw std::runtime_error("RT_ATTENTION_BLOCK must be 128, 256 or 512");
+    }
     w.open();
     // hello: magic, depth, blocks (= depth, header word 2), middle, mode =
     // quantization 4 | standard MLP 4096 | ordered detector 131072
@@ -311,6 +362,7 @@ int main(int argc, char** argv) {
         else if (op == 6) w.mlp(count, debug);
         else if (op == 8) w.resources();
         else if (op == 10) w.grow(count);
+        else if (op == 14) w.attention(count, debug);
         else throw std::runtime_error("Operation " + std::to_string(op) + " is not served by the B200 backend");
       } catch (const std::exception& e) {
         std::cerr << e.what() << std::endl;
