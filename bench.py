@@ -232,24 +232,29 @@ class MLPWorkload(Workload):
 
 
 class LMHeadWorkload(Workload):
+    """LM head 151936 x 2048 Q6_K, logits + per-row argmax, batch 1 or 64."""
     name, metric, unit, dtype, dominant = ("lmhead", "vocabulary readout tokens/s (151936x2048 Q6_K, logits+argmax)",
                                            "tokens/s", "q6k-int8mma-f32acc", "gemv_tiled_kernel<Q6_K> readout + argmax")
     V, D = 151936, 2048
-    launches_per_step = 2
-    # dram read + write of one readout launch with logits, from one ncu capture
-    # (profiles/gemv_tiled_q6k_readout_151936x2048.md)
+    # dram read + write of one batch-1 readout launch with logits, from one ncu
+    # capture (profiles/gemv_tiled_q6k_readout_151936x2048.md)
     traffic = 255.36e6 + 3.69e6
 
-    def __init__(self, seed=31):
+    def __init__(self, seed=31, batch=1):
         import torch
         from rta_b200 import ops
         self.ops, self.torch = ops, torch
+        self.B = batch
+        self.launches_per_step = 2 + (batch + 15) // 16  # memset, readout launches of <= 16 rows, finish
+        if batch != 1:
+            self.traffic = None
+            self.dominant = f"gemv_tiled_kernel<Q6_K> readout + argmax, {batch} rows (launches of <= 16 rows)"
         self.fmt, self.w = ops.tile_weights(14, ops.synthetic_blocks(14, self.V, self.D, seed), self.V, self.D)
-        self.x = ops.synthetic_normal(self.D, seed + 1)
+        self.x = ops.synthetic_normal(batch * self.D, seed + 1).reshape(batch, self.D)
         self.ws = torch.empty(4096, dtype=torch.uint8, device="cuda")
-        self.hx = torch.empty(self.D, dtype=torch.float32).pin_memory()
-        self.hx.copy_(self.x.cpu())
-        self.harg = torch.empty(1, dtype=torch.int32).pin_memory()
+        self.hx = torch.empty(batch * self.D, dtype=torch.float32).pin_memory()
+        self.hx.copy_(self.x.reshape(-1).cpu())
+        self.harg = torch.empty(batch, dtype=torch.int32).pin_memory()
 
     def step(self, i):
         self.last = self.ops.readout(self.fmt, self.w, self.V, self.D, self.x, logits=True, workspace=self.ws)
@@ -257,38 +262,40 @@ class LMHeadWorkload(Workload):
     dominant_launch = step
 
     def dominant_bytes(self):
-        return self.V * self.D // 256 * 210 + self.D * 4 + self.V * 4
+        return self.V * self.D // 256 * 210 + self.B * (self.D * 4 + self.V * 4)
 
     def units_per_step(self):
-        return 1.0
+        return float(self.B)
 
     def e2e_step(self, i):
-        self.x.copy_(self.hx, non_blocking=True)
+        self.x.view(-1).copy_(self.hx, non_blocking=True)
         self.step(i)
-        self.harg.copy_(self.last[1], non_blocking=True)
+        self.harg.copy_(self.last[1].view(-1), non_blocking=True)
 
     def e2e_bytes(self):
-        return self.D * 4, 4
+        return self.B * self.D * 4, self.B * 4
 
     def algorithmic_bytes_step(self):
         return self.dominant_bytes()
 
     def config(self):
-        return {"workload": "config3_lmhead_b1", "vocab": self.V, "hidden": self.D, "format": "Q6_K",
-                "layout": "tiled (rta_tile_weights, once before timing)", "batch": 1, "l2": "weights 255 MB > L2"}
+        return {"workload": f"config3_lmhead_b{self.B}", "vocab": self.V, "hidden": self.D, "format": "Q6_K",
+                "layout": "tiled (rta_tile_weights, once before timing)", "batch": self.B,
+                "l2": "weights 255 MB > L2"}
 
     def cpu_baseline(self, budget_s):
         from oracle import oracle
         rng = np.random.default_rng(0)
         W = oracle.quantize(14, rng.normal(0, 0.02, self.V * self.D).astype(np.float32))
-        x = rng.normal(0, 1, (1, self.D)).astype(np.float32)
+        x = rng.normal(0, 1, (self.B, self.D)).astype(np.float32)
         n, t0 = 0, time.perf_counter()
         while time.perf_counter() - t0 < budget_s or n == 0:
             oracle.lmhead(14, W, self.V, self.D, x, want_logits=True)
             n += 1
         dt = time.perf_counter() - t0
-        return {"value": n / dt, "unit": self.unit, "cores": oracle.threads(), "kind": "port",
-                "sample": f"{n} full readouts (C restatement of resident_math.comp ops 16/17/23, OpenMP)"}
+        return {"value": n * self.B / dt, "unit": self.unit, "cores": oracle.threads(), "kind": "port",
+                "sample": f"{n} full readouts of {self.B} rows (C restatement of resident_math.comp ops 16/17/23, "
+                          "OpenMP)"}
 
 
 class AttentionWorkload(Workload):
@@ -688,7 +695,9 @@ def time_steps(fn, steps, warmup, world, graph=True, min_seconds=0.0):
 
 def run_ours(args, world, rank, local):
     import torch
-    wl = WORKLOADS[args.workload](**({"history": args.history} if args.workload == "attention" else {}))
+    kw = {"history": args.history} if args.workload == "attention" else \
+        {"batch": args.batch} if args.workload == "lmhead" else {}
+    wl = WORKLOADS[args.workload](**kw)
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
         ms = time_steps(wl.step, args.steps, args.warmup, world, min_seconds=args.min_seconds)
@@ -742,6 +751,8 @@ def run_reference(args, world, rank):
         wl.L = args.history
     if args.workload == "decode2b":
         wl.seed = 20261201
+    if args.workload == "lmhead":
+        wl.B = args.batch
     budget = max(1.0, args.cpu_budget / max(args.steps, 1))
     vals = []
     for _ in range(args.warmup + args.steps):
@@ -749,7 +760,7 @@ def run_reference(args, world, rank):
     vals = vals[args.warmup:]
     v = float(np.median([b["value"] for b in vals]))
     base = dict(vals[-1], value=v)
-    cfg = {"mlp": {"workload": "config1_swiglu_mlp_b1"}, "lmhead": {"workload": "config3_lmhead_b1"},
+    cfg = {"mlp": {"workload": "config1_swiglu_mlp_b1"}, "lmhead": {"workload": f"config3_lmhead_b{args.batch}"},
            "attention": {"workload": f"config2_gqa_decode_L{args.history}"},
            "decode2b": {"workload": "config4_2b_hybrid_decode_b1"}}[args.workload]
     return {"impl": "reference", "metric": cls.metric, "value": v, "unit": cls.unit, "n_gpus": world,
@@ -803,6 +814,7 @@ def main():
     ap.add_argument("--min-seconds", type=float, default=1.0,
                     help="repeat the timed K-step region for at least this long (clock sampling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=1, help="lmhead: hidden rows per readout (config 3: 1 or 64)")
     ap.add_argument("--prompt", type=int, default=512,
                     help="decode2b: prompt length before the timed tokens (short prompts keep profiler runs small)")
     args = ap.parse_args()

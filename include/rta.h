@@ -107,7 +107,7 @@ RTA_API rta_status rta_mlp_swiglu(int format, const void* w_gate, const void* w_
                           void* stream);
 
 /* Vocabulary readout: logits[b][w] = sum_c W[w][c] x[b][c] and the argmax per
- * row (ties -> lowest id).  1 <= batch <= 8.  logits and best may be NULL.
+ * row (ties -> lowest id).  1 <= batch <= 64.  logits and best may be NULL.
  * workspace: rta_readout_workspace_bytes(batch) bytes.  Replaces ops 16/17/23
  * (ray_tracing/native/shaders/resident_math.comp:117-130). */
 RTA_API size_t rta_readout_workspace_bytes(uint32_t batch);

@@ -172,8 +172,8 @@ size_t rta_readout_workspace_bytes(uint32_t batch) { return kErrBytes + 8ull * (
 rta_status rta_readout(int format, const void* w, uint32_t vocab, uint32_t hidden, const float* x, uint32_t batch,
                        float* logits, uint32_t* argmax, float* best, void* workspace, void* stream) {
   if (!gemv_format(format) || !w || !x || !argmax || !workspace || vocab == 0 || vocab % 16 || hidden % 256 ||
-      hidden == 0 || batch == 0 || batch > 8)
-    return fail(RTA_E_ARG, "rta_readout: bad arguments (vocab % 16 == 0, hidden % 256 == 0, 1 <= batch <= 8)");
+      hidden == 0 || batch == 0 || batch > 64)
+    return fail(RTA_E_ARG, "rta_readout: bad arguments (vocab % 16 == 0, hidden % 256 == 0, 1 <= batch <= 64)");
   cudaStream_t s = as_stream(stream);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   uint32_t* err = reinterpret_cast<uint32_t*>(ws);
@@ -195,7 +195,7 @@ rta_status rta_readout(int format, const void* w, uint32_t vocab, uint32_t hidde
   a.err = err;
   st = cuda_status(rta::launch_gemv(a, s), "rta_readout");
   if (st != RTA_OK) return st;
-  readout_finish_kernel<<<1, 32, 0, s>>>(keys, batch, vocab, argmax, best, err);
+  readout_finish_kernel<<<1, (batch + 31u) / 32u * 32u, 0, s>>>(keys, batch, vocab, argmax, best, err);
   return cuda_status(cudaGetLastError(), "rta_readout(finish)");
 }
 

@@ -717,8 +717,141 @@ __device__ __forceinline__ void load_xterms(XTerms<FMT>& x, const uint32_t* xq, 
 
 // NB: batch rows per launch (1, 2, 4, 8); every batch row runs the identical
 // batch-1 arithmetic, so a row's result does not depend on the batch size.
+// One 16-row x 256-column block for up to 4*NJ batch rows in the batch-column
+// layout.  B column g of column set j is batch row 4j + g/2 (H for even g, L for
+// odd); lane t receives rows g and g+8 of batch row 4j + t.  Per batch row the
+// float operations and their order equal the batch-1 layout's: a (row, group)
+// product enters slot group % 4 with coefficient fmul(fmul(d, sc), xs), groups in
+// increasing order, then (Q4_K) the slot's dmin * m offset.
+template <int FMT, int NJ>
+__device__ __forceinline__ void column_block(const uint8_t* tb, const uint4 (&pl)[TileFmt<FMT>::kPlanes],
+                                             const uint32_t* xq, const float4* xsc, uint32_t G, uint32_t xg0,
+                                             uint32_t nbatch, uint32_t g, uint32_t t, float (&cacc)[NJ][2][4]) {
+  const uint32_t hl = g & 1u, bsel = g >> 1;
+  if constexpr (FMT == kQ4K) {
+    uint4 hdr[2];
+    float d[2], dmin[2];
+#pragma unroll
+    for (uint32_t hr = 0; hr < 2u; ++hr) {
+      hdr[hr] = *reinterpret_cast<const uint4*>(tb + TileFmt<FMT>::kScaleAt + (g + 8u * hr) * 16u);
+      d[hr] = half_bits_to_float(hdr[hr].x & 0xffffu);
+      dmin[hr] = half_bits_to_float(hdr[hr].x >> 16);
+    }
+    float dmm[8][2];
+#pragma unroll
+    for (uint32_t grp = 0; grp < 8u; ++grp) {
+      float dsc[2];
+#pragma unroll
+      for (uint32_t hr = 0; hr < 2u; ++hr) {
+        const uint4 h = hdr[hr];
+        uint32_t sc, mn;
+        if (grp < 4u) {
+          sc = (h.y >> (8u * grp)) & 63u;
+          mn = (h.z >> (8u * grp)) & 63u;
+        } else {
+          const uint32_t u = grp - 4u, e = (h.w >> (8u * u)) & 0xffu;
+          sc = (e & 15u) | (((h.y >> (8u * u + 6u)) & 3u) << 4);
+          mn = (e >> 4) | (((h.z >> (8u * u + 6u)) & 3u) << 4);
+        }
+        dsc[hr] = __fmul_rn(d[hr], static_cast<float>(sc));
+        dmm[grp][hr] = __fmul_rn(dmin[hr], static_cast<float>(mn));
+      }
+      const uint4 w = pl[grp / 2u];
+      const uint32_t sh = 4u * (grp % 2u);
+      const uint32_t a0 = (w.x >> sh) & 0x0f0f0f0fu, a1 = (w.y >> sh) & 0x0f0f0f0fu;
+      const uint32_t a2 = (w.z >> sh) & 0x0f0f0f0fu, a3 = (w.w >> sh) & 0x0f0f0f0fu;
+      const uint32_t xg = xg0 + grp;
+#pragma unroll
+      for (int j = 0; j < NJ; ++j) {
+        if (4u * j >= nbatch) break;
+        const uint32_t bb = 4u * j + bsel, bm = 4u * j + t;
+        uint32_t b0 = 0u, b1 = 0u;
+        if (bb < nbatch) {
+          const uint32_t* xw = xq + (static_cast<size_t>(bb) * G + xg) * 16u;
+          b0 = xw[hl * 4u + t];
+          b1 = xw[8u + hl * 4u + t];
+        }
+        int c[4] = {0, 0, 0, 0};
+        mma_u8s8_k32(c, a0, a1, a2, a3, b0, b1);
+        const float xs = bm < nbatch ? xsc[static_cast<size_t>(bm) * G + xg].x : 0.f;
+        cacc[j][0][grp & 3u] =
+            fmaf(__fmul_rn(dsc[0], xs), static_cast<float>(c[0] * 256 + c[1]), cacc[j][0][grp & 3u]);
+        cacc[j][1][grp & 3u] =
+            fmaf(__fmul_rn(dsc[1], xs), static_cast<float>(c[2] * 256 + c[3]), cacc[j][1][grp & 3u]);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) {
+      const uint32_t bm = 4u * j + t;
+      if (4u * j >= nbatch) break;
+#pragma unroll
+      for (uint32_t q = 0; q < 4u; ++q) {
+        const float aux0 = bm < nbatch ? xsc[static_cast<size_t>(bm) * G + xg0 + q].w : 0.f;
+        const float aux1 = bm < nbatch ? xsc[static_cast<size_t>(bm) * G + xg0 + 4u + q].w : 0.f;
+#pragma unroll
+        for (uint32_t hr = 0; hr < 2u; ++hr)
+          cacc[j][hr][q] -= fmaf(dmm[4u + q][hr], aux1, __fmul_rn(dmm[q][hr], aux0));
+      }
+    }
+  } else {
+    const uint4 sc4[2] = {*reinterpret_cast<const uint4*>(tb + TileFmt<FMT>::kScaleAt + g * 16u),
+                          *reinterpret_cast<const uint4*>(tb + TileFmt<FMT>::kScaleAt + (g + 8u) * 16u)};
+    const uint16_t* dp = reinterpret_cast<const uint16_t*>(tb + TileFmt<FMT>::kDAt);
+    const float dr[2] = {half_bits_to_float(dp[g]), half_bits_to_float(dp[g + 8u])};
+    const uint32_t w[24] = {pl[0].x, pl[0].y, pl[0].z, pl[0].w, pl[1].x, pl[1].y, pl[1].z, pl[1].w,
+                            pl[2].x, pl[2].y, pl[2].z, pl[2].w, pl[3].x, pl[3].y, pl[3].z, pl[3].w,
+                            pl[4].x, pl[4].y, pl[4].z, pl[4].w, pl[5].x, pl[5].y, pl[5].z, pl[5].w};
+#pragma unroll
+    for (uint32_t jc = 0; jc < 8u; ++jc) {  // 32-coefficient chunk = groups 2jc, 2jc + 1
+      const uint32_t L0 = w[3u * jc], L1 = w[3u * jc + 1u], Hh = w[3u * jc + 2u];
+      const uint32_t a[4] = {(L0 & 0x0f0f0f0fu) | ((Hh << 4) & 0x30303030u),
+                             ((L0 >> 4) & 0x0f0f0f0fu) | ((Hh << 2) & 0x30303030u),
+                             (L1 & 0x0f0f0f0fu) | (Hh & 0x30303030u),
+                             ((L1 >> 4) & 0x0f0f0f0fu) | ((Hh >> 2) & 0x30303030u)};
+      const uint32_t xg = xg0 + jc;
+#pragma unroll
+      for (uint32_t h2 = 0; h2 < 2u; ++h2) {
+        const uint32_t grp = 2u * jc + h2;
+        float dsc[2];
+#pragma unroll
+        for (uint32_t hr = 0; hr < 2u; ++hr) {
+          const uint32_t word = grp / 4u == 0u ? sc4[hr].x : grp / 4u == 1u ? sc4[hr].y
+                                : grp / 4u == 2u ? sc4[hr].z : sc4[hr].w;
+          const int sc = static_cast<int8_t>((word >> (8u * (grp % 4u))) & 0xffu);
+          dsc[hr] = __fmul_rn(dr[hr], static_cast<float>(sc));
+        }
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) {
+          if (4u * j >= nbatch) break;
+          const uint32_t bb = 4u * j + bsel, bm = 4u * j + t;
+          const uint32_t b0 =
+              bb < nbatch ? xq[(static_cast<size_t>(bb) * G + xg) * 16u + h2 * 8u + hl * 4u + t] : 0u;
+          const float4 xv = bm < nbatch ? xsc[static_cast<size_t>(bm) * G + xg] : make_float4(0.f, 0.f, 0.f, 0.f);
+          // the L column starts at -32 * sum X of the 16-group (the batch-1 seed)
+          const int off = __float_as_int(h2 ? xv.z : xv.y);
+          int c[4] = {0, off, 0, off};
+          mma_u8s8_k16(c, a[2u * h2], a[2u * h2 + 1u], b0);
+          cacc[j][0][grp & 3u] =
+              fmaf(__fmul_rn(dsc[0], xv.x), static_cast<float>(c[0] * 256 + c[1]), cacc[j][0][grp & 3u]);
+          cacc[j][1][grp & 3u] =
+              fmaf(__fmul_rn(dsc[1], xv.x), static_cast<float>(c[2] * 256 + c[3]), cacc[j][1][grp & 3u]);
+        }
+      }
+    }
+  }
+}
+
+// NB <= 2: the lanes' MMA columns carry groups (four groups chained per
+// accumulator, the batch-1 layout).  NB >= 4: the columns carry four batch
+// rows each (H, L per row), NJ = NB / 4 column sets per MMA step, so one MMA
+// serves four rows; each lane keeps, per row, the four per-slot partial sums
+// (slot = group % 4) that the batch-1 layout keeps in its four lanes, and
+// combines them in the same order, so every row's bits equal the batch-1 result.
 template <int FMT, int NB>
-__global__ void __launch_bounds__(kThreads, 2) gemv_tiled_kernel(const Params p) {
+__global__ void __launch_bounds__(kThreads, NB >= 8 ? 1 : 2) gemv_tiled_kernel(const Params p) {
+  constexpr bool kCols = NB >= 4;
+  constexpr int NJ = kCols ? NB / 4 : 1;
+  constexpr int NR = kCols ? 1 : NB;
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr uint32_t kTile = TileFmt<FMT>::kBytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.off_bar);
@@ -787,9 +920,16 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_tiled_kernel(const Params p)
   if (hoist && static_cast<uint32_t>(warp) < p.kb_total)  // warps past the last block never read x
     load_xterms<FMT>(xh, xq, xsc, static_cast<uint32_t>(warp) * 8u, g, t);
 
-  float acc[NB][2], held[NB][2];
+  float acc[NR][2], held[NR][2];
 #pragma unroll
-  for (int b = 0; b < NB; ++b) acc[b][0] = acc[b][1] = held[b][0] = held[b][1] = 0.f;
+  for (int b = 0; b < NR; ++b) acc[b][0] = acc[b][1] = held[b][0] = held[b][1] = 0.f;
+  float cacc[NJ][2][4], cheld[NJ][2][4];  // batch columns: [column set][row g / g+8][slot]
+#pragma unroll
+  for (int j = 0; j < NJ; ++j)
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) cacc[j][hr][q] = cheld[j][hr][q] = 0.f;
 
   unsigned long long best = 0ull;  // epilogue thread's running argmax key
   bool aborted = false;
@@ -810,6 +950,9 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_tiled_kernel(const Params p)
 #pragma unroll
       for (uint32_t i = 0; i < TileFmt<FMT>::kPlanes; ++i)
         pl[i] = *reinterpret_cast<const uint4*>(tb + i * 512u + static_cast<uint32_t>(lane) * 16u);
+      if constexpr (kCols) {
+        column_block<FMT, NJ>(tb, pl, xq, xsc, G, xg0, nbatch, g, t, cacc);
+      } else {
       uint32_t a[8][4];  // A fragments of the 8 mma steps
       // per-chain scale factors of rows g and g+8 (before the activation scale)
       float dsc[FMT == kQ4K ? 2 : 4][2];
@@ -899,23 +1042,54 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_tiled_kernel(const Params p)
           }
         }
       }
+      }  // lane-group layout
     }
 
     const bool tile_end = (r == ipt - 1u);
     float* redbuf = red + (tile_local & 1u) * redsz;
     if (p.nmat == 2u && kst == p.ks - 1u && cons.mat == 0u) {  // matrix 0 of the tile is complete
 #pragma unroll
-      for (int b = 0; b < NB; ++b) {
+      for (int b = 0; b < NR; ++b) {
         held[b][0] = acc[b][0];
         held[b][1] = acc[b][1];
         acc[b][0] = acc[b][1] = 0.f;
       }
-    }
-    if (tile_end) {
-      // the four lanes of a row hold disjoint groups: (t0 + t1) + (t2 + t3)
-      auto publish = [&](int m, float (&v)[NB][2]) {
 #pragma unroll
-        for (int b = 0; b < NB; ++b) {
+      for (int j = 0; j < NJ; ++j)
+#pragma unroll
+        for (int hr = 0; hr < 2; ++hr)
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            cheld[j][hr][q] = cacc[j][hr][q];
+            cacc[j][hr][q] = 0.f;
+          }
+    }
+    if (tile_end && kCols) {
+      // lane t holds rows g, g+8 of batch rows 4j + t, four slots each: (s0 + s1) + (s2 + s3)
+      auto publish_cols = [&](int m, float (&v)[NJ][2][4]) {
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) {
+          const uint32_t bm = 4u * j + t;
+#pragma unroll
+          for (int hr = 0; hr < 2; ++hr) {
+            const float s2 = (v[j][hr][0] + v[j][hr][1]) + (v[j][hr][2] + v[j][hr][3]);
+            if (bm < nbatch) redbuf[((warp * 2 + m) * kTileRows + g + 8u * hr) * nbatch + bm] = s2;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) v[j][hr][q] = 0.f;
+          }
+        }
+      };
+      if (p.nmat == 2u) {
+        publish_cols(0, cheld);
+        publish_cols(1, cacc);
+      } else {
+        publish_cols(0, cacc);
+      }
+    } else if (tile_end) {
+      // the four lanes of a row hold disjoint groups: (t0 + t1) + (t2 + t3)
+      auto publish = [&](int m, float (&v)[NR][2]) {
+#pragma unroll
+        for (int b = 0; b < NR; ++b) {
 #pragma unroll
           for (int hr = 0; hr < 2; ++hr) {
             float s2 = v[b][hr] + __shfl_xor_sync(0xffffffffu, v[b][hr], 1);
@@ -1019,7 +1193,8 @@ uint32_t smem_bytes(uint32_t cols, uint32_t batch, Params* p) {
     off += sz;
     return at;
   };
-  const uint32_t nstage = FMT == kQ4K ? 4u : 3u;
+  // batch launches spend shared memory on the activation tables instead of stages
+  const uint32_t nstage = TILED && batch >= 4u ? 2u : FMT == kQ4K ? 4u : 3u;
   const uint32_t stage_bytes =
       TILED ? kStageBlocks * TileFmt<FMT>::kBytes : kTileRows * (kStageBlocks * Fmt<FMT>::kBytes + Fmt<FMT>::kPad);
   carve(nstage * stage_bytes, 128);
@@ -1046,7 +1221,9 @@ uint32_t smem_bytes(uint32_t cols, uint32_t batch, Params* p) {
 
 template <int FMT, int NB, bool TILED>
 cudaError_t launch_t(const GemvArgs& a, Params p, cudaStream_t s) {
-  auto kernel = TILED ? gemv_tiled_kernel<FMT, NB> : gemv_kernel<FMT, NB>;
+  void (*kernel)(const Params);
+  if constexpr (TILED) kernel = gemv_tiled_kernel<FMT, NB>;
+  else kernel = gemv_kernel<FMT, NB>;
   const uint32_t smem = smem_bytes<FMT, TILED>(a.cols, p.batch, &p);
   // One-time kernel setup and occupancy per (kernel instance, smem size): these
   // queries cost microseconds and must stay off the per-launch path
@@ -1100,6 +1277,8 @@ cudaError_t launch_fmt(const GemvArgs& a, Params p, cudaStream_t s) {
   if (p.batch == 1) return launch_t<FMT, 1, TILED>(a, p, s);
   if (p.batch == 2) return launch_t<FMT, 2, TILED>(a, p, s);
   if (p.batch <= 4) return launch_t<FMT, 4, TILED>(a, p, s);
+  if constexpr (TILED)
+    if (p.batch > 8) return launch_t<FMT, 16, TILED>(a, p, s);
   return launch_t<FMT, 8, TILED>(a, p, s);
 }
 
@@ -1158,7 +1337,7 @@ cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t s) {
   // Batch rows run in launches of at most 8 rows (each launch streams the
   // weights once); a launch's activation tables must fit in shared memory.
   for (uint32_t b0 = 0; b0 < a.batch;) {
-    uint32_t nb = min(8u, a.batch - b0);
+    uint32_t nb = min(tiled ? 16u : 8u, a.batch - b0);
     auto smem = [&](uint32_t n) {
       return tiled ? (fmt == kQ4K ? smem_for<kQ4K, true>(a.cols, n) : smem_for<kQ6K, true>(a.cols, n))
                    : (fmt == kQ4K ? smem_for<kQ4K, false>(a.cols, n) : smem_for<kQ6K, false>(a.cols, n));

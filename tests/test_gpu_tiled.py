@@ -147,18 +147,26 @@ def test_tiled_gemv_parity(ops, fmt, rows, cols, batch):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("fmt", [12, 14])
-def test_tiled_batch_rows_equal_batch_one(ops, fmt):
-    """Each batch row runs the batch-1 arithmetic: identical bits at any batch size."""
-    rng = np.random.default_rng(11 + fmt)
-    rows, cols = 256, 2048
+@pytest.mark.parametrize("fmt,cols", [(12, 2048), (14, 2048), (12, 6144), (14, 4096)])
+def test_tiled_batch_rows_equal_batch_one(ops, fmt, cols):
+    """Every batch row runs the batch-1 arithmetic, in both batch layouts (lanes
+    carrying groups for 2 rows, MMA columns carrying rows for 3..16 rows per
+    launch): identical bits at any batch size, SwiGLU pairs included."""
+    rng = np.random.default_rng(11 + fmt + cols)
+    rows = 256
     W = oracle.quantize(fmt, rng.normal(0, 0.02, rows * cols).astype(np.float32))
-    x = rng.normal(0, 1, (8, cols)).astype(np.float32)
+    U = oracle.quantize(fmt, rng.normal(0, 0.02, rows * cols).astype(np.float32))
+    x = rng.normal(0, 1, (29, cols)).astype(np.float32)
+    x[3] = 0.0
     code, T = ops.tile_weights(fmt, _t(W), rows, cols)
-    full = _np(ops.gemv(code, T, rows, cols, _t(x)))
-    for b in range(8):
-        one = _np(ops.gemv(code, T, rows, cols, _t(x[b:b + 1])))
-        assert np.array_equal(one[0].view(np.uint32), full[b].view(np.uint32)), b
+    _, TU = ops.tile_weights(fmt, _t(U), rows, cols)
+    one = np.stack([_np(ops.gemv(code, T, rows, cols, _t(x[b:b + 1])))[0] for b in range(29)])
+    one_act = np.stack([_np(ops.gemv_swiglu(code, T, TU, rows, cols, _t(x[b:b + 1])))[0] for b in range(29)])
+    for batch in (2, 3, 5, 8, 13, 16, 29):
+        full = _np(ops.gemv(code, T, rows, cols, _t(x[:batch])))
+        assert np.array_equal(full.view(np.uint32), one[:batch].view(np.uint32)), batch
+        act = _np(ops.gemv_swiglu(code, T, TU, rows, cols, _t(x[:batch])))
+        assert np.array_equal(act.view(np.uint32), one_act[:batch].view(np.uint32)), batch
 
 
 @pytest.mark.gpu
@@ -176,7 +184,7 @@ def test_tiled_mlp_config1_parity(ops):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("batch", [1, 4])
+@pytest.mark.parametrize("batch", [1, 4, 64])
 def test_tiled_readout_parity(ops, batch):
     rng = np.random.default_rng(77 + batch)
     V, D = 4096, 2048
