@@ -446,25 +446,8 @@ class DecodeWorkload(Workload):
 def host_payloads(layout, seed):
     """Host-side payloads of the layout's shapes with random valid packed blocks
     (no GPU kernels involved: the CPU arms time the reference's CPU path only)."""
-    rng = np.random.default_rng(seed)
-    mats = np.zeros(layout.matrix_words * 4, np.uint8)
-    basis = np.zeros(layout.basis_words * 4, np.uint8)
-    for i, t in enumerate(layout.matrices + layout.basis):
-        buf = mats if i < len(layout.matrices) else basis
-        if t.fmt == 0:
-            buf[t.offset:t.offset + t.nbytes] = rng.normal(0, 0.02, t.rows * t.cols).astype(np.float32).view(np.uint8)
-            continue
-        bs = 144 if t.fmt == 12 else 210
-        nb = t.rows * t.cols // 256
-        blk = rng.integers(0, 256, (nb, bs), dtype=np.uint8)
-        d = rng.uniform(1e-4, 6e-4, nb).astype(np.float16).view(np.uint8).reshape(nb, 2)
-        if t.fmt == 12:
-            blk[:, 0:2] = d
-            blk[:, 2:4] = rng.uniform(1e-4, 6e-4, nb).astype(np.float16).view(np.uint8).reshape(nb, 2)
-        else:
-            blk[:, 208:210] = d
-        buf[t.offset:t.offset + t.nbytes] = blk.reshape(-1)
-    return layout.params(), mats, basis
+    from rta_b200 import assets
+    return assets.generate_host(layout, seed)
 
 
 class RaggedBatchWorkload:

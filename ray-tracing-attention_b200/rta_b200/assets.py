@@ -280,6 +280,30 @@ def generate_device(layout: Layout, seed: int, sigma: float = 0.02, device="cuda
     return mats, basis
 
 
+def generate_host(layout: Layout, seed: int):
+    """Host-side payloads of a layout: random valid packed blocks (numpy, seeded) for
+    every matrix, N(0, 0.02) for the F32 ones.  Returns (params, matrices, basis)."""
+    rng = np.random.default_rng(seed)
+    mats = np.zeros(layout.matrix_words * 4, np.uint8)
+    basis = np.zeros(layout.basis_words * 4, np.uint8)
+    for i, t in enumerate(layout.matrices + layout.basis):
+        buf = mats if i < len(layout.matrices) else basis
+        if t.fmt == F32:
+            buf[t.offset:t.offset + t.nbytes] = rng.normal(0, 0.02, t.rows * t.cols).astype(np.float32).view(np.uint8)
+            continue
+        bs = 144 if t.fmt == Q4_K else 210
+        nb = t.rows * t.cols // 256
+        blk = rng.integers(0, 256, (nb, bs), dtype=np.uint8)
+        d = rng.uniform(1e-4, 6e-4, nb).astype(np.float16).view(np.uint8).reshape(nb, 2)
+        if t.fmt == Q4_K:
+            blk[:, 0:2] = d
+            blk[:, 2:4] = rng.uniform(1e-4, 6e-4, nb).astype(np.float16).view(np.uint8).reshape(nb, 2)
+        else:
+            blk[:, 208:210] = d
+        buf[t.offset:t.offset + t.nbytes] = blk.reshape(-1)
+    return layout.params(), mats, basis
+
+
 def write_files(directory, layout: Layout, matrices: np.ndarray, basis: np.ndarray) -> Path:
     """Write optical_model.bin / geometry_weights.bin / vocabulary.bin / model.json."""
     directory = Path(directory)
