@@ -52,6 +52,10 @@ enum { RTA_F32 = 0, RTA_F16 = 1, RTA_BF16 = 30, RTA_Q4_K = 12, RTA_Q6_K = 14 };
  * counterpart in the exporter's format table); accepted by the GEMV operators
  * (rta_gemv, rta_gemv_swiglu, rta_mlp_swiglu, rta_readout) in place of 12 / 14. */
 enum { RTA_Q4_K_TILED = 112, RTA_Q6_K_TILED = 114 };
+/* Panel re-layouts made by rta_panel_weights for the tensor-core batched
+ * product (rta_gemm_tc): per 128-row tile and 256-column block one contiguous
+ * panel of the same bytes, ordered for the dequantizing threads. */
+enum { RTA_Q4_K_PANEL = 212, RTA_Q6_K_PANEL = 214 };
 
 /* Text of the last error raised on this thread (never NULL). */
 RTA_API const char* rta_last_error(void);
@@ -86,6 +90,27 @@ RTA_API rta_status rta_dequantize(int format, const void* blocks, size_t nblocks
  * order, optical_resident.cpp:139-153). */
 RTA_API rta_status rta_tile_weights(int format, const void* src, uint32_t rows, uint32_t cols, void* dst,
                                     void* stream);
+
+/* Re-lay a row-major [rows x cols] Q4_K / Q6_K matrix (rows % 128 == 0,
+ * cols % 256 == 0) into the panel order of RTA_Q4_K_PANEL / RTA_Q6_K_PANEL
+ * (same byte size; dst 16-byte aligned, not overlapping src). */
+RTA_API rta_status rta_panel_weights(int format, const void* src, uint32_t rows, uint32_t cols, void* dst,
+                                     void* stream);
+
+/* Batched product on the tensor cores (tcgen05), for batches of 16 rows or
+ * more: y[b][r] (+)= sum_c W[r][c] x[b][c] with W in panel order
+ * (RTA_Q4_K_PANEL / RTA_Q6_K_PANEL), rows % 128 == 0, cols % 256 == 0,
+ * 1 <= batch <= 256, fp32 accumulation over fp16-rounded x.  When argmax is
+ * not NULL the row of the largest y[b][.] (ties -> lowest row) and its value
+ * (best, may be NULL) are returned per batch row, and y may be NULL
+ * (vocabulary readout).  workspace: rta_gemm_tc_workspace_bytes(format,
+ * batch, cols) bytes.  Replaces op 2 of
+ * ray_tracing/native/shaders/resident_math.comp:39-75 and the readout ops
+ * 16/17/23 (:117-130) for batched rows. */
+RTA_API size_t rta_gemm_tc_workspace_bytes(int format, uint32_t batch, uint32_t cols);
+RTA_API rta_status rta_gemm_tc(int format, const void* w, uint32_t rows, uint32_t cols, const float* x,
+                               uint32_t batch, float* y, int accumulate, uint32_t* argmax, float* best,
+                               void* workspace, size_t workspace_bytes, void* stream);
 
 /* y[b][r] (+)= sum_c W[r][c] x[b][c]; W Q4_K or Q6_K row-major, rows % 16 == 0,
  * cols % 256 == 0, 1 <= batch <= 32.  Replaces op 2 of

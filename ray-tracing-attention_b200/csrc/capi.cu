@@ -32,7 +32,7 @@ constexpr size_t kErrBytes = 256;  // device error word + padding at the head of
 
 __global__ void readout_finish_kernel(const unsigned long long* keys, uint32_t batch, uint32_t vocab,
                                       uint32_t* argmax, float* best, uint32_t* err) {
-  const uint32_t b = threadIdx.x;
+  const uint32_t b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= batch) return;
   const unsigned long long k = keys[b];
   const uint32_t id = ~static_cast<uint32_t>(k & 0xffffffffull);
@@ -91,6 +91,58 @@ rta_status rta_tile_weights(int format, const void* src, uint32_t rows, uint32_t
   return cuda_status(rta::launch_tile_weights(format, static_cast<const uint8_t*>(src), rows, cols,
                                               static_cast<uint8_t*>(dst), as_stream(stream)),
                      "rta_tile_weights");
+}
+
+rta_status rta_panel_weights(int format, const void* src, uint32_t rows, uint32_t cols, void* dst, void* stream) {
+  if (!quant_format(format) || !src || !dst || rows == 0 || rows % 128 || cols == 0 || cols % 256)
+    return fail(RTA_E_ARG, "rta_panel_weights: format must be Q4_K/Q6_K, rows % 128 == 0, cols % 256 == 0");
+  const size_t bytes = static_cast<size_t>(rows) * (cols / 256) * rta::block_bytes(format);
+  const uintptr_t a = reinterpret_cast<uintptr_t>(src), b = reinterpret_cast<uintptr_t>(dst);
+  if (a < b + bytes && b < a + bytes) return fail(RTA_E_ARG, "rta_panel_weights: dst overlaps src");
+  return cuda_status(rta::launch_tile_tc(format, static_cast<const uint8_t*>(src), rows, cols,
+                                         static_cast<uint8_t*>(dst), as_stream(stream)),
+                     "rta_panel_weights");
+}
+
+size_t rta_gemm_tc_workspace_bytes(int format, uint32_t batch, uint32_t cols) {
+  const size_t keys = (8ull * (batch ? batch : 1) + 255u) / 256u * 256u;
+  return kErrBytes + keys + rta::tc_workspace_bytes(format, batch ? batch : 1, cols);
+}
+
+rta_status rta_gemm_tc(int format, const void* w, uint32_t rows, uint32_t cols, const float* x, uint32_t batch,
+                       float* y, int accumulate, uint32_t* argmax, float* best, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+  if ((format != RTA_Q4_K_PANEL && format != RTA_Q6_K_PANEL) || !w || !x || (!y && !argmax) || !workspace ||
+      rows == 0 || rows % 128 || cols == 0 || cols % 256 || batch == 0 || batch > rta::kMaxBatch)
+    return fail(RTA_E_ARG, "rta_gemm_tc: panel format, rows % 128 == 0, cols % 256 == 0, 1 <= batch <= 256");
+  if (workspace_bytes < rta_gemm_tc_workspace_bytes(format, batch, cols))
+    return fail(RTA_E_ARG, "rta_gemm_tc: workspace too small");
+  cudaStream_t s = as_stream(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  const size_t keys_bytes = (8ull * batch + 255u) / 256u * 256u;
+  uint32_t* err = reinterpret_cast<uint32_t*>(ws);
+  auto* keys = reinterpret_cast<unsigned long long*>(ws + kErrBytes);
+  rta_status st = cuda_status(cudaMemsetAsync(ws, 0, kErrBytes + keys_bytes, s), "rta_gemm_tc(memset)");
+  if (st != RTA_OK) return st;
+  rta::TcGemmArgs a;
+  a.fmt = format;
+  a.w0 = static_cast<const uint8_t*>(w);
+  a.rows = rows;
+  a.cols = cols;
+  a.x = x;
+  a.x_stride = cols;
+  a.batch = batch;
+  a.epilogue = accumulate ? rta::kAccumulate : rta::kStore;
+  a.y = y;
+  a.y_stride = rows;
+  a.argmax = argmax ? keys : nullptr;
+  a.err = err;
+  a.xb = ws + kErrBytes + keys_bytes;
+  a.xb_bytes = workspace_bytes - kErrBytes - keys_bytes;
+  st = cuda_status(rta::launch_tc_gemm(a, s), "rta_gemm_tc");
+  if (st != RTA_OK || !argmax) return st;
+  readout_finish_kernel<<<(batch + 255u) / 256u, 256, 0, s>>>(keys, batch, rows, argmax, best, err);
+  return cuda_status(cudaGetLastError(), "rta_gemm_tc(finish)");
 }
 
 rta_status rta_gemv(int format, const void* w, uint32_t rows, uint32_t cols, const float* x, uint32_t batch,

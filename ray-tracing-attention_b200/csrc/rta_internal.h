@@ -16,10 +16,15 @@ constexpr int kF32 = 0, kF16 = 1, kBF16 = 30, kQ4K = 12, kQ6K = 14;  // export.p
 // Tiled re-layouts of Q4_K / Q6_K matrices (same bytes, GEMV-friendly order;
 // see launch_tile_weights).  Codes of this library, not of the exporter.
 constexpr int kTiledOffset = 100, kQ4KTiled = kQ4K + kTiledOffset, kQ6KTiled = kQ6K + kTiledOffset;
+// Panel re-layouts for the tensor-core batched path (qgemm.cu): per 128-row
+// tile and 256-wide block column one contiguous panel of the same bytes.
+constexpr int kPanelOffset = 200, kQ4KPanel = kQ4K + kPanelOffset, kQ6KPanel = kQ6K + kPanelOffset;
 constexpr uint32_t kQ4KBytes = 144, kQ6KBytes = 210;
 constexpr uint32_t kMaxBatch = 256;  // GEMV batch rows per call (run as launches of up to 8 rows)
 
-inline uint32_t block_bytes(int fmt) { return fmt == kQ4K || fmt == kQ4KTiled ? kQ4KBytes : kQ6KBytes; }
+inline uint32_t block_bytes(int fmt) {
+  return fmt == kQ4K || fmt == kQ4KTiled || fmt == kQ4KPanel ? kQ4KBytes : kQ6KBytes;
+}
 
 // Record the thread-local text returned by rta_last_error() (capi.cu).
 void set_last_error(const std::string& msg);
@@ -43,7 +48,8 @@ enum Prologue : int {
   kPlain = 0,      // x as given
   kRmsNorm = 1,    // x * inversesqrt(mean(x^2) + eps) * norm_w
   kHeadGate = 2,   // per 128-wide head: x * inversesqrt(mean_head(x^2)+eps) * norm_w * z * sigmoid(z)
-  kSigmoidGate = 3 // x * sigmoid(z)
+  kSigmoidGate = 3, // x * sigmoid(z)
+  kSwiGLUIn = 4     // swiglu(x, z): the gate / up outputs of the batched path (qgemm.cu only)
 };
 enum Epilogue : int {
   kStore = 0,      // y = W x
@@ -78,6 +84,40 @@ cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t s);
 // order into the tiled order the kTiled formats name (dst != src, same size).
 cudaError_t launch_tile_weights(int fmt, const uint8_t* src, uint32_t rows, uint32_t cols, uint8_t* dst,
                                 cudaStream_t s);
+// ---------------------------------------------------------------- qgemm.cu
+// Batched product on the tensor cores with panel-layout weights (kQ4KPanel /
+// kQ6KPanel, rows % 128 == 0): a prep launch (prologue, x -> fp16 stages) and
+// the persistent tcgen05 kernel per kTcMaxN batch rows.  w1 (optional) is a
+// second matrix whose rows follow w0's in y (the gate / up pair).
+constexpr uint32_t kTcMaxN = 64;
+struct TcGemmArgs {
+  int fmt = kQ4KPanel;
+  const uint8_t* w0 = nullptr;
+  const uint8_t* w1 = nullptr;
+  uint32_t rows = 0, cols = 0;  // rows per matrix (multiple of 128), cols (multiple of 256)
+  const float* x = nullptr;
+  uint32_t x_stride = 0, batch = 1;
+  int prologue = kPlain;
+  const float* norm_w = nullptr;
+  float eps = 1e-6f;
+  const float* z = nullptr;
+  uint32_t z_stride = 0;
+  int epilogue = kStore;  // kStore or kAccumulate
+  float* y = nullptr;
+  uint32_t y_stride = 0;
+  unsigned long long* argmax = nullptr;
+  uint32_t argmax_step = 1;
+  uint32_t* err = nullptr;
+  const uint32_t* running = nullptr;
+  uint32_t running_step = 1;
+  uint8_t* xb = nullptr;  // workspace of tc_workspace_bytes(fmt, batch, cols) bytes
+  size_t xb_bytes = 0;
+  bool pdl = false;
+};
+size_t tc_workspace_bytes(int fmt, uint32_t batch, uint32_t cols);
+cudaError_t launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s);
+// GGUF rows of a Q4_K / Q6_K matrix (rows % 128 == 0) -> panel layout.
+cudaError_t launch_tile_tc(int fmt, const uint8_t* src, uint32_t rows, uint32_t cols, uint8_t* dst, cudaStream_t s);
 // Dense F32 GEMV for the tiny recurrent alpha/beta projections.
 cudaError_t launch_gemv_f32(const float* W, uint32_t rows, uint32_t cols, const float* x, uint32_t x_stride,
                             uint32_t batch, float* y, uint32_t y_stride, cudaStream_t s);

@@ -15,8 +15,10 @@ from . import _build
 RTA_OK, RTA_E_ARG, RTA_E_ASSET, RTA_E_CUDA, RTA_E_DEVICE_CHECK, RTA_E_TIMEOUT, RTA_E_STATE = range(7)
 F32, F16, BF16, Q4_K, Q6_K = 0, 1, 30, 12, 14
 Q4_K_TILED, Q6_K_TILED = 112, 114  # rta_tile_weights re-layouts (same bytes)
-BLOCK_BYTES = {Q4_K: 144, Q6_K: 210, Q4_K_TILED: 144, Q6_K_TILED: 210}
+Q4_K_PANEL, Q6_K_PANEL = 212, 214  # rta_panel_weights re-layouts for the tensor-core product
+BLOCK_BYTES = {Q4_K: 144, Q6_K: 210, Q4_K_TILED: 144, Q6_K_TILED: 210, Q4_K_PANEL: 144, Q6_K_PANEL: 210}
 TILED = {Q4_K: Q4_K_TILED, Q6_K: Q6_K_TILED}
+PANEL = {Q4_K: Q4_K_PANEL, Q6_K: Q6_K_PANEL}
 
 
 class RtaError(RuntimeError):
@@ -37,6 +39,9 @@ _SIGNATURES = {
     "rta_synthetic_normal": (c_i32, [c_u64, c_f, c_f, c_sz, c_p, c_p]),
     "rta_dequantize": (c_i32, [c_i32, c_p, c_sz, c_p, c_p]),
     "rta_tile_weights": (c_i32, [c_i32, c_p, c_u32, c_u32, c_p, c_p]),
+    "rta_panel_weights": (c_i32, [c_i32, c_p, c_u32, c_u32, c_p, c_p]),
+    "rta_gemm_tc_workspace_bytes": (c_sz, [c_i32, c_u32, c_u32]),
+    "rta_gemm_tc": (c_i32, [c_i32, c_p, c_u32, c_u32, c_p, c_u32, c_p, c_i32, c_p, c_p, c_p, c_sz, c_p]),
     "rta_gemv": (c_i32, [c_i32, c_p, c_u32, c_u32, c_p, c_u32, c_p, c_i32, c_p]),
     "rta_gemv_swiglu": (c_i32, [c_i32, c_p, c_p, c_u32, c_u32, c_p, c_u32, c_p, c_p]),
     "rta_mlp_swiglu": (c_i32, [c_i32, c_p, c_p, c_p, c_u32, c_u32, c_p, c_u32, c_p, c_p, c_i32, c_p]),

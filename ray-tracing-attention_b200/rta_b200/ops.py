@@ -9,7 +9,7 @@ from __future__ import annotations
 import torch
 
 from . import _lib
-from ._lib import BLOCK_BYTES, Q4_K, Q6_K, TILED, check
+from ._lib import BLOCK_BYTES, PANEL, Q4_K, Q6_K, TILED, check
 
 
 def _stream():
@@ -71,6 +71,33 @@ def tile_weights(fmt: int, w: torch.Tensor, rows: int, cols: int) -> tuple[int, 
     out = torch.empty_like(w)
     check(_lib.load().rta_tile_weights(fmt, _ptr(w), rows, cols, _ptr(out), _stream()))
     return TILED[fmt], out
+
+
+def panel_weights(fmt: int, w: torch.Tensor, rows: int, cols: int) -> tuple[int, torch.Tensor]:
+    """Re-lay a row-major Q4_K / Q6_K matrix (rows % 128 == 0) into the panel order
+    of the tensor-core product.  Returns (panel format code, panel bytes)."""
+    out = torch.empty_like(w)
+    check(_lib.load().rta_panel_weights(fmt, _ptr(w), rows, cols, _ptr(out), _stream()))
+    return PANEL[fmt], out
+
+
+def gemm_tc(fmt: int, w: torch.Tensor, rows: int, cols: int, x: torch.Tensor, y: torch.Tensor | None = None,
+            accumulate: bool = False, argmax: bool = False, store: bool = True,
+            workspace: torch.Tensor | None = None):
+    """Tensor-core batched product with panel weights: returns (y, argmax ids, best)
+    (ids / best None unless argmax; y None when store is False)."""
+    x = x.reshape(-1, cols)
+    B = x.shape[0]
+    lib = _lib.load()
+    if workspace is None:
+        workspace = torch.empty(lib.rta_gemm_tc_workspace_bytes(fmt, B, cols), dtype=torch.uint8, device=x.device)
+    if store and y is None:
+        y = torch.empty(B, rows, dtype=torch.float32, device=x.device)
+    ids = torch.empty(B, dtype=torch.int32, device=x.device) if argmax else None
+    best = torch.empty(B, dtype=torch.float32, device=x.device) if argmax else None
+    check(lib.rta_gemm_tc(fmt, _ptr(w), rows, cols, _ptr(x), B, _ptr(y if store else None), int(accumulate),
+                          _ptr(ids), _ptr(best), _ptr(workspace), workspace.numel(), _stream()))
+    return (y if store else None), ids, best
 
 
 def gemv(fmt: int, w: torch.Tensor, rows: int, cols: int, x: torch.Tensor, y: torch.Tensor | None = None,
