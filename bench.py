@@ -2,7 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
 
-Workloads (synthetic seeded inputs of the stated shapes):
+Workloads (the benchmark configs, synthetic seeded inputs of the stated shapes):
   decode2b  config 4: 2B-shape hybrid decoder, batch 1, greedy decode tokens/s (default)
   mlp       config 1: SwiGLU MLP 2048 -> 6144 -> 2048, Q4_K, batch 1
   attention config 2: GQA decode 16q/4kv, head_dim 256, fp16 KV, history --history (default 32768)
@@ -232,7 +232,7 @@ class MLPWorkload(Workload):
 
 
 class LMHeadWorkload(Workload):
-    """LM head 151936 x 2048 Q6_K, logits + per-row argmax, batch 1 or 64."""
+    """benchmark config 3: LM head 151936 x 2048 Q6_K, logits + per-row argmax, batch 1 or 64."""
     name, metric, unit, dtype, dominant = ("lmhead", "vocabulary readout tokens/s (151936x2048 Q6_K, logits+argmax)",
                                            "tokens/s", "q6k-int8mma-f32acc", "gemv_tiled_kernel<Q6_K> readout + argmax")
     V, D = 151936, 2048
@@ -245,19 +245,38 @@ class LMHeadWorkload(Workload):
         from rta_b200 import ops
         self.ops, self.torch = ops, torch
         self.B = batch
-        self.launches_per_step = 2 + (batch + 15) // 16  # memset, readout launches of <= 16 rows, finish
-        if batch != 1:
+        # batches of 16 rows or more run on the tensor cores (rta_gemm_tc, panel layout)
+        self.tc = batch >= 16
+        raw = ops.synthetic_blocks(14, self.V, self.D, seed)
+        if self.tc:
+            self.launches_per_step = 3 + (batch + 63) // 64 * 2  # memset, (prep, tcgen05 kernel) per 64 rows, finish
             self.traffic = None
-            self.dominant = f"gemv_tiled_kernel<Q6_K> readout + argmax, {batch} rows (launches of <= 16 rows)"
-        self.fmt, self.w = ops.tile_weights(14, ops.synthetic_blocks(14, self.V, self.D, seed), self.V, self.D)
+            self.dtype = "q6k-fp16-tcgen05-f32acc"
+            self.dominant = f"tc_gemm_kernel<Q6_K,{min(64, batch)}> readout + argmax, {batch} rows"
+            self.fmt, self.w = ops.panel_weights(14, raw, self.V, self.D)
+            self.ws = torch.empty(ops._lib.load().rta_gemm_tc_workspace_bytes(self.fmt, batch, self.D),
+                                  dtype=torch.uint8, device="cuda")
+            self.y = torch.empty(batch, self.V, dtype=torch.float32, device="cuda")
+        else:
+            self.launches_per_step = 2 + (batch + 15) // 16  # memset, readout launches of <= 16 rows, finish
+            if batch != 1:
+                self.traffic = None
+                self.dominant = f"gemv_tiled_kernel<Q6_K> readout + argmax, {batch} rows (launches of <= 16 rows)"
+            self.fmt, self.w = ops.tile_weights(14, raw, self.V, self.D)
+            self.ws = torch.empty(4096, dtype=torch.uint8, device="cuda")
+        del raw
         self.x = ops.synthetic_normal(batch * self.D, seed + 1).reshape(batch, self.D)
-        self.ws = torch.empty(4096, dtype=torch.uint8, device="cuda")
         self.hx = torch.empty(batch * self.D, dtype=torch.float32).pin_memory()
         self.hx.copy_(self.x.reshape(-1).cpu())
         self.harg = torch.empty(batch, dtype=torch.int32).pin_memory()
 
     def step(self, i):
-        self.last = self.ops.readout(self.fmt, self.w, self.V, self.D, self.x, logits=True, workspace=self.ws)
+        if self.tc:
+            y, ids, best = self.ops.gemm_tc(self.fmt, self.w, self.V, self.D, self.x, y=self.y, argmax=True,
+                                            workspace=self.ws)
+            self.last = (y, ids, best)
+        else:
+            self.last = self.ops.readout(self.fmt, self.w, self.V, self.D, self.x, logits=True, workspace=self.ws)
 
     dominant_launch = step
 
@@ -279,9 +298,10 @@ class LMHeadWorkload(Workload):
         return self.dominant_bytes()
 
     def config(self):
+        layout = ("panel (rta_panel_weights, once before timing); tcgen05 tensor cores" if self.tc
+                  else "tiled (rta_tile_weights, once before timing)")
         return {"workload": f"config3_lmhead_b{self.B}", "vocab": self.V, "hidden": self.D, "format": "Q6_K",
-                "layout": "tiled (rta_tile_weights, once before timing)", "batch": self.B,
-                "l2": "weights 255 MB > L2"}
+                "layout": layout, "batch": self.B, "l2": "weights 255 MB > L2"}
 
     def cpu_baseline(self, budget_s):
         from oracle import oracle
@@ -367,7 +387,7 @@ class AttentionWorkload(Workload):
 
 
 class DecodeWorkload(Workload):
-    """2B-shape hybrid (24 layers, 3:1 recurrent:full), batch 1,
+    """benchmark config 4: 2B-shape hybrid (24 layers, 3:1 recurrent:full), batch 1,
     prompt 512 random ids, then greedy decode.  A step is one decode token."""
     name, metric, unit, dtype, dominant = ("decode2b", "decode tokens/s (2B-shape hybrid, batch 1)", "tokens/s",
                                            "q4k/q6k-int8mma, f16-kv, f32 state",
@@ -451,7 +471,7 @@ def host_payloads(layout, seed):
 
 
 class RaggedBatchWorkload:
-    """9B-shape hybrid (32 layers 3:1, D 4096, F 12288), a ragged batch of
+    """benchmark config 5: 9B-shape hybrid (32 layers 3:1, D 4096, F 12288), a ragged batch of
     64 sequences with seeded histories U[128, 8192], sharded by sequence over the ranks
     (weights replicated, no collective on the data path).  A step is one decode token
     for every sequence of the job."""
@@ -695,7 +715,7 @@ def run_ours(args, world, rank, local):
     line = {
         "metric": wl.metric, "value": value, "unit": wl.unit, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic (seeded, BASELINE shapes)",
+        "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic (seeded, benchmark shapes)",
         "config": dict(wl.config(), parallelism=f"replicas x{world}" if world > 1 else "single GPU"),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": achieved / pk["hbm_gbs"], "traffic": getattr(wl, "traffic", None), "kernel": wl.dominant,
@@ -748,7 +768,7 @@ def run_reference(args, world, rank):
            "decode2b": {"workload": "config4_2b_hybrid_decode_b1"}}[args.workload]
     return {"impl": "reference", "metric": cls.metric, "value": v, "unit": cls.unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "dtype": "f32",
-            "data": "synthetic (seeded, BASELINE shapes)", "config": cfg,
+            "data": "synthetic (seeded, benchmark shapes)", "config": cfg,
             "cpu_baseline": base, "e2e": {"value": v, "unit": cls.unit, "h2d_bytes_per_step": 0,
                                           "d2h_bytes_per_step": 0},
             "note": "reference Vulkan ray-query worker unavailable on this box (no graphics stack, no RT cores); "

@@ -229,11 +229,15 @@ RTA_API rta_status rta_model_open_files_ex(const rta_model_spec* spec, const cha
                                            uint32_t sequences, uint32_t flags, int device, rta_model** out);
 RTA_API void rta_model_close(rta_model* model);
 
-/* A handle that decodes `sequences` independent sequences side by side (the
- * ragged multi-sequence batch of BASELINE config 5): one decode step produces
- * one token for every running sequence, each with its own history ring,
- * recurrent state, position and stop state, the GEMVs streaming the weights
- * once per up-to-8 sequences.  No reference counterpart: the reference worker
+/* A handle that decodes `sequences` independent sequences side by side (a
+ * ragged multi-sequence batch): one decode step produces one token for every
+ * running sequence, each with its own history ring, recurrent state, position
+ * and stop state.  Below 16 sequences the GEMVs stream the weights once per
+ * up-to-16 sequences; from 16 sequences on, every matrix with a multiple of 128
+ * rows is kept in panel order and its products run on the tensor cores
+ * (rta_gemm_tc arithmetic: fp16-rounded activations, fp32 accumulation), so the
+ * tokens then follow the single-sequence ones wherever the top-2 margin exceeds
+ * that rounding.  No reference counterpart: the reference worker
  * serves one sequence per process (optical_resident.cpp:964-971).  The
  * single-sequence calls (rta_model_prefill / rta_model_generate) require
  * sequences == 1. */
@@ -297,7 +301,7 @@ RTA_API rta_status rta_model_vocabulary(rta_model* model, const float* hidden, f
 RTA_API rta_status rta_model_state(rta_model* model, float* state, uint32_t* position);
 /* Resource counters, worker op 8: payload bytes, derived layer bytes, KV bytes,
  * recurrent state bytes, capacity, attention splits, kernels per decode step,
- * kernels per prefill step, position, sequences. */
+ * kernels per prefill step, position, sequences, matrices on the tensor cores. */
 RTA_API rta_status rta_model_resources(rta_model* model, uint64_t* out, size_t n);
 
 #ifdef __cplusplus

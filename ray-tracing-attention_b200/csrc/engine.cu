@@ -100,7 +100,16 @@ struct Engine {
   uint32_t n_full = 0, n_rec = 0;
   const uint8_t* lm = nullptr;
   int lm_fmt = kQ6K;
-  DevBuf<uint8_t> lm_tiled;  // the LM head in tiled order (its GGUF rows may double as the embedding)
+  DevBuf<uint8_t> lm_tiled;  // the LM head in tiled / panel order (its GGUF rows may double as the embedding)
+  // Batched products run on the tensor cores (qgemm.cu) when the handle decodes
+  // at least kTcMinSeq sequences: matrices with rows % 128 == 0 are then kept in
+  // panel order, the gate / up outputs go to gu (raw, [row][gate | up]) and the
+  // down projection's prep applies SwiGLU; tc_ws holds the fp16 activation stages.
+  static constexpr uint32_t kTcMinSeq = 16;
+  bool tc = false;
+  uint32_t panel_matrices = 0;  // matrices kept in panel order (products on the tensor cores)
+  DevBuf<float> gu;
+  DevBuf<uint8_t> tc_ws;
   const uint8_t* embed = nullptr;
   int embed_fmt = kQ6K;
   const float* out_norm = nullptr;
@@ -228,18 +237,31 @@ struct Engine {
     }
     DevBuf<uint8_t> tmp;
     tmp.alloc(need);
+    // gate and up share one format field: both take the panel order only together
+    auto panel_ok = [&](uint32_t rows) { return tc && rows % 128u == 0u; };
     for (const Job& j : jobs) {
       const size_t bytes = static_cast<size_t>(j.rows) * (j.cols / 256) * block_bytes(j.fmt);
-      RTA_CUDA(launch_tile_weights(j.fmt, j.p, j.rows, j.cols, tmp.p, stream));
+      if (panel_ok(j.rows))
+        RTA_CUDA(launch_tile_tc(j.fmt, j.p, j.rows, j.cols, tmp.p, stream));
+      else
+        RTA_CUDA(launch_tile_weights(j.fmt, j.p, j.rows, j.cols, tmp.p, stream));
       RTA_CUDA(cudaMemcpyAsync(j.p, tmp.p, bytes, cudaMemcpyDeviceToDevice, stream));
     }
-    for (const Job& j : jobs)
-      if (j.tiled_field) *j.tiled_field = j.fmt + kTiledOffset;
+    for (const Job& j : jobs) {
+      if (j.tiled_field) *j.tiled_field = j.fmt + (panel_ok(j.rows) ? kPanelOffset : kTiledOffset);
+      panel_matrices += panel_ok(j.rows) ? 1u : 0u;
+    }
     const size_t lm_bytes = static_cast<size_t>(spec.vocabulary_size) * (D / 256) * block_bytes(lm_fmt);
     lm_tiled.alloc(lm_bytes);
-    RTA_CUDA(launch_tile_weights(lm_fmt, lm, spec.vocabulary_size, D, lm_tiled.p, stream));
+    if (panel_ok(spec.vocabulary_size)) {
+      RTA_CUDA(launch_tile_tc(lm_fmt, lm, spec.vocabulary_size, D, lm_tiled.p, stream));
+      lm_fmt += kPanelOffset;
+      ++panel_matrices;
+    } else {
+      RTA_CUDA(launch_tile_weights(lm_fmt, lm, spec.vocabulary_size, D, lm_tiled.p, stream));
+      lm_fmt += kTiledOffset;
+    }
     lm = lm_tiled.p;
-    lm_fmt += kTiledOffset;
     RTA_CUDA(cudaStreamSynchronize(stream));
   }
 
@@ -363,6 +385,7 @@ struct Engine {
       layers.push_back(std::move(L));
     }
     RTA_CUDA(cudaStreamSynchronize(stream));
+    tc = nseq >= kTcMinSeq;
     tile_matrices();
 
     // activations and state, one row per sequence
@@ -376,6 +399,14 @@ struct Engine {
     act.alloc(static_cast<size_t>(nseq) * spec.middle_size);
     scratch_x.alloc(32ull * std::max(D, spec.middle_size));
     scratch_y.alloc(32ull * std::max(D, spec.middle_size));
+    if (tc) {  // raw gate | up rows and the tensor-core activation stages (largest K, largest batch)
+      const uint32_t rows = std::max(nseq, 32u);
+      gu.alloc(static_cast<size_t>(rows) * 2 * spec.middle_size);
+      size_t ws = 0;
+      for (uint32_t cols : {D, Q(), std::max(1u, S()), spec.middle_size})
+        if (cols % 256 == 0) ws = std::max({ws, tc_workspace_bytes(kQ4KPanel, rows, cols), tc_workspace_bytes(kQ6KPanel, rows, cols)});
+      tc_ws.alloc(ws);
+    }
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
     nsplit = std::max(1u, std::min(static_cast<uint32_t>(sms) / spec.kv_heads, capacity / 256u));
@@ -418,6 +449,69 @@ struct Engine {
     RTA_CUDA(cudaStreamSynchronize(stream));
   }
 
+  // One product: panel formats run on the tensor cores, the others on the GEMV.
+  cudaError_t matmul(const GemvArgs& a, cudaStream_t s) {
+    if (a.fmt != kQ4KPanel && a.fmt != kQ6KPanel) return launch_gemv(a, s);
+    TcGemmArgs t;
+    t.fmt = a.fmt;
+    t.w0 = a.w0;
+    t.w1 = a.w1;
+    t.rows = a.rows;
+    t.cols = a.cols;
+    t.x = a.x;
+    t.x_stride = a.x_stride ? a.x_stride : a.cols;
+    t.batch = a.batch;
+    t.prologue = a.prologue;
+    t.norm_w = a.norm_w;
+    t.eps = a.eps;
+    t.z = a.z;
+    t.z_stride = a.z_stride;
+    t.epilogue = a.epilogue;
+    t.y = a.y;
+    t.y_stride = a.y_stride ? a.y_stride : a.rows;
+    t.argmax = a.argmax;
+    t.argmax_step = a.argmax_step;
+    t.err = a.err;
+    t.running = a.running;
+    t.running_step = a.running_step;
+    t.xb = tc_ws.p;
+    t.xb_bytes = tc_ws.n;
+    t.pdl = a.pdl;
+    return launch_tc_gemm(t, s);
+  }
+
+  // SwiGLU MLP: `g` (gate / up with the kSwiGLU epilogue into g.y = the
+  // activation rows) then `dn` (down, reading them).  Panel-format gate / up
+  // write the raw gate | up rows to gu instead; a panel-format down then applies
+  // SwiGLU in its own prep unless the caller wants the activation rows too,
+  // otherwise they are formed from gu first.
+  void mlp_pair(GemvArgs g, GemvArgs dn, bool need_act, cudaStream_t s) {
+    const uint32_t F = g.rows;
+    const bool gpanel = g.fmt == kQ4KPanel || g.fmt == kQ6KPanel;
+    const bool dpanel = dn.fmt == kQ4KPanel || dn.fmt == kQ6KPanel;
+    if (!gpanel) {
+      RTA_CUDA(launch_gemv(g, s));
+      RTA_CUDA(matmul(dn, s));
+      return;
+    }
+    float* act_rows = g.y;
+    const uint32_t act_stride = g.y_stride ? g.y_stride : F;
+    g.epilogue = kStore;
+    g.y = gu.p;
+    g.y_stride = 2 * F;  // matrix 1 (up) rows follow matrix 0 (gate) rows
+    RTA_CUDA(matmul(g, s));
+    if (dpanel && !need_act) {
+      dn.prologue = kSwiGLUIn;
+      dn.x = gu.p;
+      dn.z = gu.p + F;
+      dn.x_stride = 2 * F;
+      dn.z_stride = 2 * F;
+    } else {
+      RTA_CUDA(launch_swiglu_rows(gu.p, g.batch, F, 2 * F, act_rows, act_stride, s));
+    }
+    RTA_CUDA(matmul(dn, s));
+  }
+
   // ---------------------------------------------------------- step recording
   uint32_t record_step(bool decode) {
     const cudaStream_t s = stream;
@@ -445,7 +539,7 @@ struct Engine {
       r.running = running;
       r.running_step = cstep;
       r.pdl = true;
-      RTA_CUDA(launch_gemv(r, s));
+      RTA_CUDA(matmul(r, s));
       ++n;
     }
     EmbedParams e;
@@ -482,7 +576,7 @@ struct Engine {
         g.running_step = cstep;
         g.err = &c->err;
         g.pdl = true;
-        RTA_CUDA(launch_gemv(g, s));
+        RTA_CUDA(matmul(g, s));
         PrepParams pp;
         pp.qkvg = proj.p;
         pp.qnorm = L.qnorm;
@@ -556,7 +650,7 @@ struct Engine {
         o.running_step = cstep;
         o.err = &c->err;
         o.pdl = true;
-        RTA_CUDA(launch_gemv(o, s));
+        RTA_CUDA(matmul(o, s));
         n += 5;
       } else {
         GemvArgs g;
@@ -576,7 +670,7 @@ struct Engine {
         g.running_step = cstep;
         g.err = &c->err;
         g.pdl = true;
-        RTA_CUDA(launch_gemv(g, s));
+        RTA_CUDA(matmul(g, s));
         GdnParams gp;
         gp.x = state.p;
         gp.attn_norm = L.attn_norm;
@@ -621,7 +715,7 @@ struct Engine {
         o.running_step = cstep;
         o.err = &c->err;
         o.pdl = true;
-        RTA_CUDA(launch_gemv(o, s));
+        RTA_CUDA(matmul(o, s));
         n += 3;
       }
       GemvArgs gu;
@@ -643,7 +737,6 @@ struct Engine {
       gu.running_step = cstep;
       gu.err = &c->err;
       gu.pdl = true;
-      RTA_CUDA(launch_gemv(gu, s));
       GemvArgs dn;
       dn.fmt = L.down_fmt;
       dn.w0 = L.down;
@@ -659,7 +752,7 @@ struct Engine {
       dn.running_step = cstep;
       dn.err = &c->err;
       dn.pdl = true;
-      RTA_CUDA(launch_gemv(dn, s));
+      mlp_pair(gu, dn, false, s);
       n += 2;
     }
     return n;
@@ -990,6 +1083,35 @@ struct Engine {
       require(std::isfinite(x[i]), "MLP input must be finite", RTA_E_ARG);
     Layer& L = *layers[layer];
     RTA_CUDA(cudaMemcpyAsync(scratch_x.p, x, static_cast<size_t>(rows) * D * 4, cudaMemcpyHostToDevice, stream));
+    if (L.mlp_fmt == kQ4KPanel || L.mlp_fmt == kQ6KPanel) {  // tensor-core handle: all rows in one pair
+      GemvArgs gu;
+      gu.fmt = L.mlp_fmt;
+      gu.w0 = L.gate;
+      gu.w1 = L.up;
+      gu.rows = F;
+      gu.cols = D;
+      gu.x = scratch_x.p;
+      gu.x_stride = D;
+      gu.batch = rows;
+      gu.epilogue = kSwiGLU;
+      gu.y = scratch_y.p;
+      gu.y_stride = F;
+      GemvArgs dn;
+      dn.fmt = L.down_fmt;
+      dn.w0 = L.down;
+      dn.rows = D;
+      dn.cols = F;
+      dn.x = scratch_y.p;
+      dn.x_stride = F;
+      dn.batch = rows;
+      dn.y = scratch_x.p;  // x no longer needed
+      dn.y_stride = D;
+      mlp_pair(gu, dn, true, stream);
+      RTA_CUDA(cudaMemcpyAsync(a, scratch_y.p, static_cast<size_t>(rows) * F * 4, cudaMemcpyDeviceToHost, stream));
+      RTA_CUDA(cudaMemcpyAsync(y, scratch_x.p, static_cast<size_t>(rows) * D * 4, cudaMemcpyDeviceToHost, stream));
+      RTA_CUDA(cudaStreamSynchronize(stream));
+      return;
+    }
     for (uint32_t r0 = 0; r0 < rows; r0 += 8) {  // 8-row launches keep the activation tables in shared memory
       const uint32_t nb = std::min(8u, rows - r0);
       GemvArgs gu;
@@ -1041,7 +1163,7 @@ struct Engine {
     r.x = scratch_x.p;
     r.y = logits ? lg.p : nullptr;
     r.argmax = key;
-    RTA_CUDA(launch_gemv(r, stream));
+    RTA_CUDA(matmul(r, stream));
     unsigned long long k = 0;
     RTA_CUDA(cudaMemcpyAsync(&k, key, 8, cudaMemcpyDeviceToHost, stream));
     if (logits) RTA_CUDA(cudaMemcpyAsync(logits, lg.p, V * 4ull, cudaMemcpyDeviceToHost, stream));
@@ -1307,6 +1429,7 @@ rta_status rta_model_resources(rta_model* m, uint64_t* out, size_t n) {
       e.kernels_per_prefill,
       e.position,
       e.nseq,
+      e.panel_matrices,
   };
   for (size_t i = 0; i < n && i < sizeof(v) / sizeof(v[0]); ++i) out[i] = v[i];
   return RTA_OK;

@@ -60,7 +60,8 @@ namespace tc {
 constexpr uint32_t kThreads = 576;  // 18 warps
 constexpr uint32_t kTileRows = 128;
 constexpr uint32_t kQ4KPanel = 128u * kQ4KBytes, kQ6KPanel = 128u * kQ6KBytes;  // 18432, 26880
-constexpr uint32_t kAStages = 3, kBStages = 4;
+constexpr uint32_t kAStages = 3, kScaleSlots = 4;  // tensor-memory A stages; block-scale ring slots
+__host__ __device__ constexpr uint32_t b_stages(uint32_t N) { return N <= 32u ? 8u : 4u; }  // activation ring
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kAColBase = 256, kA2ColBase = 448;  // tensor-memory columns of the A / A2 stages
 constexpr uint32_t kMinSmem = 120u * 1024u;             // keeps one CTA per SM (tensor memory is taken whole)
@@ -210,14 +211,34 @@ __device__ __forceinline__ void q4_scale_min(const uint4& h, uint32_t G, uint32_
   }
 }
 
+// Code bytes of row m that one dequantizing thread (j) needs for one half
+// block column (h): loaded for both halves as soon as the panel lands, so the
+// shared-memory latency overlaps the previous half's arithmetic.
+struct Q4Words {
+  uint4 c0, c1;  // GGUF code bytes 16 + 32*pl .. +31, pl = 2h + j
+};
+struct Q6Words {
+  uint4 l0, l1;  // ql bytes 64h + 32j .. +31
+  uint4 g0, g1;  // qh bytes 128 + 32h .. +31
+};
+__device__ __forceinline__ Q4Words load_q4(const uint8_t* panel, uint32_t m, uint32_t h, uint32_t j) {
+  const uint32_t pl = 2u * h + j;
+  return {*reinterpret_cast<const uint4*>(panel + ((pl * 2u + 0u) * 128u + m) * 16u),
+          *reinterpret_cast<const uint4*>(panel + ((pl * 2u + 1u) * 128u + m) * 16u)};
+}
+__device__ __forceinline__ Q6Words load_q6(const uint8_t* panel, uint32_t m, uint32_t h, uint32_t j) {
+  const uint8_t* base = panel + h * 12288u;
+  return {*reinterpret_cast<const uint4*>(base + ((j * 2u + 0u) * 128u + m) * 16u),
+          *reinterpret_cast<const uint4*>(base + ((j * 2u + 1u) * 128u + m) * 16u),
+          *reinterpret_cast<const uint4*>(base + 8192u + m * 16u),
+          *reinterpret_cast<const uint4*>(base + 8192u + (128u + m) * 16u)};
+}
+
 // Row m's 64 coefficients 128h + 64j .. +63 of one Q4_K panel -> 32 tensor-
 // memory columns (fp16 pairs sc*q), plus (h == 0, j == 0) the 8 mins columns.
-__device__ __forceinline__ void dequant_q4(const uint8_t* panel, uint32_t m, uint32_t h, uint32_t j, uint32_t tcol,
+__device__ __forceinline__ void dequant_q4(const Q4Words& cw, const uint4& hdr, uint32_t h, uint32_t j, uint32_t tcol,
                                            uint32_t a2col) {
-  const uint4 hdr = *reinterpret_cast<const uint4*>(panel + 16384u + 16u * m);
   const uint32_t pl = 2u * h + j;
-  const uint4 c0 = *reinterpret_cast<const uint4*>(panel + ((pl * 2u + 0u) * 128u + m) * 16u);
-  const uint4 c1 = *reinterpret_cast<const uint4*>(panel + ((pl * 2u + 1u) * 128u + m) * 16u);
   uint32_t sc0, mn0, sc1, mn1;
   q4_scale_min(hdr, 2u * pl, sc0, mn0);
   q4_scale_min(hdr, 2u * pl + 1u, sc1, mn1);
@@ -225,7 +246,7 @@ __device__ __forceinline__ void dequant_q4(const uint8_t* panel, uint32_t m, uin
   // high nibbles hold 1024 + 16q: (1024+16q)*(sc/16) - 64*sc.  Both exact.
   const __half2 s0 = __float2half2_rn(static_cast<float>(sc0)), k0 = __float2half2_rn(-1024.f * sc0);
   const __half2 s1 = __float2half2_rn(static_cast<float>(sc1) * 0.0625f), k1 = __float2half2_rn(-64.f * sc1);
-  const uint32_t words[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+  const uint32_t words[8] = {cw.c0.x, cw.c0.y, cw.c0.z, cw.c0.w, cw.c1.x, cw.c1.y, cw.c1.z, cw.c1.w};
   uint32_t lo[16], hi[16];
 #pragma unroll
   for (int w = 0; w < 8; ++w) {
@@ -253,46 +274,43 @@ __device__ __forceinline__ void dequant_q4(const uint8_t* panel, uint32_t m, uin
 
 // Row m's coefficients 128h + 32j + 0..31 and 128h + 64 + 32j + 0..31 of one
 // Q6_K panel -> tensor-memory columns 16j.. and 32 + 16j.. (fp16 sc*(q-32)).
-__device__ __forceinline__ void dequant_q6(const uint8_t* panel, uint32_t m, uint32_t h, uint32_t j, uint32_t tcol) {
-  const uint8_t* base = panel + h * 12288u;
-  const uint4 l0 = *reinterpret_cast<const uint4*>(base + ((j * 2u + 0u) * 128u + m) * 16u);
-  const uint4 l1 = *reinterpret_cast<const uint4*>(base + ((j * 2u + 1u) * 128u + m) * 16u);
-  const uint4 g0 = *reinterpret_cast<const uint4*>(base + 8192u + m * 16u);
-  const uint4 g1 = *reinterpret_cast<const uint4*>(base + 8192u + (128u + m) * 16u);
-  const uint4 s4 = *reinterpret_cast<const uint4*>(panel + 24576u + 16u * m);
-  const uint32_t qlw[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
-  const uint32_t qhw[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-  auto scale = [&](uint32_t i) -> int {  // int8 scale i (0..15) of the block
-    const uint32_t w = i < 4u ? s4.x : i < 8u ? s4.y : i < 12u ? s4.z : s4.w;
-    return static_cast<int>(static_cast<int8_t>((w >> (8u * (i & 3u))) & 0xFFu));
-  };
-  // x = 0x6400 | 16q is 1024 + 16q; (1024 + 16q)*(sc/16) - 96*sc = sc*(q-32)
+// Each fp16 pair is assembled by one bit-select of two byte permutes: the
+// nibble (at bits 4-7) and the 0x64 exponent byte from the ql permute, the
+// two high bits (at bits 8-9) from the permute of the pre-shifted qh word:
+// 0x6400 | 16q = 1024 + 16q, then (1024 + 16q)*(sc/16) - 96*sc = sc*(q-32).
+__device__ __forceinline__ void dequant_q6(const Q6Words& cw, const uint4& s4, uint32_t h, uint32_t j,
+                                           uint32_t tcol) {
+  const uint32_t qlw[8] = {cw.l0.x, cw.l0.y, cw.l0.z, cw.l0.w, cw.l1.x, cw.l1.y, cw.l1.z, cw.l1.w};
+  const uint32_t qhw[8] = {cw.g0.x, cw.g0.y, cw.g0.z, cw.g0.w, cw.g1.x, cw.g1.y, cw.g1.z, cw.g1.w};
+  // int8 scales 8h + 2j + u (low run) and 8h + 4 + 2j + u (high run), u = 0, 1:
+  // bytes 2j + u of word h*2 and of word h*2 + 1
+  const uint32_t wl = h ? s4.z : s4.x, wh = h ? s4.w : s4.y;
   __half2 sl[2], kl[2], sh[2], kh[2];
 #pragma unroll
   for (uint32_t u = 0; u < 2u; ++u) {
-    const int a = scale(8u * h + 2u * j + u), b = scale(8u * h + 4u + 2u * j + u);
-    sl[u] = __float2half2_rn(static_cast<float>(a) * 0.0625f);
-    kl[u] = __float2half2_rn(-96.f * static_cast<float>(a));
-    sh[u] = __float2half2_rn(static_cast<float>(b) * 0.0625f);
-    kh[u] = __float2half2_rn(-96.f * static_cast<float>(b));
+    const float a = static_cast<float>(static_cast<int8_t>((wl >> (8u * (2u * j + u))) & 0xFFu));
+    const float b = static_cast<float>(static_cast<int8_t>((wh >> (8u * (2u * j + u))) & 0xFFu));
+    sl[u] = __float2half2_rn(a * 0.0625f);
+    kl[u] = __float2half2_rn(-96.f * a);
+    sh[u] = __float2half2_rn(b * 0.0625f);
+    kh[u] = __float2half2_rn(-96.f * b);
   }
-  const uint32_t lshift = 2u * j, hshift = 4u + 2u * j;
+  constexpr uint32_t kSel = 0xFCF0FCF0u;  // bits taken from the ql permute
   uint32_t lo[16], hi[16];
 #pragma unroll
   for (int w = 0; w < 8; ++w) {
-    const uint32_t qs = qlw[w] << 4;  // low nibbles moved to bits 4-7 of each byte
+    const uint32_t qs = qlw[w] << 4;               // low-run nibbles to bits 4-7 of each byte
+    const uint32_t hl = qhw[w] >> (2u * j);        // low-run high bits to bits 0-1 of each byte
+    const uint32_t hh = qhw[w] >> (4u + 2u * j);   // high-run high bits to bits 0-1 of each byte
     const uint32_t u = static_cast<uint32_t>(w) / 4u;  // first / second 16 coefficients of the run
 #pragma unroll
     for (int pr = 0; pr < 2; ++pr) {
       const uint32_t sel_l = pr == 0 ? 0x5140u : 0x5342u;  // bytes (2pr, 2pr+1) -> low byte of each half
       const uint32_t sel_h = pr == 0 ? 0x1404u : 0x3424u;  // the same bytes -> high byte of each half
-      const uint32_t lq = __byte_perm(qs, 0x64646464u, sel_l) & 0xFFF0FFF0u;
-      const uint32_t hq = __byte_perm(qlw[w], 0x64646464u, sel_l) & 0xFFF0FFF0u;
-      const uint32_t qh = __byte_perm(qhw[w], 0u, sel_h);
-      const uint32_t xl = lq | ((qh >> lshift) & 0x03000300u);
-      const uint32_t xh = hq | ((qh >> hshift) & 0x03000300u);
-      lo[2 * w + pr] = hfma2_bits(xl, sl[u], kl[u]);
-      hi[2 * w + pr] = hfma2_bits(xh, sh[u], kh[u]);
+      const uint32_t al = __byte_perm(qs, 0x64646464u, sel_l), ah = __byte_perm(qlw[w], 0x64646464u, sel_l);
+      const uint32_t bl = __byte_perm(hl, 0u, sel_h), bh = __byte_perm(hh, 0u, sel_h);
+      lo[2 * w + pr] = hfma2_bits((al & kSel) | (bl & ~kSel), sl[u], kl[u]);
+      hi[2 * w + pr] = hfma2_bits((ah & kSel) | (bh & ~kSel), sh[u], kh[u]);
     }
   }
   tmem_st16(tcol + 16u * j, lo);
@@ -306,6 +324,7 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 18 warps: 5
   constexpr bool kQ4 = C::kQ4;
   constexpr uint32_t kPanel = C::kPanel, kRawS = C::kRawStages;
   constexpr uint32_t kDStride = kQ4 ? 2u * N : static_cast<uint32_t>(N);  // tensor-memory columns per accumulator pair
+  constexpr uint32_t kBStages = b_stages(N);
   static_assert(2u * kDStride <= kAColBase, "accumulators overlap the A stages");
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.off_bar);
@@ -317,11 +336,16 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 18 warps: 5
   uint64_t* a_empty = a_full + kAStages;
   uint64_t* d_full = a_empty + kAStages;
   uint64_t* d_empty = d_full + 2;
-  uint64_t* drain = d_empty + 2;
+  uint64_t* sc_full = d_empty + 2;
+  uint64_t* sc_empty = sc_full + kScaleSlots;
+  uint64_t* drain = sc_empty + kScaleSlots;
   uint32_t* misc = reinterpret_cast<uint32_t*>(smem + p.off_misc);
   volatile uint32_t* tmem_slot = misc;
   volatile uint32_t* abort_flag = misc + 1;
   unsigned long long* cand = reinterpret_cast<unsigned long long*>(misc + 4);  // [N] argmax candidates
+  // block scales of the 128 rows per block column, handed from the dequantizers
+  // to the epilogue: Q4_K (d, dmin) fp16 pair, Q6_K d
+  uint32_t* sc_ring = misc + 4 + 2 * N;  // [kScaleSlots][128]
 
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   if (threadIdx.x == 0) {
@@ -340,6 +364,10 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 18 warps: 5
     for (uint32_t s = 0; s < 2; ++s) {
       mbar_init(&d_full[s], 1);
       mbar_init(&d_empty[s], 8);
+    }
+    for (uint32_t s = 0; s < kScaleSlots; ++s) {
+      mbar_init(&sc_full[s], 4);   // the four j == 0 dequantizing warps
+      mbar_init(&sc_empty[s], 8);  // the eight epilogue warps
     }
     mbar_init(drain, 1);
     fence_mbar_init();
@@ -467,21 +495,18 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 18 warps: 5
     bool stop = false;
     for (uint32_t i = 0; i < my_tiles && !stop; ++i) {
       const uint32_t t = blockIdx.x + i * gridDim.x, mat = t / tiles_per_mat, mt = t % tiles_per_mat;
-      const uint8_t* wbase = (mat ? p.w[1] : p.w[0]) + static_cast<size_t>(mt) * p.KB * kPanel;
       float acc[NH];
 #pragma unroll
       for (int n = 0; n < NH; ++n) acc[n] = 0.f;
-      // block scales of row m: Q4_K (d, dmin) at the header, Q6_K d after the scales
-      auto scales = [&](uint32_t kb) -> uint32_t {
-        const uint8_t* pn = wbase + static_cast<size_t>(kb) * kPanel;
-        return kQ4 ? *reinterpret_cast<const uint32_t*>(pn + 16384u + 16u * m)
-                   : static_cast<uint32_t>(*reinterpret_cast<const unsigned short*>(pn + 26624u + 2u * m));
-      };
-      uint32_t sc_next = scales(0);
       for (uint32_t kb = 0; kb < p.KB; ++kb, ++blk) {
-        const uint32_t sc = sc_next;
-        if (kb + 1u < p.KB) sc_next = scales(kb + 1u);
-        const uint32_t buf = blk & 1u;
+        const uint32_t buf = blk & 1u, slot = blk % kScaleSlots;
+        if (!warp_wait(&sc_full[slot], (blk / kScaleSlots) & 1u, p.err, abort_flag)) {
+          stop = true;
+          break;
+        }
+        const uint32_t sc = sc_ring[slot * 128u + m];
+        __syncwarp();
+        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&sc_empty[slot])) : "memory");
         if (!warp_wait(&d_full[buf], (blk >> 1) & 1u, p.err, abort_flag)) {
           stop = true;
           break;
@@ -539,16 +564,45 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 18 warps: 5
     // ---------------------------------------------------------- dequantizers
     const uint32_t q = warp & 3u, j = (warp - 10u) >> 2, m = 32u * q + lane;
     const uint32_t lane_addr = (32u * q) << 16;
-    uint32_t rit = 0, ait = 0;
+    uint32_t rit = 0, ait = 0, blk = 0;
     bool stop = false;
     for (uint32_t i = 0; i < my_tiles && !stop; ++i) {
-      for (uint32_t kb = 0; kb < p.KB && !stop; ++kb) {
+      for (uint32_t kb = 0; kb < p.KB && !stop; ++kb, ++blk) {
         const uint32_t rs = rit % kRawS;
         if (!warp_wait(&raw_full[rs], (rit / kRawS) & 1u, p.err, abort_flag)) {
           stop = true;
           break;
         }
         const uint8_t* panel = raw + rs * kPanel;
+        // everything this thread needs from the panel, then the panel is released
+        uint4 hdr;  // Q4_K block header / Q6_K int8 scales of row m
+        uint32_t scale_word;
+        Q4Words c4[2];
+        Q6Words c6[2];
+        if constexpr (kQ4) {
+          hdr = *reinterpret_cast<const uint4*>(panel + 16384u + 16u * m);
+          scale_word = hdr.x;  // d, dmin
+          c4[0] = load_q4(panel, m, 0u, j);
+          c4[1] = load_q4(panel, m, 1u, j);
+        } else {
+          hdr = *reinterpret_cast<const uint4*>(panel + 24576u + 16u * m);
+          scale_word = *reinterpret_cast<const unsigned short*>(panel + 26624u + 2u * m);  // d
+          c6[0] = load_q6(panel, m, 0u, j);
+          c6[1] = load_q6(panel, m, 1u, j);
+        }
+        __syncwarp();
+        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&raw_empty[rs])) : "memory");
+        ++rit;
+        if (j == 0u) {  // hand the row's block scales to the epilogue
+          const uint32_t slot = blk % kScaleSlots;
+          if (!warp_wait(&sc_empty[slot], ((blk / kScaleSlots) & 1u) ^ 1u, p.err, abort_flag)) {
+            stop = true;
+            break;
+          }
+          sc_ring[slot * 128u + m] = scale_word;
+          __syncwarp();
+          if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&sc_full[slot])) : "memory");
+        }
         for (uint32_t h = 0; h < 2u; ++h) {
           const uint32_t as = ait % kAStages;
           if (!warp_wait(&a_empty[as], ((ait / kAStages) & 1u) ^ 1u, p.err, abort_flag)) {
@@ -559,9 +613,9 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 18 warps: 5
           const uint32_t tcol = tmem + lane_addr + kAColBase + 64u * as;
           if constexpr (kQ4) {
             const uint32_t a2 = (h == 0u && j == 0u) ? tmem + lane_addr + kA2ColBase + 8u * as : 0u;
-            dequant_q4(panel, m, h, j, tcol, a2);
+            dequant_q4(c4[h], hdr, h, j, tcol, a2);
           } else {
-            dequant_q6(panel, m, h, j, tcol);
+            dequant_q6(c6[h], hdr, h, j, tcol);
           }
           tmem_wait_st();
           tc_fence_before();
@@ -569,9 +623,6 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 18 warps: 5
           if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&a_full[as])) : "memory");
           ++ait;
         }
-        __syncwarp();
-        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&raw_empty[rs])) : "memory");
-        ++rit;
       }
     }
     if (stop) *abort_flag = 1u;
@@ -689,6 +740,19 @@ __global__ void __launch_bounds__(256) tc_prep_kernel(const Prep p) {
   }
 }
 
+// act[r][c] = swiglu(gu[r][c], gu[r][F + c]) (op 2 kind 3's epilogue, for the
+// callers that need the activation rows themselves).
+__global__ void swiglu_rows_kernel(const float* __restrict__ gu, uint32_t rows, uint32_t F, uint32_t gu_stride,
+                                   float* __restrict__ act, uint32_t act_stride) {
+  const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= static_cast<size_t>(rows) * F) return;
+  const uint32_t r = static_cast<uint32_t>(i / F), c = static_cast<uint32_t>(i % F);
+  const float gv = gu[static_cast<size_t>(r) * gu_stride + c], uv = gu[static_cast<size_t>(r) * gu_stride + F + c];
+  const float amp = fabsf(gv) * fabsf(uv) * detector_sigmoid(gv);
+  const float sgn = (gv > 0.f ? 1.f : gv < 0.f ? -1.f : 0.f) * (uv > 0.f ? 1.f : uv < 0.f ? -1.f : 0.f);
+  act[static_cast<size_t>(r) * act_stride + c] = sgn * amp;
+}
+
 // ------------------------------------------------------------- panel tiler
 // grid (KB, rows / 128); one panel per CTA.
 template <int FMT>
@@ -744,9 +808,9 @@ cudaError_t launch_n(const tc::Params& p0, const tc::Prep& pr, uint32_t grid, bo
   p.b_stage = (static_cast<uint32_t>(N) * 256u + (C::kQ4 ? static_cast<uint32_t>(N) * 32u : 0u) + 1023u) / 1024u * 1024u;
   p.off_b = C::kRawStages * C::kPanel;
   p.off_b = (p.off_b + 1023u) / 1024u * 1024u;
-  p.off_bar = p.off_b + tc::kBStages * p.b_stage;
-  p.off_misc = p.off_bar + 256u;
-  uint32_t smem = p.off_misc + 16u + 8u * static_cast<uint32_t>(N);
+  p.off_bar = p.off_b + tc::b_stages(N) * p.b_stage;
+  p.off_misc = p.off_bar + 512u;
+  uint32_t smem = p.off_misc + 16u + 8u * static_cast<uint32_t>(N) + tc::kScaleSlots * 128u * 4u;
   smem = smem < tc::kMinSmem ? tc::kMinSmem : smem;
   auto kernel = tc::tc_gemm_kernel<FMT, N>;
   static int attr_done[64] = {0};
@@ -867,6 +931,14 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
+}
+
+cudaError_t launch_swiglu_rows(const float* gu, uint32_t rows, uint32_t F, uint32_t gu_stride, float* act,
+                               uint32_t act_stride, cudaStream_t s) {
+  if (!gu || !act || rows == 0 || F == 0) return cudaErrorInvalidValue;
+  const size_t n = static_cast<size_t>(rows) * F;
+  tc::swiglu_rows_kernel<<<static_cast<uint32_t>((n + 255) / 256), 256, 0, s>>>(gu, rows, F, gu_stride, act, act_stride);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_tile_tc(int fmt, const uint8_t* src, uint32_t rows, uint32_t cols, uint8_t* dst, cudaStream_t s) {

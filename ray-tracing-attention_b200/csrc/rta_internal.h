@@ -116,6 +116,9 @@ struct TcGemmArgs {
 };
 size_t tc_workspace_bytes(int fmt, uint32_t batch, uint32_t cols);
 cudaError_t launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s);
+// act[r][c] = swiglu(gu[r][c], gu[r][F + c]) for r < rows, c < F.
+cudaError_t launch_swiglu_rows(const float* gu, uint32_t rows, uint32_t F, uint32_t gu_stride, float* act,
+                               uint32_t act_stride, cudaStream_t s);
 // GGUF rows of a Q4_K / Q6_K matrix (rows % 128 == 0) -> panel layout.
 cudaError_t launch_tile_tc(int fmt, const uint8_t* src, uint32_t rows, uint32_t cols, uint8_t* dst, cudaStream_t s);
 // Dense F32 GEMV for the tiny recurrent alpha/beta projections.

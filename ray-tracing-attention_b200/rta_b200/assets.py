@@ -76,14 +76,14 @@ class Spec:
 
 
 def spec_2b() -> Spec:
-    """24 layers [rec, rec, rec, full] x 6, D 2048, F 6144, 16q/4kv x 256,
+    """benchmark config 4: 24 layers [rec, rec, rec, full] x 6, D 2048, F 6144, 16q/4kv x 256,
     16 recurrent heads (16 key heads) x 128, V 151936; rotary 64 of 256 (Qwen3.5 partial rotary)."""
     return Spec("qwen35", 2048, 6144, 151936, ("recurrent", "recurrent", "recurrent", "full") * 6, 16, 4, 256, 64,
                 state_heads=16, state_key_heads=16)
 
 
 def spec_9b() -> Spec:
-    """32 layers (3:1), D 4096, F 12288, 16q/4kv x 256, 32 recurrent heads
+    """benchmark config 5: 32 layers (3:1), D 4096, F 12288, 16q/4kv x 256, 32 recurrent heads
     over 16 key heads x 128, V 151936."""
     return Spec("qwen35", 4096, 12288, 151936, ("recurrent", "recurrent", "recurrent", "full") * 8, 16, 4, 256, 64,
                 state_heads=32, state_key_heads=16)

@@ -57,7 +57,7 @@ _SIGS = {
 PACKET_HISTORY = 1  # RTA_MODEL_PACKET_HISTORY
 RESOURCE_NAMES = ("payload_bytes", "derived_layer_bytes", "history_bytes", "recurrent_state_bytes", "capacity",
                   "attention_splits", "kernels_per_decode_step", "kernels_per_prefill_step", "position",
-                  "sequences")
+                  "sequences", "tensor_core_matrices")
 
 
 def _lib_model():

@@ -1,6 +1,6 @@
 """Sequence sharding of a ragged decode batch over the GPUs of one box.
 
-BASELINE config 5 decodes 64 independent sequences whose histories are drawn
+benchmark config 5 decodes 64 independent sequences whose histories are drawn
 uniformly from [128, 8192].  Sequences share nothing but the weights, so the
 batch shards by sequence with no collective on the data path: every rank owns
 a disjoint set of sequences on its own GPU, with the weights replicated.  The

@@ -131,7 +131,7 @@ def main() -> None:
                         activation=act, output=y, shape=np.array([D, F]))
     manifest["sources"]["mlp_q4k.npz"] = "verify_rt_mlp.py:85-89 expression, FP64, gguf-decoded Q4_K weights"
 
-    # 4. Geometry of the BASELINE shapes.
+    # 4. Geometry of the benchmark shapes.
     manifest["spec_2b"] = {"history_bytes": spec.history_bytes, "fingerprint": spec.fingerprint,
                            "feed_forward_stride": spec.feed_forward_stride, "working_width": spec.working_width}
     s9 = spec_9b(ModelSpec)

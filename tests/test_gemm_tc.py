@@ -83,26 +83,28 @@ def dequant_q4_host(P, m, h, j):
 
 
 def dequant_q6_host(P, m, h, j):
-    """Emulates dequant_q6: columns 16j.. (low run) and 32 + 16j.. (high run) of row m."""
+    """Emulates dequant_q6: columns 16j.. (low run) and 32 + 16j.. (high run) of row m
+    (bit-select of the ql permute and the permute of the pre-shifted qh word)."""
     base = 12288 * h
     ql = np.concatenate([P[base + ((j * 2 + p) * 128 + m) * 16:base + ((j * 2 + p) * 128 + m) * 16 + 16]
                          for p in range(2)])
     qh = np.concatenate([P[base + 8192 + (p * 128 + m) * 16:base + 8192 + (p * 128 + m) * 16 + 16] for p in range(2)])
-    sc = P[24576 + 16 * m:24576 + 16 * m + 16].view(np.int8).astype(np.int64)
+    s4 = words(P[24576 + 16 * m:24576 + 16 * m + 16])
+    wl, wh = (s4[2], s4[3]) if h else (s4[0], s4[1])
+    int8 = lambda word, i: ((word >> (8 * i)) & 0xFF) - 256 * (((word >> (8 * i)) & 0xFF) > 127)
     qlw, qhw = words(ql), words(qh)
+    sel = 0xFCF0FCF0
     lo, hi = [], []
     for w in range(8):
         u = w // 4
-        a, b = sc[8 * h + 2 * j + u], sc[8 * h + 4 + 2 * j + u]
+        a, b = int8(wl, 2 * j + u), int8(wh, 2 * j + u)
         qs = (qlw[w] << 4) & 0xFFFFFFFF
+        hl, hh = qhw[w] >> (2 * j), qhw[w] >> (4 + 2 * j)
         for sel_l, sel_h in ((0x5140, 0x1404), (0x5342, 0x3424)):
-            lq = byte_perm(qs, 0x64646464, sel_l) & 0xFFF0FFF0
-            hq = byte_perm(qlw[w], 0x64646464, sel_l) & 0xFFF0FFF0
-            qhp = byte_perm(qhw[w], 0, sel_h)
-            xl = lq | ((qhp >> (2 * j)) & 0x03000300)
-            xh = hq | ((qhp >> (4 + 2 * j)) & 0x03000300)
-            lo += list(hfma2(xl, a * 0.0625, -96.0 * a))
-            hi += list(hfma2(xh, b * 0.0625, -96.0 * b))
+            al, ah = byte_perm(qs, 0x64646464, sel_l), byte_perm(qlw[w], 0x64646464, sel_l)
+            bl, bh = byte_perm(hl, 0, sel_h), byte_perm(hh, 0, sel_h)
+            lo += list(hfma2((al & sel) | (bl & ~sel & 0xFFFFFFFF), a * 0.0625, -96.0 * a))
+            hi += list(hfma2((ah & sel) | (bh & ~sel & 0xFFFFFFFF), b * 0.0625, -96.0 * b))
     return np.array(lo), np.array(hi)
 
 

@@ -80,7 +80,7 @@ def test_gemv_rejects_bad_shapes(ops):
 
 
 def test_mlp_config1_parity(ops):
-    """SwiGLU MLP, hidden 2048, intermediate 6144, Q4_K, batch 1."""
+    """benchmark config 1: SwiGLU MLP, hidden 2048, intermediate 6144, Q4_K, batch 1."""
     D, F = 2048, 6144
     rng = np.random.default_rng(20261110)
     mats = [oracle.quantize(12, rng.normal(0, 0.02, n).astype(np.float32)) for n in (F * D, F * D, D * F)]
@@ -110,7 +110,7 @@ def test_mlp_matches_reference_fp64_expression(ops, golden):
 
 @pytest.mark.parametrize("batch", [1, 4])
 def test_readout_config3_parity(ops, batch):
-    """LM head 151936 x 2048 Q6_K, logits + argmax."""
+    """benchmark config 3: LM head 151936 x 2048 Q6_K, logits + argmax."""
     V, D = 151936, 2048
     rng = np.random.default_rng(31 + batch)
     W = oracle.quantize(14, rng.normal(0, 0.02, V * D).astype(np.float32))

@@ -1,11 +1,14 @@
-"""GPU tests of the multi-sequence engine (ragged batch).
+"""GPU tests of the multi-sequence engine (ragged batch, benchmark config 5).
 
 A handle with S sequences decodes one token per running sequence per step.
-Every batched kernel runs the single-sequence arithmetic for each sequence, so
-each sequence must produce exactly the tokens and the residual state of a
-single-sequence handle fed the same prompt: compared bit for bit here, with
-ragged prompt lengths, a per-sequence stop, more than 8 sequences (several GEMV
-launches per step) and seeded synthetic histories.
+Below 16 sequences every batched kernel runs the single-sequence arithmetic for
+each sequence, so each sequence must produce exactly the tokens and the
+residual state of a single-sequence handle fed the same prompt: compared bit
+for bit here, with ragged prompt lengths, a per-sequence stop, more than 8
+sequences (several GEMV launches per step) and seeded synthetic histories.
+From 16 sequences on the products run on the tensor cores (fp16-rounded
+activations, fp32 accumulation): those handles are held to the oracle within
+the north-star tolerance, tokens compared wherever the top-2 margin exceeds it.
 """
 import numpy as np
 import pytest
@@ -97,4 +100,71 @@ def test_seeded_histories_decode():
     assert res["position"] == 105
     again = batch.generate_batch(3)
     assert all(len(g) == 3 for g in again)
+    batch.close()
+
+
+TOL = 1e-3  # relative L2
+
+
+def test_tensor_core_batch_tracks_the_oracle():
+    """18 sequences: every matrix on the tensor cores.  Per sequence: greedy tokens
+    equal the oracle's wherever the oracle's top-2 margin exceeds the tolerance
+    (the first legitimate near-tie flip ends the comparison, as in the
+    single-sequence tests)."""
+    import torch
+    from oracle.model import OracleModel
+    from rta_b200 import assets
+    from rta_b200.model import ResidentModel
+    spec = small_spec(kinds=("recurrent", "full"))
+    layout = assets.plan(spec, 9)
+    mats, basis = assets.generate_device(layout, 9)
+    params = layout.params()
+    batch = ResidentModel.from_payloads(spec, params, mats, basis, 32, sequences=18)
+    m, b = mats.cpu().numpy(), basis.cpu().numpy()
+    del mats, basis
+    torch.cuda.empty_cache()
+    res = batch.resources()
+    assert res["tensor_core_matrices"] == 2 * 5 + 1  # (in/qkvg, out/o, gate, up, down) x 2 layers + LM head
+    rng = np.random.default_rng(9)
+    prompts = [rng.integers(0, spec.vocabulary_size, int(n)) for n in rng.integers(1, 10, 18)]
+    batch.prefill_batch(prompts)
+    got = batch.generate_batch(6)
+    compared = 0
+    for z in (0, 1, 9, 17):
+        ref = OracleModel(spec, params, m, b, 32)
+        ref.prefill(prompts[z])
+        want, margins = ref.generate(6)
+        for i in range(min(len(got[z]), len(want))):
+            if margins[i] > TOL:
+                assert got[z][i] == want[i], (z, i, got[z], want, margins)
+                compared += 1
+            if got[z][i] != want[i]:
+                break
+    assert compared >= 8
+    batch.close()
+
+
+def test_tensor_core_batch_diagnostics_match_the_oracle():
+    """mlp (worker op 6) and vocabulary (op 4) on a tensor-core handle."""
+    import torch
+    from conftest import rel_l2
+    from oracle import oracle
+    from rta_b200 import assets
+    from rta_b200.model import ResidentModel
+    spec = small_spec(kinds=("recurrent", "full"))
+    layout = assets.plan(spec, 10)
+    mats, basis = assets.generate_device(layout, 10)
+    params = layout.params()
+    batch = ResidentModel.from_payloads(spec, params, mats, basis, 32, sequences=16)
+    m = mats.cpu().numpy()
+    del mats, basis
+    torch.cuda.empty_cache()
+    t = {x.name: x for x in layout.matrices}
+    rng = np.random.default_rng(10)
+    x = rng.normal(0, 0.5, (5, spec.hidden_size)).astype(np.float32)
+    y, act = batch.mlp(x, 1)
+    g, u, d = (t[f"blk.1.ffn_{n}.weight"] for n in ("gate", "up", "down"))
+    wg, wu, wd = (m[w.offset:w.offset + w.nbytes] for w in (g, u, d))
+    want_act, want_y = oracle.mlp(g.fmt, wg, wu, wd, spec.hidden_size, spec.middle_size, x)
+    assert rel_l2(act, want_act) < TOL and rel_l2(y, want_y) < TOL
     batch.close()

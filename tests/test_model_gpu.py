@@ -124,7 +124,7 @@ def test_engine_mlp_and_vocabulary_ops():
 
 
 def test_engine_2b_shape_decodes():
-    """BASELINE config 4 shape (random init): prefill, a few greedy steps vs the oracle."""
+    """benchmark config 4 shape (random init): prefill, a few greedy steps vs the oracle."""
     from rta_b200 import assets
     spec = assets.spec_2b()
     model, ref = build(spec, 11, capacity=64)

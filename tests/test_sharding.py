@@ -1,5 +1,5 @@
 """Host logic of the multi-GPU paths, on CPU: the sequence-sharding plan of the
-ragged batch and the max-over-ranks timing reduction of
+ragged batch (benchmark config 5) and the max-over-ranks timing reduction of
 bench.py, including a world_size-2 run over the gloo backend."""
 import os
 
