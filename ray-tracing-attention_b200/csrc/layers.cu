@@ -173,15 +173,19 @@ __global__ void __launch_bounds__(256) attn_prep_kernel(PrepParams p) {
 // decay = exp(-exp(A_log) * softplus(a + dt_bias)), beta = sigmoid(b) from the
 // RMS-normed layer input; 4-tap causal conv + SiLU; L2-normalised q, k; and the
 // gated delta rule s <- s*decay; r = k.s; s += k*(v - r)*beta; o = (q/sqrt(128)).s
-// on a [128 value x 128 key] fp32 state per head.  Grid (head, value slice).
+// on a [128 value x 128 key] fp32 state per head.  Grid (head, value slice,
+// sequence), ROWS value rows per CTA.
 //
 // Latency layout: the kernel is a short chain of dependent steps, so everything
 // that does not depend on the preceding kernels (this CTA's state rows, the
 // gate / norm / conv weights, the conv history) is requested before
 // griddepcontrol.wait -- state rows into registers, the rest into L2 -- and the
-// block reductions carry several values per barrier.
-constexpr uint32_t kGdnRows = 16;                 // value rows per CTA
-constexpr uint32_t kGdnRowsPerWarp = kGdnRows / 8u;
+// block reductions carry several values per barrier.  A few sequences split
+// each head's rows over 8 CTAs (16 rows: parallelism for one token); many
+// sequences give each (sequence, head) one CTA of all 128 rows, so the gates,
+// norms and convolutions (64 KB of L2 reads over x and the gate rows) are
+// computed once per head instead of once per slice.
+constexpr uint32_t kGdnRowsSmall = 16, kGdnRowsBatch = 128;
 
 __device__ __forceinline__ float signed_product_sum(float a0, float a1, float a2, float a3, float b0, float b1,
                                                     float b2, float b3) {
@@ -222,7 +226,9 @@ __device__ __forceinline__ void prefetch_l2(const void* ptr) {
   asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr));
 }
 
+template <uint32_t ROWS>
 __global__ void __launch_bounds__(256) gdn_kernel(GdnParams p) {
+  constexpr uint32_t kGdnRows = ROWS, kGdnRowsPerWarp = ROWS / 8u;
   __shared__ float red1[8], red2[16], red3[16];
   __shared__ float qn[128], kn[128], vv[kGdnRows];
   const uint32_t h = blockIdx.x, slice = blockIdx.y, z = blockIdx.z, tid = threadIdx.x;
@@ -387,8 +393,11 @@ cudaError_t launch_attn_prep(const PrepParams& p, cudaStream_t s, bool pdl) {
 }
 cudaError_t launch_gdn(const GdnParams& p, cudaStream_t s, bool pdl) {
   void* args[] = {const_cast<GdnParams*>(&p)};
-  return launch_pdl(reinterpret_cast<const void*>(gdn_kernel), dim3(p.H, 128u / kGdnRows, p.nseq), dim3(256), args,
-                    s, pdl);
+  if (p.H * p.nseq >= 2u * 148u)  // enough (sequence, head) pairs to fill the GPU with whole heads
+    return launch_pdl(reinterpret_cast<const void*>(gdn_kernel<kGdnRowsBatch>), dim3(p.H, 1, p.nseq), dim3(256),
+                      args, s, pdl);
+  return launch_pdl(reinterpret_cast<const void*>(gdn_kernel<kGdnRowsSmall>),
+                    dim3(p.H, 128u / kGdnRowsSmall, p.nseq), dim3(256), args, s, pdl);
 }
 cudaError_t launch_gather_rows(const uint8_t* src, const uint32_t* map, uint32_t rows, uint32_t row_bytes,
                                uint8_t* dst, cudaStream_t s) {

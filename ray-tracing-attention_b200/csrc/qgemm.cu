@@ -79,6 +79,7 @@ __host__ __device__ constexpr uint32_t blk_bytes(bool q4, uint32_t N) { return N
 struct Params {
   const uint8_t* w[2];  // panels of matrix 0 / 1 (rows appended after matrix 0's in the output)
   uint32_t nmat, rows, KB, ntiles;
+  uint32_t ksplit;  // K slices per tile: work unit = (tile, slice); > 1 only for the residual epilogue
   const uint8_t* xb;  // prep output
   uint32_t blk;       // prep bytes per block
   uint32_t batch;     // live batch rows of this launch (<= N)
@@ -387,8 +388,16 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 18 warps: 5
   const uint32_t tmem = *tmem_slot;
   pdl_launch_dependents();
 
-  const uint32_t my_tiles = blockIdx.x < p.ntiles ? (p.ntiles - blockIdx.x + gridDim.x - 1u) / gridDim.x : 0u;
+  // work units (tile, K slice), walked in the same order by every role
+  const uint32_t nunits = p.ntiles * p.ksplit;
+  const uint32_t my_tiles = blockIdx.x < nunits ? (nunits - blockIdx.x + gridDim.x - 1u) / gridDim.x : 0u;
   const uint32_t tiles_per_mat = p.rows / kTileRows;
+  auto unit = [&](uint32_t i, uint32_t& t, uint32_t& kb0, uint32_t& kb1) {
+    const uint32_t u = blockIdx.x + i * gridDim.x, sl = u % p.ksplit;
+    t = u / p.ksplit;
+    kb0 = sl * p.KB / p.ksplit;
+    kb1 = (sl + 1u) * p.KB / p.ksplit;
+  };
   uint8_t* raw = smem;
   uint8_t* bst = smem + p.off_b;
   const uint32_t b_bytes0 = static_cast<uint32_t>(N) * 256u + (kQ4 ? static_cast<uint32_t>(N) * 32u : 0u);
@@ -402,9 +411,11 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 18 warps: 5
       bool stop = false;
       pdl_wait();  // the activation stages are written by the preceding prep kernel
       for (uint32_t i = 0; i < my_tiles && !stop; ++i) {
-        const uint32_t t = blockIdx.x + i * gridDim.x, mat = t / tiles_per_mat, mt = t % tiles_per_mat;
+        uint32_t t, kb0, kb1;
+        unit(i, t, kb0, kb1);
+        const uint32_t mat = t / tiles_per_mat, mt = t % tiles_per_mat;
         const uint8_t* wbase = (mat ? p.w[1] : p.w[0]) + static_cast<size_t>(mt) * p.KB * kPanel;
-        for (uint32_t kb = 0; kb < p.KB && !stop; ++kb) {
+        for (uint32_t kb = kb0; kb < kb1 && !stop; ++kb) {
           const uint32_t rs = rit % kRawS;
           if (*abort_flag || !mbar_wait(&raw_empty[rs], ((rit / kRawS) & 1u) ^ 1u, p.err)) {
             stop = true;
@@ -448,7 +459,9 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 18 warps: 5
       bool stop = false;
       const uint32_t b0 = smem_u32(bst);
       for (uint32_t i = 0; i < my_tiles && !stop; ++i) {
-        for (uint32_t kb = 0; kb < p.KB && !stop; ++kb, ++blk) {
+        uint32_t t, kb0, kb1;
+        unit(i, t, kb0, kb1);
+        for (uint32_t kb = kb0; kb < kb1 && !stop; ++kb, ++blk) {
           const uint32_t buf = blk & 1u;
           if (*abort_flag || !mbar_wait(&d_empty[buf], ((blk >> 1) & 1u) ^ 1u, p.err)) {
             stop = true;
@@ -494,11 +507,13 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 18 warps: 5
     uint32_t blk = 0;
     bool stop = false;
     for (uint32_t i = 0; i < my_tiles && !stop; ++i) {
-      const uint32_t t = blockIdx.x + i * gridDim.x, mat = t / tiles_per_mat, mt = t % tiles_per_mat;
+      uint32_t t, kb0, kb1;
+      unit(i, t, kb0, kb1);
+      const uint32_t mat = t / tiles_per_mat, mt = t % tiles_per_mat;
       float acc[NH];
 #pragma unroll
       for (int n = 0; n < NH; ++n) acc[n] = 0.f;
-      for (uint32_t kb = 0; kb < p.KB; ++kb, ++blk) {
+      for (uint32_t kb = kb0; kb < kb1; ++kb, ++blk) {
         const uint32_t buf = blk & 1u, slot = blk % kScaleSlots;
         if (!warp_wait(&sc_full[slot], (blk / kScaleSlots) & 1u, p.err, abort_flag)) {
           stop = true;
@@ -543,7 +558,9 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 18 warps: 5
         if (p.running && p.running[static_cast<size_t>(n) * p.run_step] == 0u) continue;  // stopped sequence
         if (p.y) {
           float* yp = p.y + static_cast<size_t>(n) * p.y_stride + R;
-          if (p.epilogue == kAccumulate)
+          if (p.ksplit > 1u)  // partial sum of one K slice into the residual
+            atomicAdd(yp, acc[i]);
+          else if (p.epilogue == kAccumulate)
             *yp += acc[i];
           else
             *yp = acc[i];
@@ -567,7 +584,9 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 18 warps: 5
     uint32_t rit = 0, ait = 0, blk = 0;
     bool stop = false;
     for (uint32_t i = 0; i < my_tiles && !stop; ++i) {
-      for (uint32_t kb = 0; kb < p.KB && !stop; ++kb, ++blk) {
+      uint32_t t, kb0, kb1;
+      unit(i, t, kb0, kb1);
+      for (uint32_t kb = kb0; kb < kb1 && !stop; ++kb, ++blk) {
         const uint32_t rs = rit % kRawS;
         if (!warp_wait(&raw_full[rs], (rit / kRawS) & 1u, p.err, abort_flag)) {
           stop = true;
@@ -885,8 +904,15 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const uint32_t nmat = a.w1 ? 2u : 1u, ntiles = nmat * (a.rows / tc::kTileRows);
-  const uint32_t grid = ntiles < static_cast<uint32_t>(sms) ? ntiles : static_cast<uint32_t>(sms);
+  const uint32_t nmat = a.w1 ? 2u : 1u, ntiles = nmat * (a.rows / tc::kTileRows), KB = a.cols / 256u;
+  // Residual products with fewer tiles than SMs split K over CTAs (each slice
+  // at least 2 blocks) and add their partial sums atomically; stores and the
+  // argmax need whole sums.
+  uint32_t ksplit = 1;
+  if (a.epilogue == kAccumulate && !a.argmax)
+    while (ntiles * ksplit < static_cast<uint32_t>(sms) && KB / (ksplit + 1u) >= 2u) ++ksplit;
+  const uint32_t units = ntiles * ksplit;
+  const uint32_t grid = units < static_cast<uint32_t>(sms) ? units : static_cast<uint32_t>(sms);
   // batch rows run in launches of at most kTcMaxN (each streams the weights once)
   for (uint32_t b0 = 0; b0 < a.batch; b0 += kTcMaxN) {
     const uint32_t nb = a.batch - b0 < kTcMaxN ? a.batch - b0 : kTcMaxN;
@@ -915,6 +941,7 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
     p.rows = a.rows;
     p.KB = a.cols / 256u;
     p.ntiles = ntiles;
+    p.ksplit = ksplit;
     p.xb = a.xb;
     p.blk = pr.blk;
     p.batch = nb;
