@@ -108,7 +108,10 @@ struct Prep {
   uint8_t* xb;
   uint32_t blk;
   bool q4;
+  float* zero_y;  // split stores: y rows of live sequences are zeroed here before the partial sums land
+  uint32_t zero_cols, zero_stride;
 };
+constexpr uint32_t kPrepCols = 2048;  // activation columns per prep CTA (grid: batch rows x column chunks)
 
 // ------------------------------------------------------------- tcgen05 glue
 __device__ __forceinline__ uint32_t h2_bits(__half2 h) {
@@ -558,7 +561,7 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 18 warps: 5
         if (p.running && p.running[static_cast<size_t>(n) * p.run_step] == 0u) continue;  // stopped sequence
         if (p.y) {
           float* yp = p.y + static_cast<size_t>(n) * p.y_stride + R;
-          if (p.ksplit > 1u)  // partial sum of one K slice into the residual
+          if (p.ksplit > 1u)  // partial sum of one K slice (into the residual, or into zeroed rows)
             atomicAdd(yp, acc[i]);
           else if (p.epilogue == kAccumulate)
             *yp += acc[i];
@@ -662,15 +665,23 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 18 warps: 5
 }
 
 // -------------------------------------------------------- activation prep
-// Batch row n (one CTA): prologue, x -> fp16 in the K-major core-matrix layout
-// of the activation stages, and (Q4_K) the fp32 32-group sums as fp16 hi / lo.
-// Rows past the batch, or of stopped sequences, are written as zeros.
+// Batch row n, columns [kPrepCols*blockIdx.y, +kPrepCols) (one CTA): prologue,
+// x -> fp16 in the K-major core-matrix layout of the activation stages, and
+// (Q4_K) the fp32 32-group sums of the fp16 x as fp16 hi / lo.  Rows past the
+// batch, or of stopped sequences, are written as zeros.  The RMS norm's sum
+// runs over the whole row in every chunk (an L2-resident re-read).
 __global__ void __launch_bounds__(256) tc_prep_kernel(const Prep p) {
   __shared__ float red[8];
   const uint32_t n = blockIdx.x, tid = threadIdx.x, lane = tid & 31u;
   pdl_wait();
   pdl_launch_dependents();
   const bool live = n < p.batch && (!p.running || p.running[static_cast<size_t>(n) * p.run_step] != 0u);
+  if (live && p.zero_y) {  // this chunk's share of the output row
+    const uint32_t per = (p.zero_cols + gridDim.y - 1u) / gridDim.y;
+    const uint32_t a = blockIdx.y * per, b = min(p.zero_cols, a + per);
+    float* yr = p.zero_y + static_cast<size_t>(n) * p.zero_stride;
+    for (uint32_t c = a + tid; c < b; c += 256u) yr[c] = 0.f;
+  }
   const float* xr = p.x + static_cast<size_t>(n < p.batch ? n : 0u) * p.x_stride;
   const float* zr = p.z ? p.z + static_cast<size_t>(n < p.batch ? n : 0u) * p.z_stride : nullptr;
   const uint32_t nch = p.cols / 8u;
@@ -691,7 +702,8 @@ __global__ void __launch_bounds__(256) tc_prep_kernel(const Prep p) {
     inv = rsqrtf(t / static_cast<float>(p.cols) + p.eps);
   }
   const uint32_t N = p.N;
-  for (uint32_t c = tid; c < nch; c += 256u) {  // a warp covers 32 consecutive chunks (cols % 256 == 0)
+  const uint32_t c_end = min(nch, (blockIdx.y + 1u) * (kPrepCols / 8u));
+  for (uint32_t c = blockIdx.y * (kPrepCols / 8u) + tid; c < c_end; c += 256u) {  // a warp: 32 consecutive 8-chunks
     float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     if (live) {
       const float4 a = reinterpret_cast<const float4*>(xr)[2u * c];
@@ -847,7 +859,7 @@ cudaError_t launch_n(const tc::Params& p0, const tc::Prep& pr, uint32_t grid, bo
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(pr.N);
+  cfg.gridDim = dim3(pr.N, (pr.cols + tc::kPrepCols - 1u) / tc::kPrepCols);
   cfg.blockDim = dim3(256);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = s;
@@ -905,12 +917,20 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
   if (e != cudaSuccess) return e;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const uint32_t nmat = a.w1 ? 2u : 1u, ntiles = nmat * (a.rows / tc::kTileRows), KB = a.cols / 256u;
-  // Residual products with fewer tiles than SMs split K over CTAs (each slice
-  // at least 2 blocks) and add their partial sums atomically; stores and the
-  // argmax need whole sums.
+  // K splits: each CTA walks its share of (tile, K slice) units; the slice
+  // count minimises the block columns of the busiest CTA plus one block of
+  // fixed cost per unit.  Partial sums land atomically (residual products add
+  // into y, stores into rows the prep kernel zeroes); the argmax needs whole sums.
   uint32_t ksplit = 1;
-  if (a.epilogue == kAccumulate && !a.argmax)
-    while (ntiles * ksplit < static_cast<uint32_t>(sms) && KB / (ksplit + 1u) >= 2u) ++ksplit;
+  if (!a.argmax && a.y) {
+    uint64_t best = ~0ull;
+    for (uint32_t ks = 1; ks <= 8u && ks <= KB; ++ks) {
+      const uint64_t units = static_cast<uint64_t>(ntiles) * ks;
+      const uint64_t per_cta = (units + sms - 1) / sms;
+      const uint64_t cost = per_cta * ((KB + ks - 1) / ks + 1);
+      if (cost < best) best = cost, ksplit = ks;
+    }
+  }
   const uint32_t units = ntiles * ksplit;
   const uint32_t grid = units < static_cast<uint32_t>(sms) ? units : static_cast<uint32_t>(sms);
   // batch rows run in launches of at most kTcMaxN (each streams the weights once)
@@ -934,6 +954,11 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
     pr.xb = a.xb;
     pr.blk = tc::blk_bytes(q4, pr.N);
     pr.q4 = q4;
+    if (ksplit > 1u && a.epilogue == kStore) {
+      pr.zero_y = a.y + static_cast<size_t>(b0) * a.y_stride;
+      pr.zero_cols = nmat * a.rows;
+      pr.zero_stride = a.y_stride;
+    }
     tc::Params p = {};
     p.w[0] = a.w0;
     p.w[1] = a.w1 ? a.w1 : a.w0;
