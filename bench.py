@@ -231,6 +231,79 @@ class MLPWorkload(Workload):
                 "sample": f"{n} full config-1 MLP steps (C restatement of resident_math.comp op 2, OpenMP)"}
 
 
+class GemmWorkload(Workload):
+    """The tensor-core batched product alone (rta_gemm_tc): one 9B-shape projection
+    (default: the 12288 x 4096 Q4_K gate) at a decode batch, weights in panel order,
+    rotating weight copies larger than L2.  Kernel-level measurement for the ragged
+    batch (benchmark config 5) projections; not a benchmark config of its own."""
+    name, metric, unit, dtype = ("gemm", "tensor-core batched product rows/s (Q4_K/Q6_K panel x fp16 batch)",
+                                 "batch-rows/s", "fp16-tcgen05-f32acc")
+    launches_per_step = 3  # memset, prep, tcgen05 kernel
+
+    def __init__(self, seed=20261207, batch=64, rows=12288, cols=4096, fmt=12):
+        import torch
+        from rta_b200 import ops
+        self.ops, self.torch = ops, torch
+        self.B, self.R, self.K, self.gf = batch, rows, cols, fmt
+        self.wbytes = rows * cols // 256 * (144 if fmt == 12 else 210)
+        self.copies = _rotations(self.wbytes)
+        self.w = []
+        for c in range(self.copies):
+            code, w = ops.panel_weights(fmt, ops.synthetic_blocks(fmt, rows, cols, seed + c), rows, cols)
+            self.w.append(w)
+        self.fmt = code
+        tile_n = 16 if batch <= 16 else 32 if batch <= 32 else 64
+        self.dominant = f"tc_gemm_kernel<{'Q4_K' if fmt == 12 else 'Q6_K'},{tile_n}>"
+        self.x = ops.synthetic_normal(batch * cols, seed + 99).reshape(batch, cols)
+        self.y = torch.empty(batch, rows, device="cuda")
+        self.ws = torch.empty(ops._lib.load().rta_gemm_tc_workspace_bytes(code, batch, cols), dtype=torch.uint8,
+                              device="cuda")
+        self.hx = torch.empty(batch * cols, dtype=torch.float32).pin_memory()
+        self.hx.copy_(self.x.reshape(-1).cpu())
+        self.hy = torch.empty(batch * rows, dtype=torch.float32).pin_memory()
+
+    def step(self, i):
+        self.ops.gemm_tc(self.fmt, self.w[i % self.copies], self.R, self.K, self.x, y=self.y, workspace=self.ws)
+
+    dominant_launch = step
+
+    def dominant_bytes(self):
+        return self.wbytes + self.B * (self.K + self.R) * 4
+
+    def units_per_step(self):
+        return float(self.B)
+
+    def e2e_step(self, i):
+        self.x.view(-1).copy_(self.hx, non_blocking=True)
+        self.step(i)
+        self.hy.copy_(self.y.view(-1), non_blocking=True)
+
+    def e2e_bytes(self):
+        return self.B * self.K * 4, self.B * self.R * 4
+
+    def algorithmic_bytes_step(self):
+        return self.dominant_bytes()
+
+    def config(self):
+        return {"workload": f"gemm_{'q4k' if self.gf == 12 else 'q6k'}_{self.R}x{self.K}_b{self.B}", "rows": self.R,
+                "cols": self.K, "batch": self.B, "format": "Q4_K" if self.gf == 12 else "Q6_K",
+                "layout": "panel (rta_panel_weights, once before timing)",
+                "l2": f"rotating {self.copies} weight copies (> L2 per pass)"}
+
+    def cpu_baseline(self, budget_s):
+        from oracle import oracle
+        rng = np.random.default_rng(0)
+        W = oracle.quantize(self.gf, rng.normal(0, 0.02, self.R * self.K).astype(np.float32))
+        x = rng.normal(0, 1, (self.B, self.K)).astype(np.float32)
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < budget_s or n == 0:
+            oracle.gemv(self.gf, W, self.R, self.K, x)
+            n += 1
+        dt = time.perf_counter() - t0
+        return {"value": n * self.B / dt, "unit": self.unit, "cores": oracle.threads(), "kind": "port",
+                "sample": f"{n} full products of {self.B} rows (C restatement of resident_math.comp op 2, OpenMP)"}
+
+
 class LMHeadWorkload(Workload):
     """benchmark config 3: LM head 151936 x 2048 Q6_K, logits + per-row argmax, batch 1 or 64."""
     name, metric, unit, dtype, dominant = ("lmhead", "vocabulary readout tokens/s (151936x2048 Q6_K, logits+argmax)",
@@ -482,7 +555,7 @@ class RaggedBatchWorkload:
 
 
 WORKLOADS = {"mlp": MLPWorkload, "lmhead": LMHeadWorkload, "attention": AttentionWorkload,
-             "decode2b": DecodeWorkload, "ragged9b": RaggedBatchWorkload}
+             "decode2b": DecodeWorkload, "ragged9b": RaggedBatchWorkload, "gemm": GemmWorkload}
 
 
 def ragged_step_bytes(spec, layout, lengths, capacity):
@@ -711,7 +784,9 @@ def time_steps(fn, steps, warmup, world, graph=True, min_seconds=0.0):
 def run_ours(args, world, rank, local):
     import torch
     kw = {"history": args.history} if args.workload == "attention" else \
-        {"batch": args.batch} if args.workload == "lmhead" else {}
+        {"batch": args.batch} if args.workload == "lmhead" else \
+        {"batch": args.batch, "rows": args.rows, "cols": args.cols, "fmt": {"q4k": 12, "q6k": 14}[args.format]} \
+        if args.workload == "gemm" else {}
     wl = WORKLOADS[args.workload](**kw)
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
@@ -768,6 +843,8 @@ def run_reference(args, world, rank):
         wl.seed = 20261201
     if args.workload == "lmhead":
         wl.B = args.batch
+    if args.workload == "gemm":
+        wl.B, wl.R, wl.K, wl.gf = args.batch, args.rows, args.cols, {"q4k": 12, "q6k": 14}[args.format]
     budget = max(1.0, args.cpu_budget / max(args.steps, 1))
     vals = []
     for _ in range(args.warmup + args.steps):
@@ -777,7 +854,8 @@ def run_reference(args, world, rank):
     base = dict(vals[-1], value=v)
     cfg = {"mlp": {"workload": "config1_swiglu_mlp_b1"}, "lmhead": {"workload": f"config3_lmhead_b{args.batch}"},
            "attention": {"workload": f"config2_gqa_decode_L{args.history}"},
-           "decode2b": {"workload": "config4_2b_hybrid_decode_b1"}}[args.workload]
+           "decode2b": {"workload": "config4_2b_hybrid_decode_b1"},
+           "gemm": {"workload": f"gemm_{args.format}_{args.rows}x{args.cols}_b{args.batch}"}}[args.workload]
     return {"impl": "reference", "metric": cls.metric, "value": v, "unit": cls.unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "dtype": "f32",
             "data": "synthetic (seeded, benchmark shapes)", "config": cfg,
@@ -829,7 +907,11 @@ def main():
     ap.add_argument("--min-seconds", type=float, default=1.0,
                     help="repeat the timed K-step region for at least this long (clock sampling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--batch", type=int, default=1, help="lmhead: hidden rows per readout (config 3: 1 or 64)")
+    ap.add_argument("--batch", type=int, default=1,
+                    help="lmhead: hidden rows per readout (config 3: 1 or 64); gemm: batch rows")
+    ap.add_argument("--rows", type=int, default=12288, help="gemm: weight rows (multiple of 128)")
+    ap.add_argument("--cols", type=int, default=4096, help="gemm: weight columns (multiple of 256)")
+    ap.add_argument("--format", choices=("q4k", "q6k"), default="q4k", help="gemm: weight format")
     ap.add_argument("--prompt", type=int, default=512,
                     help="decode2b: prompt length before the timed tokens (short prompts keep profiler runs small)")
     args = ap.parse_args()

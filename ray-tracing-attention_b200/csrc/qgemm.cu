@@ -31,9 +31,11 @@
 //     = qh bytes 128 + 32h + 16part .. +15; then scales [row 128][16 int8],
 //     then d [row 128][fp16].
 //
-// One persistent CTA per SM (576 threads) walks 128-row tiles:
-//   warp 0      bulk-copies each tile's panels (one copy per block column) and
-//               the activation stage of each 128-wide K step
+// One persistent CTA per SM (608 threads) walks (128-row tile, K slice) units:
+//   warp 0      bulk-copies each tile's panels (one copy per block column),
+//               from kernel start (weights do not depend on earlier kernels)
+//   warp 18     bulk-copies the activation stage of each 128-wide K step, after
+//               griddepcontrol.wait (written by the preceding prep kernel)
 //   warps 10-17 dequantize the panel into tensor memory (A operand; thread =
 //               row, tcgen05.st), two warps per 32-lane quarter (warp % 4)
 //   warp 1      issues tcgen05.mma kind::f16 M=128 N=batch K=16 (A from tensor
@@ -57,7 +59,7 @@
 namespace rta {
 namespace tc {
 
-constexpr uint32_t kThreads = 576;  // 18 warps
+constexpr uint32_t kThreads = 608;  // 19 warps
 constexpr uint32_t kTileRows = 128;
 constexpr uint32_t kQ4KPanel = 128u * kQ4KBytes, kQ6KPanel = 128u * kQ6KBytes;  // 18432, 26880
 constexpr uint32_t kAStages = 3, kScaleSlots = 4;  // tensor-memory A stages; block-scale ring slots
@@ -323,7 +325,7 @@ __device__ __forceinline__ void dequant_q6(const Q6Words& cw, const uint4& s4, u
 
 // ---------------------------------------------------------------- the kernel
 template <int FMT, int N>
-__global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 18 warps: 5 per sub-partition x 96 x 32 <= 16384
+__global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 19 warps: <= 5 per sub-partition x 96 x 32 <= 16384
   using C = Cfg<FMT>;
   constexpr bool kQ4 = C::kQ4;
   constexpr uint32_t kPanel = C::kPanel, kRawS = C::kRawStages;
@@ -407,12 +409,13 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 18 warps: 5
   const uint32_t b_bytes1 = static_cast<uint32_t>(N) * 256u;
 
   if (warp == 0) {
-    // ------------------------------------------------------------ producer
+    // ----------------------------------------------- weight panel producer
+    // Weights never depend on earlier kernels: their copies start at once, so
+    // the dequantizers fill tensor memory while the prep kernel still runs.
     if (lane == 0) {
       const uint64_t policy = evict_first_policy();
-      uint32_t rit = 0, bit = 0;  // copies issued into the raw / activation rings
+      uint32_t rit = 0;  // copies issued into the raw ring
       bool stop = false;
-      pdl_wait();  // the activation stages are written by the preceding prep kernel
       for (uint32_t i = 0; i < my_tiles && !stop; ++i) {
         uint32_t t, kb0, kb1;
         unit(i, t, kb0, kb1);
@@ -427,6 +430,27 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 18 warps: 5
           mbar_expect_tx(&raw_full[rs], kPanel);
           bulk_g2s_stream(raw + rs * kPanel, wbase + static_cast<size_t>(kb) * kPanel, kPanel, &raw_full[rs], policy);
           ++rit;
+        }
+      }
+      if (stop) {
+        *abort_flag = 1u;
+        // bounded drain: the last copy into each stage has landed before the CTA exits
+        for (uint32_t s = 0; s < kRawS; ++s) {
+          const uint32_t n = rit / kRawS + (s < rit % kRawS ? 1u : 0u);
+          if (n) (void)mbar_wait(&raw_full[s], (n - 1u) & 1u, nullptr);
+        }
+      }
+    }
+  } else if (warp == 18) {
+    // ------------------------------------------- activation stage producer
+    if (lane == 0) {
+      uint32_t bit = 0;  // copies issued into the activation ring
+      bool stop = false;
+      pdl_wait();  // the activation stages are written by the preceding prep kernel
+      for (uint32_t i = 0; i < my_tiles && !stop; ++i) {
+        uint32_t t, kb0, kb1;
+        unit(i, t, kb0, kb1);
+        for (uint32_t kb = kb0; kb < kb1 && !stop; ++kb)
           for (uint32_t h = 0; h < 2u; ++h) {
             const uint32_t bs = bit % kBStages;
             if (*abort_flag || !mbar_wait(&b_empty[bs], ((bit / kBStages) & 1u) ^ 1u, p.err)) {
@@ -439,15 +463,9 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 18 warps: 5
             bulk_g2s(bst + bs * p.b_stage, p.xb + off, bytes, &b_full[bs]);
             ++bit;
           }
-        }
       }
       if (stop) {
         *abort_flag = 1u;
-        // bounded drain: the last copy into each stage has landed before the CTA exits
-        for (uint32_t s = 0; s < kRawS; ++s) {
-          const uint32_t n = rit / kRawS + (s < rit % kRawS ? 1u : 0u);
-          if (n) (void)mbar_wait(&raw_full[s], (n - 1u) & 1u, nullptr);
-        }
         for (uint32_t s = 0; s < kBStages; ++s) {
           const uint32_t n = bit / kBStages + (s < bit % kBStages ? 1u : 0u);
           if (n) (void)mbar_wait(&b_full[s], (n - 1u) & 1u, nullptr);
@@ -580,7 +598,7 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 18 warps: 5
       }
     }
     if (stop) *abort_flag = 1u;
-  } else {
+  } else if (warp >= 10 && warp < 18) {
     // ---------------------------------------------------------- dequantizers
     const uint32_t q = warp & 3u, j = (warp - 10u) >> 2, m = 32u * q + lane;
     const uint32_t lane_addr = (32u * q) << 16;
