@@ -411,9 +411,10 @@ struct Engine {
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
     // History splits per (sequence, KV head): one sequence needs sms / kvh of them
     // to fill the GPU; many sequences fill it by themselves, and then a few
-    // splits (about four waves of CTAs in all) keep the ragged lengths balanced
-    // without paying every split's fixed cost (query load, combine, record, merge).
-    const uint32_t fill = (4u * static_cast<uint32_t>(sms) + spec.kv_heads * nseq - 1u) / (spec.kv_heads * nseq);
+    // splits (about eight waves of CTAs in all) keep the longest histories' CTAs
+    // short next to the ragged mean without paying every split's fixed cost
+    // (query load, combine, record, merge) for the short ones.
+    const uint32_t fill = (8u * static_cast<uint32_t>(sms) + spec.kv_heads * nseq - 1u) / (spec.kv_heads * nseq);
     nsplit = std::max(1u, std::min({static_cast<uint32_t>(sms) / spec.kv_heads, capacity / 256u, fill}));
     const size_t recs = static_cast<size_t>(nseq) * spec.kv_heads * nsplit * 4;
     part_m.alloc(recs);

@@ -354,10 +354,37 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 19 warps: <
   uint32_t* sc_ring = misc + 4 + 2 * N;  // [kScaleSlots][128]
 
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+  // work units (tile, K slice), walked in the same order by every role
+  const uint32_t nunits = p.ntiles * p.ksplit;
+  const uint32_t my_tiles = blockIdx.x < nunits ? (nunits - blockIdx.x + gridDim.x - 1u) / gridDim.x : 0u;
+  const uint32_t tiles_per_mat = p.rows / kTileRows;
+  auto unit = [&](uint32_t i, uint32_t& t, uint32_t& kb0, uint32_t& kb1) {
+    const uint32_t u = blockIdx.x + i * gridDim.x, sl = u % p.ksplit;
+    t = u / p.ksplit;
+    kb0 = sl * p.KB / p.ksplit;
+    kb1 = (sl + 1u) * p.KB / p.ksplit;
+  };
+  uint8_t* raw = smem;
+  // Thread 0 initialises the barriers and is also the panel producer: its first
+  // kRawS copies (free stages, no wait) leave before the block-wide set-up.
+  uint32_t early = 0;  // panel copies issued before the set-up (thread 0)
   if (threadIdx.x == 0) {
     for (uint32_t s = 0; s < kRawS; ++s) {
       mbar_init(&raw_full[s], 1);
       mbar_init(&raw_empty[s], 8);
+    }
+    fence_mbar_init();
+    const uint64_t policy = evict_first_policy();
+    for (uint32_t i = 0; i < my_tiles && early < kRawS; ++i) {
+      uint32_t t, kb0, kb1;
+      unit(i, t, kb0, kb1);
+      const uint32_t mat = t / tiles_per_mat, mt = t % tiles_per_mat;
+      const uint8_t* wbase = (mat ? p.w[1] : p.w[0]) + static_cast<size_t>(mt) * p.KB * kPanel;
+      for (uint32_t kb = kb0; kb < kb1 && early < kRawS; ++kb, ++early) {
+        mbar_expect_tx(&raw_full[early], kPanel);
+        bulk_g2s_stream(raw + early * kPanel, wbase + static_cast<size_t>(kb) * kPanel, kPanel, &raw_full[early],
+                        policy);
+      }
     }
     for (uint32_t s = 0; s < kBStages; ++s) {
       mbar_init(&b_full[s], 1);
@@ -392,18 +419,6 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 19 warps: <
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   pdl_launch_dependents();
-
-  // work units (tile, K slice), walked in the same order by every role
-  const uint32_t nunits = p.ntiles * p.ksplit;
-  const uint32_t my_tiles = blockIdx.x < nunits ? (nunits - blockIdx.x + gridDim.x - 1u) / gridDim.x : 0u;
-  const uint32_t tiles_per_mat = p.rows / kTileRows;
-  auto unit = [&](uint32_t i, uint32_t& t, uint32_t& kb0, uint32_t& kb1) {
-    const uint32_t u = blockIdx.x + i * gridDim.x, sl = u % p.ksplit;
-    t = u / p.ksplit;
-    kb0 = sl * p.KB / p.ksplit;
-    kb1 = (sl + 1u) * p.KB / p.ksplit;
-  };
-  uint8_t* raw = smem;
   uint8_t* bst = smem + p.off_b;
   const uint32_t b_bytes0 = static_cast<uint32_t>(N) * 256u + (kQ4 ? static_cast<uint32_t>(N) * 32u : 0u);
   const uint32_t b_bytes1 = static_cast<uint32_t>(N) * 256u;
@@ -423,6 +438,10 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 19 warps: <
         const uint8_t* wbase = (mat ? p.w[1] : p.w[0]) + static_cast<size_t>(mt) * p.KB * kPanel;
         for (uint32_t kb = kb0; kb < kb1 && !stop; ++kb) {
           const uint32_t rs = rit % kRawS;
+          if (rit < early) {  // issued before the set-up
+            ++rit;
+            continue;
+          }
           if (*abort_flag || !mbar_wait(&raw_empty[rs], ((rit / kRawS) & 1u) ^ 1u, p.err)) {
             stop = true;
             break;
@@ -571,15 +590,18 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 19 warps: <
         if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&d_empty[buf])) : "memory");
       }
       if (stop) break;
-      const uint32_t R = mat * p.rows + mt * kTileRows + m;  // output row
+      const uint32_t R0 = mat * p.rows + mt * kTileRows, R = R0 + m;  // output rows of the tile, this thread's
 #pragma unroll
       for (int i = 0; i < NH; ++i) {
         const uint32_t n = c0 * NH + static_cast<uint32_t>(i);
         if (n >= p.batch) break;
         if (p.running && p.running[static_cast<size_t>(n) * p.run_step] == 0u) continue;  // stopped sequence
         if (p.y) {
+          // a warp's 32 rows of one batch column are one 128-byte line: scalar
+          // atomics of split partial sums cost one L2 line operation per warp
+          // instruction, as many as 16-byte vector or 512-byte bulk reductions
           float* yp = p.y + static_cast<size_t>(n) * p.y_stride + R;
-          if (p.ksplit > 1u)  // partial sum of one K slice (into the residual, or into zeroed rows)
+          if (p.ksplit > 1u)  // partial sum of one K slice (into the residual, or into rows the prep zeroed)
             atomicAdd(yp, acc[i]);
           else if (p.epilogue == kAccumulate)
             *yp += acc[i];
@@ -868,11 +890,11 @@ cudaError_t launch_n(const tc::Params& p0, const tc::Prep& pr, uint32_t grid, bo
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!attr_done[dev]) {
-    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return e;
     attr_done[dev] = 1;
   }
-  if (smem > 200u * 1024u) return cudaErrorInvalidConfiguration;
+  if (smem > 227u * 1024u) return cudaErrorInvalidConfiguration;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
@@ -985,6 +1007,7 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
     p.KB = a.cols / 256u;
     p.ntiles = ntiles;
     p.ksplit = ksplit;
+
     p.xb = a.xb;
     p.blk = pr.blk;
     p.batch = nb;
