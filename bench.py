@@ -7,9 +7,15 @@ Workloads (the benchmark configs, synthetic seeded inputs of the stated shapes):
   mlp       config 1: SwiGLU MLP 2048 -> 6144 -> 2048, Q4_K, batch 1
   attention config 2: GQA decode 16q/4kv, head_dim 256, fp16 KV, history --history (default 32768)
   lmhead    config 3: vocabulary readout 151936 x 2048 Q6_K, batch 1, logits + argmax
+  ragged9b  config 5: 9B-shape ragged batch of 64 sequences, sharded by sequence
+  gemm      the tensor-core batched product alone (--rows --cols --batch --format)
+  mlp_tp    the MLP split over the ranks (tensor parallel; --hidden --middle --batch)
+  lmhead_tp config 3's readout split over the ranks (tensor parallel; --batch)
 At N > 1 (torchrun, one process per GPU, NCCL) every rank runs the same
 workload on its own GPU (replicas: the decode of one sequence does not shard),
-the time is the max over ranks and `value` is the whole-job aggregate.
+except ragged9b (sequences sharded) and the *_tp workloads (one job split over
+the ranks, strong scaling); the time is the max over ranks and `value` is the
+whole-job aggregate.
 """
 from __future__ import annotations
 
@@ -536,6 +542,169 @@ class DecodeWorkload(Workload):
                           "through the model oracle (C restatement of the reference shader math, OpenMP)"}
 
 
+class MLPTPWorkload(Workload):
+    """The SwiGLU MLP split over the GPUs of one box (tensor parallel, strong
+    scaling): gate / up rows and down columns divided among the ranks
+    (rta_b200.tensor_parallel.ShardedMLP), the partial products and the residual
+    summed on every rank by one peer-memory exchange kernel
+    (rta_team_allreduce_f32).  Default shape: benchmark config 1 (2048-6144-2048
+    Q4_K, batch 1); --hidden 4096 --middle 12288 --batch 64 is config 5's MLP."""
+    name, unit, strong = "mlp_tp", "steps/s", True
+
+    def __init__(self, seed=20261110, batch=1, hidden=2048, middle=6144):
+        import torch
+        from rta_b200 import ops
+        from rta_b200 import tensor_parallel as tp
+        self.ops, self.torch, self.tp = ops, torch, tp
+        self.B, self.D, self.F = batch, hidden, middle
+        self.team = tp.Team(capacity_bytes=batch * hidden * 4)
+        world = self.team.world
+        self.local_cols = tp.split_units(middle, tp.MIDDLE_UNIT, world)[self.team.rank][1]
+        self.local_bytes = 3 * self.local_cols * hidden // 256 * 144
+        self.copies = _rotations(self.local_bytes)
+        self.mlps = []
+        for c in range(self.copies):
+            full = [ops.synthetic_blocks(12, middle, hidden, seed + 3 * c + j) for j in range(2)]
+            full.append(ops.synthetic_blocks(12, hidden, middle, seed + 3 * c + 2))
+            self.mlps.append(tp.ShardedMLP(self.team, 12, *full, hidden, middle, batch))
+            del full
+        self.tc = self.mlps[0].tc
+        self.metric = (f"SwiGLU MLP steps/s, tensor parallel (Q4_K, {hidden}-{middle}-{hidden}, batch {batch})")
+        self.dtype = "q4k-fp16-tcgen05-f32acc" if self.tc else "q4k-int8mma-f32acc"
+        # ours per step: (prep, tcgen05 kernel) x 2 per 64 rows (gate+up, down) or 2 GEMVs, plus the exchange
+        self.launches_per_step = (4 * ((batch + 63) // 64) if self.tc else 2) + 1
+        self.dominant = (f"local MLP slice ({self.local_cols} middle rows): "
+                         + ("tc_gemm_kernel<Q4_K> gate+up, down" if self.tc else "gemv_tiled_kernel<Q4_K> gate+up, down"))
+        self.x = ops.synthetic_normal(batch * hidden, seed + 999).reshape(batch, hidden)
+        self.res = ops.synthetic_normal(batch * hidden, seed + 998).reshape(batch, hidden)
+        self.y = torch.empty(batch, hidden, device="cuda")
+        self.hx = torch.empty(batch * hidden, dtype=torch.float32).pin_memory()
+        self.hx.copy_(self.x.reshape(-1).cpu())
+        self.hy = torch.empty(batch * hidden, dtype=torch.float32).pin_memory()
+
+    def step(self, i):
+        self.mlps[i % self.copies](self.x, residual=self.res, out=self.y)
+
+    def dominant_launch(self, i):
+        m = self.mlps[i % self.copies]
+        if m.tc:
+            self.ops.mlp_tc(m.code, m.wg, m.wu, m.wd, self.D, m.count, self.x, y=m.partial, workspace=m.workspace)
+        else:
+            self.ops.mlp_swiglu(m.code, m.wg, m.wu, m.wd, self.D, m.count, self.x, y=m.partial, act=m.act)
+
+    def dominant_bytes(self):
+        return self.local_bytes + self.B * (2 * self.D + 2 * self.local_cols) * 4
+
+    def units_per_step(self):
+        return 1.0
+
+    def e2e_step(self, i):
+        self.x.view(-1).copy_(self.hx, non_blocking=True)
+        self.step(i)
+        self.hy.copy_(self.y.view(-1), non_blocking=True)
+
+    def e2e_bytes(self):
+        return self.B * self.D * 4, self.B * self.D * 4
+
+    def config(self):
+        return {"workload": f"mlp_tp_{self.D}x{self.F}_b{self.B}", "hidden": self.D, "intermediate": self.F,
+                "format": "Q4_K", "batch": self.B, "split": f"{self.local_cols} middle rows on rank {self.team.rank}",
+                "layout": ("panel (tensor cores)" if self.tc else "tiled (GEMV)") + ", relaid once before timing",
+                "exchange": "rta_team_allreduce_f32: one kernel, NVLink peer stores, rank-order sum",
+                "l2": f"rotating {self.copies} weight copies (> L2 per pass)"}
+
+    def cpu_baseline(self, budget_s):
+        from oracle import oracle
+        rng = np.random.default_rng(0)
+        mats = [oracle.quantize(12, rng.normal(0, 0.02, self.F * self.D).astype(np.float32)) for _ in range(3)]
+        x = rng.normal(0, 1, (self.B, self.D)).astype(np.float32)
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < budget_s or n == 0:
+            oracle.mlp(12, *mats, self.D, self.F, x)
+            n += 1
+        dt = time.perf_counter() - t0
+        return {"value": n / dt, "unit": self.unit, "cores": oracle.threads(), "kind": "port",
+                "sample": f"{n} whole MLP steps of {self.B} rows, one process (the reference has no split; C "
+                          "restatement of resident_math.comp op 2, OpenMP)"}
+
+    def close(self):
+        self.team.close()
+
+
+class LMHeadTPWorkload(Workload):
+    """benchmark config 3's readout split over the GPUs of one box (tensor
+    parallel, strong scaling): vocabulary rows divided among the ranks
+    (rta_b200.tensor_parallel.ShardedReadout), each rank's best row merged by one
+    peer-memory exchange kernel (rta_team_argmax).  Argmax only (no logits)."""
+    name, unit, strong = "lmhead_tp", "tokens/s", True
+    V, D = 151936, 2048
+
+    def __init__(self, seed=31, batch=1):
+        import torch
+        from rta_b200 import ops
+        from rta_b200 import tensor_parallel as tp
+        self.ops, self.torch = ops, torch
+        self.B = batch
+        self.team = tp.Team(capacity_bytes=max(batch * 8, 16))
+        raw = ops.synthetic_blocks(14, self.V, self.D, seed)
+        self.head = tp.ShardedReadout(self.team, 14, raw, self.V, self.D, batch)
+        del raw
+        self.tc = self.head.tc
+        self.local_rows = self.head.count
+        self.metric = f"vocabulary readout tokens/s, tensor parallel (151936x2048 Q6_K, argmax, batch {batch})"
+        self.dtype = "q6k-fp16-tcgen05-f32acc" if self.tc else "q6k-int8mma-f32acc"
+        self.launches_per_step = ((batch + 63) // 64 * 2 + 1 if self.tc else (batch + 15) // 16 + 1) + 1
+        self.dominant = (f"local readout slice ({self.local_rows} rows): "
+                         + ("tc_gemm_kernel<Q6_K> + argmax" if self.tc else "gemv_tiled_kernel<Q6_K> + argmax"))
+        self.x = ops.synthetic_normal(batch * self.D, seed + 1).reshape(batch, self.D)
+        self.hx = torch.empty(batch * self.D, dtype=torch.float32).pin_memory()
+        self.hx.copy_(self.x.reshape(-1).cpu())
+        self.harg = torch.empty(batch, dtype=torch.int32).pin_memory()
+
+    def step(self, i):
+        self.last = self.head(self.x)
+
+    def dominant_launch(self, i):
+        self.head.local(self.x)
+
+    def dominant_bytes(self):
+        return self.local_rows * self.D // 256 * 210 + self.B * self.D * 4
+
+    def units_per_step(self):
+        return float(self.B)
+
+    def e2e_step(self, i):
+        self.x.view(-1).copy_(self.hx, non_blocking=True)
+        self.step(i)
+        self.harg.copy_(self.last[0].view(-1), non_blocking=True)
+
+    def e2e_bytes(self):
+        return self.B * self.D * 4, self.B * 4
+
+    def config(self):
+        return {"workload": f"lmhead_tp_b{self.B}", "vocab": self.V, "hidden": self.D, "format": "Q6_K",
+                "batch": self.B, "split": f"{self.local_rows} vocabulary rows on rank {self.team.rank}",
+                "layout": ("panel (tensor cores)" if self.tc else "tiled (GEMV)") + ", relaid once before timing",
+                "exchange": "rta_team_argmax: one kernel, NVLink peer stores", "l2": "weights 255 MB > L2"}
+
+    def cpu_baseline(self, budget_s):
+        from oracle import oracle
+        rng = np.random.default_rng(0)
+        W = oracle.quantize(14, rng.normal(0, 0.02, self.V * self.D).astype(np.float32))
+        x = rng.normal(0, 1, (self.B, self.D)).astype(np.float32)
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < budget_s or n == 0:
+            oracle.lmhead(14, W, self.V, self.D, x, want_logits=False)
+            n += 1
+        dt = time.perf_counter() - t0
+        return {"value": n * self.B / dt, "unit": self.unit, "cores": oracle.threads(), "kind": "port",
+                "sample": f"{n} whole readouts (argmax) of {self.B} rows, one process (C restatement of "
+                          "resident_math.comp ops 16/17, OpenMP)"}
+
+    def close(self):
+        self.team.close()
+
+
 def host_payloads(layout, seed):
     """Host-side payloads of the layout's shapes with random valid packed blocks
     (no GPU kernels involved: the CPU arms time the reference's CPU path only)."""
@@ -555,7 +724,8 @@ class RaggedBatchWorkload:
 
 
 WORKLOADS = {"mlp": MLPWorkload, "lmhead": LMHeadWorkload, "attention": AttentionWorkload,
-             "decode2b": DecodeWorkload, "ragged9b": RaggedBatchWorkload, "gemm": GemmWorkload}
+             "decode2b": DecodeWorkload, "ragged9b": RaggedBatchWorkload, "gemm": GemmWorkload,
+             "mlp_tp": MLPTPWorkload, "lmhead_tp": LMHeadTPWorkload}
 
 
 def ragged_step_bytes(spec, layout, lengths, capacity):
@@ -736,6 +906,8 @@ def run_decode(args, world, rank, local):
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = wl.cpu_baseline(args.cpu_budget)
+    if hasattr(wl, "close"):
+        wl.close()
     return line
 
 
@@ -749,6 +921,8 @@ def time_steps(fn, steps, warmup, world, graph=True, min_seconds=0.0):
     region (same K steps each time) and reports the per-replay mean, so the
     clock sampler sees the load."""
     import torch
+    torch.cuda.synchronize()
+    barrier(world)  # ranks that exchange data start together (their peer waits are bounded)
     for i in range(warmup):
         fn(i)
     torch.cuda.synchronize()
@@ -784,7 +958,8 @@ def time_steps(fn, steps, warmup, world, graph=True, min_seconds=0.0):
 def run_ours(args, world, rank, local):
     import torch
     kw = {"history": args.history} if args.workload == "attention" else \
-        {"batch": args.batch} if args.workload == "lmhead" else \
+        {"batch": args.batch} if args.workload in ("lmhead", "lmhead_tp") else \
+        {"batch": args.batch, "hidden": args.hidden, "middle": args.middle} if args.workload == "mlp_tp" else \
         {"batch": args.batch, "rows": args.rows, "cols": args.cols, "fmt": {"q4k": 12, "q6k": 14}[args.format]} \
         if args.workload == "gemm" else {}
     wl = WORKLOADS[args.workload](**kw)
@@ -792,7 +967,9 @@ def run_ours(args, world, rank, local):
     with ClockSampler(local) as clk:
         ms = time_steps(wl.step, args.steps, args.warmup, world, min_seconds=args.min_seconds)
     ms_step = ms / args.steps
-    value = wl.units_per_step() * world / (ms_step / 1e3)
+    strong = getattr(wl, "strong", False)  # tensor parallel: the job's work is fixed, split over the ranks
+    jobs = 1 if strong else world
+    value = wl.units_per_step() * jobs / (ms_step / 1e3)
     # dominant kernel alone, CUDA events on the launching (current) stream
     dom_ms = time_steps(wl.dominant_launch, args.steps, args.warmup, world) / args.steps
     pk = peaks()
@@ -802,19 +979,23 @@ def run_ours(args, world, rank, local):
     line = {
         "metric": wl.metric, "value": value, "unit": wl.unit, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic (seeded, benchmark shapes)",
-        "config": dict(wl.config(), parallelism=f"replicas x{world}" if world > 1 else "single GPU"),
+        "scaling": "strong" if strong else "weak", "vs_baseline": None, "dtype": wl.dtype,
+        "data": "synthetic (seeded, benchmark shapes)",
+        "config": dict(wl.config(), parallelism=(f"tensor parallel x{world}" if strong else f"replicas x{world}")
+                       if world > 1 else "single GPU"),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": achieved / pk["hbm_gbs"], "traffic": getattr(wl, "traffic", None), "kernel": wl.dominant,
                      "algorithmic_bytes": wl.dominant_bytes(), "kernel_ms": dom_ms,
                      "peak_source": f"{pk['source']} hbm_gbs (burst copy)"},
-        "e2e": {"value": wl.units_per_step() * world / (e2e_ms / 1e3), "unit": wl.unit,
+        "e2e": {"value": wl.units_per_step() * jobs / (e2e_ms / 1e3), "unit": wl.unit,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "api": "rta_b200.ops -> librta_cuda.so C-ABI"},
         "gpu_launches": wl.launches_per_step * args.steps,
         "clocks": clk.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = wl.cpu_baseline(args.cpu_budget)
+    if hasattr(wl, "close"):
+        wl.close()
     return line
 
 
@@ -841,8 +1022,10 @@ def run_reference(args, world, rank):
         wl.L = args.history
     if args.workload == "decode2b":
         wl.seed = 20261201
-    if args.workload == "lmhead":
+    if args.workload in ("lmhead", "lmhead_tp"):
         wl.B = args.batch
+    if args.workload == "mlp_tp":
+        wl.B, wl.D, wl.F = args.batch, args.hidden, args.middle
     if args.workload == "gemm":
         wl.B, wl.R, wl.K, wl.gf = args.batch, args.rows, args.cols, {"q4k": 12, "q6k": 14}[args.format]
     budget = max(1.0, args.cpu_budget / max(args.steps, 1))
@@ -855,8 +1038,14 @@ def run_reference(args, world, rank):
     cfg = {"mlp": {"workload": "config1_swiglu_mlp_b1"}, "lmhead": {"workload": f"config3_lmhead_b{args.batch}"},
            "attention": {"workload": f"config2_gqa_decode_L{args.history}"},
            "decode2b": {"workload": "config4_2b_hybrid_decode_b1"},
-           "gemm": {"workload": f"gemm_{args.format}_{args.rows}x{args.cols}_b{args.batch}"}}[args.workload]
-    return {"impl": "reference", "metric": cls.metric, "value": v, "unit": cls.unit, "n_gpus": world,
+           "gemm": {"workload": f"gemm_{args.format}_{args.rows}x{args.cols}_b{args.batch}"},
+           "mlp_tp": {"workload": f"mlp_tp_{args.hidden}x{args.middle}_b{args.batch}"},
+           "lmhead_tp": {"workload": f"lmhead_tp_b{args.batch}"}}[args.workload]
+    metric = {"mlp_tp": f"SwiGLU MLP steps/s, tensor parallel (Q4_K, {args.hidden}-{args.middle}-{args.hidden}, "
+                        f"batch {args.batch})",
+              "lmhead_tp": f"vocabulary readout tokens/s, tensor parallel (151936x2048 Q6_K, argmax, batch "
+                           f"{args.batch})"}.get(args.workload, getattr(cls, "metric", ""))
+    return {"impl": "reference", "metric": metric, "value": v, "unit": cls.unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "dtype": "f32",
             "data": "synthetic (seeded, benchmark shapes)", "config": cfg,
             "cpu_baseline": base, "e2e": {"value": v, "unit": cls.unit, "h2d_bytes_per_step": 0,
@@ -910,6 +1099,8 @@ def main():
     ap.add_argument("--batch", type=int, default=1,
                     help="lmhead: hidden rows per readout (config 3: 1 or 64); gemm: batch rows")
     ap.add_argument("--rows", type=int, default=12288, help="gemm: weight rows (multiple of 128)")
+    ap.add_argument("--hidden", type=int, default=2048, help="mlp_tp: hidden size (multiple of 256)")
+    ap.add_argument("--middle", type=int, default=6144, help="mlp_tp: intermediate size (multiple of 256 x ranks)")
     ap.add_argument("--cols", type=int, default=4096, help="gemm: weight columns (multiple of 256)")
     ap.add_argument("--format", choices=("q4k", "q6k"), default="q4k", help="gemm: weight format")
     ap.add_argument("--prompt", type=int, default=512,

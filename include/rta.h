@@ -112,6 +112,56 @@ RTA_API rta_status rta_gemm_tc(int format, const void* w, uint32_t rows, uint32_
                                uint32_t batch, float* y, int accumulate, uint32_t* argmax, float* best,
                                void* workspace, size_t workspace_bytes, void* stream);
 
+/* SwiGLU MLP on the tensor cores: y (+)= Wd swiglu(Wg x, Wu x) with the three
+ * matrices in panel order (middle % 256 == 0, hidden % 256 == 0), 1 <= batch
+ * <= 256.  Gate and up run as one launch; SwiGLU is applied while the down
+ * projection stages its activation (act, [batch][middle], may be NULL; when
+ * given it receives the activation rows).  workspace:
+ * rta_mlp_tc_workspace_bytes(format, batch, hidden, middle) bytes.  Replaces
+ * executeMLP (optical_resident.cpp:484-491: op 2 kind 3 then kind 4) for
+ * batched rows. */
+RTA_API size_t rta_mlp_tc_workspace_bytes(int format, uint32_t batch, uint32_t hidden, uint32_t middle);
+RTA_API rta_status rta_mlp_tc(int format, const void* w_gate, const void* w_up, const void* w_down, uint32_t hidden,
+                              uint32_t middle, const float* x, uint32_t batch, float* act, float* y, int accumulate,
+                              void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------- 1b. tensor-parallel peer exchange
+ *
+ * The reference has no collective (one worker, one GPU).  For the MLP and the
+ * vocabulary readout split over the GPUs of one box (one process per GPU), a
+ * team gives every rank an exchange buffer that the other ranks write through
+ * NVLink peer memory; each exchange is one kernel launch with bounded waits.
+ * Set-up: every rank calls rta_team_create on its own device, the caller
+ * passes the world handles (rta_team_handle_bytes() each, rank order) to every
+ * rank by any host means, and every rank calls rta_team_connect.  All ranks
+ * must then make the same exchange calls in the same order.  Tear-down:
+ * rta_team_disconnect on every rank, a host barrier, rta_team_destroy.  A rank
+ * whose peers do not arrive within about a second records RTA_DEVERR_TIMEOUT
+ * (read by rta_team_error) instead of hanging. */
+typedef struct rta_team rta_team;
+RTA_API size_t rta_team_handle_bytes(void);
+/* capacity_bytes: the largest contribution of one rank to one exchange
+ * (<= 2 MiB); handle: rta_team_handle_bytes() bytes out (unused at world 1). */
+RTA_API rta_status rta_team_create(uint32_t rank, uint32_t world, size_t capacity_bytes, rta_team** team,
+                                   void* handle);
+RTA_API rta_status rta_team_connect(rta_team* team, const void* handles);
+/* out[i] = addend[i] + sum over ranks of partial[i] (rank order, so every
+ * rank gets the same bits); addend may be NULL; n % 4 == 0; 16-byte aligned
+ * device buffers; out may alias partial or addend.  The sum of the row-split
+ * MLP's partial down projections (the residual as addend). */
+RTA_API rta_status rta_team_allreduce_f32(rta_team* team, const float* partial, const float* addend, float* out,
+                                          size_t n, void* stream);
+/* Best row over the ranks' local argmax (ids local to each rank's vocabulary
+ * rows, which start at id_base; 0xffffffff = none): largest value, ties ->
+ * lowest global id, as ops 16/17 of resident_math.comp:117-127.  best_out may
+ * be NULL; batch <= 1024. */
+RTA_API rta_status rta_team_argmax(rta_team* team, const uint32_t* ids, const float* best, uint32_t id_base,
+                                   uint32_t batch, uint32_t* argmax, float* best_out, void* stream);
+/* Synchronizes `stream`, returns and clears the team's device error word. */
+RTA_API rta_status rta_team_error(rta_team* team, void* stream, uint32_t* error_word);
+RTA_API rta_status rta_team_disconnect(rta_team* team);
+RTA_API void rta_team_destroy(rta_team* team);
+
 /* y[b][r] (+)= sum_c W[r][c] x[b][c]; W Q4_K or Q6_K row-major, rows % 16 == 0,
  * cols % 256 == 0, 1 <= batch <= 32.  Replaces op 2 of
  * ray_tracing/native/shaders/resident_math.comp:39-75 (kinds 0-2, 4-6, 8). */

@@ -4,6 +4,7 @@
 // CUDA failures into rta_status codes with a thread-local message; nothing
 // here aborts the process.  There is no host fallback: every operator runs
 // its CUDA kernel or returns an error.
+#include <algorithm>
 #include <cstdio>
 #include <cstring>
 #include <string>
@@ -143,6 +144,68 @@ rta_status rta_gemm_tc(int format, const void* w, uint32_t rows, uint32_t cols, 
   if (st != RTA_OK || !argmax) return st;
   readout_finish_kernel<<<(batch + 255u) / 256u, 256, 0, s>>>(keys, batch, rows, argmax, best, err);
   return cuda_status(cudaGetLastError(), "rta_gemm_tc(finish)");
+}
+
+size_t rta_mlp_tc_workspace_bytes(int format, uint32_t batch, uint32_t hidden, uint32_t middle) {
+  const uint32_t b = batch ? batch : 1u;
+  const size_t gu = (8ull * b * middle + 255u) / 256u * 256u;
+  const size_t xb = std::max(rta::tc_workspace_bytes(format, b, hidden), rta::tc_workspace_bytes(format, b, middle));
+  return kErrBytes + gu + xb;
+}
+
+rta_status rta_mlp_tc(int format, const void* wg, const void* wu, const void* wd, uint32_t hidden, uint32_t middle,
+                      const float* x, uint32_t batch, float* act, float* y, int accumulate, void* workspace,
+                      size_t workspace_bytes, void* stream) {
+  if ((format != RTA_Q4_K_PANEL && format != RTA_Q6_K_PANEL) || !wg || !wu || !wd || !x || !y || !workspace ||
+      hidden == 0 || hidden % 256 || middle == 0 || middle % 256 || batch == 0 || batch > rta::kMaxBatch)
+    return fail(RTA_E_ARG, "rta_mlp_tc: panel format, hidden and middle multiples of 256, 1 <= batch <= 256");
+  if (workspace_bytes < rta_mlp_tc_workspace_bytes(format, batch, hidden, middle))
+    return fail(RTA_E_ARG, "rta_mlp_tc: workspace too small");
+  cudaStream_t s = as_stream(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  uint32_t* err = reinterpret_cast<uint32_t*>(ws);
+  float* gu = reinterpret_cast<float*>(ws + kErrBytes);
+  const size_t gu_bytes = (8ull * batch * middle + 255u) / 256u * 256u;
+  rta_status st = cuda_status(cudaMemsetAsync(ws, 0, kErrBytes, s), "rta_mlp_tc(memset)");
+  if (st != RTA_OK) return st;
+  rta::TcGemmArgs g;  // gate rows then up rows of each batch row: gu[b][0:middle], gu[b][middle:2 middle]
+  g.fmt = format;
+  g.w0 = static_cast<const uint8_t*>(wg);
+  g.w1 = static_cast<const uint8_t*>(wu);
+  g.rows = middle;
+  g.cols = hidden;
+  g.x = x;
+  g.x_stride = hidden;
+  g.batch = batch;
+  g.y = gu;
+  g.y_stride = 2u * middle;
+  g.err = err;
+  g.xb = ws + kErrBytes + gu_bytes;
+  g.xb_bytes = workspace_bytes - kErrBytes - gu_bytes;
+  st = cuda_status(rta::launch_tc_gemm(g, s), "rta_mlp_tc(gate/up)");
+  if (st != RTA_OK) return st;
+  rta::TcGemmArgs d = g;
+  d.w0 = static_cast<const uint8_t*>(wd);
+  d.w1 = nullptr;
+  d.rows = hidden;
+  d.cols = middle;
+  d.epilogue = accumulate ? rta::kAccumulate : rta::kStore;
+  d.y = y;
+  d.y_stride = hidden;
+  d.pdl = true;
+  if (act) {
+    st = cuda_status(rta::launch_swiglu_rows(gu, batch, middle, 2u * middle, act, middle, s), "rta_mlp_tc(swiglu)");
+    if (st != RTA_OK) return st;
+    d.x = act;
+    d.x_stride = middle;
+  } else {
+    d.prologue = rta::kSwiGLUIn;
+    d.x = gu;
+    d.z = gu + middle;
+    d.x_stride = 2u * middle;
+    d.z_stride = 2u * middle;
+  }
+  return cuda_status(rta::launch_tc_gemm(d, s), "rta_mlp_tc(down)");
 }
 
 rta_status rta_gemv(int format, const void* w, uint32_t rows, uint32_t cols, const float* x, uint32_t batch,

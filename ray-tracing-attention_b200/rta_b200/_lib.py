@@ -42,6 +42,16 @@ _SIGNATURES = {
     "rta_panel_weights": (c_i32, [c_i32, c_p, c_u32, c_u32, c_p, c_p]),
     "rta_gemm_tc_workspace_bytes": (c_sz, [c_i32, c_u32, c_u32]),
     "rta_gemm_tc": (c_i32, [c_i32, c_p, c_u32, c_u32, c_p, c_u32, c_p, c_i32, c_p, c_p, c_p, c_sz, c_p]),
+    "rta_mlp_tc_workspace_bytes": (c_sz, [c_i32, c_u32, c_u32, c_u32]),
+    "rta_mlp_tc": (c_i32, [c_i32, c_p, c_p, c_p, c_u32, c_u32, c_p, c_u32, c_p, c_p, c_i32, c_p, c_sz, c_p]),
+    "rta_team_handle_bytes": (c_sz, []),
+    "rta_team_create": (c_i32, [c_u32, c_u32, c_sz, ctypes.POINTER(c_p), c_p]),
+    "rta_team_connect": (c_i32, [c_p, c_p]),
+    "rta_team_allreduce_f32": (c_i32, [c_p, c_p, c_p, c_p, c_sz, c_p]),
+    "rta_team_argmax": (c_i32, [c_p, c_p, c_p, c_u32, c_u32, c_p, c_p, c_p]),
+    "rta_team_error": (c_i32, [c_p, c_p, ctypes.POINTER(c_u32)]),
+    "rta_team_disconnect": (c_i32, [c_p]),
+    "rta_team_destroy": (None, [c_p]),
     "rta_gemv": (c_i32, [c_i32, c_p, c_u32, c_u32, c_p, c_u32, c_p, c_i32, c_p]),
     "rta_gemv_swiglu": (c_i32, [c_i32, c_p, c_p, c_u32, c_u32, c_p, c_u32, c_p, c_p]),
     "rta_mlp_swiglu": (c_i32, [c_i32, c_p, c_p, c_p, c_u32, c_u32, c_p, c_u32, c_p, c_p, c_i32, c_p]),

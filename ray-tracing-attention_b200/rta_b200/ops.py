@@ -127,6 +127,22 @@ def mlp_swiglu(fmt: int, wg, wu, wd, hidden: int, middle: int, x: torch.Tensor, 
     return act, y
 
 
+def mlp_tc(fmt: int, wg, wu, wd, hidden: int, middle: int, x: torch.Tensor, y: torch.Tensor | None = None,
+           act: torch.Tensor | None = None, accumulate: bool = False, workspace: torch.Tensor | None = None):
+    """SwiGLU MLP on the tensor cores (panel weights): returns y; act receives
+    the activation rows when given."""
+    x = x.reshape(-1, hidden)
+    B = x.shape[0]
+    lib = _lib.load()
+    if workspace is None:
+        workspace = torch.empty(lib.rta_mlp_tc_workspace_bytes(fmt, B, hidden, middle), dtype=torch.uint8,
+                                device=x.device)
+    y = torch.empty(B, hidden, dtype=torch.float32, device=x.device) if y is None else y
+    check(lib.rta_mlp_tc(fmt, _ptr(wg), _ptr(wu), _ptr(wd), hidden, middle, _ptr(x), B, _ptr(act), _ptr(y),
+                         int(accumulate), _ptr(workspace), workspace.numel(), _stream()))
+    return y
+
+
 def readout(fmt: int, w: torch.Tensor, vocab: int, hidden: int, x: torch.Tensor, logits: bool = True,
             workspace: torch.Tensor | None = None):
     x = x.reshape(-1, hidden)
