@@ -82,10 +82,10 @@ __global__ void __launch_bounds__(kThreads) attention_split_kernel(const AttnPar
   __syncthreads();
   pdl_wait();
   pdl_launch_dependents();
-  if (p.running && p.running[blockIdx.z * p.ctrl_step] == 0u) return;
-
+  const uint32_t run = p.running ? p.running[blockIdx.z * p.ctrl_step] : 1u;  // same round trip as the position
   uint32_t t, lo, n;
   window(p, z, t, lo, n);
+  if (run == 0u) return;
   const uint32_t nsplit = gridDim.x;
   uint32_t chunk = (n + nsplit - 1u) / nsplit;
   chunk = (chunk + 63u) / 64u * 64u;
@@ -492,11 +492,12 @@ __global__ void __launch_bounds__(kHD) attention_merge_kernel(const AttnParams p
   pdl_wait();
   pdl_launch_dependents();
   const uint32_t head = blockIdx.x, z = blockIdx.y, d = threadIdx.x;
-  if (p.running && p.running[z * p.ctrl_step] == 0u) return;
+  const uint32_t run = p.running ? p.running[z * p.ctrl_step] : 1u;  // checked once the maxima are in
   const uint32_t kv = head / kGroup, h = head % kGroup;
   const size_t rec0 = (static_cast<size_t>(z) * p.kvh + kv) * nsplit;
   float m = -INFINITY;
   for (uint32_t s = 0; s < nsplit; ++s) m = fmaxf(m, p.part_m[(rec0 + s) * kGroup + h]);
+  if (run == 0u) return;
   float zs = 0.f, os = 0.f;
   if (m != -INFINITY)
     for (uint32_t s = 0; s < nsplit; ++s) {

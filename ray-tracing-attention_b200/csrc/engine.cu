@@ -210,8 +210,8 @@ struct Engine {
     };
     std::vector<Job> jobs;
     auto mut = [](const uint8_t* q) { return const_cast<uint8_t*>(q); };
-    for (auto& Lp : layers) {
-      Layer& L = *Lp;
+    for (size_t li = 0; li < layers.size(); ++li) {
+      Layer& L = *layers[li];
       if (L.full) {
         jobs.push_back({L.qkvg.p, L.qkvg_fmt, &L.qkvg_fmt, L.qkvg_rows, D});
         jobs.push_back({mut(L.o), L.o_fmt, &L.o_fmt, D, Q()});
@@ -527,6 +527,20 @@ struct Engine {
     const uint32_t D = this->D(), F = spec.middle_size, hd = spec.attention_head_dim;
     const uint32_t cstep = static_cast<uint32_t>(sizeof(Control) / 4);  // u32 between sequences' control words
     static_assert(sizeof(Control) % 8 == 0, "control blocks must keep 8-byte alignment");
+    // Every batch-1 GEMV prefetches the next GEMV's weights into L2 (see
+    // prefetch_next_weights in gemv.cu): o / out <- first projection, gate / up
+    // <- o / out, down <- gate / up, the next layer's first projection <- down.
+    auto mbytes = [](int fmt, uint32_t rows, uint32_t cols) {
+      return static_cast<size_t>(rows) * (cols / 256u) * block_bytes(fmt);
+    };
+    auto first_proj = [&](size_t i, GemvArgs& a) {
+      a.pf[0] = nullptr;
+      a.pf_bytes[0] = 0;
+      if (i >= layers.size()) return;
+      const Layer& N = *layers[i];
+      a.pf[0] = N.full ? N.qkvg.p : N.inproj.p;
+      a.pf_bytes[0] = N.full ? mbytes(N.qkvg_fmt, N.qkvg_rows, D) : mbytes(N.inproj_fmt, N.inproj_rows, D);
+    };
     if (decode) {
       GemvArgs r;
       r.fmt = lm_fmt;
@@ -545,6 +559,7 @@ struct Engine {
       r.running = running;
       r.running_step = cstep;
       r.pdl = true;
+      first_proj(0, r);
       RTA_CUDA(matmul(r, s));
       ++n;
     }
@@ -562,8 +577,8 @@ struct Engine {
     e.state = state.p;
     RTA_CUDA(launch_embed(e, s, true));
     ++n;
-    for (auto& Lp : layers) {
-      Layer& L = *Lp;
+    for (size_t li = 0; li < layers.size(); ++li) {
+      Layer& L = *layers[li];
       if (L.full) {
         GemvArgs g;
         g.fmt = L.qkvg_fmt;
@@ -582,6 +597,8 @@ struct Engine {
         g.running_step = cstep;
         g.err = &c->err;
         g.pdl = true;
+        g.pf[0] = L.o;
+        g.pf_bytes[0] = mbytes(L.o_fmt, D, Q());
         RTA_CUDA(matmul(g, s));
         PrepParams pp;
         pp.qkvg = proj.p;
@@ -656,6 +673,9 @@ struct Engine {
         o.running_step = cstep;
         o.err = &c->err;
         o.pdl = true;
+        o.pf[0] = L.gate;
+        o.pf[1] = L.up;
+        o.pf_bytes[0] = o.pf_bytes[1] = mbytes(L.mlp_fmt, F, D);
         RTA_CUDA(matmul(o, s));
         n += 5;
       } else {
@@ -676,6 +696,8 @@ struct Engine {
         g.running_step = cstep;
         g.err = &c->err;
         g.pdl = true;
+        g.pf[0] = L.out;
+        g.pf_bytes[0] = mbytes(L.out_fmt, D, S());
         RTA_CUDA(matmul(g, s));
         GdnParams gp;
         gp.x = state.p;
@@ -721,6 +743,9 @@ struct Engine {
         o.running_step = cstep;
         o.err = &c->err;
         o.pdl = true;
+        o.pf[0] = L.gate;
+        o.pf[1] = L.up;
+        o.pf_bytes[0] = o.pf_bytes[1] = mbytes(L.mlp_fmt, F, D);
         RTA_CUDA(matmul(o, s));
         n += 3;
       }
@@ -743,6 +768,8 @@ struct Engine {
       gu.running_step = cstep;
       gu.err = &c->err;
       gu.pdl = true;
+      gu.pf[0] = L.down;
+      gu.pf_bytes[0] = mbytes(L.down_fmt, D, F);
       GemvArgs dn;
       dn.fmt = L.down_fmt;
       dn.w0 = L.down;
@@ -758,6 +785,7 @@ struct Engine {
       dn.running_step = cstep;
       dn.err = &c->err;
       dn.pdl = true;
+      first_proj(li + 1, dn);
       mlp_pair(gu, dn, false, s);
       n += 2;
     }

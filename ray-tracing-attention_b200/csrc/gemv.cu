@@ -63,7 +63,28 @@ struct Params {
   uint32_t run_step, arg_step;  // elements between batch rows' running flags / argmax keys
   // shared-memory carve (byte offsets from the dynamic base)
   uint32_t off_bar, off_xq, off_xsc, off_scr, off_red, off_misc;
+  const uint8_t* pf[2];  // next launch's weights to prefetch into L2 (null: none)
+  uint32_t pf_bytes[2];
 };
+
+// L2 prefetch of this CTA's share of the next launch's weights.  Batch-1
+// launches are latency-bound (a few MB each, HBM mostly idle), so the next
+// launch's first HBM round trips are taken here, in the shadow of this one;
+// it then streams from L2.
+__device__ __forceinline__ void prefetch_next_weights(const Params& p) {
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const uint32_t total = p.pf_bytes[r];
+    if (!p.pf[r] || total == 0u) continue;
+    const uint32_t per = ((total + gridDim.x - 1u) / gridDim.x + 15u) & ~15u;
+    const uint64_t first = static_cast<uint64_t>(blockIdx.x) * per;
+    if (first >= total) continue;
+    const uint32_t end = static_cast<uint32_t>(min(static_cast<uint64_t>(total), first + per));
+    for (uint32_t off = static_cast<uint32_t>(first); off < end; off += 65536u)
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p.pf[r] + off), "r"(min(65536u, end - off))
+                   : "memory");
+  }
+}
 
 template <int FMT>
 struct Fmt;
@@ -97,7 +118,28 @@ __device__ __forceinline__ float block_sum(float v, float* red8) {
 //   xsc : [batch][xgroup] float4(xs, -32 * sum X first 16, -32 * sum X last 16 (int bits), xs * sum X)
 // Thread i owns float4 chunks i, i+256, ...; 8 consecutive chunks form one
 // 32-coefficient group (8 consecutive lanes), 32 chunks one 128-wide head.
-__device__ void prepare_x(const Params& p, uint8_t* smem, const float4 (&wv)[kPass]) {
+// Batch row 0's first pass of x (and z), loaded right after the PDL wait so
+// that its round trip overlaps the running-flag check instead of following it.
+struct XFirst {
+  float4 xv[kPass], zv[kPass];
+};
+__device__ __forceinline__ void load_x_first(const Params& p, XFirst& f) {
+  const float4* xr = reinterpret_cast<const float4*>(p.x);
+  const float4* zr = reinterpret_cast<const float4*>(p.z);
+  const uint32_t nchunk = p.cols / 4u;
+#pragma unroll
+  for (int i = 0; i < kPass; ++i) {
+    const uint32_t c = threadIdx.x + i * kThreads;
+    f.xv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    f.zv[i] = f.xv[i];
+    if (c < nchunk) {
+      f.xv[i] = xr[c];
+      if (zr) f.zv[i] = zr[c];
+    }
+  }
+}
+
+__device__ void prepare_x(const Params& p, uint8_t* smem, const float4 (&wv)[kPass], const XFirst& first) {
   uint32_t* xq = reinterpret_cast<uint32_t*>(smem + p.off_xq);
   float4* xsc = reinterpret_cast<float4*>(smem + p.off_xsc);
   float* red8 = reinterpret_cast<float*>(smem + p.off_misc);
@@ -114,7 +156,10 @@ __device__ void prepare_x(const Params& p, uint8_t* smem, const float4 (&wv)[kPa
         const uint32_t c = tid + (pass * kPass + i) * kThreads;
         xv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
         zv[i] = xv[i];
-        if (c < nchunk) {
+        if (b == 0u && pass == 0u) {
+          xv[i] = first.xv[i];
+          zv[i] = first.zv[i];
+        } else if (c < nchunk) {
           xv[i] = xr[c];
           if (zr) zv[i] = zr[c];
         }
@@ -283,12 +328,14 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const Params p) {
 
   pdl_wait();                 // activations (and residual target) are now visible
   pdl_launch_dependents();    // let the next kernel start streaming its weights
+  XFirst xfirst;
+  load_x_first(p, xfirst);
   if (!any_running(p)) {
     if (threadIdx.x == 0)  // generation stopped: drain the stages in flight and leave
       for (uint32_t j = 0; j < issued; ++j) (void)mbar_wait(&bars[j % p.nstage], (j / p.nstage) & 1u, nullptr);
     return;
   }
-  prepare_x(p, smem, wv);
+  prepare_x(p, smem, wv, xfirst);
 
   const uint32_t* xq = reinterpret_cast<const uint32_t*>(smem + p.off_xq);
   const float4* xsc = reinterpret_cast<const float4*>(smem + p.off_xsc);
@@ -883,8 +930,10 @@ __global__ void __launch_bounds__(kThreads, NB >= 8 ? 1 : 2) gemv_tiled_kernel(c
   };
 
   uint32_t issued = min(total, p.nstage), drain_from = 0;  // tracked by every thread alike
-  if (threadIdx.x == 0)
+  if (threadIdx.x == 0) {
     for (uint32_t it = 0; it < issued; ++it) issue();
+    prefetch_next_weights(p);
+  }
 
   // norm weights are constant: read them before waiting on the producer
   float4 wv[kPass];
@@ -899,12 +948,19 @@ __global__ void __launch_bounds__(kThreads, NB >= 8 ? 1 : 2) gemv_tiled_kernel(c
 
   pdl_wait();                 // activations (and residual target) are now visible
   pdl_launch_dependents();    // let the next kernel start streaming its weights
+  XFirst xfirst;
+  load_x_first(p, xfirst);
+  // the residual rows of the first tile, read now so the epilogue does not wait on them
+  float ypre = 0.f;
+  if (p.epilogue == kAccumulate && my_tiles > 0u && threadIdx.x < kTileRows * p.batch)
+    ypre = p.y[static_cast<size_t>(threadIdx.x / kTileRows) * p.y_stride + blockIdx.x * kTileRows +
+               threadIdx.x % kTileRows];
   if (!any_running(p)) {
     if (threadIdx.x == 0)  // generation stopped: drain the stages in flight and leave
       for (uint32_t j = 0; j < issued; ++j) (void)mbar_wait(&bars[j % p.nstage], (j / p.nstage) & 1u, nullptr);
     return;
   }
-  prepare_x(p, smem, wv);
+  prepare_x(p, smem, wv, xfirst);
 
   const uint32_t* xq = reinterpret_cast<const uint32_t*>(smem + p.off_xq);
   const float4* xsc = reinterpret_cast<const float4*>(smem + p.off_xsc);
@@ -1136,7 +1192,7 @@ __global__ void __launch_bounds__(kThreads, NB >= 8 ? 1 : 2) gemv_tiled_kernel(c
           const float sgn = (gv > 0.f ? 1.f : gv < 0.f ? -1.f : 0.f) * (uv > 0.f ? 1.f : uv < 0.f ? -1.f : 0.f);
           *yp = sgn * amp;
         } else if (p.epilogue == kAccumulate) {
-          *yp += v[0];
+          *yp = (tile_local == 0u ? ypre : *yp) + v[0];
         } else if (yp) {
           *yp = v[0];
         }

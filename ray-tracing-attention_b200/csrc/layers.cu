@@ -120,16 +120,18 @@ __global__ void __launch_bounds__(256) attn_prep_kernel(PrepParams p) {
   pdl_wait();
   pdl_launch_dependents();
   const uint32_t z = blockIdx.y;  // sequence
-  if (p.running && p.running[z * p.ctrl_step] == 0u) return;
   __shared__ float red[16];
   __shared__ float xs[256];
   const uint32_t d = threadIdx.x, hd = p.hd;
+  // the running flag, the position and this head's row travel in one round trip
+  const uint32_t run = p.running ? p.running[z * p.ctrl_step] : 1u;
   const uint32_t pos = p.pos[z * p.ctrl_step];
   const bool is_q = blockIdx.x < p.heads;
   const uint32_t head = is_q ? blockIdx.x : blockIdx.x - p.heads;
   const float* qkvg = p.qkvg + z * p.qkvg_seq;
   const float* src = is_q ? qkvg + head * hd : qkvg + p.q_width + head * hd;
   float x = d < hd ? src[d] : 0.f;
+  if (run == 0u) return;
   if (p.qk_norm) {
     const float ss = block_sum256(x * x, red);
     const float inv = rsqrtf(ss / static_cast<float>(hd) + p.eps);
@@ -222,9 +224,8 @@ __device__ __forceinline__ void block_sums(float (&v)[N], float* red) {
   }
 }
 
-__device__ __forceinline__ void prefetch_l2(const void* ptr) {
-  asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr));
-}
+
+constexpr uint32_t kGdnDPer = 16;  // hidden values per thread: hidden size <= 4096
 
 template <uint32_t ROWS>
 __global__ void __launch_bounds__(256) gdn_kernel(GdnParams p) {
@@ -247,10 +248,27 @@ __global__ void __launch_bounds__(256) gdn_kernel(GdnParams p) {
     s0[i] = *reinterpret_cast<const float2*>(row + 2 * lane);   // lane owns keys (2l, 2l+1) and
     s1[i] = *reinterpret_cast<const float2*>(row + 2 * lane + 64);  // (2l+64, 2l+65), as op 21
   }
-  for (uint32_t c = tid * 32u; c < p.D; c += 256u * 32u) {  // one 128-byte line per thread
-    prefetch_l2(p.wa + static_cast<size_t>(h) * p.D + c);
-    prefetch_l2(p.wb + static_cast<size_t>(h) * p.D + c);
-    prefetch_l2(p.attn_norm + c);
+  // Few CTAs (one sequence): the gate weights and the norm weight of this
+  // thread's hidden values (c = tid + 256 i) are held in registers, read before
+  // the wait.  Many CTAs: they stay in memory (occupancy), prefetched to L2.
+  constexpr bool kHold = ROWS <= 16u;
+  constexpr uint32_t kPer = kHold ? kGdnDPer : 1u;
+  float nw[kPer], wa[kPer], wb[kPer], xr[kPer];
+  if constexpr (kHold) {
+#pragma unroll
+    for (uint32_t i = 0; i < kPer; ++i) {
+      const uint32_t c = tid + 256u * i;
+      const bool in = c < p.D;
+      nw[i] = in ? p.attn_norm[c] : 0.f;
+      wa[i] = in ? p.wa[static_cast<size_t>(h) * p.D + c] : 0.f;
+      wb[i] = in ? p.wb[static_cast<size_t>(h) * p.D + c] : 0.f;
+    }
+  } else {
+    for (uint32_t c = tid * 32u; c < p.D; c += 256u * 32u) {  // one 128-byte line per thread
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(p.wa + static_cast<size_t>(h) * p.D + c));
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(p.wb + static_cast<size_t>(h) * p.D + c));
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(p.attn_norm + c));
+    }
   }
   // The conv history is double-buffered by position parity; the position is
   // written by this step's embed kernel, so both buffers are read here and the
@@ -277,24 +295,51 @@ __global__ void __launch_bounds__(256) gdn_kernel(GdnParams p) {
 
   pdl_wait();
   pdl_launch_dependents();
-  if (p.running && p.running[z * p.ctrl_step] == 0u) return;
-  const uint32_t par = p.pos[z * p.ctrl_step] & 1u;
+  // every load that depends on the preceding kernels is issued before the first
+  // use, so they share one round trip
+  const uint32_t run = p.running ? p.running[z * p.ctrl_step] : 1u;
+  const uint32_t posv = p.pos[z * p.ctrl_step];
+  if constexpr (kHold) {
+#pragma unroll
+    for (uint32_t i = 0; i < kPer; ++i) {
+      const uint32_t c = tid + 256u * i;
+      xr[i] = c < p.D ? x_seq[c] : 0.f;
+    }
+  }
+  const float raw_q = proj[tid < 128u ? kh * HD + tid : K + kh * HD + (tid - 128u)];
+  const float raw_v = tid < kGdnRows ? proj[2u * K + h * HD + slice * kGdnRows + tid] : 0.f;
+  if (run == 0u) return;
+  const uint32_t par = posv & 1u;
   float* next = conv_state + (par ^ 1u) * buf;
   const float pq0 = par ? pq[1][0] : pq[0][0], pq1 = par ? pq[1][1] : pq[0][1], pq2 = par ? pq[1][2] : pq[0][2];
   const float pv0 = par ? pv[1][0] : pv[0][0], pv1 = par ? pv[1][1] : pv[0][1], pv2 = par ? pv[1][2] : pv[0][2];
 
   // ---- op 18 gates: a, b = (rmsnorm(x) * attn_norm) . W_alpha[h], W_beta[h]
   float ss[1] = {0.f};
-  for (uint32_t c = tid; c < p.D; c += 256u) ss[0] += x_seq[c] * x_seq[c];
-  const float raw_q = proj[tid < 128u ? kh * HD + tid : K + kh * HD + (tid - 128u)];
-  const float raw_v = tid < kGdnRows ? proj[2u * K + h * HD + slice * kGdnRows + tid] : 0.f;
+  if constexpr (kHold) {
+#pragma unroll
+    for (uint32_t i = 0; i < kPer; ++i)
+      if (tid + 256u * i < p.D) ss[0] += xr[i] * xr[i];
+  } else {
+    for (uint32_t c = tid; c < p.D; c += 256u) ss[0] += x_seq[c] * x_seq[c];
+  }
   block_sums<1>(ss, red1);
   const float inv = rsqrtf(ss[0] / static_cast<float>(p.D) + p.eps);
   float ab[2] = {0.f, 0.f};
-  for (uint32_t c = tid; c < p.D; c += 256u) {
-    const float xn = x_seq[c] * inv * p.attn_norm[c];
-    ab[0] += xn * p.wa[static_cast<size_t>(h) * p.D + c];
-    ab[1] += xn * p.wb[static_cast<size_t>(h) * p.D + c];
+  if constexpr (kHold) {
+#pragma unroll
+    for (uint32_t i = 0; i < kPer; ++i) {
+      if (tid + 256u * i >= p.D) continue;
+      const float xn = xr[i] * inv * nw[i];
+      ab[0] += xn * wa[i];
+      ab[1] += xn * wb[i];
+    }
+  } else {
+    for (uint32_t c = tid; c < p.D; c += 256u) {
+      const float xn = x_seq[c] * inv * p.attn_norm[c];
+      ab[0] += xn * p.wa[static_cast<size_t>(h) * p.D + c];
+      ab[1] += xn * p.wb[static_cast<size_t>(h) * p.D + c];
+    }
   }
 
   // ---- op 19: causal conv + SiLU (independent of the gates)
@@ -392,6 +437,7 @@ cudaError_t launch_attn_prep(const PrepParams& p, cudaStream_t s, bool pdl) {
                     pdl);
 }
 cudaError_t launch_gdn(const GdnParams& p, cudaStream_t s, bool pdl) {
+  if (p.D == 0 || p.D > 256u * kGdnDPer) return cudaErrorInvalidValue;
   void* args[] = {const_cast<GdnParams*>(&p)};
   if (p.H * p.nseq >= 2u * 148u)  // enough (sequence, head) pairs to fill the GPU with whole heads
     return launch_pdl(reinterpret_cast<const void*>(gdn_kernel<kGdnRowsBatch>), dim3(p.H, 1, p.nseq), dim3(256),
