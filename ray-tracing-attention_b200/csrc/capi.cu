@@ -265,8 +265,6 @@ rta_status rta_mlp_swiglu(int format, const void* wg, const void* wu, const void
   g.epilogue = rta::kSwiGLU;
   g.y = act;
   g.y_stride = middle;
-  g.pf[0] = static_cast<const uint8_t*>(wd);  // the down projection streams from L2 (tiled formats)
-  g.pf_bytes[0] = static_cast<size_t>(hidden) * (middle / 256u) * rta::block_bytes(format);
   rta_status st = cuda_status(rta::launch_gemv(g, as_stream(stream)), "rta_mlp_swiglu(gate/up)");
   if (st != RTA_OK) return st;
   rta::GemvArgs d;

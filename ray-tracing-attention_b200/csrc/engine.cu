@@ -527,20 +527,6 @@ struct Engine {
     const uint32_t D = this->D(), F = spec.middle_size, hd = spec.attention_head_dim;
     const uint32_t cstep = static_cast<uint32_t>(sizeof(Control) / 4);  // u32 between sequences' control words
     static_assert(sizeof(Control) % 8 == 0, "control blocks must keep 8-byte alignment");
-    // Every batch-1 GEMV prefetches the next GEMV's weights into L2 (see
-    // prefetch_next_weights in gemv.cu): o / out <- first projection, gate / up
-    // <- o / out, down <- gate / up, the next layer's first projection <- down.
-    auto mbytes = [](int fmt, uint32_t rows, uint32_t cols) {
-      return static_cast<size_t>(rows) * (cols / 256u) * block_bytes(fmt);
-    };
-    auto first_proj = [&](size_t i, GemvArgs& a) {
-      a.pf[0] = nullptr;
-      a.pf_bytes[0] = 0;
-      if (i >= layers.size()) return;
-      const Layer& N = *layers[i];
-      a.pf[0] = N.full ? N.qkvg.p : N.inproj.p;
-      a.pf_bytes[0] = N.full ? mbytes(N.qkvg_fmt, N.qkvg_rows, D) : mbytes(N.inproj_fmt, N.inproj_rows, D);
-    };
     if (decode) {
       GemvArgs r;
       r.fmt = lm_fmt;
@@ -559,7 +545,6 @@ struct Engine {
       r.running = running;
       r.running_step = cstep;
       r.pdl = true;
-      first_proj(0, r);
       RTA_CUDA(matmul(r, s));
       ++n;
     }
@@ -597,8 +582,6 @@ struct Engine {
         g.running_step = cstep;
         g.err = &c->err;
         g.pdl = true;
-        g.pf[0] = L.o;
-        g.pf_bytes[0] = mbytes(L.o_fmt, D, Q());
         RTA_CUDA(matmul(g, s));
         PrepParams pp;
         pp.qkvg = proj.p;
@@ -673,9 +656,6 @@ struct Engine {
         o.running_step = cstep;
         o.err = &c->err;
         o.pdl = true;
-        o.pf[0] = L.gate;
-        o.pf[1] = L.up;
-        o.pf_bytes[0] = o.pf_bytes[1] = mbytes(L.mlp_fmt, F, D);
         RTA_CUDA(matmul(o, s));
         n += 5;
       } else {
@@ -696,8 +676,6 @@ struct Engine {
         g.running_step = cstep;
         g.err = &c->err;
         g.pdl = true;
-        g.pf[0] = L.out;
-        g.pf_bytes[0] = mbytes(L.out_fmt, D, S());
         RTA_CUDA(matmul(g, s));
         GdnParams gp;
         gp.x = state.p;
@@ -743,9 +721,6 @@ struct Engine {
         o.running_step = cstep;
         o.err = &c->err;
         o.pdl = true;
-        o.pf[0] = L.gate;
-        o.pf[1] = L.up;
-        o.pf_bytes[0] = o.pf_bytes[1] = mbytes(L.mlp_fmt, F, D);
         RTA_CUDA(matmul(o, s));
         n += 3;
       }
@@ -768,8 +743,6 @@ struct Engine {
       gu.running_step = cstep;
       gu.err = &c->err;
       gu.pdl = true;
-      gu.pf[0] = L.down;
-      gu.pf_bytes[0] = mbytes(L.down_fmt, D, F);
       GemvArgs dn;
       dn.fmt = L.down_fmt;
       dn.w0 = L.down;
@@ -785,7 +758,6 @@ struct Engine {
       dn.running_step = cstep;
       dn.err = &c->err;
       dn.pdl = true;
-      first_proj(li + 1, dn);
       mlp_pair(gu, dn, false, s);
       n += 2;
     }

@@ -63,28 +63,7 @@ struct Params {
   uint32_t run_step, arg_step;  // elements between batch rows' running flags / argmax keys
   // shared-memory carve (byte offsets from the dynamic base)
   uint32_t off_bar, off_xq, off_xsc, off_scr, off_red, off_misc;
-  const uint8_t* pf[2];  // next launch's weights to prefetch into L2 (null: none)
-  uint32_t pf_bytes[2];
 };
-
-// L2 prefetch of this CTA's share of the next launch's weights.  Batch-1
-// launches are latency-bound (a few MB each, HBM mostly idle), so the next
-// launch's first HBM round trips are taken here, in the shadow of this one;
-// it then streams from L2.
-__device__ __forceinline__ void prefetch_next_weights(const Params& p) {
-#pragma unroll
-  for (int r = 0; r < 2; ++r) {
-    const uint32_t total = p.pf_bytes[r];
-    if (!p.pf[r] || total == 0u) continue;
-    const uint32_t per = ((total + gridDim.x - 1u) / gridDim.x + 15u) & ~15u;
-    const uint64_t first = static_cast<uint64_t>(blockIdx.x) * per;
-    if (first >= total) continue;
-    const uint32_t end = static_cast<uint32_t>(min(static_cast<uint64_t>(total), first + per));
-    for (uint32_t off = static_cast<uint32_t>(first); off < end; off += 65536u)
-      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p.pf[r] + off), "r"(min(65536u, end - off))
-                   : "memory");
-  }
-}
 
 template <int FMT>
 struct Fmt;
@@ -930,10 +909,8 @@ __global__ void __launch_bounds__(kThreads, NB >= 8 ? 1 : 2) gemv_tiled_kernel(c
   };
 
   uint32_t issued = min(total, p.nstage), drain_from = 0;  // tracked by every thread alike
-  if (threadIdx.x == 0) {
+  if (threadIdx.x == 0)
     for (uint32_t it = 0; it < issued; ++it) issue();
-    prefetch_next_weights(p);
-  }
 
   // norm weights are constant: read them before waiting on the producer
   float4 wv[kPass];

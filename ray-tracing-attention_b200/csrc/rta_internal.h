@@ -78,10 +78,6 @@ struct GemvArgs {
   const uint32_t* running = nullptr;     // optional per-row device flags: 0 -> that row is skipped
   uint32_t running_step = 1;             // u32 elements between batch rows' flags
   bool pdl = false;                      // launch with programmatic stream serialization
-  // optional L2 prefetch of the next launch's weights (tiled formats; 16-byte
-  // aligned, sizes multiples of 16): each CTA requests its share at start
-  const uint8_t* pf[2] = {nullptr, nullptr};
-  size_t pf_bytes[2] = {0, 0};
 };
 cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t s);
 // Re-lay a [rows x cols] Q4_K / Q6_K matrix (rows % 16 == 0) out of GGUF row
