@@ -79,6 +79,17 @@ def _np_ptr(a: np.ndarray):
     return a.ctypes.data_as(ctypes.c_void_p)
 
 
+def _current_device() -> int:
+    """The caller's current CUDA device (one process per GPU sets it before opening a model)."""
+    try:
+        import torch
+        if torch.cuda.is_available():
+            return int(torch.cuda.current_device())
+    except ImportError:
+        pass
+    return 0
+
+
 class ResidentModel:
     """One resident model on one GPU (prefill / generate / mlp / vocabulary).
     With sequences > 1 the handle decodes that many sequences side by side
@@ -94,10 +105,12 @@ class ResidentModel:
 
     # ---------------------------------------------------------------- open
     @classmethod
-    def from_payloads(cls, spec: assets.Spec, params, matrices, basis, capacity: int, device: int = 0,
+    def from_payloads(cls, spec: assets.Spec, params, matrices, basis, capacity: int, device: int | None = None,
                       sequences: int = 1, history: str = "fp16"):
-        """history: "fp16" K/V rings, or "packet" (the reference's Q4_K/Q6_K history packets)."""
-        """params: uint32 numpy; matrices/basis: uint8 numpy (host) or torch CUDA tensors (device)."""
+        """history: "fp16" K/V rings, or "packet" (the reference's Q4_K/Q6_K history packets).
+        params: uint32 numpy; matrices/basis: uint8 numpy (host) or torch CUDA tensors (device).
+        device: CUDA ordinal (default: the caller's current device)."""
+        device = _current_device() if device is None else device
         lib = _lib_model()
         params = np.ascontiguousarray(params, np.uint32)
 
@@ -121,7 +134,8 @@ class ResidentModel:
         return model
 
     @classmethod
-    def from_directory(cls, directory, capacity: int, device: int = 0):
+    def from_directory(cls, directory, capacity: int, device: int | None = None):
+        device = _current_device() if device is None else device
         directory = Path(directory)
         import json
         spec = assets.Spec.from_dict(json.loads((directory / "model.json").read_text())["model_spec"])
@@ -135,10 +149,11 @@ class ResidentModel:
         return cls(h, spec, capacity, device)
 
     @classmethod
-    def synthetic(cls, spec: assets.Spec, seed: int = 0, capacity: int = 1024, device: int = 0,
+    def synthetic(cls, spec: assets.Spec, seed: int = 0, capacity: int = 1024, device: int | None = None,
                   sequences: int = 1, history: str = "fp16"):
         """Random-init model of `spec` generated on the GPU (payloads in the exporter's layout)."""
         import torch
+        device = _current_device() if device is None else device
         torch.cuda.set_device(device)
         layout = assets.plan(spec, seed)
         mats, basis = assets.generate_device(layout, seed)
