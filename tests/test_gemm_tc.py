@@ -251,8 +251,8 @@ def test_gemm_tc_parity(ops, fmt, rows, cols, batch):
 @pytest.mark.gpu
 @pytest.mark.parametrize("fmt,rows,cols", [(12, 256, 2048), (14, 256, 2048), (12, 1024, 4096), (14, 512, 12288)])
 def test_gemm_tc_accumulates_into_the_residual(ops, fmt, rows, cols):
-    """K-split (256 x 2048) and stream-K (1024 x 4096, 512 x 12288) schedules add
-    their partial sums into the residual."""
+    """K-split schedules (8 slices of 1, 2 or 6 blocks here) add their partial
+    sums into the residual."""
     batch = 24
     rng = np.random.default_rng(fmt + 40)
     W = oracle.quantize(fmt, rng.normal(0, 0.02, rows * cols).astype(np.float32))
