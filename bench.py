@@ -750,6 +750,12 @@ def run_ragged(args, world, rank, local):
     wl = RaggedBatchWorkload
     spec = assets.spec_9b()
     lengths = sharding.config5_histories(wl.seed)
+    small = bool(args.layers or args.max_history)  # profiling case: the 9B layer shapes, fewer layers / shorter histories
+    if args.layers:
+        import dataclasses
+        spec = dataclasses.replace(spec, layer_types=spec.layer_types[:args.layers])
+    if args.max_history:
+        lengths = np.minimum(lengths, args.max_history).astype(lengths.dtype)
     shards = sharding.shard_sequences(lengths, world)
     mine = lengths[shards[rank]]
     capacity = (int(lengths.max()) + 256 + 255) // 256 * 256
@@ -810,7 +816,9 @@ def run_ragged(args, world, rank, local):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": wl.dtype,
         "data": "synthetic (seeded random init; seeded K/V, recurrent state and residual histories)",
-        "config": {"workload": "config5_9b_ragged_batch64", "layers": spec.depth, "pattern": "rec,rec,rec,full",
+        "config": {"workload": "config5_9b_ragged_batch64" if not small else
+                   f"ragged9b_profile_case_{spec.depth}_layers_history_le_{int(lengths.max())}",
+                   "layers": spec.depth, "pattern": "rec,rec,rec,full",
                    "hidden": spec.hidden_size, "intermediate": spec.middle_size, "vocab": spec.vocabulary_size,
                    "q_heads": 16, "kv_heads": 4, "head_dim": 256, "state_heads": spec.state_heads,
                    "state_key_heads": spec.state_key_heads, "sequences": total,
@@ -1103,6 +1111,10 @@ def main():
     ap.add_argument("--middle", type=int, default=6144, help="mlp_tp: intermediate size (multiple of 256 x ranks)")
     ap.add_argument("--cols", type=int, default=4096, help="gemm: weight columns (multiple of 256)")
     ap.add_argument("--format", choices=("q4k", "q6k"), default="q4k", help="gemm: weight format")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="ragged9b: first N layers of the 9B pattern only (profiling case; 0 = all 32)")
+    ap.add_argument("--max-history", type=int, default=0,
+                    help="ragged9b: cap the seeded histories (profiling case; 0 = config 5's U[128, 8192])")
     ap.add_argument("--prompt", type=int, default=512,
                     help="decode2b: prompt length before the timed tokens (short prompts keep profiler runs small)")
     args = ap.parse_args()

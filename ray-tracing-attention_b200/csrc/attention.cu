@@ -67,6 +67,13 @@ __device__ __forceinline__ void window(const AttnParams& p, uint32_t z, uint32_t
   n = t >= lo ? t - lo + 1u : 0u;
 }
 
+// Splits sequence z uses out of the launch's nsplit (see split_by_length).
+__device__ __forceinline__ uint32_t used_splits(const AttnParams& p, uint32_t n, uint32_t nsplit) {
+  if (!p.split_by_length || p.packets || p.group_block) return nsplit;
+  const uint32_t want = static_cast<uint32_t>((static_cast<uint64_t>(n) * nsplit + p.capacity - 1u) / p.capacity);
+  return want < 1u ? 1u : want > nsplit ? nsplit : want;
+}
+
 __global__ void __launch_bounds__(kThreads) attention_split_kernel(const AttnParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
@@ -86,7 +93,8 @@ __global__ void __launch_bounds__(kThreads) attention_split_kernel(const AttnPar
   uint32_t t, lo, n;
   window(p, z, t, lo, n);
   if (run == 0u) return;
-  const uint32_t nsplit = gridDim.x;
+  const uint32_t nsplit = used_splits(p, n, gridDim.x);
+  if (split >= nsplit) return;  // not used by this sequence: no record, the merge skips it
   uint32_t chunk = (n + nsplit - 1u) / nsplit;
   chunk = (chunk + 63u) / 64u * 64u;
   if (chunk < 64u) chunk = 64u;
@@ -495,6 +503,11 @@ __global__ void __launch_bounds__(kHD) attention_merge_kernel(const AttnParams p
   const uint32_t run = p.running ? p.running[z * p.ctrl_step] : 1u;  // checked once the maxima are in
   const uint32_t kv = head / kGroup, h = head % kGroup;
   const size_t rec0 = (static_cast<size_t>(z) * p.kvh + kv) * nsplit;
+  if (p.split_by_length) {  // only the records this sequence's splits wrote
+    uint32_t t, lo, n;
+    window(p, z, t, lo, n);
+    nsplit = used_splits(p, n, nsplit);
+  }
   float m = -INFINITY;
   for (uint32_t s = 0; s < nsplit; ++s) m = fmaxf(m, p.part_m[(rec0 + s) * kGroup + h]);
   if (run == 0u) return;

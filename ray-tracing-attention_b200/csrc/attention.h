@@ -41,6 +41,11 @@ struct AttnParams {
   // 0: splits cut the visible window into equal chunks; > 0: split g covers the
   // g-th newest group of `group_block` positions (the reference's receipt groups).
   uint32_t group_block = 0;
+  // fp16 history, several sequences: sequence z uses only the first
+  // ceil(n_z * nsplit / capacity) splits of the launch (n_z its visible
+  // history), so every split covers about capacity / nsplit positions; the
+  // unused splits leave at once and the merge reads only the used records.
+  uint32_t split_by_length = 0;
 };
 
 size_t attention_smem_bytes();

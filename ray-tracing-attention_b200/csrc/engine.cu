@@ -81,6 +81,9 @@ struct Layer {
   int out_fmt = kQ4K;
   const float *wa = nullptr, *wb = nullptr, *a_log = nullptr, *dt_bias = nullptr, *conv_w = nullptr,
               *ssm_norm = nullptr;
+  // 16-byte aligned copies [wa H*D | wb H*D | attn_norm D] that the gated-delta
+  // kernel stages with bulk copies (the payload only aligns tensors to words)
+  DevBuf<float> gate_w;
   // MLP
   const uint8_t *gate = nullptr, *up = nullptr, *down = nullptr;
   int mlp_fmt = kQ4K, down_fmt = kQ4K;
@@ -366,8 +369,16 @@ struct Engine {
                 "recurrent alpha/beta projections must be F32 in this build");
         require((static_cast<size_t>(std::max(at_a, at_b)) * 4 + static_cast<size_t>(H) * D * 4) <= matrices.n,
                 "alpha/beta beyond geometry_weights");
-        L->wa = reinterpret_cast<const float*>(matrices.p + static_cast<size_t>(at_a) * 4);
-        L->wb = reinterpret_cast<const float*>(matrices.p + static_cast<size_t>(at_b) * 4);
+        const size_t hd_floats = static_cast<size_t>(H) * D;
+        L->gate_w.alloc(2 * hd_floats + D);
+        RTA_CUDA(cudaMemcpyAsync(L->gate_w.p, matrices.p + static_cast<size_t>(at_a) * 4, hd_floats * 4,
+                                 cudaMemcpyDeviceToDevice, stream));
+        RTA_CUDA(cudaMemcpyAsync(L->gate_w.p + hd_floats, matrices.p + static_cast<size_t>(at_b) * 4, hd_floats * 4,
+                                 cudaMemcpyDeviceToDevice, stream));
+        RTA_CUDA(cudaMemcpyAsync(L->gate_w.p + 2 * hd_floats, L->attn_norm, static_cast<size_t>(D) * 4,
+                                 cudaMemcpyDeviceToDevice, stream));
+        L->wa = L->gate_w.p;
+        L->wb = L->gate_w.p + hd_floats;
         L->dt_bias = pf(word(base + 37u), H);
         L->a_log = pf(word(base + 38u), H);
         L->conv_w = pf(word(base + 34u), 3ull * Sw * 4);
@@ -414,8 +425,14 @@ struct Engine {
     // splits (about eight waves of CTAs in all) keep the longest histories' CTAs
     // short next to the ragged mean without paying every split's fixed cost
     // (query load, combine, record, merge) for the short ones.
+    // Several sequences: splits in proportion to each sequence's history
+    // (AttnParams::split_by_length), up to capacity / 2048 of them, so a split
+    // covers up to ~2048 positions whatever the history (config 5: 4 splits for
+    // the longest histories, 1 for the shortest; measured against 512 / 1024 /
+    // 1536 positions per split and against a uniform split count).
     const uint32_t fill = (8u * static_cast<uint32_t>(sms) + spec.kv_heads * nseq - 1u) / (spec.kv_heads * nseq);
-    nsplit = std::max(1u, std::min({static_cast<uint32_t>(sms) / spec.kv_heads, capacity / 256u, fill}));
+    nsplit = nseq > 1u ? std::max(1u, std::min(static_cast<uint32_t>(sms) / spec.kv_heads, capacity / 2048u))
+                       : std::max(1u, std::min({static_cast<uint32_t>(sms) / spec.kv_heads, capacity / 256u, fill}));
     const size_t recs = static_cast<size_t>(nseq) * spec.kv_heads * nsplit * 4;
     part_m.alloc(recs);
     part_z.alloc(recs);
@@ -640,6 +657,7 @@ struct Engine {
         ap.part_o = part_o.p;
         ap.err = &c->err;
         ap.running = running;
+        ap.split_by_length = nseq > 1u ? 1u : 0u;
         RTA_CUDA(launch_attention(ap, nsplit, nseq, true, s));
         GemvArgs o;
         o.fmt = L.o_fmt;
@@ -679,7 +697,7 @@ struct Engine {
         RTA_CUDA(matmul(g, s));
         GdnParams gp;
         gp.x = state.p;
-        gp.attn_norm = L.attn_norm;
+        gp.attn_norm = L.gate_w.p + 2ull * spec.state_heads * D;  // aligned copy of L.attn_norm
         gp.eps = spec.norm_epsilon;
         gp.wa = L.wa;
         gp.wb = L.wb;
@@ -699,6 +717,7 @@ struct Engine {
         gp.H = spec.state_heads;
         gp.KH = spec.state_key_heads;
         gp.pos = &c->pos_cur;
+        gp.err = &c->err;
         gp.running = running;
         RTA_CUDA(launch_gdn(gp, s, true));
         GemvArgs o;

@@ -181,8 +181,11 @@ __global__ void __launch_bounds__(256) attn_prep_kernel(PrepParams p) {
 // Latency layout: the kernel is a short chain of dependent steps, so everything
 // that does not depend on the preceding kernels (this CTA's state rows, the
 // gate / norm / conv weights, the conv history) is requested before
-// griddepcontrol.wait -- state rows into registers, the rest into L2 -- and the
-// block reductions carry several values per barrier.  A few sequences split
+// griddepcontrol.wait -- state rows into registers; the gate and norm weights
+// into registers (16-row CTAs) or by bulk copies into shared memory together
+// with the hidden row after the wait (128-row CTAs, the batch case: 64 KB of
+// inputs per CTA in three copies instead of 64 dependent L2 loads per thread)
+// -- and the block reductions carry several values per barrier.  A few sequences split
 // each head's rows over 8 CTAs (16 rows: parallelism for one token); many
 // sequences give each (sequence, head) one CTA of all 128 rows, so the gates,
 // norms and convolutions (64 KB of L2 reads over x and the gate rows) are
@@ -228,10 +231,15 @@ __device__ __forceinline__ void block_sums(float (&v)[N], float* red) {
 constexpr uint32_t kGdnDPer = 16;  // hidden values per thread: hidden size <= 4096
 
 template <uint32_t ROWS>
-__global__ void __launch_bounds__(256) gdn_kernel(GdnParams p) {
+__global__ void __launch_bounds__(256, ROWS > 16u ? 2 : 1) gdn_kernel(GdnParams p) {
   constexpr uint32_t kGdnRows = ROWS, kGdnRowsPerWarp = ROWS / 8u;
   __shared__ float red1[8], red2[16], red3[16];
   __shared__ float qn[128], kn[128], vv[kGdnRows];
+  // Many CTAs (ROWS > 16): the head's gate rows, the norm weight and the hidden
+  // row are staged by bulk copies, [wa D | wb D | norm D | x D] floats
+  extern __shared__ __align__(16) float gdn_stage[];
+  __shared__ __align__(8) uint64_t gdn_bar[2];
+  __shared__ int gdn_ok;
   const uint32_t h = blockIdx.x, slice = blockIdx.y, z = blockIdx.z, tid = threadIdx.x;
   const uint32_t HD = 128u, S = p.H * HD, K = p.KH * HD, kh = h % p.KH;
   const uint32_t warp = tid >> 5, lane = tid & 31u;
@@ -264,11 +272,17 @@ __global__ void __launch_bounds__(256) gdn_kernel(GdnParams p) {
       wb[i] = in ? p.wb[static_cast<size_t>(h) * p.D + c] : 0.f;
     }
   } else {
-    for (uint32_t c = tid * 32u; c < p.D; c += 256u * 32u) {  // one 128-byte line per thread
-      asm volatile("prefetch.global.L2 [%0];" ::"l"(p.wa + static_cast<size_t>(h) * p.D + c));
-      asm volatile("prefetch.global.L2 [%0];" ::"l"(p.wb + static_cast<size_t>(h) * p.D + c));
-      asm volatile("prefetch.global.L2 [%0];" ::"l"(p.attn_norm + c));
+    if (tid == 0) {  // constant weights: requested before the wait
+      mbar_init(&gdn_bar[0], 1);
+      mbar_init(&gdn_bar[1], 1);
+      fence_mbar_init();
+      const uint32_t bytes = p.D * 4u;
+      mbar_expect_tx(&gdn_bar[0], 3u * bytes);
+      bulk_g2s(gdn_stage, p.wa + static_cast<size_t>(h) * p.D, bytes, &gdn_bar[0]);
+      bulk_g2s(gdn_stage + p.D, p.wb + static_cast<size_t>(h) * p.D, bytes, &gdn_bar[0]);
+      bulk_g2s(gdn_stage + 2u * p.D, p.attn_norm, bytes, &gdn_bar[0]);
     }
+    __syncthreads();  // barriers initialised before anyone waits on them
   }
   // The conv history is double-buffered by position parity; the position is
   // written by this step's embed kernel, so both buffers are read here and the
@@ -305,9 +319,22 @@ __global__ void __launch_bounds__(256) gdn_kernel(GdnParams p) {
       const uint32_t c = tid + 256u * i;
       xr[i] = c < p.D ? x_seq[c] : 0.f;
     }
+  } else if (tid == 0) {
+    mbar_expect_tx(&gdn_bar[1], p.D * 4u);
+    bulk_g2s(gdn_stage + 3u * p.D, x_seq, p.D * 4u, &gdn_bar[1]);
   }
   const float raw_q = proj[tid < 128u ? kh * HD + tid : K + kh * HD + (tid - 128u)];
   const float raw_v = tid < kGdnRows ? proj[2u * K + h * HD + slice * kGdnRows + tid] : 0.f;
+  if constexpr (!kHold) {  // both copies land (bounded) before the CTA may leave
+    if (tid == 0) {
+      uint32_t* err = p.err ? p.err + static_cast<size_t>(z) * p.ctrl_step : nullptr;
+      const bool a_ok = mbar_wait(&gdn_bar[0], 0u, err);
+      const bool b_ok = mbar_wait(&gdn_bar[1], 0u, err);
+      gdn_ok = a_ok && b_ok ? 1 : 0;
+    }
+    __syncthreads();
+    if (!gdn_ok) return;
+  }
   if (run == 0u) return;
   const uint32_t par = posv & 1u;
   float* next = conv_state + (par ^ 1u) * buf;
@@ -321,7 +348,8 @@ __global__ void __launch_bounds__(256) gdn_kernel(GdnParams p) {
     for (uint32_t i = 0; i < kPer; ++i)
       if (tid + 256u * i < p.D) ss[0] += xr[i] * xr[i];
   } else {
-    for (uint32_t c = tid; c < p.D; c += 256u) ss[0] += x_seq[c] * x_seq[c];
+    const float* xs = gdn_stage + 3u * p.D;
+    for (uint32_t c = tid; c < p.D; c += 256u) ss[0] += xs[c] * xs[c];
   }
   block_sums<1>(ss, red1);
   const float inv = rsqrtf(ss[0] / static_cast<float>(p.D) + p.eps);
@@ -335,10 +363,11 @@ __global__ void __launch_bounds__(256) gdn_kernel(GdnParams p) {
       ab[1] += xn * wb[i];
     }
   } else {
+    const float *was = gdn_stage, *wbs = gdn_stage + p.D, *nws = gdn_stage + 2u * p.D, *xs = gdn_stage + 3u * p.D;
     for (uint32_t c = tid; c < p.D; c += 256u) {
-      const float xn = x_seq[c] * inv * p.attn_norm[c];
-      ab[0] += xn * p.wa[static_cast<size_t>(h) * p.D + c];
-      ab[1] += xn * p.wb[static_cast<size_t>(h) * p.D + c];
+      const float xn = xs[c] * inv * nws[c];
+      ab[0] += xn * was[c];
+      ab[1] += xn * wbs[c];
     }
   }
 
@@ -439,9 +468,33 @@ cudaError_t launch_attn_prep(const PrepParams& p, cudaStream_t s, bool pdl) {
 cudaError_t launch_gdn(const GdnParams& p, cudaStream_t s, bool pdl) {
   if (p.D == 0 || p.D > 256u * kGdnDPer) return cudaErrorInvalidValue;
   void* args[] = {const_cast<GdnParams*>(&p)};
-  if (p.H * p.nseq >= 2u * 148u)  // enough (sequence, head) pairs to fill the GPU with whole heads
-    return launch_pdl(reinterpret_cast<const void*>(gdn_kernel<kGdnRowsBatch>), dim3(p.H, 1, p.nseq), dim3(256),
-                      args, s, pdl);
+  if (p.H * p.nseq >= 2u * 148u) {  // enough (sequence, head) pairs to fill the GPU with whole heads
+    // bulk-copy staging: 16-byte aligned sources, sizes a multiple of 16 bytes
+    if (p.D % 4u || (reinterpret_cast<uintptr_t>(p.wa) | reinterpret_cast<uintptr_t>(p.wb) |
+                     reinterpret_cast<uintptr_t>(p.attn_norm) | reinterpret_cast<uintptr_t>(p.x)) % 16u)
+      return cudaErrorMisalignedAddress;
+    const uint32_t smem = 16u * p.D;
+    static int attr_dev[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_dev[dev]) {
+      const cudaError_t e = cudaFuncSetAttribute(gdn_kernel<kGdnRowsBatch>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, 16 * 4096);
+      if (e != cudaSuccess) return e;
+      attr_dev[dev] = 1;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.H, 1, p.nseq);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelExC(&cfg, reinterpret_cast<const void*>(gdn_kernel<kGdnRowsBatch>), args);
+  }
   return launch_pdl(reinterpret_cast<const void*>(gdn_kernel<kGdnRowsSmall>),
                     dim3(p.H, 128u / kGdnRowsSmall, p.nseq), dim3(256), args, s, pdl);
 }

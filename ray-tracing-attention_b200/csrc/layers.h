@@ -73,6 +73,7 @@ struct GdnParams {
   uint32_t D = 0, H = 0, KH = 0;
   const uint32_t* pos = nullptr;      // sequence z reads pos[z * ctrl_step]
   const uint32_t* running = nullptr;  // likewise
+  uint32_t* err = nullptr;            // device error words, likewise (bounded staging waits)
   uint32_t nseq = 1, ctrl_step = 0;
   size_t proj_seq = 0;                // floats between sequences' projections
   size_t conv_seq = 0, rec_seq = 0;   // floats between sequences' conv history / recurrent state
