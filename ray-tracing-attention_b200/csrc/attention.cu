@@ -30,7 +30,8 @@ namespace {
 constexpr int kWarps = 4;
 constexpr int kThreads = 128;
 constexpr int kTile = 16;      // positions per stage
-constexpr int kStages = 8;     // two per warp
+constexpr int kStages = 8;     // two per warp (one long history: all splits resident at once)
+constexpr int kStagesMany = 4;  // one per warp, three CTAs per SM (several waves of splits)
 constexpr int kHD = 256;       // head dimension handled by this kernel
 constexpr int kRowBytes = kHD * 2 + 16;
 constexpr int kStageBytes = 2 * kTile * kRowBytes;  // K rows then V rows
@@ -74,7 +75,13 @@ __device__ __forceinline__ uint32_t used_splits(const AttnParams& p, uint32_t n,
   return want < 1u ? 1u : want > nsplit ? nsplit : want;
 }
 
+// STAGES (a multiple of kWarps: warp w owns stages w, w + 4, ...): 8 when the
+// splits fit in one wave of CTAs, 4 when they take several waves, so that three
+// CTAs share an SM and overlap each other's stage waits.
+template <int STAGES>
 __global__ void __launch_bounds__(kThreads) attention_split_kernel(const AttnParams p) {
+  static_assert(STAGES % kWarps == 0, "stages are owned by warps");
+  constexpr int kStages = STAGES;
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
   __half* pbuf = reinterpret_cast<__half*>(smem + kStages * kStageBytes + 128);  // [warp][8 cols][16 pos]
@@ -534,7 +541,7 @@ __global__ void __launch_bounds__(kHD) attention_merge_kernel(const AttnParams p
 
 }  // namespace
 
-size_t attention_smem_bytes() { return kStages * kStageBytes + 128 + kWarps * 8 * kTile * 2; }
+size_t attention_smem_bytes(int stages) { return stages * kStageBytes + 128 + kWarps * 8 * kTile * 2; }
 
 cudaError_t launch_attention_merge(const AttnParams& p, uint32_t nsplit, uint32_t nseq, bool pdl, cudaStream_t s) {
   cudaLaunchAttribute attr[1];
@@ -574,18 +581,24 @@ cudaError_t launch_attention(const AttnParams& p, uint32_t nsplit, uint32_t nseq
   if (reinterpret_cast<uintptr_t>(p.k) % 16 || reinterpret_cast<uintptr_t>(p.v) % 16 || p.pos_stride % 8 ||
       p.kv_stride % 8 || p.seq_stride % 8)
     return cudaErrorMisalignedAddress;
-  const size_t smem = attention_smem_bytes();
   static bool attr_set[64] = {false};  // one-time per-device kernel setup, off the per-launch path
+  static int sms_of[64] = {0};
   cudaError_t e = cudaSuccess;
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!attr_set[dev]) {
-    e = cudaFuncSetAttribute(attention_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem));
+    e = cudaFuncSetAttribute(attention_split_kernel<kStages>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(attention_smem_bytes(kStages)));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(attention_split_kernel<kStagesMany>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(attention_smem_bytes(kStagesMany)));
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms_of[dev], cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
+  const bool many = static_cast<uint64_t>(nsplit) * p.kvh * nseq > static_cast<uint64_t>(sms_of[dev]);
+  const size_t smem = attention_smem_bytes(many ? kStagesMany : kStages);
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
@@ -596,7 +609,8 @@ cudaError_t launch_attention(const AttnParams& p, uint32_t nsplit, uint32_t nseq
   cfg.stream = s;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, attention_split_kernel, p);
+  e = many ? cudaLaunchKernelEx(&cfg, attention_split_kernel<kStagesMany>, p)
+           : cudaLaunchKernelEx(&cfg, attention_split_kernel<kStages>, p);
   if (e != cudaSuccess) return e;
   return launch_attention_merge(p, nsplit, nseq, pdl, s);
 }

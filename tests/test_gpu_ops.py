@@ -138,7 +138,7 @@ def test_readout_tie_goes_to_lowest_id(ops):
     assert int(_np(arg)[0]) == 77
 
 
-def _attention_case(ops, q, keys, values, gate, time, capacity, layout="LHD"):
+def _attention_case(ops, q, keys, values, gate, time, capacity, layout="LHD", splits=None):
     """Run the CUDA kernel with fp16 K/V; return (out, phys, oracle_out, oracle_phys)."""
     import torch
     count = keys.shape[0]
@@ -158,7 +158,7 @@ def _attention_case(ops, q, keys, values, gate, time, capacity, layout="LHD"):
             _t(np.ascontiguousarray(slots[1].transpose(1, 0, 2)))
         pos_stride, kv_stride = 1, capacity
     out, phys, ws = ops.attention_decode_f16(_t(q), kd, vd, time, capacity, pos_stride, kv_stride,
-                                             gate=None if gate is None else _t(gate))
+                                             gate=None if gate is None else _t(gate), splits=splits)
     torch.cuda.synchronize()
     assert ops.workspace_error(ws) == 0
     want, want_phys = oracle.attention(q[None], k16.astype(np.float32), v16.astype(np.float32),
@@ -173,6 +173,21 @@ def test_attention_config2_parity(ops, L):
     keys = rng.normal(0, 1, (L, 4, 256)).astype(np.float32)
     values = rng.normal(0, 1, (L, 4, 256)).astype(np.float32)
     out, phys, want, want_phys = _attention_case(ops, q, keys, values, None, L - 1, L)
+    assert rel_l2(out, want) < TOL
+    np.testing.assert_allclose(phys, want_phys, rtol=1e-4, atol=1e-4)
+
+
+@pytest.mark.parametrize("L,splits", [(4096, 64), (5000, 48), (300, 40)])
+def test_attention_many_splits(ops, L, splits):
+    """More split CTAs than SMs (64 x 4 KV heads, 48 x 4, 40 x 4): the four-stage
+    kernel that runs several CTAs per SM; 300 positions over 40 splits leaves
+    most of them empty."""
+    rng = np.random.default_rng(L + splits)
+    q = rng.normal(0, 1, (16, 256)).astype(np.float32)
+    keys = rng.normal(0, 1, (L, 4, 256)).astype(np.float32)
+    values = rng.normal(0, 1, (L, 4, 256)).astype(np.float32)
+    gate = rng.normal(0, 2, (16, 256)).astype(np.float32)
+    out, phys, want, want_phys = _attention_case(ops, q, keys, values, gate, L - 1, L, splits=splits)
     assert rel_l2(out, want) < TOL
     np.testing.assert_allclose(phys, want_phys, rtol=1e-4, atol=1e-4)
 
