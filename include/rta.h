@@ -197,7 +197,8 @@ RTA_API rta_status rta_readout(int format, const void* w, uint32_t vocab, uint32
  *   attends to positions [max(0, time-capacity+1), time] (slot p % capacity).
  *   gate [heads][head_dim] or NULL: out *= sigmoid(gate)
  *   out  [heads][head_dim];  phys [heads][2] = (max + 20, Z) or NULL.
- * head_dim must be 256 and heads == 4 * kv_heads.  Replaces the S_t/R_t detector
+ * head_dim must be 256, heads == 4 * kv_heads and 1 <= splits <= 1024 (history
+ * splits per KV head, merged after).  Replaces the S_t/R_t detector
  * (ray_tracing/native/shaders/resident_ray.comp:97-117 and
  *  resident_detector_ordered_{scores,normalize,value}.comp). */
 RTA_API size_t rta_attention_workspace_bytes(uint32_t heads, uint32_t kv_heads, uint32_t head_dim, uint32_t splits);

@@ -503,10 +503,17 @@ __global__ void __launch_bounds__(kThreads) attention_packet_split_kernel(const 
 
 // Merge the split records of every (sequence, head): m = max m_s,
 // Z = sum Z_s e^(m_s-m), U = sum U_s e^(m_s-m), out = U/max(Z,1e-30)*gate.
+// The split maxima and the weights e^(m_s-m) are formed once per CTA (one
+// split per thread), so only the value rows are walked per output dimension,
+// with several loads in flight.
+constexpr uint32_t kMaxMergeSplits = 1024;
 __global__ void __launch_bounds__(kHD) attention_merge_kernel(const AttnParams p, uint32_t nsplit) {
+  __shared__ float es[kMaxMergeSplits];
+  __shared__ float red[kHD / 32];
   pdl_wait();
   pdl_launch_dependents();
   const uint32_t head = blockIdx.x, z = blockIdx.y, d = threadIdx.x;
+  const uint32_t lane = d & 31u, warp = d >> 5;
   const uint32_t run = p.running ? p.running[z * p.ctrl_step] : 1u;  // checked once the maxima are in
   const uint32_t kv = head / kGroup, h = head % kGroup;
   const size_t rec0 = (static_cast<size_t>(z) * p.kvh + kv) * nsplit;
@@ -515,18 +522,42 @@ __global__ void __launch_bounds__(kHD) attention_merge_kernel(const AttnParams p
     window(p, z, t, lo, n);
     nsplit = used_splits(p, n, nsplit);
   }
-  float m = -INFINITY;
-  for (uint32_t s = 0; s < nsplit; ++s) m = fmaxf(m, p.part_m[(rec0 + s) * kGroup + h]);
+  float mloc = -INFINITY;
+  for (uint32_t s = d; s < nsplit; s += kHD) {
+    const float ms = p.part_m[(rec0 + s) * kGroup + h];
+    es[s] = ms;
+    mloc = fmaxf(mloc, ms);
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, o));
+  if (lane == 0) red[warp] = mloc;
+  __syncthreads();
+  float m = red[0];
+#pragma unroll
+  for (uint32_t w = 1; w < kHD / 32u; ++w) m = fmaxf(m, red[w]);
   if (run == 0u) return;
-  float zs = 0.f, os = 0.f;
-  if (m != -INFINITY)
-    for (uint32_t s = 0; s < nsplit; ++s) {
-      const float ms = p.part_m[(rec0 + s) * kGroup + h];
-      if (ms == -INFINITY) continue;
-      const float e = expf(ms - m);
-      zs += p.part_z[(rec0 + s) * kGroup + h] * e;
-      os += p.part_o[((rec0 + s) * kGroup + h) * kHD + d] * e;
-    }
+  float zloc = 0.f;
+  for (uint32_t s = d; s < nsplit; s += kHD) {  // this thread's own entries of es
+    const float ms = es[s];
+    const float e = (ms == -INFINITY || m == -INFINITY) ? 0.f : expf(ms - m);
+    es[s] = e;
+    if (e != 0.f) zloc += p.part_z[(rec0 + s) * kGroup + h] * e;
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) zloc += __shfl_xor_sync(0xffffffffu, zloc, o);
+  __syncthreads();  // maxima read by every thread before red is reused; weights visible
+  if (lane == 0) red[warp] = zloc;
+  __syncthreads();
+  float zs = 0.f;
+#pragma unroll
+  for (uint32_t w = 0; w < kHD / 32u; ++w) zs += red[w];
+  float os = 0.f;
+  const float* po = p.part_o + (rec0 * kGroup + h) * kHD + d;
+#pragma unroll 8
+  for (uint32_t s = 0; s < nsplit; ++s) {
+    const float e = es[s];
+    if (e != 0.f) os += po[static_cast<size_t>(s) * kGroup * kHD] * e;
+  }
   float v = os / fmaxf(zs, 1e-30f);
   if (p.gate) v *= detector_sigmoid(p.gate[static_cast<size_t>(z) * p.gate_seq_stride + static_cast<size_t>(head) * kHD + d]);
   uint32_t od = d;
@@ -558,7 +589,7 @@ cudaError_t launch_attention_merge(const AttnParams& p, uint32_t nsplit, uint32_
 
 cudaError_t launch_attention(const AttnParams& p, uint32_t nsplit, uint32_t nseq, bool pdl, cudaStream_t s) {
   if (p.hd != kHD || p.heads != p.kvh * kGroup || !p.q || !p.out || !p.part_m || !p.part_z || !p.part_o ||
-      nsplit == 0 || nseq == 0 || p.capacity == 0)
+      nsplit == 0 || nsplit > kMaxMergeSplits || nseq == 0 || p.capacity == 0)
     return cudaErrorInvalidValue;
   if (p.packets) {  // the reference's packet history
     if (p.packet_stride != packet_bytes(p.kvh) || p.packet_stride % 8 || p.packet_seq_stride % 8 ||

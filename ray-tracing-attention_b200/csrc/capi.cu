@@ -331,8 +331,8 @@ rta_status rta_attention_decode_f16(const float* q, const void* k, const void* v
                                     uint32_t kv_stride, const float* gate, float* out, float* phys, uint32_t splits,
                                     void* workspace, size_t workspace_bytes, void* stream) {
   if (!q || !k || !v || !out || !workspace || head_dim != 256 || kv_heads == 0 || heads != 4 * kv_heads ||
-      capacity == 0 || splits == 0)
-    return fail(RTA_E_ARG, "rta_attention_decode_f16: head_dim 256, heads == 4*kv_heads, capacity and splits > 0");
+      capacity == 0 || splits == 0 || splits > 1024)
+    return fail(RTA_E_ARG, "rta_attention_decode_f16: head_dim 256, heads == 4*kv_heads, capacity > 0, 1 <= splits <= 1024");
   if (workspace_bytes < rta_attention_workspace_bytes(heads, kv_heads, head_dim, splits))
     return fail(RTA_E_ARG, "rta_attention_decode_f16: workspace too small");
   uint8_t* ws = static_cast<uint8_t*>(workspace);

@@ -425,13 +425,14 @@ struct Engine {
     // splits (about eight waves of CTAs in all) keep the longest histories' CTAs
     // short next to the ragged mean without paying every split's fixed cost
     // (query load, combine, record, merge) for the short ones.
-    // Several sequences: splits in proportion to each sequence's history
+    // Many sequences (the tensor-core regime; below it a batch keeps the
+    // single-sequence arithmetic): splits in proportion to each sequence's history
     // (AttnParams::split_by_length), up to capacity / 2048 of them, so a split
     // covers up to ~2048 positions whatever the history (config 5: 4 splits for
     // the longest histories, 1 for the shortest; measured against 512 / 1024 /
     // 1536 positions per split and against a uniform split count).
     const uint32_t fill = (8u * static_cast<uint32_t>(sms) + spec.kv_heads * nseq - 1u) / (spec.kv_heads * nseq);
-    nsplit = nseq > 1u ? std::max(1u, std::min(static_cast<uint32_t>(sms) / spec.kv_heads, capacity / 2048u))
+    nsplit = nseq >= kTcMinSeq ? std::max(1u, std::min(static_cast<uint32_t>(sms) / spec.kv_heads, capacity / 2048u))
                        : std::max(1u, std::min({static_cast<uint32_t>(sms) / spec.kv_heads, capacity / 256u, fill}));
     const size_t recs = static_cast<size_t>(nseq) * spec.kv_heads * nsplit * 4;
     part_m.alloc(recs);
@@ -657,7 +658,7 @@ struct Engine {
         ap.part_o = part_o.p;
         ap.err = &c->err;
         ap.running = running;
-        ap.split_by_length = nseq > 1u ? 1u : 0u;
+        ap.split_by_length = nseq >= kTcMinSeq ? 1u : 0u;
         RTA_CUDA(launch_attention(ap, nsplit, nseq, true, s));
         GemvArgs o;
         o.fmt = L.o_fmt;
