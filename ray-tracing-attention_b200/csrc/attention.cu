@@ -554,9 +554,10 @@ __global__ void __launch_bounds__(kHD) attention_merge_kernel(const AttnParams p
   float os = 0.f;
   const float* po = p.part_o + (rec0 * kGroup + h) * kHD + d;
 #pragma unroll 8
-  for (uint32_t s = 0; s < nsplit; ++s) {
+  for (uint32_t s = 0; s < nsplit; ++s) {  // every record below nsplit is written (empty ones as zeros)
     const float e = es[s];
-    if (e != 0.f) os += po[static_cast<size_t>(s) * kGroup * kHD] * e;
+    const float ov = po[static_cast<size_t>(s) * kGroup * kHD];  // unconditional: the loads go out together
+    os += e != 0.f ? ov * e : 0.f;
   }
   float v = os / fmaxf(zs, 1e-30f);
   if (p.gate) v *= detector_sigmoid(p.gate[static_cast<size_t>(z) * p.gate_seq_stride + static_cast<size_t>(head) * kHD + d]);
