@@ -62,7 +62,7 @@ namespace tc {
 constexpr uint32_t kThreads = 608;  // 19 warps
 constexpr uint32_t kTileRows = 128;
 constexpr uint32_t kQ4KPanel = 128u * kQ4KBytes, kQ6KPanel = 128u * kQ6KBytes;  // 18432, 26880
-constexpr uint32_t kAStages = 3, kScaleSlots = 4;  // tensor-memory A stages; block-scale ring slots
+constexpr uint32_t kAStages = 3;  // tensor-memory A stages
 __host__ __device__ constexpr uint32_t b_stages(uint32_t N) { return N <= 32u ? 8u : 4u; }  // activation ring
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kAColBase = 256, kA2ColBase = 448;  // tensor-memory columns of the A / A2 stages
@@ -129,6 +129,13 @@ __device__ __forceinline__ __half2 bits_h2(uint32_t u) {
 __device__ __forceinline__ uint32_t hfma2_bits(uint32_t a, __half2 b, __half2 c) {
   return h2_bits(__hfma2(bits_h2(a), b, c));
 }
+__device__ __forceinline__ uint32_t hmul2_bits(uint32_t a, __half2 b) { return h2_bits(__hmul2(bits_h2(a), b)); }
+__device__ __forceinline__ uint32_t hsub2_bits(uint32_t a, __half2 b) { return h2_bits(__hsub2(bits_h2(a), b)); }
+
+// The block scales are folded into the fp16 operand, pre-multiplied by 2^6 so
+// that small weights stay clear of fp16 subnormals (|w| < 1023 stays finite);
+// the epilogue multiplies the accumulator by 2^-6.
+constexpr float kOperandScale = 64.0f;
 
 // Shared-memory matrix descriptor, K-major, no swizzle: 8-row x 16-byte core
 // matrices, `lbo` bytes between the two core matrices of one K=16 step, `sbo`
@@ -242,8 +249,11 @@ __device__ __forceinline__ Q6Words load_q6(const uint8_t* panel, uint32_t m, uin
 
 // Row m's 64 coefficients 128h + 64j .. +63 of one Q4_K panel -> 32 tensor-
 // memory columns (fp16 pairs sc*q), plus (h == 0, j == 0) the 8 mins columns.
+// Q4_K operand: the codes centred on 8, sc*(q-8) (exact), times 2^6 d (one
+// rounding); the mins term carries 2^6 (8 d sc - dmin m) per group, so the two
+// rounded terms stay small next to the weight they sum to.
 __device__ __forceinline__ void dequant_q4(const Q4Words& cw, const uint4& hdr, uint32_t h, uint32_t j, uint32_t tcol,
-                                           uint32_t a2col) {
+                                           uint32_t a2col, __half2 dd, float d64, float dmin64) {
   const uint32_t pl = 2u * h + j;
   uint32_t sc0, mn0, sc1, mn1;
   q4_scale_min(hdr, 2u * pl, sc0, mn0);
@@ -252,16 +262,17 @@ __device__ __forceinline__ void dequant_q4(const Q4Words& cw, const uint4& hdr, 
   // high nibbles hold 1024 + 16q: (1024+16q)*(sc/16) - 64*sc.  Both exact.
   const __half2 s0 = __float2half2_rn(static_cast<float>(sc0)), k0 = __float2half2_rn(-1024.f * sc0);
   const __half2 s1 = __float2half2_rn(static_cast<float>(sc1) * 0.0625f), k1 = __float2half2_rn(-64.f * sc1);
+  const __half2 e0 = __float2half2_rn(8.f * sc0), e1 = __float2half2_rn(8.f * sc1);  // centre: q -> q - 8
   const uint32_t words[8] = {cw.c0.x, cw.c0.y, cw.c0.z, cw.c0.w, cw.c1.x, cw.c1.y, cw.c1.z, cw.c1.w};
   uint32_t lo[16], hi[16];
 #pragma unroll
   for (int w = 0; w < 8; ++w) {
     const uint32_t p01 = __byte_perm(words[w], 0x64646464u, 0x5140u);
     const uint32_t p23 = __byte_perm(words[w], 0x64646464u, 0x5342u);
-    lo[2 * w] = hfma2_bits(p01 & 0xFF0FFF0Fu, s0, k0);
-    lo[2 * w + 1] = hfma2_bits(p23 & 0xFF0FFF0Fu, s0, k0);
-    hi[2 * w] = hfma2_bits(p01 & 0xFFF0FFF0u, s1, k1);
-    hi[2 * w + 1] = hfma2_bits(p23 & 0xFFF0FFF0u, s1, k1);
+    lo[2 * w] = hmul2_bits(hsub2_bits(hfma2_bits(p01 & 0xFF0FFF0Fu, s0, k0), e0), dd);
+    lo[2 * w + 1] = hmul2_bits(hsub2_bits(hfma2_bits(p23 & 0xFF0FFF0Fu, s0, k0), e0), dd);
+    hi[2 * w] = hmul2_bits(hsub2_bits(hfma2_bits(p01 & 0xFFF0FFF0u, s1, k1), e1), dd);
+    hi[2 * w + 1] = hmul2_bits(hsub2_bits(hfma2_bits(p23 & 0xFFF0FFF0u, s1, k1), e1), dd);
   }
   tmem_st16(tcol + 32u * j, lo);
   tmem_st16(tcol + 32u * j + 16u, hi);
@@ -272,7 +283,8 @@ __device__ __forceinline__ void dequant_q4(const Q4Words& cw, const uint4& hdr, 
       uint32_t sa, ma, sb, mb;
       q4_scale_min(hdr, 2u * p, sa, ma);
       q4_scale_min(hdr, 2u * p + 1u, sb, mb);
-      mv[p] = mv[4 + p] = h2_bits(__floats2half2_rn(static_cast<float>(ma), static_cast<float>(mb)));
+      mv[p] = mv[4 + p] = h2_bits(__floats2half2_rn(8.f * d64 * static_cast<float>(sa) - dmin64 * static_cast<float>(ma),
+                                                     8.f * d64 * static_cast<float>(sb) - dmin64 * static_cast<float>(mb)));
     }
     tmem_st8(a2col, mv);
   }
@@ -285,7 +297,7 @@ __device__ __forceinline__ void dequant_q4(const Q4Words& cw, const uint4& hdr, 
 // two high bits (at bits 8-9) from the permute of the pre-shifted qh word:
 // 0x6400 | 16q = 1024 + 16q, then (1024 + 16q)*(sc/16) - 96*sc = sc*(q-32).
 __device__ __forceinline__ void dequant_q6(const Q6Words& cw, const uint4& s4, uint32_t h, uint32_t j,
-                                           uint32_t tcol) {
+                                           uint32_t tcol, __half2 dd) {
   const uint32_t qlw[8] = {cw.l0.x, cw.l0.y, cw.l0.z, cw.l0.w, cw.l1.x, cw.l1.y, cw.l1.z, cw.l1.w};
   const uint32_t qhw[8] = {cw.g0.x, cw.g0.y, cw.g0.z, cw.g0.w, cw.g1.x, cw.g1.y, cw.g1.z, cw.g1.w};
   // int8 scales 8h + 2j + u (low run) and 8h + 4 + 2j + u (high run), u = 0, 1:
@@ -315,8 +327,8 @@ __device__ __forceinline__ void dequant_q6(const Q6Words& cw, const uint4& s4, u
       const uint32_t sel_h = pr == 0 ? 0x1404u : 0x3424u;  // the same bytes -> high byte of each half
       const uint32_t al = __byte_perm(qs, 0x64646464u, sel_l), ah = __byte_perm(qlw[w], 0x64646464u, sel_l);
       const uint32_t bl = __byte_perm(hl, 0u, sel_h), bh = __byte_perm(hh, 0u, sel_h);
-      lo[2 * w + pr] = hfma2_bits((al & kSel) | (bl & ~kSel), sl[u], kl[u]);
-      hi[2 * w + pr] = hfma2_bits((ah & kSel) | (bh & ~kSel), sh[u], kh[u]);
+      lo[2 * w + pr] = hmul2_bits(hfma2_bits((al & kSel) | (bl & ~kSel), sl[u], kl[u]), dd);
+      hi[2 * w + pr] = hmul2_bits(hfma2_bits((ah & kSel) | (bh & ~kSel), sh[u], kh[u]), dd);
     }
   }
   tmem_st16(tcol + 16u * j, lo);
@@ -329,7 +341,7 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 19 warps: <
   using C = Cfg<FMT>;
   constexpr bool kQ4 = C::kQ4;
   constexpr uint32_t kPanel = C::kPanel, kRawS = C::kRawStages;
-  constexpr uint32_t kDStride = kQ4 ? 2u * N : static_cast<uint32_t>(N);  // tensor-memory columns per accumulator pair
+  constexpr uint32_t kDStride = static_cast<uint32_t>(N);  // tensor-memory columns of one accumulator
   constexpr uint32_t kBStages = b_stages(N);
   static_assert(2u * kDStride <= kAColBase, "accumulators overlap the A stages");
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -342,16 +354,11 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 19 warps: <
   uint64_t* a_empty = a_full + kAStages;
   uint64_t* d_full = a_empty + kAStages;
   uint64_t* d_empty = d_full + 2;
-  uint64_t* sc_full = d_empty + 2;
-  uint64_t* sc_empty = sc_full + kScaleSlots;
-  uint64_t* drain = sc_empty + kScaleSlots;
+  uint64_t* drain = d_empty + 2;
   uint32_t* misc = reinterpret_cast<uint32_t*>(smem + p.off_misc);
   volatile uint32_t* tmem_slot = misc;
   volatile uint32_t* abort_flag = misc + 1;
   unsigned long long* cand = reinterpret_cast<unsigned long long*>(misc + 4);  // [N] argmax candidates
-  // block scales of the 128 rows per block column, handed from the dequantizers
-  // to the epilogue: Q4_K (d, dmin) fp16 pair, Q6_K d
-  uint32_t* sc_ring = misc + 4 + 2 * N;  // [kScaleSlots][128]
 
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   // work units (tile, K slice), walked in the same order by every role
@@ -397,10 +404,6 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 19 warps: <
     for (uint32_t s = 0; s < 2; ++s) {
       mbar_init(&d_full[s], 1);
       mbar_init(&d_empty[s], 8);
-    }
-    for (uint32_t s = 0; s < kScaleSlots; ++s) {
-      mbar_init(&sc_full[s], 4);   // the four j == 0 dequantizing warps
-      mbar_init(&sc_empty[s], 8);  // the eight epilogue warps
     }
     mbar_init(drain, 1);
     fence_mbar_init();
@@ -495,20 +498,21 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 19 warps: <
     // ----------------------------------------------------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = instr_desc(N);
-      uint32_t ait = 0, bit = 0, blk = 0;
+      uint32_t ait = 0, bit = 0;
       bool stop = false;
       const uint32_t b0 = smem_u32(bst);
       for (uint32_t i = 0; i < my_tiles && !stop; ++i) {
         uint32_t t, kb0, kb1;
         unit(i, t, kb0, kb1);
-        for (uint32_t kb = kb0; kb < kb1 && !stop; ++kb, ++blk) {
-          const uint32_t buf = blk & 1u;
-          if (*abort_flag || !mbar_wait(&d_empty[buf], ((blk >> 1) & 1u) ^ 1u, p.err)) {
-            stop = true;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t d1 = tmem + buf * kDStride;
+        // one accumulator per unit (block scales are in the operand), double-buffered by unit
+        const uint32_t buf = i & 1u;
+        if (*abort_flag || !mbar_wait(&d_empty[buf], ((i >> 1) & 1u) ^ 1u, p.err)) {
+          stop = true;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d1 = tmem + buf * kDStride;
+        for (uint32_t kb = kb0; kb < kb1 && !stop; ++kb) {
           for (uint32_t h = 0; h < 2u; ++h) {
             const uint32_t as = ait % kAStages, bs = bit % kBStages;
             if (*abort_flag || !mbar_wait(&a_full[as], (ait / kAStages) & 1u, p.err) ||
@@ -519,19 +523,21 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 19 warps: <
             tc_fence_after();
             const uint32_t acol = tmem + kAColBase + 64u * as;
             const uint32_t bsa = b0 + bs * p.b_stage;
+            const bool first = kb == kb0 && h == 0u;
 #pragma unroll
             for (uint32_t kk = 0; kk < 8u; ++kk)
-              mma_ts(d1, acol + 8u * kk, smem_desc(bsa + 256u * kk, 128u, 2048u), idesc, (h | kk) != 0u ? 1u : 0u);
-            if (kQ4 && h == 0u)  // mins term: [m_G, m_G] x [X_G hi, X_G lo]
-              mma_ts(d1 + N, tmem + kA2ColBase + 8u * as, smem_desc(bsa + static_cast<uint32_t>(N) * 256u, 128u, 256u),
-                     idesc, 0u);
+              mma_ts(d1, acol + 8u * kk, smem_desc(bsa + 256u * kk, 128u, 2048u), idesc,
+                     (first && kk == 0u) ? 0u : 1u);
+            if (kQ4 && h == 0u)  // mins term: [c_G, c_G] x [X_G hi, X_G lo], c_G = 2^6 (8 d sc - dmin m), same accumulator
+              mma_ts(d1, tmem + kA2ColBase + 8u * as, smem_desc(bsa + static_cast<uint32_t>(N) * 256u, 128u, 256u),
+                     idesc, 1u);
             mma_commit(&a_empty[as]);
             mma_commit(&b_empty[bs]);
             ++ait;
             ++bit;
           }
-          if (!stop) mma_commit(&d_full[buf]);
         }
+        if (!stop) mma_commit(&d_full[buf]);
       }
       if (stop) *abort_flag = 1u;
       mma_commit(drain);  // every MMA issued above has completed once this arrives
@@ -544,52 +550,31 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 19 warps: <
     const uint32_t q = warp & 3u, m = 32u * q + lane, c0 = (warp - 2u) >> 2;  // columns c0*NH ..
     const uint32_t lane_addr = (32u * q) << 16;
     pdl_wait();  // residual targets and running flags are written by earlier kernels
-    uint32_t blk = 0;
     bool stop = false;
     for (uint32_t i = 0; i < my_tiles && !stop; ++i) {
       uint32_t t, kb0, kb1;
       unit(i, t, kb0, kb1);
       const uint32_t mat = t / tiles_per_mat, mt = t % tiles_per_mat;
-      float acc[NH];
-#pragma unroll
-      for (int n = 0; n < NH; ++n) acc[n] = 0.f;
-      for (uint32_t kb = kb0; kb < kb1; ++kb, ++blk) {
-        const uint32_t buf = blk & 1u, slot = blk % kScaleSlots;
-        if (!warp_wait(&sc_full[slot], (blk / kScaleSlots) & 1u, p.err, abort_flag)) {
-          stop = true;
-          break;
-        }
-        const uint32_t sc = sc_ring[slot * 128u + m];
-        __syncwarp();
-        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&sc_empty[slot])) : "memory");
-        if (!warp_wait(&d_full[buf], (blk >> 1) & 1u, p.err, abort_flag)) {
-          stop = true;
-          break;
-        }
-        tc_fence_after();
-        const float d = half_bits_to_float(sc), dmin = half_bits_to_float(sc >> 16);
-        const uint32_t dcol = tmem + lane_addr + buf * kDStride + c0 * NH;
-#pragma unroll
-        for (int c = 0; c < NH / 8; ++c) {
-          float v[8];
-          tmem_ld8(dcol + 8u * c, v);
-          if constexpr (kQ4) {
-            float u[8];
-            tmem_ld8(dcol + N + 8u * c, u);
-            tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 8; ++e) acc[8 * c + e] = fmaf(-dmin, u[e], fmaf(d, v[e], acc[8 * c + e]));
-          } else {
-            tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 8; ++e) acc[8 * c + e] = fmaf(d, v[e], acc[8 * c + e]);
-          }
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&d_empty[buf])) : "memory");
+      // the unit's whole sum (block scales were folded into the operand): one drain per unit
+      const uint32_t buf = i & 1u;
+      if (!warp_wait(&d_full[buf], (i >> 1) & 1u, p.err, abort_flag)) {
+        stop = true;
+        break;
       }
-      if (stop) break;
+      tc_fence_after();
+      float acc[NH];
+      const uint32_t dcol = tmem + lane_addr + buf * kDStride + c0 * NH;
+#pragma unroll
+      for (int c = 0; c < NH / 8; ++c) {
+        float v[8];
+        tmem_ld8(dcol + 8u * c, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[8 * c + e] = v[e] * (1.0f / kOperandScale);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&d_empty[buf])) : "memory");
       const uint32_t R0 = mat * p.rows + mt * kTileRows, R = R0 + m;  // output rows of the tile, this thread's
 #pragma unroll
       for (int i = 0; i < NH; ++i) {
@@ -624,12 +609,12 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 19 warps: <
     // ---------------------------------------------------------- dequantizers
     const uint32_t q = warp & 3u, j = (warp - 10u) >> 2, m = 32u * q + lane;
     const uint32_t lane_addr = (32u * q) << 16;
-    uint32_t rit = 0, ait = 0, blk = 0;
+    uint32_t rit = 0, ait = 0;
     bool stop = false;
     for (uint32_t i = 0; i < my_tiles && !stop; ++i) {
       uint32_t t, kb0, kb1;
       unit(i, t, kb0, kb1);
-      for (uint32_t kb = kb0; kb < kb1 && !stop; ++kb, ++blk) {
+      for (uint32_t kb = kb0; kb < kb1 && !stop; ++kb) {
         const uint32_t rs = rit % kRawS;
         if (!warp_wait(&raw_full[rs], (rit / kRawS) & 1u, p.err, abort_flag)) {
           stop = true;
@@ -655,16 +640,10 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 19 warps: <
         __syncwarp();
         if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&raw_empty[rs])) : "memory");
         ++rit;
-        if (j == 0u) {  // hand the row's block scales to the epilogue
-          const uint32_t slot = blk % kScaleSlots;
-          if (!warp_wait(&sc_empty[slot], ((blk / kScaleSlots) & 1u) ^ 1u, p.err, abort_flag)) {
-            stop = true;
-            break;
-          }
-          sc_ring[slot * 128u + m] = scale_word;
-          __syncwarp();
-          if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&sc_full[slot])) : "memory");
-        }
+        // the row's block scale (and Q4_K min scale) times 2^6, folded into the operand
+        const float d64 = kOperandScale * half_bits_to_float(scale_word & 0xFFFFu);
+        const float dmin64 = kOperandScale * half_bits_to_float(scale_word >> 16);  // Q4_K only
+        const __half2 dd = __float2half2_rn(d64);
         for (uint32_t h = 0; h < 2u; ++h) {
           const uint32_t as = ait % kAStages;
           if (!warp_wait(&a_empty[as], ((ait / kAStages) & 1u) ^ 1u, p.err, abort_flag)) {
@@ -675,9 +654,9 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 19 warps: <
           const uint32_t tcol = tmem + lane_addr + kAColBase + 64u * as;
           if constexpr (kQ4) {
             const uint32_t a2 = (h == 0u && j == 0u) ? tmem + lane_addr + kA2ColBase + 8u * as : 0u;
-            dequant_q4(c4[h], hdr, h, j, tcol, a2);
+            dequant_q4(c4[h], hdr, h, j, tcol, a2, dd, d64, dmin64);
           } else {
-            dequant_q6(c6[h], hdr, h, j, tcol);
+            dequant_q6(c6[h], hdr, h, j, tcol, dd);
           }
           tmem_wait_st();
           tc_fence_before();
@@ -881,7 +860,7 @@ cudaError_t launch_n(const tc::Params& p0, const tc::Prep& pr, uint32_t grid, bo
   p.off_b = (p.off_b + 1023u) / 1024u * 1024u;
   p.off_bar = p.off_b + tc::b_stages(N) * p.b_stage;
   p.off_misc = p.off_bar + 512u;
-  uint32_t smem = p.off_misc + 16u + 8u * static_cast<uint32_t>(N) + tc::kScaleSlots * 128u * 4u;
+  uint32_t smem = p.off_misc + 16u + 8u * static_cast<uint32_t>(N);
   smem = smem < tc::kMinSmem ? tc::kMinSmem : smem;
   auto kernel = tc::tc_gemm_kernel<FMT, N>;
   static int attr_done[64] = {0};
