@@ -63,7 +63,9 @@ constexpr uint32_t kThreads = 608;  // 19 warps
 constexpr uint32_t kTileRows = 128;
 constexpr uint32_t kQ4KPanel = 128u * kQ4KBytes, kQ6KPanel = 128u * kQ6KBytes;  // 18432, 26880
 constexpr uint32_t kAStages = 3;  // tensor-memory A stages
-__host__ __device__ constexpr uint32_t b_stages(uint32_t N) { return N <= 32u ? 8u : 4u; }  // activation ring
+// Activation ring: the same depth as the tensor-memory A ring, so one barrier
+// pair per stage serves both (A and B of a half block are ready and released together).
+__host__ __device__ constexpr uint32_t b_stages(uint32_t) { return kAStages; }
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kAColBase = 256, kA2ColBase = 448;  // tensor-memory columns of the A / A2 stages
 constexpr uint32_t kMinSmem = 120u * 1024u;             // keeps one CTA per SM (tensor memory is taken whole)
@@ -348,11 +350,13 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 19 warps: <
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.off_bar);
   uint64_t* raw_full = bars;
   uint64_t* raw_empty = raw_full + kRawS;
-  uint64_t* b_full = raw_empty + kRawS;
-  uint64_t* b_empty = b_full + kBStages;
-  uint64_t* a_full = b_empty + kBStages;
-  uint64_t* a_empty = a_full + kAStages;
-  uint64_t* d_full = a_empty + kAStages;
+  static_assert(kBStages == kAStages, "one barrier pair per (A, B) stage");
+  // stage s of a half block: full once the 8 dequantizing warps have written A
+  // and the activation copy has landed (8 arrivals + the stager's expect-tx
+  // arrival), empty once the MMAs that read both have completed (one commit)
+  uint64_t* ab_full = raw_empty + kRawS;
+  uint64_t* ab_empty = ab_full + kAStages;
+  uint64_t* d_full = ab_empty + kAStages;
   uint64_t* d_empty = d_full + 2;
   uint64_t* drain = d_empty + 2;
   uint32_t* misc = reinterpret_cast<uint32_t*>(smem + p.off_misc);
@@ -393,13 +397,9 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 19 warps: <
                         policy);
       }
     }
-    for (uint32_t s = 0; s < kBStages; ++s) {
-      mbar_init(&b_full[s], 1);
-      mbar_init(&b_empty[s], 1);
-    }
     for (uint32_t s = 0; s < kAStages; ++s) {
-      mbar_init(&a_full[s], 8);
-      mbar_init(&a_empty[s], 1);
+      mbar_init(&ab_full[s], 9);
+      mbar_init(&ab_empty[s], 1);
     }
     for (uint32_t s = 0; s < 2; ++s) {
       mbar_init(&d_full[s], 1);
@@ -475,14 +475,14 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 19 warps: <
         for (uint32_t kb = kb0; kb < kb1 && !stop; ++kb)
           for (uint32_t h = 0; h < 2u; ++h) {
             const uint32_t bs = bit % kBStages;
-            if (*abort_flag || !mbar_wait(&b_empty[bs], ((bit / kBStages) & 1u) ^ 1u, p.err)) {
+            if (*abort_flag || !mbar_wait(&ab_empty[bs], ((bit / kBStages) & 1u) ^ 1u, p.err)) {
               stop = true;
               break;
             }
             const uint32_t bytes = h == 0 ? b_bytes0 : b_bytes1;
             const uint32_t off = kb * p.blk + (h == 0 ? 0u : b_bytes0);
-            mbar_expect_tx(&b_full[bs], bytes);
-            bulk_g2s(bst + bs * p.b_stage, p.xb + off, bytes, &b_full[bs]);
+            mbar_expect_tx(&ab_full[bs], bytes);
+            bulk_g2s(bst + bs * p.b_stage, p.xb + off, bytes, &ab_full[bs]);
             ++bit;
           }
       }
@@ -490,7 +490,7 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 19 warps: <
         *abort_flag = 1u;
         for (uint32_t s = 0; s < kBStages; ++s) {
           const uint32_t n = bit / kBStages + (s < bit % kBStages ? 1u : 0u);
-          if (n) (void)mbar_wait(&b_full[s], (n - 1u) & 1u, nullptr);
+          if (n) (void)mbar_wait(&ab_full[s], (n - 1u) & 1u, nullptr);  // bounded: ends after its limit
         }
       }
     }
@@ -514,9 +514,8 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 19 warps: <
         const uint32_t d1 = tmem + buf * kDStride;
         for (uint32_t kb = kb0; kb < kb1 && !stop; ++kb) {
           for (uint32_t h = 0; h < 2u; ++h) {
-            const uint32_t as = ait % kAStages, bs = bit % kBStages;
-            if (*abort_flag || !mbar_wait(&a_full[as], (ait / kAStages) & 1u, p.err) ||
-                !mbar_wait(&b_full[bs], (bit / kBStages) & 1u, p.err)) {
+            const uint32_t as = ait % kAStages, bs = as;  // the rings advance together (one stage per half)
+            if (*abort_flag || !mbar_wait(&ab_full[as], (ait / kAStages) & 1u, p.err)) {
               stop = true;
               break;
             }
@@ -531,8 +530,7 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 19 warps: <
             if (kQ4 && h == 0u)  // mins term: [c_G, c_G] x [X_G hi, X_G lo], c_G = 2^6 (8 d sc - dmin m), same accumulator
               mma_ts(d1, tmem + kA2ColBase + 8u * as, smem_desc(bsa + static_cast<uint32_t>(N) * 256u, 128u, 256u),
                      idesc, 1u);
-            mma_commit(&a_empty[as]);
-            mma_commit(&b_empty[bs]);
+            mma_commit(&ab_empty[as]);
             ++ait;
             ++bit;
           }
@@ -646,7 +644,7 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 19 warps: <
         const __half2 dd = __float2half2_rn(d64);
         for (uint32_t h = 0; h < 2u; ++h) {
           const uint32_t as = ait % kAStages;
-          if (!warp_wait(&a_empty[as], ((ait / kAStages) & 1u) ^ 1u, p.err, abort_flag)) {
+          if (!warp_wait(&ab_empty[as], ((ait / kAStages) & 1u) ^ 1u, p.err, abort_flag)) {
             stop = true;
             break;
           }
@@ -661,7 +659,7 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 19 warps: <
           tmem_wait_st();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&a_full[as])) : "memory");
+          if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&ab_full[as])) : "memory");
           ++ait;
         }
       }
