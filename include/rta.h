@@ -100,7 +100,9 @@ RTA_API rta_status rta_panel_weights(int format, const void* src, uint32_t rows,
 /* Batched product on the tensor cores (tcgen05), for batches of 16 rows or
  * more: y[b][r] (+)= sum_c W[r][c] x[b][c] with W in panel order
  * (RTA_Q4_K_PANEL / RTA_Q6_K_PANEL), rows % 128 == 0, cols % 256 == 0,
- * 1 <= batch <= 256, fp32 accumulation over fp16-rounded x.  When argmax is
+ * 1 <= batch <= 256.  Both operands are fp16: x rounded once, each weight
+ * rounded once after its block scale is applied (about 3e-4 relative L2 from
+ * the exact product at random weights); accumulation is fp32.  When argmax is
  * not NULL the row of the largest y[b][.] (ties -> lowest row) and its value
  * (best, may be NULL) are returned per batch row, and y may be NULL
  * (vocabulary readout).  workspace: rta_gemm_tc_workspace_bytes(format,
