@@ -288,7 +288,8 @@ RTA_API void rta_model_close(rta_model* model);
  * and stop state.  Below 16 sequences the GEMVs stream the weights once per
  * up-to-16 sequences; from 16 sequences on, every matrix with a multiple of 128
  * rows is kept in panel order and its products run on the tensor cores
- * (rta_gemm_tc arithmetic: fp16-rounded activations, fp32 accumulation), so the
+ * (rta_gemm_tc arithmetic: fp16 activations and block-scaled fp16 weights,
+ * fp32 accumulation), so the
  * tokens then follow the single-sequence ones wherever the top-2 margin exceeds
  * that rounding.  No reference counterpart: the reference worker
  * serves one sequence per process (optical_resident.cpp:964-971).  The
