@@ -97,7 +97,8 @@ class LayoutSource:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True,
+                    help="root of a checkout of the reference project (holds the ray_tracing package)")
     args = ap.parse_args()
     sys.path.insert(0, str(Path(args.reference).resolve()))
     from ray_tracing.compiler import export as ref_export
