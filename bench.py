@@ -3,7 +3,8 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
 
 Workloads (the benchmark configs, synthetic seeded inputs of the stated shapes):
-  decode2b  config 4: 2B-shape hybrid decoder, batch 1, greedy decode tokens/s (default)
+  decode2b  config 4: 2B-shape hybrid decoder, batch 1, greedy decode tokens/s (default;
+            --kv packet keeps the history as the reference's Q4_K/Q6_K packets)
   mlp       config 1: SwiGLU MLP 2048 -> 6144 -> 2048, Q4_K, batch 1
   attention config 2: GQA decode 16q/4kv, head_dim 256, fp16 KV, history --history (default 32768)
   lmhead    config 3: vocabulary readout 151936 x 2048 Q6_K, batch 1, logits + argmax
@@ -465,21 +466,28 @@ class AttentionWorkload(Workload):
                           "(C restatement of the S_t/R_t detector, OpenMP over heads)"}
 
 
+def decode_workload_name(kv):
+    return "config4_2b_hybrid_decode_b1" + ("" if kv == "fp16" else "_packet_history")
+
+
 class DecodeWorkload(Workload):
     """benchmark config 4: 2B-shape hybrid (24 layers, 3:1 recurrent:full), batch 1,
     prompt 512 random ids, then greedy decode.  A step is one decode token."""
     name, metric, unit, dtype, dominant = ("decode2b", "decode tokens/s (2B-shape hybrid, batch 1)", "tokens/s",
                                            "q4k/q6k-int8mma, f16-kv, f32 state",
                                            "gemv_tiled_kernel<Q6_K> vocabulary readout + argmax")
-    def __init__(self, seed=20261201, prompt_len=512):
+    def __init__(self, seed=20261201, prompt_len=512, kv="fp16"):
         self.prompt_len = prompt_len
+        self.kv = kv
+        if kv == "packet":
+            self.dtype = "q4k/q6k-int8mma, q4k/q6k-packet-kv (f32 decode), f32 state"
         import torch
         from rta_b200 import assets, ops
         from rta_b200.model import ResidentModel
         self.ops, self.torch, self.assets = ops, torch, assets
         self.spec = assets.spec_2b()
         self.seed = seed
-        self.model = ResidentModel.synthetic(self.spec, seed, capacity=2048)
+        self.model = ResidentModel.synthetic(self.spec, seed, capacity=2048, history=kv)
         self.prompt = np.random.default_rng(seed).integers(0, self.spec.vocabulary_size, self.prompt_len)
         self.model.prefill(self.prompt)
         self.launches_per_step = self.model.resources()["kernels_per_decode_step"]
@@ -502,10 +510,12 @@ class DecodeWorkload(Workload):
         return self.spec.vocabulary_size * self.spec.hidden_size // 256 * 210 + self.spec.hidden_size * 4
 
     def step_bytes(self, position):
-        """Algorithmic HBM bytes of one decode token at `position` (weights once, fp16 KV, recurrent state)."""
+        """Algorithmic HBM bytes of one decode token at `position` (weights once, the visible
+        history -- fp16 K and V, or one 1416-byte packet per position at 4 x 256 --, recurrent state)."""
         lay = self.model.layout
         weights = sum(t.nbytes for t in lay.matrices) + lay.basis[1].nbytes + self.spec.hidden_size * 210 // 256
-        kv = len(self.spec.full_layers) * min(position + 1, 2048) * self.spec.kv_width * 2 * 2
+        per_pos = self.spec.kv_width * 2 * 2 if self.kv == "fp16" else self.spec.kv_width // 256 * (144 + 210)
+        kv = len(self.spec.full_layers) * min(position + 1, 2048) * per_pos
         rec = len(self.spec.recurrent_layers) * self.spec.state_heads * 128 * 128 * 4 * 2
         return weights + kv + rec
 
@@ -513,12 +523,13 @@ class DecodeWorkload(Workload):
         return 1.0
 
     def config(self):
-        return {"workload": "config4_2b_hybrid_decode_b1", "layers": self.spec.depth, "pattern": "rec,rec,rec,full",
+        return {"workload": decode_workload_name(self.kv), "layers": self.spec.depth, "pattern": "rec,rec,rec,full",
                 "hidden": self.spec.hidden_size, "intermediate": self.spec.middle_size,
                 "vocab": self.spec.vocabulary_size, "q_heads": 16, "kv_heads": 4, "head_dim": 256,
                 "rotary_dim": self.spec.rotary_dim, "state_heads": self.spec.state_heads,
                 "state_key_heads": self.spec.state_key_heads, "formats": "Q4_K matrices, Q6_K embedding + LM head",
-                "kv_cache": "fp16", "prompt": self.prompt_len, "batch": 1, "tied_embeddings": False,
+                "kv_cache": "fp16" if self.kv == "fp16" else "packets: 4 Q4_K key + 4 Q6_K value blocks, 1416 B",
+                "prompt": self.prompt_len, "batch": 1, "tied_embeddings": False,
                 "l2": "per-token weight stream 1.1 GB > L2"}
 
     def cpu_baseline(self, budget_s):
@@ -528,7 +539,7 @@ class DecodeWorkload(Workload):
         spec = assets.spec_2b()
         lay = assets.plan(spec, self.seed)
         params, mats, basis = host_payloads(lay, self.seed)
-        ref = OracleModel(spec, params, mats, basis, 2048)
+        ref = OracleModel(spec, params, mats, basis, 2048, kv=self.kv)
         t0 = time.perf_counter()
         ref.prefill(np.random.default_rng(self.seed).integers(0, spec.vocabulary_size, 4))
         n = 0
@@ -538,8 +549,9 @@ class DecodeWorkload(Workload):
             n += 1
         dt = time.perf_counter() - t0
         return {"value": (n + 4) / dt, "unit": self.unit, "cores": oracle.threads(), "kind": "port",
-                "sample": f"4 prompt + {n} greedy tokens of a 2B-shape model (random valid Q4_K/Q6_K blocks) "
-                          "through the model oracle (C restatement of the reference shader math, OpenMP)"}
+                "sample": f"4 prompt + {n} greedy tokens of a 2B-shape model (random valid Q4_K/Q6_K blocks, "
+                          f"{self.kv} history) through the model oracle (C restatement of the reference shader "
+                          "math, OpenMP)"}
 
 
 class MLPTPWorkload(Workload):
@@ -871,7 +883,7 @@ def run_decode(args, world, rank, local):
     graph replays, GPU time by CUDA events on the engine stream); `e2e` = K calls
     of generate(1) (host round trip per token: control H2D, ids D2H)."""
     import torch
-    wl = DecodeWorkload(prompt_len=args.prompt)
+    wl = DecodeWorkload(prompt_len=args.prompt, kv=args.kv)
     wl.decode(args.warmup)                       # warm-up tokens
     torch.cuda.synchronize()
     barrier(world)
@@ -1071,7 +1083,7 @@ def run_reference_decode(args, world):
     spec = assets.spec_2b()
     lay = assets.plan(spec, 20261201)
     params, mats, basis = host_payloads(lay, 20261201)
-    ref = OracleModel(spec, params, mats, basis, 2048)
+    ref = OracleModel(spec, params, mats, basis, 2048, kv=args.kv)
     ref.prefill(np.random.default_rng(1).integers(0, spec.vocabulary_size, 4))
     for _ in range(min(args.warmup, 3)):
         ref.forward(ref.readout()[0])
@@ -1082,11 +1094,12 @@ def run_reference_decode(args, world):
     v = n / (time.perf_counter() - t0)
     base = {"value": v, "unit": "tokens/s", "cores": oracle.threads(), "kind": "port",
             "sample": f"{n} greedy tokens after a 4-token prompt of a 2B-shape model (random valid Q4_K/Q6_K "
-                      "blocks) through the model oracle, the C restatement of the reference shader math (OpenMP)"}
+                      f"blocks, {args.kv} history) through the model oracle, the C restatement of the reference "
+                      "shader math (OpenMP)"}
     return {"impl": "reference", "metric": DecodeWorkload.metric, "value": v, "unit": "tokens/s", "n_gpus": world,
             "steps": n, "warmup": min(args.warmup, 3), "higher_is_better": True, "dtype": "f32",
             "data": "synthetic (seeded random init, prompt ids)",
-            "config": {"workload": "config4_2b_hybrid_decode_b1"}, "cpu_baseline": base,
+            "config": {"workload": decode_workload_name(args.kv)}, "cpu_baseline": base,
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "note": "reference Vulkan ray-query worker unavailable on this box (no graphics stack, no RT cores); "
                     "timed its CPU path: the C restatement of its shader math"}
@@ -1115,6 +1128,9 @@ def main():
                     help="ragged9b: first N layers of the 9B pattern only (profiling case; 0 = all 32)")
     ap.add_argument("--max-history", type=int, default=0,
                     help="ragged9b: cap the seeded histories (profiling case; 0 = config 5's U[128, 8192])")
+    ap.add_argument("--kv", choices=("fp16", "packet"), default="fp16",
+                    help="decode2b: attention history format (packet: the reference's Q4_K key / Q6_K value "
+                         "packets, the worker's default)")
     ap.add_argument("--prompt", type=int, default=512,
                     help="decode2b: prompt length before the timed tokens (short prompts keep profiler runs small)")
     args = ap.parse_args()
