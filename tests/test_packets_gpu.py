@@ -56,17 +56,19 @@ def test_engine_packet_history_tracks_the_oracle_closely():
     model.close()
 
 
-@pytest.mark.parametrize("seed,capacity,prompt_len", [(14, 64, 20), (15, 16, 14)])
+@pytest.mark.parametrize("seed,capacity,prompt_len", [(14, 64, 20), (15, 16, 14), (16, 512, 300), (17, 128, 126)])
 def test_engine_packet_attention_step_matches_fp64(seed, capacity, prompt_len):
     """Teacher-forced: the decode step's own q, gate and ring packets, read back,
     give the FP64 detector output the step produced (prefill and decode graphs,
-    with the ring wrapping in the second case)."""
+    with the ring wrapping in the second and fourth cases; the last two split
+    the history over several CTAs per KV head, some of them empty)."""
     spec = small_spec(kinds=("recurrent", "full"))
     model, _ = build_packet(spec, seed, capacity)
     H, KVH, hd = spec.attention_heads, spec.kv_heads, spec.attention_head_dim
     R = spec.rotary_dim
     prompt = np.random.default_rng(seed).integers(0, spec.vocabulary_size, prompt_len)
     model.prefill(prompt)
+    assert model.resources()["attention_splits"] == max(1, capacity // 64)
     for step in range(3):   # after prefill, then after 3 and 6 decode steps (16-slot ring wraps at 16)
         q, gate, att, packets = model.debug_attention()
         assert len(packets) == min(model.state()[1], capacity)
