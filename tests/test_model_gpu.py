@@ -65,6 +65,19 @@ def test_engine_prefill_generate_matches_oracle(seed):
     model.close()
 
 
+@pytest.mark.parametrize("capacity,prompt_len", [(512, 300), (256, 250)])
+def test_engine_multi_split_history_matches_oracle(capacity, prompt_len):
+    """A single sequence's history split over several CTAs per KV head (capacity
+    / 64 splits of at least 64 positions, some empty), the second case wrapping
+    the ring during generation."""
+    spec = small_spec(kinds=("full", "recurrent"))
+    model, ref = build(spec, 21, capacity=capacity)
+    assert model.resources()["attention_splits"] == capacity // 64
+    prompt = np.random.default_rng(21).integers(0, spec.vocabulary_size, prompt_len)
+    check_generation(model, ref, prompt, 12)
+    model.close()
+
+
 def test_engine_history_ring_wraps():
     """capacity 16 < prompt + generated: only the newest 16 positions are visible."""
     spec = small_spec(kinds=("full", "recurrent", "full", "recurrent"))
