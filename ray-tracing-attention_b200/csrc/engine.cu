@@ -432,10 +432,10 @@ struct Engine {
     // the longest histories, 1 for the shortest; measured against 512 / 1024 /
     // 1536 positions per split and against a uniform split count).
     const uint32_t fill = (8u * static_cast<uint32_t>(sms) + spec.kv_heads * nseq - 1u) / (spec.kv_heads * nseq);
-    // Below that regime both split kernels cover 64 positions per pass.  One
-    // sequence, and packet history (every K/V value decoded on the CUDA cores),
-    // get up to capacity / 64 splits, so a decode-length history takes one pass
-    // per CTA; a few fp16 sequences keep capacity / 256.
+    // Below that regime both split kernels round a split up to a multiple of 64
+    // positions.  One sequence, and packet history (every K/V value decoded on
+    // the CUDA cores), get up to capacity / 64 splits, so a decode-length history
+    // gives each CTA about 64 positions; a few fp16 sequences keep capacity / 256.
     const uint32_t per_split = packet_history || nseq == 1 ? 64u : 256u;
     nsplit = nseq >= kTcMinSeq ? std::max(1u, std::min(static_cast<uint32_t>(sms) / spec.kv_heads, capacity / 2048u))
                        : std::max(1u, std::min({static_cast<uint32_t>(sms) / spec.kv_heads, capacity / per_split, fill}));
