@@ -26,3 +26,60 @@ def test_argument_validation_without_device():
     assert lib.rta_workspace_error(None, 0, None, ctypes.byref(word)) == _lib.RTA_E_ARG
     assert lib.rta_attention_workspace_bytes(16, 4, 256, 8) > 16 * 8 * 256 * 4
 
+
+
+_SCALARS = {"int": ctypes.c_int, "rta_status": ctypes.c_int, "uint32_t": ctypes.c_uint32,
+            "uint64_t": ctypes.c_uint64, "size_t": ctypes.c_size_t, "float": ctypes.c_float,
+            "double": ctypes.c_double}
+
+
+def _header_declarations():
+    """name -> (return type, [parameter types]) for every RTA_API function of
+    include/*.h; a parameter or return with '*' or '[' reads as "pointer"."""
+    import re
+    from rta_b200 import _build
+
+    def kind(decl):
+        decl = decl.strip()
+        if "*" in decl or "[" in decl:
+            return "pointer"
+        words = [w for w in decl.split() if w != "const"]
+        return words[0] if len(words) == 1 else " ".join(words[:-1])
+
+    out = {}
+    for h in sorted(_build.INCLUDE.glob("*.h")):
+        for ret, name, params in re.findall(r"^RTA_API\s+([\w\s\*]+?)\s*\b(rta_\w+)\s*\(([^)]*)\)\s*;",
+                                             h.read_text(), flags=re.M):
+            plist = [p for p in (x.strip() for x in params.split(",")) if p and p != "void"]
+            out[name] = ("pointer" if "*" in ret else ret.replace("const", "").strip(), [kind(p) for p in plist])
+    return out
+
+
+def _is_pointer(t):
+    return t in (ctypes.c_void_p, ctypes.c_char_p) or (isinstance(t, type) and issubclass(t, ctypes._Pointer))
+
+
+def test_bindings_match_header_declarations():
+    """Every ctypes binding (operators and the model handle) has the arity and
+    the scalar / pointer kind of each argument and of the result that the
+    header declares, so the Python mirror cannot drift from the C-ABI."""
+    from rta_b200 import model
+    decls = _header_declarations()
+    assert set(decls) == set(_lib.header_symbols())
+    bindings = dict(_lib._SIGNATURES)
+    bindings.update(model._SIGS)
+    assert set(bindings) <= set(decls), sorted(set(bindings) - set(decls))
+    for name, (res, args) in bindings.items():
+        ret, params = decls[name]
+        assert len(args) == len(params), (name, len(args), len(params))
+        for i, (have, want) in enumerate(zip(args, params)):
+            if want == "pointer":
+                assert _is_pointer(have), (name, i, have)
+            else:
+                assert have is _SCALARS[want], (name, i, have, want)
+        if ret == "void":
+            assert res is None, name
+        elif ret == "pointer":
+            assert _is_pointer(res), (name, res)
+        else:
+            assert res is _SCALARS[ret], (name, res, ret)
