@@ -2,8 +2,13 @@
 without a GPU, exports every symbol include/rta.h declares, and rejects bad
 arguments with a status code (host-side validation, no device work)."""
 import ctypes
+import re
+import shutil
+import subprocess
 
-from rta_b200 import _lib
+import pytest
+
+from rta_b200 import _build, _lib
 
 
 def test_library_builds_and_exports_header_symbols():
@@ -36,9 +41,6 @@ _SCALARS = {"int": ctypes.c_int, "rta_status": ctypes.c_int, "uint32_t": ctypes.
 def _header_declarations():
     """name -> (return type, [parameter types]) for every RTA_API function of
     include/*.h; a parameter or return with '*' or '[' reads as "pointer"."""
-    import re
-    from rta_b200 import _build
-
     def kind(decl):
         decl = decl.strip()
         if "*" in decl or "[" in decl:
@@ -83,3 +85,23 @@ def test_bindings_match_header_declarations():
             assert _is_pointer(res), (name, res)
         else:
             assert res is _SCALARS[ret], (name, res, ret)
+
+
+def test_model_spec_mirror_has_the_c_layout(tmp_path):
+    """The ctypes mirror of rta_model_spec has the size and field offsets that a
+    C compiler gives the header's struct (the handle reads it by value)."""
+    from rta_b200.model import ModelSpecC
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    fields = [f[0] for f in ModelSpecC._fields_]
+    src = tmp_path / "layout.c"
+    src.write_text("#include <stddef.h>\n#include <stdio.h>\n#include \"rta.h\"\nint main(void) {\n"
+                   "  printf(\"%zu\\n\", sizeof(rta_model_spec));\n"
+                   + "".join(f"  printf(\"%zu\\n\", offsetof(rta_model_spec, {f}));\n" for f in fields)
+                   + "  return 0;\n}\n")
+    exe = tmp_path / "layout"
+    subprocess.run([cc, "-I", str(_build.INCLUDE), str(src), "-o", str(exe)], check=True)
+    got = [int(v) for v in subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split()]
+    assert got[0] == ctypes.sizeof(ModelSpecC)
+    assert got[1:] == [getattr(ModelSpecC, f).offset for f in fields]
