@@ -1,6 +1,7 @@
 """CPU tests of the C-ABI boundary: the library builds for sm_100a, loads
-without a GPU, exports every symbol include/rta.h declares, and rejects bad
-arguments with a status code (host-side validation, no device work)."""
+without a GPU, exports every symbol include/rta.h declares, rejects bad
+arguments with a status code (host-side validation, no device work), and its
+Python mirror (ctypes signatures, the model-spec struct) matches the header."""
 import ctypes
 import re
 import shutil
