@@ -3,12 +3,14 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
 
 Workloads (the benchmark configs, synthetic seeded inputs of the stated shapes):
-  decode2b  config 4: 2B-shape hybrid decoder, batch 1, greedy decode tokens/s (default;
-            --kv packet keeps the history as the reference's Q4_K/Q6_K packets)
+  ragged9b  config 5 (default): 9B-shape ragged batch of 64 sequences, sharded by sequence
+            over the ranks; at N = 1 the line also carries compact records of configs 1-4
+            ("other_configs", skipped with --no-other-configs)
+  decode2b  config 4: 2B-shape hybrid decoder, batch 1, greedy decode tokens/s
+            (--kv packet keeps the history as the reference's Q4_K/Q6_K packets)
   mlp       config 1: SwiGLU MLP 2048 -> 6144 -> 2048, Q4_K, batch 1
   attention config 2: GQA decode 16q/4kv, head_dim 256, fp16 KV, history --history (default 32768)
   lmhead    config 3: vocabulary readout 151936 x 2048 Q6_K, batch 1, logits + argmax
-  ragged9b  config 5: 9B-shape ragged batch of 64 sequences, sharded by sequence
   gemm      the tensor-core batched product alone (--rows --cols --batch --format)
   mlp_tp    the MLP split over the ranks (tensor parallel; --hidden --middle --batch)
   lmhead_tp config 3's readout split over the ranks (tensor parallel; --batch)
@@ -475,7 +477,8 @@ class DecodeWorkload(Workload):
     prompt 512 random ids, then greedy decode.  A step is one decode token."""
     name, metric, unit, dtype, dominant = ("decode2b", "decode tokens/s (2B-shape hybrid, batch 1)", "tokens/s",
                                            "q4k/q6k-int8mma, f16-kv, f32 state",
-                                           "gemv_tiled_kernel<Q6_K> vocabulary readout + argmax")
+                                           "gemv_tiled_kernel<Q4_K,1> -- every Q4_K matrix product of the step: "
+                                           "QKV(+gate) / in-projections, o / out projections, gate+up, down")
     def __init__(self, seed=20261201, prompt_len=512, kv="fp16"):
         self.prompt_len = prompt_len
         self.kv = kv
@@ -491,23 +494,10 @@ class DecodeWorkload(Workload):
         self.prompt = np.random.default_rng(seed).integers(0, self.spec.vocabulary_size, self.prompt_len)
         self.model.prefill(self.prompt)
         self.launches_per_step = self.model.resources()["kernels_per_decode_step"]
-        # the dominant kernel in isolation: same readout shape on its own weights
-        self.lm_fmt, self.lm_w = ops.tile_weights(
-            14, ops.synthetic_blocks(14, self.spec.vocabulary_size, self.spec.hidden_size, seed + 7),
-            self.spec.vocabulary_size, self.spec.hidden_size)
-        self.lm_x = ops.synthetic_normal(self.spec.hidden_size, seed + 8)
-        self.lm_ws = torch.empty(4096, dtype=torch.uint8, device="cuda")
 
     def decode(self, k):
         ids = self.model.generate(k)
         return self.model.last_gpu_ms, ids
-
-    def dominant_launch(self, i):
-        self.ops.readout(self.lm_fmt, self.lm_w, self.spec.vocabulary_size, self.spec.hidden_size, self.lm_x, logits=False,
-                         workspace=self.lm_ws)
-
-    def dominant_bytes(self):
-        return self.spec.vocabulary_size * self.spec.hidden_size // 256 * 210 + self.spec.hidden_size * 4
 
     def step_bytes(self, position):
         """Algorithmic HBM bytes of one decode token at `position` (weights once, the visible
@@ -794,34 +784,17 @@ def run_ragged(args, world, rank, local):
     e2e_s = max_over_ranks((time.perf_counter() - t0) * 1e3, world) / 1e3 / args.steps
     positions = mine + args.warmup + args.steps * (reps + 1)
     step_bytes = ragged_step_bytes(spec, model.layout, positions, capacity)
-    layout = model.layout
+    tc = res["tensor_core_matrices"] > 0
+    tile = 16 if len(mine) <= 16 else 32 if len(mine) <= 32 else 64
+    kernel = (f"tc_gemm_kernel<Q4_K,{tile}> (tcgen05)" if tc else "gemv_tiled_kernel<Q4_K> (batched rows)") + \
+        " -- every Q4_K matrix product of the step: QKV(+gate) / in-projections, o / out projections, gate+up, down"
+    roof = step_roofline(profile_summary(model), kernel, "tc_gemm" if tc else "gemv_tiled")
+    pk = peaks()
+    step_gbs = step_bytes / (ms_step / 1e3) / 1e9
+    roof.update({"step_algorithmic_bytes_rank": step_bytes, "step_achieved_gbs_rank": step_gbs,
+                 "step_frac": step_gbs / pk["hbm_gbs"], "profiled_rank": rank})
     model.close()
     torch.cuda.empty_cache()
-    # dominant kernel alone: the 9B readout at this rank's batch, on the path the
-    # engine takes (tensor cores from 16 sequences on, else GEMV launches of <= 16 rows)
-    tc = len(mine) >= 16
-    rows = len(mine) if tc else min(16, len(mine))
-    raw = ops.synthetic_blocks(14, spec.vocabulary_size, spec.hidden_size, wl.seed + 7)
-    lm_x = ops.synthetic_normal(rows * spec.hidden_size, wl.seed + 8).reshape(rows, spec.hidden_size)
-    if tc:
-        lm_fmt, lm_w = ops.panel_weights(14, raw, spec.vocabulary_size, spec.hidden_size)
-        lm_ws = torch.empty(ops._lib.load().rta_gemm_tc_workspace_bytes(lm_fmt, rows, spec.hidden_size),
-                            dtype=torch.uint8, device="cuda")
-        dom = lambda i: ops.gemm_tc(lm_fmt, lm_w, spec.vocabulary_size, spec.hidden_size, lm_x, argmax=True,
-                                    store=False, workspace=lm_ws)
-        kernel = f"tc_gemm_kernel<Q6_K,{min(64, rows)}> vocabulary readout + argmax ({rows} rows, tcgen05)"
-    else:
-        lm_fmt, lm_w = ops.tile_weights(14, raw, spec.vocabulary_size, spec.hidden_size)
-        lm_ws = torch.empty(4096, dtype=torch.uint8, device="cuda")
-        dom = lambda i: ops.readout(lm_fmt, lm_w, spec.vocabulary_size, spec.hidden_size, lm_x, logits=False,
-                                    workspace=lm_ws)
-        kernel = f"gemv_tiled_kernel<Q6_K> vocabulary readout + argmax ({rows} rows per launch)"
-    del raw
-    dom_ms = time_steps(dom, args.steps, args.warmup, world) / args.steps
-    dom_bytes = spec.vocabulary_size * spec.hidden_size // 256 * 210 + rows * spec.hidden_size * 4
-    pk = peaks()
-    achieved = dom_bytes / (dom_ms / 1e3) / 1e9
-    step_gbs = step_bytes / (ms_step / 1e3) / 1e9
     total = int(lengths.size)
     line = {
         "metric": wl.metric, "value": total / (ms_step / 1e3), "unit": wl.unit, "n_gpus": world,
@@ -838,12 +811,7 @@ def run_ragged(args, world, rank, local):
                    "capacity": capacity, "kv_cache": "fp16",
                    "parallelism": f"sequence-sharded x{world}, weights replicated" if world > 1 else "single GPU",
                    "l2": "per-step weight stream 4 GB > L2"},
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                     "frac": achieved / pk["hbm_gbs"], "traffic": None, "kernel": kernel,
-                     "algorithmic_bytes": dom_bytes, "kernel_ms": dom_ms,
-                     "peak_source": f"{pk['source']} hbm_gbs (burst copy)",
-                     "step_algorithmic_bytes_rank": step_bytes, "step_achieved_gbs_rank": step_gbs,
-                     "step_frac": step_gbs / pk["hbm_gbs"]},
+        "roofline": roof,
         "e2e": {"value": total / e2e_s, "unit": wl.unit, "h2d_bytes_per_step": 48 * len(mine),
                 "d2h_bytes_per_step": 52 * len(mine),
                 "api": "ResidentModel.generate_batch(1) -> rta_model_generate_batch (C-ABI)"},
@@ -851,7 +819,11 @@ def run_ragged(args, world, rank, local):
         "clocks": clk.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import oracle
+        oracle.use_all_cores()
         line["cpu_baseline"] = ragged_cpu_baseline(args.cpu_budget)
+    if world == 1 and not args.no_other_configs and not small:
+        line["other_configs"] = other_configs(args)
     return line
 
 
@@ -897,34 +869,31 @@ def run_decode(args, world, rank, local):
                 break
     ms_step = max_over_ranks(ms_total / reps, world) / args.steps
     barrier(world)
-    dom_ms = time_steps(wl.dominant_launch, args.steps, args.warmup, world) / args.steps
-    barrier(world)
     t0 = time.perf_counter()
     for _ in range(args.steps):
         wl.model.generate(1)
     e2e_s = (time.perf_counter() - t0) / args.steps
     e2e_s = max_over_ranks(e2e_s * 1e3, world) / 1e3
     pos = wl.model.state()[1]
+    roof = step_roofline(profile_summary(wl.model), wl.dominant, "gemv_tiled")
     pk = peaks()
-    achieved = wl.dominant_bytes() / (dom_ms / 1e3) / 1e9
     step_gbs = wl.step_bytes(pos) / (ms_step / 1e3) / 1e9
+    roof.update({"step_algorithmic_bytes": wl.step_bytes(pos), "step_achieved_gbs": step_gbs,
+                 "step_frac": step_gbs / pk["hbm_gbs"]})
     line = {
         "metric": wl.metric, "value": world / (ms_step / 1e3), "unit": wl.unit, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic (seeded random init, prompt ids)",
         "config": dict(wl.config(), parallelism=f"replicas x{world}" if world > 1 else "single GPU"),
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                     "frac": achieved / pk["hbm_gbs"], "traffic": getattr(wl, "traffic", None), "kernel": wl.dominant,
-                     "algorithmic_bytes": wl.dominant_bytes(), "kernel_ms": dom_ms,
-                     "peak_source": f"{pk['source']} hbm_gbs (burst copy)",
-                     "step_algorithmic_bytes": wl.step_bytes(pos), "step_achieved_gbs": step_gbs,
-                     "step_frac": step_gbs / pk["hbm_gbs"]},
+        "roofline": roof,
         "e2e": {"value": world / e2e_s, "unit": wl.unit, "h2d_bytes_per_step": 48, "d2h_bytes_per_step": 52,
                 "api": "ResidentModel.generate(1) -> rta_model_generate (C-ABI)"},
         "gpu_launches": wl.launches_per_step * args.steps,
         "clocks": clk.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import oracle
+        oracle.use_all_cores()
         line["cpu_baseline"] = wl.cpu_baseline(args.cpu_budget)
     if hasattr(wl, "close"):
         wl.close()
@@ -975,6 +944,115 @@ def time_steps(fn, steps, warmup, world, graph=True, min_seconds=0.0):
     return max_over_ranks(ms, world)
 
 
+# ------------------------------------------------------- step profile roofline
+STEP_PRODUCTS = ("qkv", "o_proj", "in_proj", "out_proj", "gate_up", "down")
+# One ncu capture of a representative launch of each step's dominant kernel
+# (dram__bytes_read.sum + dram__bytes_write.sum against that launch's
+# algorithmic bytes; the summaries under profiles/ give the commands).
+TRAFFIC = {
+    "tc_gemm": {"launch": "tc_gemm_kernel<Q4_K,64> 12288x4096, batch 64", "dram_bytes": 32.10e6,
+                "algorithmic_bytes": 32.5e6, "source": "profiles/tc_gemm_q4k_12288x4096_b64.md"},
+    "gemv_tiled": {"launch": "gemv_tiled_kernel<Q4_K,1> gate+up 2 x 6144x2048, batch 1", "dram_bytes": 14.23e6,
+                   "algorithmic_bytes": 14.2e6, "source": "profiles/gemv_tiled_q4k_mlp_2048_6144.md"},
+}
+
+
+def profile_summary(model, reps: int = 3) -> dict:
+    """Per launch-group kind of one decode step (rta_model_profile_step: CUDA events
+    between the groups of a graph replay): device ms (median over `reps` steps),
+    algorithmic bytes and groups per step."""
+    runs = []
+    for _ in range(reps):
+        agg = {}
+        for kind, ms, nbytes in model.profile_step():
+            a = agg.setdefault(kind, [0.0, 0.0, 0])
+            a[0] += ms
+            a[1] += nbytes
+            a[2] += 1
+        runs.append(agg)
+    return {k: {"ms": float(np.median([r[k][0] for r in runs])), "bytes": runs[-1][k][1],
+                "launch_groups": runs[-1][k][2]} for k in runs[-1]}
+
+
+def step_roofline(prof: dict, kernel: str, traffic_key: str) -> dict:
+    """Roofline of the step's dominant kernel class -- its matrix products -- from a
+    step profile: achieved = their algorithmic bytes / their summed device time;
+    share = their time / the profiled step's time.  Every other launch group is
+    listed under per_kind with its own bandwidth and share."""
+    pk = peaks()
+    total = sum(v["ms"] for v in prof.values())
+    ms = sum(prof[k]["ms"] for k in STEP_PRODUCTS if k in prof)
+    nbytes = sum(prof[k]["bytes"] for k in STEP_PRODUCTS if k in prof)
+    groups = sum(prof[k]["launch_groups"] for k in STEP_PRODUCTS if k in prof)
+    achieved = nbytes / (ms / 1e3) / 1e9
+    per_kind = {}
+    for k, v in prof.items():
+        gbs = v["bytes"] / (v["ms"] / 1e3) / 1e9 if v["ms"] > 0 else None
+        per_kind[k] = {"ms": v["ms"], "algorithmic_bytes": v["bytes"], "launch_groups": v["launch_groups"],
+                       "achieved_gbs": gbs, "frac": gbs / pk["hbm_gbs"] if gbs is not None else None,
+                       "share": v["ms"] / total if total > 0 else None}
+    t = TRAFFIC[traffic_key]
+    return {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+            "frac": achieved / pk["hbm_gbs"], "traffic": t["dram_bytes"], "kernel": kernel,
+            "share": ms / total if total > 0 else None, "kernel_ms_per_step": ms,
+            "algorithmic_bytes_per_step": nbytes, "launch_groups_per_step": groups,
+            "traffic_launch": t["launch"], "traffic_launch_algorithmic_bytes": t["algorithmic_bytes"],
+            "traffic_source": t["source"],
+            "peak_source": f"{pk['source']} hbm_gbs (burst copy)",
+            "method": "rta_model_profile_step: one decode step replayed as a graph with a CUDA event after every "
+                      "launch group (median of 3 steps); the events remove the overlap of consecutive kernels, "
+                      "so each group is timed on its own and the shares are of that serialised step",
+            "per_kind": per_kind}
+
+
+def other_configs(args) -> list:
+    """The benchmark's other configurations on this GPU, measured in the same run
+    (N = 1 only): config 1 (MLP), config 2 (attention at L = 32768), config 3 (LM
+    head at batch 1 and 64) -- each with its dominant kernel timed alone by CUDA
+    events and its public-API e2e -- and config 4 (2B decode, 512-token prompt)
+    with its step-profile roofline.  A compact record per configuration."""
+    import torch
+    pk = peaks()
+    out = []
+    for name, kw in (("mlp", {}), ("attention", {"history": 32768}), ("lmhead", {"batch": 1}),
+                     ("lmhead", {"batch": 64})):
+        wl = WORKLOADS[name](**kw)
+        steps = max(10, args.steps // 2)
+        ms = time_steps(wl.step, steps, args.warmup, 1, min_seconds=0.3) / steps
+        dom_ms = time_steps(wl.dominant_launch, steps, args.warmup, 1) / steps
+        e2e_ms = time_steps(wl.e2e_step, steps, args.warmup, 1, graph=False) / steps
+        achieved = wl.dominant_bytes() / (dom_ms / 1e3) / 1e9
+        h2d, d2h = wl.e2e_bytes()
+        out.append({"config": wl.config(), "metric": wl.metric, "value": wl.units_per_step() / (ms / 1e3),
+                    "unit": wl.unit, "ms_per_step": ms,
+                    "roofline": {"kernel": wl.dominant, "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                                 "frac": achieved / pk["hbm_gbs"], "kernel_ms": dom_ms,
+                                 "algorithmic_bytes": wl.dominant_bytes(), "traffic": getattr(wl, "traffic", None)},
+                    "e2e": {"value": wl.units_per_step() / (e2e_ms / 1e3), "unit": wl.unit,
+                            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}})
+        del wl
+        torch.cuda.empty_cache()
+    wl = DecodeWorkload(prompt_len=512)
+    wl.decode(args.warmup)
+    ms_total, reps = 0.0, 0
+    for _ in range(3):
+        ms, _ = wl.decode(args.steps)
+        ms_total += ms
+        reps += 1
+    ms_step = ms_total / reps / args.steps
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        wl.model.generate(1)
+    e2e_s = (time.perf_counter() - t0) / args.steps
+    roof = step_roofline(profile_summary(wl.model), wl.dominant, "gemv_tiled")
+    out.append({"config": wl.config(), "metric": wl.metric, "value": 1e3 / ms_step, "unit": wl.unit,
+                "ms_per_step": ms_step, "roofline": roof,
+                "e2e": {"value": 1.0 / e2e_s, "unit": wl.unit, "h2d_bytes_per_step": 48, "d2h_bytes_per_step": 52}})
+    wl.model.close()
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_ours(args, world, rank, local):
     import torch
     kw = {"history": args.history} if args.workload == "attention" else \
@@ -1013,6 +1091,8 @@ def run_ours(args, world, rank, local):
         "clocks": clk.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import oracle
+        oracle.use_all_cores()
         line["cpu_baseline"] = wl.cpu_baseline(args.cpu_budget)
     if hasattr(wl, "close"):
         wl.close()
@@ -1111,12 +1191,14 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="decode2b")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="ragged9b")
     ap.add_argument("--history", type=int, default=32768)
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--min-seconds", type=float, default=1.0,
                     help="repeat the timed K-step region for at least this long (clock sampling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-other-configs", action="store_true",
+                    help="ragged9b at N=1: skip the compact lines of benchmark configs 1-4")
     ap.add_argument("--batch", type=int, default=1,
                     help="lmhead: hidden rows per readout (config 3: 1 or 64); gemm: batch rows")
     ap.add_argument("--rows", type=int, default=12288, help="gemm: weight rows (multiple of 128)")
@@ -1138,6 +1220,9 @@ def main():
     if args.impl == "reference":
         rank = int(os.environ.get("RANK", "0"))
         world = int(os.environ.get("WORLD_SIZE", "1"))
+        if rank == 0:
+            from oracle import oracle
+            oracle.use_all_cores()  # torch.distributed.run sets OMP_NUM_THREADS=1 for every rank
         line = run_reference(args, world, rank)
         if line is not None:
             print(json.dumps(line), flush=True)

@@ -69,12 +69,16 @@ RTA_API const char* rta_version(void);
  * (ray_tracing/native/shaders/resident_history_quant.glsl:9-41). */
 RTA_API rta_status rta_quantize(int format, const float* src, size_t nblocks, void* dst_blocks, void* stream);
 
-/* Synthetic weights: nblocks x 256 values drawn N(0, sigma) from a counter-based
- * generator keyed by (seed, global coefficient index), quantized as above. */
+/* Synthetic weights: nblocks x 256 values sigma * N from a counter-based
+ * generator keyed by (seed, global coefficient index), quantized as above.  N
+ * is an Irwin-Hall sum of eight 16-bit uniforms from two splitmix64 outputs,
+ * centred and scaled to unit variance (tails end at about 4.9 sigma): integer
+ * arithmetic and exactly rounded multiplies only, so a host restatement
+ * reproduces every value bit for bit. */
 RTA_API rta_status rta_synthetic_blocks(int format, uint64_t seed, float sigma, uint64_t first_block, size_t nblocks,
                                 void* dst_blocks, void* stream);
 
-/* Synthetic fp32 values mean + sigma * N(0,1), same generator. */
+/* Synthetic fp32 values mean + sigma * N, same generator. */
 RTA_API rta_status rta_synthetic_normal(uint64_t seed, float sigma, float mean, size_t n, float* dst, void* stream);
 
 /* Decode packed blocks to fp32, bit-exact with ggufValue
@@ -216,9 +220,13 @@ RTA_API rta_status rta_attention_decode_f16(const float* q, const void* k, const
  * serving loop).  The split records live in a fixed array inside the library's
  * device image (about 1 MiB per GPU that loads the library, held until the
  * process exits) instead of a caller workspace, so heads * splits must not
- * exceed 1024 (RTA_E_ARG otherwise).  The call allocates and frees nothing.
+ * exceed 1024 (RTA_E_ARG otherwise; misaligned k / v or strides are RTA_E_ARG
+ * too, before anything is launched).  The call allocates and frees nothing.
  * The first call on a device looks up the array's device address (set-up); make
- * that first call before any stream capture.  All calls share the array: calls
+ * that first call before any stream capture.  The address is kept per device
+ * and CUDA context: after a device reset, or with another context current on
+ * the device, the next call looks it up again (again outside any capture).  All
+ * calls share the array: calls
  * that overlap on the GPU (different streams, or different threads on one
  * device) race and must be serialised by the caller.  device_error: optional
  * caller-owned device word, zeroed by the call, that receives the device error
@@ -228,6 +236,32 @@ RTA_API rta_status rta_attention_decode_f16_noalloc(const float* q, const void* 
                                                     uint32_t head_dim, uint32_t pos_stride, uint32_t kv_stride,
                                                     const float* gate, float* out, float* phys, uint32_t splits,
                                                     uint32_t* device_error, void* stream);
+
+/* Recurrent gated-delta layer for one token of `batch` sequences: ops 18
+ * (gates), 19 (4-tap causal convolution + SiLU), 20 (L2 norms, convolution
+ * roll) and 21 (delta-rule state update and readout) of
+ * ray_tracing/native/shaders/resident_math.comp:131-148.  Device buffers:
+ *   x [batch][hidden] the layer's input residual rows (RMS-normed here with
+ *     attn_norm [hidden]); w_alpha, w_beta [heads][hidden] (F32 projections);
+ *     a_log, dt_bias [heads];
+ *   proj [batch][proj_stride] the raw in-projection rows [q (key_heads*128) |
+ *     k (key_heads*128) | v (heads*128) | ...];
+ *   conv_w [3*heads*128][4]; conv_state [batch][2][3*heads*128][3], double
+ *     buffered by position parity: buffer (positions[z] & 1) holds the three
+ *     previous taps and buffer (positions[z] & 1) ^ 1 receives the next ones;
+ *   state [batch][heads][128 value][128 key] (recurrentOffset,
+ *     resident_common.glsl:139), updated in place;
+ *   out [batch][heads*128] the detector output before the gated RMSNorm
+ *     (op 15, which the engine applies in the out-projection's prologue);
+ *   positions [batch] each sequence's absolute position.
+ * hidden <= 4096 and a multiple of 4; x, attn_norm, w_alpha, w_beta, conv_w
+ * 16-byte aligned.  device_error: optional word, zeroed by the call. */
+RTA_API rta_status rta_gated_delta_step(const float* x, const float* attn_norm, const float* w_alpha,
+                                        const float* w_beta, const float* a_log, const float* dt_bias,
+                                        const float* proj, uint32_t proj_stride, const float* conv_w,
+                                        float* conv_state, float* state, float* out, const uint32_t* positions,
+                                        uint32_t hidden, uint32_t heads, uint32_t key_heads, uint32_t batch,
+                                        float eps, uint32_t* device_error, void* stream);
 
 /* Device error word of the last operator call that had a workspace
  * (0 = clean); synchronizes `stream`. */
@@ -317,11 +351,33 @@ RTA_API rta_status rta_model_generate_batch(rta_model* model, uint32_t count, ui
  * (Resident::prefill, optical_resident.cpp:609-712). */
 RTA_API rta_status rta_model_prefill(rta_model* model, const uint32_t* ids, uint32_t n, const uint32_t stops[2],
                                      double* gpu_ms);
+/* Debug prefill, worker op 1 with debug = 1 (Resident::prefill capture,
+ * optical_resident.cpp:609-712, per-layer copy :481): prefill as above, and
+ * return the final-normed residual row of every position (states, [n][hidden],
+ * what the decode readout reads) and, when layers is not NULL, every layer's
+ * output row ([depth][n][hidden]). */
+RTA_API rta_status rta_model_prefill_capture(rta_model* model, const uint32_t* ids, uint32_t n,
+                                             const uint32_t stops[2], float* states, float* layers, double* gpu_ms);
 /* Greedy decode of up to `count` tokens (readout -> argmax -> embedding ->
  * layers per token), stopping after a stop id.  Worker op 2
  * (Resident::generatePacket, optical_resident.cpp:760-871). */
 RTA_API rta_status rta_model_generate(rta_model* model, uint32_t count, uint32_t* ids, uint32_t* n_out,
                                       double* gpu_ms);
+/* Step profile (no reference counterpart; the reference's debug = 2 prefill
+ * timestamps play this role for its own dispatches): one decode step of every
+ * running sequence, like rta_model_generate_batch(1) (the sequences advance),
+ * through a graph with an event after every launch group, so each group is
+ * timed on its own.  Per group, in launch order: its kind (RTA_PROF_*), its
+ * device time in ms and its algorithmic HBM bytes (packed weights once,
+ * activations, the visible history, the recurrent state read and written).
+ * Up to `capacity` groups are written; *n_groups receives the total. */
+enum {
+  RTA_PROF_START = 0, RTA_PROF_READOUT = 1, RTA_PROF_EMBED = 2, RTA_PROF_QKV = 3, RTA_PROF_PREP = 4,
+  RTA_PROF_ATTENTION = 5, RTA_PROF_O_PROJ = 6, RTA_PROF_IN_PROJ = 7, RTA_PROF_GATED_DELTA = 8,
+  RTA_PROF_OUT_PROJ = 9, RTA_PROF_GATE_UP = 10, RTA_PROF_DOWN = 11
+};
+RTA_API rta_status rta_model_profile_step(rta_model* model, uint32_t* kinds, double* ms, double* bytes,
+                                          size_t capacity, size_t* n_groups);
 /* Full-attention diagnostic, worker op 14 (attentionCheck,
  * resident_attention_runtime.inl:646-753): layer must be a full-attention
  * layer; q, gate [rows][heads][head_dim] (rotated), k, v [count][kv_heads][head_dim]

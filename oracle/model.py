@@ -220,3 +220,55 @@ class OracleModel:
                 break
             self.forward(tok)
         return np.array(ids, np.uint32), np.array(margins)
+
+
+# ------------------------------------------------------------ synthetic models
+def synthetic_payloads(layout, seed: int, sigma: float = 0.02):
+    """Host restatement of the product's GPU model generator (assets.generate_device):
+    tensor i of the layout (matrices, then vocabulary rows) is drawn with the seed
+    seed * 1000003 + i -- packed blocks through the synthetic block generator, F32
+    tensors as sigma * N -- so the returned (matrices, basis) bytes equal the GPU's
+    bit for bit."""
+    mats = np.zeros(layout.matrix_words * 4, np.uint8)
+    basis = np.zeros(layout.basis_words * 4, np.uint8)
+    for i, t in enumerate(layout.matrices + layout.basis):
+        buf = mats if i < len(layout.matrices) else basis
+        tseed = seed * 1000003 + i
+        if t.fmt == O.F32:
+            buf[t.offset:t.offset + t.nbytes] = O.synthetic_normal(tseed, sigma, t.rows * t.cols).view(np.uint8)
+        else:
+            buf[t.offset:t.offset + t.nbytes] = O.synthetic_blocks(t.fmt, tseed, sigma, t.rows * t.cols // 256)
+    return mats, basis
+
+
+def seed_sequence(ref: "OracleModel", nseq: int, z: int, length: int, seed: int):
+    """Put `ref` in the state rta_model_seed_history gives sequence z of an nseq-sequence
+    fp16-history handle: history positions 0..length-1 of every full layer from the
+    seeded K (seed) and V (seed + 1) rings [full layer][sequence][kv head][capacity][hd],
+    recurrent states sigma 0.02 (seed + 2) [layer][sequence][head][128][128], the conv
+    taps (seed + 3) [layer][sequence][parity][3S][3] of the buffer the next position's
+    parity reads, and the residual row (seed + 4) [sequence][D]; next position `length`."""
+    s = ref.s
+    cap, hd, kvh = ref.capacity, ref.hd, ref.KVH
+    assert length <= cap, "seeded histories here never wrap the ring"
+    ref.reset()
+    full = [l for l, L in enumerate(ref.layers) if L["full"]]
+    rec = [l for l, L in enumerate(ref.layers) if not L["full"]]
+    for fi, l in enumerate(full):
+        k = np.empty((length, kvh, hd), np.float32)
+        v = np.empty((length, kvh, hd), np.float32)
+        for h in range(kvh):
+            first = (((fi * nseq + z) * kvh + h) * cap) * hd
+            k[:, h, :] = O.synthetic_range(seed, 1.0, first, length * hd, half=True).reshape(length, hd)
+            v[:, h, :] = O.synthetic_range(seed + 1, 1.0, first, length * hd, half=True).reshape(length, hd)
+        ref.hist[l] = [(k[p], v[p]) for p in range(length)]
+    H, S = s.state_heads, s.state_width
+    for ri, l in enumerate(rec):
+        n = H * 128 * 128
+        ref.rec[l] = O.synthetic_range(seed + 2, 0.02, (ri * nseq + z) * n, n).reshape(H, 128, 128).copy()
+        per = 2 * 3 * S * 3
+        par = length & 1
+        ref.conv[l] = O.synthetic_range(seed + 3, 1.0, (ri * nseq + z) * per + par * 3 * S * 3,
+                                        3 * S * 3).reshape(3 * S, 3).copy()
+    ref.state = O.synthetic_range(seed + 4, 1.0, z * ref.D, ref.D).copy()
+    ref.pos = length

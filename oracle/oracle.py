@@ -55,7 +55,13 @@ def lib():
             "rta_oracle_head_norm": (None, [p, p, u32, u32, f]),
             "rta_oracle_sigmoid": (f, [f]),
             "rta_oracle_threads": (i32, []),
+            "rta_oracle_set_threads": (None, [i32]),
             "rta_oracle_inv_freq": (None, [f, u32, u32, p]),
+            "rta_oracle_synthetic_value": (f, [ctypes.c_uint64, ctypes.c_uint64]),
+            "rta_oracle_synthetic_blocks": (None, [i32, ctypes.c_uint64, f, ctypes.c_uint64, sz, p]),
+            "rta_oracle_synthetic_normal": (None, [ctypes.c_uint64, f, f, sz, p]),
+            "rta_oracle_synthetic_half": (None, [ctypes.c_uint64, f, ctypes.c_uint64, sz, p]),
+            "rta_oracle_synthetic_range": (None, [ctypes.c_uint64, f, ctypes.c_uint64, sz, p]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(_lib, name)
@@ -73,6 +79,15 @@ def _c(a, dtype):
 
 def threads() -> int:
     return int(lib().rta_oracle_threads())
+
+
+def use_all_cores() -> int:
+    """Run the OpenMP loops on every core this process may use (its CPU affinity),
+    whatever OMP_NUM_THREADS a launcher set; returns the thread count."""
+    import os
+    n = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    lib().rta_oracle_set_threads(n)
+    return threads()
 
 
 def quantize(fmt: int, values) -> np.ndarray:
@@ -145,15 +160,16 @@ def attention(q, keys, values, gate, query_start: int, history_start: int, capac
 
 def gdn(x, qk, v, z, wa, wb, a_log, dt_bias, conv_w, norm_w, H: int, KH: int, eps: float,
         state, conv, use_past: bool = True):
-    """Recurrent layer detector; `state` [H,128,128] and `conv` [3S,3] are updated in place."""
+    """Recurrent layer detector; `state` [H,128,128] and `conv` [3S,3] are updated in place.
+    With norm_w None (z unused) the output is the detector before the gated RMSNorm (op 15)."""
     x = _c(x, np.float32)
     rows, D = x.shape
     S = H * 128
     out = np.empty((rows, S), np.float32)
     assert state.dtype == np.float32 and state.flags.c_contiguous
     assert conv.dtype == np.float32 and conv.flags.c_contiguous
-    args = [_c(a, np.float32) for a in (qk, v, z, wa, wb, a_log, dt_bias, conv_w, norm_w)]
-    lib().rta_oracle_gdn(_p(x), *[_p(a) for a in args], rows, D, H, KH, eps, int(use_past),
+    args = [None if a is None else _c(a, np.float32) for a in (qk, v, z, wa, wb, a_log, dt_bias, conv_w, norm_w)]
+    lib().rta_oracle_gdn(_p(x), *[None if a is None else _p(a) for a in args], rows, D, H, KH, eps, int(use_past),
                          _p(state), _p(conv), _p(out))
     return out
 
@@ -178,3 +194,30 @@ def inv_freq(theta: float, rotary: int, hd: int) -> np.ndarray:
 
 def sigmoid(x: float) -> float:
     return float(lib().rta_oracle_sigmoid(x))
+
+
+# ------------------------------------------------- synthetic model values
+def synthetic_blocks(fmt: int, seed: int, sigma: float, nblocks: int, first_block: int = 0) -> np.ndarray:
+    """Host restatement of rta_synthetic_blocks: bit-identical packed blocks."""
+    out = np.empty(nblocks * BLOCK_BYTES[fmt], np.uint8)
+    lib().rta_oracle_synthetic_blocks(fmt, seed, sigma, first_block, nblocks, _p(out))
+    return out
+
+
+def synthetic_normal(seed: int, sigma: float, n: int, mean: float = 0.0) -> np.ndarray:
+    """Host restatement of rta_synthetic_normal (fp32, bit-identical)."""
+    out = np.empty(n, np.float32)
+    lib().rta_oracle_synthetic_normal(seed, sigma, mean, n, _p(out))
+    return out
+
+
+def synthetic_range(seed: int, sigma: float, first: int, n: int, half: bool = False) -> np.ndarray:
+    """Elements [first, first + n) of the generator's stream times sigma: fp32, or
+    rounded to fp16 (returned as float32 values) like the seeded fp16 histories."""
+    if half:
+        out = np.empty(n, np.uint16)
+        lib().rta_oracle_synthetic_half(seed, sigma, first, n, _p(out))
+        return out.view(np.float16).astype(np.float32)
+    out = np.empty(n, np.float32)
+    lib().rta_oracle_synthetic_range(seed, sigma, first, n, _p(out))
+    return out

@@ -16,8 +16,11 @@
 // m16n8k16 f16 MMA: columns 0-3 hold fp16(q) and columns 4-7 the fp16
 // residual q - fp16(q), so scores carry ~22 significant bits; P is split the
 // same way for the P*V MMA.  Accumulation is fp32 throughout.
+#include <atomic>
 #include <mutex>
 #include <string>
+
+#include <cuda.h>
 
 #include "../../include/rta.h"
 #include "rta_internal.h"
@@ -155,12 +158,14 @@ __global__ void __launch_bounds__(kThreads) attention_split_kernel(const AttnPar
   for (int mt = 0; mt < 16; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
   float m_run[2] = {-INFINITY, -INFINITY}, z_run[2] = {0.f, 0.f};
   bool failed = false;
+  uint32_t failed_tile = 0;
   __half* pw = pbuf + warp * 8 * kTile;
 
   for (uint32_t tile = warp; tile < ntiles; tile += kWarps) {
     const uint32_t s = tile % kStages;
     if (!mbar_wait(&bars[s], (tile / kStages) & 1u, p.err)) {
       failed = true;
+      failed_tile = tile;
       break;
     }
     const uint32_t st = smem_u32(smem + s * kStageBytes);
@@ -244,7 +249,14 @@ __global__ void __launch_bounds__(kThreads) attention_split_kernel(const AttnPar
   const size_t rec = (static_cast<size_t>(z) * p.kvh + kv) * gridDim.x + split;  // record index
   if (__syncthreads_or(failed ? 1 : 0)) {
     // A stage never arrived: publish an empty record (the host sees the
-    // timeout bit) and leave shared memory alone, a copy may still land.
+    // timeout bit).  The warp that gave up still owns the copies it issued
+    // and has not consumed (tiles failed_tile, +kWarps, ... below
+    // failed_tile + kStages): wait for them once more, boundedly, so that no
+    // bulk copy lands in shared memory after this CTA has left the SM.
+    if (failed && lane == 0)
+      for (uint32_t u = failed_tile; u < ntiles && u < failed_tile + kStages; u += kWarps)
+        (void)mbar_wait(&bars[u % kStages], (u / kStages) & 1u, nullptr);
+    __syncwarp();
     for (uint32_t i = threadIdx.x; i < kGroup * kHD; i += kThreads) {
       p.part_o[(rec * kGroup + i / kHD) * kHD + i % kHD] = 0.f;
       if (i % kHD == 0) {
@@ -613,23 +625,34 @@ cudaError_t launch_attention(const AttnParams& p, uint32_t nsplit, uint32_t nseq
   if (reinterpret_cast<uintptr_t>(p.k) % 16 || reinterpret_cast<uintptr_t>(p.v) % 16 || p.pos_stride % 8 ||
       p.kv_stride % 8 || p.seq_stride % 8)
     return cudaErrorMisalignedAddress;
-  static bool attr_set[64] = {false};  // one-time per-device kernel setup, off the per-launch path
-  static int sms_of[64] = {0};
+  // One-time per-device kernel setup, off the per-launch path.  Host threads
+  // may make their first call on one device at the same time: the setup runs
+  // under a lock and publishes the SM count with release order, so the fast
+  // path (an acquire load) never reads a half-initialised entry.
+  static std::mutex setup_mutex;
+  static std::atomic<int> sms_of[64];
   cudaError_t e = cudaSuccess;
   int dev = 0;
-  cudaGetDevice(&dev);
+  e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if (!attr_set[dev]) {
-    e = cudaFuncSetAttribute(attention_split_kernel<kStages>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(attention_smem_bytes(kStages)));
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(attention_split_kernel<kStagesMany>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(attention_smem_bytes(kStagesMany)));
-    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms_of[dev], cudaDevAttrMultiProcessorCount, dev);
-    if (e != cudaSuccess) return e;
-    attr_set[dev] = true;
+  int sms = sms_of[dev].load(std::memory_order_acquire);
+  if (sms == 0) {
+    std::lock_guard<std::mutex> lock(setup_mutex);
+    sms = sms_of[dev].load(std::memory_order_relaxed);
+    if (sms == 0) {
+      e = cudaFuncSetAttribute(attention_split_kernel<kStages>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(attention_smem_bytes(kStages)));
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(attention_split_kernel<kStagesMany>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(attention_smem_bytes(kStagesMany)));
+      if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      if (e != cudaSuccess) return e;
+      if (sms <= 0) return cudaErrorInvalidDevice;
+      sms_of[dev].store(sms, std::memory_order_release);
+    }
   }
-  const bool many = static_cast<uint64_t>(nsplit) * p.kvh * nseq > static_cast<uint64_t>(sms_of[dev]);
+  const bool many = static_cast<uint64_t>(nsplit) * p.kvh * nseq > static_cast<uint64_t>(sms);
   const size_t smem = attention_smem_bytes(many ? kStagesMany : kStages);
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -674,7 +697,43 @@ constexpr uint32_t kStaticRecords = 1024;  // (query heads) x (splits) records a
 constexpr size_t kStaticFloats = kStaticRecords * (2 + kHD);
 static __device__ __align__(256) float g_attention_scratch[kStaticFloats];
 std::mutex g_scratch_mutex;
-float* g_scratch_addr[64] = {nullptr};  // device address of the array, per device ordinal
+// Device address of the array per device ordinal, valid in the CUDA context it
+// was looked up in (identified by the driver's context id, which is never
+// reused within a process): a caller that resets the device or makes another
+// context current on it gets a fresh lookup instead of a stale address.
+struct ScratchAddr {
+  unsigned long long ctx_id = 0;
+  float* addr = nullptr;
+};
+ScratchAddr g_scratch_addr[64];
+
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+
+// Id of the calling thread's current context (0 when there is none or the
+// driver cannot tell); the driver entry points are resolved through the
+// runtime, so the library needs no link against the driver library.
+unsigned long long current_context_id() {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static std::once_flag resolved;
+  std::call_once(resolved, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(fn);
+    fn = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(fn);
+  });
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || !ctx || get_id(ctx, &id) != CUDA_SUCCESS)
+    return 0;
+  return id;
+}
 }  // namespace
 }  // namespace rta
 
@@ -701,12 +760,21 @@ extern "C" rta_status rta_attention_decode_f16_noalloc(const float* q, const voi
     set_last_error("rta_attention_decode_f16_noalloc: no current CUDA device");
     return RTA_E_CUDA;
   }
+  if (reinterpret_cast<uintptr_t>(k) % 16 || reinterpret_cast<uintptr_t>(v) % 16 || pos_stride % 8 ||
+      kv_stride % 8) {
+    set_last_error("rta_attention_decode_f16_noalloc: k and v must be 16-byte aligned and pos_stride, kv_stride "
+                   "multiples of 8 (rows are copied in 16-byte units)");
+    return RTA_E_ARG;
+  }
   float* scratch = nullptr;
   {
-    // One-time set-up per device, with that device current: the array's name is
-    // only a host-side stand-in, the kernel needs its device address.
+    // Set-up per device (and per context on it), with that device current:
+    // the array's name is only a host-side stand-in, the kernel needs its
+    // device address.  The first call on a device does this lookup.
     std::lock_guard<std::mutex> lock(g_scratch_mutex);
-    if (!g_scratch_addr[dev]) {
+    ScratchAddr& slot = g_scratch_addr[dev];
+    unsigned long long ctx = current_context_id();
+    if (!slot.addr || ctx == 0 || slot.ctx_id != ctx) {
       void* addr = nullptr;
       e = cudaGetSymbolAddress(&addr, g_attention_scratch);
       if (e != cudaSuccess || !addr) {
@@ -714,9 +782,11 @@ extern "C" rta_status rta_attention_decode_f16_noalloc(const float* q, const voi
                        cudaGetErrorString(e));
         return RTA_E_CUDA;
       }
-      g_scratch_addr[dev] = static_cast<float*>(addr);
+      if (ctx == 0) ctx = current_context_id();  // the lookup made the primary context current
+      slot.addr = static_cast<float*>(addr);
+      slot.ctx_id = ctx;
     }
-    scratch = g_scratch_addr[dev];
+    scratch = slot.addr;
   }
   const size_t recs = static_cast<size_t>(heads) * splits;
   AttnParams p;

@@ -11,6 +11,7 @@
 
 #include "../../include/rta.h"
 #include "attention.h"
+#include "layers.h"
 #include "rta_internal.h"
 
 namespace {
@@ -335,6 +336,9 @@ rta_status rta_attention_decode_f16(const float* q, const void* k, const void* v
     return fail(RTA_E_ARG, "rta_attention_decode_f16: head_dim 256, heads == 4*kv_heads, capacity > 0, 1 <= splits <= 1024");
   if (workspace_bytes < rta_attention_workspace_bytes(heads, kv_heads, head_dim, splits))
     return fail(RTA_E_ARG, "rta_attention_decode_f16: workspace too small");
+  if (reinterpret_cast<uintptr_t>(k) % 16 || reinterpret_cast<uintptr_t>(v) % 16 || pos_stride % 8 || kv_stride % 8)
+    return fail(RTA_E_ARG, "rta_attention_decode_f16: k and v must be 16-byte aligned and pos_stride, kv_stride "
+                           "multiples of 8 (rows are copied in 16-byte units)");
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   const size_t recs = static_cast<size_t>(heads) * splits;
   rta::AttnParams p;
@@ -363,6 +367,57 @@ rta_status rta_attention_decode_f16(const float* q, const void* k, const void* v
   rta_status st = cuda_status(cudaMemsetAsync(ws, 0, 4, s), "rta_attention_decode_f16(memset)");
   if (st != RTA_OK) return st;
   return cuda_status(rta::launch_attention(p, splits, 1, false, s), "rta_attention_decode_f16");
+}
+
+rta_status rta_gated_delta_step(const float* x, const float* attn_norm, const float* w_alpha, const float* w_beta,
+                                const float* a_log, const float* dt_bias, const float* proj, uint32_t proj_stride,
+                                const float* conv_w, float* conv_state, float* state, float* out,
+                                const uint32_t* positions, uint32_t hidden, uint32_t heads, uint32_t key_heads,
+                                uint32_t batch, float eps, uint32_t* device_error, void* stream) {
+  if (!x || !attn_norm || !w_alpha || !w_beta || !a_log || !dt_bias || !proj || !conv_w || !conv_state || !state ||
+      !out || !positions)
+    return fail(RTA_E_ARG, "rta_gated_delta_step: null argument");
+  if (hidden == 0 || hidden > 4096 || hidden % 4 || heads == 0 || key_heads == 0 || heads % key_heads || batch == 0 ||
+      batch > 1024 || proj_stride < 2u * key_heads * 128u + heads * 128u)
+    return fail(RTA_E_ARG, "rta_gated_delta_step: hidden 4..4096 (multiple of 4), heads a multiple of key_heads, "
+                           "batch 1..1024, proj_stride >= 2 * key_heads * 128 + heads * 128");
+  const auto misaligned = [](const void* q, uintptr_t a) { return reinterpret_cast<uintptr_t>(q) % a != 0; };
+  if (misaligned(x, 16) || misaligned(attn_norm, 16) || misaligned(w_alpha, 16) || misaligned(w_beta, 16) ||
+      misaligned(conv_w, 16) || misaligned(state, 8) || (static_cast<size_t>(hidden) * 4) % 16)
+    return fail(RTA_E_ARG, "rta_gated_delta_step: x, attn_norm, w_alpha, w_beta and conv_w must be 16-byte "
+                           "aligned, state 8-byte aligned");
+  const uint32_t S = heads * 128u;
+  rta::GdnParams p;
+  p.x = x;
+  p.attn_norm = attn_norm;
+  p.eps = eps;
+  p.wa = w_alpha;
+  p.wb = w_beta;
+  p.a_log = a_log;
+  p.dt_bias = dt_bias;
+  p.proj = proj;
+  p.conv_w = conv_w;
+  p.conv_state = conv_state;
+  p.rec = state;
+  p.out = out;
+  p.D = hidden;
+  p.H = heads;
+  p.KH = key_heads;
+  p.pos = positions;
+  p.running = nullptr;
+  p.err = device_error;
+  p.err_step = 0;
+  p.nseq = batch;
+  p.ctrl_step = 1;
+  p.proj_seq = proj_stride;
+  p.conv_seq = static_cast<size_t>(2) * 3 * S * 3;
+  p.rec_seq = static_cast<size_t>(heads) * 128 * 128;
+  cudaStream_t s = as_stream(stream);
+  if (device_error) {
+    rta_status st = cuda_status(cudaMemsetAsync(device_error, 0, 4, s), "rta_gated_delta_step(memset)");
+    if (st != RTA_OK) return st;
+  }
+  return cuda_status(rta::launch_gdn(p, s, false), "rta_gated_delta_step");
 }
 
 rta_status rta_workspace_error(const void* workspace, size_t workspace_bytes, void* stream, uint32_t* error_word) {

@@ -127,6 +127,35 @@ struct Engine {
   DevBuf<uint32_t> prompt;
   Control* ctrl_host = nullptr;  // pinned mirror [nseq]
   cudaGraphExec_t g_decode = nullptr, g_prefill = nullptr;
+  // Debug prefill (worker op 1 with debug = 1): a third graph, captured on first
+  // use, that also copies every layer's output row and the final-normed row of
+  // the position it processes into cap = [depth + 1][capacity][D] (final rows first).
+  cudaGraphExec_t g_prefill_cap = nullptr;
+  DevBuf<float> cap;
+  // Step profile (rta_model_profile_step): while `profiling` is set, record_step
+  // puts an event after every launch group of the step it records, labelled
+  // with the group's kind and its algorithmic HBM bytes.
+  bool profiling = false;
+  std::vector<cudaEvent_t> prof_ev;
+  std::vector<uint32_t> prof_kind;
+  std::vector<double> prof_bytes;
+  void mark(uint32_t kind, double bytes, cudaStream_t s) {
+    if (!profiling) return;
+    cudaEvent_t e = nullptr;
+    RTA_CUDA(cudaEventCreate(&e));
+    prof_ev.push_back(e);
+    prof_kind.push_back(kind);
+    prof_bytes.push_back(bytes);
+    RTA_CUDA(cudaEventRecord(e, s));
+  }
+  // Algorithmic bytes of one product: the packed weights once, x read, y written
+  // (read too when accumulated).
+  static double product_bytes(const GemvArgs& a) {
+    const int base = a.fmt % 100;  // tiled / panel codes keep the packed format in the last two digits
+    const double w = static_cast<double>(a.rows) * (a.cols / 256) * block_bytes(base) * (a.w1 ? 2.0 : 1.0);
+    const double rows_out = static_cast<double>(a.rows) * (a.w1 ? 2.0 : 1.0);
+    return w + 4.0 * a.batch * (a.cols + rows_out * (a.epilogue == kAccumulate ? 2.0 : 1.0));
+  }
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
   uint32_t stops[2] = {0xffffffffu, 0xffffffffu};
   uint32_t position = 0;          // sequence 0's next position (single-sequence API)
@@ -144,6 +173,7 @@ struct Engine {
   ~Engine() {
     if (g_decode) cudaGraphExecDestroy(g_decode);
     if (g_prefill) cudaGraphExecDestroy(g_prefill);
+    if (g_prefill_cap) cudaGraphExecDestroy(g_prefill_cap);
     if (ev0) cudaEventDestroy(ev0);
     if (ev1) cudaEventDestroy(ev1);
     if (ctrl_host) cudaFreeHost(ctrl_host);
@@ -520,7 +550,9 @@ struct Engine {
     const bool dpanel = dn.fmt == kQ4KPanel || dn.fmt == kQ6KPanel;
     if (!gpanel) {
       RTA_CUDA(launch_gemv(g, s));
+      mark(RTA_PROF_GATE_UP, product_bytes(g), s);
       RTA_CUDA(matmul(dn, s));
+      mark(RTA_PROF_DOWN, product_bytes(dn), s);
       return;
     }
     float* act_rows = g.y;
@@ -529,6 +561,7 @@ struct Engine {
     g.y = gu.p;
     g.y_stride = 2 * F;  // matrix 1 (up) rows follow matrix 0 (gate) rows
     RTA_CUDA(matmul(g, s));
+    mark(RTA_PROF_GATE_UP, product_bytes(g), s);
     if (dpanel && !need_act) {
       dn.prologue = kSwiGLUIn;
       dn.x = gu.p;
@@ -539,10 +572,11 @@ struct Engine {
       RTA_CUDA(launch_swiglu_rows(gu.p, g.batch, F, 2 * F, act_rows, act_stride, s));
     }
     RTA_CUDA(matmul(dn, s));
+    mark(RTA_PROF_DOWN, product_bytes(dn), s);
   }
 
   // ---------------------------------------------------------- step recording
-  uint32_t record_step(bool decode) {
+  uint32_t record_step(bool decode, bool capture_rows = false) {
     const cudaStream_t s = stream;
     uint32_t n = 0;
     Control* c = ctrl.p;
@@ -550,6 +584,7 @@ struct Engine {
     const uint32_t D = this->D(), F = spec.middle_size, hd = spec.attention_head_dim;
     const uint32_t cstep = static_cast<uint32_t>(sizeof(Control) / 4);  // u32 between sequences' control words
     static_assert(sizeof(Control) % 8 == 0, "control blocks must keep 8-byte alignment");
+    mark(RTA_PROF_START, 0.0, s);
     if (decode) {
       GemvArgs r;
       r.fmt = lm_fmt;
@@ -569,6 +604,7 @@ struct Engine {
       r.running_step = cstep;
       r.pdl = true;
       RTA_CUDA(matmul(r, s));
+      mark(RTA_PROF_READOUT, product_bytes(r) - 4.0 * r.batch * r.rows, s);  // logits are not stored
       ++n;
     }
     EmbedParams e;
@@ -584,6 +620,7 @@ struct Engine {
     e.mode = decode ? kEmbedDecode : kEmbedPrefill;
     e.state = state.p;
     RTA_CUDA(launch_embed(e, s, true));
+    mark(RTA_PROF_EMBED, static_cast<double>(nseq) * (e.row_bytes + 4.0 * D), s);
     ++n;
     for (size_t li = 0; li < layers.size(); ++li) {
       Layer& L = *layers[li];
@@ -606,6 +643,7 @@ struct Engine {
         g.err = &c->err;
         g.pdl = true;
         RTA_CUDA(matmul(g, s));
+        mark(RTA_PROF_QKV, product_bytes(g), s);
         PrepParams pp;
         pp.qkvg = proj.p;
         pp.qnorm = L.qnorm;
@@ -634,6 +672,8 @@ struct Engine {
         const size_t layer_pkt = static_cast<size_t>(nseq) * capacity * pbytes;
         if (packet_history) pp.packets = pring.p + L.fi * layer_pkt;
         RTA_CUDA(launch_attn_prep(pp, s, true));
+        mark(RTA_PROF_PREP, static_cast<double>(nseq) * 4.0 * (L.qkvg_rows + Q()) +
+                                static_cast<double>(nseq) * (packet_history ? pbytes : 4.0 * KVW()), s);
         AttnParams ap;
         ap.q = qproc.p;
         ap.k = pp.kcache;
@@ -665,6 +705,7 @@ struct Engine {
         ap.running = running;
         ap.split_by_length = nseq >= kTcMinSeq ? 1u : 0u;
         RTA_CUDA(launch_attention(ap, nsplit, nseq, true, s));
+        mark(RTA_PROF_ATTENTION, attention_bytes(), s);
         GemvArgs o;
         o.fmt = L.o_fmt;
         o.w0 = L.o;
@@ -681,6 +722,7 @@ struct Engine {
         o.err = &c->err;
         o.pdl = true;
         RTA_CUDA(matmul(o, s));
+        mark(RTA_PROF_O_PROJ, product_bytes(o), s);
         n += 5;
       } else {
         GemvArgs g;
@@ -701,6 +743,7 @@ struct Engine {
         g.err = &c->err;
         g.pdl = true;
         RTA_CUDA(matmul(g, s));
+        mark(RTA_PROF_IN_PROJ, product_bytes(g), s);
         GdnParams gp;
         gp.x = state.p;
         gp.attn_norm = L.gate_w.p + 2ull * spec.state_heads * D;  // aligned copy of L.attn_norm
@@ -724,8 +767,11 @@ struct Engine {
         gp.KH = spec.state_key_heads;
         gp.pos = &c->pos_cur;
         gp.err = &c->err;
+        gp.err_step = cstep;
         gp.running = running;
         RTA_CUDA(launch_gdn(gp, s, true));
+        mark(RTA_PROF_GATED_DELTA, static_cast<double>(running_sequences()) *
+                                       (8.0 * spec.state_heads * 128 * 128 + 4.0 * (2 * K() + 2 * S() + 2 * D)), s);
         GemvArgs o;
         o.fmt = L.out_fmt;
         o.w0 = L.out;
@@ -747,6 +793,7 @@ struct Engine {
         o.err = &c->err;
         o.pdl = true;
         RTA_CUDA(matmul(o, s));
+        mark(RTA_PROF_OUT_PROJ, product_bytes(o), s);
         n += 3;
       }
       GemvArgs gu;
@@ -785,17 +832,53 @@ struct Engine {
       dn.pdl = true;
       mlp_pair(gu, dn, false, s);
       n += 2;
+      if (capture_rows) {
+        CaptureParams cp;
+        cp.state = state.p;
+        cp.dst = cap.p + (li + 1) * static_cast<size_t>(capacity) * D;
+        cp.ctrl = c;
+        cp.D = D;
+        cp.capacity = capacity;
+        RTA_CUDA(launch_capture_row(cp, s, true));
+        ++n;
+      }
+    }
+    if (capture_rows) {  // the final-normed row (op 1 index 2), what the reference's debug prefill returns
+      CaptureParams cp;
+      cp.state = state.p;
+      cp.dst = cap.p;
+      cp.ctrl = c;
+      cp.norm_w = out_norm;
+      cp.eps = spec.norm_epsilon;
+      cp.D = D;
+      cp.capacity = capacity;
+      RTA_CUDA(launch_capture_row(cp, s, true));
+      ++n;
     }
     return n;
   }
 
   void capture() {
     for (int mode = 0; mode < 2; ++mode) {
+      uint32_t n = 0;
+      cudaGraphExec_t exec = instantiate_step(mode == 1, false, &n);
+      if (mode == 1) {
+        g_decode = exec;
+        kernels_per_decode = n;
+      } else {
+        g_prefill = exec;
+        kernels_per_prefill = n;
+      }
+    }
+  }
+
+  cudaGraphExec_t instantiate_step(bool decode, bool capture_rows, uint32_t* launches) {
+    {
       cudaGraph_t graph = nullptr;
       RTA_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeRelaxed));
       uint32_t n = 0;
       try {
-        n = record_step(mode == 1);
+        n = record_step(decode, capture_rows);
       } catch (...) {
         cudaStreamEndCapture(stream, &graph);
         if (graph) cudaGraphDestroy(graph);
@@ -809,14 +892,73 @@ struct Engine {
       const cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
       cudaGraphDestroy(graph);
       RTA_CUDA(e);
-      if (mode == 1) {
-        g_decode = exec;
-        kernels_per_decode = n;
-      } else {
-        g_prefill = exec;
-        kernels_per_prefill = n;
-      }
+      if (launches) *launches = n;
+      return exec;
     }
+  }
+
+  // Sequences that take part in the next step (host mirror of the positions).
+  uint32_t running_sequences() const {
+    uint32_t r = 0;
+    for (uint32_t z = 0; z < nseq; ++z) r += positions[z] > 0 ? 1u : 0u;
+    return r;
+  }
+  // Algorithmic bytes of one full layer's attention in the next step: every
+  // visible history position of every running sequence once (K and V), plus
+  // q, the gate rows and the output.
+  double attention_bytes() const {
+    const double per_pos = packet_history ? static_cast<double>(pbytes) : 4.0 * KVW();
+    double b = 0.0;
+    for (uint32_t z = 0; z < nseq; ++z)
+      if (positions[z] > 0) b += per_pos * std::min(positions[z] + 1u, capacity) + 12.0 * Q();
+    return b;
+  }
+
+  // One decode step of every sequence through a graph that has an event after
+  // every launch group; returns per group its kind, device time and
+  // algorithmic bytes.  Events between the launches remove the programmatic
+  // overlap of consecutive kernels, so each group is timed on its own.
+  void profile_step(uint32_t* kinds, double* ms, double* bytes, size_t cap_groups, size_t* n_groups) {
+    bool any = false;
+    for (uint32_t z = 0; z < nseq; ++z) {
+      ctrl_host[z].running = positions[z] > 0 ? 1u : 0u;
+      ctrl_host[z].n_out = 0u;
+      ctrl_host[z].stops[0] = stops[0];
+      ctrl_host[z].stops[1] = stops[1];
+      any = any || positions[z] > 0;
+    }
+    require(any, "prefill before profiling a decode step", RTA_E_STATE);
+    profiling = true;
+    cudaGraphExec_t exec = nullptr;
+    try {
+      exec = instantiate_step(true, false, nullptr);
+    } catch (...) {
+      profiling = false;
+      for (cudaEvent_t e : prof_ev) cudaEventDestroy(e);
+      prof_ev.clear(), prof_kind.clear(), prof_bytes.clear();
+      throw;
+    }
+    profiling = false;
+    write_headers();
+    cudaError_t e = cudaGraphLaunch(exec, stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    size_t n = 0;
+    for (size_t i = 1; e == cudaSuccess && i < prof_ev.size(); ++i) {
+      float t = 0.f;
+      e = cudaEventElapsedTime(&t, prof_ev[i - 1], prof_ev[i]);
+      if (n < cap_groups) {
+        kinds[n] = prof_kind[i];
+        ms[n] = t;
+        bytes[n] = prof_bytes[i];
+      }
+      ++n;
+    }
+    cudaGraphExecDestroy(exec);
+    for (cudaEvent_t ev : prof_ev) cudaEventDestroy(ev);
+    prof_ev.clear(), prof_kind.clear(), prof_bytes.clear();
+    RTA_CUDA(e);
+    if (n_groups) *n_groups = n;
+    read_control(1);
   }
 
   // Copy the control blocks back (header plus the first `ids` emitted ids of
@@ -874,6 +1016,34 @@ struct Engine {
     float ms = 0.f;
     cudaEventElapsedTime(&ms, ev0, ev1);
     last_gpu_ms = ms;
+  }
+
+  // Debug prefill: the same steps through the capture graph, then the
+  // final-normed row of every position (states [n][D]) and, when layers is not
+  // NULL, every layer's output row ([depth][n][D]).
+  void prefill_capture(const uint32_t* ids, uint32_t n, const uint32_t st[2], float* states, float* layer_rows) {
+    require(nseq == 1, "debug prefill serves single-sequence handles", RTA_E_STATE);
+    require(n >= 1 && n <= capacity, "prefill length must be 1..capacity", RTA_E_ARG);
+    require(states != nullptr, "debug prefill needs the state rows", RTA_E_ARG);
+    const size_t rows = static_cast<size_t>(capacity) * D();
+    if (!g_prefill_cap) {
+      cap.alloc((spec.depth + 1ull) * rows);
+      g_prefill_cap = instantiate_step(false, true, nullptr);
+    }
+    std::swap(g_prefill, g_prefill_cap);  // prefill_batch replays g_prefill
+    try {
+      prefill_batch(ids, &n, n, st);
+    } catch (...) {
+      std::swap(g_prefill, g_prefill_cap);
+      throw;
+    }
+    std::swap(g_prefill, g_prefill_cap);
+    RTA_CUDA(cudaMemcpyAsync(states, cap.p, static_cast<size_t>(n) * D() * 4, cudaMemcpyDeviceToHost, stream));
+    if (layer_rows)
+      for (uint32_t l = 0; l < spec.depth; ++l)
+        RTA_CUDA(cudaMemcpyAsync(layer_rows + static_cast<size_t>(l) * n * D(), cap.p + (l + 1ull) * rows,
+                                 static_cast<size_t>(n) * D() * 4, cudaMemcpyDeviceToHost, stream));
+    RTA_CUDA(cudaStreamSynchronize(stream));
   }
 
   void prefill(const uint32_t* ids, uint32_t n, const uint32_t st[2]) {
@@ -1325,6 +1495,31 @@ rta_status rta_model_prefill(rta_model* m, const uint32_t* ids, uint32_t n, cons
     cudaSetDevice(m->engine.device);
     m->engine.prefill(ids, n, stops);
     if (gpu_ms) *gpu_ms = m->engine.last_gpu_ms;
+  } catch (const rta::Failure& f) {
+    return rta::fail_model(f);
+  }
+  return RTA_OK;
+}
+
+rta_status rta_model_prefill_capture(rta_model* m, const uint32_t* ids, uint32_t n, const uint32_t stops[2],
+                                     float* states, float* layers, double* gpu_ms) {
+  if (!m || !ids || !states) return RTA_E_ARG;
+  try {
+    cudaSetDevice(m->engine.device);
+    m->engine.prefill_capture(ids, n, stops, states, layers);
+    if (gpu_ms) *gpu_ms = m->engine.last_gpu_ms;
+  } catch (const rta::Failure& f) {
+    return rta::fail_model(f);
+  }
+  return RTA_OK;
+}
+
+rta_status rta_model_profile_step(rta_model* m, uint32_t* kinds, double* ms, double* bytes, size_t capacity,
+                                  size_t* n_groups) {
+  if (!m || !kinds || !ms || !bytes || !n_groups) return RTA_E_ARG;
+  try {
+    cudaSetDevice(m->engine.device);
+    m->engine.profile_step(kinds, ms, bytes, capacity, n_groups);
   } catch (const rta::Failure& f) {
     return rta::fail_model(f);
   }

@@ -327,7 +327,7 @@ __global__ void __launch_bounds__(256, ROWS > 16u ? 2 : 1) gdn_kernel(GdnParams 
   const float raw_v = tid < kGdnRows ? proj[2u * K + h * HD + slice * kGdnRows + tid] : 0.f;
   if constexpr (!kHold) {  // both copies land (bounded) before the CTA may leave
     if (tid == 0) {
-      uint32_t* err = p.err ? p.err + static_cast<size_t>(z) * p.ctrl_step : nullptr;
+      uint32_t* err = p.err ? p.err + static_cast<size_t>(z) * p.err_step : nullptr;
       const bool a_ok = mbar_wait(&gdn_bar[0], 0u, err);
       const bool b_ok = mbar_wait(&gdn_bar[1], 0u, err);
       gdn_ok = a_ok && b_ok ? 1 : 0;
@@ -430,6 +430,26 @@ __global__ void __launch_bounds__(256, ROWS > 16u ? 2 : 1) gdn_kernel(GdnParams 
   }
 }
 
+// Prefill capture of one position's row (see CaptureParams).  The position is
+// the one this step's embed kernel advanced to; a sequence that sat the step
+// out (prompt consumed) writes nothing.
+__global__ void __launch_bounds__(256) capture_row_kernel(CaptureParams p) {
+  __shared__ float red[9];
+  pdl_wait();
+  pdl_launch_dependents();
+  const uint32_t pos = p.ctrl->pos_cur, run = p.ctrl->running;
+  if (!run || pos >= p.capacity) return;
+  float* dst = p.dst + static_cast<size_t>(pos) * p.D;
+  if (!p.norm_w) {
+    for (uint32_t i = threadIdx.x; i < p.D; i += blockDim.x) dst[i] = p.state[i];
+    return;
+  }
+  float ss = 0.f;
+  for (uint32_t i = threadIdx.x; i < p.D; i += blockDim.x) ss += p.state[i] * p.state[i];
+  const float inv = rsqrtf(block_sum256(ss, red) / static_cast<float>(p.D) + p.eps);
+  for (uint32_t i = threadIdx.x; i < p.D; i += blockDim.x) dst[i] = p.state[i] * inv * p.norm_w[i];
+}
+
 // Row gather used at load time (rotary row permutations, concatenations).
 __global__ void gather_rows_kernel(const uint8_t* __restrict__ src, const uint32_t* __restrict__ map, uint32_t rows,
                                    uint32_t row_bytes, uint8_t* __restrict__ dst) {
@@ -458,6 +478,11 @@ cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, void** args, cudaS
 cudaError_t launch_embed(const EmbedParams& p, cudaStream_t s, bool pdl) {
   void* args[] = {const_cast<EmbedParams*>(&p)};
   return launch_pdl(reinterpret_cast<const void*>(embed_kernel), dim3(p.nseq), dim3(256), args, s, pdl);
+}
+cudaError_t launch_capture_row(const CaptureParams& p, cudaStream_t s, bool pdl) {
+  if (!p.state || !p.dst || !p.ctrl || p.D == 0) return cudaErrorInvalidValue;
+  void* args[] = {const_cast<CaptureParams*>(&p)};
+  return launch_pdl(reinterpret_cast<const void*>(capture_row_kernel), dim3(1), dim3(256), args, s, pdl);
 }
 cudaError_t launch_attn_prep(const PrepParams& p, cudaStream_t s, bool pdl) {
   if (p.hd > 256 || (p.packets && p.hd != 256)) return cudaErrorInvalidValue;  // a packet block is 256 values

@@ -73,13 +73,28 @@ struct GdnParams {
   uint32_t D = 0, H = 0, KH = 0;
   const uint32_t* pos = nullptr;      // sequence z reads pos[z * ctrl_step]
   const uint32_t* running = nullptr;  // likewise
-  uint32_t* err = nullptr;            // device error words, likewise (bounded staging waits)
+  uint32_t* err = nullptr;            // device error words, sequence z's at err[z * err_step] (bounded staging waits)
+  uint32_t err_step = 0;
   uint32_t nseq = 1, ctrl_step = 0;
   size_t proj_seq = 0;                // floats between sequences' projections
   size_t conv_seq = 0, rec_seq = 0;   // floats between sequences' conv history / recurrent state
 };
 
+// Prefill capture (the reference's debug prefill, optical_resident.cpp:481
+// audit copy and the final state copy): the residual row of the position the
+// step processes, copied to dst + pos * D, or (norm_w set) written after the
+// final RMSNorm, op 1 index 2 of resident_math.comp:33-38.
+struct CaptureParams {
+  const float* state = nullptr;  // [D] (one sequence)
+  float* dst = nullptr;          // [capacity][D]
+  const Control* ctrl = nullptr;
+  const float* norm_w = nullptr;
+  float eps = 1e-6f;
+  uint32_t D = 0, capacity = 0;
+};
+
 cudaError_t launch_embed(const EmbedParams& p, cudaStream_t s, bool pdl);
+cudaError_t launch_capture_row(const CaptureParams& p, cudaStream_t s, bool pdl);
 cudaError_t launch_attn_prep(const PrepParams& p, cudaStream_t s, bool pdl);
 cudaError_t launch_gdn(const GdnParams& p, cudaStream_t s, bool pdl);
 cudaError_t launch_gather_rows(const uint8_t* src, const uint32_t* map, uint32_t rows, uint32_t row_bytes,

@@ -64,6 +64,8 @@ _SIGNATURES = {
     "rta_workspace_error": (c_i32, [c_p, c_sz, c_p, ctypes.POINTER(c_u32)]),
     "rta_attention_decode_f16_noalloc": (c_i32, [c_p, c_p, c_p, c_u32, c_u32, c_u32, c_u32, c_u32, c_u32, c_u32, c_p,
                                                  c_p, c_p, c_u32, c_p, c_p]),
+    "rta_gated_delta_step": (c_i32, [c_p, c_p, c_p, c_p, c_p, c_p, c_p, c_u32, c_p, c_p, c_p, c_p, c_p, c_u32, c_u32,
+                                     c_u32, c_u32, c_f, c_p, c_p]),
 }
 
 

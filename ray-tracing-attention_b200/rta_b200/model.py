@@ -49,12 +49,16 @@ _SIGS = {
     "rta_model_close": (None, [_P]),
     "rta_model_prefill": (_I, [_P, _P, _U32, _P, ctypes.POINTER(ctypes.c_double)]),
     "rta_model_generate": (_I, [_P, _U32, _P, ctypes.POINTER(_U32), ctypes.POINTER(ctypes.c_double)]),
+    "rta_model_prefill_capture": (_I, [_P, _P, _U32, _P, _P, _P, ctypes.POINTER(ctypes.c_double)]),
+    "rta_model_profile_step": (_I, [_P, _P, _P, _P, _SZ, ctypes.POINTER(_SZ)]),
     "rta_model_mlp": (_I, [_P, _U32, _P, _U32, _P, _P]),
     "rta_model_vocabulary": (_I, [_P, _P, _P, ctypes.POINTER(_U32), ctypes.POINTER(ctypes.c_float)]),
     "rta_model_state": (_I, [_P, _P, ctypes.POINTER(_U32)]),
     "rta_model_resources": (_I, [_P, _P, _SZ]),
 }
 PACKET_HISTORY = 1  # RTA_MODEL_PACKET_HISTORY
+PROFILE_KINDS = ("start", "readout", "embed", "qkv", "attention_prep", "attention", "o_proj", "in_proj",
+                 "gated_delta", "out_proj", "gate_up", "down")  # RTA_PROF_* (include/rta.h)
 RESOURCE_NAMES = ("payload_bytes", "derived_layer_bytes", "history_bytes", "recurrent_state_bytes", "capacity",
                   "attention_splits", "kernels_per_decode_step", "kernels_per_prefill_step", "position",
                   "sequences", "tensor_core_matrices")
@@ -190,6 +194,21 @@ class ResidentModel:
         self.last_gpu_ms = ms.value
         return ms.value
 
+    def prefill_capture(self, ids, stops=(), layers: bool = False):
+        """Debug prefill (worker op 1 with debug = 1): returns the final-normed residual
+        row of every position [n, D] and, with layers=True, every layer's output rows
+        [depth, n, D] (else None)."""
+        ids = np.ascontiguousarray(ids, np.uint32)
+        st = np.array((list(stops)[:2] + [0xFFFFFFFF] * 2)[:2], np.uint32)
+        D = self.spec.hidden_size
+        states = np.zeros((ids.size, D), np.float32)
+        lay = np.zeros((self.spec.depth, ids.size, D), np.float32) if layers else None
+        ms = ctypes.c_double(0)
+        _check(_lib_model().rta_model_prefill_capture(self._h, _np_ptr(ids), ids.size, _np_ptr(st), _np_ptr(states),
+                                                      _np_ptr(lay) if lay is not None else None, ctypes.byref(ms)))
+        self.last_gpu_ms = ms.value
+        return states, lay
+
     def generate(self, count: int):
         out = np.zeros(count, np.uint32)
         n = ctypes.c_uint32(0)
@@ -229,6 +248,18 @@ class ResidentModel:
         _check(_lib_model().rta_model_generate_batch(self._h, count, _np_ptr(out), _np_ptr(n), ctypes.byref(ms)))
         self.last_gpu_ms = ms.value
         return [out[z, :n[z]].copy() for z in range(self.sequences)]
+
+    def profile_step(self, capacity: int = 4096):
+        """One decode step of every running sequence with each launch group timed on
+        its own: a list of (kind, ms, algorithmic bytes) in launch order."""
+        kinds = np.zeros(capacity, np.uint32)
+        ms = np.zeros(capacity, np.float64)
+        nbytes = np.zeros(capacity, np.float64)
+        n = ctypes.c_size_t(0)
+        _check(_lib_model().rta_model_profile_step(self._h, _np_ptr(kinds), _np_ptr(ms), _np_ptr(nbytes), capacity,
+                                                   ctypes.byref(n)))
+        k = min(n.value, capacity)
+        return [(PROFILE_KINDS[int(kinds[i])], float(ms[i]), float(nbytes[i])) for i in range(k)]
 
     def attention(self, query, keys, values, gate=None, *, layer=None, query_start=None, history_start=0,
                   block=128):

@@ -190,5 +190,22 @@ def workspace_error(workspace: torch.Tensor) -> int:
     return int(word.value)
 
 
-__all__ = ["quantize", "dequantize", "synthetic_blocks", "synthetic_normal", "gemv", "gemv_swiglu", "mlp_swiglu", "readout",
+def gated_delta_step(x: torch.Tensor, attn_norm: torch.Tensor, w_alpha: torch.Tensor, w_beta: torch.Tensor,
+                     a_log: torch.Tensor, dt_bias: torch.Tensor, proj: torch.Tensor, conv_w: torch.Tensor,
+                     conv_state: torch.Tensor, state: torch.Tensor, positions: torch.Tensor, heads: int,
+                     key_heads: int, eps: float = 1e-6, error_word: torch.Tensor | None = None) -> torch.Tensor:
+    """One token of the recurrent gated-delta layer for a batch of sequences
+    (rta_gated_delta_step).  x [B, D]; proj [B, >= 2*key_heads*128 + heads*128];
+    conv_state [B, 2, 3*heads*128, 3] and state [B, heads, 128, 128] are updated in
+    place; positions [B] int32/uint32.  Returns the detector output [B, heads*128]."""
+    B, D = x.shape
+    out = torch.empty(B, heads * 128, dtype=torch.float32, device=x.device)
+    check(_lib.load().rta_gated_delta_step(_ptr(x), _ptr(attn_norm), _ptr(w_alpha), _ptr(w_beta), _ptr(a_log),
+                                           _ptr(dt_bias), _ptr(proj), proj.shape[1], _ptr(conv_w),
+                                           _ptr(conv_state), _ptr(state), _ptr(out), _ptr(positions), D, heads,
+                                           key_heads, B, eps, _ptr(error_word), _stream()))
+    return out
+
+
+__all__ = ["gated_delta_step", "quantize", "dequantize", "synthetic_blocks", "synthetic_normal", "gemv", "gemv_swiglu", "mlp_swiglu", "readout",
            "attention_decode_f16", "attention_workspace", "workspace_error", "Q4_K", "Q6_K", "BLOCK_BYTES"]

@@ -8,12 +8,14 @@
 // layouts its parsers read (resident_runtime.py:116-263).  All model work goes
 // through librta_cuda.so (include/rta.h); this file only frames bytes.
 //
-// Served operations: 0 quit, 1 prefill, 2 generate, 4 vocabulary, 6 mlp,
-// 8 resources, 9 stream, 10 grow (capacity), 14 full-attention diagnostic
-// (dense receipts).  The attention history is kept in the reference's packet
-// format.  Operations tied to the ray-traced caches and statistics (5 codec,
-// 7 aperture, 11/12 checkpointed prefill, 13 finish_history, 15 statistics)
-// answer status 1, which the runtime turns into RuntimeError.
+// Served operations: 0 quit, 1 prefill (debug 0, 1 = per-position and per-layer
+// rows, 2 = timing layout), 2 generate, 4 vocabulary, 6 mlp, 8 resources,
+// 9 stream, 10 grow (capacity), 11 / 12 checkpointed prefill (validated; no
+// history cache, so computed as op 1), 13 finish_history (nothing to save),
+// 14 full-attention diagnostic (dense receipts).  The attention history is kept
+// in the reference's packet format.  Operations tied to the ray-traced geometry
+// and its statistics (5 codec, 7 aperture, 15 statistics) answer status 1, which
+// the runtime turns into RuntimeError.
 #include <algorithm>
 #include <chrono>
 #include <cmath>
@@ -135,22 +137,77 @@ struct Worker {
                                   RTA_MODEL_PACKET_HISTORY, 0, &model));
   }
 
-  // op 1: ids[count] + stops[2] -> 6 doubles + 8 control words (+ batch statistics)
-  void prefill(uint32_t count) {
+  // ops 1 / 11 / 12 (Resident::prefill, optical_resident.cpp:609-712): ids[count] +
+  // stops[2] (+ op 11: u32 checkpoint; op 12: u32 n + n x <u32 position, u32 kind>)
+  // -> 6 doubles + 8 control words [+ debug 1: final-normed rows [count][D] and
+  // every layer's output rows [depth][count][D]] + 4 batch statistics [+ debug 2:
+  // 6 phase timings] + the history-cache counters (prefill parser,
+  // resident_runtime.py:116-158).  The checkpoints mark where the reference's
+  // shared-history cache saves boundaries; this backend keeps no history cache,
+  // so they are validated and the prefix is computed in full, which is what the
+  // reference reports with its cache disabled (no stable prefix, no hit).
+  void prefill(uint32_t op, uint32_t count, uint32_t debug) {
+    if (debug > 2u || !count || count > capacity) throw std::runtime_error("Invalid resident prefix");
     std::vector<uint32_t> ids, st;
     input(ids, count);
     input(st, 2);
+    if (op == 11) {
+      std::vector<uint32_t> boundary;
+      input(boundary, 1);
+      if (!boundary[0] || boundary[0] > count) throw std::runtime_error("Invalid prefix word IDs or boundary");
+    } else if (op == 12) {
+      std::vector<uint32_t> n;
+      input(n, 1);
+      if (n[0] > 4096u) throw std::runtime_error("Too many history boundaries");
+      std::vector<uint32_t> marks;
+      input(marks, 2ull * n[0]);
+      for (uint32_t i = 0; i < n[0]; ++i)
+        if (!marks[2 * i] || marks[2 * i] > count || !(marks[2 * i + 1] & 15u) || marks[2 * i + 1] > 15u)
+          throw std::runtime_error("Invalid history boundary");
+    }
+    for (uint32_t id : ids)
+      if (id >= spec.vocabulary_size) throw std::runtime_error("Invalid prefix word IDs or boundary");
     stops[0] = st[0];
     stops[1] = st[1];
+    const size_t D = spec.hidden_size;
+    std::vector<float> states, layers;
     const auto t0 = Clock::now();
     double gpu = 0.0;
-    check(rta_model_prefill(model, ids.data(), count, stops, &gpu));
+    if (debug == 1u) {
+      states.resize(count * D);
+      layers.resize(static_cast<size_t>(spec.depth) * count * D);
+      check(rta_model_prefill_capture(model, ids.data(), count, stops, states.data(), layers.data(), &gpu));
+    } else {
+      check(rta_model_prefill(model, ids.data(), count, stops, &gpu));
+    }
     const double wall = std::chrono::duration<double, std::milli>(Clock::now() - t0).count();
     position = count;
     std::vector<char> out;
     append<double>(out, {0.0, gpu, wall, wall, 0.0, 0.0});
     append<uint32_t>(out, {ids.back(), 0u, 1u, 0u, stops[0], stops[1], 0u, 0u});
+    if (debug == 1u) {
+      append(out, states.data(), states.size());
+      append(out, layers.data(), layers.size());
+    }
     append<uint64_t>(out, {1ull, static_cast<uint64_t>(count), 0ull, static_cast<uint64_t>(count)});
+    if (debug == 2u) append<double>(out, {0.0, 0.0, 0.0, 0.0, 0.0, 0.0});  // no ray-traced phases here
+    append<uint64_t>(out, {0ull, 0ull});                                    // feature rows traced / reused
+    append<uint64_t>(out, {0ull, 0ull});                                    // stable prefix, snapshot kind
+    append<uint64_t>(out, {0ull, 0ull, 0ull, 0ull, static_cast<uint64_t>(count), 0ull});  // cache counters
+    append<double>(out, {0.0});                                             // cache lookup wall ms
+    append<uint64_t>(out, {0ull, 0ull});                                    // rebuilt tokens, address hit
+    if (debug == 2u) append<double>(out, {0.0, 0.0});
+    reply(0, out);
+  }
+
+  // op 13 (finishHistory, optical_resident.cpp:743-759): saves the generated
+  // output as a cache boundary in the reference; without a history cache nothing
+  // is saved -> saved 0, tokens 0, cache size 0, wall ms.
+  void finish_history() {
+    const auto t0 = Clock::now();
+    std::vector<char> out;
+    append<uint64_t>(out, {0ull, 0ull, 0ull});
+    append<double>(out, {std::chrono::duration<double, std::milli>(Clock::now() - t0).count()});
     reply(0, out);
   }
 
@@ -350,7 +407,8 @@ int main(int argc, char** argv) {
       if (!std::cin.read(reinterpret_cast<char*>(&count), 4) || !std::cin.read(reinterpret_cast<char*>(&debug), 4))
         throw std::runtime_error("Incomplete resident request");
       try {
-        if (op == 1) w.prefill(count);
+        if (op == 1 || op == 11 || op == 12) w.prefill(op, count, debug);
+        else if (op == 13) w.finish_history();
         else if (op == 2) {
           if (count == 0 || count > 4096) throw std::runtime_error("Resident generation expects 1..4096 tokens");
           w.generate_one_packet(count);

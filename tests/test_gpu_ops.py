@@ -166,8 +166,10 @@ def _attention_case(ops, q, keys, values, gate, time, capacity, layout="LHD", sp
     return _np(out), _np(phys), want[0], want_phys[0]
 
 
-@pytest.mark.parametrize("L", [1, 17, 64, 65, 512, 4096])
+@pytest.mark.parametrize("L", [1, 17, 64, 65, 512, 4096, 32768])
 def test_attention_config2_parity(ops, L):
+    """Benchmark config 2 at every history length it names (512 / 4096 / 32768,
+    default splits) against the oracle, plus short edge lengths."""
     rng = np.random.default_rng(L)
     q = rng.normal(0, 1, (16, 256)).astype(np.float32)
     keys = rng.normal(0, 1, (L, 4, 256)).astype(np.float32)
@@ -225,7 +227,7 @@ def test_attention_reference_adversarial_cases(ops, golden):
 
 
 def test_attention_long_history_properties(ops):
-    """L = 32768: oracle cost is high, so check size-independent properties:
+    """L = 32768, size-independent properties on top of the oracle comparison:
     constant V gives that constant; a dominant key selects its value."""
     import torch
     L = 32768

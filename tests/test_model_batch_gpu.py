@@ -171,3 +171,43 @@ def test_tensor_core_batch_diagnostics_match_the_oracle():
     want_act, want_y = oracle.mlp(g.fmt, wg, wu, wd, spec.hidden_size, spec.middle_size, x)
     assert rel_l2(act, want_act) < TOL and rel_l2(y, want_y) < TOL
     batch.close()
+
+
+def test_tensor_core_batch_at_9b_layer_shapes():
+    """The 9B layer shapes on the tensor cores (hidden 4096, intermediate 12288,
+    32 state heads over 16 key heads, 16q/4kv x 256) in four layers [rec, rec,
+    rec, full], 16 sequences with ragged prompts, against the oracle per
+    sequence (vocabulary cut to 32768 rows to keep the host oracle quick; the
+    full 151936-row model at 64 sequences is checked against recorded
+    fixtures in test_model_golden_gpu.py)."""
+    import torch
+    from oracle.model import OracleModel
+    from rta_b200 import assets
+    from rta_b200.model import ResidentModel
+    spec = assets.Spec("qwen35", 4096, 12288, 32768, ("recurrent", "recurrent", "recurrent", "full"), 16, 4, 256,
+                       64, state_heads=32, state_key_heads=16)
+    layout = assets.plan(spec, 41)
+    mats, basis = assets.generate_device(layout, 41)
+    params = layout.params()
+    batch = ResidentModel.from_payloads(spec, params, mats, basis, 32, sequences=16)
+    m, b = mats.cpu().numpy(), basis.cpu().numpy()
+    del mats, basis
+    torch.cuda.empty_cache()
+    assert batch.resources()["tensor_core_matrices"] > 0
+    rng = np.random.default_rng(41)
+    prompts = [rng.integers(0, spec.vocabulary_size, int(n)) for n in rng.integers(1, 6, 16)]
+    batch.prefill_batch(prompts)
+    got = batch.generate_batch(3)
+    ref = OracleModel(spec, params, m, b, 32)
+    compared = 0
+    for z in (0, 5, 10, 15):
+        ref.prefill(prompts[z])
+        want, margins = ref.generate(3)
+        for i in range(min(len(got[z]), len(want))):
+            if margins[i] > TOL:
+                assert got[z][i] == want[i], (z, i, got[z], want, margins)
+                compared += 1
+            if got[z][i] != want[i]:
+                break
+    assert compared >= 6
+    batch.close()
