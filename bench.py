@@ -730,13 +730,17 @@ WORKLOADS = {"mlp": MLPWorkload, "lmhead": LMHeadWorkload, "attention": Attentio
              "mlp_tp": MLPTPWorkload, "lmhead_tp": LMHeadTPWorkload}
 
 
-def ragged_step_bytes(spec, layout, lengths, capacity):
-    """Algorithmic HBM bytes of one ragged-batch step on one rank: weights once,
-    one embedding row per sequence, every visible fp16 K/V position, and the
-    recurrent state read and written."""
+def ragged_step_bytes(spec, layout, lengths, capacity, tp_world: int = 1, all_sequences: int | None = None):
+    """Algorithmic HBM bytes of one ragged-batch step on one rank: weights once
+    (with tensor parallelism: the attention / recurrent projections whole, a
+    1/tp_world share of the MLP and vocabulary rows), one embedding row per
+    sequence it embeds, every visible fp16 K/V position of its sequences, and
+    their recurrent state read and written."""
     seqs = len(lengths)
-    weights = sum(t.nbytes for t in layout.matrices) + layout.basis[1].nbytes
-    emb = seqs * spec.hidden_size * 210 // 256
+    mlp = sum(t.nbytes for t in layout.matrices if ".ffn_" in t.name)
+    other = sum(t.nbytes for t in layout.matrices) - mlp
+    weights = other + (mlp + layout.basis[1].nbytes) / tp_world
+    emb = (all_sequences or seqs) * spec.hidden_size * 210 // 256
     kv = sum(min(int(n) + 1, capacity) for n in lengths) * len(spec.full_layers) * spec.kv_width * 2 * 2
     rec = seqs * len(spec.recurrent_layers) * spec.state_heads * 128 * 128 * 4 * 2
     return weights + emb + kv + rec
@@ -761,8 +765,23 @@ def run_ragged(args, world, rank, local):
     shards = sharding.shard_sequences(lengths, world)
     mine = lengths[shards[rank]]
     capacity = (int(lengths.max()) + 256 + 255) // 256 * 256
-    model = ResidentModel.synthetic(spec, wl.seed, capacity=capacity, device=local, sequences=len(mine))
-    model.seed_history(mine, seed=wl.seed + 1)
+    tp = world > 1 and not args.no_tp
+    team = None
+    if tp:
+        # hybrid: every rank keeps the residual rows of all 64 sequences (its shard
+        # contiguous), runs the attention / recurrent layers of its own shard, and a
+        # 1/world slice of every MLP and of the vocabulary readout for all of them
+        from rta_b200 import tensor_parallel
+        order = np.concatenate([np.asarray(sh, np.int64) for sh in shards])
+        starts = np.concatenate([[0], np.cumsum([len(sh) for sh in shards])]).astype(np.uint32)
+        team = tensor_parallel.Team(capacity_bytes=len(lengths) * spec.hidden_size * 4)
+        model = ResidentModel.synthetic_team(spec, wl.seed, capacity, starts, team, device=local)
+        model.seed_history(lengths[order], seed=wl.seed + 1)
+    else:
+        model = ResidentModel.synthetic(spec, wl.seed, capacity=capacity, device=local, sequences=len(mine))
+        model.seed_history(mine, seed=wl.seed + 1)
+    torch.cuda.synchronize()
+    barrier(world)  # the ranks' step graphs wait for each other (bounded): start them together
     model.generate_batch(args.warmup)
     torch.cuda.synchronize()
     barrier(world)
@@ -783,7 +802,8 @@ def run_ragged(args, world, rank, local):
         model.generate_batch(1)
     e2e_s = max_over_ranks((time.perf_counter() - t0) * 1e3, world) / 1e3 / args.steps
     positions = mine + args.warmup + args.steps * (reps + 1)
-    step_bytes = ragged_step_bytes(spec, model.layout, positions, capacity)
+    step_bytes = ragged_step_bytes(spec, model.layout, positions, capacity, world if tp else 1,
+                                   len(lengths) if tp else None)
     tc = res["tensor_core_matrices"] > 0
     tile = 16 if len(mine) <= 16 else 32 if len(mine) <= 32 else 64
     kernel = (f"tc_gemm_kernel<Q4_K,{tile}> (tcgen05)" if tc else "gemv_tiled_kernel<Q4_K> (batched rows)") + \
@@ -794,6 +814,8 @@ def run_ragged(args, world, rank, local):
     roof.update({"step_algorithmic_bytes_rank": step_bytes, "step_achieved_gbs_rank": step_gbs,
                  "step_frac": step_gbs / pk["hbm_gbs"], "profiled_rank": rank})
     model.close()
+    if team is not None:
+        team.close()
     torch.cuda.empty_cache()
     total = int(lengths.size)
     line = {
@@ -809,11 +831,15 @@ def run_ragged(args, world, rank, local):
                    "state_key_heads": spec.state_key_heads, "sequences": total,
                    "history": "U[128, 8192] seeded", "sequences_per_rank": [len(x) for x in shards],
                    "capacity": capacity, "kv_cache": "fp16",
-                   "parallelism": f"sequence-sharded x{world}, weights replicated" if world > 1 else "single GPU",
+                   "parallelism": (f"hybrid x{world}: attention / recurrent layers sharded by sequence, MLP "
+                                   "(gate/up rows, down columns) and vocabulary rows tensor-parallel, peer-memory "
+                                   "exchanges after every block" if tp else
+                                   f"sequence-sharded x{world}, weights replicated") if world > 1 else "single GPU",
                    "l2": "per-step weight stream 4 GB > L2"},
         "roofline": roof,
-        "e2e": {"value": total / e2e_s, "unit": wl.unit, "h2d_bytes_per_step": 48 * len(mine),
-                "d2h_bytes_per_step": 52 * len(mine),
+        "e2e": {"value": total / e2e_s, "unit": wl.unit,
+                "h2d_bytes_per_step": 48 * (len(lengths) if tp else len(mine)),
+                "d2h_bytes_per_step": 52 * (len(lengths) if tp else len(mine)),
                 "api": "ResidentModel.generate_batch(1) -> rta_model_generate_batch (C-ABI)"},
         "gpu_launches": res["kernels_per_decode_step"] * args.steps,
         "clocks": clk.summary(),
@@ -1197,6 +1223,8 @@ def main():
     ap.add_argument("--min-seconds", type=float, default=1.0,
                     help="repeat the timed K-step region for at least this long (clock sampling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-tp", action="store_true",
+                    help="ragged9b at N > 1: shard by sequence only (weights replicated, no exchanges)")
     ap.add_argument("--no-other-configs", action="store_true",
                     help="ragged9b at N=1: skip the compact lines of benchmark configs 1-4")
     ap.add_argument("--batch", type=int, default=1,

@@ -220,7 +220,7 @@ RTA_API rta_status rta_attention_decode_f16(const float* q, const void* k, const
  * serving loop).  The split records live in a fixed array inside the library's
  * device image (about 1 MiB per GPU that loads the library, held until the
  * process exits) instead of a caller workspace, so heads * splits must not
- * exceed 1024 (RTA_E_ARG otherwise; misaligned k / v or strides are RTA_E_ARG
+ * exceed 1024 (RTA_E_ARG otherwise; k / v not 16-byte aligned are RTA_E_ARG
  * too, before anything is launched).  The call allocates and frees nothing.
  * The first call on a device looks up the array's device address (set-up); make
  * that first call before any stream capture.  The address is kept per device
@@ -333,6 +333,33 @@ RTA_API rta_status rta_model_open_batch(const rta_model_spec* spec, const uint32
                                         const void* matrices, size_t matrix_bytes, const void* basis,
                                         size_t basis_bytes, uint32_t capacity, uint32_t sequences, int device,
                                         rta_model** out);
+/* A handle that decodes `sequences` sequences together with the other ranks of
+ * `team` (one process per GPU, every rank opens its handle with the same
+ * payloads, spec, capacity, sequence count and starts): the tensor-parallel
+ * hybrid of the ragged batch.  Rank r runs the attention and recurrent layers
+ * of sequences [sequence_starts[r], sequence_starts[r + 1]) (their histories
+ * and recurrent states live on its GPU only), and a 1/world slice of every MLP
+ * (gate / up rows and down-projection columns, the middle dimension divided in
+ * units of 256, the first ranks one unit more) and of the vocabulary readout
+ * (rows in units of 128) for all the sequences.  After every attention /
+ * recurrent block the ranks add each other's block outputs to the residual
+ * rows, after every MLP they sum their partial down projections (rank order,
+ * the same bits on every rank), and after the readout they agree on each
+ * sequence's best row: one peer-memory exchange kernel each, recorded in the
+ * handle's step graphs, so every rank keeps identical residual rows and
+ * emits identical tokens.  sequence_starts has world + 1 entries (0 first,
+ * `sequences` last, every rank at least one sequence); the team must be
+ * connected, hold sequences x hidden_size floats per exchange, and serve no
+ * other exchange while the handle is open.  All ranks must make the same calls
+ * (prefill_batch / seed_history / generate_batch) in the same order.  No
+ * reference counterpart: the reference worker runs one sequence on one GPU
+ * (optical_resident.cpp:964-971) with whole matrices per layer
+ * (compiler/export.py:87-91). */
+RTA_API rta_status rta_model_open_team(const rta_model_spec* spec, const uint32_t* params, size_t n_params,
+                                       const void* matrices, size_t matrix_bytes, const void* basis,
+                                       size_t basis_bytes, uint32_t capacity, uint32_t sequences,
+                                       const uint32_t* sequence_starts, rta_team* team, uint32_t flags, int device,
+                                       rta_model** out);
 /* Prefill every sequence: ids[z * stride + i], i < lengths[z] (0 = idle
  * sequence); the sequences advance in lockstep, a shorter prompt sits out the
  * remaining steps. */
@@ -374,7 +401,7 @@ RTA_API rta_status rta_model_generate(rta_model* model, uint32_t count, uint32_t
 enum {
   RTA_PROF_START = 0, RTA_PROF_READOUT = 1, RTA_PROF_EMBED = 2, RTA_PROF_QKV = 3, RTA_PROF_PREP = 4,
   RTA_PROF_ATTENTION = 5, RTA_PROF_O_PROJ = 6, RTA_PROF_IN_PROJ = 7, RTA_PROF_GATED_DELTA = 8,
-  RTA_PROF_OUT_PROJ = 9, RTA_PROF_GATE_UP = 10, RTA_PROF_DOWN = 11
+  RTA_PROF_OUT_PROJ = 9, RTA_PROF_GATE_UP = 10, RTA_PROF_DOWN = 11, RTA_PROF_EXCHANGE = 12
 };
 RTA_API rta_status rta_model_profile_step(rta_model* model, uint32_t* kinds, double* ms, double* bytes,
                                           size_t capacity, size_t* n_groups);

@@ -760,10 +760,10 @@ extern "C" rta_status rta_attention_decode_f16_noalloc(const float* q, const voi
     set_last_error("rta_attention_decode_f16_noalloc: no current CUDA device");
     return RTA_E_CUDA;
   }
-  if (reinterpret_cast<uintptr_t>(k) % 16 || reinterpret_cast<uintptr_t>(v) % 16 || pos_stride % 8 ||
-      kv_stride % 8) {
-    set_last_error("rta_attention_decode_f16_noalloc: k and v must be 16-byte aligned and pos_stride, kv_stride "
-                   "multiples of 8 (rows are copied in 16-byte units)");
+  // strides count head_dim-wide rows, so only the base pointers can break the 16-byte row copies
+  if (reinterpret_cast<uintptr_t>(k) % 16 || reinterpret_cast<uintptr_t>(v) % 16) {
+    set_last_error("rta_attention_decode_f16_noalloc: k and v must be 16-byte aligned (rows are copied in 16-byte "
+                   "units)");
     return RTA_E_ARG;
   }
   float* scratch = nullptr;

@@ -336,9 +336,9 @@ rta_status rta_attention_decode_f16(const float* q, const void* k, const void* v
     return fail(RTA_E_ARG, "rta_attention_decode_f16: head_dim 256, heads == 4*kv_heads, capacity > 0, 1 <= splits <= 1024");
   if (workspace_bytes < rta_attention_workspace_bytes(heads, kv_heads, head_dim, splits))
     return fail(RTA_E_ARG, "rta_attention_decode_f16: workspace too small");
-  if (reinterpret_cast<uintptr_t>(k) % 16 || reinterpret_cast<uintptr_t>(v) % 16 || pos_stride % 8 || kv_stride % 8)
-    return fail(RTA_E_ARG, "rta_attention_decode_f16: k and v must be 16-byte aligned and pos_stride, kv_stride "
-                           "multiples of 8 (rows are copied in 16-byte units)");
+  if (reinterpret_cast<uintptr_t>(k) % 16 || reinterpret_cast<uintptr_t>(v) % 16)
+    return fail(RTA_E_ARG, "rta_attention_decode_f16: k and v must be 16-byte aligned (rows are copied in 16-byte "
+                           "units)");
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   const size_t recs = static_cast<size_t>(heads) * splits;
   rta::AttnParams p;

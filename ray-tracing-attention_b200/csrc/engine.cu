@@ -87,6 +87,7 @@ struct Layer {
   // MLP
   const uint8_t *gate = nullptr, *up = nullptr, *down = nullptr;
   int mlp_fmt = kQ4K, down_fmt = kQ4K;
+  DevBuf<uint8_t> gate_s, up_s, down_s;  // tensor-parallel mode: this rank's slices (own copies)
 };
 
 struct Engine {
@@ -95,6 +96,21 @@ struct Engine {
   cudaStream_t stream = nullptr;
   uint32_t capacity = 0, nsplit = 1;
   uint32_t nseq = 1;   // sequences decoded side by side (one token each per step)
+  // Tensor-parallel hybrid (rta_model_open_team): every rank holds the residual
+  // rows of all nseq sequences, runs the attention / recurrent blocks of its own
+  // sequences [z0, z0 + na) only, and a 1/world slice of every MLP (middle rows
+  // [f0, f0 + fcount)) and of the vocabulary readout (rows [v0, v0 + vcount)) for
+  // all of them; team exchanges after each block keep the residual rows equal
+  // on every rank.  Without a team: z0 = 0, na = nseq, whole matrices.
+  rta_team* team = nullptr;
+  uint32_t z0 = 0, na = 1;
+  uint32_t f0 = 0, fcount = 0, v0 = 0, vcount = 0;
+  uint32_t xblocks = 0;             // blocks of every team exchange (team_blocks)
+  std::vector<uint32_t> row_start;  // [world + 1] first sequence of every rank
+  DevBuf<float> delta, partial;     // block outputs of this rank's rows / MLP partial sums, [nseq][D]
+  DevBuf<uint8_t> lm_slice;         // this rank's vocabulary rows (GGUF order)
+  uint32_t F() const { return team ? fcount : spec.middle_size; }
+  uint32_t VL() const { return team ? vcount : spec.vocabulary_size; }
   uint32_t projw = 0;  // floats of one sequence's projection row
   std::vector<uint32_t> hp;  // host copy of the parameter words
   DevBuf<uint32_t> params;
@@ -146,7 +162,9 @@ struct Engine {
     prof_ev.push_back(e);
     prof_kind.push_back(kind);
     prof_bytes.push_back(bytes);
-    RTA_CUDA(cudaEventRecord(e, s));
+    // External: recorded as an event node of the graph being captured (a plain
+    // record inside a capture only orders the capture's streams)
+    RTA_CUDA(cudaEventRecordWithFlags(e, s, cudaEventRecordExternal));
   }
   // Algorithmic bytes of one product: the packed weights once, x read, y written
   // (read too when accumulated).
@@ -230,11 +248,62 @@ struct Engine {
     RTA_CUDA(cudaStreamSynchronize(stream));
   }
 
+  // Tensor-parallel hybrid: this rank's sequences and slices.  The middle
+  // dimension is divided in units of 256 (one block column of the down
+  // projection) and the vocabulary in units of 128 rows, the first ranks taking
+  // one unit more; every rank derives the same split.
+  static void split_units(uint32_t total, uint32_t unit, uint32_t world, uint32_t rank, uint32_t& start,
+                          uint32_t& count) {
+    const uint32_t units = total / unit, base = units / world, extra = units % world;
+    start = (rank * base + std::min(rank, extra)) * unit;
+    count = (base + (rank < extra ? 1u : 0u)) * unit;
+  }
+  void setup_team(rta_team* tm, const uint32_t* seq_starts) {
+    require(seq_starts != nullptr, "a team handle needs every rank's first sequence", RTA_E_ARG);
+    require(team_ready(tm), "the team is not connected", RTA_E_STATE);
+    const uint32_t world = team_world(tm), rank = team_rank(tm);
+    row_start.assign(seq_starts, seq_starts + world + 1);
+    require(row_start[0] == 0 && row_start[world] == nseq, "sequence starts must run from 0 to the sequence count",
+            RTA_E_ARG);
+    for (uint32_t r = 0; r < world; ++r)
+      require(row_start[r + 1] > row_start[r], "every rank needs at least one sequence", RTA_E_ARG);
+    require(spec.middle_size % 256 == 0 && spec.middle_size / 256 >= world && spec.vocabulary_size % 128 == 0 &&
+                spec.vocabulary_size / 128 >= world,
+            "middle size (units of 256) and vocabulary (units of 128) must cover every rank", RTA_E_ARG);
+    require(team_capacity_words(tm) >= static_cast<size_t>(nseq) * spec.hidden_size &&
+                team_capacity_words(tm) >= 2ull * nseq,
+            "the team's exchange capacity must hold sequences x hidden floats", RTA_E_ARG);
+    team = tm;
+    z0 = row_start[rank];
+    na = row_start[rank + 1] - row_start[rank];
+    split_units(spec.middle_size, 256u, world, rank, f0, fcount);
+    split_units(spec.vocabulary_size, 128u, world, rank, v0, vcount);
+  }
+  // Copies of this rank's gate / up rows and down-projection columns.
+  void slice_mlp(Layer& L) {
+    const uint32_t D = this->D(), Ff = spec.middle_size;
+    const size_t rg = static_cast<size_t>(D) / 256 * block_bytes(L.mlp_fmt);
+    L.gate_s.alloc(static_cast<size_t>(fcount) * rg);
+    L.up_s.alloc(static_cast<size_t>(fcount) * rg);
+    RTA_CUDA(cudaMemcpyAsync(L.gate_s.p, L.gate + static_cast<size_t>(f0) * rg, L.gate_s.n, cudaMemcpyDeviceToDevice,
+                             stream));
+    RTA_CUDA(cudaMemcpyAsync(L.up_s.p, L.up + static_cast<size_t>(f0) * rg, L.up_s.n, cudaMemcpyDeviceToDevice,
+                             stream));
+    const size_t bb = block_bytes(L.down_fmt), row = static_cast<size_t>(Ff) / 256 * bb;
+    const size_t width = static_cast<size_t>(fcount) / 256 * bb;
+    L.down_s.alloc(static_cast<size_t>(D) * width);
+    RTA_CUDA(cudaMemcpy2DAsync(L.down_s.p, width, L.down + static_cast<size_t>(f0) / 256 * bb, row, width, D,
+                               cudaMemcpyDeviceToDevice, stream));
+    L.gate = L.gate_s.p;
+    L.up = L.up_s.p;
+    L.down = L.down_s.p;
+  }
+
   // Re-lay every GEMV matrix once into the tiled order (same bytes; see
   // launch_tile_weights): layer matrices in place through a scratch buffer,
   // the LM head into its own buffer.  Fails on projections sharing bytes.
   void tile_matrices() {
-    const uint32_t D = this->D(), F = spec.middle_size;
+    const uint32_t D = this->D(), F = this->F();
     struct Job {
       uint8_t* p;
       int fmt;           // packed format of the payload (Q4_K / Q6_K)
@@ -284,28 +353,37 @@ struct Engine {
       if (j.tiled_field) *j.tiled_field = j.fmt + (panel_ok(j.rows) ? kPanelOffset : kTiledOffset);
       panel_matrices += panel_ok(j.rows) ? 1u : 0u;
     }
-    const size_t lm_bytes = static_cast<size_t>(spec.vocabulary_size) * (D / 256) * block_bytes(lm_fmt);
+    const size_t lm_bytes = static_cast<size_t>(VL()) * (D / 256) * block_bytes(lm_fmt);
     lm_tiled.alloc(lm_bytes);
-    if (panel_ok(spec.vocabulary_size)) {
-      RTA_CUDA(launch_tile_tc(lm_fmt, lm, spec.vocabulary_size, D, lm_tiled.p, stream));
+    if (panel_ok(VL())) {
+      RTA_CUDA(launch_tile_tc(lm_fmt, lm, VL(), D, lm_tiled.p, stream));
       lm_fmt += kPanelOffset;
       ++panel_matrices;
     } else {
-      RTA_CUDA(launch_tile_weights(lm_fmt, lm, spec.vocabulary_size, D, lm_tiled.p, stream));
+      RTA_CUDA(launch_tile_weights(lm_fmt, lm, VL(), D, lm_tiled.p, stream));
       lm_fmt += kTiledOffset;
+    }
+    if (lm_slice.p) {  // the tiled copy replaces this rank's GGUF-order rows
+      RTA_CUDA(cudaStreamSynchronize(stream));
+      cudaFree(lm_slice.p);
+      lm_slice.p = nullptr;
+      lm_slice.n = 0;
     }
     lm = lm_tiled.p;
     RTA_CUDA(cudaStreamSynchronize(stream));
   }
 
   void load(const rta_model_spec& sp, const uint32_t* prm, size_t n_params, const void* mat, size_t matrix_bytes,
-            const void* bas, size_t basis_bytes, uint32_t cap, uint32_t sequences, uint32_t flags, int dev) {
+            const void* bas, size_t basis_bytes, uint32_t cap, uint32_t sequences, uint32_t flags, int dev,
+            rta_team* tm = nullptr, const uint32_t* seq_starts = nullptr) {
     spec = sp;
     device = dev;
     require((flags & ~static_cast<uint32_t>(RTA_MODEL_PACKET_HISTORY)) == 0, "unknown model flags", RTA_E_ARG);
     packet_history = (flags & RTA_MODEL_PACKET_HISTORY) != 0;
     require(sequences >= 1 && sequences <= 256, "sequences must be 1..256", RTA_E_ARG);
     nseq = sequences;
+    na = nseq;
+    if (tm) setup_team(tm, seq_starts);
     require(spec.depth >= 1 && spec.depth <= 256, "depth must be 1..256", RTA_E_ARG);
     require(spec.hidden_size % 256 == 0 && spec.middle_size % 256 == 0, "hidden/middle must be multiples of 256",
             RTA_E_ARG);
@@ -423,7 +501,15 @@ struct Engine {
       L->down = dd.ptr;
       L->mlp_fmt = dg.fmt;
       L->down_fmt = dd.fmt;
+      if (team) slice_mlp(*L);
       layers.push_back(std::move(L));
+    }
+    if (team) {  // this rank's vocabulary rows, a contiguous run of the GGUF rows
+      const size_t rb = static_cast<size_t>(D) / 256 * block_bytes(lm_fmt);
+      lm_slice.alloc(static_cast<size_t>(vcount) * rb);
+      RTA_CUDA(cudaMemcpyAsync(lm_slice.p, lm + static_cast<size_t>(v0) * rb, lm_slice.n, cudaMemcpyDeviceToDevice,
+                               stream));
+      lm = lm_slice.p;
     }
     RTA_CUDA(cudaStreamSynchronize(stream));
     tc = nseq >= kTcMinSeq;
@@ -433,18 +519,25 @@ struct Engine {
     projw = std::max(Q() + 2 * KVW() + Q(), 2 * K() + 2 * S());
     projw = (projw + 3u) / 4u * 4u;  // 16-byte aligned rows
     state.alloc(static_cast<size_t>(nseq) * D);
-    proj.alloc(static_cast<size_t>(nseq) * projw);
-    qproc.alloc(static_cast<size_t>(nseq) * Q());
-    att.alloc(static_cast<size_t>(nseq) * Q());
-    gdn.alloc(static_cast<size_t>(nseq) * std::max(1u, S()));
-    act.alloc(static_cast<size_t>(nseq) * spec.middle_size);
+    proj.alloc(static_cast<size_t>(na) * projw);
+    qproc.alloc(static_cast<size_t>(na) * Q());
+    att.alloc(static_cast<size_t>(na) * Q());
+    gdn.alloc(static_cast<size_t>(na) * std::max(1u, S()));
+    act.alloc(static_cast<size_t>(nseq) * F());
+    if (team) {
+      delta.alloc(static_cast<size_t>(nseq) * D);
+      partial.alloc(static_cast<size_t>(nseq) * D);
+      delta.zero(stream);
+      partial.zero(stream);
+      xblocks = team_blocks(static_cast<size_t>(nseq) * D);
+    }
     scratch_x.alloc(32ull * std::max(D, spec.middle_size));
     scratch_y.alloc(32ull * std::max(D, spec.middle_size));
     if (tc) {  // raw gate | up rows and the tensor-core activation stages (largest K, largest batch)
       const uint32_t rows = std::max(nseq, 32u);
-      gu.alloc(static_cast<size_t>(rows) * 2 * spec.middle_size);
+      gu.alloc(static_cast<size_t>(rows) * 2 * F());
       size_t ws = 0;
-      for (uint32_t cols : {D, Q(), std::max(1u, S()), spec.middle_size})
+      for (uint32_t cols : {D, Q(), std::max(1u, S()), F()})
         if (cols % 256 == 0) ws = std::max({ws, tc_workspace_bytes(kQ4KPanel, rows, cols), tc_workspace_bytes(kQ6KPanel, rows, cols)});
       tc_ws.alloc(ws);
     }
@@ -461,30 +554,30 @@ struct Engine {
     // covers up to ~2048 positions whatever the history (config 5: 4 splits for
     // the longest histories, 1 for the shortest; measured against 512 / 1024 /
     // 1536 positions per split and against a uniform split count).
-    const uint32_t fill = (8u * static_cast<uint32_t>(sms) + spec.kv_heads * nseq - 1u) / (spec.kv_heads * nseq);
+    const uint32_t fill = (8u * static_cast<uint32_t>(sms) + spec.kv_heads * na - 1u) / (spec.kv_heads * na);
     // Below that regime both split kernels round a split up to a multiple of 64
     // positions.  One sequence, and packet history (every K/V value decoded on
     // the CUDA cores), get up to capacity / 64 splits, so a decode-length history
     // gives each CTA about 64 positions; a few fp16 sequences keep capacity / 256.
-    const uint32_t per_split = packet_history || nseq == 1 ? 64u : 256u;
+    const uint32_t per_split = packet_history || na == 1 ? 64u : 256u;
     nsplit = nseq >= kTcMinSeq ? std::max(1u, std::min(static_cast<uint32_t>(sms) / spec.kv_heads, capacity / 2048u))
                        : std::max(1u, std::min({static_cast<uint32_t>(sms) / spec.kv_heads, capacity / per_split, fill}));
-    const size_t recs = static_cast<size_t>(nseq) * spec.kv_heads * nsplit * 4;
+    const size_t recs = static_cast<size_t>(na) * spec.kv_heads * nsplit * 4;
     part_m.alloc(recs);
     part_z.alloc(recs);
     part_o.alloc(recs * hd);
     // [layer][sequence] x per-sequence blocks
     pbytes = packet_bytes(spec.kv_heads);
     if (packet_history) {
-      pring.alloc(static_cast<size_t>(std::max(1u, n_full)) * nseq * capacity * pbytes);
+      pring.alloc(static_cast<size_t>(std::max(1u, n_full)) * na * capacity * pbytes);
       kcache.alloc(1);
       vcache.alloc(1);
     } else {
-      kcache.alloc(static_cast<size_t>(std::max(1u, n_full)) * nseq * spec.kv_heads * capacity * hd);
+      kcache.alloc(static_cast<size_t>(std::max(1u, n_full)) * na * spec.kv_heads * capacity * hd);
       vcache.alloc(kcache.n);
     }
-    rec.alloc(static_cast<size_t>(std::max(1u, n_rec)) * nseq * spec.state_heads * 128 * 128);
-    conv.alloc(static_cast<size_t>(std::max(1u, n_rec)) * nseq * 2 * 3 * S() * 3);
+    rec.alloc(static_cast<size_t>(std::max(1u, n_rec)) * na * spec.state_heads * 128 * 128);
+    conv.alloc(static_cast<size_t>(std::max(1u, n_rec)) * na * 2 * 3 * S() * 3);
     ctrl.alloc(nseq);
     prompt.alloc(static_cast<size_t>(nseq) * capacity);
     positions.assign(nseq, 0u);
@@ -575,13 +668,26 @@ struct Engine {
     mark(RTA_PROF_DOWN, product_bytes(dn), s);
   }
 
+  // Team mode: every rank's attention / recurrent block outputs (its own rows of
+  // delta) are added to the residual rows on every rank; returns launches made.
+  uint32_t gather_block_outputs(cudaStream_t s) {
+    if (!team) return 0;
+    RTA_CUDA(team_gather_add(team, delta.p, state.p, D(), row_start.data(), xblocks, s));
+    mark(RTA_PROF_EXCHANGE, 4.0 * nseq * D(), s);
+    return 1;
+  }
+
   // ---------------------------------------------------------- step recording
   uint32_t record_step(bool decode, bool capture_rows = false) {
     const cudaStream_t s = stream;
     uint32_t n = 0;
     Control* c = ctrl.p;
     const uint32_t* running = &c->running;
-    const uint32_t D = this->D(), F = spec.middle_size, hd = spec.attention_head_dim;
+    // this rank's sequences (all of them without a team): attention / recurrent blocks
+    Control* cl = c + z0;
+    const uint32_t* running_l = &cl->running;
+    float* state_l = state.p + static_cast<size_t>(z0) * this->D();
+    const uint32_t D = this->D(), F = this->F(), hd = spec.attention_head_dim;
     const uint32_t cstep = static_cast<uint32_t>(sizeof(Control) / 4);  // u32 between sequences' control words
     static_assert(sizeof(Control) % 8 == 0, "control blocks must keep 8-byte alignment");
     mark(RTA_PROF_START, 0.0, s);
@@ -589,7 +695,7 @@ struct Engine {
       GemvArgs r;
       r.fmt = lm_fmt;
       r.w0 = lm;
-      r.rows = spec.vocabulary_size;
+      r.rows = VL();
       r.cols = D;
       r.x = state.p;
       r.prologue = kRmsNorm;
@@ -606,6 +712,11 @@ struct Engine {
       RTA_CUDA(matmul(r, s));
       mark(RTA_PROF_READOUT, product_bytes(r) - 4.0 * r.batch * r.rows, s);  // logits are not stored
       ++n;
+      if (team) {  // the best row of every rank's vocabulary slice -> the global best, in the control blocks
+        RTA_CUDA(team_allmax_keys(team, &c->argkey, nseq, static_cast<uint32_t>(sizeof(Control) / 8), v0, xblocks, s));
+        mark(RTA_PROF_EXCHANGE, static_cast<double>(nseq) * 8.0 * team_world(team), s);
+        ++n;
+      }
     }
     EmbedParams e;
     e.table = embed;
@@ -630,17 +741,17 @@ struct Engine {
         g.w0 = L.qkvg.p;
         g.rows = L.qkvg_rows;
         g.cols = D;
-        g.x = state.p;
+        g.x = state_l;
         g.prologue = kRmsNorm;
         g.norm_w = L.attn_norm;
         g.eps = spec.norm_epsilon;
         g.y = proj.p;
-        g.batch = nseq;
+        g.batch = na;
         g.x_stride = D;
         g.y_stride = projw;
-        g.running = running;
+        g.running = running_l;
         g.running_step = cstep;
-        g.err = &c->err;
+        g.err = &cl->err;
         g.pdl = true;
         RTA_CUDA(matmul(g, s));
         mark(RTA_PROF_QKV, product_bytes(g), s);
@@ -660,20 +771,20 @@ struct Engine {
         pp.kv_width = KVW();
         pp.qout = qproc.p;
         const size_t seq_kv = static_cast<size_t>(spec.kv_heads) * capacity * hd;
-        const size_t layer_kv = seq_kv * nseq;
+        const size_t layer_kv = seq_kv * na;
         pp.kcache = kcache.p + L.fi * layer_kv;
         pp.vcache = vcache.p + L.fi * layer_kv;
         pp.capacity = capacity;
-        pp.pos = &c->pos_cur;
-        pp.running = running;
-        pp.nseq = nseq;
+        pp.pos = &cl->pos_cur;
+        pp.running = running_l;
+        pp.nseq = na;
         pp.ctrl_step = cstep;
         pp.qkvg_seq = projw;
-        const size_t layer_pkt = static_cast<size_t>(nseq) * capacity * pbytes;
+        const size_t layer_pkt = static_cast<size_t>(na) * capacity * pbytes;
         if (packet_history) pp.packets = pring.p + L.fi * layer_pkt;
         RTA_CUDA(launch_attn_prep(pp, s, true));
-        mark(RTA_PROF_PREP, static_cast<double>(nseq) * 4.0 * (L.qkvg_rows + Q()) +
-                                static_cast<double>(nseq) * (packet_history ? pbytes : 4.0 * KVW()), s);
+        mark(RTA_PROF_PREP, static_cast<double>(na) * 4.0 * (L.qkvg_rows + Q()) +
+                                static_cast<double>(na) * (packet_history ? pbytes : 4.0 * KVW()), s);
         AttnParams ap;
         ap.q = qproc.p;
         ap.k = pp.kcache;
@@ -691,7 +802,7 @@ struct Engine {
         ap.kvh = spec.kv_heads;
         ap.hd = hd;
         ap.capacity = capacity;
-        ap.pos = &c->pos_cur;
+        ap.pos = &cl->pos_cur;
         ap.ctrl_step = cstep;
         ap.gate = L.gated ? proj.p + Q() + 2 * KVW() : nullptr;
         ap.gate_seq_stride = projw;
@@ -701,10 +812,10 @@ struct Engine {
         ap.part_m = part_m.p;
         ap.part_z = part_z.p;
         ap.part_o = part_o.p;
-        ap.err = &c->err;
-        ap.running = running;
+        ap.err = &cl->err;
+        ap.running = running_l;
         ap.split_by_length = nseq >= kTcMinSeq ? 1u : 0u;
-        RTA_CUDA(launch_attention(ap, nsplit, nseq, true, s));
+        RTA_CUDA(launch_attention(ap, nsplit, na, true, s));
         mark(RTA_PROF_ATTENTION, attention_bytes(), s);
         GemvArgs o;
         o.fmt = L.o_fmt;
@@ -712,40 +823,41 @@ struct Engine {
         o.rows = D;
         o.cols = Q();
         o.x = att.p;
-        o.epilogue = kAccumulate;
-        o.y = state.p;
-        o.batch = nseq;
+        o.epilogue = team ? kStore : kAccumulate;
+        o.y = team ? delta.p + static_cast<size_t>(z0) * D : state.p;
+        o.batch = na;
         o.x_stride = Q();
         o.y_stride = D;
-        o.running = running;
+        o.running = running_l;
         o.running_step = cstep;
-        o.err = &c->err;
+        o.err = &cl->err;
         o.pdl = true;
         RTA_CUDA(matmul(o, s));
         mark(RTA_PROF_O_PROJ, product_bytes(o), s);
         n += 5;
+        n += gather_block_outputs(s);
       } else {
         GemvArgs g;
         g.fmt = L.inproj_fmt;
         g.w0 = L.inproj.p;
         g.rows = L.inproj_rows;
         g.cols = D;
-        g.x = state.p;
+        g.x = state_l;
         g.prologue = kRmsNorm;
         g.norm_w = L.attn_norm;
         g.eps = spec.norm_epsilon;
         g.y = proj.p;
-        g.batch = nseq;
+        g.batch = na;
         g.x_stride = D;
         g.y_stride = projw;
-        g.running = running;
+        g.running = running_l;
         g.running_step = cstep;
-        g.err = &c->err;
+        g.err = &cl->err;
         g.pdl = true;
         RTA_CUDA(matmul(g, s));
         mark(RTA_PROF_IN_PROJ, product_bytes(g), s);
         GdnParams gp;
-        gp.x = state.p;
+        gp.x = state_l;
         gp.attn_norm = L.gate_w.p + 2ull * spec.state_heads * D;  // aligned copy of L.attn_norm
         gp.eps = spec.norm_epsilon;
         gp.wa = L.wa;
@@ -756,19 +868,19 @@ struct Engine {
         gp.conv_w = L.conv_w;
         gp.conv_seq = static_cast<size_t>(2) * 3 * S() * 3;
         gp.rec_seq = static_cast<size_t>(spec.state_heads) * 128 * 128;
-        gp.conv_state = conv.p + static_cast<size_t>(L.ri) * nseq * gp.conv_seq;
-        gp.rec = rec.p + static_cast<size_t>(L.ri) * nseq * gp.rec_seq;
+        gp.conv_state = conv.p + static_cast<size_t>(L.ri) * na * gp.conv_seq;
+        gp.rec = rec.p + static_cast<size_t>(L.ri) * na * gp.rec_seq;
         gp.proj_seq = projw;
-        gp.nseq = nseq;
+        gp.nseq = na;
         gp.ctrl_step = cstep;
         gp.out = gdn.p;
         gp.D = D;
         gp.H = spec.state_heads;
         gp.KH = spec.state_key_heads;
-        gp.pos = &c->pos_cur;
-        gp.err = &c->err;
+        gp.pos = &cl->pos_cur;
+        gp.err = &cl->err;
         gp.err_step = cstep;
-        gp.running = running;
+        gp.running = running_l;
         RTA_CUDA(launch_gdn(gp, s, true));
         mark(RTA_PROF_GATED_DELTA, static_cast<double>(running_sequences()) *
                                        (8.0 * spec.state_heads * 128 * 128 + 4.0 * (2 * K() + 2 * S() + 2 * D)), s);
@@ -779,22 +891,23 @@ struct Engine {
         o.cols = S();
         o.x = gdn.p;
         o.x_stride = S();
-        o.batch = nseq;
+        o.batch = na;
         o.prologue = kHeadGate;
         o.z = proj.p + 2 * K() + S();
         o.z_stride = projw;
         o.norm_w = L.ssm_norm;
         o.eps = spec.norm_epsilon;
-        o.epilogue = kAccumulate;
-        o.y = state.p;
+        o.epilogue = team ? kStore : kAccumulate;
+        o.y = team ? delta.p + static_cast<size_t>(z0) * D : state.p;
         o.y_stride = D;
-        o.running = running;
+        o.running = running_l;
         o.running_step = cstep;
-        o.err = &c->err;
+        o.err = &cl->err;
         o.pdl = true;
         RTA_CUDA(matmul(o, s));
         mark(RTA_PROF_OUT_PROJ, product_bytes(o), s);
         n += 3;
+        n += gather_block_outputs(s);
       }
       GemvArgs gu;
       gu.fmt = L.mlp_fmt;
@@ -821,8 +934,8 @@ struct Engine {
       dn.rows = D;
       dn.cols = F;
       dn.x = act.p;
-      dn.epilogue = kAccumulate;
-      dn.y = state.p;
+      dn.epilogue = team ? kStore : kAccumulate;
+      dn.y = team ? partial.p : state.p;
       dn.batch = nseq;
       dn.x_stride = F;
       dn.y_stride = D;
@@ -832,6 +945,11 @@ struct Engine {
       dn.pdl = true;
       mlp_pair(gu, dn, false, s);
       n += 2;
+      if (team) {  // residual + the partial down projections of every rank, in rank order
+        RTA_CUDA(team_allreduce(team, partial.p, state.p, state.p, static_cast<size_t>(nseq) * D, xblocks, s));
+        mark(RTA_PROF_EXCHANGE, 4.0 * nseq * D * team_world(team), s);
+        ++n;
+      }
       if (capture_rows) {
         CaptureParams cp;
         cp.state = state.p;
@@ -900,7 +1018,7 @@ struct Engine {
   // Sequences that take part in the next step (host mirror of the positions).
   uint32_t running_sequences() const {
     uint32_t r = 0;
-    for (uint32_t z = 0; z < nseq; ++z) r += positions[z] > 0 ? 1u : 0u;
+    for (uint32_t z = z0; z < z0 + na; ++z) r += positions[z] > 0 ? 1u : 0u;
     return r;
   }
   // Algorithmic bytes of one full layer's attention in the next step: every
@@ -909,7 +1027,7 @@ struct Engine {
   double attention_bytes() const {
     const double per_pos = packet_history ? static_cast<double>(pbytes) : 4.0 * KVW();
     double b = 0.0;
-    for (uint32_t z = 0; z < nseq; ++z)
+    for (uint32_t z = z0; z < z0 + na; ++z)
       if (positions[z] > 0) b += per_pos * std::min(positions[z] + 1u, capacity) + 12.0 * Q();
     return b;
   }
@@ -974,6 +1092,11 @@ struct Engine {
       positions[z] = ctrl_host[z].pos_next;
     }
     position = positions[0];
+    if (team) {  // the exchanges' own error word (a peer that never arrived)
+      uint32_t terr = 0;
+      RTA_CUDA(cudaMemcpy(&terr, team_error_word(team), 4, cudaMemcpyDeviceToHost));
+      err |= terr;
+    }
     if (err & RTA_DEVERR_TIMEOUT) throw Failure{RTA_E_TIMEOUT, "device-side wait exceeded its bound"};
     if (err) throw Failure{RTA_E_DEVICE_CHECK, "device error word " + std::to_string(err)};
   }
@@ -1022,7 +1145,7 @@ struct Engine {
   // final-normed row of every position (states [n][D]) and, when layers is not
   // NULL, every layer's output row ([depth][n][D]).
   void prefill_capture(const uint32_t* ids, uint32_t n, const uint32_t st[2], float* states, float* layer_rows) {
-    require(nseq == 1, "debug prefill serves single-sequence handles", RTA_E_STATE);
+    require(nseq == 1 && !team, "debug prefill serves single-sequence handles", RTA_E_STATE);
     require(n >= 1 && n <= capacity, "prefill length must be 1..capacity", RTA_E_ARG);
     require(states != nullptr, "debug prefill needs the state rows", RTA_E_ARG);
     const size_t rows = static_cast<size_t>(capacity) * D();
@@ -1123,6 +1246,7 @@ struct Engine {
                        float* out, float* phys, uint8_t* packets_out, uint32_t* receipts, uint32_t* n_records,
                        double* timing) {
     const uint32_t H = spec.attention_heads, KVH = spec.kv_heads, hd = spec.attention_head_dim;
+    require(!team, "diagnostics are served by single-GPU handles", RTA_E_STATE);
     require(layer < spec.depth && layers[layer]->full, "attention diagnostic needs a full-attention layer", RTA_E_ARG);
     require(rows >= 1 && rows <= 32 && count >= 1 && count <= capacity, "attention rows 1..32, count 1..capacity",
             RTA_E_ARG);
@@ -1251,7 +1375,7 @@ struct Engine {
   // o-projection axis order) and that layer's visible history packets, oldest
   // first: what a test needs to recompute the layer's attention independently.
   uint32_t debug_attention(uint32_t z, float* q, float* gate, float* att, uint8_t* packets) {
-    require(packet_history, "needs a packet-history handle", RTA_E_STATE);
+    require(packet_history && !team, "needs a single-GPU packet-history handle", RTA_E_STATE);
     require(z < nseq && positions[z] > 0, "sequence has no history", RTA_E_ARG);
     uint32_t fi = 0;
     bool any = false;
@@ -1277,6 +1401,7 @@ struct Engine {
   }
 
   void mlp(uint32_t layer, const float* x, uint32_t rows, float* y, float* a) {
+    require(!team, "diagnostics are served by single-GPU handles", RTA_E_STATE);
     require(layer < spec.depth, "layer out of range", RTA_E_ARG);
     require(rows >= 1 && rows <= 32, "MLP check supports 1..32 rows", RTA_E_ARG);
     const uint32_t D = this->D(), F = spec.middle_size;
@@ -1349,6 +1474,7 @@ struct Engine {
   }
 
   void vocabulary(const float* hidden, float* logits, uint32_t* argmax, float* best) {
+    require(!team, "diagnostics are served by single-GPU handles", RTA_E_STATE);
     const uint32_t D = this->D(), V = spec.vocabulary_size;
     for (uint32_t i = 0; i < D; ++i) require(std::isfinite(hidden[i]), "vocabulary input must be finite", RTA_E_ARG);
     RTA_CUDA(cudaMemcpyAsync(scratch_x.p, hidden, D * 4ull, cudaMemcpyHostToDevice, stream));
@@ -1418,6 +1544,28 @@ rta_status rta_model_open_ex(const rta_model_spec* spec, const uint32_t* params,
   try {
     m->engine.load(*spec, params, n_params, matrices, matrix_bytes, basis, basis_bytes, capacity, sequences, flags,
                    device);
+  } catch (const rta::Failure& f) {
+    delete m;
+    return rta::fail_model(f);
+  }
+  *out = m;
+  return RTA_OK;
+}
+
+rta_status rta_model_open_team(const rta_model_spec* spec, const uint32_t* params, size_t n_params,
+                               const void* matrices, size_t matrix_bytes, const void* basis, size_t basis_bytes,
+                               uint32_t capacity, uint32_t sequences, const uint32_t* sequence_starts,
+                               rta_team* team, uint32_t flags, int device, rta_model** out) {
+  if (!spec || !params || !matrices || !basis || !out || !team || !sequence_starts) {
+    rta::g_model_error = "rta_model_open_team: null argument";
+    return RTA_E_ARG;
+  }
+  *out = nullptr;
+  auto* m = new (std::nothrow) rta_model;
+  if (!m) return RTA_E_CUDA;
+  try {
+    m->engine.load(*spec, params, n_params, matrices, matrix_bytes, basis, basis_bytes, capacity, sequences, flags,
+                   device, team, sequence_starts);
   } catch (const rta::Failure& f) {
     delete m;
     return rta::fail_model(f);

@@ -10,6 +10,8 @@
 
 #include "rta_device.cuh"
 
+struct rta_team;  // team.cu (include/rta.h: typedef struct rta_team rta_team)
+
 namespace rta {
 
 constexpr int kF32 = 0, kF16 = 1, kBF16 = 30, kQ4K = 12, kQ6K = 14;  // export.py FORMATS codes
@@ -124,5 +126,27 @@ cudaError_t launch_tile_tc(int fmt, const uint8_t* src, uint32_t rows, uint32_t 
 // Dense F32 GEMV for the tiny recurrent alpha/beta projections.
 cudaError_t launch_gemv_f32(const float* W, uint32_t rows, uint32_t cols, const float* x, uint32_t x_stride,
                             uint32_t batch, float* y, uint32_t y_stride, cudaStream_t s);
+
+// ----------------------------------------------------------------- team.cu
+// The decode engine's tensor-parallel mode drives the team exchanges from its
+// own graphs (every rank records the same exchanges in the same order).
+uint32_t team_rank(const rta_team* t);
+uint32_t team_world(const rta_team* t);
+bool team_ready(const rta_team* t);
+size_t team_capacity_words(const rta_team* t);
+uint32_t* team_error_word(rta_team* t);
+// Every exchange a handle records uses team_blocks(largest exchange in words)
+// blocks, which keeps the slot parity of each call the same in every block.
+uint32_t team_blocks(size_t words);
+// out = addend + sum over ranks of partial (rank order; same bits everywhere)
+cudaError_t team_allreduce(rta_team* t, const float* partial, const float* addend, float* out, size_t n,
+                           uint32_t blocks, cudaStream_t s);
+// state rows of every rank r, [row_start[r], row_start[r + 1]) x width, += that
+// rank's delta rows (row_start has world + 1 entries)
+cudaError_t team_gather_add(rta_team* t, const float* delta, float* state, uint32_t width,
+                            const uint32_t* row_start, uint32_t blocks, cudaStream_t s);
+// packed argmax keys (local ids from id_base) -> the largest over the ranks, in place
+cudaError_t team_allmax_keys(rta_team* t, unsigned long long* keys, uint32_t n, uint32_t stride, uint32_t id_base,
+                             uint32_t blocks, cudaStream_t s);
 
 }  // namespace rta

@@ -166,6 +166,81 @@ __global__ void __launch_bounds__(kThreads) argmax_kernel(View v, const uint32_t
   end_call(v, 0, e);
 }
 
+// state[i] += delta_s[i] for the rows of every source s: each rank owns the
+// rows [row_start[rank], row_start[rank + 1]) of a [rows][width] float matrix
+// and contributes only those (its attention / recurrent block outputs); the
+// rows of different ranks are disjoint, so every element of state receives
+// exactly one addend and every rank ends with the same bits.  Block b handles
+// chunk b of every source's rows.  Pushes 1/world of the one-shot allreduce's
+// bytes.
+__global__ void __launch_bounds__(kThreads) gather_add_kernel(View v, const float* __restrict__ delta, float* state,
+                                                              uint32_t width, uint32_t start0, uint32_t start1,
+                                                              uint32_t start2, uint32_t start3, uint32_t start4,
+                                                              uint32_t start5, uint32_t start6, uint32_t start7,
+                                                              uint32_t start8) {
+  const uint32_t starts[kMaxRanks + 1] = {start0, start1, start2, start3, start4, start5, start6, start7, start8};
+  const uint32_t b = blockIdx.x, nb = gridDim.x;
+  const uint32_t e = begin_call(v, b);
+  const uint32_t par = e & 1u;
+  auto chunk = [&](uint32_t s, uint32_t& q0, uint32_t& q1) {  // float4 range of source s handled by block b
+    const uint32_t lo = starts[s] * width / 4u, hi = starts[s + 1] * width / 4u, n = hi - lo;
+    q0 = lo + static_cast<uint32_t>(static_cast<uint64_t>(n) * b / nb);
+    q1 = lo + static_cast<uint32_t>(static_cast<uint64_t>(n) * (b + 1) / nb);
+  };
+  uint32_t q0, q1;
+  chunk(v.rank, q0, q1);
+  for (uint32_t i = q0 + threadIdx.x; i < q1; i += blockDim.x) {
+    const float4 val = reinterpret_cast<const float4*>(delta)[i];
+    for (uint32_t p = 0; p < v.world; ++p) reinterpret_cast<float4*>(slot_at(v, p, par, v.rank))[i] = val;
+  }
+  publish(v, b, e);
+  if (await_all(v, b, e)) {
+    for (uint32_t s = 0; s < v.world; ++s) {
+      chunk(s, q0, q1);
+      for (uint32_t i = q0 + threadIdx.x; i < q1; i += blockDim.x) {
+        float4 acc = reinterpret_cast<const float4*>(state)[i];
+        const float4 c = __ldcg(reinterpret_cast<const float4*>(slot_at(v, v.rank, par, s)) + i);
+        acc.x += c.x;
+        acc.y += c.y;
+        acc.z += c.z;
+        acc.w += c.w;
+        reinterpret_cast<float4*>(state)[i] = acc;
+      }
+    }
+  }
+  end_call(v, b, e);
+}
+
+// In place over n packed argmax keys (order key << 32 | ~id, 0 = none) spaced
+// `stride` u64 apart: this rank's keys carry ids local to its vocabulary rows
+// starting at id_base; afterwards every rank holds the largest key over the
+// ranks with global ids (ties -> lowest id, as ops 16/17 of resident_math.comp).
+__global__ void __launch_bounds__(kThreads) allmax_keys_kernel(View v, unsigned long long* keys, uint32_t n,
+                                                               uint32_t stride, uint32_t id_base) {
+  const uint32_t b = blockIdx.x;
+  const uint32_t e = begin_call(v, b);
+  const uint32_t par = e & 1u;
+  if (b != 0u) n = 0u;  // the other blocks only keep the per-block call counters in step
+  for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+    unsigned long long k = keys[static_cast<size_t>(i) * stride];
+    if (k != 0ull) {
+      const uint32_t low = static_cast<uint32_t>(k & 0xffffffffull) - id_base;  // ~(id + base) = ~id - base
+      k = (k & 0xffffffff00000000ull) | low;
+    }
+    for (uint32_t p = 0; p < v.world; ++p) reinterpret_cast<unsigned long long*>(slot_at(v, p, par, v.rank))[i] = k;
+  }
+  publish(v, b, e);
+  if (await_all(v, b, e)) {
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+      unsigned long long k = 0ull;
+      for (uint32_t s = 0; s < v.world; ++s)
+        k = max(k, __ldcg(reinterpret_cast<const unsigned long long*>(slot_at(v, v.rank, par, s)) + i));
+      keys[static_cast<size_t>(i) * stride] = k;
+    }
+  }
+  end_call(v, b, e);
+}
+
 rta_status team_fail(rta_status code, const std::string& msg) {
   rta::set_last_error(msg);
   return code;
@@ -197,6 +272,50 @@ struct rta_team {
     return v;
   }
 };
+
+// Internal entry points of the decode engine's tensor-parallel mode.
+namespace rta {
+uint32_t team_rank(const rta_team* t) { return t->rank; }
+uint32_t team_world(const rta_team* t) { return t->world; }
+bool team_ready(const rta_team* t) { return t->connected; }
+size_t team_capacity_words(const rta_team* t) { return t->cap_words; }
+// The engine launches every exchange of a handle with the same block count
+// (team_blocks), so the per-block call counters -- and with them the slot
+// parity of a call -- advance in step across exchange kinds whose chunks of
+// the slots differ.
+uint32_t team_blocks(size_t words) {
+  const size_t b = (words + kChunkWords - 1u) / kChunkWords;
+  return b < 1u ? 1u : b > kMaxBlocks ? kMaxBlocks : static_cast<uint32_t>(b);
+}
+cudaError_t team_allreduce(rta_team* t, const float* partial, const float* addend, float* out, size_t n,
+                           uint32_t blocks, cudaStream_t s) {
+  if (!t->connected || n == 0 || n % 4u || n > t->cap_words || blocks > kMaxBlocks ||
+      static_cast<size_t>(blocks) * kChunkWords < n)
+    return cudaErrorInvalidValue;
+  allreduce_kernel<<<blocks, kThreads, 0, s>>>(t->view(), partial, addend, out, static_cast<uint32_t>(n));
+  return cudaGetLastError();
+}
+cudaError_t team_gather_add(rta_team* t, const float* delta, float* state, uint32_t width,
+                            const uint32_t* row_start, uint32_t blocks, cudaStream_t s) {
+  if (!t->connected || width % 4u || static_cast<size_t>(row_start[t->world]) * width > t->cap_words ||
+      blocks == 0 || blocks > kMaxBlocks)
+    return cudaErrorInvalidValue;
+  uint32_t st[kMaxRanks + 1];
+  for (uint32_t i = 0; i <= kMaxRanks; ++i) st[i] = row_start[i < t->world ? i : t->world];
+  gather_add_kernel<<<blocks, kThreads, 0, s>>>(t->view(), delta, state, width, st[0], st[1], st[2], st[3], st[4],
+                                                st[5], st[6], st[7], st[8]);
+  return cudaGetLastError();
+}
+cudaError_t team_allmax_keys(rta_team* t, unsigned long long* keys, uint32_t n, uint32_t stride, uint32_t id_base,
+                             uint32_t blocks, cudaStream_t s) {
+  if (!t->connected || n == 0 || n > kChunkWords / 2u || 2ull * n > t->cap_words || blocks == 0 ||
+      blocks > kMaxBlocks)
+    return cudaErrorInvalidValue;
+  allmax_keys_kernel<<<blocks, kThreads, 0, s>>>(t->view(), keys, n, stride, id_base);
+  return cudaGetLastError();
+}
+uint32_t* team_error_word(rta_team* t) { return t->ctr + kMaxBlocks; }
+}  // namespace rta
 
 extern "C" {
 

@@ -36,6 +36,8 @@ _SIGS = {
     "rta_model_open": (_I, [ctypes.POINTER(ModelSpecC), _P, _SZ, _P, _SZ, _P, _SZ, _U32, _I, ctypes.POINTER(_P)]),
     "rta_model_open_batch": (_I, [ctypes.POINTER(ModelSpecC), _P, _SZ, _P, _SZ, _P, _SZ, _U32, _U32, _I,
                                   ctypes.POINTER(_P)]),
+    "rta_model_open_team": (_I, [ctypes.POINTER(ModelSpecC), _P, _SZ, _P, _SZ, _P, _SZ, _U32, _U32, _P, _P, _U32,
+                                 _I, ctypes.POINTER(_P)]),
     "rta_model_open_ex": (_I, [ctypes.POINTER(ModelSpecC), _P, _SZ, _P, _SZ, _P, _SZ, _U32, _U32, _U32, _I,
                                ctypes.POINTER(_P)]),
     "rta_model_attention": (_I, [_P, _U32, _P, _P, _P, _P, _U32, _U32, _U32, _U32, _U32, _P, _P, _P, _P,
@@ -58,7 +60,7 @@ _SIGS = {
 }
 PACKET_HISTORY = 1  # RTA_MODEL_PACKET_HISTORY
 PROFILE_KINDS = ("start", "readout", "embed", "qkv", "attention_prep", "attention", "o_proj", "in_proj",
-                 "gated_delta", "out_proj", "gate_up", "down")  # RTA_PROF_* (include/rta.h)
+                 "gated_delta", "out_proj", "gate_up", "down", "exchange")  # RTA_PROF_* (include/rta.h)
 RESOURCE_NAMES = ("payload_bytes", "derived_layer_bytes", "history_bytes", "recurrent_state_bytes", "capacity",
                   "attention_splits", "kernels_per_decode_step", "kernels_per_prefill_step", "position",
                   "sequences", "tensor_core_matrices")
@@ -135,6 +137,53 @@ class ResidentModel:
         del mkeep, bkeep
         model = cls(h, spec, capacity, device, sequences)
         model.history = history
+        return model
+
+    @classmethod
+    def with_team(cls, spec: assets.Spec, params, matrices, basis, capacity: int, sequence_starts, team,
+                  device: int | None = None, history: str = "fp16"):
+        """Tensor-parallel hybrid handle (rta_model_open_team): this rank decodes the
+        attention / recurrent layers of sequences [starts[rank], starts[rank + 1]) and
+        a 1/world slice of every MLP and of the vocabulary readout for all of them.
+        team: a connected tensor_parallel.Team whose exchanges this handle owns."""
+        device = _current_device() if device is None else device
+        lib = _lib_model()
+        params = np.ascontiguousarray(params, np.uint32)
+        starts = np.ascontiguousarray(sequence_starts, np.uint32)
+
+        def addr(buf):
+            if isinstance(buf, np.ndarray):
+                b = np.ascontiguousarray(buf, np.uint8)
+                return _np_ptr(b), b.nbytes, b
+            return ctypes.c_void_p(buf.data_ptr()), buf.numel() * buf.element_size(), buf
+        mp, mb, mkeep = addr(matrices)
+        bp, bb, bkeep = addr(basis)
+        cs = ModelSpecC.from_spec(spec)
+        h = ctypes.c_void_p()
+        flags = PACKET_HISTORY if history == "packet" else 0
+        sequences = int(starts[-1])
+        _check(lib.rta_model_open_team(ctypes.byref(cs), _np_ptr(params), params.size, mp, mb, bp, bb, capacity,
+                                       sequences, _np_ptr(starts), team._ptr, flags, device, ctypes.byref(h)))
+        del mkeep, bkeep
+        model = cls(h, spec, capacity, device, sequences)
+        model.history = history
+        model.team = team
+        return model
+
+    @classmethod
+    def synthetic_team(cls, spec: assets.Spec, seed: int, capacity: int, sequence_starts, team,
+                       device: int | None = None, history: str = "fp16"):
+        """Random-init model of `spec` (same weights on every rank: generated from the seed)
+        opened as a tensor-parallel hybrid handle."""
+        import torch
+        device = _current_device() if device is None else device
+        torch.cuda.set_device(device)
+        layout = assets.plan(spec, seed)
+        mats, basis = assets.generate_device(layout, seed)
+        model = cls.with_team(spec, layout.params(), mats, basis, capacity, sequence_starts, team, device, history)
+        model.layout = layout
+        del mats, basis
+        torch.cuda.empty_cache()
         return model
 
     @classmethod
