@@ -168,9 +168,14 @@ RTA_API rta_status rta_team_error(rta_team* team, void* stream, uint32_t* error_
 RTA_API rta_status rta_team_disconnect(rta_team* team);
 RTA_API void rta_team_destroy(rta_team* team);
 
-/* y[b][r] (+)= sum_c W[r][c] x[b][c]; W Q4_K or Q6_K row-major, rows % 16 == 0,
- * cols % 256 == 0, 1 <= batch <= 32.  Replaces op 2 of
- * ray_tracing/native/shaders/resident_math.comp:39-75 (kinds 0-2, 4-6, 8). */
+/* y[b][r] (+)= sum_c W[r][c] x[b][c]; W row-major Q4_K or Q6_K (or their tiled
+ * re-layouts), or dense F32 / F16 / BF16 (the exporter's codes 0 / 1 / 30,
+ * 16-byte aligned rows), rows % 16 == 0, cols % 256 == 0, 1 <= batch <= 32.
+ * The same formats are accepted by rta_gemv_swiglu, rta_mlp_swiglu and
+ * rta_readout, and by the model handle for every projection, the embedding
+ * and the output rows.  Replaces op 2 of
+ * ray_tracing/native/shaders/resident_math.comp:39-75 (kinds 0-2, 4-6, 8)
+ * over ggufValue (resident_quant.glsl:6-20). */
 RTA_API rta_status rta_gemv(int format, const void* w, uint32_t rows, uint32_t cols, const float* x, uint32_t batch,
                     float* y, int accumulate, void* stream);
 

@@ -50,14 +50,14 @@ class OracleModel:
         at = int(self.p[base + 27] + self.p[field]) * 4
         meta = int(self.p[field + 1])
         fmt, mode = meta & 255, meta >> 8
-        nbytes = rows * cols * 4 if fmt == O.F32 else rows * cols // 256 * BLOCK[fmt]
+        nbytes = rows * O.row_bytes(fmt, cols)
         return self.m[at:at + nbytes], fmt, mode
 
     def _orig(self, a):
         return np.where(a < self.R, (a % 2) * (self.R // 2) + a // 2, a)
 
     def _rows(self, raw, fmt, cols, rows_src, idx):
-        rb = cols // 256 * BLOCK[fmt]
+        rb = O.row_bytes(fmt, cols)
         return raw.reshape(rows_src, rb)[idx].reshape(-1)
 
     def _mode_rows(self, mode, n):
@@ -129,13 +129,15 @@ class OracleModel:
 
     def _embed(self, token):
         fmt = int(self.p[13])
-        rb = self.D // 256 * BLOCK[fmt]
+        rb = O.row_bytes(fmt, self.D)
         off = int(self.p[14]) * 4 + token * rb
+        if fmt in O.DENSE_BYTES:
+            return O.dense_values(fmt, self.b[off:off + rb])
         return O.dequantize(fmt, self.b[off:off + rb])
 
     def readout(self, logits=True):
         fmt = int(self.p[15])
-        rb = self.D // 256 * BLOCK[fmt]
+        rb = O.row_bytes(fmt, self.D)
         off = int(self.p[16]) * 4
         W = self.b[off:off + rb * self.V]
         x = O.rmsnorm(self.state, self.f32(self.p[4], self.D), self.eps)
@@ -236,6 +238,12 @@ def synthetic_payloads(layout, seed: int, sigma: float = 0.02):
         tseed = seed * 1000003 + i
         if t.fmt == O.F32:
             buf[t.offset:t.offset + t.nbytes] = O.synthetic_normal(tseed, sigma, t.rows * t.cols).view(np.uint8)
+        elif t.fmt == O.F16:
+            v = O.synthetic_normal(tseed, sigma, t.rows * t.cols)
+            buf[t.offset:t.offset + t.nbytes] = v.astype(np.float16).view(np.uint8)
+        elif t.fmt == O.BF16:
+            v = O.synthetic_normal(tseed, sigma, t.rows * t.cols)
+            buf[t.offset:t.offset + t.nbytes] = O.to_bf16_bits(v).view(np.uint8)
         else:
             buf[t.offset:t.offset + t.nbytes] = O.synthetic_blocks(t.fmt, tseed, sigma, t.rows * t.cols // 256)
     return mats, basis

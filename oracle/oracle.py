@@ -18,8 +18,31 @@ HERE = Path(__file__).resolve().parent
 SOURCE = HERE / "rta_oracle.c"
 LIBRARY = HERE / "liboracle.so"
 
-Q4_K, Q6_K, F32 = 12, 14, 0
+Q4_K, Q6_K, F32, F16, BF16 = 12, 14, 0, 1, 30
 BLOCK_BYTES = {Q4_K: 144, Q6_K: 210}
+DENSE_BYTES = {F32: 4, F16: 2, BF16: 2}
+
+
+def row_bytes(fmt: int, cols: int) -> int:
+    """Bytes of one row of `cols` coefficients in an exporter format."""
+    return cols * DENSE_BYTES[fmt] if fmt in DENSE_BYTES else cols // 256 * BLOCK_BYTES[fmt]
+
+
+def to_bf16_bits(values) -> np.ndarray:
+    """fp32 -> bf16 bits, round to nearest even (NaN kept quiet)."""
+    u = np.ascontiguousarray(values, np.float32).view(np.uint32)
+    rounded = (u + 0x7FFF + ((u >> 16) & 1)) >> 16
+    return np.where(np.isnan(np.ascontiguousarray(values, np.float32)), (u >> 16) | 0x40, rounded).astype(np.uint16)
+
+
+def dense_values(fmt: int, raw) -> np.ndarray:
+    """Decode a dense F32 / F16 / BF16 byte run to fp32 (ggufValue's dense branches)."""
+    b = np.ascontiguousarray(raw, np.uint8)
+    if fmt == F32:
+        return b.view(np.float32).copy()
+    if fmt == F16:
+        return b.view(np.float16).astype(np.float32)
+    return (b.view(np.uint16).astype(np.uint32) << 16).view(np.float32)
 
 
 def build(force: bool = False) -> Path:
@@ -110,7 +133,7 @@ def dequantize(fmt: int, blocks) -> np.ndarray:
 
 def gemv(fmt: int, W, rows_out: int, cols: int, x) -> np.ndarray:
     x = _c(x, np.float32).reshape(-1, cols)
-    W = _c(W, np.uint8) if fmt != F32 else _c(W, np.float32)
+    W = _c(W, np.uint8).reshape(-1) if fmt != F32 or np.asarray(W).dtype == np.uint8 else _c(W, np.float32)
     y = np.empty((x.shape[0], rows_out), np.float32)
     lib().rta_oracle_gemv(fmt, _p(W), rows_out, cols, _p(x), x.shape[0], _p(y))
     return y

@@ -27,7 +27,10 @@ rta_status cuda_status(cudaError_t e, const char* what) {
 }
 cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
 bool quant_format(int f) { return f == RTA_Q4_K || f == RTA_Q6_K; }
-bool gemv_format(int f) { return quant_format(f) || f == RTA_Q4_K_TILED || f == RTA_Q6_K_TILED; }
+bool gemv_format(int f) {
+  return quant_format(f) || f == RTA_Q4_K_TILED || f == RTA_Q6_K_TILED || f == RTA_F32 || f == RTA_F16 ||
+         f == RTA_BF16;
+}
 
 constexpr uint32_t kApiMaxBatch = 32;  // batch rows accepted by the GEMV operators (rta.h)
 constexpr size_t kErrBytes = 256;  // device error word + padding at the head of every workspace
@@ -213,7 +216,8 @@ rta_status rta_gemv(int format, const void* w, uint32_t rows, uint32_t cols, con
                     float* y, int accumulate, void* stream) {
   if (!gemv_format(format) || !w || !x || !y || rows == 0 || rows % 16 || cols == 0 || cols % 256 || batch == 0 ||
       batch > kApiMaxBatch)
-    return fail(RTA_E_ARG, "rta_gemv: format must be Q4_K/Q6_K, rows % 16 == 0, cols % 256 == 0, 1 <= batch <= 32");
+    return fail(RTA_E_ARG, "rta_gemv: format Q4_K/Q6_K (tiled too), F32, F16 or BF16, rows % 16 == 0, "
+                           "cols % 256 == 0, 1 <= batch <= 32");
   rta::GemvArgs a;
   a.fmt = format;
   a.w0 = static_cast<const uint8_t*>(w);

@@ -44,6 +44,14 @@ inline void require(bool ok, const std::string& msg, rta_status code = RTA_E_ASS
   if (!ok) throw Failure{code, msg};
 }
 
+// Packed (Q4_K / Q6_K) or dense (F32 / F16 / BF16) exporter formats the engine serves.
+inline bool packed_fmt(int f) { return f == kQ4K || f == kQ6K; }
+inline bool served_fmt(int f) { return packed_fmt(f) || dense_format(f); }
+// Bytes of one row of `cols` coefficients (tiled / panel codes count as their packed format).
+inline size_t row_bytes(int fmt, size_t cols) {
+  return dense_format(fmt) ? cols * dense_bytes(fmt) : cols / 256 * block_bytes(fmt % 100);
+}
+
 template <class T>
 struct DevBuf {
   T* p = nullptr;
@@ -88,6 +96,8 @@ struct Layer {
   const uint8_t *gate = nullptr, *up = nullptr, *down = nullptr;
   int mlp_fmt = kQ4K, down_fmt = kQ4K;
   DevBuf<uint8_t> gate_s, up_s, down_s;  // tensor-parallel mode: this rank's slices (own copies)
+  // dense (F32 / F16 / BF16) matrices that sat off a 16-byte boundary in the payload: aligned copies
+  std::vector<std::unique_ptr<DevBuf<uint8_t>>> dense_copies;
 };
 
 struct Engine {
@@ -170,7 +180,7 @@ struct Engine {
   // (read too when accumulated).
   static double product_bytes(const GemvArgs& a) {
     const int base = a.fmt % 100;  // tiled / panel codes keep the packed format in the last two digits
-    const double w = static_cast<double>(a.rows) * (a.cols / 256) * block_bytes(base) * (a.w1 ? 2.0 : 1.0);
+    const double w = static_cast<double>(a.rows) * row_bytes(base, a.cols) * (a.w1 ? 2.0 : 1.0);
     const double rows_out = static_cast<double>(a.rows) * (a.w1 ? 2.0 : 1.0);
     return w + 4.0 * a.batch * (a.cols + rows_out * (a.epilogue == kAccumulate ? 2.0 : 1.0));
   }
@@ -217,8 +227,7 @@ struct Engine {
     const uint32_t at = word(base + 27u) + word(field), meta = word(field + 1u);
     Desc d{matrices.p + static_cast<size_t>(at) * 4u, static_cast<int>(meta & 255u), static_cast<int>(meta >> 8)};
     size_t bytes = 0;
-    if (d.fmt == kQ4K || d.fmt == kQ6K) bytes = rows * cols / 256 * block_bytes(d.fmt);
-    else if (d.fmt == kF32) bytes = rows * cols * 4;
+    if (served_fmt(d.fmt)) bytes = rows * row_bytes(d.fmt, cols);
     else throw Failure{RTA_E_ASSET, "layer " + std::to_string(l) + " descriptor " + std::to_string(i) +
                                         ": coefficient format " + std::to_string(d.fmt) + " not supported"};
     require(static_cast<size_t>(at) * 4u + bytes <= matrices.n, "matrix descriptor beyond geometry_weights");
@@ -282,18 +291,17 @@ struct Engine {
   // Copies of this rank's gate / up rows and down-projection columns.
   void slice_mlp(Layer& L) {
     const uint32_t D = this->D(), Ff = spec.middle_size;
-    const size_t rg = static_cast<size_t>(D) / 256 * block_bytes(L.mlp_fmt);
+    const size_t rg = row_bytes(L.mlp_fmt, D);
     L.gate_s.alloc(static_cast<size_t>(fcount) * rg);
     L.up_s.alloc(static_cast<size_t>(fcount) * rg);
     RTA_CUDA(cudaMemcpyAsync(L.gate_s.p, L.gate + static_cast<size_t>(f0) * rg, L.gate_s.n, cudaMemcpyDeviceToDevice,
                              stream));
     RTA_CUDA(cudaMemcpyAsync(L.up_s.p, L.up + static_cast<size_t>(f0) * rg, L.up_s.n, cudaMemcpyDeviceToDevice,
                              stream));
-    const size_t bb = block_bytes(L.down_fmt), row = static_cast<size_t>(Ff) / 256 * bb;
-    const size_t width = static_cast<size_t>(fcount) / 256 * bb;
+    const size_t row = row_bytes(L.down_fmt, Ff), width = row_bytes(L.down_fmt, fcount);
+    const size_t skip = row_bytes(L.down_fmt, f0);  // f0 is a multiple of 256
     L.down_s.alloc(static_cast<size_t>(D) * width);
-    RTA_CUDA(cudaMemcpy2DAsync(L.down_s.p, width, L.down + static_cast<size_t>(f0) / 256 * bb, row, width, D,
-                               cudaMemcpyDeviceToDevice, stream));
+    RTA_CUDA(cudaMemcpy2DAsync(L.down_s.p, width, L.down + skip, row, width, D, cudaMemcpyDeviceToDevice, stream));
     L.gate = L.gate_s.p;
     L.up = L.up_s.p;
     L.down = L.down_s.p;
@@ -312,23 +320,39 @@ struct Engine {
     };
     std::vector<Job> jobs;
     auto mut = [](const uint8_t* q) { return const_cast<uint8_t*>(q); };
+    // Dense matrices keep their row-major layout (the dense GEMV streams rows);
+    // the ones off a 16-byte boundary get an aligned copy.
+    auto add = [&](Layer& L, const uint8_t*& ptr, int fmt, int* field, uint32_t rows, uint32_t cols) {
+      if (!dense_format(fmt)) {
+        jobs.push_back({mut(ptr), fmt, field, rows, cols});
+        return;
+      }
+      if (reinterpret_cast<uintptr_t>(ptr) % 16 == 0) return;
+      auto copy = std::make_unique<DevBuf<uint8_t>>();
+      copy->alloc(static_cast<size_t>(rows) * row_bytes(fmt, cols));
+      RTA_CUDA(cudaMemcpyAsync(copy->p, ptr, copy->n, cudaMemcpyDeviceToDevice, stream));
+      ptr = copy->p;
+      L.dense_copies.push_back(std::move(copy));
+    };
     for (size_t li = 0; li < layers.size(); ++li) {
       Layer& L = *layers[li];
       if (L.full) {
-        jobs.push_back({L.qkvg.p, L.qkvg_fmt, &L.qkvg_fmt, L.qkvg_rows, D});
-        jobs.push_back({mut(L.o), L.o_fmt, &L.o_fmt, D, Q()});
+        const uint8_t* q = L.qkvg.p;
+        add(L, q, L.qkvg_fmt, &L.qkvg_fmt, L.qkvg_rows, D);
+        add(L, L.o, L.o_fmt, &L.o_fmt, D, Q());
       } else {
-        jobs.push_back({L.inproj.p, L.inproj_fmt, &L.inproj_fmt, L.inproj_rows, D});
-        jobs.push_back({mut(L.out), L.out_fmt, &L.out_fmt, D, S()});
+        const uint8_t* q = L.inproj.p;
+        add(L, q, L.inproj_fmt, &L.inproj_fmt, L.inproj_rows, D);
+        add(L, L.out, L.out_fmt, &L.out_fmt, D, S());
       }
-      jobs.push_back({mut(L.gate), L.mlp_fmt, &L.mlp_fmt, F, D});
-      jobs.push_back({mut(L.up), L.mlp_fmt, nullptr, F, D});  // up shares the gate's format field
-      jobs.push_back({mut(L.down), L.down_fmt, &L.down_fmt, D, F});
+      add(L, L.gate, L.mlp_fmt, &L.mlp_fmt, F, D);
+      add(L, L.up, L.mlp_fmt, nullptr, F, D);  // up shares the gate's format field
+      add(L, L.down, L.down_fmt, &L.down_fmt, D, F);
     }
     std::vector<std::pair<uintptr_t, size_t>> spans;
     size_t need = 0;
     for (const Job& j : jobs) {
-      const size_t bytes = static_cast<size_t>(j.rows) * (j.cols / 256) * block_bytes(j.fmt);
+      const size_t bytes = static_cast<size_t>(j.rows) * row_bytes(j.fmt, j.cols);
       const uintptr_t a = reinterpret_cast<uintptr_t>(j.p);
       for (const auto& d : spans)
         require(!(a < d.first + d.second && d.first < a + bytes),
@@ -338,11 +362,11 @@ struct Engine {
       need = std::max(need, bytes);
     }
     DevBuf<uint8_t> tmp;
-    tmp.alloc(need);
+    tmp.alloc(std::max<size_t>(need, 1));
     // gate and up share one format field: both take the panel order only together
     auto panel_ok = [&](uint32_t rows) { return tc && rows % 128u == 0u; };
     for (const Job& j : jobs) {
-      const size_t bytes = static_cast<size_t>(j.rows) * (j.cols / 256) * block_bytes(j.fmt);
+      const size_t bytes = static_cast<size_t>(j.rows) * row_bytes(j.fmt, j.cols);
       if (panel_ok(j.rows))
         RTA_CUDA(launch_tile_tc(j.fmt, j.p, j.rows, j.cols, tmp.p, stream));
       else
@@ -353,9 +377,11 @@ struct Engine {
       if (j.tiled_field) *j.tiled_field = j.fmt + (panel_ok(j.rows) ? kPanelOffset : kTiledOffset);
       panel_matrices += panel_ok(j.rows) ? 1u : 0u;
     }
-    const size_t lm_bytes = static_cast<size_t>(VL()) * (D / 256) * block_bytes(lm_fmt);
+    const size_t lm_bytes = static_cast<size_t>(VL()) * row_bytes(lm_fmt, D);
     lm_tiled.alloc(lm_bytes);
-    if (panel_ok(VL())) {
+    if (dense_format(lm_fmt)) {  // row-major as exported, in an aligned buffer of its own
+      RTA_CUDA(cudaMemcpyAsync(lm_tiled.p, lm, lm_bytes, cudaMemcpyDeviceToDevice, stream));
+    } else if (panel_ok(VL())) {
       RTA_CUDA(launch_tile_tc(lm_fmt, lm, VL(), D, lm_tiled.p, stream));
       lm_fmt += kPanelOffset;
       ++panel_matrices;
@@ -414,9 +440,9 @@ struct Engine {
     out_norm = pf(word(4), D);
     embed_fmt = static_cast<int>(word(13));
     lm_fmt = static_cast<int>(word(15));
-    require((embed_fmt == kQ4K || embed_fmt == kQ6K) && (lm_fmt == kQ4K || lm_fmt == kQ6K),
-            "token embedding and output rows must be Q4_K or Q6_K");
-    const size_t row_e = D / 256 * block_bytes(embed_fmt), row_l = D / 256 * block_bytes(lm_fmt);
+    require(served_fmt(embed_fmt) && served_fmt(lm_fmt),
+            "token embedding and output rows must be Q4_K, Q6_K, F32, F16 or BF16");
+    const size_t row_e = row_bytes(embed_fmt, D), row_l = row_bytes(lm_fmt, D);
     require(static_cast<size_t>(word(14)) * 4 + row_e * spec.vocabulary_size <= basis_bytes, "token_embd out of range");
     require(static_cast<size_t>(word(16)) * 4 + row_l * spec.vocabulary_size <= basis_bytes, "output rows out of range");
     require(spec.vocabulary_size % 16 == 0, "vocabulary must be a multiple of 16 rows");
@@ -437,10 +463,10 @@ struct Engine {
         Desc dq = desc(l, 0, static_cast<size_t>(Qw) * (L->gated ? 2 : 1), D);
         Desc dk = desc(l, 1, KV, D), dv = desc(l, 8, KV, D);
         Desc dg = L->gated ? desc(l, 6, static_cast<size_t>(Qw) * 2, D) : dq;
-        require(dq.fmt == dk.fmt && dq.fmt == dv.fmt && (dq.fmt == kQ4K || dq.fmt == kQ6K),
-                "q/k/v projections must share one packed format");
+        require(dq.fmt == dk.fmt && dq.fmt == dv.fmt && dq.fmt == dg.fmt && served_fmt(dq.fmt),
+                "q/k/v (and gate) projections must share one format");
         L->qkvg_fmt = dq.fmt;
-        const uint32_t rb = D / 256 * block_bytes(dq.fmt);
+        const uint32_t rb = static_cast<uint32_t>(row_bytes(dq.fmt, D));
         L->qkvg_rows = Qw + 2 * KV + (L->gated ? Qw : 0);
         L->qkvg.alloc(static_cast<size_t>(L->qkvg_rows) * rb);
         gather(L->qkvg.p, dq, Qw, rb, dq.mode);
@@ -459,9 +485,9 @@ struct Engine {
         const uint32_t Kw = K(), Sw = S(), H = spec.state_heads;
         Desc dqkv = desc(l, 0, 2ull * Kw + Sw, D);
         Desc dz = desc(l, 6, Sw, D);
-        require(dqkv.fmt == dz.fmt && (dqkv.fmt == kQ4K || dqkv.fmt == kQ6K),
-                "recurrent qkv and gate projections must share one packed format");
-        const uint32_t rb = D / 256 * block_bytes(dqkv.fmt);
+        require(dqkv.fmt == dz.fmt && served_fmt(dqkv.fmt),
+                "recurrent qkv and gate projections must share one format");
+        const uint32_t rb = static_cast<uint32_t>(row_bytes(dqkv.fmt, D));
         L->inproj_fmt = dqkv.fmt;
         L->inproj_rows = 2 * Kw + 2 * Sw;
         L->inproj.alloc(static_cast<size_t>(L->inproj_rows) * rb);
@@ -494,8 +520,8 @@ struct Engine {
       }
       Desc dg = desc(l, 3, spec.middle_size, D), du = desc(l, 5, spec.middle_size, D),
            dd = desc(l, 4, D, spec.middle_size);
-      require(dg.fmt == du.fmt && (dg.fmt == kQ4K || dg.fmt == kQ6K) && (dd.fmt == kQ4K || dd.fmt == kQ6K),
-              "MLP projections must be Q4_K / Q6_K (gate and up alike)");
+      require(dg.fmt == du.fmt && served_fmt(dg.fmt) && served_fmt(dd.fmt),
+              "MLP projections must be Q4_K, Q6_K, F32, F16 or BF16 (gate and up alike)");
       L->gate = dg.ptr;
       L->up = du.ptr;
       L->down = dd.ptr;
@@ -505,7 +531,7 @@ struct Engine {
       layers.push_back(std::move(L));
     }
     if (team) {  // this rank's vocabulary rows, a contiguous run of the GGUF rows
-      const size_t rb = static_cast<size_t>(D) / 256 * block_bytes(lm_fmt);
+      const size_t rb = row_bytes(lm_fmt, D);
       lm_slice.alloc(static_cast<size_t>(vcount) * rb);
       RTA_CUDA(cudaMemcpyAsync(lm_slice.p, lm + static_cast<size_t>(v0) * rb, lm_slice.n, cudaMemcpyDeviceToDevice,
                                stream));
@@ -722,7 +748,7 @@ struct Engine {
     e.table = embed;
     e.fmt = embed_fmt;
     e.D = D;
-    e.row_bytes = D / 256 * block_bytes(embed_fmt);
+    e.row_bytes = static_cast<uint32_t>(row_bytes(embed_fmt, D));
     e.vocab = spec.vocabulary_size;
     e.ctrl = c;
     e.prompt = prompt.p;

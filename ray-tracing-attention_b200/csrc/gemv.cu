@@ -1323,6 +1323,7 @@ uint32_t smem_for(uint32_t cols, uint32_t nb) {
 }  // namespace
 
 cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t s) {
+  if (dense_format(a.fmt)) return launch_gemv_dense(a, s);
   const bool tiled = a.fmt == kQ4KTiled || a.fmt == kQ6KTiled;
   const int fmt = tiled ? a.fmt - kTiledOffset : a.fmt;
   if ((fmt != kQ4K && fmt != kQ6K) || !a.w0 || !a.x || a.rows == 0 || a.rows % kTileRows ||

@@ -103,6 +103,20 @@ __global__ void __launch_bounds__(256) embed_kernel(EmbedParams p) {
   __syncthreads();
   if (!go_s) return;
   const uint8_t* row = p.table + static_cast<size_t>(token_s) * p.row_bytes;
+  if (p.fmt == kF32 || p.fmt == kF16 || p.fmt == kBF16) {  // dense rows (ggufValue's first branches)
+    float* st = p.state + static_cast<size_t>(z) * p.D;
+    for (uint32_t i = threadIdx.x; i < p.D; i += blockDim.x) {
+      float v;
+      if (p.fmt == kF32) {
+        v = reinterpret_cast<const float*>(row)[i];
+      } else {
+        const uint32_t h = reinterpret_cast<const uint16_t*>(row)[i];
+        v = p.fmt == kF16 ? half_bits_to_float(h) : __uint_as_float(h << 16);
+      }
+      st[i] = v;
+    }
+    return;
+  }
   const uint32_t bb = p.fmt == kQ4K ? 144u : 210u;
   float* state = p.state + static_cast<size_t>(z) * p.D;
   for (uint32_t i = threadIdx.x; i < p.D; i += blockDim.x) {

@@ -127,6 +127,13 @@ cudaError_t launch_tile_tc(int fmt, const uint8_t* src, uint32_t rows, uint32_t 
 cudaError_t launch_gemv_f32(const float* W, uint32_t rows, uint32_t cols, const float* x, uint32_t x_stride,
                             uint32_t batch, float* y, uint32_t y_stride, cudaStream_t s);
 
+// ----------------------------------------------------------- gemv_dense.cu
+// F32 / F16 / BF16 matrices (export.py format codes 0 / 1 / 30), row-major:
+// the same GemvArgs contract as launch_gemv (which forwards them here).
+bool dense_format(int fmt);
+uint32_t dense_bytes(int fmt);  // bytes per coefficient
+cudaError_t launch_gemv_dense(const GemvArgs& a, cudaStream_t s);
+
 // ----------------------------------------------------------------- team.cu
 // The decode engine's tensor-parallel mode drives the team exchanges from its
 // own graphs (every rank records the same exchanges in the same order).

@@ -24,8 +24,8 @@ from pathlib import Path
 
 import numpy as np
 
-Q4_K, Q6_K, F32 = 12, 14, 0
-FORMAT_BYTES = {F32: 4.0, Q4_K: 144 / 256, Q6_K: 210 / 256}
+Q4_K, Q6_K, F32, F16, BF16 = 12, 14, 0, 1, 30
+FORMAT_BYTES = {F32: 4.0, F16: 2.0, BF16: 2.0, Q4_K: 144 / 256, Q6_K: 210 / 256}
 STRIDE = 64
 
 
@@ -273,6 +273,12 @@ def generate_device(layout: Layout, seed: int, sigma: float = 0.02, device="cuda
         if t.fmt == F32:
             out = view.view(torch.float32)
             _lib.check(lib.rta_synthetic_normal(tseed, sigma, 0.0, t.rows * t.cols, _ptr(out), _stream()))
+        elif t.fmt in (F16, BF16):  # the same fp32 draws, rounded to nearest even
+            tmp = torch.empty(t.rows * t.cols, dtype=torch.float32, device=device)
+            _lib.check(lib.rta_synthetic_normal(tseed, sigma, 0.0, t.rows * t.cols, _ptr(tmp), _stream()))
+            view.view(torch.float16 if t.fmt == F16 else torch.bfloat16).copy_(
+                tmp.to(torch.float16 if t.fmt == F16 else torch.bfloat16))
+            del tmp
         else:
             _lib.check(lib.rta_synthetic_blocks(t.fmt, tseed, sigma, 0, t.rows * t.cols // 256, _ptr(view),
                                                 _stream()))

@@ -160,3 +160,26 @@ def test_reference_geometry_manifest():
     assert m["spec_2b"]["history_bytes"] == 1416 and m["spec_2b"]["fingerprint"] == "d1b9251ad05ff9b6"
     assert m["cpu_selftest"]["group_merge_FP64"] is True
     assert m["gguf_version"] == "0.19.0"
+
+
+@pytest.mark.parametrize("fmt", [0, 1, 30])
+def test_dense_formats_decode_and_gemv(fmt):
+    """Dense F32 / F16 / BF16 rows (ggufValue's first branches): the oracle's decode
+    equals numpy's conversion of the same bits, and its octet-order GEMV equals an
+    FP64 matrix product of the decoded weights within fp32 rounding."""
+    rng = np.random.default_rng(fmt + 3)
+    rows, cols = 48, 512
+    w = rng.normal(0, 0.02, rows * cols).astype(np.float32)
+    raw = {0: w.view(np.uint8), 1: w.astype(np.float16).view(np.uint8),
+           30: oracle.to_bf16_bits(w).view(np.uint8)}[fmt]
+    dec = oracle.dense_values(fmt, raw)
+    want_dec = {0: w, 1: w.astype(np.float16).astype(np.float32),
+                30: (oracle.to_bf16_bits(w).astype(np.uint32) << 16).view(np.float32)}[fmt]
+    assert np.array_equal(dec.view(np.uint32), want_dec.view(np.uint32))
+    assert oracle.row_bytes(fmt, cols) * rows == raw.size
+    x = rng.normal(0, 1, (3, cols)).astype(np.float32)
+    y = oracle.gemv(fmt, raw, rows, cols, x)
+    want = x.astype(np.float64) @ dec.reshape(rows, cols).astype(np.float64).T
+    assert rel_l2(y, want) < 1e-6
+    if fmt == 30:  # bf16 rounds to nearest even: halfway cases go to the even neighbour
+        assert oracle.to_bf16_bits(np.float32([1.00390625, 1.01171875])).tolist() == [0x3F80, 0x3F82]
