@@ -492,7 +492,7 @@ class DecodeWorkload(Workload):
         self.seed = seed
         self.model = ResidentModel.synthetic(self.spec, seed, capacity=2048, history=kv)
         self.prompt = np.random.default_rng(seed).integers(0, self.spec.vocabulary_size, self.prompt_len)
-        self.model.prefill(self.prompt)
+        self.prefill_ms = self.model.prefill(self.prompt)  # 64-position chunks on the tensor cores
         self.launches_per_step = self.model.resources()["kernels_per_decode_step"]
 
     def decode(self, k):
@@ -519,7 +519,9 @@ class DecodeWorkload(Workload):
                 "rotary_dim": self.spec.rotary_dim, "state_heads": self.spec.state_heads,
                 "state_key_heads": self.spec.state_key_heads, "formats": "Q4_K matrices, Q6_K embedding + LM head",
                 "kv_cache": "fp16" if self.kv == "fp16" else "packets: 4 Q4_K key + 4 Q6_K value blocks, 1416 B",
-                "prompt": self.prompt_len, "batch": 1, "tied_embeddings": False,
+                "prompt": self.prompt_len, "prefill_ms": getattr(self, "prefill_ms", None),
+                "prefill": "64-position chunks (tcgen05 products, per-row attention, sequential recurrent rows)",
+                "batch": 1, "tied_embeddings": False,
                 "l2": "per-token weight stream 1.1 GB > L2"}
 
     def cpu_baseline(self, budget_s):

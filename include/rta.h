@@ -306,7 +306,16 @@ enum {
   /* Keep the attention history as the reference's packets (per position kv_heads
    * Q4_K key blocks then kv_heads Q6_K value blocks, 1416 B at 4 x 256;
    * resident_history_quant.glsl:9-41) instead of fp16 K/V. */
-  RTA_MODEL_PACKET_HISTORY = 1
+  RTA_MODEL_PACKET_HISTORY = 1,
+  /* Prefill one prompt position per step (the decode step's kernels) instead of
+   * the default chunks of 64 positions.  A single-sequence handle prefills in
+   * chunks: the chunk's rows go through every matrix product as one batch (on
+   * the tensor cores, from panel-order copies of the Q4_K / Q6_K matrices made
+   * at open, about the weights' size again in HBM), the attention rows over
+   * the sequence's one history ring (each row its own causal window), and the
+   * recurrent layers row after row (Resident::prefill's batched forward,
+   * optical_resident.cpp:672-676, which forwards spans of its prefill batch). */
+  RTA_MODEL_TOKEN_PREFILL = 2
 };
 RTA_API rta_status rta_model_open_ex(const rta_model_spec* spec, const uint32_t* params, size_t n_params,
                                      const void* matrices, size_t matrix_bytes, const void* basis, size_t basis_bytes,

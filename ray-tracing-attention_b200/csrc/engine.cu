@@ -98,6 +98,12 @@ struct Layer {
   DevBuf<uint8_t> gate_s, up_s, down_s;  // tensor-parallel mode: this rank's slices (own copies)
   // dense (F32 / F16 / BF16) matrices that sat off a 16-byte boundary in the payload: aligned copies
   std::vector<std::unique_ptr<DevBuf<uint8_t>>> dense_copies;
+  // Prefill chunks of a single-sequence handle: panel-order copies of the packed
+  // matrices (a: QKV(+gate) / in-projection, b: o / out projection), so the
+  // chunk's rows run on the tensor cores; fmt -1 = none (the tiled / dense
+  // matrix serves the chunk on the GEMV).
+  DevBuf<uint8_t> pc_a, pc_b, pc_gate, pc_up, pc_down;
+  int pc_a_fmt = -1, pc_b_fmt = -1, pc_gate_fmt = -1, pc_down_fmt = -1;
 };
 
 struct Engine {
@@ -158,6 +164,17 @@ struct Engine {
   // the position it processes into cap = [depth + 1][capacity][D] (final rows first).
   cudaGraphExec_t g_prefill_cap = nullptr;
   DevBuf<float> cap;
+  // Chunked prefill (single-sequence handles): kChunk prompt positions per graph
+  // replay as kChunk rows -- products as one batch (tensor cores on the panel
+  // copies), attention rows over the one ring (each row sees its own causal
+  // window), the recurrent layers row after row (their state is sequential).
+  static constexpr uint32_t kChunk = 64, kChunkSplits = 2;
+  bool chunked = false, token_prefill = false;
+  cudaGraphExec_t g_chunk = nullptr;
+  uint32_t kernels_per_chunk = 0;
+  DevBuf<float> c_rows, c_proj, c_q, c_att, c_gdn, c_act, c_gu, c_pm, c_pz, c_po, c_gates, c_qk, c_vc;
+  DevBuf<uint32_t> c_rowctl;
+  DevBuf<uint8_t> c_tcws;
   // Step profile (rta_model_profile_step): while `profiling` is set, record_step
   // puts an event after every launch group of the step it records, labelled
   // with the group's kind and its algorithmic HBM bytes.
@@ -202,6 +219,7 @@ struct Engine {
     if (g_decode) cudaGraphExecDestroy(g_decode);
     if (g_prefill) cudaGraphExecDestroy(g_prefill);
     if (g_prefill_cap) cudaGraphExecDestroy(g_prefill_cap);
+    if (g_chunk) cudaGraphExecDestroy(g_chunk);
     if (ev0) cudaEventDestroy(ev0);
     if (ev1) cudaEventDestroy(ev1);
     if (ctrl_host) cudaFreeHost(ctrl_host);
@@ -317,14 +335,17 @@ struct Engine {
       int fmt;           // packed format of the payload (Q4_K / Q6_K)
       int* tiled_field;  // format field switched to the tiled code afterwards (null: shared with another job)
       uint32_t rows, cols;
+      DevBuf<uint8_t>* pc = nullptr;  // prefill-chunk panel copy (single-sequence handles)
+      int* pc_fmt = nullptr;
     };
     std::vector<Job> jobs;
     auto mut = [](const uint8_t* q) { return const_cast<uint8_t*>(q); };
     // Dense matrices keep their row-major layout (the dense GEMV streams rows);
     // the ones off a 16-byte boundary get an aligned copy.
-    auto add = [&](Layer& L, const uint8_t*& ptr, int fmt, int* field, uint32_t rows, uint32_t cols) {
+    auto add = [&](Layer& L, const uint8_t*& ptr, int fmt, int* field, uint32_t rows, uint32_t cols,
+                   DevBuf<uint8_t>* pc, int* pc_fmt) {
       if (!dense_format(fmt)) {
-        jobs.push_back({mut(ptr), fmt, field, rows, cols});
+        jobs.push_back({mut(ptr), fmt, field, rows, cols, pc, pc_fmt});
         return;
       }
       if (reinterpret_cast<uintptr_t>(ptr) % 16 == 0) return;
@@ -338,16 +359,16 @@ struct Engine {
       Layer& L = *layers[li];
       if (L.full) {
         const uint8_t* q = L.qkvg.p;
-        add(L, q, L.qkvg_fmt, &L.qkvg_fmt, L.qkvg_rows, D);
-        add(L, L.o, L.o_fmt, &L.o_fmt, D, Q());
+        add(L, q, L.qkvg_fmt, &L.qkvg_fmt, L.qkvg_rows, D, &L.pc_a, &L.pc_a_fmt);
+        add(L, L.o, L.o_fmt, &L.o_fmt, D, Q(), &L.pc_b, &L.pc_b_fmt);
       } else {
         const uint8_t* q = L.inproj.p;
-        add(L, q, L.inproj_fmt, &L.inproj_fmt, L.inproj_rows, D);
-        add(L, L.out, L.out_fmt, &L.out_fmt, D, S());
+        add(L, q, L.inproj_fmt, &L.inproj_fmt, L.inproj_rows, D, &L.pc_a, &L.pc_a_fmt);
+        add(L, L.out, L.out_fmt, &L.out_fmt, D, S(), &L.pc_b, &L.pc_b_fmt);
       }
-      add(L, L.gate, L.mlp_fmt, &L.mlp_fmt, F, D);
-      add(L, L.up, L.mlp_fmt, nullptr, F, D);  // up shares the gate's format field
-      add(L, L.down, L.down_fmt, &L.down_fmt, D, F);
+      add(L, L.gate, L.mlp_fmt, &L.mlp_fmt, F, D, &L.pc_gate, &L.pc_gate_fmt);
+      add(L, L.up, L.mlp_fmt, nullptr, F, D, &L.pc_up, nullptr);  // up shares the gate's format field
+      add(L, L.down, L.down_fmt, &L.down_fmt, D, F, &L.pc_down, &L.pc_down_fmt);
     }
     std::vector<std::pair<uintptr_t, size_t>> spans;
     size_t need = 0;
@@ -365,6 +386,13 @@ struct Engine {
     tmp.alloc(std::max<size_t>(need, 1));
     // gate and up share one format field: both take the panel order only together
     auto panel_ok = [&](uint32_t rows) { return tc && rows % 128u == 0u; };
+    if (chunked)  // panel copies for the prefill chunks, from the GGUF-order bytes (before tiling)
+      for (const Job& j : jobs) {
+        if (!j.pc || j.rows % 128u) continue;
+        j.pc->alloc(static_cast<size_t>(j.rows) * row_bytes(j.fmt, j.cols));
+        RTA_CUDA(launch_tile_tc(j.fmt, j.p, j.rows, j.cols, j.pc->p, stream));
+        if (j.pc_fmt) *j.pc_fmt = j.fmt + kPanelOffset;
+      }
     for (const Job& j : jobs) {
       const size_t bytes = static_cast<size_t>(j.rows) * row_bytes(j.fmt, j.cols);
       if (panel_ok(j.rows))
@@ -404,7 +432,9 @@ struct Engine {
             rta_team* tm = nullptr, const uint32_t* seq_starts = nullptr) {
     spec = sp;
     device = dev;
-    require((flags & ~static_cast<uint32_t>(RTA_MODEL_PACKET_HISTORY)) == 0, "unknown model flags", RTA_E_ARG);
+    require((flags & ~static_cast<uint32_t>(RTA_MODEL_PACKET_HISTORY | RTA_MODEL_TOKEN_PREFILL)) == 0,
+            "unknown model flags", RTA_E_ARG);
+    token_prefill = (flags & RTA_MODEL_TOKEN_PREFILL) != 0;
     packet_history = (flags & RTA_MODEL_PACKET_HISTORY) != 0;
     require(sequences >= 1 && sequences <= 256, "sequences must be 1..256", RTA_E_ARG);
     nseq = sequences;
@@ -539,6 +569,7 @@ struct Engine {
     }
     RTA_CUDA(cudaStreamSynchronize(stream));
     tc = nseq >= kTcMinSeq;
+    chunked = nseq == 1 && !team && !token_prefill;
     tile_matrices();
 
     // activations and state, one row per sequence
@@ -592,6 +623,29 @@ struct Engine {
     part_m.alloc(recs);
     part_z.alloc(recs);
     part_o.alloc(recs * hd);
+    if (chunked) {
+      const size_t C = kChunk;
+      c_rows.alloc(C * D);
+      c_proj.alloc(C * projw);
+      c_q.alloc(C * Q());
+      c_att.alloc(C * Q());
+      c_gdn.alloc(C * std::max(1u, S()));
+      c_act.alloc(C * F());
+      c_gu.alloc(C * 2 * F());
+      const size_t crecs = C * spec.kv_heads * kChunkSplits * 4;
+      c_pm.alloc(crecs);
+      c_pz.alloc(crecs);
+      c_po.alloc(crecs * hd);
+      c_rowctl.alloc(2 * C);
+      c_gates.alloc(C * std::max(1u, spec.state_heads) * 2);
+      c_qk.alloc(C * std::max(1u, spec.state_heads) * 2 * 128);
+      c_vc.alloc(C * std::max(1u, spec.state_heads) * 128);
+      size_t ws = 0;
+      for (uint32_t cols : {D, Q(), std::max(1u, S()), F()})
+        if (cols % 256 == 0)
+          ws = std::max({ws, tc_workspace_bytes(kQ4KPanel, kChunk, cols), tc_workspace_bytes(kQ6KPanel, kChunk, cols)});
+      c_tcws.alloc(ws);
+    }
     // [layer][sequence] x per-sequence blocks
     pbytes = packet_bytes(spec.kv_heads);
     if (packet_history) {
@@ -628,8 +682,9 @@ struct Engine {
   }
 
   // One product: panel formats run on the tensor cores, the others on the GEMV.
-  cudaError_t matmul(const GemvArgs& a, cudaStream_t s) {
+  cudaError_t matmul(const GemvArgs& a, cudaStream_t s, DevBuf<uint8_t>* ws = nullptr) {
     if (a.fmt != kQ4KPanel && a.fmt != kQ6KPanel) return launch_gemv(a, s);
+    if (!ws) ws = &tc_ws;
     TcGemmArgs t;
     t.fmt = a.fmt;
     t.w0 = a.w0;
@@ -652,8 +707,8 @@ struct Engine {
     t.err = a.err;
     t.running = a.running;
     t.running_step = a.running_step;
-    t.xb = tc_ws.p;
-    t.xb_bytes = tc_ws.n;
+    t.xb = ws->p;
+    t.xb_bytes = ws->n;
     t.pdl = a.pdl;
     return launch_tc_gemm(t, s);
   }
@@ -663,34 +718,36 @@ struct Engine {
   // write the raw gate | up rows to gu instead; a panel-format down then applies
   // SwiGLU in its own prep unless the caller wants the activation rows too,
   // otherwise they are formed from gu first.
-  void mlp_pair(GemvArgs g, GemvArgs dn, bool need_act, cudaStream_t s) {
+  void mlp_pair(GemvArgs g, GemvArgs dn, bool need_act, cudaStream_t s, float* gu_rows = nullptr,
+                DevBuf<uint8_t>* ws = nullptr) {
     const uint32_t F = g.rows;
+    if (!gu_rows) gu_rows = gu.p;
     const bool gpanel = g.fmt == kQ4KPanel || g.fmt == kQ6KPanel;
     const bool dpanel = dn.fmt == kQ4KPanel || dn.fmt == kQ6KPanel;
     if (!gpanel) {
       RTA_CUDA(launch_gemv(g, s));
       mark(RTA_PROF_GATE_UP, product_bytes(g), s);
-      RTA_CUDA(matmul(dn, s));
+      RTA_CUDA(matmul(dn, s, ws));
       mark(RTA_PROF_DOWN, product_bytes(dn), s);
       return;
     }
     float* act_rows = g.y;
     const uint32_t act_stride = g.y_stride ? g.y_stride : F;
     g.epilogue = kStore;
-    g.y = gu.p;
+    g.y = gu_rows;
     g.y_stride = 2 * F;  // matrix 1 (up) rows follow matrix 0 (gate) rows
-    RTA_CUDA(matmul(g, s));
+    RTA_CUDA(matmul(g, s, ws));
     mark(RTA_PROF_GATE_UP, product_bytes(g), s);
     if (dpanel && !need_act) {
       dn.prologue = kSwiGLUIn;
-      dn.x = gu.p;
-      dn.z = gu.p + F;
+      dn.x = gu_rows;
+      dn.z = gu_rows + F;
       dn.x_stride = 2 * F;
       dn.z_stride = 2 * F;
     } else {
-      RTA_CUDA(launch_swiglu_rows(gu.p, g.batch, F, 2 * F, act_rows, act_stride, s));
+      RTA_CUDA(launch_swiglu_rows(gu_rows, g.batch, F, 2 * F, act_rows, act_stride, s));
     }
-    RTA_CUDA(matmul(dn, s));
+    RTA_CUDA(matmul(dn, s, ws));
     mark(RTA_PROF_DOWN, product_bytes(dn), s);
   }
 
@@ -1002,7 +1059,227 @@ struct Engine {
     return n;
   }
 
+  // One prefill chunk of a single-sequence handle: kChunk consecutive prompt
+  // positions from the control block's pos_next (rows past the prompt sit out).
+  uint32_t record_chunk() {
+    const cudaStream_t s = stream;
+    uint32_t n = 0;
+    Control* c = ctrl.p;
+    const uint32_t D = this->D(), F = this->F(), hd = spec.attention_head_dim, C = kChunk;
+    const uint32_t* rpos = c_rowctl.p;       // row r: position at rpos[2r]
+    const uint32_t* rlive = c_rowctl.p + 1;  // row r: live at rlive[2r]
+    ChunkParams cp;
+    cp.table = embed;
+    cp.fmt = embed_fmt;
+    cp.D = D;
+    cp.row_bytes = static_cast<uint32_t>(row_bytes(embed_fmt, D));
+    cp.vocab = spec.vocabulary_size;
+    cp.C = C;
+    cp.ctrl = c;
+    cp.prompt = prompt.p;
+    cp.rowctl = c_rowctl.p;
+    cp.rows = c_rows.p;
+    cp.state = state.p;
+    RTA_CUDA(launch_chunk_begin(cp, s, true));
+    ++n;
+    // the chunk's products: the panel copy when the matrix has one, else the decode matrix
+    auto product = [&](const uint8_t* pc, int pc_fmt, const uint8_t* w, int fmt) {
+      GemvArgs a;
+      a.fmt = pc_fmt >= 0 ? pc_fmt : fmt;
+      a.w0 = pc_fmt >= 0 ? pc : w;
+      a.batch = C;
+      a.running = rlive;
+      a.running_step = 2;
+      a.err = &c->err;
+      a.pdl = true;
+      return a;
+    };
+    for (size_t li = 0; li < layers.size(); ++li) {
+      Layer& L = *layers[li];
+      if (L.full) {
+        GemvArgs g = product(L.pc_a.p, L.pc_a_fmt, L.qkvg.p, L.qkvg_fmt);
+        g.rows = L.qkvg_rows;
+        g.cols = D;
+        g.x = c_rows.p;
+        g.x_stride = D;
+        g.prologue = kRmsNorm;
+        g.norm_w = L.attn_norm;
+        g.eps = spec.norm_epsilon;
+        g.y = c_proj.p;
+        g.y_stride = projw;
+        RTA_CUDA(matmul(g, s, &c_tcws));
+        PrepParams pp;
+        pp.qkvg = c_proj.p;
+        pp.qnorm = L.qnorm;
+        pp.knorm = L.knorm;
+        pp.inv_freq = inv_freq.p;
+        pp.eps = spec.norm_epsilon;
+        pp.heads = spec.attention_heads;
+        pp.kvh = spec.kv_heads;
+        pp.hd = hd;
+        pp.group = spec.attention_heads / spec.kv_heads;
+        pp.rotary = spec.rotary_dim;
+        pp.qk_norm = spec.qk_norm;
+        pp.q_width = Q();
+        pp.kv_width = KVW();
+        pp.qout = c_q.p;
+        const size_t layer_kv = static_cast<size_t>(spec.kv_heads) * capacity * hd;  // one sequence
+        pp.kcache = kcache.p + L.fi * layer_kv;
+        pp.vcache = vcache.p + L.fi * layer_kv;
+        pp.capacity = capacity;
+        pp.pos = rpos;
+        pp.running = rlive;
+        pp.nseq = C;
+        pp.ctrl_step = 2;
+        pp.qkvg_seq = projw;
+        pp.ring_seq = 0;  // every row writes the sequence's one ring
+        if (packet_history) pp.packets = pring.p + L.fi * static_cast<size_t>(capacity) * pbytes;
+        RTA_CUDA(launch_attn_prep(pp, s, true));
+        AttnParams ap;
+        ap.q = c_q.p;
+        ap.k = pp.kcache;
+        ap.v = pp.vcache;
+        ap.q_seq_stride = Q();
+        ap.seq_stride = 0;
+        if (packet_history) {
+          ap.packets = pp.packets;
+          ap.packet_seq_stride = 0;
+          ap.packet_stride = pbytes;
+        }
+        ap.kv_stride = static_cast<size_t>(capacity) * hd;
+        ap.pos_stride = hd;
+        ap.heads = spec.attention_heads;
+        ap.kvh = spec.kv_heads;
+        ap.hd = hd;
+        ap.capacity = capacity;
+        ap.pos = rpos;
+        ap.ctrl_step = 2;
+        ap.gate = L.gated ? c_proj.p + Q() + 2 * KVW() : nullptr;
+        ap.gate_seq_stride = projw;
+        ap.out = c_att.p;
+        ap.out_seq_stride = Q();
+        ap.rotary_out = L.rotary_out;
+        ap.part_m = c_pm.p;
+        ap.part_z = c_pz.p;
+        ap.part_o = c_po.p;
+        ap.err = &c->err;
+        ap.running = rlive;
+        RTA_CUDA(launch_attention(ap, kChunkSplits, C, true, s));
+        GemvArgs o = product(L.pc_b.p, L.pc_b_fmt, L.o, L.o_fmt);
+        o.rows = D;
+        o.cols = Q();
+        o.x = c_att.p;
+        o.x_stride = Q();
+        o.epilogue = kAccumulate;
+        o.y = c_rows.p;
+        o.y_stride = D;
+        RTA_CUDA(matmul(o, s, &c_tcws));
+        n += 5;
+      } else {
+        GemvArgs g = product(L.pc_a.p, L.pc_a_fmt, L.inproj.p, L.inproj_fmt);
+        g.rows = L.inproj_rows;
+        g.cols = D;
+        g.x = c_rows.p;
+        g.x_stride = D;
+        g.prologue = kRmsNorm;
+        g.norm_w = L.attn_norm;
+        g.eps = spec.norm_epsilon;
+        g.y = c_proj.p;
+        g.y_stride = projw;
+        RTA_CUDA(matmul(g, s, &c_tcws));
+        ++n;
+        // the recurrent rows: a parallel pre-pass (gates, convolution, norms of
+        // every row), then a scan of the rows in order on register-held state
+        GdnChunkParams gc;
+        GdnParams& gp = gc.g;
+        gp.x = c_rows.p;
+        gp.attn_norm = L.gate_w.p + 2ull * spec.state_heads * D;
+        gp.eps = spec.norm_epsilon;
+        gp.wa = L.wa;
+        gp.wb = L.wb;
+        gp.a_log = L.a_log;
+        gp.dt_bias = L.dt_bias;
+        gp.proj = c_proj.p;
+        gp.proj_seq = projw;
+        gp.conv_w = L.conv_w;
+        gp.conv_seq = static_cast<size_t>(2) * 3 * S() * 3;
+        gp.rec_seq = static_cast<size_t>(spec.state_heads) * 128 * 128;
+        gp.conv_state = conv.p + static_cast<size_t>(L.ri) * gp.conv_seq;
+        gp.rec = rec.p + static_cast<size_t>(L.ri) * gp.rec_seq;
+        gp.out = c_gdn.p;
+        gp.D = D;
+        gp.H = spec.state_heads;
+        gp.KH = spec.state_key_heads;
+        gp.err = &c->err;
+        gc.rowctl = c_rowctl.p;
+        gc.C = C;
+        gc.gates = c_gates.p;
+        gc.qk = c_qk.p;
+        gc.vc = c_vc.p;
+        RTA_CUDA(launch_gdn_chunk(gc, s, true));
+        n += 2;
+        GemvArgs o = product(L.pc_b.p, L.pc_b_fmt, L.out, L.out_fmt);
+        o.rows = D;
+        o.cols = S();
+        o.x = c_gdn.p;
+        o.x_stride = S();
+        o.prologue = kHeadGate;
+        o.z = c_proj.p + 2 * K() + S();
+        o.z_stride = projw;
+        o.norm_w = L.ssm_norm;
+        o.eps = spec.norm_epsilon;
+        o.epilogue = kAccumulate;
+        o.y = c_rows.p;
+        o.y_stride = D;
+        RTA_CUDA(matmul(o, s, &c_tcws));
+        ++n;
+      }
+      GemvArgs gu = product(L.pc_gate.p, L.pc_gate_fmt, L.gate, L.mlp_fmt);
+      gu.w1 = L.pc_gate_fmt >= 0 ? L.pc_up.p : L.up;
+      gu.rows = F;
+      gu.cols = D;
+      gu.x = c_rows.p;
+      gu.x_stride = D;
+      gu.prologue = kRmsNorm;
+      gu.norm_w = L.post_norm;
+      gu.eps = spec.norm_epsilon;
+      gu.epilogue = kSwiGLU;
+      gu.y = c_act.p;
+      gu.y_stride = F;
+      GemvArgs dn = product(L.pc_down.p, L.pc_down_fmt, L.down, L.down_fmt);
+      dn.rows = D;
+      dn.cols = F;
+      dn.x = c_act.p;
+      dn.x_stride = F;
+      dn.epilogue = kAccumulate;
+      dn.y = c_rows.p;
+      dn.y_stride = D;
+      mlp_pair(gu, dn, false, s, c_gu.p, &c_tcws);
+      n += 2;
+    }
+    RTA_CUDA(launch_chunk_end(cp, s, true));
+    return n + 1;
+  }
+
   void capture() {
+    if (chunked) {
+      cudaGraph_t graph = nullptr;
+      RTA_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeRelaxed));
+      try {
+        record_chunk();
+      } catch (...) {
+        cudaStreamEndCapture(stream, &graph);
+        if (graph) cudaGraphDestroy(graph);
+        throw;
+      }
+      RTA_CUDA(cudaStreamEndCapture(stream, &graph));
+      size_t nodes = 0;
+      cudaGraphGetNodes(graph, nullptr, &nodes);
+      kernels_per_chunk = static_cast<uint32_t>(nodes);
+      const cudaError_t e = cudaGraphInstantiate(&g_chunk, graph, 0);
+      cudaGraphDestroy(graph);
+      RTA_CUDA(e);
+    }
     for (int mode = 0; mode < 2; ++mode) {
       uint32_t n = 0;
       cudaGraphExec_t exec = instantiate_step(mode == 1, false, &n);
@@ -1133,7 +1410,8 @@ struct Engine {
 
   // Prefill every sequence in lockstep: replay i feeds prompt id i of each
   // sequence that has one; a sequence with a shorter prompt sits out the rest.
-  void prefill_batch(const uint32_t* ids, const uint32_t* lengths, uint32_t stride, const uint32_t st[2]) {
+  void prefill_batch(const uint32_t* ids, const uint32_t* lengths, uint32_t stride, const uint32_t st[2],
+                     bool allow_chunks = true) {
     uint32_t longest = 0;
     for (uint32_t z = 0; z < nseq; ++z) {
       require(lengths[z] <= capacity && lengths[z] <= stride, "prefill length must be at most capacity", RTA_E_ARG);
@@ -1159,7 +1437,10 @@ struct Engine {
     }
     write_headers();
     RTA_CUDA(cudaEventRecord(ev0, stream));
-    for (uint32_t i = 0; i < longest; ++i) RTA_CUDA(cudaGraphLaunch(g_prefill, stream));
+    if (chunked && g_chunk && allow_chunks)  // kChunk prompt positions per replay
+      for (uint32_t i = 0; i < longest; i += kChunk) RTA_CUDA(cudaGraphLaunch(g_chunk, stream));
+    else
+      for (uint32_t i = 0; i < longest; ++i) RTA_CUDA(cudaGraphLaunch(g_prefill, stream));
     RTA_CUDA(cudaEventRecord(ev1, stream));
     read_control();
     float ms = 0.f;
@@ -1181,7 +1462,7 @@ struct Engine {
     }
     std::swap(g_prefill, g_prefill_cap);  // prefill_batch replays g_prefill
     try {
-      prefill_batch(ids, &n, n, st);
+      prefill_batch(ids, &n, n, st, false);
     } catch (...) {
       std::swap(g_prefill, g_prefill_cap);
       throw;

@@ -125,6 +125,55 @@ __global__ void __launch_bounds__(256) embed_kernel(EmbedParams p) {
   }
 }
 
+// ----------------------------------------------------------- prefill chunk
+__device__ __forceinline__ float embed_value(const ChunkParams& p, const uint8_t* row, uint32_t i) {
+  if (p.fmt == kF32) return reinterpret_cast<const float*>(row)[i];
+  if (p.fmt == kF16 || p.fmt == kBF16) {
+    const uint32_t h = reinterpret_cast<const uint16_t*>(row)[i];
+    return p.fmt == kF16 ? half_bits_to_float(h) : __uint_as_float(h << 16);
+  }
+  const uint8_t* blk = row + (i / 256u) * (p.fmt == kQ4K ? 144u : 210u);
+  return p.fmt == kQ4K ? q4k_row_value(blk, i % 256u) : q6k_row_value(blk, i % 256u);
+}
+// CTA r: row r of the chunk.
+__global__ void __launch_bounds__(256) chunk_begin_kernel(ChunkParams p) {
+  pdl_wait();
+  pdl_launch_dependents();
+  __shared__ uint32_t token_s, live_s;
+  const uint32_t r = blockIdx.x;
+  if (threadIdx.x == 0) {
+    const uint32_t pos = p.ctrl->pos_next + r;
+    uint32_t live = p.ctrl->running && pos < p.ctrl->prompt_len ? 1u : 0u;
+    const uint32_t token = live ? p.prompt[pos] : 0u;
+    if (live && token >= p.vocab) {
+      atomicOr(&p.ctrl->err, RTA_DEVERR_TOKEN);
+      live = 0u;
+    }
+    p.rowctl[2u * r] = pos;
+    p.rowctl[2u * r + 1u] = live;
+    token_s = token;
+    live_s = live;
+  }
+  __syncthreads();
+  float* dst = p.rows + static_cast<size_t>(r) * p.D;
+  const uint8_t* row = p.table + static_cast<size_t>(token_s) * p.row_bytes;
+  for (uint32_t i = threadIdx.x; i < p.D; i += blockDim.x) dst[i] = live_s ? embed_value(p, row, i) : 0.f;
+}
+__global__ void __launch_bounds__(256) chunk_end_kernel(ChunkParams p) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const uint32_t next = p.ctrl->pos_next, plen = p.ctrl->prompt_len;
+  const uint32_t live = p.ctrl->running && next < plen ? min(p.C, plen - next) : 0u;
+  if (live == 0u) return;
+  const float* src = p.rows + static_cast<size_t>(live - 1u) * p.D;
+  for (uint32_t i = threadIdx.x; i < p.D; i += blockDim.x) p.state[i] = src[i];
+  __syncthreads();  // every thread has read the control words above
+  if (threadIdx.x == 0) {
+    p.ctrl->pos_cur = next + live - 1u;
+    p.ctrl->pos_next = next + live;
+  }
+}
+
 // ------------------------------------------------------------ attn prep
 // Op 14 (per-head RMS QK-norm, resident_math.comp:113-114), op 3 (RoPE on
 // adjacent pairs with coordinatePhase, :76-77, resident_common.glsl:117) and
@@ -165,7 +214,7 @@ __global__ void __launch_bounds__(256) attn_prep_kernel(PrepParams p) {
   }
   if (p.packets && !is_q) {  // op 34: pack this KV head's K (Q4_K) and V (Q6_K) into the position's packet
     __shared__ PackScratch sh;
-    const size_t row = static_cast<size_t>(z) * p.capacity + pos % p.capacity;
+    const size_t row = static_cast<size_t>(z * p.ring_seq) * p.capacity + pos % p.capacity;
     uint8_t* pkt = p.packets + row * packet_bytes(p.kvh);
     pack_q4k_block(x, pkt + head * kPacketKeyBytes, sh);
     pack_q6k_block(qkvg[p.q_width + p.kv_width + head * hd + d],
@@ -177,7 +226,7 @@ __global__ void __launch_bounds__(256) attn_prep_kernel(PrepParams p) {
     p.qout[(static_cast<size_t>(z) * p.heads + head) * hd + d] = x;
   } else {
     const size_t slot = static_cast<size_t>(pos % p.capacity);
-    const size_t at = ((static_cast<size_t>(z) * p.kvh + head) * p.capacity + slot) * hd + d;
+    const size_t at = ((static_cast<size_t>(z * p.ring_seq) * p.kvh + head) * p.capacity + slot) * hd + d;
     p.kcache[at] = __float2half_rn(x);
     const float v = qkvg[p.q_width + p.kv_width + head * hd + d];
     p.vcache[at] = __float2half_rn(v);
@@ -464,6 +513,171 @@ __global__ void __launch_bounds__(256) capture_row_kernel(CaptureParams p) {
   for (uint32_t i = threadIdx.x; i < p.D; i += blockDim.x) dst[i] = p.state[i] * inv * p.norm_w[i];
 }
 
+// -------------------------------------------------- chunked recurrent layer
+// Pre-pass, CTA (head h, row r): ops 18 (gates from the RMS-normed row), 19
+// (4-tap causal convolution + SiLU of the head's q, k and v channels; the taps
+// before row r are rows r-3..r-1 of the chunk or, for the first rows, the conv
+// history of the chunk's first position) and 20 (L2 norms).
+__global__ void __launch_bounds__(256) gdn_chunk_pre_kernel(GdnChunkParams cp) {
+  const GdnParams& p = cp.g;
+  __shared__ float red1[8], red2[16], red3[16];
+  const uint32_t h = blockIdx.x, r = blockIdx.y, tid = threadIdx.x;
+  const uint32_t HD = 128u, S = p.H * HD, K = p.KH * HD, kh = h % p.KH;
+  pdl_wait();
+  pdl_launch_dependents();
+  const uint32_t pos0 = cp.rowctl[0];
+  if (!cp.rowctl[2u * r + 1u]) return;  // past the prompt
+  const float* x = p.x + static_cast<size_t>(r) * p.D;
+  const size_t buf = static_cast<size_t>(3u) * S * 3u;
+  const float* hist = p.conv_state + (pos0 & 1u) * buf;  // taps before the chunk's first position
+  // ---- op 18
+  float ss[1] = {0.f};
+  for (uint32_t c = tid; c < p.D; c += 256u) ss[0] += x[c] * x[c];
+  block_sums<1>(ss, red1);
+  const float inv = rsqrtf(ss[0] / static_cast<float>(p.D) + p.eps);
+  float ab[2] = {0.f, 0.f};
+  for (uint32_t c = tid; c < p.D; c += 256u) {
+    const float xn = x[c] * inv * p.attn_norm[c];
+    ab[0] += xn * p.wa[static_cast<size_t>(h) * p.D + c];
+    ab[1] += xn * p.wb[static_cast<size_t>(h) * p.D + c];
+  }
+  block_sums<2>(ab, red2);
+  if (tid == 0) {
+    cp.gates[(static_cast<size_t>(r) * p.H + h) * 2u] = expf(-expf(p.a_log[h]) * softplus(ab[0] + p.dt_bias[h]));
+    cp.gates[(static_cast<size_t>(r) * p.H + h) * 2u + 1u] = detector_sigmoid(ab[1]);
+  }
+  // ---- op 19: this thread's q (tid < 128) or k channel, and (tid < 128) a v channel
+  auto raw_of = [&](uint32_t row, uint32_t coord) {  // raw projection of a conv channel at chunk row `row`
+    const float* pr = p.proj + static_cast<size_t>(row) * p.proj_seq;
+    return coord < S ? pr[kh * HD + (coord - h * HD)]
+         : coord < 2u * S ? pr[K + kh * HD + (coord - S - h * HD)]
+                          : pr[2u * K + (coord - 2u * S)];
+  };
+  auto conv_at = [&](uint32_t coord) {
+    const float4 w = *reinterpret_cast<const float4*>(p.conv_w + static_cast<size_t>(coord) * 4u);
+    float t[3];
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {  // taps t[j] = position (first row of this row) - 3 + j
+      const int at = static_cast<int>(r) - 3 + j;
+      t[j] = at >= 0 ? raw_of(static_cast<uint32_t>(at), coord) : hist[coord * 3u + static_cast<uint32_t>(3 + at)];
+    }
+    float signal = 0.f;
+    signal = signal + t[0] * w.x;
+    signal = signal + t[1] * w.y;
+    signal = signal + t[2] * w.z;
+    signal = signal + raw_of(r, coord) * w.w;
+    return signal * detector_sigmoid(signal);
+  };
+  const uint32_t qk_coord = tid < 128u ? h * HD + tid : S + h * HD + (tid - 128u);
+  const float f = conv_at(qk_coord);
+  float vcv = 0.f;
+  if (tid < 128u) vcv = conv_at(2u * S + h * HD + tid);
+  // ---- op 20
+  float qk2[2] = {tid < 128u ? f * f : 0.f, tid >= 128u ? f * f : 0.f};
+  block_sums<2>(qk2, red3);
+  float* qk = cp.qk + (static_cast<size_t>(r) * p.H + h) * 2u * HD;
+  if (tid < 128u) {
+    qk[tid] = (f * rsqrtf(qk2[0] + p.eps)) / sqrtf(128.0f);
+    cp.vc[(static_cast<size_t>(r) * p.H + h) * HD + tid] = vcv;
+  } else {
+    qk[HD + (tid - 128u)] = f * rsqrtf(qk2[1] + p.eps);
+  }
+}
+
+// Scan, CTA (head h, 16 value rows): op 21 row after row, the state rows in
+// registers (lane owns keys 2l, 2l+1, 2l+64, 2l+65 as in the decode kernel);
+// no block-wide barrier inside the walk, the next row's q / k are loaded while
+// the current one is applied.
+__global__ void __launch_bounds__(256) gdn_chunk_scan_kernel(GdnChunkParams cp) {
+  const GdnParams& p = cp.g;
+  constexpr uint32_t kRows = kGdnRowsSmall, kPerWarp = kRows / 8u;
+  const uint32_t h = blockIdx.x, slice = blockIdx.y, tid = threadIdx.x;
+  const uint32_t HD = 128u, S = p.H * HD, warp = tid >> 5, lane = tid & 31u;
+  float* st = p.rec + static_cast<size_t>(h) * HD * HD;
+  float2 s0[kPerWarp], s1[kPerWarp];
+#pragma unroll
+  for (uint32_t i = 0; i < kPerWarp; ++i) {
+    const float* row = st + static_cast<size_t>(slice * kRows + warp * kPerWarp + i) * HD;
+    s0[i] = *reinterpret_cast<const float2*>(row + 2 * lane);
+    s1[i] = *reinterpret_cast<const float2*>(row + 2 * lane + 64);
+  }
+  pdl_wait();
+  pdl_launch_dependents();
+  uint32_t nlive = 0;
+  for (uint32_t i = 0; i < cp.C; ++i) nlive += cp.rowctl[2u * i + 1u];
+  auto load_row = [&](uint32_t r, float4& q, float4& k, float2& g, float (&v)[kPerWarp]) {
+    const float* qk = cp.qk + (static_cast<size_t>(r) * p.H + h) * 2u * HD;
+    const float2 qa = *reinterpret_cast<const float2*>(qk + 2 * lane), qb = *reinterpret_cast<const float2*>(qk + 2 * lane + 64);
+    const float2 ka = *reinterpret_cast<const float2*>(qk + HD + 2 * lane),
+                 kb = *reinterpret_cast<const float2*>(qk + HD + 2 * lane + 64);
+    q = make_float4(qa.x, qa.y, qb.x, qb.y);
+    k = make_float4(ka.x, ka.y, kb.x, kb.y);
+    g = *reinterpret_cast<const float2*>(cp.gates + (static_cast<size_t>(r) * p.H + h) * 2u);
+#pragma unroll
+    for (uint32_t i = 0; i < kPerWarp; ++i)
+      v[i] = cp.vc[(static_cast<size_t>(r) * p.H + h) * HD + slice * kRows + warp * kPerWarp + i];
+  };
+  float4 q, k, qn, kn;
+  float2 g, gn;
+  float v[kPerWarp], vn[kPerWarp];
+  if (nlive) load_row(0, q, k, g, v);
+  for (uint32_t r = 0; r < nlive; ++r) {
+    if (r + 1u < nlive) load_row(r + 1u, qn, kn, gn, vn);  // in flight while row r is applied
+    const float decay = g.x, beta = g.y;
+#pragma unroll
+    for (uint32_t i = 0; i < kPerWarp; ++i) {
+      float2 a = s0[i], b = s1[i];
+      a.x *= decay;
+      a.y *= decay;
+      b.x *= decay;
+      b.y *= decay;
+      const float received = signed_product_sum(k.x, k.y, k.z, k.w, a.x, a.y, b.x, b.y);
+      const float delta = (v[i] - received) * beta;
+      a.x += k.x * delta;
+      a.y += k.y * delta;
+      b.x += k.z * delta;
+      b.y += k.w * delta;
+      const float o = signed_product_sum(q.x, q.y, q.z, q.w, a.x, a.y, b.x, b.y);
+      s0[i] = a;
+      s1[i] = b;
+      if (lane == 0)
+        p.out[static_cast<size_t>(r) * S + h * HD + slice * kRows + warp * kPerWarp + i] = o;
+    }
+    q = qn, k = kn, g = gn;
+#pragma unroll
+    for (uint32_t i = 0; i < kPerWarp; ++i) v[i] = vn[i];
+  }
+#pragma unroll
+  for (uint32_t i = 0; i < kPerWarp; ++i) {
+    float* row = st + static_cast<size_t>(slice * kRows + warp * kPerWarp + i) * HD;
+    *reinterpret_cast<float2*>(row + 2 * lane) = s0[i];
+    *reinterpret_cast<float2*>(row + 2 * lane + 64) = s1[i];
+  }
+  // The conv history of the position after the chunk: the three newest raw
+  // rows of head h's q, k and v channels (slice 0 of the head; each channel is
+  // read and then written by one thread, so the parity buffer may be the one
+  // the chunk started from).
+  if (slice == 0u && nlive) {
+    const uint32_t K = p.KH * HD, kh = h % p.KH, pos0 = cp.rowctl[0];
+    const size_t buf = static_cast<size_t>(3u) * S * 3u;
+    const float* hist = p.conv_state + (pos0 & 1u) * buf;
+    float* next = p.conv_state + ((pos0 + nlive) & 1u) * buf;
+    for (uint32_t c = tid; c < 3u * HD; c += 256u) {
+      const uint32_t part = c / HD, i = c % HD, coord = part * S + h * HD + i;
+      const uint32_t raw_at = part == 0u ? kh * HD + i : part == 1u ? K + kh * HD + i : 2u * K + h * HD + i;
+      float t[3];
+#pragma unroll
+      for (int j = 0; j < 3; ++j) {  // taps = positions (last live) - 2 + j
+        const int at = static_cast<int>(nlive) - 3 + j;
+        t[j] = at >= 0 ? p.proj[static_cast<size_t>(at) * p.proj_seq + raw_at]
+                       : hist[coord * 3u + static_cast<uint32_t>(3 + at)];
+      }
+#pragma unroll
+      for (int j = 0; j < 3; ++j) next[coord * 3u + j] = t[j];
+    }
+  }
+}
+
 // Row gather used at load time (rotary row permutations, concatenations).
 __global__ void gather_rows_kernel(const uint8_t* __restrict__ src, const uint32_t* __restrict__ map, uint32_t rows,
                                    uint32_t row_bytes, uint8_t* __restrict__ dst) {
@@ -497,6 +711,16 @@ cudaError_t launch_capture_row(const CaptureParams& p, cudaStream_t s, bool pdl)
   if (!p.state || !p.dst || !p.ctrl || p.D == 0) return cudaErrorInvalidValue;
   void* args[] = {const_cast<CaptureParams*>(&p)};
   return launch_pdl(reinterpret_cast<const void*>(capture_row_kernel), dim3(1), dim3(256), args, s, pdl);
+}
+cudaError_t launch_chunk_begin(const ChunkParams& p, cudaStream_t s, bool pdl) {
+  if (!p.table || !p.ctrl || !p.prompt || !p.rowctl || !p.rows || p.C == 0) return cudaErrorInvalidValue;
+  void* args[] = {const_cast<ChunkParams*>(&p)};
+  return launch_pdl(reinterpret_cast<const void*>(chunk_begin_kernel), dim3(p.C), dim3(256), args, s, pdl);
+}
+cudaError_t launch_chunk_end(const ChunkParams& p, cudaStream_t s, bool pdl) {
+  if (!p.ctrl || !p.rows || !p.state || p.C == 0) return cudaErrorInvalidValue;
+  void* args[] = {const_cast<ChunkParams*>(&p)};
+  return launch_pdl(reinterpret_cast<const void*>(chunk_end_kernel), dim3(1), dim3(256), args, s, pdl);
 }
 cudaError_t launch_attn_prep(const PrepParams& p, cudaStream_t s, bool pdl) {
   if (p.hd > 256 || (p.packets && p.hd != 256)) return cudaErrorInvalidValue;  // a packet block is 256 values
@@ -536,6 +760,16 @@ cudaError_t launch_gdn(const GdnParams& p, cudaStream_t s, bool pdl) {
   }
   return launch_pdl(reinterpret_cast<const void*>(gdn_kernel<kGdnRowsSmall>),
                     dim3(p.H, 128u / kGdnRowsSmall, p.nseq), dim3(256), args, s, pdl);
+}
+cudaError_t launch_gdn_chunk(const GdnChunkParams& p, cudaStream_t s, bool pdl) {
+  if (p.g.D == 0 || p.g.D > 256u * kGdnDPer || p.C == 0 || !p.rowctl || !p.gates || !p.qk || !p.vc)
+    return cudaErrorInvalidValue;
+  void* args[] = {const_cast<GdnChunkParams*>(&p)};
+  cudaError_t e = launch_pdl(reinterpret_cast<const void*>(gdn_chunk_pre_kernel), dim3(p.g.H, p.C), dim3(256), args,
+                             s, pdl);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(reinterpret_cast<const void*>(gdn_chunk_scan_kernel), dim3(p.g.H, 128u / kGdnRowsSmall),
+                    dim3(256), args, s, true);
 }
 cudaError_t launch_gather_rows(const uint8_t* src, const uint32_t* map, uint32_t rows, uint32_t row_bytes,
                                uint8_t* dst, cudaStream_t s) {

@@ -55,6 +55,24 @@ struct PrepParams {
   // non-null: append the reference's history packet (kvh Q4_K keys + kvh Q6_K
   // values, packet_bytes(kvh) per position) to this ring instead of fp16 K/V
   uint8_t* packets = nullptr;         // this layer: [nseq][capacity][packet]
+  // 1: sequence z writes ring z; 0: every z writes the one ring (the rows of a
+  // prefill chunk are consecutive positions of one sequence)
+  uint32_t ring_seq = 1;
+};
+
+// Prefill chunk (C consecutive prompt positions of one sequence as C rows):
+// chunk_begin embeds prompt ids pos_next .. pos_next + C - 1 into rows and writes
+// each row's (position, live) pair; chunk_end copies the last live row into the
+// sequence's residual row and advances its positions.
+struct ChunkParams {
+  const uint8_t* table = nullptr;  // token_embd rows
+  int fmt = 14;
+  uint32_t D = 0, row_bytes = 0, vocab = 0, C = 0;
+  Control* ctrl = nullptr;            // the sequence's control block
+  const uint32_t* prompt = nullptr;   // prompt ids by absolute position
+  uint32_t* rowctl = nullptr;         // [C][2]: position, live
+  float* rows = nullptr;              // [C][D] residual rows of the chunk
+  float* state = nullptr;             // [D] the sequence's residual row
 };
 
 struct GdnParams {
@@ -93,7 +111,24 @@ struct CaptureParams {
   uint32_t D = 0, capacity = 0;
 };
 
+// The recurrent layer over the rows of a prefill chunk (consecutive positions of
+// one sequence): a parallel pre-pass forms every row's gates, convolved and
+// normalised q / k and convolved v (nothing there depends on the recurrent
+// state: the convolution reads earlier rows' raw projections), then a scan
+// walks the rows in order on each CTA's value rows held in registers.
+struct GdnChunkParams {
+  GdnParams g;                 // x / proj rows (g.proj_seq floats apart), weights, conv_state, rec, out rows
+  const uint32_t* rowctl = nullptr;  // [C][2]: position, live (live rows are a prefix)
+  uint32_t C = 0;
+  float* gates = nullptr;      // [C][H][2] decay, beta
+  float* qk = nullptr;         // [C][H][2][128] normalised q (scaled by 1/sqrt(128)), k
+  float* vc = nullptr;         // [C][H][128] convolved v
+};
+cudaError_t launch_gdn_chunk(const GdnChunkParams& p, cudaStream_t s, bool pdl);
+
 cudaError_t launch_embed(const EmbedParams& p, cudaStream_t s, bool pdl);
+cudaError_t launch_chunk_begin(const ChunkParams& p, cudaStream_t s, bool pdl);
+cudaError_t launch_chunk_end(const ChunkParams& p, cudaStream_t s, bool pdl);
 cudaError_t launch_capture_row(const CaptureParams& p, cudaStream_t s, bool pdl);
 cudaError_t launch_attn_prep(const PrepParams& p, cudaStream_t s, bool pdl);
 cudaError_t launch_gdn(const GdnParams& p, cudaStream_t s, bool pdl);

@@ -144,3 +144,53 @@ def test_engine_2b_shape_decodes():
     prompt = np.random.default_rng(11).integers(0, spec.vocabulary_size, 6)
     check_generation(model, ref, prompt, 3)
     model.close()
+
+
+@pytest.mark.parametrize("history,prompt_len", [("fp16", 150), ("packet", 70)])
+def test_chunked_prefill_matches_token_prefill(history, prompt_len):
+    """The default prefill runs 64-position chunks (products on the tensor cores
+    from panel copies, attention rows over the one ring, recurrent rows in
+    order); RTA_MODEL_TOKEN_PREFILL runs the decode step per position.  Both
+    leave the same state (1e-3: the chunk products round activations to fp16)
+    and the same history: the tokens that follow agree with the oracle."""
+    import torch
+    from oracle.model import OracleModel
+    from rta_b200 import assets
+    from rta_b200.model import ResidentModel
+    spec = small_spec(kinds=("recurrent", "full", "recurrent", "full"))
+    layout = assets.plan(spec, 71)
+    mats, basis = assets.generate_device(layout, 71)
+    params = layout.params()
+    chunk = ResidentModel.from_payloads(spec, params, mats, basis, 256, history=history)
+    token = ResidentModel.from_payloads(spec, params, mats, basis, 256, history=history, token_prefill=True)
+    m, b = mats.cpu().numpy(), basis.cpu().numpy()
+    del mats, basis
+    torch.cuda.empty_cache()
+    prompt = np.random.default_rng(71).integers(0, spec.vocabulary_size, prompt_len)
+    t_chunk = chunk.prefill(prompt)
+    t_token = token.prefill(prompt)
+    s_chunk, p_chunk = chunk.state()
+    s_token, p_token = token.state()
+    assert p_chunk == p_token == prompt_len
+    # packet history: the 4-bit keys are re-quantized from K rows that differ in the
+    # last bits, so a few codes may land on the other side of a boundary
+    bar = TOL if history == "fp16" else 5e-2
+    assert rel_l2(s_chunk, s_token) < bar, rel_l2(s_chunk, s_token)
+    assert chunk.resources()["kernels_per_prefill_step"] == token.resources()["kernels_per_prefill_step"]
+    if history == "fp16":
+        ref = OracleModel(spec, params, m, b, 256)
+        ref.prefill(prompt)
+        assert rel_l2(s_chunk, ref.state) < TOL
+        got = chunk.generate(8)
+        want, margins = ref.generate(8)
+        for i in range(len(want)):
+            if margins[i] > TOL:
+                assert got[i] == want[i], (i, got, want, margins)
+            if got[i] != want[i]:
+                break
+    else:  # packet history: the chunked handle decodes on from its history
+        got = chunk.generate(6)
+        assert len(got) == 6 and int(got.max()) < spec.vocabulary_size
+    assert t_chunk < t_token  # fewer, larger launches
+    chunk.close()
+    token.close()
