@@ -309,13 +309,19 @@ enum {
   RTA_MODEL_PACKET_HISTORY = 1,
   /* Prefill one prompt position per step (the decode step's kernels) instead of
    * the default chunks of 64 positions.  A single-sequence handle prefills in
-   * chunks: the chunk's rows go through every matrix product as one batch (on
-   * the tensor cores, from panel-order copies of the Q4_K / Q6_K matrices made
-   * at open, about the weights' size again in HBM), the attention rows over
-   * the sequence's one history ring (each row its own causal window), and the
-   * recurrent layers row after row (Resident::prefill's batched forward,
-   * optical_resident.cpp:672-676, which forwards spans of its prefill batch). */
-  RTA_MODEL_TOKEN_PREFILL = 2
+   * chunks: the chunk's rows go through every matrix product as one batch (the
+   * decode GEMV's exact integer products, one weight pass per 16 rows), the
+   * attention rows over the sequence's one history ring (each row its own
+   * causal window), and the recurrent layer as a parallel pre-pass (gates,
+   * convolution, norms of every row) and a scan over the rows
+   * (Resident::prefill's batched forward, optical_resident.cpp:672-676, which
+   * forwards spans of its prefill batch). */
+  RTA_MODEL_TOKEN_PREFILL = 2,
+  /* Prefill chunks with their products on the tensor cores (tcgen05), from
+   * panel-order copies of the Q4_K / Q6_K matrices made at open (about the
+   * weights' size again in HBM): one weight pass per chunk, activations
+   * rounded once to fp16 per product (the 16+-sequence arithmetic). */
+  RTA_MODEL_TC_PREFILL = 4
 };
 RTA_API rta_status rta_model_open_ex(const rta_model_spec* spec, const uint32_t* params, size_t n_params,
                                      const void* matrices, size_t matrix_bytes, const void* basis, size_t basis_bytes,

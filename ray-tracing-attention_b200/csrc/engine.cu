@@ -165,11 +165,13 @@ struct Engine {
   cudaGraphExec_t g_prefill_cap = nullptr;
   DevBuf<float> cap;
   // Chunked prefill (single-sequence handles): kChunk prompt positions per graph
-  // replay as kChunk rows -- products as one batch (tensor cores on the panel
-  // copies), attention rows over the one ring (each row sees its own causal
-  // window), the recurrent layers row after row (their state is sequential).
+  // replay as kChunk rows -- products as one batch (the decode GEMV's exact
+  // integer products, 16 rows per weight pass; with RTA_MODEL_TC_PREFILL the
+  // tensor cores on panel copies), attention rows over the one ring (each row
+  // sees its own causal window), the recurrent layer as a parallel pre-pass and
+  // a scan over the rows (its state is sequential).
   static constexpr uint32_t kChunk = 64, kChunkSplits = 2;
-  bool chunked = false, token_prefill = false;
+  bool chunked = false, token_prefill = false, tc_prefill = false;
   cudaGraphExec_t g_chunk = nullptr;
   uint32_t kernels_per_chunk = 0;
   DevBuf<float> c_rows, c_proj, c_q, c_att, c_gdn, c_act, c_gu, c_pm, c_pz, c_po, c_gates, c_qk, c_vc;
@@ -386,7 +388,7 @@ struct Engine {
     tmp.alloc(std::max<size_t>(need, 1));
     // gate and up share one format field: both take the panel order only together
     auto panel_ok = [&](uint32_t rows) { return tc && rows % 128u == 0u; };
-    if (chunked)  // panel copies for the prefill chunks, from the GGUF-order bytes (before tiling)
+    if (chunked && tc_prefill)  // panel copies for the prefill chunks, from the GGUF-order bytes (before tiling)
       for (const Job& j : jobs) {
         if (!j.pc || j.rows % 128u) continue;
         j.pc->alloc(static_cast<size_t>(j.rows) * row_bytes(j.fmt, j.cols));
@@ -432,9 +434,11 @@ struct Engine {
             rta_team* tm = nullptr, const uint32_t* seq_starts = nullptr) {
     spec = sp;
     device = dev;
-    require((flags & ~static_cast<uint32_t>(RTA_MODEL_PACKET_HISTORY | RTA_MODEL_TOKEN_PREFILL)) == 0,
+    require((flags & ~static_cast<uint32_t>(RTA_MODEL_PACKET_HISTORY | RTA_MODEL_TOKEN_PREFILL |
+                                            RTA_MODEL_TC_PREFILL)) == 0,
             "unknown model flags", RTA_E_ARG);
     token_prefill = (flags & RTA_MODEL_TOKEN_PREFILL) != 0;
+    tc_prefill = (flags & RTA_MODEL_TC_PREFILL) != 0;
     packet_history = (flags & RTA_MODEL_PACKET_HISTORY) != 0;
     require(sequences >= 1 && sequences <= 256, "sequences must be 1..256", RTA_E_ARG);
     nseq = sequences;
@@ -624,7 +628,7 @@ struct Engine {
     part_z.alloc(recs);
     part_o.alloc(recs * hd);
     if (chunked) {
-      const size_t C = kChunk;
+      const size_t C = kChunk;  // chunk buffers (the tensor-core workspace only with panel copies)
       c_rows.alloc(C * D);
       c_proj.alloc(C * projw);
       c_q.alloc(C * Q());
@@ -1029,7 +1033,12 @@ struct Engine {
       mlp_pair(gu, dn, false, s);
       n += 2;
       if (team) {  // residual + the partial down projections of every rank, in rank order
-        RTA_CUDA(team_allreduce(team, partial.p, state.p, state.p, static_cast<size_t>(nseq) * D, xblocks, s));
+        // two-phase (reduce-scatter + all-gather) between ranks: each rank sends
+        // 2 (world - 1) / world of its partial rows instead of world - 1 copies
+        if (team_world(team) >= 2)
+          RTA_CUDA(team_allreduce2(team, partial.p, state.p, state.p, static_cast<size_t>(nseq) * D, xblocks, s));
+        else
+          RTA_CUDA(team_allreduce(team, partial.p, state.p, state.p, static_cast<size_t>(nseq) * D, xblocks, s));
         mark(RTA_PROF_EXCHANGE, 4.0 * nseq * D * team_world(team), s);
         ++n;
       }

@@ -22,6 +22,7 @@ namespace rta {
 namespace {
 
 constexpr uint32_t kDThreads = 256, kDWarps = 8, kDRowsPerWarp = 2, kDRows = kDWarps * kDRowsPerWarp;
+constexpr uint32_t kDenseSmemBudget = 200u * 1024u;  // activation rows of one launch
 
 struct DenseParams {
   const uint8_t* w[2];
@@ -187,7 +188,10 @@ cudaError_t launch_nb(const DenseParams& p, bool pdl, cudaStream_t s) {
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
     std::lock_guard<std::mutex> lock(m);
     if (!done[dev]) {
-      e = cudaFuncSetAttribute(gemv_dense_kernel<FMT, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+      // the launcher keeps a launch's activation rows within 200 KB (kDenseSmemBudget),
+      // leaving the static shared memory its room under the 227 KB limit
+      e = cudaFuncSetAttribute(gemv_dense_kernel<FMT, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(kDenseSmemBudget));
       if (e != cudaSuccess) return e;
       done[dev] = true;
     }
@@ -249,7 +253,7 @@ cudaError_t launch_gemv_dense(const GemvArgs& a, cudaStream_t s) {
   p.arg_step = a.argmax_step ? a.argmax_step : 1u;
   p.run_step = a.running_step ? a.running_step : 1u;
   // batch rows in launches of up to 8 whose activation rows fit in shared memory
-  const uint32_t fit = static_cast<uint32_t>((200u * 1024u) / (static_cast<size_t>(a.cols) * 4u));
+  const uint32_t fit = static_cast<uint32_t>(kDenseSmemBudget / (static_cast<size_t>(a.cols) * 4u));
   for (uint32_t b0 = 0; b0 < a.batch;) {
     uint32_t nb = 8u;
     while (nb > 1u && (nb > a.batch - b0 || nb > fit)) nb /= 2u;

@@ -148,6 +148,10 @@ uint32_t team_blocks(size_t words);
 // out = addend + sum over ranks of partial (rank order; same bits everywhere)
 cudaError_t team_allreduce(rta_team* t, const float* partial, const float* addend, float* out, size_t n,
                            uint32_t blocks, cudaStream_t s);
+// the same sum as a reduce-scatter + all-gather in one launch (two flag rounds,
+// 2 (world - 1) / world of the contribution sent instead of world - 1 times it)
+cudaError_t team_allreduce2(rta_team* t, const float* partial, const float* addend, float* out, size_t n,
+                            uint32_t blocks, cudaStream_t s);
 // state rows of every rank r, [row_start[r], row_start[r + 1]) x width, += that
 // rank's delta rows (row_start has world + 1 entries)
 cudaError_t team_gather_add(rta_team* t, const float* delta, float* state, uint32_t width,

@@ -211,6 +211,66 @@ __global__ void __launch_bounds__(kThreads) gather_add_kernel(View v, const floa
   end_call(v, b, e);
 }
 
+// out = addend + sum over ranks of partial, in two phases of one launch (a
+// reduce-scatter, then an all-gather): rank o owns chunk o of the n floats;
+// phase 1 pushes every other rank's chunk of this rank's partial to that rank
+// only, the owner sums its chunk in rank order (plus the addend) and phase 2
+// pushes the sum to every rank.  Each rank sends 2 (world - 1) / world of its
+// contribution instead of world - 1 copies of all of it (the one-shot
+// allreduce_kernel), for one more flag round trip.  Block b handles part b of
+// every chunk.  Counters: phase 1 publishes e, phase 2 e + 1 (the other slot
+// parity); the call leaves the counter at e + 1.
+__global__ void __launch_bounds__(kThreads) allreduce2_kernel(View v, const float* __restrict__ partial,
+                                                              const float* addend, float* out, uint32_t n) {
+  const uint32_t b = blockIdx.x, nb = gridDim.x;
+  __shared__ uint32_t e_s;
+  if (threadIdx.x == 0) e_s = v.ctr[b] + 1u;
+  __syncthreads();
+  const uint32_t e1 = e_s, e2 = e1 + 1u;
+  const uint32_t q4 = n / 4u;  // float4 elements
+  auto part = [&](uint32_t o, uint32_t& lo, uint32_t& hi) {  // float4 range of chunk o handled by block b
+    const uint32_t c0 = static_cast<uint32_t>(static_cast<uint64_t>(q4) * o / v.world);
+    const uint32_t c1 = static_cast<uint32_t>(static_cast<uint64_t>(q4) * (o + 1u) / v.world);
+    lo = c0 + static_cast<uint32_t>(static_cast<uint64_t>(c1 - c0) * b / nb);
+    hi = c0 + static_cast<uint32_t>(static_cast<uint64_t>(c1 - c0) * (b + 1u) / nb);
+  };
+  uint32_t lo, hi;
+  // phase 1: chunk o of this rank's partial -> slot [e1 & 1][rank] of rank o
+  for (uint32_t o = 0; o < v.world; ++o) {
+    part(o, lo, hi);
+    float4* dst = reinterpret_cast<float4*>(slot_at(v, o, e1 & 1u, v.rank));
+    for (uint32_t i = lo + threadIdx.x; i < hi; i += blockDim.x) dst[i] = reinterpret_cast<const float4*>(partial)[i];
+  }
+  publish(v, b, e1);
+  bool ok = await_all(v, b, e1);
+  // the owner's sum of its chunk, in rank order, to every rank (slot [e2 & 1][rank])
+  part(v.rank, lo, hi);
+  if (ok)
+    for (uint32_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+      float4 acc = addend ? reinterpret_cast<const float4*>(addend)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+      for (uint32_t s = 0; s < v.world; ++s) {
+        const float4 c = __ldcg(reinterpret_cast<const float4*>(slot_at(v, v.rank, e1 & 1u, s)) + i);
+        acc.x += c.x;
+        acc.y += c.y;
+        acc.z += c.z;
+        acc.w += c.w;
+      }
+      reinterpret_cast<float4*>(out)[i] = acc;
+      for (uint32_t pr = 0; pr < v.world; ++pr)
+        if (pr != v.rank) reinterpret_cast<float4*>(slot_at(v, pr, e2 & 1u, v.rank))[i] = acc;
+    }
+  publish(v, b, e2);
+  ok = await_all(v, b, e2) && ok;
+  if (ok)
+    for (uint32_t o = 0; o < v.world; ++o) {
+      if (o == v.rank) continue;
+      part(o, lo, hi);
+      for (uint32_t i = lo + threadIdx.x; i < hi; i += blockDim.x)
+        reinterpret_cast<float4*>(out)[i] = __ldcg(reinterpret_cast<const float4*>(slot_at(v, v.rank, e2 & 1u, o)) + i);
+    }
+  end_call(v, b, e2);
+}
+
 // In place over n packed argmax keys (order key << 32 | ~id, 0 = none) spaced
 // `stride` u64 apart: this rank's keys carry ids local to its vocabulary rows
 // starting at id_base; afterwards every rank holds the largest key over the
@@ -293,6 +353,13 @@ cudaError_t team_allreduce(rta_team* t, const float* partial, const float* adden
       static_cast<size_t>(blocks) * kChunkWords < n)
     return cudaErrorInvalidValue;
   allreduce_kernel<<<blocks, kThreads, 0, s>>>(t->view(), partial, addend, out, static_cast<uint32_t>(n));
+  return cudaGetLastError();
+}
+cudaError_t team_allreduce2(rta_team* t, const float* partial, const float* addend, float* out, size_t n,
+                            uint32_t blocks, cudaStream_t s) {
+  if (!t->connected || n == 0 || n % 4u || n > t->cap_words || blocks == 0 || blocks > kMaxBlocks)
+    return cudaErrorInvalidValue;
+  allreduce2_kernel<<<blocks, kThreads, 0, s>>>(t->view(), partial, addend, out, static_cast<uint32_t>(n));
   return cudaGetLastError();
 }
 cudaError_t team_gather_add(rta_team* t, const float* delta, float* state, uint32_t width,

@@ -146,13 +146,17 @@ def test_engine_2b_shape_decodes():
     model.close()
 
 
-@pytest.mark.parametrize("history,prompt_len", [("fp16", 150), ("packet", 70)])
-def test_chunked_prefill_matches_token_prefill(history, prompt_len):
-    """The default prefill runs 64-position chunks (products on the tensor cores
-    from panel copies, attention rows over the one ring, recurrent rows in
-    order); RTA_MODEL_TOKEN_PREFILL runs the decode step per position.  Both
-    leave the same state (1e-3: the chunk products round activations to fp16)
-    and the same history: the tokens that follow agree with the oracle."""
+@pytest.mark.parametrize("history,prompt_len,tc", [("fp16", 150, False), ("packet", 70, False),
+                                                   ("fp16", 150, True)])
+def test_chunked_prefill_matches_token_prefill(history, prompt_len, tc):
+    """The default prefill runs 64-position chunks (the chunk's rows through the
+    decode GEMV's exact products, attention rows over the one ring, the
+    recurrent pre-pass and row scan); RTA_MODEL_TOKEN_PREFILL runs the decode
+    step per position.  Both leave the same state within 1e-3 and the same
+    history: the tokens that follow agree with the oracle.  With
+    RTA_MODEL_TC_PREFILL the chunk products run on the tensor cores from panel
+    copies and round activations once to fp16, which the state bar of 5e-3
+    allows for; the tokens still follow the oracle under the margin rule."""
     import torch
     from oracle.model import OracleModel
     from rta_b200 import assets
@@ -161,7 +165,7 @@ def test_chunked_prefill_matches_token_prefill(history, prompt_len):
     layout = assets.plan(spec, 71)
     mats, basis = assets.generate_device(layout, 71)
     params = layout.params()
-    chunk = ResidentModel.from_payloads(spec, params, mats, basis, 256, history=history)
+    chunk = ResidentModel.from_payloads(spec, params, mats, basis, 256, history=history, tc_prefill=tc)
     token = ResidentModel.from_payloads(spec, params, mats, basis, 256, history=history, token_prefill=True)
     m, b = mats.cpu().numpy(), basis.cpu().numpy()
     del mats, basis
@@ -174,17 +178,17 @@ def test_chunked_prefill_matches_token_prefill(history, prompt_len):
     assert p_chunk == p_token == prompt_len
     # packet history: the 4-bit keys are re-quantized from K rows that differ in the
     # last bits, so a few codes may land on the other side of a boundary
-    bar = TOL if history == "fp16" else 5e-2
+    bar = 5e-2 if history == "packet" else (5e-3 if tc else TOL)
     assert rel_l2(s_chunk, s_token) < bar, rel_l2(s_chunk, s_token)
     assert chunk.resources()["kernels_per_prefill_step"] == token.resources()["kernels_per_prefill_step"]
     if history == "fp16":
         ref = OracleModel(spec, params, m, b, 256)
         ref.prefill(prompt)
-        assert rel_l2(s_chunk, ref.state) < TOL
+        assert rel_l2(s_chunk, ref.state) < bar
         got = chunk.generate(8)
         want, margins = ref.generate(8)
         for i in range(len(want)):
-            if margins[i] > TOL:
+            if margins[i] > bar:
                 assert got[i] == want[i], (i, got, want, margins)
             if got[i] != want[i]:
                 break
