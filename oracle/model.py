@@ -193,7 +193,7 @@ class OracleModel:
 
     def _mlp(self, L):
         xn = O.rmsnorm(self.state, L["post_norm"], self.eps)
-        act, y = O.mlp(L["mlp_fmt"], L["g"], L["u"], L["d"], self.D, self.F, xn)
+        act, y = O.mlp(L["mlp_fmt"], L["g"], L["u"], L["d"], self.D, self.F, xn, L["down_fmt"])
         self.state = self.state + y[0]
 
     def forward(self, token):

@@ -70,6 +70,7 @@ def lib():
             "rta_oracle_quantize": (None, [i32, p, sz, p]),
             "rta_oracle_gemv": (None, [i32, p, u32, u32, p, u32, p]),
             "rta_oracle_mlp": (None, [i32, p, p, p, u32, u32, p, u32, p, p]),
+            "rta_oracle_mlp_fmt": (None, [i32, i32, p, p, p, u32, u32, p, u32, p, p]),
             "rta_oracle_rmsnorm": (None, [p, p, u32, f, p]),
             "rta_oracle_lmhead": (None, [i32, p, u32, u32, p, u32, p, p, p]),
             "rta_oracle_attention": (None, [p, p, p, p, u32, u32, u32, u32, u32, u32, u32, u32, i32, p, p]),
@@ -139,12 +140,13 @@ def gemv(fmt: int, W, rows_out: int, cols: int, x) -> np.ndarray:
     return y
 
 
-def mlp(fmt: int, wg, wu, wd, D: int, F: int, x):
+def mlp(fmt: int, wg, wu, wd, D: int, F: int, x, down_fmt: int | None = None):
+    """SwiGLU MLP (op 2 kind 3 then op 2); down_fmt: the down rows' format when it differs."""
     x = _c(x, np.float32).reshape(-1, D)
     act = np.empty((x.shape[0], F), np.float32)
     y = np.empty((x.shape[0], D), np.float32)
-    lib().rta_oracle_mlp(fmt, _p(_c(wg, np.uint8)), _p(_c(wu, np.uint8)), _p(_c(wd, np.uint8)),
-                         D, F, _p(x), x.shape[0], _p(act), _p(y))
+    lib().rta_oracle_mlp_fmt(fmt, fmt if down_fmt is None else down_fmt, _p(_c(wg, np.uint8)), _p(_c(wu, np.uint8)),
+                             _p(_c(wd, np.uint8)), D, F, _p(x), x.shape[0], _p(act), _p(y))
     return act, y
 
 

@@ -759,7 +759,8 @@ struct Engine {
   // delta) are added to the residual rows on every rank; returns launches made.
   uint32_t gather_block_outputs(cudaStream_t s) {
     if (!team) return 0;
-    RTA_CUDA(team_gather_add(team, delta.p, state.p, D(), row_start.data(), xblocks, s));
+    RTA_CUDA(team_gather_add(team, delta.p, state.p, D(), row_start.data(), xblocks, s, &ctrl.p->running,
+                             static_cast<uint32_t>(sizeof(Control) / 4)));
     mark(RTA_PROF_EXCHANGE, 4.0 * nseq * D(), s);
     return 1;
   }
@@ -1035,10 +1036,13 @@ struct Engine {
       if (team) {  // residual + the partial down projections of every rank, in rank order
         // two-phase (reduce-scatter + all-gather) between ranks: each rank sends
         // 2 (world - 1) / world of its partial rows instead of world - 1 copies
+        // (rows of sequences that sat the step out are left alone: their products wrote nothing)
         if (team_world(team) >= 2)
-          RTA_CUDA(team_allreduce2(team, partial.p, state.p, state.p, static_cast<size_t>(nseq) * D, xblocks, s));
+          RTA_CUDA(team_allreduce2(team, partial.p, state.p, state.p, static_cast<size_t>(nseq) * D, xblocks, s,
+                                   running, cstep, D));
         else
-          RTA_CUDA(team_allreduce(team, partial.p, state.p, state.p, static_cast<size_t>(nseq) * D, xblocks, s));
+          RTA_CUDA(team_allreduce(team, partial.p, state.p, state.p, static_cast<size_t>(nseq) * D, xblocks, s,
+                                  running, cstep, D));
         mark(RTA_PROF_EXCHANGE, 4.0 * nseq * D * team_world(team), s);
         ++n;
       }

@@ -179,7 +179,7 @@ __global__ void __launch_bounds__(kDThreads) gemv_dense_kernel(const DenseParams
 template <int FMT, int NB>
 cudaError_t launch_nb(const DenseParams& p, bool pdl, cudaStream_t s) {
   const size_t smem = static_cast<size_t>(NB) * p.cols * 4u;
-  if (smem > 48u * 1024u) {  // opt-in to large dynamic shared memory, once per device
+  {  // opt-in to large dynamic shared memory (with the static arrays above 48 KB in all), once per device
     static std::mutex m;
     static bool done[64] = {false};
     int dev = 0;
@@ -206,7 +206,9 @@ cudaError_t launch_nb(const DenseParams& p, bool pdl, cudaStream_t s) {
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemv_dense_kernel<FMT, NB>, p);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_dense_kernel<FMT, NB>, p);
+  if (e != cudaSuccess) (void)cudaGetLastError();  // a refused launch is reported here, not to the next call
+  return e;
 }
 
 template <int FMT>

@@ -1,6 +1,8 @@
 // layers.cu -- per-token kernels of the resident decode step that sit between
 // the GEMVs: token readout->embedding control, QK-norm + RoPE + history append
 // for full-attention layers, and the fused recurrent (gated delta rule) layer.
+#include <atomic>
+
 #include "layers.h"
 #include "packets.cuh"
 #include "rta_internal.h"
@@ -493,6 +495,214 @@ __global__ void __launch_bounds__(256, ROWS > 16u ? 2 : 1) gdn_kernel(GdnParams 
   }
 }
 
+// Batched recurrent layer (many sequences): one persistent CTA per SM walks
+// an equal contiguous range of (head, sequence) units in head-major order.
+// The unit's [128 value x 128 key] state arrives by one bulk copy into a
+// shared stage of a kGdnStages-deep ring, issued units ahead (the first ones
+// before griddepcontrol.wait: the state is written only by this layer's
+// previous step); the gate weights of the current head and the norm weight
+// sit in registers; the next unit's layer input, raw projections and conv
+// history are loaded into registers while the current unit runs.  The RMS sum,
+// both gate dot products and both L2 norms share one block reduction
+// (a = inv * sum x nw w_a instead of sum (x inv nw) w_a: one multiplication
+// moved out of the sum).  The delta rule reads the state rows from the stage
+// and writes the new rows to global memory.
+constexpr uint32_t kGdnStages = 3;
+constexpr uint32_t kGdnStateFloats = 128u * 128u;
+
+__global__ void __launch_bounds__(256, 1) gdn_batch_kernel(GdnParams p) {
+  extern __shared__ __align__(1024) float gst[];  // [kGdnStages][128][128]
+  __shared__ __align__(8) uint64_t full[kGdnStages];
+  __shared__ float red[8 * 5];
+  __shared__ float qn[128], kn[128], vv[128];
+  __shared__ uint32_t gdn_abort;
+  const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
+  const uint32_t HD = 128u, S = p.H * HD, K = p.KH * HD;
+  const uint32_t U = p.H * p.nseq;
+  const uint32_t u0 = static_cast<uint32_t>(static_cast<uint64_t>(blockIdx.x) * U / gridDim.x);
+  const uint32_t u1 = static_cast<uint32_t>(static_cast<uint64_t>(blockIdx.x + 1u) * U / gridDim.x);
+  auto state_of = [&](uint32_t u) {
+    const uint32_t h = u / p.nseq, z = u % p.nseq;
+    return p.rec + z * p.rec_seq + static_cast<size_t>(h) * HD * HD;
+  };
+  uint32_t issued = 0;  // state copies issued (thread 0): units u0 .. u0 + issued - 1
+  if (tid == 0) {
+    for (uint32_t s = 0; s < kGdnStages; ++s) mbar_init(&full[s], 1);
+    fence_mbar_init();
+    for (uint32_t i = 0; i < kGdnStages && u0 + i < u1; ++i, ++issued) {
+      mbar_expect_tx(&full[i], kGdnStateFloats * 4u);
+      bulk_g2s(gst + i * kGdnStateFloats, state_of(u0 + i), kGdnStateFloats * 4u, &full[i]);
+    }
+    gdn_abort = 0u;
+  }
+  __syncthreads();
+  // constant per CTA: the norm weight of this thread's hidden values c = tid + 256 i
+  float nw[kGdnDPer];
+#pragma unroll
+  for (uint32_t i = 0; i < kGdnDPer; ++i) {
+    const uint32_t c = tid + 256u * i;
+    nw[i] = c < p.D ? p.attn_norm[c] : 0.f;
+  }
+  const size_t buf = static_cast<size_t>(3u) * S * 3u;  // floats of one conv-history parity buffer
+  // Inputs of one unit held in registers (loaded one unit ahead).
+  struct In {
+    float x[kGdnDPer];
+    float raw_q, raw_v, pq[2][3], pv[2][3], a_log, dt_bias;
+    float4 wq, wv;
+    uint32_t pos, run;
+  };
+  auto load_in = [&](uint32_t u, In& in) {
+    const uint32_t h = u / p.nseq, z = u % p.nseq, kh = h % p.KH;
+    const float* xz = p.x + static_cast<size_t>(z) * p.D;
+#pragma unroll
+    for (uint32_t i = 0; i < kGdnDPer; ++i) {
+      const uint32_t c = tid + 256u * i;
+      in.x[i] = c < p.D ? xz[c] : 0.f;
+    }
+    const float* proj = p.proj + z * p.proj_seq;
+    in.raw_q = proj[tid < 128u ? kh * HD + tid : K + kh * HD + (tid - 128u)];
+    in.raw_v = tid < 128u ? proj[2u * K + h * HD + tid] : 0.f;
+    const float* cs = p.conv_state + z * p.conv_seq;
+    const uint32_t qk = tid < 128u ? h * HD + tid : S + h * HD + (tid - 128u), vc = 2u * S + h * HD + (tid & 127u);
+#pragma unroll
+    for (int b = 0; b < 2; ++b)
+#pragma unroll
+      for (int j = 0; j < 3; ++j) {
+        in.pq[b][j] = cs[b * buf + qk * 3u + j];
+        in.pv[b][j] = tid < 128u ? cs[b * buf + vc * 3u + j] : 0.f;
+      }
+    in.wq = *reinterpret_cast<const float4*>(p.conv_w + static_cast<size_t>(qk) * 4u);
+    in.wv = *reinterpret_cast<const float4*>(p.conv_w + static_cast<size_t>(vc) * 4u);
+    in.a_log = p.a_log[h];
+    in.dt_bias = p.dt_bias[h];
+    in.pos = p.pos[z * p.ctrl_step];
+    in.run = p.running ? p.running[z * p.ctrl_step] : 1u;
+  };
+  auto conv = [](float4 w, float c0, float c1, float c2, float raw) {
+    float signal = 0.f;
+    signal = signal + c0 * w.x;
+    signal = signal + c1 * w.y;
+    signal = signal + c2 * w.z;
+    signal = signal + raw * w.w;
+    return signal * detector_sigmoid(signal);
+  };
+
+  pdl_wait();
+  pdl_launch_dependents();
+  In cur, nxt;
+  if (u0 < u1) load_in(u0, cur);
+  float wa[kGdnDPer], wb[kGdnDPer];
+  uint32_t wh = 0xFFFFFFFFu;  // head whose gate rows are in wa / wb
+  for (uint32_t u = u0; u < u1; ++u) {
+    const uint32_t i = u - u0, stage = i % kGdnStages;
+    const uint32_t h = u / p.nseq, z = u % p.nseq;
+    if (u + 1u < u1) load_in(u + 1u, nxt);
+    if (h != wh) {  // the head's gate rows (a head spans nseq consecutive units)
+#pragma unroll
+      for (uint32_t k = 0; k < kGdnDPer; ++k) {
+        const uint32_t c = tid + 256u * k;
+        wa[k] = c < p.D ? p.wa[static_cast<size_t>(h) * p.D + c] : 0.f;
+        wb[k] = c < p.D ? p.wb[static_cast<size_t>(h) * p.D + c] : 0.f;
+      }
+      wh = h;
+    }
+    const uint32_t qk = tid < 128u ? h * HD + tid : S + h * HD + (tid - 128u), vc = 2u * S + h * HD + (tid & 127u);
+    const bool run = cur.run != 0u;
+    float v5[5] = {0.f, 0.f, 0.f, 0.f, 0.f};
+    float f = 0.f;
+    if (run) {
+      // ---- op 18 sums: x^2, x nw w_a, x nw w_b
+#pragma unroll
+      for (uint32_t k = 0; k < kGdnDPer; ++k) {
+        const float xv = cur.x[k], xw = xv * nw[k];
+        v5[0] += xv * xv;
+        v5[1] += xw * wa[k];
+        v5[2] += xw * wb[k];
+      }
+      // ---- op 19: causal conv + SiLU of this thread's q / k channel (and v channel, tid < 128)
+      const uint32_t par = cur.pos & 1u;
+      const float c0 = par ? cur.pq[1][0] : cur.pq[0][0], c1 = par ? cur.pq[1][1] : cur.pq[0][1],
+                  c2 = par ? cur.pq[1][2] : cur.pq[0][2];
+      f = conv(cur.wq, c0, c1, c2, cur.raw_q);
+      float* cs = p.conv_state + z * p.conv_seq + (par ^ 1u) * buf;
+      float* nc = cs + static_cast<size_t>(qk) * 3u;
+      nc[0] = c1;
+      nc[1] = c2;
+      nc[2] = cur.raw_q;
+      if (tid < 128u) {
+        const float e0 = par ? cur.pv[1][0] : cur.pv[0][0], e1 = par ? cur.pv[1][1] : cur.pv[0][1],
+                    e2 = par ? cur.pv[1][2] : cur.pv[0][2];
+        vv[tid] = conv(cur.wv, e0, e1, e2, cur.raw_v);
+        float* nv = cs + static_cast<size_t>(vc) * 3u;
+        nv[0] = e1;
+        nv[1] = e2;
+        nv[2] = cur.raw_v;
+      }
+      v5[3] = tid < 128u ? f * f : 0.f;
+      v5[4] = tid >= 128u ? f * f : 0.f;
+    }
+    block_sums<5>(v5, red);  // uniform: every thread takes part, running or not
+    if (run) {
+      const float inv = rsqrtf(v5[0] / static_cast<float>(p.D) + p.eps);
+      const float decay = expf(-expf(cur.a_log) * softplus(inv * v5[1] + cur.dt_bias));
+      const float beta = detector_sigmoid(inv * v5[2]);
+      // ---- op 20: L2 norms
+      if (tid < 128u) qn[tid] = (f * rsqrtf(v5[3] + p.eps)) / sqrtf(128.0f);
+      else kn[tid - 128u] = f * rsqrtf(v5[4] + p.eps);
+      __syncthreads();
+      // ---- op 21 on this warp's 16 value rows, read from the stage
+      const bool ok = mbar_wait(&full[stage], (i / kGdnStages) & 1u,
+                                p.err ? p.err + static_cast<size_t>(z) * p.err_step : nullptr);
+      if (ok) {
+        const float* sst = gst + stage * kGdnStateFloats;
+        float* st = p.rec + z * p.rec_seq + static_cast<size_t>(h) * HD * HD;
+        const float k0 = kn[2 * lane], k1 = kn[2 * lane + 1], k2 = kn[2 * lane + 64], k3 = kn[2 * lane + 65];
+        const float q0 = qn[2 * lane], q1 = qn[2 * lane + 1], q2 = qn[2 * lane + 64], q3 = qn[2 * lane + 65];
+#pragma unroll 4
+        for (uint32_t r = warp * 16u; r < warp * 16u + 16u; ++r) {
+          float2 a = *reinterpret_cast<const float2*>(sst + r * HD + 2 * lane);
+          float2 b = *reinterpret_cast<const float2*>(sst + r * HD + 2 * lane + 64);
+          a.x *= decay;
+          a.y *= decay;
+          b.x *= decay;
+          b.y *= decay;
+          const float received = signed_product_sum(k0, k1, k2, k3, a.x, a.y, b.x, b.y);
+          const float delta = (vv[r] - received) * beta;
+          a.x += k0 * delta;
+          a.y += k1 * delta;
+          b.x += k2 * delta;
+          b.y += k3 * delta;
+          const float o = signed_product_sum(q0, q1, q2, q3, a.x, a.y, b.x, b.y);
+          *reinterpret_cast<float2*>(st + r * HD + 2 * lane) = a;
+          *reinterpret_cast<float2*>(st + r * HD + 2 * lane + 64) = b;
+          if (lane == 0) p.out[static_cast<size_t>(z) * S + h * HD + r] = o;
+        }
+      } else {
+        gdn_abort = 1u;
+      }
+    } else {
+      __syncthreads();  // pairs with the running units' barrier above (uniform per unit)
+      (void)mbar_wait(&full[stage], (i / kGdnStages) & 1u, nullptr);  // the copy into the stage has landed
+    }
+    __syncthreads();  // every read of the stage, of qn / kn / vv and of red is done
+    if (gdn_abort) break;
+    if (tid == 0 && u + kGdnStages < u1) {
+      mbar_expect_tx(&full[stage], kGdnStateFloats * 4u);
+      bulk_g2s(gst + stage * kGdnStateFloats, state_of(u + kGdnStages), kGdnStateFloats * 4u, &full[stage]);
+      ++issued;
+    }
+    if (u + 1u < u1) cur = nxt;
+  }
+  // an aborted walk leaves no copy in flight: wait (bounded) for the stages' last copies
+  if (gdn_abort && tid == 0) {
+    for (uint32_t s = 0; s < kGdnStages; ++s) {
+      // copies into stage s: units u0 + s, u0 + s + kGdnStages, ... below u0 + issued
+      const uint32_t cnt = issued > s ? (issued - s + kGdnStages - 1u) / kGdnStages : 0u;
+      if (cnt) (void)mbar_wait(&full[s], (cnt - 1u) & 1u, nullptr);
+    }
+  }
+}
+
 // Prefill capture of one position's row (see CaptureParams).  The position is
 // the one this step's embed kernel advanced to; a sequence that sat the step
 // out (prompt consumed) writes nothing.
@@ -731,23 +941,23 @@ cudaError_t launch_attn_prep(const PrepParams& p, cudaStream_t s, bool pdl) {
 cudaError_t launch_gdn(const GdnParams& p, cudaStream_t s, bool pdl) {
   if (p.D == 0 || p.D > 256u * kGdnDPer) return cudaErrorInvalidValue;
   void* args[] = {const_cast<GdnParams*>(&p)};
-  if (p.H * p.nseq >= 2u * 148u) {  // enough (sequence, head) pairs to fill the GPU with whole heads
-    // bulk-copy staging: 16-byte aligned sources, sizes a multiple of 16 bytes
-    if (p.D % 4u || (reinterpret_cast<uintptr_t>(p.wa) | reinterpret_cast<uintptr_t>(p.wb) |
-                     reinterpret_cast<uintptr_t>(p.attn_norm) | reinterpret_cast<uintptr_t>(p.x)) % 16u)
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (p.H * p.nseq >= 2u * static_cast<uint32_t>(sms)) {  // enough (head, sequence) units for every SM
+    // bulk copies of whole states: 16-byte aligned, and each state row block contiguous
+    if ((reinterpret_cast<uintptr_t>(p.rec) % 16u) || (p.rec_seq * 4u) % 16u || (reinterpret_cast<uintptr_t>(p.conv_w) % 16u))
       return cudaErrorMisalignedAddress;
-    const uint32_t smem = 16u * p.D;
-    static int attr_dev[64] = {0};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr_dev[dev]) {
-      const cudaError_t e = cudaFuncSetAttribute(gdn_kernel<kGdnRowsBatch>,
-                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, 16 * 4096);
+    const uint32_t smem = kGdnStages * kGdnStateFloats * 4u;
+    static std::atomic<int> attr_dev[64];
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!attr_dev[dev].load()) {
+      const cudaError_t e = cudaFuncSetAttribute(gdn_batch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 static_cast<int>(smem));
       if (e != cudaSuccess) return e;
-      attr_dev[dev] = 1;
+      attr_dev[dev].store(1);
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(p.H, 1, p.nseq);
+    cfg.gridDim = dim3(static_cast<uint32_t>(sms));
     cfg.blockDim = dim3(256);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
@@ -756,7 +966,7 @@ cudaError_t launch_gdn(const GdnParams& p, cudaStream_t s, bool pdl) {
     attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelExC(&cfg, reinterpret_cast<const void*>(gdn_kernel<kGdnRowsBatch>), args);
+    return cudaLaunchKernelExC(&cfg, reinterpret_cast<const void*>(gdn_batch_kernel), args);
   }
   return launch_pdl(reinterpret_cast<const void*>(gdn_kernel<kGdnRowsSmall>),
                     dim3(p.H, 128u / kGdnRowsSmall, p.nseq), dim3(256), args, s, pdl);

@@ -9,42 +9,52 @@
 // Arithmetic.  Per 256-wide block b of a weight row the quantized value is
 //   Q4_K: w = (d*sc_G)*q - dmin*m_G  (resident_quant.glsl:10-15)
 //   Q6_K: w = (d*sc_g)*(q - 32)      (resident_quant.glsl:16-19)
-// so  sum_k w_k x_k = d * sum_k A_k x_k - dmin * sum_G m_G X_G  with the exact
-// integers A_k = sc*q (Q4_K, <= 945) or sc*(q-32) (Q6_K, |A| <= 4096; fp16
-// holds them exactly up to 2048 and rounds to even above) and the group sums
-// X_G.  The tensor cores form sum A_k x_k per block in fp32 (A fp16 in tensor
-// memory, x rounded once to fp16), the mins term is one more K=16 MMA per
-// block against the group sums of the same fp16 x (fp32 sums split into two
-// fp16 halves, so the mins cancel against exactly what the codes see), and
-// the epilogue applies the fp32 block scales d / dmin and sums the blocks in
-// fp32.  The only rounding beyond fp32 accumulation is x -> fp16.
+// so  sum_k w_k x_k = sum_G (d sc_G) sum_{k in G} (q_k - 8) x_k
+//                    + sum_G (8 d sc_G - dmin m_G) X_G       (Q4_K)
+// with the exact integers sc (q - 8) (Q4_K, |.| <= 504) or sc (q - 32) (Q6_K,
+// |.| <= 4096; fp16 holds them exactly up to 2048 and rounds to even above)
+// and the group sums X_G.  The A operand in tensor memory is fp16(2^6 d *
+// integer) (one rounding), the mins term is one more K=16 MMA per block of
+// fp16(2^6 (8 d sc - dmin m)) against the group sums of the same fp16 x (fp32
+// sums split into two fp16 halves, so the mins cancel against exactly what
+// the codes see), the tensor cores accumulate every block of a work unit in
+// fp32, and the epilogue scales by 2^-6.  Beyond fp32 accumulation the
+// roundings are x -> fp16 and the two operand roundings.
 //
 // Weights use the "panel" layout of this library (formats 212 / 214, made by
 // launch_tile_tc): per 128-row tile and 256-wide block column one contiguous
 // panel of the same bytes, ordered so that the dequantizing thread of row m
 // reads its bytes with conflict-free 16-byte shared loads:
 //   Q4_K panel (18432 B): codes [pl 4][part 2][row 128][16 B] = GGUF bytes
-//     16 + 32*pl + 16*part .. +15 of the row; then headers [row 128][16 B]
-//     (d, dmin, 12 packed 6-bit scales and mins).
+//     16 + 32*pl + 16*part .. +15 of the row, each 4-byte word as bytes
+//     (0, 2, 1, 3); then headers [row 128][16 B] (d, dmin, 12 packed 6-bit
+//     scales and mins).
 //   Q6_K panel (26880 B): per half h (2): ql [j 2][part 2][row 128][16 B] =
 //     GGUF ql bytes 64h + 32j + 16part .. +15, then qh [part 2][row 128][16 B]
 //     = qh bytes 128 + 32h + 16part .. +15; then scales [row 128][16 int8],
 //     then d [row 128][fp16].
 //
-// One persistent CTA per SM (608 threads) walks (128-row tile, K slice) units:
-//   warp 0      bulk-copies each tile's panels (one copy per block column),
+// Work order: K slices as wide as the activation slots (4 block columns at
+// N = 64), within a slice every 128-row tile, within a tile the slice's block
+// columns.  One persistent CTA per SM (608 threads) takes an equal contiguous
+// range of that order (whole tiles when an argmax needs whole sums), so the
+// activations of a slice are copied into shared memory once per CTA and stay
+// there while the CTA walks the slice's tiles; a unit (one tile's run of block
+// columns) ends in a partial sum that lands atomically.
+//   warp 0      bulk-copies the range's weight panels, one per block column,
 //               from kernel start (weights do not depend on earlier kernels)
-//   warp 18     bulk-copies the activation stage of each 128-wide K step, after
+//   warp 18     bulk-copies an activation block column into its slot (block
+//               column % slots) when the slot holds another one, after
 //               griddepcontrol.wait (written by the preceding prep kernel)
 //   warps 10-17 dequantize the panel into tensor memory (A operand; thread =
 //               row, tcgen05.st), two warps per 32-lane quarter (warp % 4)
 //   warp 1      issues tcgen05.mma kind::f16 M=128 N=batch K=16 (A from tensor
-//               memory, B from shared memory) into one of two fp32 block
-//               accumulators, and commits stage releases to mbarriers
-//   warps 2-9   read the block accumulators (tcgen05.ld; thread = row, each
-//               warp half of the batch columns), scale and sum them per row in
-//               registers, and run the store / residual / argmax epilogue at
-//               the end of the tile
+//               memory, B from the slot), the K steps taking 128/N unit
+//               accumulators in turn (double-buffered by unit), and commits
+//               stage and slot releases to mbarriers
+//   warps 2-9   add a finished unit's accumulators (tcgen05.ld; thread = row,
+//               each warp half of the batch columns) and run the atomic /
+//               store / residual / argmax epilogue
 // Every wait is bounded (RTA_WAIT_NS): a stuck pipeline flags
 // RTA_DEVERR_TIMEOUT, drains its copies and MMAs and frees tensor memory.
 #include <cuda_fp16.h>
@@ -63,9 +73,6 @@ constexpr uint32_t kThreads = 608;  // 19 warps
 constexpr uint32_t kTileRows = 128;
 constexpr uint32_t kQ4KPanel = 128u * kQ4KBytes, kQ6KPanel = 128u * kQ6KBytes;  // 18432, 26880
 constexpr uint32_t kAStages = 3;  // tensor-memory A stages
-// Activation ring: the same depth as the tensor-memory A ring, so one barrier
-// pair per stage serves both (A and B of a half block are ready and released together).
-__host__ __device__ constexpr uint32_t b_stages(uint32_t) { return kAStages; }
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kAColBase = 256, kA2ColBase = 448;  // tensor-memory columns of the A / A2 stages
 constexpr uint32_t kMinSmem = 120u * 1024u;             // keeps one CTA per SM (tensor memory is taken whole)
@@ -83,7 +90,14 @@ __host__ __device__ constexpr uint32_t blk_bytes(bool q4, uint32_t N) { return N
 struct Params {
   const uint8_t* w[2];  // panels of matrix 0 / 1 (rows appended after matrix 0's in the output)
   uint32_t nmat, rows, KB, ntiles;
-  uint32_t ksplit;  // K slices per tile: work unit = (tile, slice); > 1 only for the residual epilogue
+  // Work order: K slices of `width` block columns, within a slice every tile,
+  // within a tile the slice's block columns -- one panel per step.  A CTA takes
+  // a contiguous range of that order (whole tiles when `whole_tiles`), and a
+  // unit is a run of one tile's block columns inside the range.
+  uint32_t width;        // block columns per K slice (== slots: activations resident per slice; == KB: streamed)
+  uint32_t slots;        // activation block columns held in shared memory (slot = block column % slots)
+  uint32_t total;        // panels of the product (ntiles * KB)
+  uint32_t whole_tiles;  // 1: every unit is a whole tile (argmax, plain stores); 0: partial sums land atomically
   const uint8_t* xb;  // prep output
   uint32_t blk;       // prep bytes per block
   uint32_t batch;     // live batch rows of this launch (<= N)
@@ -95,8 +109,48 @@ struct Params {
   const uint32_t* running;
   uint32_t run_step;
   uint32_t* err;
-  uint32_t off_b, off_bar, off_misc, b_stage;
+  uint32_t off_b, off_bar, off_misc, b_slot;  // b_slot: bytes between activation slots
 };
+
+// Position of one panel in the work order.
+struct Walk {
+  uint32_t t, kb, k0, k1;  // tile, block column, the slice's block columns [k0, k1)
+  __device__ __forceinline__ void start(const Params& p, uint32_t q) {
+    const uint32_t full = p.ntiles * p.width;  // panels of a full-width slice (only the last may be narrower)
+    const uint32_t sl = q / full, r = q - sl * full;
+    k0 = sl * p.width;
+    k1 = min(p.KB, k0 + p.width);
+    t = r / (k1 - k0);
+    kb = k0 + r % (k1 - k0);
+  }
+  __device__ __forceinline__ void next(const Params& p) {
+    if (++kb < k1) return;
+    kb = k0;
+    if (++t < p.ntiles) return;
+    t = 0;
+    k0 = k1;
+    k1 = min(p.KB, k0 + p.width);
+    kb = k0;
+  }
+};
+__device__ __forceinline__ void cta_range(const Params& p, uint32_t& q0, uint32_t& q1) {
+  if (p.whole_tiles) {
+    q0 = static_cast<uint32_t>(static_cast<uint64_t>(blockIdx.x) * p.ntiles / gridDim.x) * p.KB;
+    q1 = static_cast<uint32_t>(static_cast<uint64_t>(blockIdx.x + 1u) * p.ntiles / gridDim.x) * p.KB;
+  } else {
+    q0 = static_cast<uint32_t>(static_cast<uint64_t>(blockIdx.x) * p.total / gridDim.x);
+    q1 = static_cast<uint32_t>(static_cast<uint64_t>(blockIdx.x + 1u) * p.total / gridDim.x);
+  }
+}
+// After panel q at `w`, does the activation slot of w.kb get another block
+// column before its next use (so its MMAs must release it)?  The next use of
+// the slot is the same tile's block column kb + slots, else the next tile's
+// first block column in the slot (k0 + (kb - k0) % slots), else a later slice.
+__device__ __forceinline__ bool slot_changes(const Params& p, const Walk& w, uint32_t q, uint32_t q1) {
+  const bool keep = w.kb + p.slots >= w.k1 && w.kb - w.k0 < p.slots && w.t + 1u < p.ntiles &&
+                    q + (w.k1 - w.k0) < q1;
+  return !keep;
+}
 
 struct Prep {
   const float* x;
@@ -132,7 +186,6 @@ __device__ __forceinline__ uint32_t hfma2_bits(uint32_t a, __half2 b, __half2 c)
   return h2_bits(__hfma2(bits_h2(a), b, c));
 }
 __device__ __forceinline__ uint32_t hmul2_bits(uint32_t a, __half2 b) { return h2_bits(__hmul2(bits_h2(a), b)); }
-__device__ __forceinline__ uint32_t hsub2_bits(uint32_t a, __half2 b) { return h2_bits(__hsub2(bits_h2(a), b)); }
 
 // The block scales are folded into the fp16 operand, pre-multiplied by 2^6 so
 // that small weights stay clear of fp16 subnormals (|w| < 1023 stays finite);
@@ -151,17 +204,59 @@ __host__ __device__ constexpr uint32_t instr_desc(uint32_t N) {
   return (1u << 4) | ((N >> 3) << 17) | ((kTileRows >> 4) << 24);
 }
 
-__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
-                                       uint32_t accumulate) {
+// MMA and commit, issued by a whole warp in warp-uniform control flow: one
+// elected lane issues.  (Operands computed uniformly stay in uniform
+// registers; a loop run by a single lane pays register moves per MMA and
+// issues at about half the rate.)
+__device__ __forceinline__ void mma_ts_elect(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+      "{\n\t.reg .pred p, e;\n\t.reg .b32 r;\n\telect.sync r|e, 0xffffffff;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
+// Four MMAs under one election: D_i += A_i B_i (D_i, A_i tensor-memory
+// addresses, B_i shared-memory descriptors); the first `fresh` of them
+// overwrite their accumulators instead.
+__device__ __forceinline__ void mma4_ts_elect(const uint32_t (&d)[4], const uint32_t (&a)[4], const uint64_t (&b)[4],
+                                              uint32_t idesc, uint32_t fresh) {
+  asm volatile(
+      "{\n\t.reg .pred e, p0, p1, p2, p3;\n\t.reg .b32 r;\n\t"
+      "setp.le.u32 p0, %13, 0;\n\tsetp.le.u32 p1, %13, 1;\n\tsetp.le.u32 p2, %13, 2;\n\tsetp.le.u32 p3, %13, 3;\n\t"
+      "elect.sync r|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%4], %8, %12, p0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%1], [%5], %9, %12, p1;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%2], [%6], %10, %12, p2;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%3], [%7], %11, %12, p3;\n\t}\n" ::"r"(d[0]),
+      "r"(d[1]), "r"(d[2]), "r"(d[3]), "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "l"(b[0]), "l"(b[1]), "l"(b[2]),
+      "l"(b[3]), "r"(idesc), "r"(fresh));
 }
+// Bounded wait by a whole warp, with the first test inline.
+__device__ __forceinline__ bool warp_wait_fast(uint64_t* bar, uint32_t parity, uint32_t* err,
+                                               volatile uint32_t* abort_flag);
+__device__ __forceinline__ void mma_commit_elect(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t.reg .b32 r;\n\telect.sync r|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}\n" ::"r"(smem_u32(bar))
+      : "memory");
+}
+
+// Which block column each activation slot holds (8 bits per slot, 0xFF: none)
+// and the parity of each slot's copy count, in registers (slot indices are
+// not compile-time constants, so an array would live in local memory).
+struct SlotTable {
+  uint32_t w[4], par;
+  __device__ __forceinline__ void clear() { w[0] = w[1] = w[2] = w[3] = 0xFFFFFFFFu, par = 0u; }
+  __device__ __forceinline__ uint32_t get(uint32_t s) const {
+    const uint32_t x = s < 8u ? (s < 4u ? w[0] : w[1]) : (s < 12u ? w[2] : w[3]);
+    return (x >> (8u * (s & 3u))) & 0xFFu;
+  }
+  __device__ __forceinline__ void set(uint32_t s, uint32_t v) {
+    const uint32_t sh = 8u * (s & 3u), keep = ~(0xFFu << sh), put = (v & 0xFFu) << sh, i = s >> 2;
+#pragma unroll
+    for (uint32_t k = 0; k < 4u; ++k) w[k] = i == k ? (w[k] & keep) | put : w[k];
+  }
+};
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
@@ -178,6 +273,11 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16
 __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8]) {
   asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(v[0]),
                "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
+}
+__device__ __forceinline__ void tmem_st4(uint32_t taddr, const uint32_t (&v)[4]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};" ::"r"(taddr), "r"(v[0]), "r"(v[1]),
+               "r"(v[2]), "r"(v[3])
                : "memory");
 }
 __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
@@ -209,132 +309,101 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, uint32
   return __all_sync(0xffffffffu, ok);
 }
 
+__device__ __forceinline__ bool warp_wait_fast(uint64_t* bar, uint32_t parity, uint32_t* err,
+                                               volatile uint32_t* abort_flag) {
+  if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
+  return warp_wait(bar, parity, err, abort_flag);
+}
+
 // ------------------------------------------------------------- dequantizers
-// Q4_K header word w (bytes 4..15 of the block: scales / mins, 6 bits each).
-__device__ __forceinline__ void q4_scale_min(const uint4& h, uint32_t G, uint32_t& sc, uint32_t& mn) {
-  auto byte = [&](uint32_t i) -> uint32_t {  // header byte i (0..15)
-    const uint32_t w = i < 4u ? h.x : i < 8u ? h.y : i < 12u ? h.z : h.w;
-    return (w >> (8u * (i & 3u))) & 0xFFu;
-  };
-  if (G < 4u) {
-    sc = byte(4u + G) & 63u;
-    mn = byte(8u + G) & 63u;
-  } else {
-    const uint32_t mixed = byte(12u + G - 4u);
-    sc = (mixed & 15u) | ((byte(G) >> 6) << 4);
-    mn = (mixed >> 4) | ((byte(4u + G) >> 6) << 4);
-  }
-}
-
-// Code bytes of row m that one dequantizing thread (j) needs for one half
-// block column (h): loaded for both halves as soon as the panel lands, so the
-// shared-memory latency overlaps the previous half's arithmetic.
-struct Q4Words {
-  uint4 c0, c1;  // GGUF code bytes 16 + 32*pl .. +31, pl = 2h + j
+// Scale operands of one thread's four Q4_K groups: the thread (j) of row m
+// expands groups 2j, 2j+1 (half 0) and 4+2j, 5+2j (half 1), i.e. the
+// header's 6-bit scale / min fields at bytes 4+2j.., 8+2j.., 12+2j..
+// (get_scale_min_k4 order, resident_quant.glsl:10-15).
+struct Q4Scales {
+  __half2 s[4], k[4];  // per group g of (2j, 2j+1, 4+2j, 5+2j): sc/16 and -72 sc (both exact in fp16)
+  uint32_t mins[2];    // fp16 pairs 2^6 (8 d sc - dmin m) of groups (2j, 2j+1) and (4+2j, 5+2j)
 };
-struct Q6Words {
-  uint4 l0, l1;  // ql bytes 64h + 32j .. +31
-  uint4 g0, g1;  // qh bytes 128 + 32h .. +31
-};
-__device__ __forceinline__ Q4Words load_q4(const uint8_t* panel, uint32_t m, uint32_t h, uint32_t j) {
-  const uint32_t pl = 2u * h + j;
-  return {*reinterpret_cast<const uint4*>(panel + ((pl * 2u + 0u) * 128u + m) * 16u),
-          *reinterpret_cast<const uint4*>(panel + ((pl * 2u + 1u) * 128u + m) * 16u)};
-}
-__device__ __forceinline__ Q6Words load_q6(const uint8_t* panel, uint32_t m, uint32_t h, uint32_t j) {
-  const uint8_t* base = panel + h * 12288u;
-  return {*reinterpret_cast<const uint4*>(base + ((j * 2u + 0u) * 128u + m) * 16u),
-          *reinterpret_cast<const uint4*>(base + ((j * 2u + 1u) * 128u + m) * 16u),
-          *reinterpret_cast<const uint4*>(base + 8192u + m * 16u),
-          *reinterpret_cast<const uint4*>(base + 8192u + (128u + m) * 16u)};
+__device__ __forceinline__ Q4Scales q4_scales(const uint4& hdr, uint32_t j, float d64, float dmin64) {
+  const uint32_t sh = 16u * j;
+  const uint32_t Y = hdr.y >> sh, Z = hdr.z >> sh, W = hdr.w >> sh;  // bytes 4+2j.., 8+2j.., 12+2j.. in bits 0-15
+  const uint32_t sc[4] = {Y & 63u, (Y >> 8) & 63u, (W & 15u) | ((Y >> 2) & 48u), ((W >> 8) & 15u) | ((Y >> 10) & 48u)};
+  const uint32_t mn[4] = {Z & 63u, (Z >> 8) & 63u, ((W >> 4) & 15u) | ((Z >> 2) & 48u),
+                          ((W >> 12) & 15u) | ((Z >> 10) & 48u)};
+  Q4Scales r;
+  float c[4];
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const float f = static_cast<float>(sc[g]);
+    r.s[g] = __float2half2_rn(f * 0.0625f);
+    r.k[g] = __float2half2_rn(-72.f * f);
+    c[g] = 8.f * d64 * f - dmin64 * static_cast<float>(mn[g]);
+  }
+  r.mins[0] = h2_bits(__floats2half2_rn(c[0], c[1]));
+  r.mins[1] = h2_bits(__floats2half2_rn(c[2], c[3]));
+  return r;
 }
 
-// Row m's 64 coefficients 128h + 64j .. +63 of one Q4_K panel -> 32 tensor-
-// memory columns (fp16 pairs sc*q), plus (h == 0, j == 0) the 8 mins columns.
-// Q4_K operand: the codes centred on 8, sc*(q-8) (exact), times 2^6 d (one
-// rounding); the mins term carries 2^6 (8 d sc - dmin m) per group, so the two
-// rounded terms stay small next to the weight they sum to.
-__device__ __forceinline__ void dequant_q4(const Q4Words& cw, const uint4& hdr, uint32_t h, uint32_t j, uint32_t tcol,
-                                           uint32_t a2col, __half2 dd, float d64, float dmin64) {
-  const uint32_t pl = 2u * h + j;
-  uint32_t sc0, mn0, sc1, mn1;
-  q4_scale_min(hdr, 2u * pl, sc0, mn0);
-  q4_scale_min(hdr, 2u * pl + 1u, sc1, mn1);
-  // low nibbles hold 1024 + q after the 0x64 exponent byte: (1024+q)*sc - 1024*sc;
-  // high nibbles hold 1024 + 16q: (1024+16q)*(sc/16) - 64*sc.  Both exact.
-  const __half2 s0 = __float2half2_rn(static_cast<float>(sc0)), k0 = __float2half2_rn(-1024.f * sc0);
-  const __half2 s1 = __float2half2_rn(static_cast<float>(sc1) * 0.0625f), k1 = __float2half2_rn(-64.f * sc1);
-  const __half2 e0 = __float2half2_rn(8.f * sc0), e1 = __float2half2_rn(8.f * sc1);  // centre: q -> q - 8
-  const uint32_t words[8] = {cw.c0.x, cw.c0.y, cw.c0.z, cw.c0.w, cw.c1.x, cw.c1.y, cw.c1.z, cw.c1.w};
-  uint32_t lo[16], hi[16];
+// Sixteen coefficients of each group of one Q4_K group pair of row m (one
+// 16-byte part of the pair's 32 code bytes: coefficients 16 wh .. +15 of the
+// low group in the low nibbles, of the high group in the high nibbles) ->
+// fp16 pairs 2^6 d sc (q - 8), eight per group, for tensor memory.  The panel
+// stores each 4-byte word of codes as bytes (0, 2, 1, 3), so one mask-and-or
+// of the word, or of the word shifted by 4 or 8 bits, puts two consecutive
+// coefficients' nibbles at bits 4-7 of the two halves under the exponent byte
+// 0x64: 1024 + 16q.  One fp16 FMA (1024 + 16q) * (sc/16) - 72 sc = sc (q - 8)
+// is exact (every operand and the result are small integers or sc/16), and
+// the product with 2^6 d is the one rounding.  The centring on 8 keeps the
+// operand and the mins term small next to the weight they sum to.
+__device__ __forceinline__ void expand_q4(const uint4& c, __half2 slo, __half2 klo, __half2 shi, __half2 khi,
+                                          __half2 dd, uint32_t (&lo)[8], uint32_t (&hi)[8]) {
+  constexpr uint32_t kMask = 0x00F000F0u, kMagic = 0x64006400u;
+  const uint32_t words[4] = {c.x, c.y, c.z, c.w};
 #pragma unroll
-  for (int w = 0; w < 8; ++w) {
-    const uint32_t p01 = __byte_perm(words[w], 0x64646464u, 0x5140u);
-    const uint32_t p23 = __byte_perm(words[w], 0x64646464u, 0x5342u);
-    lo[2 * w] = hmul2_bits(hsub2_bits(hfma2_bits(p01 & 0xFF0FFF0Fu, s0, k0), e0), dd);
-    lo[2 * w + 1] = hmul2_bits(hsub2_bits(hfma2_bits(p23 & 0xFF0FFF0Fu, s0, k0), e0), dd);
-    hi[2 * w] = hmul2_bits(hsub2_bits(hfma2_bits(p01 & 0xFFF0FFF0u, s1, k1), e1), dd);
-    hi[2 * w + 1] = hmul2_bits(hsub2_bits(hfma2_bits(p23 & 0xFFF0FFF0u, s1, k1), e1), dd);
-  }
-  tmem_st16(tcol + 32u * j, lo);
-  tmem_st16(tcol + 32u * j + 16u, hi);
-  if (a2col != 0u) {  // mins of the 8 groups, twice (against the hi and lo halves of the group sums)
-    uint32_t mv[8];
-#pragma unroll
-    for (uint32_t p = 0; p < 4u; ++p) {
-      uint32_t sa, ma, sb, mb;
-      q4_scale_min(hdr, 2u * p, sa, ma);
-      q4_scale_min(hdr, 2u * p + 1u, sb, mb);
-      mv[p] = mv[4 + p] = h2_bits(__floats2half2_rn(8.f * d64 * static_cast<float>(sa) - dmin64 * static_cast<float>(ma),
-                                                     8.f * d64 * static_cast<float>(sb) - dmin64 * static_cast<float>(mb)));
-    }
-    tmem_st8(a2col, mv);
+  for (int w = 0; w < 4; ++w) {
+    const uint32_t x = words[w];
+    lo[2 * w] = hmul2_bits(hfma2_bits(((x << 4) & kMask) | kMagic, slo, klo), dd);      // coefficients 4w, 4w+1
+    lo[2 * w + 1] = hmul2_bits(hfma2_bits(((x >> 4) & kMask) | kMagic, slo, klo), dd);  // 4w+2, 4w+3
+    hi[2 * w] = hmul2_bits(hfma2_bits((x & kMask) | kMagic, shi, khi), dd);             // the same of the high group
+    hi[2 * w + 1] = hmul2_bits(hfma2_bits(((x >> 8) & kMask) | kMagic, shi, khi), dd);
   }
 }
 
-// Row m's coefficients 128h + 32j + 0..31 and 128h + 64 + 32j + 0..31 of one
-// Q6_K panel -> tensor-memory columns 16j.. and 32 + 16j.. (fp16 sc*(q-32)).
-// Each fp16 pair is assembled by one bit-select of two byte permutes: the
-// nibble (at bits 4-7) and the 0x64 exponent byte from the ql permute, the
-// two high bits (at bits 8-9) from the permute of the pre-shifted qh word:
-// 0x6400 | 16q = 1024 + 16q, then (1024 + 16q)*(sc/16) - 96*sc = sc*(q-32).
-__device__ __forceinline__ void dequant_q6(const Q6Words& cw, const uint4& s4, uint32_t h, uint32_t j,
-                                           uint32_t tcol, __half2 dd) {
-  const uint32_t qlw[8] = {cw.l0.x, cw.l0.y, cw.l0.z, cw.l0.w, cw.l1.x, cw.l1.y, cw.l1.z, cw.l1.w};
-  const uint32_t qhw[8] = {cw.g0.x, cw.g0.y, cw.g0.z, cw.g0.w, cw.g1.x, cw.g1.y, cw.g1.z, cw.g1.w};
-  // int8 scales 8h + 2j + u (low run) and 8h + 4 + 2j + u (high run), u = 0, 1:
-  // bytes 2j + u of word h*2 and of word h*2 + 1
-  const uint32_t wl = h ? s4.z : s4.x, wh = h ? s4.w : s4.y;
-  __half2 sl[2], kl[2], sh[2], kh[2];
-#pragma unroll
-  for (uint32_t u = 0; u < 2u; ++u) {
-    const float a = static_cast<float>(static_cast<int8_t>((wl >> (8u * (2u * j + u))) & 0xFFu));
-    const float b = static_cast<float>(static_cast<int8_t>((wh >> (8u * (2u * j + u))) & 0xFFu));
-    sl[u] = __float2half2_rn(a * 0.0625f);
-    kl[u] = __float2half2_rn(-96.f * a);
-    sh[u] = __float2half2_rn(b * 0.0625f);
-    kh[u] = __float2half2_rn(-96.f * b);
-  }
+// Sixteen coefficients of each run of one Q6_K run pair of row m, half h:
+// coefficients 128h + 32j + 16wh .. +15 (low run) and 128h + 64 + 32j + 16wh
+// .. +15 (high run) -> fp16 sc (q - 32) times 2^6 d, eight pairs per run.  ql
+// holds the runs' 16 ql bytes (low nibbles: low run, high nibbles: high run),
+// qh the 16 qh bytes (bit pairs 2j and 4+2j).  Each fp16 pair is assembled by
+// one bit-select of two byte permutes: the nibble (at bits 4-7) and the 0x64
+// exponent byte from the ql permute, the two high bits (at bits 8-9) from the
+// permute of the pre-shifted qh word: 0x6400 | 16q = 1024 + 16q, then
+// (1024 + 16q)*(sc/16) - 96*sc = sc*(q-32).
+__device__ __forceinline__ void expand_q6(const uint4& ql, const uint4& qh, const uint4& s4, uint32_t h, uint32_t j,
+                                          uint32_t wh, __half2 dd, uint32_t (&lo)[8], uint32_t (&hi)[8]) {
+  const uint32_t qlw[4] = {ql.x, ql.y, ql.z, ql.w};
+  const uint32_t qhw[4] = {qh.x, qh.y, qh.z, qh.w};
+  // int8 scales 8h + 2j + wh (low run) and 8h + 4 + 2j + wh (high run): byte 2j + wh of words 2h and 2h + 1
+  const uint32_t sl_w = h ? s4.z : s4.x, sh_w = h ? s4.w : s4.y;
+  const float a = static_cast<float>(static_cast<int8_t>((sl_w >> (8u * (2u * j + wh))) & 0xFFu));
+  const float b = static_cast<float>(static_cast<int8_t>((sh_w >> (8u * (2u * j + wh))) & 0xFFu));
+  const __half2 sl = __float2half2_rn(a * 0.0625f), kl = __float2half2_rn(-96.f * a);
+  const __half2 sh = __float2half2_rn(b * 0.0625f), kh = __float2half2_rn(-96.f * b);
   constexpr uint32_t kSel = 0xFCF0FCF0u;  // bits taken from the ql permute
-  uint32_t lo[16], hi[16];
 #pragma unroll
-  for (int w = 0; w < 8; ++w) {
+  for (int w = 0; w < 4; ++w) {
     const uint32_t qs = qlw[w] << 4;               // low-run nibbles to bits 4-7 of each byte
     const uint32_t hl = qhw[w] >> (2u * j);        // low-run high bits to bits 0-1 of each byte
     const uint32_t hh = qhw[w] >> (4u + 2u * j);   // high-run high bits to bits 0-1 of each byte
-    const uint32_t u = static_cast<uint32_t>(w) / 4u;  // first / second 16 coefficients of the run
 #pragma unroll
     for (int pr = 0; pr < 2; ++pr) {
       const uint32_t sel_l = pr == 0 ? 0x5140u : 0x5342u;  // bytes (2pr, 2pr+1) -> low byte of each half
       const uint32_t sel_h = pr == 0 ? 0x1404u : 0x3424u;  // the same bytes -> high byte of each half
       const uint32_t al = __byte_perm(qs, 0x64646464u, sel_l), ah = __byte_perm(qlw[w], 0x64646464u, sel_l);
       const uint32_t bl = __byte_perm(hl, 0u, sel_h), bh = __byte_perm(hh, 0u, sel_h);
-      lo[2 * w + pr] = hmul2_bits(hfma2_bits((al & kSel) | (bl & ~kSel), sl[u], kl[u]), dd);
-      hi[2 * w + pr] = hmul2_bits(hfma2_bits((ah & kSel) | (bh & ~kSel), sh[u], kh[u]), dd);
+      lo[2 * w + pr] = hmul2_bits(hfma2_bits((al & kSel) | (bl & ~kSel), sl, kl), dd);
+      hi[2 * w + pr] = hmul2_bits(hfma2_bits((ah & kSel) | (bh & ~kSel), sh, kh), dd);
     }
   }
-  tmem_st16(tcol + 16u * j, lo);
-  tmem_st16(tcol + 32u + 16u * j, hi);
 }
 
 // ---------------------------------------------------------------- the kernel
@@ -343,37 +412,43 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 19 warps: <
   using C = Cfg<FMT>;
   constexpr bool kQ4 = C::kQ4;
   constexpr uint32_t kPanel = C::kPanel, kRawS = C::kRawStages;
-  constexpr uint32_t kDStride = static_cast<uint32_t>(N);  // tensor-memory columns of one accumulator
-  constexpr uint32_t kBStages = b_stages(N);
+  // A unit's sum is spread over kParts accumulators that the K=16 steps of a
+  // block column take in turn, so consecutive MMAs do not wait on one another's
+  // accumulation (at N <= 64 one MMA's work is shorter than that latency); the
+  // epilogue adds the parts.  Two units' accumulators (double buffering):
+  // 2 * kParts * N = 256 columns below the A stages.
+  constexpr uint32_t kParts = 128u / static_cast<uint32_t>(N);
+  constexpr uint32_t kDStride = kParts * static_cast<uint32_t>(N);  // tensor-memory columns of one unit's parts
+  constexpr uint32_t kMaxSlots = 4u * 64u / static_cast<uint32_t>(N);
   static_assert(2u * kDStride <= kAColBase, "accumulators overlap the A stages");
+  static_assert(kParts <= 8u, "every part takes its first K step in the first half block");
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.off_bar);
   uint64_t* raw_full = bars;
   uint64_t* raw_empty = raw_full + kRawS;
-  static_assert(kBStages == kAStages, "one barrier pair per (A, B) stage");
-  // stage s of a half block: full once the 8 dequantizing warps have written A
-  // and the activation copy has landed (8 arrivals + the stager's expect-tx
-  // arrival), empty once the MMAs that read both have completed (one commit)
+  // A stage s of a half block: full once the 8 dequantizing warps have written
+  // it, empty once the MMAs that read it have completed (one commit)
   uint64_t* ab_full = raw_empty + kRawS;
   uint64_t* ab_empty = ab_full + kAStages;
   uint64_t* d_full = ab_empty + kAStages;
   uint64_t* d_empty = d_full + 2;
   uint64_t* drain = d_empty + 2;
+  // activation slot s: full when its block column has landed (expect-tx),
+  // empty when the MMAs of the last use of that block column have completed
+  uint64_t* b_full = drain + 1;
+  uint64_t* b_empty = b_full + kMaxSlots;
   uint32_t* misc = reinterpret_cast<uint32_t*>(smem + p.off_misc);
   volatile uint32_t* tmem_slot = misc;
   volatile uint32_t* abort_flag = misc + 1;
   unsigned long long* cand = reinterpret_cast<unsigned long long*>(misc + 4);  // [N] argmax candidates
 
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-  // work units (tile, K slice), walked in the same order by every role
-  const uint32_t nunits = p.ntiles * p.ksplit;
-  const uint32_t my_tiles = blockIdx.x < nunits ? (nunits - blockIdx.x + gridDim.x - 1u) / gridDim.x : 0u;
+  uint32_t q0, q1;  // this CTA's panels of the work order
+  cta_range(p, q0, q1);
   const uint32_t tiles_per_mat = p.rows / kTileRows;
-  auto unit = [&](uint32_t i, uint32_t& t, uint32_t& kb0, uint32_t& kb1) {
-    const uint32_t u = blockIdx.x + i * gridDim.x, sl = u % p.ksplit;
-    t = u / p.ksplit;
-    kb0 = sl * p.KB / p.ksplit;
-    kb1 = (sl + 1u) * p.KB / p.ksplit;
+  auto panel_src = [&](const Walk& w) {
+    const uint32_t mat = w.t / tiles_per_mat, mt = w.t % tiles_per_mat;
+    return (mat ? p.w[1] : p.w[0]) + (static_cast<size_t>(mt) * p.KB + w.kb) * kPanel;
   };
   uint8_t* raw = smem;
   // Thread 0 initialises the barriers and is also the panel producer: its first
@@ -386,19 +461,14 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 19 warps: <
     }
     fence_mbar_init();
     const uint64_t policy = evict_first_policy();
-    for (uint32_t i = 0; i < my_tiles && early < kRawS; ++i) {
-      uint32_t t, kb0, kb1;
-      unit(i, t, kb0, kb1);
-      const uint32_t mat = t / tiles_per_mat, mt = t % tiles_per_mat;
-      const uint8_t* wbase = (mat ? p.w[1] : p.w[0]) + static_cast<size_t>(mt) * p.KB * kPanel;
-      for (uint32_t kb = kb0; kb < kb1 && early < kRawS; ++kb, ++early) {
-        mbar_expect_tx(&raw_full[early], kPanel);
-        bulk_g2s_stream(raw + early * kPanel, wbase + static_cast<size_t>(kb) * kPanel, kPanel, &raw_full[early],
-                        policy);
-      }
+    Walk w;
+    if (q0 < q1) w.start(p, q0);
+    for (uint32_t q = q0; q < q1 && early < kRawS; ++q, ++early, w.next(p)) {
+      mbar_expect_tx(&raw_full[early], kPanel);
+      bulk_g2s_stream(raw + early * kPanel, panel_src(w), kPanel, &raw_full[early], policy);
     }
     for (uint32_t s = 0; s < kAStages; ++s) {
-      mbar_init(&ab_full[s], 9);
+      mbar_init(&ab_full[s], 8);
       mbar_init(&ab_empty[s], 1);
     }
     for (uint32_t s = 0; s < 2; ++s) {
@@ -406,6 +476,10 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 19 warps: <
       mbar_init(&d_empty[s], 8);
     }
     mbar_init(drain, 1);
+    for (uint32_t s = 0; s < p.slots; ++s) {
+      mbar_init(&b_full[s], 1);
+      mbar_init(&b_empty[s], 1);
+    }
     fence_mbar_init();
     *abort_flag = 0u;
   }
@@ -424,7 +498,6 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 19 warps: <
   pdl_launch_dependents();
   uint8_t* bst = smem + p.off_b;
   const uint32_t b_bytes0 = static_cast<uint32_t>(N) * 256u + (kQ4 ? static_cast<uint32_t>(N) * 32u : 0u);
-  const uint32_t b_bytes1 = static_cast<uint32_t>(N) * 256u;
 
   if (warp == 0) {
     // ----------------------------------------------- weight panel producer
@@ -434,25 +507,21 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 19 warps: <
       const uint64_t policy = evict_first_policy();
       uint32_t rit = 0;  // copies issued into the raw ring
       bool stop = false;
-      for (uint32_t i = 0; i < my_tiles && !stop; ++i) {
-        uint32_t t, kb0, kb1;
-        unit(i, t, kb0, kb1);
-        const uint32_t mat = t / tiles_per_mat, mt = t % tiles_per_mat;
-        const uint8_t* wbase = (mat ? p.w[1] : p.w[0]) + static_cast<size_t>(mt) * p.KB * kPanel;
-        for (uint32_t kb = kb0; kb < kb1 && !stop; ++kb) {
-          const uint32_t rs = rit % kRawS;
-          if (rit < early) {  // issued before the set-up
-            ++rit;
-            continue;
-          }
-          if (*abort_flag || !mbar_wait(&raw_empty[rs], ((rit / kRawS) & 1u) ^ 1u, p.err)) {
-            stop = true;
-            break;
-          }
-          mbar_expect_tx(&raw_full[rs], kPanel);
-          bulk_g2s_stream(raw + rs * kPanel, wbase + static_cast<size_t>(kb) * kPanel, kPanel, &raw_full[rs], policy);
+      Walk w;
+      if (q0 < q1) w.start(p, q0);
+      for (uint32_t q = q0; q < q1; ++q, w.next(p)) {
+        const uint32_t rs = rit % kRawS;
+        if (rit < early) {  // issued before the set-up
           ++rit;
+          continue;
         }
+        if (*abort_flag || !mbar_wait(&raw_empty[rs], ((rit / kRawS) & 1u) ^ 1u, p.err)) {
+          stop = true;
+          break;
+        }
+        mbar_expect_tx(&raw_full[rs], kPanel);
+        bulk_g2s_stream(raw + rs * kPanel, panel_src(w), kPanel, &raw_full[rs], policy);
+        ++rit;
       }
       if (stop) {
         *abort_flag = 1u;
@@ -464,204 +533,273 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 19 warps: <
       }
     }
   } else if (warp == 18) {
-    // ------------------------------------------- activation stage producer
+    // ------------------------------------------------- activation slot stager
+    // A block column is copied into slot kb % slots when the slot holds another
+    // one, after the MMAs of that one's last use have released the slot.
     if (lane == 0) {
-      uint32_t bit = 0;  // copies issued into the activation ring
+      SlotTable tab;  // par bit s: copies into slot s so far, mod 2
+      tab.clear();
+      uint32_t used = 0;  // slots that received a copy
       bool stop = false;
-      pdl_wait();  // the activation stages are written by the preceding prep kernel
-      for (uint32_t i = 0; i < my_tiles && !stop; ++i) {
-        uint32_t t, kb0, kb1;
-        unit(i, t, kb0, kb1);
-        for (uint32_t kb = kb0; kb < kb1 && !stop; ++kb)
-          for (uint32_t h = 0; h < 2u; ++h) {
-            const uint32_t bs = bit % kBStages;
-            if (*abort_flag || !mbar_wait(&ab_empty[bs], ((bit / kBStages) & 1u) ^ 1u, p.err)) {
-              stop = true;
-              break;
-            }
-            const uint32_t bytes = h == 0 ? b_bytes0 : b_bytes1;
-            const uint32_t off = kb * p.blk + (h == 0 ? 0u : b_bytes0);
-            mbar_expect_tx(&ab_full[bs], bytes);
-            bulk_g2s(bst + bs * p.b_stage, p.xb + off, bytes, &ab_full[bs]);
-            ++bit;
-          }
+      pdl_wait();  // the activation blocks are written by the preceding prep kernel
+      Walk w;
+      if (q0 < q1) w.start(p, q0);
+      for (uint32_t q = q0; q < q1; ++q, w.next(p)) {
+        const uint32_t s = w.kb % p.slots;
+        if (tab.get(s) == w.kb) continue;
+        // wait for as many releases as copies so far
+        if (*abort_flag || !mbar_wait(&b_empty[s], ((tab.par >> s) & 1u) ^ 1u, p.err)) {
+          stop = true;
+          break;
+        }
+        mbar_expect_tx(&b_full[s], p.blk);
+        bulk_g2s(bst + s * p.b_slot, p.xb + static_cast<size_t>(w.kb) * p.blk, p.blk, &b_full[s]);
+        tab.set(s, w.kb);
+        tab.par ^= 1u << s;
+        used |= 1u << s;
       }
       if (stop) {
         *abort_flag = 1u;
-        for (uint32_t s = 0; s < kBStages; ++s) {
-          const uint32_t n = bit / kBStages + (s < bit % kBStages ? 1u : 0u);
-          if (n) (void)mbar_wait(&ab_full[s], (n - 1u) & 1u, nullptr);  // bounded: ends after its limit
-        }
+        for (uint32_t s = 0; s < p.slots; ++s)  // the last copy into each used slot (bounded)
+          if ((used >> s) & 1u) (void)mbar_wait(&b_full[s], ((tab.par >> s) & 1u) ^ 1u, nullptr);
       }
     }
   } else if (warp == 1) {
     // ----------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = instr_desc(N);
-      uint32_t ait = 0, bit = 0;
-      bool stop = false;
-      const uint32_t b0 = smem_u32(bst);
-      for (uint32_t i = 0; i < my_tiles && !stop; ++i) {
-        uint32_t t, kb0, kb1;
-        unit(i, t, kb0, kb1);
-        // one accumulator per unit (block scales are in the operand), double-buffered by unit
-        const uint32_t buf = i & 1u;
-        if (*abort_flag || !mbar_wait(&d_empty[buf], ((i >> 1) & 1u) ^ 1u, p.err)) {
+    // The whole warp walks the work (warp-uniform), one elected lane issues.
+    constexpr uint32_t idesc = instr_desc(N);
+    SlotTable tab;
+    tab.clear();
+    uint32_t ait = 0, u = 0;  // A stages consumed, units begun
+    bool stop = false;
+    const uint32_t b0 = smem_u32(bst);
+    Walk w;
+    if (q0 < q1) w.start(p, q0);
+    for (uint32_t q = q0; q < q1 && !stop; ++q, w.next(p)) {
+      const bool first = q == q0 || w.kb == w.k0, last = q + 1u == q1 || w.kb + 1u == w.k1;
+      // one set of accumulators per unit (block scales are in the operand), double-buffered by unit
+      const uint32_t buf = u & 1u;
+      if (first) {
+        if (!warp_wait(&d_empty[buf], ((u >> 1) & 1u) ^ 1u, p.err, abort_flag)) {
           stop = true;
           break;
         }
         tc_fence_after();
-        const uint32_t d1 = tmem + buf * kDStride;
-        for (uint32_t kb = kb0; kb < kb1 && !stop; ++kb) {
-          for (uint32_t h = 0; h < 2u; ++h) {
-            const uint32_t as = ait % kAStages, bs = as;  // the rings advance together (one stage per half)
-            if (*abort_flag || !mbar_wait(&ab_full[as], (ait / kAStages) & 1u, p.err)) {
-              stop = true;
-              break;
-            }
-            tc_fence_after();
-            const uint32_t acol = tmem + kAColBase + 64u * as;
-            const uint32_t bsa = b0 + bs * p.b_stage;
-            const bool first = kb == kb0 && h == 0u;
-#pragma unroll
-            for (uint32_t kk = 0; kk < 8u; ++kk)
-              mma_ts(d1, acol + 8u * kk, smem_desc(bsa + 256u * kk, 128u, 2048u), idesc,
-                     (first && kk == 0u) ? 0u : 1u);
-            if (kQ4 && h == 0u)  // mins term: [c_G, c_G] x [X_G hi, X_G lo], c_G = 2^6 (8 d sc - dmin m), same accumulator
-              mma_ts(d1, tmem + kA2ColBase + 8u * as, smem_desc(bsa + static_cast<uint32_t>(N) * 256u, 128u, 256u),
-                     idesc, 1u);
-            mma_commit(&ab_empty[as]);
-            ++ait;
-            ++bit;
-          }
-        }
-        if (!stop) mma_commit(&d_full[buf]);
       }
-      if (stop) *abort_flag = 1u;
-      mma_commit(drain);  // every MMA issued above has completed once this arrives
-      (void)mbar_wait(drain, 0u, nullptr);
+      const uint32_t s = w.kb % p.slots;
+      if (tab.get(s) != w.kb) {  // the stager copies this block column in: wait for it
+        if (!warp_wait(&b_full[s], (tab.par >> s) & 1u, p.err, abort_flag)) {
+          stop = true;
+          break;
+        }
+        tab.set(s, w.kb);
+        tab.par ^= 1u << s;
+      }
+      const uint32_t d1 = tmem + buf * kDStride;
+      const uint32_t sb = b0 + s * p.b_slot;
+#pragma unroll
+      for (uint32_t h = 0; h < 2u; ++h) {
+        const uint32_t as = ait % kAStages;
+        if (!warp_wait_fast(&ab_full[as], (ait / kAStages) & 1u, p.err, abort_flag)) {
+          stop = true;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t acol = tmem + kAColBase + 64u * as;
+        const uint64_t bd = smem_desc(sb + (h ? b_bytes0 : 0u), 128u, 2048u);  // + 16 per K step (256 bytes)
+        const uint32_t fresh = (first && h == 0u) ? kParts : 0u;  // each part's first step overwrites it
+#pragma unroll
+        for (uint32_t k4 = 0; k4 < 8u; k4 += 4u) {
+          uint32_t dd[4], aa[4];
+          uint64_t bb[4];
+#pragma unroll
+          for (uint32_t i = 0; i < 4u; ++i) {
+            dd[i] = d1 + ((k4 + i) % kParts) * static_cast<uint32_t>(N);
+            aa[i] = acol + 8u * (k4 + i);
+            bb[i] = bd + 16u * (k4 + i);
+          }
+          mma4_ts_elect(dd, aa, bb, idesc, fresh > k4 ? fresh - k4 : 0u);
+        }
+        if (kQ4 && h == 0u)  // mins term: c_G against the group sums (hi, lo), into part 0
+          mma_ts_elect(d1, tmem + kA2ColBase + 8u * as, smem_desc(sb + static_cast<uint32_t>(N) * 256u, 128u, 256u),
+                       idesc, 1u);
+        mma_commit_elect(&ab_empty[as]);
+        ++ait;
+      }
+      if (stop) break;
+      if (slot_changes(p, w, q, q1)) mma_commit_elect(&b_empty[s]);  // the slot's next use is another block column
+      if (last) {
+        mma_commit_elect(&d_full[buf]);
+        ++u;
+      }
     }
+    if (stop) *abort_flag = 1u;
+    mma_commit_elect(drain);  // every MMA issued above has completed once this arrives
+    (void)mbar_wait(drain, 0u, nullptr);
     __syncwarp();
   } else if (warp >= 2 && warp < 10) {
     // ------------------------------------------------------------- epilogue
-    constexpr int NH = N / 2;  // batch columns of this warp
-    const uint32_t q = warp & 3u, m = 32u * q + lane, c0 = (warp - 2u) >> 2;  // columns c0*NH ..
-    const uint32_t lane_addr = (32u * q) << 16;
+    constexpr uint32_t NH = N / 2;  // batch columns of this warp
+    const uint32_t qd = warp & 3u, m = 32u * qd + lane, c0 = (warp - 2u) >> 2;  // columns c0*NH ..
+    const uint32_t lane_addr = (32u * qd) << 16;
     pdl_wait();  // residual targets and running flags are written by earlier kernels
+    uint32_t live = 0;  // bit i: batch column c0*NH + i is in the launch and still generating
+    for (uint32_t i = 0; i < NH; ++i) {
+      const uint32_t n = c0 * NH + i;
+      if (n < p.batch && (!p.running || p.running[static_cast<size_t>(n) * p.run_step] != 0u)) live |= 1u << i;
+    }
     bool stop = false;
-    for (uint32_t i = 0; i < my_tiles && !stop; ++i) {
-      uint32_t t, kb0, kb1;
-      unit(i, t, kb0, kb1);
+    Walk w;
+    if (q0 < q1) w.start(p, q0);
+    for (uint32_t q = q0, u = 0; q < q1 && !stop; ++u) {
+      const uint32_t t = w.t;
+      const uint32_t len = min(q1 - q, w.k1 - w.kb);  // panels of this unit
+      for (uint32_t i = 0; i < len; ++i) w.next(p);
+      q += len;
       const uint32_t mat = t / tiles_per_mat, mt = t % tiles_per_mat;
-      // the unit's whole sum (block scales were folded into the operand): one drain per unit
-      const uint32_t buf = i & 1u;
-      if (!warp_wait(&d_full[buf], (i >> 1) & 1u, p.err, abort_flag)) {
+      const uint32_t R = mat * p.rows + mt * kTileRows + m;  // this thread's output row
+      // the unit's whole sum (block scales were folded into the operand)
+      const uint32_t buf = u & 1u;
+      if (!warp_wait(&d_full[buf], (u >> 1) & 1u, p.err, abort_flag)) {
         stop = true;
         break;
       }
       tc_fence_after();
-      float acc[NH];
-      const uint32_t dcol = tmem + lane_addr + buf * kDStride + c0 * NH;
-#pragma unroll
-      for (int c = 0; c < NH / 8; ++c) {
+      const uint32_t dcol = tmem + lane_addr + buf * kDStride + c0 * NH;  // part 0; part i at + i * N
+      // eight columns at a time: a warp's 32 rows of one column are one 128-byte
+      // line, so scalar atomics of partial sums cost one L2 line operation per instruction
+#pragma unroll 1
+      for (uint32_t c = 0; c < NH; c += 8u) {
         float v[8];
-        tmem_ld8(dcol + 8u * c, v);
-        tmem_wait_ld();
+        tmem_ld8(dcol + c, v);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) acc[8 * c + e] = v[e] * (1.0f / kOperandScale);
+        for (uint32_t i = 1; i < kParts; ++i) {
+          float v2[8];
+          tmem_ld8(dcol + c + i * static_cast<uint32_t>(N), v2);
+          tmem_wait_ld();
+#pragma unroll
+          for (uint32_t e = 0; e < 8u; ++e) v[e] += v2[e];
+        }
+        tmem_wait_ld();
+        if (p.y) {
+          float* yp = p.y + static_cast<size_t>(c0 * NH + c) * p.y_stride + R;
+          if (!p.whole_tiles) {  // partial sum of one K range (into the residual, or into rows the prep zeroed)
+#pragma unroll
+            for (uint32_t e = 0; e < 8u; ++e)
+              if ((live >> (c + e)) & 1u) atomicAdd(yp + static_cast<size_t>(e) * p.y_stride, v[e] * (1.0f / kOperandScale));
+          } else {
+#pragma unroll
+            for (uint32_t e = 0; e < 8u; ++e) {
+              if (!((live >> (c + e)) & 1u)) continue;
+              float* ye = yp + static_cast<size_t>(e) * p.y_stride;
+              *ye = (p.epilogue == kAccumulate ? *ye : 0.f) + v[e] * (1.0f / kOperandScale);
+            }
+          }
+        }
+        if (p.argmax) {
+#pragma unroll
+          for (uint32_t e = 0; e < 8u; ++e) {
+            unsigned long long key = pack_argmax(v[e] * (1.0f / kOperandScale), R);
+#pragma unroll
+            for (int o = 16; o >= 1; o >>= 1) {
+              const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+              key = other > key ? other : key;
+            }
+            if (lane == 0 && ((live >> (c + e)) & 1u)) atomicMax(&cand[c0 * NH + c + e], key);
+          }
+        }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&d_empty[buf])) : "memory");
-      const uint32_t R0 = mat * p.rows + mt * kTileRows, R = R0 + m;  // output rows of the tile, this thread's
-#pragma unroll
-      for (int i = 0; i < NH; ++i) {
-        const uint32_t n = c0 * NH + static_cast<uint32_t>(i);
-        if (n >= p.batch) break;
-        if (p.running && p.running[static_cast<size_t>(n) * p.run_step] == 0u) continue;  // stopped sequence
-        if (p.y) {
-          // a warp's 32 rows of one batch column are one 128-byte line: scalar
-          // atomics of split partial sums cost one L2 line operation per warp
-          // instruction, as many as 16-byte vector or 512-byte bulk reductions
-          float* yp = p.y + static_cast<size_t>(n) * p.y_stride + R;
-          if (p.ksplit > 1u)  // partial sum of one K slice (into the residual, or into rows the prep zeroed)
-            atomicAdd(yp, acc[i]);
-          else if (p.epilogue == kAccumulate)
-            *yp += acc[i];
-          else
-            *yp = acc[i];
-        }
-        if (p.argmax) {
-          unsigned long long key = pack_argmax(acc[i], R);
-#pragma unroll
-          for (int o = 16; o >= 1; o >>= 1) {
-            const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
-            key = other > key ? other : key;
-          }
-          if (lane == 0) atomicMax(&cand[n], key);
-        }
-      }
     }
     if (stop) *abort_flag = 1u;
   } else if (warp >= 10 && warp < 18) {
     // ---------------------------------------------------------- dequantizers
-    const uint32_t q = warp & 3u, j = (warp - 10u) >> 2, m = 32u * q + lane;
-    const uint32_t lane_addr = (32u * q) << 16;
+    // Warp (quarter qd, j): rows 32 qd .. +31; of each half block, the pair of
+    // groups j (Q4_K) or run pair j (Q6_K).  Each half is expanded into
+    // registers before its stage is waited for.
+    const uint32_t qd = warp & 3u, j = (warp - 10u) >> 2, m = 32u * qd + lane;
+    const uint32_t lane_addr = (32u * qd) << 16;
     uint32_t rit = 0, ait = 0;
     bool stop = false;
-    for (uint32_t i = 0; i < my_tiles && !stop; ++i) {
-      uint32_t t, kb0, kb1;
-      unit(i, t, kb0, kb1);
-      for (uint32_t kb = kb0; kb < kb1 && !stop; ++kb) {
-        const uint32_t rs = rit % kRawS;
-        if (!warp_wait(&raw_full[rs], (rit / kRawS) & 1u, p.err, abort_flag)) {
+    for (uint32_t q = q0; q < q1 && !stop; ++q) {
+      const uint32_t rs = rit % kRawS;
+      if (!warp_wait_fast(&raw_full[rs], (rit / kRawS) & 1u, p.err, abort_flag)) {
+        stop = true;
+        break;
+      }
+      const uint8_t* panel = raw + rs * kPanel;
+      // everything this thread needs from the panel, then the panel is released
+      uint4 hdr, c[2][2], g[2][2];  // header / int8 scales of row m; codes (Q4_K) or ql and qh (Q6_K) [half][part]
+      uint32_t scale_word;
+      if constexpr (kQ4) {
+        hdr = *reinterpret_cast<const uint4*>(panel + 16384u + 16u * m);
+        scale_word = hdr.x;  // d, dmin
+#pragma unroll
+        for (uint32_t h = 0; h < 2u; ++h)
+#pragma unroll
+          for (uint32_t wh = 0; wh < 2u; ++wh)  // codes [pl 4][part 2][row 128][16 B], pl = 2h + j
+            c[h][wh] = *reinterpret_cast<const uint4*>(panel + (((2u * h + j) * 2u + wh) * 128u + m) * 16u);
+      } else {
+        hdr = *reinterpret_cast<const uint4*>(panel + 24576u + 16u * m);
+        scale_word = *reinterpret_cast<const unsigned short*>(panel + 26624u + 2u * m);  // d
+#pragma unroll
+        for (uint32_t h = 0; h < 2u; ++h)
+#pragma unroll
+          for (uint32_t wh = 0; wh < 2u; ++wh) {  // per half: ql [j 2][part 2][row][16 B], then qh [part 2][row][16 B]
+            const uint8_t* base = panel + h * 12288u;
+            c[h][wh] = *reinterpret_cast<const uint4*>(base + ((j * 2u + wh) * 128u + m) * 16u);
+            g[h][wh] = *reinterpret_cast<const uint4*>(base + 8192u + (wh * 128u + m) * 16u);
+          }
+      }
+      __syncwarp();
+      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&raw_empty[rs])) : "memory");
+      ++rit;
+      // the row's block scale (and Q4_K min scale) times 2^6, folded into the operand
+      const float d64 = kOperandScale * half_bits_to_float(scale_word & 0xFFFFu);
+      const __half2 dd = __float2half2_rn(d64);
+      Q4Scales sc4;
+      if constexpr (kQ4) sc4 = q4_scales(hdr, j, d64, kOperandScale * half_bits_to_float(scale_word >> 16));
+      uint32_t lo[16], hi[16];
+      auto expand = [&](uint32_t h) {
+#pragma unroll
+        for (uint32_t wh = 0; wh < 2u; ++wh) {
+          uint32_t(&l8)[8] = *reinterpret_cast<uint32_t(*)[8]>(&lo[8u * wh]);
+          uint32_t(&h8)[8] = *reinterpret_cast<uint32_t(*)[8]>(&hi[8u * wh]);
+          if constexpr (kQ4)
+            expand_q4(c[h][wh], sc4.s[2u * h], sc4.k[2u * h], sc4.s[2u * h + 1u], sc4.k[2u * h + 1u], dd, l8, h8);
+          else
+            expand_q6(c[h][wh], g[h][wh], hdr, h, j, wh, dd, l8, h8);
+        }
+      };
+      expand(0u);
+#pragma unroll
+      for (uint32_t h = 0; h < 2u; ++h) {
+        const uint32_t as = ait % kAStages;
+        if (!warp_wait_fast(&ab_empty[as], ((ait / kAStages) & 1u) ^ 1u, p.err, abort_flag)) {
           stop = true;
           break;
         }
-        const uint8_t* panel = raw + rs * kPanel;
-        // everything this thread needs from the panel, then the panel is released
-        uint4 hdr;  // Q4_K block header / Q6_K int8 scales of row m
-        uint32_t scale_word;
-        Q4Words c4[2];
-        Q6Words c6[2];
-        if constexpr (kQ4) {
-          hdr = *reinterpret_cast<const uint4*>(panel + 16384u + 16u * m);
-          scale_word = hdr.x;  // d, dmin
-          c4[0] = load_q4(panel, m, 0u, j);
-          c4[1] = load_q4(panel, m, 1u, j);
-        } else {
-          hdr = *reinterpret_cast<const uint4*>(panel + 24576u + 16u * m);
-          scale_word = *reinterpret_cast<const unsigned short*>(panel + 26624u + 2u * m);  // d
-          c6[0] = load_q6(panel, m, 0u, j);
-          c6[1] = load_q6(panel, m, 1u, j);
+        tc_fence_after();
+        const uint32_t tcol = tmem + lane_addr + kAColBase + 64u * as;
+        if constexpr (kQ4) {  // group pair j: low group at columns 32 j.., high group at 32 j + 16..
+          tmem_st16(tcol + 32u * j, lo);
+          tmem_st16(tcol + 32u * j + 16u, hi);
+          if (h == 0u) {  // the mins pairs of groups (2j, 2j+1, 4+2j, 5+2j), against the hi and the lo sums
+            const uint32_t mv[4] = {sc4.mins[0], sc4.mins[1], sc4.mins[0], sc4.mins[1]};
+            tmem_st4(tmem + lane_addr + kA2ColBase + 8u * as + 4u * j, mv);
+          }
+        } else {  // run pair j: low runs at columns 16 j.., high runs at 32 + 16 j..
+          tmem_st16(tcol + 16u * j, lo);
+          tmem_st16(tcol + 32u + 16u * j, hi);
         }
+        tmem_wait_st();
+        tc_fence_before();
         __syncwarp();
-        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&raw_empty[rs])) : "memory");
-        ++rit;
-        // the row's block scale (and Q4_K min scale) times 2^6, folded into the operand
-        const float d64 = kOperandScale * half_bits_to_float(scale_word & 0xFFFFu);
-        const float dmin64 = kOperandScale * half_bits_to_float(scale_word >> 16);  // Q4_K only
-        const __half2 dd = __float2half2_rn(d64);
-        for (uint32_t h = 0; h < 2u; ++h) {
-          const uint32_t as = ait % kAStages;
-          if (!warp_wait(&ab_empty[as], ((ait / kAStages) & 1u) ^ 1u, p.err, abort_flag)) {
-            stop = true;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t tcol = tmem + lane_addr + kAColBase + 64u * as;
-          if constexpr (kQ4) {
-            const uint32_t a2 = (h == 0u && j == 0u) ? tmem + lane_addr + kA2ColBase + 8u * as : 0u;
-            dequant_q4(c4[h], hdr, h, j, tcol, a2, dd, d64, dmin64);
-          } else {
-            dequant_q6(c6[h], hdr, h, j, tcol, dd);
-          }
-          tmem_wait_st();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&ab_full[as])) : "memory");
-          ++ait;
-        }
+        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&ab_full[as])) : "memory");
+        ++ait;
+        if (h == 0u) expand(1u);  // half 1 before its stage is waited for
       }
     }
     if (stop) *abort_flag = 1u;
@@ -777,12 +915,17 @@ __global__ void __launch_bounds__(256) tc_prep_kernel(const Prep p) {
       s += __shfl_xor_sync(0xffffffffu, s, 1);
       s += __shfl_xor_sync(0xffffffffu, s, 2);
       if ((c & 3u) == 0u) {
+        // K order of the mins product: the dequantizing thread j holds the mins of
+        // groups (2j, 2j+1, 4+2j, 5+2j) in its four columns, against the hi sums
+        // and then the lo sums: K = 8j + 4 part + 2 (g >> 2) + (g & 1), j = (g >> 1) & 1
         const uint32_t G = c / 4u, g8 = G % 8u;
         const __half hi = __float2half_rn(s);
         const __half lo = __float2half_rn(s - __half2float(hi));
-        uint8_t* b2 = p.xb + static_cast<size_t>(G / 8u) * p.blk + N * 256u + (n / 8u) * 256u + (n % 8u) * 16u;
-        reinterpret_cast<__half*>(b2)[g8] = hi;
-        reinterpret_cast<__half*>(b2 + 128u)[g8] = lo;
+        uint8_t* b2 = p.xb + static_cast<size_t>(G / 8u) * p.blk + N * 256u + (n / 8u) * 256u + (n % 8u) * 16u +
+                      ((g8 >> 1) & 1u) * 128u;
+        const uint32_t e = 2u * (g8 >> 2) + (g8 & 1u);
+        reinterpret_cast<__half*>(b2)[e] = hi;
+        reinterpret_cast<__half*>(b2)[4u + e] = lo;
       }
     }
   }
@@ -813,10 +956,11 @@ __global__ void __launch_bounds__(256) tile_tc_kernel(const uint8_t* __restrict_
   for (uint32_t o = threadIdx.x; o < PB; o += blockDim.x) {
     uint32_t r, b;  // source row and byte within its block
     if constexpr (FMT == kQ4K) {
-      if (o < 16384u) {
-        const uint32_t pl = o / 4096u, part = (o / 2048u) & 1u;
+      if (o < 16384u) {  // each 4-byte word of codes as bytes (0, 2, 1, 3): the dequantizer's nibble order
+        const uint32_t pl = o / 4096u, part = (o / 2048u) & 1u, i = o % 16u;
+        const uint32_t src = (i & ~3u) | ((i & 1u) << 1) | ((i >> 1) & 1u);
         r = (o / 16u) & 127u;
-        b = 16u + 32u * pl + 16u * part + o % 16u;
+        b = 16u + 32u * pl + 16u * part + src;
       } else {
         r = (o - 16384u) / 16u;
         b = o % 16u;
@@ -853,10 +997,10 @@ template <int FMT, int N>
 cudaError_t launch_n(const tc::Params& p0, const tc::Prep& pr, uint32_t grid, bool pdl, cudaStream_t s) {
   using C = tc::Cfg<FMT>;
   tc::Params p = p0;
-  p.b_stage = (static_cast<uint32_t>(N) * 256u + (C::kQ4 ? static_cast<uint32_t>(N) * 32u : 0u) + 1023u) / 1024u * 1024u;
+  p.b_slot = (tc::blk_bytes(C::kQ4, N) + 1023u) / 1024u * 1024u;
   p.off_b = C::kRawStages * C::kPanel;
   p.off_b = (p.off_b + 1023u) / 1024u * 1024u;
-  p.off_bar = p.off_b + tc::b_stages(N) * p.b_stage;
+  p.off_bar = p.off_b + p.slots * p.b_slot;
   p.off_misc = p.off_bar + 512u;
   uint32_t smem = p.off_misc + 16u + 8u * static_cast<uint32_t>(N);
   smem = smem < tc::kMinSmem ? tc::kMinSmem : smem;
@@ -934,22 +1078,16 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
   if (e != cudaSuccess) return e;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const uint32_t nmat = a.w1 ? 2u : 1u, ntiles = nmat * (a.rows / tc::kTileRows), KB = a.cols / 256u;
-  // K splits: each CTA walks its share of (tile, K slice) units; the slice
-  // count minimises the block columns of the busiest CTA plus one block of
-  // fixed cost per unit.  Partial sums land atomically (residual products add
-  // into y, stores into rows the prep kernel zeroes); the argmax needs whole sums.
-  uint32_t ksplit = 1;
-  if (!a.argmax && a.y) {
-    uint64_t best = ~0ull;
-    for (uint32_t ks = 1; ks <= 8u && ks <= KB; ++ks) {
-      const uint64_t units = static_cast<uint64_t>(ntiles) * ks;
-      const uint64_t per_cta = (units + sms - 1) / sms;
-      const uint64_t cost = per_cta * ((KB + ks - 1) / ks + 1);
-      if (cost < best) best = cost, ksplit = ks;
-    }
-  }
-  const uint32_t units = ntiles * ksplit;
-  const uint32_t grid = units < static_cast<uint32_t>(sms) ? units : static_cast<uint32_t>(sms);
+  // Work split.  Without an argmax every CTA takes an equal contiguous range of
+  // the panels in slice-major order (slices as wide as the activation slots,
+  // so the activations of a slice are copied once per CTA and stay resident
+  // while it walks the slice's tiles); partial sums land atomically (residual
+  // products add into y, stores into rows the prep kernel zeroes).  The argmax
+  // needs whole sums: whole tiles per CTA, activations streamed through the slots.
+  const bool whole = a.argmax != nullptr || !a.y;
+  const uint32_t total = ntiles * KB;
+  const uint32_t grid = whole ? (ntiles < static_cast<uint32_t>(sms) ? ntiles : static_cast<uint32_t>(sms))
+                              : (total < static_cast<uint32_t>(sms) ? total : static_cast<uint32_t>(sms));
   // batch rows run in launches of at most kTcMaxN (each streams the weights once)
   for (uint32_t b0 = 0; b0 < a.batch; b0 += kTcMaxN) {
     const uint32_t nb = a.batch - b0 < kTcMaxN ? a.batch - b0 : kTcMaxN;
@@ -971,7 +1109,7 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
     pr.xb = a.xb;
     pr.blk = tc::blk_bytes(q4, pr.N);
     pr.q4 = q4;
-    if (ksplit > 1u && a.epilogue == kStore) {
+    if (!whole && a.epilogue == kStore) {
       pr.zero_y = a.y + static_cast<size_t>(b0) * a.y_stride;
       pr.zero_cols = nmat * a.rows;
       pr.zero_stride = a.y_stride;
@@ -983,7 +1121,10 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
     p.rows = a.rows;
     p.KB = a.cols / 256u;
     p.ntiles = ntiles;
-    p.ksplit = ksplit;
+    p.slots = 4u * 64u / pr.N;
+    p.width = whole ? KB : p.slots;
+    p.total = total;
+    p.whole_tiles = whole ? 1u : 0u;
 
     p.xb = a.xb;
     p.blk = pr.blk;

@@ -56,8 +56,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 // Bounded wait on one mbarrier phase.  Returns false (and flags the error
 // word) when the bound is exceeded.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err) {
-  if (mbar_try_wait(bar, parity)) return true;
+// The spin is out of line: call sites keep only the first test, which keeps
+// warp-specialized kernels' hot loops small in the instruction cache.
+static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, uint32_t* err) {
   const uint64_t start = globaltimer();
   for (uint32_t spin = 1;; ++spin) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -66,6 +67,10 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
       return false;
     }
   }
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  return mbar_wait_slow(bar, parity, err);
 }
 // 1-D bulk copy global -> shared, completing on `bar` (16-byte aligned, size % 16 == 0).
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {

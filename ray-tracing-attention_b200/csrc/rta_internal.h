@@ -145,17 +145,23 @@ uint32_t* team_error_word(rta_team* t);
 // Every exchange a handle records uses team_blocks(largest exchange in words)
 // blocks, which keeps the slot parity of each call the same in every block.
 uint32_t team_blocks(size_t words);
-// out = addend + sum over ranks of partial (rank order; same bits everywhere)
+// out = addend + sum over ranks of partial (rank order; same bits everywhere).
+// With `running` (u32 flags `run_step` apart, one per row of `width` floats),
+// rows of sequences that sat the step out keep out = addend.
 cudaError_t team_allreduce(rta_team* t, const float* partial, const float* addend, float* out, size_t n,
-                           uint32_t blocks, cudaStream_t s);
+                           uint32_t blocks, cudaStream_t s, const uint32_t* running = nullptr,
+                           uint32_t run_step = 0, uint32_t width = 0);
 // the same sum as a reduce-scatter + all-gather in one launch (two flag rounds,
 // 2 (world - 1) / world of the contribution sent instead of world - 1 times it)
 cudaError_t team_allreduce2(rta_team* t, const float* partial, const float* addend, float* out, size_t n,
-                            uint32_t blocks, cudaStream_t s);
+                            uint32_t blocks, cudaStream_t s, const uint32_t* running = nullptr,
+                            uint32_t run_step = 0, uint32_t width = 0);
 // state rows of every rank r, [row_start[r], row_start[r + 1]) x width, += that
-// rank's delta rows (row_start has world + 1 entries)
+// rank's delta rows (row_start has world + 1 entries); rows of sequences that
+// sat the step out (running flag 0) are left as they are
 cudaError_t team_gather_add(rta_team* t, const float* delta, float* state, uint32_t width,
-                            const uint32_t* row_start, uint32_t blocks, cudaStream_t s);
+                            const uint32_t* row_start, uint32_t blocks, cudaStream_t s,
+                            const uint32_t* running = nullptr, uint32_t run_step = 0);
 // packed argmax keys (local ids from id_base) -> the largest over the ranks, in place
 cudaError_t team_allmax_keys(rta_team* t, unsigned long long* keys, uint32_t n, uint32_t stride, uint32_t id_base,
                              uint32_t blocks, cudaStream_t s);

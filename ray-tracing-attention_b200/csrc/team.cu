@@ -107,9 +107,21 @@ __device__ __forceinline__ void end_call(const View& v, uint32_t b, uint32_t e) 
   if (threadIdx.x == 0) v.ctr[b] = e;
 }
 
+// Rows of sequences that sat a step out (a ragged prefill's consumed prompts,
+// stopped generations): their products wrote nothing this step, so whatever
+// their rows of the exchanged buffer hold is not added.  running == null: every
+// row takes part.  Every rank holds the same flags, so every rank skips alike.
+struct RowMask {
+  const uint32_t* running;
+  uint32_t step, width;  // u32 between the sequences' flags; floats per row
+  __device__ __forceinline__ bool live(uint32_t float4_index) const {
+    return !running || running[static_cast<size_t>(4u * float4_index / width) * step] != 0u;
+  }
+};
+
 // out[i] = addend[i] + sum over ranks s (in order) of partial_s[i]; n % 4 == 0.
 __global__ void __launch_bounds__(kThreads) allreduce_kernel(View v, const float* __restrict__ partial,
-                                                             const float* addend, float* out, uint32_t n) {
+                                                             const float* addend, float* out, uint32_t n, RowMask rows) {
   const uint32_t b = blockIdx.x;
   const uint32_t e = begin_call(v, b);
   const uint32_t par = e & 1u;
@@ -122,13 +134,14 @@ __global__ void __launch_bounds__(kThreads) allreduce_kernel(View v, const float
   if (await_all(v, b, e)) {
     for (uint32_t i = q0 + threadIdx.x; i < q1; i += blockDim.x) {
       float4 acc = addend ? reinterpret_cast<const float4*>(addend)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
-      for (uint32_t s = 0; s < v.world; ++s) {
-        const float4 c = __ldcg(reinterpret_cast<const float4*>(slot_at(v, v.rank, par, s)) + i);
-        acc.x += c.x;
-        acc.y += c.y;
-        acc.z += c.z;
-        acc.w += c.w;
-      }
+      if (rows.live(i))
+        for (uint32_t s = 0; s < v.world; ++s) {
+          const float4 c = __ldcg(reinterpret_cast<const float4*>(slot_at(v, v.rank, par, s)) + i);
+          acc.x += c.x;
+          acc.y += c.y;
+          acc.z += c.z;
+          acc.w += c.w;
+        }
       reinterpret_cast<float4*>(out)[i] = acc;
     }
   }
@@ -177,7 +190,7 @@ __global__ void __launch_bounds__(kThreads) gather_add_kernel(View v, const floa
                                                               uint32_t width, uint32_t start0, uint32_t start1,
                                                               uint32_t start2, uint32_t start3, uint32_t start4,
                                                               uint32_t start5, uint32_t start6, uint32_t start7,
-                                                              uint32_t start8) {
+                                                              uint32_t start8, RowMask rows) {
   const uint32_t starts[kMaxRanks + 1] = {start0, start1, start2, start3, start4, start5, start6, start7, start8};
   const uint32_t b = blockIdx.x, nb = gridDim.x;
   const uint32_t e = begin_call(v, b);
@@ -198,6 +211,7 @@ __global__ void __launch_bounds__(kThreads) gather_add_kernel(View v, const floa
     for (uint32_t s = 0; s < v.world; ++s) {
       chunk(s, q0, q1);
       for (uint32_t i = q0 + threadIdx.x; i < q1; i += blockDim.x) {
+        if (!rows.live(i)) continue;
         float4 acc = reinterpret_cast<const float4*>(state)[i];
         const float4 c = __ldcg(reinterpret_cast<const float4*>(slot_at(v, v.rank, par, s)) + i);
         acc.x += c.x;
@@ -221,7 +235,8 @@ __global__ void __launch_bounds__(kThreads) gather_add_kernel(View v, const floa
 // every chunk.  Counters: phase 1 publishes e, phase 2 e + 1 (the other slot
 // parity); the call leaves the counter at e + 1.
 __global__ void __launch_bounds__(kThreads) allreduce2_kernel(View v, const float* __restrict__ partial,
-                                                              const float* addend, float* out, uint32_t n) {
+                                                              const float* addend, float* out, uint32_t n,
+                                                              RowMask rows) {
   const uint32_t b = blockIdx.x, nb = gridDim.x;
   __shared__ uint32_t e_s;
   if (threadIdx.x == 0) e_s = v.ctr[b] + 1u;
@@ -248,13 +263,14 @@ __global__ void __launch_bounds__(kThreads) allreduce2_kernel(View v, const floa
   if (ok)
     for (uint32_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
       float4 acc = addend ? reinterpret_cast<const float4*>(addend)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
-      for (uint32_t s = 0; s < v.world; ++s) {
-        const float4 c = __ldcg(reinterpret_cast<const float4*>(slot_at(v, v.rank, e1 & 1u, s)) + i);
-        acc.x += c.x;
-        acc.y += c.y;
-        acc.z += c.z;
-        acc.w += c.w;
-      }
+      if (rows.live(i))
+        for (uint32_t s = 0; s < v.world; ++s) {
+          const float4 c = __ldcg(reinterpret_cast<const float4*>(slot_at(v, v.rank, e1 & 1u, s)) + i);
+          acc.x += c.x;
+          acc.y += c.y;
+          acc.z += c.z;
+          acc.w += c.w;
+        }
       reinterpret_cast<float4*>(out)[i] = acc;
       for (uint32_t pr = 0; pr < v.world; ++pr)
         if (pr != v.rank) reinterpret_cast<float4*>(slot_at(v, pr, e2 & 1u, v.rank))[i] = acc;
@@ -348,29 +364,36 @@ uint32_t team_blocks(size_t words) {
   return b < 1u ? 1u : b > kMaxBlocks ? kMaxBlocks : static_cast<uint32_t>(b);
 }
 cudaError_t team_allreduce(rta_team* t, const float* partial, const float* addend, float* out, size_t n,
-                           uint32_t blocks, cudaStream_t s) {
+                           uint32_t blocks, cudaStream_t s, const uint32_t* running, uint32_t run_step,
+                           uint32_t width) {
   if (!t->connected || n == 0 || n % 4u || n > t->cap_words || blocks > kMaxBlocks ||
       static_cast<size_t>(blocks) * kChunkWords < n)
     return cudaErrorInvalidValue;
-  allreduce_kernel<<<blocks, kThreads, 0, s>>>(t->view(), partial, addend, out, static_cast<uint32_t>(n));
+  if (running && (width == 0 || width % 4u)) return cudaErrorInvalidValue;
+  allreduce_kernel<<<blocks, kThreads, 0, s>>>(t->view(), partial, addend, out, static_cast<uint32_t>(n),
+                                               RowMask{running, run_step, width});
   return cudaGetLastError();
 }
 cudaError_t team_allreduce2(rta_team* t, const float* partial, const float* addend, float* out, size_t n,
-                            uint32_t blocks, cudaStream_t s) {
+                            uint32_t blocks, cudaStream_t s, const uint32_t* running, uint32_t run_step,
+                            uint32_t width) {
   if (!t->connected || n == 0 || n % 4u || n > t->cap_words || blocks == 0 || blocks > kMaxBlocks)
     return cudaErrorInvalidValue;
-  allreduce2_kernel<<<blocks, kThreads, 0, s>>>(t->view(), partial, addend, out, static_cast<uint32_t>(n));
+  if (running && (width == 0 || width % 4u)) return cudaErrorInvalidValue;
+  allreduce2_kernel<<<blocks, kThreads, 0, s>>>(t->view(), partial, addend, out, static_cast<uint32_t>(n),
+                                                RowMask{running, run_step, width});
   return cudaGetLastError();
 }
 cudaError_t team_gather_add(rta_team* t, const float* delta, float* state, uint32_t width,
-                            const uint32_t* row_start, uint32_t blocks, cudaStream_t s) {
+                            const uint32_t* row_start, uint32_t blocks, cudaStream_t s, const uint32_t* running,
+                            uint32_t run_step) {
   if (!t->connected || width % 4u || static_cast<size_t>(row_start[t->world]) * width > t->cap_words ||
       blocks == 0 || blocks > kMaxBlocks)
     return cudaErrorInvalidValue;
   uint32_t st[kMaxRanks + 1];
   for (uint32_t i = 0; i <= kMaxRanks; ++i) st[i] = row_start[i < t->world ? i : t->world];
   gather_add_kernel<<<blocks, kThreads, 0, s>>>(t->view(), delta, state, width, st[0], st[1], st[2], st[3], st[4],
-                                                st[5], st[6], st[7], st[8]);
+                                                st[5], st[6], st[7], st[8], RowMask{running, run_step, width});
   return cudaGetLastError();
 }
 cudaError_t team_allmax_keys(rta_team* t, unsigned long long* keys, uint32_t n, uint32_t stride, uint32_t id_base,
@@ -452,7 +475,8 @@ rta_status rta_team_allreduce_f32(rta_team* t, const float* partial, const float
   if (!t->connected) return team_fail(RTA_E_STATE, "rta_team_allreduce_f32: team not connected");
   const uint32_t blocks = static_cast<uint32_t>((n + kChunkWords - 1u) / kChunkWords);
   allreduce_kernel<<<blocks, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(t->view(), partial, addend, out,
-                                                                               static_cast<uint32_t>(n));
+                                                                               static_cast<uint32_t>(n),
+                                                                               RowMask{nullptr, 0u, 0u});
   return team_cuda(cudaGetLastError(), "rta_team_allreduce_f32");
 }
 

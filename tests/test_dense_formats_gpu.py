@@ -98,10 +98,10 @@ def test_dense_model_decodes_like_the_oracle(sequences):
     ref = OracleModel(spec, params, m, b, 32)
     if sequences == 1:
         model.prefill(prompts[0])
-        got = [model.generate(6)]
+        state, _ = model.state()  # after the prompt, before any generated token
         ref.prefill(prompts[0])
-        state, _ = model.state()
-        assert rel_l2(state, ref.state) < TOL
+        assert rel_l2(state, ref.state) < TOL, rel_l2(state, ref.state)
+        got = [model.generate(6)]
         ref.reset()
     else:
         model.prefill_batch(prompts)

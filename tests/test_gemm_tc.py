@@ -1,12 +1,14 @@
 """The tensor-core batched product (qgemm.cu): panel layout, dequantizer and
 block algebra, restated on the host and checked against the GGUF decode.
 
-The kernel expands each panel row into fp16 integers A = sc*q (Q4_K) or
-sc*(q-32) (Q6_K) with byte permutes, masks and one fp16 FMA per pair
-(x = 0x6400 | code is 1024 + code), centres the Q4_K codes on 8 (exact), and
-multiplies by the row's block scale times 2^6 (one fp16 rounding), so the
-accumulator sums whole K slices; the Q4_K mins enter as one more K=16 product
-of fp16(2^6 (8 d sc - dmin m)) against the group sums, into the same
+The kernel expands each panel row into fp16 integers A = sc*(q-8) (Q4_K:
+one mask-and-or puts a nibble under the exponent byte, 0x6400 | 16q is
+1024 + 16q, and one fp16 FMA (1024 + 16q)(sc/16) - 72 sc is exact; the panel
+stores each code word as bytes (0, 2, 1, 3) so that the pairs come out in K
+order) or sc*(q-32) (Q6_K: byte permutes and a bit-select), and multiplies by
+the row's block scale times 2^6 (one fp16 rounding), so the accumulator sums
+whole K ranges; the Q4_K mins enter as one more K=16 product of
+fp16(2^6 (8 d sc - dmin m)) against the group sums, into the same
 accumulator, and the epilogue scales by 2^-6.
 These host tests emulate exactly those bit operations (an fp16 FMA is the
 exact product-sum rounded once, which float64 reproduces for these integers)
@@ -29,7 +31,8 @@ def panel_host(fmt, blocks, rows, cols):
     kb = cols // 256
     w = blocks.reshape(rows // 128, 128, kb, bb).transpose(0, 2, 1, 3)  # [tile][block col][row][byte]
     if fmt == 12:
-        codes = w[..., 16:].reshape(w.shape[:3] + (4, 2, 16)).transpose(0, 1, 3, 4, 2, 5)  # [.., pl, part, row, 16]
+        swap = np.array([0, 2, 1, 3, 4, 6, 5, 7, 8, 10, 9, 11, 12, 14, 13, 15])  # each code word as bytes (0, 2, 1, 3)
+        codes = w[..., 16:].reshape(w.shape[:3] + (4, 2, 16))[..., swap].transpose(0, 1, 3, 4, 2, 5)  # [.., pl, part, row, 16]
         out = np.concatenate([codes.reshape(w.shape[:2] + (16384,)), w[..., :16].reshape(w.shape[:2] + (2048,))], -1)
     else:
         parts = []
@@ -69,19 +72,31 @@ def q4_scale_min(hdr, G):
     return (mixed & 15) | ((hdr[G] >> 6) << 4), (mixed >> 4) | ((hdr[4 + G] >> 6) << 4)
 
 
+def q4_scales_host(hdr, j):
+    """Emulates q4_scales: the 6-bit (sc, m) of groups 2j, 2j+1, 4+2j, 5+2j from
+    the three 16-bit header fields at bytes 4+2j, 8+2j, 12+2j."""
+    w = words(np.asarray(hdr, np.uint8))
+    Y, Z, W = (w[1] >> (16 * j)) & 0xFFFF, (w[2] >> (16 * j)) & 0xFFFF, (w[3] >> (16 * j)) & 0xFFFF
+    sc = [Y & 63, (Y >> 8) & 63, (W & 15) | ((Y >> 2) & 48), ((W >> 8) & 15) | ((Y >> 10) & 48)]
+    mn = [Z & 63, (Z >> 8) & 63, ((W >> 4) & 15) | ((Z >> 2) & 48), ((W >> 12) & 15) | ((Z >> 10) & 48)]
+    return sc, mn
+
+
 def dequant_q4_host(P, m, h, j):
-    """Emulates dequant_q4: 32 tensor-memory columns (64 fp16) of row m."""
+    """Emulates dequant_q4: 32 tensor-memory columns (64 fp16 sc*(q-8), before
+    the block scale) of row m."""
     hdr = P[16384 + 16 * m:16384 + 16 * m + 16].astype(np.int64)
     pl = 2 * h + j
     c = np.concatenate([P[((pl * 2 + p) * 128 + m) * 16:((pl * 2 + p) * 128 + m) * 16 + 16] for p in range(2)])
-    sc0, _ = q4_scale_min(hdr, 2 * pl)
-    sc1, _ = q4_scale_min(hdr, 2 * pl + 1)
+    sc, _ = q4_scales_host(hdr, j)
+    sc0, sc1 = sc[2 * h], sc[2 * h + 1]
+    mask, magic = 0x00F000F0, 0x64006400
     lo, hi = [], []
-    for wd in words(c):
-        for sel in (0x5140, 0x5342):
-            p = byte_perm(wd, 0x64646464, sel)
-            lo += list(hfma2(p & 0xFF0FFF0F, sc0, -1024.0 * sc0))
-            hi += list(hfma2(p & 0xFFF0FFF0, sc1 * 0.0625, -64.0 * sc1))
+    for x in words(c):
+        lo += list(hfma2((((x << 4) & 0xFFFFFFFF) & mask) | magic, sc0 * 0.0625, -72.0 * sc0))
+        lo += list(hfma2(((x >> 4) & mask) | magic, sc0 * 0.0625, -72.0 * sc0))
+        hi += list(hfma2((x & mask) | magic, sc1 * 0.0625, -72.0 * sc1))
+        hi += list(hfma2(((x >> 8) & mask) | magic, sc1 * 0.0625, -72.0 * sc1))
     return np.array(lo + hi)  # coefficient order 64j + 0..63 of the half-step
 
 
@@ -147,12 +162,19 @@ def test_dequantizer_emulation_gives_exact_block_integers(fmt):
     for kb in range(cols // 256):
         for m in (0, 1, 31, 64, 127):
             if fmt == 12:
-                _, _, A, _ = gguf_q4(blocks[m, kb])
+                _, _, A, mins = gguf_q4(blocks[m, kb])
+                hdr = blocks[m, kb][:16].astype(np.int64)
+                scs = np.array([q4_scale_min(hdr, G)[0] for G in range(8)])
                 for h in range(2):
                     for j in range(2):
                         got = dequant_q4_host(P[kb], m, h, j)
-                        want = A[128 * h + 64 * j:128 * h + 64 * j + 64]
+                        k = np.arange(128 * h + 64 * j, 128 * h + 64 * j + 64)
+                        want = A[k] - 8 * scs[k // 32]
                         assert np.array_equal(got, want.astype(np.float64)), (kb, m, h, j)
+                    sc, mn = q4_scales_host(P[kb][16384 + 16 * m:16384 + 16 * m + 16].astype(np.int64), h)
+                    groups = [2 * h, 2 * h + 1, 4 + 2 * h, 5 + 2 * h]  # thread j = h here
+                    assert sc == [q4_scale_min(hdr, G)[0] for G in groups]
+                    assert mn == [int(mins[G]) for G in groups]
             else:
                 _, A = gguf_q6(blocks[m, kb])
                 for h in range(2):

@@ -21,7 +21,7 @@ from test_model_gpu import check_generation, small_spec
 pytestmark = pytest.mark.gpu
 
 
-def build_packet(spec, seed, capacity):
+def build_packet(spec, seed, capacity, token_prefill=False):
     import torch
     from oracle.model import OracleModel
     from rta_b200 import assets
@@ -29,7 +29,8 @@ def build_packet(spec, seed, capacity):
     layout = assets.plan(spec, seed)
     mats, basis = assets.generate_device(layout, seed)
     params = layout.params()
-    model = ResidentModel.from_payloads(spec, params, mats, basis, capacity, history="packet")
+    model = ResidentModel.from_payloads(spec, params, mats, basis, capacity, history="packet",
+                                        token_prefill=token_prefill)
     ref = OracleModel(spec, params, mats.cpu().numpy(), basis.cpu().numpy(), capacity, kv="packet")
     del mats, basis
     torch.cuda.empty_cache()
@@ -61,9 +62,12 @@ def test_engine_packet_attention_step_matches_fp64(seed, capacity, prompt_len):
     """Teacher-forced: the decode step's own q, gate and ring packets, read back,
     give the FP64 detector output the step produced (prefill and decode graphs,
     with the ring wrapping in the second and fourth cases; the last two split
-    the history over several CTAs per KV head, some of them empty)."""
+    the history over several CTAs per KV head, some of them empty).  The
+    prefill runs one position per step here so that its last step leaves the
+    decode step's own buffers to read back; the chunked prefill's packet rows
+    are checked through the history it leaves (test_model_gpu.py)."""
     spec = small_spec(kinds=("recurrent", "full"))
-    model, _ = build_packet(spec, seed, capacity)
+    model, _ = build_packet(spec, seed, capacity, token_prefill=True)
     H, KVH, hd = spec.attention_heads, spec.kv_heads, spec.attention_head_dim
     R = spec.rotary_dim
     prompt = np.random.default_rng(seed).integers(0, spec.vocabulary_size, prompt_len)
