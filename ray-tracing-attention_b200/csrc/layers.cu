@@ -497,22 +497,25 @@ __global__ void __launch_bounds__(256, ROWS > 16u ? 2 : 1) gdn_kernel(GdnParams 
 
 // Batched recurrent layer (many sequences): one persistent CTA per SM walks
 // an equal contiguous range of (head, sequence) units in head-major order.
-// The unit's [128 value x 128 key] state arrives by one bulk copy into a
+// Per unit: the [128 value x 128 key] state arrives by one bulk copy into a
 // shared stage of a kGdnStages-deep ring, issued units ahead (the first ones
 // before griddepcontrol.wait: the state is written only by this layer's
-// previous step); the gate weights of the current head and the norm weight
-// sit in registers; the next unit's layer input, raw projections and conv
-// history are loaded into registers while the current unit runs.  The RMS sum,
-// both gate dot products and both L2 norms share one block reduction
+// previous step); the sequence's layer-input row arrives the same way into a
+// two-slot ring; the raw projections, conv taps and conv history of the next
+// unit are loaded into registers while the current one runs; the gate
+// weights of the current head and the norm weight sit in registers.  The RMS
+// sum, both gate dot products and both L2 norms share one block reduction
 // (a = inv * sum x nw w_a instead of sum (x inv nw) w_a: one multiplication
-// moved out of the sum).  The delta rule reads the state rows from the stage
-// and writes the new rows to global memory.
+// moved out of the sum).  The delta rule runs four value rows per warp pass,
+// eight lanes per row with sixteen keys each, so each of the row's signed
+// reductions (E+ and E- kept apart, as op 21) is a three-level butterfly.
 constexpr uint32_t kGdnStages = 3;
 constexpr uint32_t kGdnStateFloats = 128u * 128u;
+constexpr uint32_t kGdnXSlots = 2;
 
 __global__ void __launch_bounds__(256, 1) gdn_batch_kernel(GdnParams p) {
-  extern __shared__ __align__(1024) float gst[];  // [kGdnStages][128][128]
-  __shared__ __align__(8) uint64_t full[kGdnStages];
+  extern __shared__ __align__(1024) float gst[];  // [kGdnStages][128][128] state, then [kGdnXSlots][D] input rows
+  __shared__ __align__(8) uint64_t full[kGdnStages], xfull[kGdnXSlots];
   __shared__ float red[8 * 5];
   __shared__ float qn[128], kn[128], vv[128];
   __shared__ uint32_t gdn_abort;
@@ -521,13 +524,15 @@ __global__ void __launch_bounds__(256, 1) gdn_batch_kernel(GdnParams p) {
   const uint32_t U = p.H * p.nseq;
   const uint32_t u0 = static_cast<uint32_t>(static_cast<uint64_t>(blockIdx.x) * U / gridDim.x);
   const uint32_t u1 = static_cast<uint32_t>(static_cast<uint64_t>(blockIdx.x + 1u) * U / gridDim.x);
+  float* xring = gst + kGdnStages * kGdnStateFloats;
   auto state_of = [&](uint32_t u) {
     const uint32_t h = u / p.nseq, z = u % p.nseq;
     return p.rec + z * p.rec_seq + static_cast<size_t>(h) * HD * HD;
   };
-  uint32_t issued = 0;  // state copies issued (thread 0): units u0 .. u0 + issued - 1
+  uint32_t issued = 0, xissued = 0;  // copies issued (thread 0): states of units u0.., input rows of units u0..
   if (tid == 0) {
     for (uint32_t s = 0; s < kGdnStages; ++s) mbar_init(&full[s], 1);
+    for (uint32_t s = 0; s < kGdnXSlots; ++s) mbar_init(&xfull[s], 1);
     fence_mbar_init();
     for (uint32_t i = 0; i < kGdnStages && u0 + i < u1; ++i, ++issued) {
       mbar_expect_tx(&full[i], kGdnStateFloats * 4u);
@@ -544,21 +549,14 @@ __global__ void __launch_bounds__(256, 1) gdn_batch_kernel(GdnParams p) {
     nw[i] = c < p.D ? p.attn_norm[c] : 0.f;
   }
   const size_t buf = static_cast<size_t>(3u) * S * 3u;  // floats of one conv-history parity buffer
-  // Inputs of one unit held in registers (loaded one unit ahead).
+  // Register inputs of one unit (loaded one unit ahead).
   struct In {
-    float x[kGdnDPer];
     float raw_q, raw_v, pq[2][3], pv[2][3], a_log, dt_bias;
     float4 wq, wv;
     uint32_t pos, run;
   };
   auto load_in = [&](uint32_t u, In& in) {
     const uint32_t h = u / p.nseq, z = u % p.nseq, kh = h % p.KH;
-    const float* xz = p.x + static_cast<size_t>(z) * p.D;
-#pragma unroll
-    for (uint32_t i = 0; i < kGdnDPer; ++i) {
-      const uint32_t c = tid + 256u * i;
-      in.x[i] = c < p.D ? xz[c] : 0.f;
-    }
     const float* proj = p.proj + z * p.proj_seq;
     in.raw_q = proj[tid < 128u ? kh * HD + tid : K + kh * HD + (tid - 128u)];
     in.raw_v = tid < 128u ? proj[2u * K + h * HD + tid] : 0.f;
@@ -578,6 +576,11 @@ __global__ void __launch_bounds__(256, 1) gdn_batch_kernel(GdnParams p) {
     in.pos = p.pos[z * p.ctrl_step];
     in.run = p.running ? p.running[z * p.ctrl_step] : 1u;
   };
+  auto issue_x = [&](uint32_t u) {  // thread 0: the input row of unit u into slot (u - u0) % kGdnXSlots
+    const uint32_t slot = (u - u0) % kGdnXSlots, z = u % p.nseq;
+    mbar_expect_tx(&xfull[slot], p.D * 4u);
+    bulk_g2s(xring + slot * p.D, p.x + static_cast<size_t>(z) * p.D, p.D * 4u, &xfull[slot]);
+  };
   auto conv = [](float4 w, float c0, float c1, float c2, float raw) {
     float signal = 0.f;
     signal = signal + c0 * w.x;
@@ -586,15 +589,20 @@ __global__ void __launch_bounds__(256, 1) gdn_batch_kernel(GdnParams p) {
     signal = signal + raw * w.w;
     return signal * detector_sigmoid(signal);
   };
+  // Eight lanes of a warp per value row: lane l takes row (l / 8) of the pass
+  // and keys 4 c + 32 j + e (c = l % 8, j, e < 4): four float4 of the row.
+  const uint32_t grp = lane >> 3, c8 = lane & 7u;
 
   pdl_wait();
   pdl_launch_dependents();
+  if (tid == 0)
+    for (uint32_t i = 0; i < kGdnXSlots && u0 + i < u1; ++i, ++xissued) issue_x(u0 + i);
   In cur, nxt;
   if (u0 < u1) load_in(u0, cur);
   float wa[kGdnDPer], wb[kGdnDPer];
   uint32_t wh = 0xFFFFFFFFu;  // head whose gate rows are in wa / wb
   for (uint32_t u = u0; u < u1; ++u) {
-    const uint32_t i = u - u0, stage = i % kGdnStages;
+    const uint32_t i = u - u0, stage = i % kGdnStages, xs = i % kGdnXSlots;
     const uint32_t h = u / p.nseq, z = u % p.nseq;
     if (u + 1u < u1) load_in(u + 1u, nxt);
     if (h != wh) {  // the head's gate rows (a head spans nseq consecutive units)
@@ -606,15 +614,19 @@ __global__ void __launch_bounds__(256, 1) gdn_batch_kernel(GdnParams p) {
       }
       wh = h;
     }
+    uint32_t* err = p.err ? p.err + static_cast<size_t>(z) * p.err_step : nullptr;
     const uint32_t qk = tid < 128u ? h * HD + tid : S + h * HD + (tid - 128u), vc = 2u * S + h * HD + (tid & 127u);
     const bool run = cur.run != 0u;
     float v5[5] = {0.f, 0.f, 0.f, 0.f, 0.f};
     float f = 0.f;
-    if (run) {
+    const bool x_ok = mbar_wait(&xfull[xs], (i / kGdnXSlots) & 1u, err);
+    if (run && x_ok) {
       // ---- op 18 sums: x^2, x nw w_a, x nw w_b
+      const float* xr = xring + xs * p.D;
 #pragma unroll
       for (uint32_t k = 0; k < kGdnDPer; ++k) {
-        const float xv = cur.x[k], xw = xv * nw[k];
+        const uint32_t c = tid + 256u * k;
+        const float xv = c < p.D ? xr[c] : 0.f, xw = xv * nw[k];
         v5[0] += xv * xv;
         v5[1] += xw * wa[k];
         v5[2] += xw * wb[k];
@@ -642,7 +654,10 @@ __global__ void __launch_bounds__(256, 1) gdn_batch_kernel(GdnParams p) {
       v5[4] = tid >= 128u ? f * f : 0.f;
     }
     block_sums<5>(v5, red);  // uniform: every thread takes part, running or not
-    if (run) {
+    if (!x_ok) gdn_abort = 1u;
+    const bool ok = mbar_wait(&full[stage], (i / kGdnStages) & 1u, err);  // the stage has landed
+    if (!ok) gdn_abort = 1u;
+    if (run && x_ok) {
       const float inv = rsqrtf(v5[0] / static_cast<float>(p.D) + p.eps);
       const float decay = expf(-expf(cur.a_log) * softplus(inv * v5[1] + cur.dt_bias));
       const float beta = detector_sigmoid(inv * v5[2]);
@@ -650,55 +665,91 @@ __global__ void __launch_bounds__(256, 1) gdn_batch_kernel(GdnParams p) {
       if (tid < 128u) qn[tid] = (f * rsqrtf(v5[3] + p.eps)) / sqrtf(128.0f);
       else kn[tid - 128u] = f * rsqrtf(v5[4] + p.eps);
       __syncthreads();
-      // ---- op 21 on this warp's 16 value rows, read from the stage
-      const bool ok = mbar_wait(&full[stage], (i / kGdnStages) & 1u,
-                                p.err ? p.err + static_cast<size_t>(z) * p.err_step : nullptr);
       if (ok) {
+        // ---- op 21 on this warp's 16 value rows, four per pass, from the stage
+        float kk[16], qq[16];
+#pragma unroll
+        for (uint32_t j = 0; j < 4u; ++j)
+#pragma unroll
+          for (uint32_t e = 0; e < 4u; ++e) {
+            kk[4u * j + e] = kn[4u * c8 + 32u * j + e];
+            qq[4u * j + e] = qn[4u * c8 + 32u * j + e];
+          }
         const float* sst = gst + stage * kGdnStateFloats;
         float* st = p.rec + z * p.rec_seq + static_cast<size_t>(h) * HD * HD;
-        const float k0 = kn[2 * lane], k1 = kn[2 * lane + 1], k2 = kn[2 * lane + 64], k3 = kn[2 * lane + 65];
-        const float q0 = qn[2 * lane], q1 = qn[2 * lane + 1], q2 = qn[2 * lane + 64], q3 = qn[2 * lane + 65];
-#pragma unroll 4
-        for (uint32_t r = warp * 16u; r < warp * 16u + 16u; ++r) {
-          float2 a = *reinterpret_cast<const float2*>(sst + r * HD + 2 * lane);
-          float2 b = *reinterpret_cast<const float2*>(sst + r * HD + 2 * lane + 64);
-          a.x *= decay;
-          a.y *= decay;
-          b.x *= decay;
-          b.y *= decay;
-          const float received = signed_product_sum(k0, k1, k2, k3, a.x, a.y, b.x, b.y);
-          const float delta = (vv[r] - received) * beta;
-          a.x += k0 * delta;
-          a.y += k1 * delta;
-          b.x += k2 * delta;
-          b.y += k3 * delta;
-          const float o = signed_product_sum(q0, q1, q2, q3, a.x, a.y, b.x, b.y);
-          *reinterpret_cast<float2*>(st + r * HD + 2 * lane) = a;
-          *reinterpret_cast<float2*>(st + r * HD + 2 * lane + 64) = b;
-          if (lane == 0) p.out[static_cast<size_t>(z) * S + h * HD + r] = o;
+#pragma unroll 1
+        for (uint32_t pass = 0; pass < 4u; ++pass) {
+          const uint32_t r = warp * 16u + 4u * pass + grp;
+          float s[16];
+#pragma unroll
+          for (uint32_t j = 0; j < 4u; ++j) {
+            const float4 v = *reinterpret_cast<const float4*>(sst + r * HD + 4u * c8 + 32u * j);
+            s[4u * j] = v.x * decay;
+            s[4u * j + 1u] = v.y * decay;
+            s[4u * j + 2u] = v.z * decay;
+            s[4u * j + 3u] = v.w * decay;
+          }
+          // received = E+ - E- of k . s over the row's 128 keys (resident_common.glsl:137)
+          float P = 0.f, M = 0.f;
+#pragma unroll
+          for (uint32_t e = 0; e < 16u; ++e) {
+            const float pr = kk[e] * s[e];
+            if (pr > 0.f) P += pr;
+            else if (pr < 0.f) M -= pr;
+          }
+#pragma unroll
+          for (int o = 4; o >= 1; o >>= 1) {
+            P += __shfl_xor_sync(0xffffffffu, P, o);
+            M += __shfl_xor_sync(0xffffffffu, M, o);
+          }
+          const float delta = (vv[r] - (P - M)) * beta;
+          float P2 = 0.f, M2 = 0.f;
+#pragma unroll
+          for (uint32_t e = 0; e < 16u; ++e) {
+            s[e] += kk[e] * delta;
+            const float pr = qq[e] * s[e];
+            if (pr > 0.f) P2 += pr;
+            else if (pr < 0.f) M2 -= pr;
+          }
+#pragma unroll
+          for (int o = 4; o >= 1; o >>= 1) {
+            P2 += __shfl_xor_sync(0xffffffffu, P2, o);
+            M2 += __shfl_xor_sync(0xffffffffu, M2, o);
+          }
+#pragma unroll
+          for (uint32_t j = 0; j < 4u; ++j)
+            *reinterpret_cast<float4*>(st + r * HD + 4u * c8 + 32u * j) =
+                make_float4(s[4u * j], s[4u * j + 1u], s[4u * j + 2u], s[4u * j + 3u]);
+          if (c8 == 0u) p.out[static_cast<size_t>(z) * S + h * HD + r] = P2 - M2;
         }
-      } else {
-        gdn_abort = 1u;
       }
     } else {
       __syncthreads();  // pairs with the running units' barrier above (uniform per unit)
-      (void)mbar_wait(&full[stage], (i / kGdnStages) & 1u, nullptr);  // the copy into the stage has landed
     }
-    __syncthreads();  // every read of the stage, of qn / kn / vv and of red is done
+    __syncthreads();  // every read of the stage, of the input row, of qn / kn / vv and of red is done
     if (gdn_abort) break;
-    if (tid == 0 && u + kGdnStages < u1) {
-      mbar_expect_tx(&full[stage], kGdnStateFloats * 4u);
-      bulk_g2s(gst + stage * kGdnStateFloats, state_of(u + kGdnStages), kGdnStateFloats * 4u, &full[stage]);
-      ++issued;
+    if (tid == 0) {
+      if (u + kGdnStages < u1) {
+        mbar_expect_tx(&full[stage], kGdnStateFloats * 4u);
+        bulk_g2s(gst + stage * kGdnStateFloats, state_of(u + kGdnStages), kGdnStateFloats * 4u, &full[stage]);
+        ++issued;
+      }
+      if (u + kGdnXSlots < u1) {
+        issue_x(u + kGdnXSlots);
+        ++xissued;
+      }
     }
     if (u + 1u < u1) cur = nxt;
   }
-  // an aborted walk leaves no copy in flight: wait (bounded) for the stages' last copies
+  // an aborted walk leaves no copy in flight: wait (bounded) for the last copy into each stage and slot
   if (gdn_abort && tid == 0) {
     for (uint32_t s = 0; s < kGdnStages; ++s) {
-      // copies into stage s: units u0 + s, u0 + s + kGdnStages, ... below u0 + issued
       const uint32_t cnt = issued > s ? (issued - s + kGdnStages - 1u) / kGdnStages : 0u;
       if (cnt) (void)mbar_wait(&full[s], (cnt - 1u) & 1u, nullptr);
+    }
+    for (uint32_t s = 0; s < kGdnXSlots; ++s) {
+      const uint32_t cnt = xissued > s ? (xissued - s + kGdnXSlots - 1u) / kGdnXSlots : 0u;
+      if (cnt) (void)mbar_wait(&xfull[s], (cnt - 1u) & 1u, nullptr);
     }
   }
 }
@@ -947,12 +998,15 @@ cudaError_t launch_gdn(const GdnParams& p, cudaStream_t s, bool pdl) {
     // bulk copies of whole states: 16-byte aligned, and each state row block contiguous
     if ((reinterpret_cast<uintptr_t>(p.rec) % 16u) || (p.rec_seq * 4u) % 16u || (reinterpret_cast<uintptr_t>(p.conv_w) % 16u))
       return cudaErrorMisalignedAddress;
-    const uint32_t smem = kGdnStages * kGdnStateFloats * 4u;
+    if (p.D % 4u || reinterpret_cast<uintptr_t>(p.x) % 16u) return cudaErrorMisalignedAddress;  // input rows by bulk copy
+    const uint32_t smem = (kGdnStages * kGdnStateFloats + kGdnXSlots * p.D) * 4u;
     static std::atomic<int> attr_dev[64];
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
     if (!attr_dev[dev].load()) {
-      const cudaError_t e = cudaFuncSetAttribute(gdn_batch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 static_cast<int>(smem));
+      // the largest stage set (hidden size 256 * kGdnDPer), whatever model opens first
+      const cudaError_t e = cudaFuncSetAttribute(
+          gdn_batch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+          static_cast<int>((kGdnStages * kGdnStateFloats + kGdnXSlots * 256u * kGdnDPer) * 4u));
       if (e != cudaSuccess) return e;
       attr_dev[dev].store(1);
     }
