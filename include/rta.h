@@ -106,16 +106,20 @@ RTA_API rta_status rta_panel_weights(int format, const void* src, uint32_t rows,
  * (RTA_Q4_K_PANEL / RTA_Q6_K_PANEL), rows % 128 == 0, cols % 256 == 0,
  * 1 <= batch <= 256.  Both operands are fp16: x rounded once, each weight
  * rounded once after its block scale is applied (about 3e-4 relative L2 from
- * the exact product at random weights); accumulation is fp32.  When argmax is
- * not NULL the row of the largest y[b][.] (ties -> lowest row) and its value
- * (best, may be NULL) are returned per batch row, and y may be NULL
+ * the exact product at random weights); accumulation is fp32.  `flags`
+ * (formerly accumulate; 0 / 1 keep their meaning): RTA_GEMM_ACCUMULATE adds
+ * into y; RTA_GEMM_SPLIT_ACTIVATIONS takes x as two fp16 operands,
+ * fp16(x) + fp16(x - fp16(x)), leaving only the weight rounding.  When argmax
+ * is not NULL the row of the largest y[b][.] (ties -> lowest row) and its
+ * value (best, may be NULL) are returned per batch row, and y may be NULL
  * (vocabulary readout).  workspace: rta_gemm_tc_workspace_bytes(format,
- * batch, cols) bytes.  Replaces op 2 of
+ * batch, cols) bytes (enough for either mode).  Replaces op 2 of
  * ray_tracing/native/shaders/resident_math.comp:39-75 and the readout ops
  * 16/17/23 (:117-130) for batched rows. */
+enum { RTA_GEMM_ACCUMULATE = 1, RTA_GEMM_SPLIT_ACTIVATIONS = 2 };
 RTA_API size_t rta_gemm_tc_workspace_bytes(int format, uint32_t batch, uint32_t cols);
 RTA_API rta_status rta_gemm_tc(int format, const void* w, uint32_t rows, uint32_t cols, const float* x,
-                               uint32_t batch, float* y, int accumulate, uint32_t* argmax, float* best,
+                               uint32_t batch, float* y, int flags, uint32_t* argmax, float* best,
                                void* workspace, size_t workspace_bytes, void* stream);
 
 /* SwiGLU MLP on the tensor cores: y (+)= Wd swiglu(Wg x, Wu x) with the three
@@ -319,9 +323,14 @@ enum {
   RTA_MODEL_TOKEN_PREFILL = 2,
   /* Prefill chunks with their products on the tensor cores (tcgen05), from
    * panel-order copies of the Q4_K / Q6_K matrices made at open (about the
-   * weights' size again in HBM): one weight pass per chunk, activations
-   * rounded once to fp16 per product (the 16+-sequence arithmetic). */
-  RTA_MODEL_TC_PREFILL = 4
+   * weights' size again in HBM): one weight pass per chunk; each activation
+   * row enters as two fp16 operands (x = fp16(x) + fp16(x - fp16(x))), so the
+   * products carry only the block-scaled weight operand's one fp16 rounding. */
+  RTA_MODEL_TC_PREFILL = 4,
+  /* The batched decode products on the tensor cores (16+ sequences) take each
+   * activation row as two fp16 operands as above (twice the MMA columns)
+   * instead of one fp16 rounding of x. */
+  RTA_MODEL_SPLIT_ACTIVATIONS = 8
 };
 RTA_API rta_status rta_model_open_ex(const rta_model_spec* spec, const uint32_t* params, size_t n_params,
                                      const void* matrices, size_t matrix_bytes, const void* basis, size_t basis_bytes,

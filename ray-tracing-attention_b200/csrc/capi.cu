@@ -111,14 +111,15 @@ rta_status rta_panel_weights(int format, const void* src, uint32_t rows, uint32_
 
 size_t rta_gemm_tc_workspace_bytes(int format, uint32_t batch, uint32_t cols) {
   const size_t keys = (8ull * (batch ? batch : 1) + 255u) / 256u * 256u;
-  return kErrBytes + keys + rta::tc_workspace_bytes(format, batch ? batch : 1, cols);
+  return kErrBytes + keys + rta::tc_workspace_bytes(format, batch ? batch : 1, cols, true);  // either mode
 }
 
 rta_status rta_gemm_tc(int format, const void* w, uint32_t rows, uint32_t cols, const float* x, uint32_t batch,
                        float* y, int accumulate, uint32_t* argmax, float* best, void* workspace,
                        size_t workspace_bytes, void* stream) {
   if ((format != RTA_Q4_K_PANEL && format != RTA_Q6_K_PANEL) || !w || !x || (!y && !argmax) || !workspace ||
-      rows == 0 || rows % 128 || cols == 0 || cols % 256 || batch == 0 || batch > rta::kMaxBatch)
+      rows == 0 || rows % 128 || cols == 0 || cols % 256 || batch == 0 || batch > rta::kMaxBatch ||
+      (accumulate & ~(RTA_GEMM_ACCUMULATE | RTA_GEMM_SPLIT_ACTIVATIONS)))
     return fail(RTA_E_ARG, "rta_gemm_tc: panel format, rows % 128 == 0, cols % 256 == 0, 1 <= batch <= 256");
   if (workspace_bytes < rta_gemm_tc_workspace_bytes(format, batch, cols))
     return fail(RTA_E_ARG, "rta_gemm_tc: workspace too small");
@@ -137,9 +138,11 @@ rta_status rta_gemm_tc(int format, const void* w, uint32_t rows, uint32_t cols, 
   a.x = x;
   a.x_stride = cols;
   a.batch = batch;
-  a.epilogue = accumulate ? rta::kAccumulate : rta::kStore;
+  a.epilogue = rta::kStore;
   a.y = y;
   a.y_stride = rows;
+  a.split = (accumulate & RTA_GEMM_SPLIT_ACTIVATIONS) != 0;
+  if (accumulate & RTA_GEMM_ACCUMULATE) a.epilogue = rta::kAccumulate;
   a.argmax = argmax ? keys : nullptr;
   a.err = err;
   a.xb = ws + kErrBytes + keys_bytes;

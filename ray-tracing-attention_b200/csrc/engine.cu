@@ -172,6 +172,8 @@ struct Engine {
   // a scan over the rows (its state is sequential).
   static constexpr uint32_t kChunk = 64, kChunkSplits = 2;
   bool chunked = false, token_prefill = false, tc_prefill = false;
+  bool split_decode = false;  // RTA_MODEL_SPLIT_ACTIVATIONS: batched decode products take x as two fp16 operands
+  bool tc_split = false;      // the products being recorded take x as two fp16 operands
   cudaGraphExec_t g_chunk = nullptr;
   uint32_t kernels_per_chunk = 0;
   DevBuf<float> c_rows, c_proj, c_q, c_att, c_gdn, c_act, c_gu, c_pm, c_pz, c_po, c_gates, c_qk, c_vc;
@@ -435,8 +437,9 @@ struct Engine {
     spec = sp;
     device = dev;
     require((flags & ~static_cast<uint32_t>(RTA_MODEL_PACKET_HISTORY | RTA_MODEL_TOKEN_PREFILL |
-                                            RTA_MODEL_TC_PREFILL)) == 0,
+                                            RTA_MODEL_TC_PREFILL | RTA_MODEL_SPLIT_ACTIVATIONS)) == 0,
             "unknown model flags", RTA_E_ARG);
+    split_decode = (flags & RTA_MODEL_SPLIT_ACTIVATIONS) != 0;
     token_prefill = (flags & RTA_MODEL_TOKEN_PREFILL) != 0;
     tc_prefill = (flags & RTA_MODEL_TC_PREFILL) != 0;
     packet_history = (flags & RTA_MODEL_PACKET_HISTORY) != 0;
@@ -599,7 +602,9 @@ struct Engine {
       gu.alloc(static_cast<size_t>(rows) * 2 * F());
       size_t ws = 0;
       for (uint32_t cols : {D, Q(), std::max(1u, S()), F()})
-        if (cols % 256 == 0) ws = std::max({ws, tc_workspace_bytes(kQ4KPanel, rows, cols), tc_workspace_bytes(kQ6KPanel, rows, cols)});
+        if (cols % 256 == 0)
+          ws = std::max({ws, tc_workspace_bytes(kQ4KPanel, rows, cols, split_decode),
+                         tc_workspace_bytes(kQ6KPanel, rows, cols, split_decode)});
       tc_ws.alloc(ws);
     }
     int sms = 148;
@@ -647,7 +652,8 @@ struct Engine {
       size_t ws = 0;
       for (uint32_t cols : {D, Q(), std::max(1u, S()), F()})
         if (cols % 256 == 0)
-          ws = std::max({ws, tc_workspace_bytes(kQ4KPanel, kChunk, cols), tc_workspace_bytes(kQ6KPanel, kChunk, cols)});
+          ws = std::max({ws, tc_workspace_bytes(kQ4KPanel, kChunk, cols, true),
+                         tc_workspace_bytes(kQ6KPanel, kChunk, cols, true)});
       c_tcws.alloc(ws);
     }
     // [layer][sequence] x per-sequence blocks
@@ -714,6 +720,7 @@ struct Engine {
     t.xb = ws->p;
     t.xb_bytes = ws->n;
     t.pdl = a.pdl;
+    t.split = tc_split;
     return launch_tc_gemm(t, s);
   }
 
@@ -769,6 +776,7 @@ struct Engine {
   uint32_t record_step(bool decode, bool capture_rows = false) {
     const cudaStream_t s = stream;
     uint32_t n = 0;
+    tc_split = split_decode;
     Control* c = ctrl.p;
     const uint32_t* running = &c->running;
     // this rank's sequences (all of them without a team): attention / recurrent blocks
@@ -1075,6 +1083,7 @@ struct Engine {
   // One prefill chunk of a single-sequence handle: kChunk consecutive prompt
   // positions from the control block's pos_next (rows past the prompt sit out).
   uint32_t record_chunk() {
+    tc_split = true;  // prefill chunk products on the tensor cores carry x exactly (two fp16 operands)
     const cudaStream_t s = stream;
     uint32_t n = 0;
     Control* c = ctrl.p;

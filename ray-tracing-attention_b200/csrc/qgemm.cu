@@ -98,6 +98,7 @@ struct Params {
   uint32_t slots;        // activation block columns held in shared memory (slot = block column % slots)
   uint32_t total;        // panels of the product (ntiles * KB)
   uint32_t whole_tiles;  // 1: every unit is a whole tile (argmax, plain stores); 0: partial sums land atomically
+  uint32_t split;        // 1: B columns n and n + N/2 carry fp16(x) and fp16(x - fp16(x)) of batch row n
   const uint8_t* xb;  // prep output
   uint32_t blk;       // prep bytes per block
   uint32_t batch;     // live batch rows of this launch (<= N)
@@ -166,6 +167,7 @@ struct Prep {
   uint8_t* xb;
   uint32_t blk;
   bool q4;
+  bool split;  // rows N/2 .. N-1 of the stage carry the fp16 remainders of rows 0 .. N/2-1
   float* zero_y;  // split stores: y rows of live sequences are zeroed here before the partial sums land
   uint32_t zero_cols, zero_stride;
 };
@@ -639,7 +641,8 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 19 warps: <
     __syncwarp();
   } else if (warp >= 2 && warp < 10) {
     // ------------------------------------------------------------- epilogue
-    constexpr uint32_t NH = N / 2;  // batch columns of this warp
+    const uint32_t NB = p.split ? static_cast<uint32_t>(N) / 2u : static_cast<uint32_t>(N);  // batch columns
+    const uint32_t NH = NB / 2u;  // batch columns of this warp (<= 32)
     const uint32_t qd = warp & 3u, m = 32u * qd + lane, c0 = (warp - 2u) >> 2;  // columns c0*NH ..
     const uint32_t lane_addr = (32u * qd) << 16;
     pdl_wait();  // residual targets and running flags are written by earlier kernels
@@ -679,6 +682,16 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 19 warps: <
           tmem_wait_ld();
 #pragma unroll
           for (uint32_t e = 0; e < 8u; ++e) v[e] += v2[e];
+        }
+        if (p.split) {  // + the products of the remainders (D columns N/2 on)
+#pragma unroll
+          for (uint32_t i = 0; i < kParts; ++i) {
+            float v2[8];
+            tmem_ld8(dcol + c + static_cast<uint32_t>(N) / 2u + i * static_cast<uint32_t>(N), v2);
+            tmem_wait_ld();
+#pragma unroll
+            for (uint32_t e = 0; e < 8u; ++e) v[e] += v2[e];
+          }
         }
         tmem_wait_ld();
         if (p.y) {
@@ -809,7 +822,7 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 19 warps: <
   if (warp >= 2 && warp < 10) {
     asm volatile("bar.sync 1, 256;" ::: "memory");
     const uint32_t t = threadIdx.x - 64u;
-    if (p.argmax && t < static_cast<uint32_t>(N) && t < p.batch && cand[t])
+    if (p.argmax && t < (p.split ? static_cast<uint32_t>(N) / 2u : static_cast<uint32_t>(N)) && t < p.batch && cand[t])
       atomicMax(p.argmax + static_cast<size_t>(t) * p.arg_step, cand[t]);
   }
   tc_fence_before();
@@ -828,17 +841,20 @@ __global__ void __maxnreg__(96) tc_gemm_kernel(const Params p) {  // 19 warps: <
 __global__ void __launch_bounds__(256) tc_prep_kernel(const Prep p) {
   __shared__ float red[8];
   const uint32_t n = blockIdx.x, tid = threadIdx.x, lane = tid & 31u;
+  // split stages: CTA n >= N/2 writes the fp16 remainders of batch row n - N/2
+  const uint32_t nr = p.split ? n % (p.N / 2u) : n;
+  const bool rem = p.split && n >= p.N / 2u;
   pdl_wait();
   pdl_launch_dependents();
-  const bool live = n < p.batch && (!p.running || p.running[static_cast<size_t>(n) * p.run_step] != 0u);
-  if (live && p.zero_y) {  // this chunk's share of the output row
+  const bool live = nr < p.batch && (!p.running || p.running[static_cast<size_t>(nr) * p.run_step] != 0u);
+  if (live && p.zero_y && !rem) {  // this chunk's share of the output row
     const uint32_t per = (p.zero_cols + gridDim.y - 1u) / gridDim.y;
     const uint32_t a = blockIdx.y * per, b = min(p.zero_cols, a + per);
-    float* yr = p.zero_y + static_cast<size_t>(n) * p.zero_stride;
+    float* yr = p.zero_y + static_cast<size_t>(nr) * p.zero_stride;
     for (uint32_t c = a + tid; c < b; c += 256u) yr[c] = 0.f;
   }
-  const float* xr = p.x + static_cast<size_t>(n < p.batch ? n : 0u) * p.x_stride;
-  const float* zr = p.z ? p.z + static_cast<size_t>(n < p.batch ? n : 0u) * p.z_stride : nullptr;
+  const float* xr = p.x + static_cast<size_t>(nr < p.batch ? nr : 0u) * p.x_stride;
+  const float* zr = p.z ? p.z + static_cast<size_t>(nr < p.batch ? nr : 0u) * p.z_stride : nullptr;
   const uint32_t nch = p.cols / 8u;
   float inv = 1.f;
   if (live && p.prologue == kRmsNorm) {
@@ -906,7 +922,11 @@ __global__ void __launch_bounds__(256) tc_prep_kernel(const Prep p) {
                    (n / 8u) * 2048u + kc * 128u + (n % 8u) * 16u;
     __half2 hv[4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) hv[e] = __floats2half2_rn(v[2 * e], v[2 * e + 1]);
+    for (int e = 0; e < 4; ++e) {
+      hv[e] = __floats2half2_rn(v[2 * e], v[2 * e + 1]);
+      if (rem)  // the remainder x - fp16(x), itself rounded to fp16 (x = hi + lo to about 2^-22)
+        hv[e] = __floats2half2_rn(v[2 * e] - __low2float(hv[e]), v[2 * e + 1] - __high2float(hv[e]));
+    }
     *reinterpret_cast<uint4*>(dst) = make_uint4(h2_bits(hv[0]), h2_bits(hv[1]), h2_bits(hv[2]), h2_bits(hv[3]));
     if (p.q4) {  // 32-group sum of the fp16 x over 4 consecutive chunks (lanes 4i..4i+3)
       float s = 0.f;
@@ -1044,6 +1064,7 @@ cudaError_t launch_fmt(const tc::Params& p, const tc::Prep& pr, uint32_t grid, b
     case 16: return launch_n<FMT, 16>(p, pr, grid, pdl, s);
     case 32: return launch_n<FMT, 32>(p, pr, grid, pdl, s);
     case 64: return launch_n<FMT, 64>(p, pr, grid, pdl, s);
+    case 128: return launch_n<FMT, 128>(p, pr, grid, pdl, s);  // split stages of 64 batch rows
     default: return cudaErrorInvalidValue;
   }
 }
@@ -1051,9 +1072,9 @@ cudaError_t launch_fmt(const tc::Params& p, const tc::Prep& pr, uint32_t grid, b
 uint32_t tile_n(uint32_t rows) { return rows <= 16u ? 16u : rows <= 32u ? 32u : 64u; }
 }  // namespace
 
-size_t tc_workspace_bytes(int fmt, uint32_t batch, uint32_t cols) {
+size_t tc_workspace_bytes(int fmt, uint32_t batch, uint32_t cols, bool split) {
   const bool q4 = fmt == kQ4KPanel || fmt == kQ4K;
-  const uint32_t N = tile_n(batch < kTcMaxN ? batch : kTcMaxN);
+  const uint32_t N = tile_n(batch < kTcMaxN ? batch : kTcMaxN) * (split ? 2u : 1u);
   return static_cast<size_t>(cols / 256u) * tc::blk_bytes(q4, N);
 }
 
@@ -1068,7 +1089,7 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
   if ((a.prologue == kRmsNorm || a.prologue == kHeadGate) && !a.norm_w) return cudaErrorInvalidValue;
   if (a.prologue == kHeadGate && a.cols % 128u) return cudaErrorInvalidValue;
   if (a.epilogue != kStore && a.epilogue != kAccumulate) return cudaErrorInvalidValue;
-  if (a.xb_bytes < tc_workspace_bytes(a.fmt, a.batch, a.cols)) return cudaErrorInvalidValue;
+  if (a.xb_bytes < tc_workspace_bytes(a.fmt, a.batch, a.cols, a.split)) return cudaErrorInvalidValue;
   if ((reinterpret_cast<uintptr_t>(a.w0) | reinterpret_cast<uintptr_t>(a.w1) | reinterpret_cast<uintptr_t>(a.xb) |
        reinterpret_cast<uintptr_t>(a.x) | reinterpret_cast<uintptr_t>(a.z)) & 15u)
     return cudaErrorInvalidValue;
@@ -1102,7 +1123,8 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
     pr.prologue = a.prologue;
     pr.cols = a.cols;
     pr.batch = nb;
-    pr.N = tile_n(nb);
+    pr.N = tile_n(nb) * (a.split ? 2u : 1u);  // split: hi and lo stages of every row
+    pr.split = a.split;
     const uint32_t rstep = a.running_step ? a.running_step : 1u;
     pr.running = a.running ? a.running + static_cast<size_t>(b0) * rstep : nullptr;
     pr.run_step = rstep;
@@ -1125,6 +1147,7 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
     p.width = whole ? KB : p.slots;
     p.total = total;
     p.whole_tiles = whole ? 1u : 0u;
+    p.split = a.split ? 1u : 0u;
 
     p.xb = a.xb;
     p.blk = pr.blk;

@@ -112,11 +112,15 @@ struct TcGemmArgs {
   uint32_t* err = nullptr;
   const uint32_t* running = nullptr;
   uint32_t running_step = 1;
-  uint8_t* xb = nullptr;  // workspace of tc_workspace_bytes(fmt, batch, cols) bytes
+  uint8_t* xb = nullptr;  // workspace of tc_workspace_bytes(fmt, batch, cols, split) bytes
   size_t xb_bytes = 0;
   bool pdl = false;
+  // Activations as two fp16 operands (x = fp16(x) + fp16(x - fp16(x))): the
+  // products then carry only the weight operand's rounding, at twice the MMA
+  // columns.
+  bool split = false;
 };
-size_t tc_workspace_bytes(int fmt, uint32_t batch, uint32_t cols);
+size_t tc_workspace_bytes(int fmt, uint32_t batch, uint32_t cols, bool split = false);
 cudaError_t launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s);
 // act[r][c] = swiglu(gu[r][c], gu[r][F + c]) for r < rows, c < F.
 cudaError_t launch_swiglu_rows(const float* gu, uint32_t rows, uint32_t F, uint32_t gu_stride, float* act,

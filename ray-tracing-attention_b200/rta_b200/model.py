@@ -61,6 +61,7 @@ _SIGS = {
 PACKET_HISTORY = 1  # RTA_MODEL_PACKET_HISTORY
 TOKEN_PREFILL = 2   # RTA_MODEL_TOKEN_PREFILL
 TC_PREFILL = 4      # RTA_MODEL_TC_PREFILL
+SPLIT_ACTIVATIONS = 8  # RTA_MODEL_SPLIT_ACTIVATIONS
 PROFILE_KINDS = ("start", "readout", "embed", "qkv", "attention_prep", "attention", "o_proj", "in_proj",
                  "gated_delta", "out_proj", "gate_up", "down", "exchange")  # RTA_PROF_* (include/rta.h)
 RESOURCE_NAMES = ("payload_bytes", "derived_layer_bytes", "history_bytes", "recurrent_state_bytes", "capacity",
@@ -115,10 +116,11 @@ class ResidentModel:
     @classmethod
     def from_payloads(cls, spec: assets.Spec, params, matrices, basis, capacity: int, device: int | None = None,
                       sequences: int = 1, history: str = "fp16", token_prefill: bool = False,
-                      tc_prefill: bool = False):
+                      tc_prefill: bool = False, split_activations: bool = False):
         """history: "fp16" K/V rings, or "packet" (the reference's Q4_K/Q6_K history packets).
         token_prefill: prefill one position per step instead of 64-position chunks;
-        tc_prefill: the chunks' products on the tensor cores (panel copies of the weights).
+        tc_prefill: the chunks' products on the tensor cores (panel copies of the weights);
+        split_activations: batched decode products take x as two fp16 operands.
         params: uint32 numpy; matrices/basis: uint8 numpy (host) or torch CUDA tensors (device).
         device: CUDA ordinal (default: the caller's current device)."""
         device = _current_device() if device is None else device
@@ -137,7 +139,7 @@ class ResidentModel:
         if history not in ("fp16", "packet"):
             raise ValueError("history must be 'fp16' or 'packet'")
         flags = ((PACKET_HISTORY if history == "packet" else 0) | (TOKEN_PREFILL if token_prefill else 0)
-                 | (TC_PREFILL if tc_prefill else 0))
+                 | (TC_PREFILL if tc_prefill else 0) | (SPLIT_ACTIVATIONS if split_activations else 0))
         _check(lib.rta_model_open_ex(ctypes.byref(cs), _np_ptr(params), params.size, mp, mb, bp, bb, capacity,
                                      sequences, flags, device, ctypes.byref(h)))
         del mkeep, bkeep
@@ -210,7 +212,7 @@ class ResidentModel:
     @classmethod
     def synthetic(cls, spec: assets.Spec, seed: int = 0, capacity: int = 1024, device: int | None = None,
                   sequences: int = 1, history: str = "fp16", token_prefill: bool = False,
-                  tc_prefill: bool = False):
+                  tc_prefill: bool = False, split_activations: bool = False):
         """Random-init model of `spec` generated on the GPU (payloads in the exporter's layout)."""
         import torch
         device = _current_device() if device is None else device
@@ -218,7 +220,7 @@ class ResidentModel:
         layout = assets.plan(spec, seed)
         mats, basis = assets.generate_device(layout, seed)
         model = cls.from_payloads(spec, layout.params(), mats, basis, capacity, device, sequences, history,
-                                  token_prefill, tc_prefill)
+                                  token_prefill, tc_prefill, split_activations)
         model.layout = layout
         del mats, basis
         torch.cuda.empty_cache()

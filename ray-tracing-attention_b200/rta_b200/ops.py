@@ -83,9 +83,10 @@ def panel_weights(fmt: int, w: torch.Tensor, rows: int, cols: int) -> tuple[int,
 
 def gemm_tc(fmt: int, w: torch.Tensor, rows: int, cols: int, x: torch.Tensor, y: torch.Tensor | None = None,
             accumulate: bool = False, argmax: bool = False, store: bool = True,
-            workspace: torch.Tensor | None = None):
+            workspace: torch.Tensor | None = None, split: bool = False):
     """Tensor-core batched product with panel weights: returns (y, argmax ids, best)
-    (ids / best None unless argmax; y None when store is False)."""
+    (ids / best None unless argmax; y None when store is False).  split: x enters
+    as two fp16 operands (fp16(x) + fp16(x - fp16(x)))."""
     x = x.reshape(-1, cols)
     B = x.shape[0]
     lib = _lib.load()
@@ -95,7 +96,8 @@ def gemm_tc(fmt: int, w: torch.Tensor, rows: int, cols: int, x: torch.Tensor, y:
         y = torch.empty(B, rows, dtype=torch.float32, device=x.device)
     ids = torch.empty(B, dtype=torch.int32, device=x.device) if argmax else None
     best = torch.empty(B, dtype=torch.float32, device=x.device) if argmax else None
-    check(lib.rta_gemm_tc(fmt, _ptr(w), rows, cols, _ptr(x), B, _ptr(y if store else None), int(accumulate),
+    flags = (1 if accumulate else 0) | (2 if split else 0)  # RTA_GEMM_ACCUMULATE, RTA_GEMM_SPLIT_ACTIVATIONS
+    check(lib.rta_gemm_tc(fmt, _ptr(w), rows, cols, _ptr(x), B, _ptr(y if store else None), flags,
                           _ptr(ids), _ptr(best), _ptr(workspace), workspace.numel(), _stream()))
     return (y if store else None), ids, best
 

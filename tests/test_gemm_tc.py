@@ -281,6 +281,31 @@ def test_gemm_tc_parity(ops, fmt, rows, cols, batch):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("fmt,rows,cols,batch", [(12, 384, 2048, 64), (12, 256, 4096, 20), (14, 128, 2048, 33),
+                                                 (14, 640, 2048, 64), (12, 512, 12288, 16)])
+def test_gemm_tc_split_activations(ops, fmt, rows, cols, batch):
+    """RTA_GEMM_SPLIT_ACTIVATIONS: x enters as fp16(x) + fp16(x - fp16(x)) (twice
+    the MMA columns: 32, 64 or 128), so only the weight operand's rounding is
+    left -- within the tolerance, and no farther from the oracle than the one
+    fp16 rounding of x; stores and residual adds alike."""
+    rng = np.random.default_rng(rows + cols + batch + 7)
+    W = oracle.quantize(fmt, rng.normal(0, 0.02, rows * cols).astype(np.float32))
+    x = rng.normal(0, 1, (batch, cols)).astype(np.float32)
+    x[1] = 0.0
+    code, P = ops.panel_weights(fmt, _t(W), rows, cols)
+    want = oracle.gemv(fmt, W, rows, cols, x)
+    y_plain, _, _ = ops.gemm_tc(code, P, rows, cols, _t(x))
+    y_split, _, _ = ops.gemm_tc(code, P, rows, cols, _t(x), split=True)
+    e_plain, e_split = rel_l2(_np(y_plain), want), rel_l2(_np(y_split), want)
+    assert e_split < TOL and e_split <= e_plain, (e_split, e_plain)
+    assert np.all(_np(y_split)[1] == 0)
+    y0 = rng.normal(0, 1, (batch, rows)).astype(np.float32)
+    y = _t(y0)
+    ops.gemm_tc(code, P, rows, cols, _t(x), y=y, accumulate=True, split=True)
+    assert rel_l2(_np(y) - y0, want) < TOL
+
+
+@pytest.mark.gpu
 @pytest.mark.parametrize("fmt,rows,cols", [(12, 256, 2048), (14, 256, 2048), (12, 1024, 4096), (14, 512, 12288)])
 def test_gemm_tc_accumulates_into_the_residual(ops, fmt, rows, cols):
     """K-split schedules (8 slices of 1, 2 or 6 blocks here) add their partial
@@ -298,16 +323,17 @@ def test_gemm_tc_accumulates_into_the_residual(ops, fmt, rows, cols):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("batch", [16, 64])
-def test_gemm_tc_readout_argmax(ops, batch):
-    """Config 3 shape class: Q6_K vocabulary rows with the per-row argmax."""
+@pytest.mark.parametrize("batch,split", [(16, False), (64, False), (64, True)])
+def test_gemm_tc_readout_argmax(ops, batch, split):
+    """Config 3 shape class: Q6_K vocabulary rows with the per-row argmax (also
+    with split activations: 128 MMA columns, whole tiles per CTA)."""
     V, D = 151936 // 8, 2048  # 18992 rows (a multiple of 128 would be needed: trimmed below)
     V = V // 128 * 128
     rng = np.random.default_rng(batch)
     W = oracle.quantize(14, rng.normal(0, 0.02, V * D).astype(np.float32))
     x = rng.normal(0, 1, (batch, D)).astype(np.float32)
     code, P = ops.panel_weights(14, _t(W), V, D)
-    lg, ids, best = ops.gemm_tc(code, P, V, D, _t(x), argmax=True)
+    lg, ids, best = ops.gemm_tc(code, P, V, D, _t(x), argmax=True, split=split)
     want_lg, want_arg, want_best = oracle.lmhead(14, W, V, D, x)
     lg, ids, best = _np(lg), _np(ids).astype(np.int64), _np(best)
     assert rel_l2(lg, want_lg) < TOL
@@ -317,5 +343,5 @@ def test_gemm_tc_readout_argmax(ops, batch):
         if top2[1] - top2[0] > 1e-3 * np.abs(want_lg[b]).max():
             assert ids[b] == int(want_arg[b]), b
     # argmax only (no logits written)
-    _, ids2, best2 = ops.gemm_tc(code, P, V, D, _t(x), argmax=True, store=False)
+    _, ids2, best2 = ops.gemm_tc(code, P, V, D, _t(x), argmax=True, store=False, split=split)
     assert np.array_equal(_np(ids2).astype(np.int64), ids) and np.array_equal(_np(best2), best)

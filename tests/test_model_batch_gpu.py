@@ -106,12 +106,13 @@ def test_seeded_histories_decode():
 TOL = 1e-3  # relative L2
 
 
-@pytest.mark.parametrize("sequences", [18, 20])
-def test_tensor_core_batch_tracks_the_oracle(sequences):
-    """18 or 20 sequences: every matrix on the tensor cores; at 20 x 16 heads the
-    gated delta runs one CTA per (sequence, head) with its inputs staged by bulk
-    copies (at 18, eight CTAs per head).  Per sequence: greedy tokens equal the
-    oracle's wherever the oracle's top-2 margin exceeds the tolerance (the first
+@pytest.mark.parametrize("sequences,split", [(18, False), (20, False), (20, True)])
+def test_tensor_core_batch_tracks_the_oracle(sequences, split):
+    """18 or 20 sequences: every matrix on the tensor cores (with `split`, each
+    activation row as two fp16 operands, RTA_MODEL_SPLIT_ACTIVATIONS); at
+    20 x 16 heads the gated delta runs the persistent (head, sequence) walk (at
+    18, eight CTAs per head).  Per sequence: greedy tokens equal the oracle's
+    wherever the oracle's top-2 margin exceeds the tolerance (the first
     legitimate near-tie flip ends the comparison, as in the single-sequence
     tests)."""
     import torch
@@ -122,7 +123,7 @@ def test_tensor_core_batch_tracks_the_oracle(sequences):
     layout = assets.plan(spec, 9)
     mats, basis = assets.generate_device(layout, 9)
     params = layout.params()
-    batch = ResidentModel.from_payloads(spec, params, mats, basis, 32, sequences=sequences)
+    batch = ResidentModel.from_payloads(spec, params, mats, basis, 32, sequences=sequences, split_activations=split)
     m, b = mats.cpu().numpy(), basis.cpu().numpy()
     del mats, basis
     torch.cuda.empty_cache()
