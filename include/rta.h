@@ -330,7 +330,33 @@ enum {
   /* The batched decode products on the tensor cores (16+ sequences) take each
    * activation row as two fp16 operands as above (twice the MMA columns)
    * instead of one fp16 rounding of x. */
-  RTA_MODEL_SPLIT_ACTIVATIONS = 8
+  RTA_MODEL_SPLIT_ACTIVATIONS = 8,
+  /* The decode caches of a single-sequence handle (the worker's `cache`
+   * argument, optical_resident.cpp:118, :212-216):
+   * - prefix boundaries (SharedHistoryCache, shared_history_cache.hpp:5-142):
+   *   every prefill that computes positions saves the decode state at the
+   *   prompt's end (residual row, recurrent and convolution states) and the
+   *   attention history of the prompt in immutable 16-position blocks shared
+   *   by every boundary whose ids agree up to a block's end;
+   *   rta_model_finish_history saves the same at a generated reply's end.  A
+   *   prefill whose ids extend a saved boundary restores it and computes only
+   *   the remaining positions;
+   * - the reply tree (ReplyTreeCache, reply_cache.hpp:6-68): every generated
+   *   token is recorded under the 256-bit address of the state it was read
+   *   from (a device digest of every live input of the decode step: residual
+   *   row, recurrent and convolution states, the visible history rows with
+   *   their positions, the position and the stop ids; OpticalPathKey,
+   *   optical_path_key.hpp:7-91) and its position, with the successor state's
+   *   address.  A generate call first follows the tree from the current
+   *   address and replays the tokens it holds without computing them; the
+   *   device state catches up (a saved boundary, then one step per token)
+   *   only when a later call has to compute.  The tree holds 65536 nodes, the
+   *   oldest overwritten first, and serves positions inside the ring.
+   * The tokens are those of an uncached handle: a replayed token was computed
+   * from a state with the same address.  Boundaries and blocks live in device
+   * memory up to rta_model_cache_limit bytes (least recently used dropped
+   * first). */
+  RTA_MODEL_CACHE = 16
 };
 RTA_API rta_status rta_model_open_ex(const rta_model_spec* spec, const uint32_t* params, size_t n_params,
                                      const void* matrices, size_t matrix_bytes, const void* basis, size_t basis_bytes,
@@ -463,6 +489,57 @@ RTA_API rta_status rta_model_mlp(rta_model* model, uint32_t layer, const float* 
  * argmax (ties -> lowest id) of the readout of `hidden`; logits may be NULL. */
 RTA_API rta_status rta_model_vocabulary(rta_model* model, const float* hidden, float* logits, uint32_t* argmax,
                                         float* best);
+/* Prefill with the checkpoint of worker ops 11 / 12 (optical_resident.cpp:616-622):
+ * `boundary` (1..n) is the stable prefix the request names (n for op 1); with
+ * RTA_MODEL_CACHE it is reported back as the stable prefix and decides the
+ * snapshot kind.  Without the cache this is rta_model_prefill. */
+RTA_API rta_status rta_model_prefill_checkpoint(rta_model* model, const uint32_t* ids, uint32_t n,
+                                                const uint32_t stops[2], uint32_t boundary, double* gpu_ms);
+/* Counters of the cache's last prefill / generate / finish_history, RTA_CACHE_*
+ * indices (the history-cache fields of the prefill reply, resident_runtime.py:
+ * 134-147; the reply-cache fields of the generation reply, :200-218), and
+ * ms[3] = (prefix lookup wall ms, reply-tree gpu ms of the last generate, state
+ * catch-up gpu ms of the last generate).  n words are written (at most
+ * RTA_CACHE_INFO_WORDS); ms may be NULL. */
+enum {
+  RTA_CACHE_PREFILL_HIT = 0,        /* a saved boundary matched a prefix of the prompt */
+  RTA_CACHE_REUSED_TOKENS = 1,      /* prompt positions restored instead of computed */
+  RTA_CACHE_STABLE_TOKENS = 2,      /* the request's checkpoint boundary */
+  RTA_CACHE_SNAPSHOT_KIND = 3,      /* 0 miss, 1 the whole prompt, 2 the checkpoint, 3 another prefix */
+  RTA_CACHE_SHARED_BLOCKS = 4,      /* history blocks of the boundary that was restored */
+  RTA_CACHE_SAVED_BOUNDARIES = 5,   /* boundaries saved by the call */
+  RTA_CACHE_BOUNDARIES = 6,         /* boundaries held */
+  RTA_CACHE_LOOKUPS = 7,            /* boundary lengths probed */
+  RTA_CACHE_COMPUTED_TOKENS = 8,    /* prompt positions computed */
+  RTA_CACHE_EVICTIONS = 9,          /* boundaries dropped for the byte limit so far */
+  RTA_CACHE_ADDRESS_HIT = 10,       /* the boundary held the state address: no digest ran */
+  RTA_CACHE_REPLAYED_TOKENS = 11,   /* generate: tokens taken from the reply tree */
+  RTA_CACHE_TREE_QUERIES = 12,      /* generate: reply-tree lookups */
+  RTA_CACHE_TREE_NODES = 13,        /* nodes held */
+  RTA_CACHE_TREE_CAPACITY = 14,     /* 65536 */
+  RTA_CACHE_TREE_LEAF = 15,         /* slot of the last replayed node (0xffffffff: none) */
+  RTA_CACHE_RESTORED_TOKENS = 16,   /* generate: replayed tokens the device state caught up on */
+  RTA_CACHE_CHECKPOINT_RESTORED = 17, /* generate: the catch-up started from a saved boundary */
+  RTA_CACHE_FINISH_SAVED = 18,      /* finish_history: a boundary was saved */
+  RTA_CACHE_FINISH_TOKENS = 19,     /* finish_history: its length */
+  RTA_CACHE_BYTES = 20,             /* device bytes held by boundaries and blocks */
+  RTA_CACHE_DIGESTS = 21,           /* state digests run by the call */
+  RTA_CACHE_INFO_WORDS = 22
+};
+RTA_API rta_status rta_model_cache_info(rta_model* model, uint64_t* out, size_t n, double* ms);
+/* Worker op 13 (finishHistory, optical_resident.cpp:743-759): save the prompt
+ * plus the generated reply (a trailing stop id left out: it has no state) as a
+ * boundary, when the device state has computed every one of them and they fit
+ * the ring.  saved = 1 when a new boundary was saved, tokens = its length,
+ * boundaries = boundaries held (any may be NULL). */
+RTA_API rta_status rta_model_finish_history(rta_model* model, uint64_t* saved, uint64_t* tokens,
+                                            uint64_t* boundaries);
+/* Device bytes the boundaries and history blocks may hold (default: a quarter
+ * of the device memory free at open, at most 8 GiB). */
+RTA_API rta_status rta_model_cache_limit(rta_model* model, uint64_t bytes);
+/* The 256-bit address of the current decode state (the digest the reply tree
+ * keys on), after the state has caught up with every emitted token. */
+RTA_API rta_status rta_model_state_address(rta_model* model, uint32_t address[8], uint32_t* position);
 /* Current residual state (hidden_size floats) and absolute position (sequence 0). */
 RTA_API rta_status rta_model_state(rta_model* model, float* state, uint32_t* position);
 /* Resource counters, worker op 8: payload bytes, derived layer bytes, KV bytes,

@@ -11,6 +11,7 @@
 // embedding -> layers).  Positions, the running flag and emitted ids live in a
 // device control block, so the graphs replay unchanged step after step.
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -21,6 +22,7 @@
 
 #include "../../include/rta.h"
 #include "attention.h"
+#include "cache.h"
 #include "layers.h"
 #include "packets.cuh"
 #include "rta_internal.h"
@@ -219,7 +221,36 @@ struct Engine {
   uint32_t S() const { return spec.state_heads * spec.state_head_dim; }
   uint32_t K() const { return spec.state_key_heads * 128u; }
 
+  // ---------------------------------------------------------------- caches
+  // Prefix boundaries, the reply tree and the state address of a
+  // single-sequence handle opened with RTA_MODEL_CACHE (cache.h).
+  struct Caches {
+    HistoryIndex index;
+    ReplyTree tree;
+    DevBuf<uint32_t> slot_hash;  // [n_full][capacity][8] row digests
+    DevBuf<uint32_t> cursor;     // [1] history positions digested so far
+    DevBuf<uint32_t> partial;    // [kDigestBlocks][8]
+    DevBuf<uint32_t> addresses;  // [kMaxOut + 1][8]: slot 0 the state now, slot i + 1 after step i
+    DevBuf<CopySeg> segs;        // the copy list of one save / restore
+    uint64_t budget = 0;
+    uint32_t epoch = 0;
+    // The live sequence: its prompt, the tokens emitted since (a trailing stop
+    // id is emitted but never consumed), how many of them the device state has
+    // consumed, and the address of the state after all of them.
+    std::vector<uint32_t> prefix, gen;
+    uint32_t fwd = 0;
+    bool ready = false;      // prefix / gen describe the handle's sequence (a cached prefill ran)
+    bool prefix_ok = false;  // boundaries may be saved from / restored into the live state
+    Key256 address{};
+    bool address_ok = false;
+    std::vector<std::shared_ptr<HistoryBlock>> attached;  // blocks of the last restored boundary
+    uint64_t info[RTA_CACHE_INFO_WORDS] = {};
+    double ms[3] = {0.0, 0.0, 0.0};
+  };
+  std::unique_ptr<Caches> cache;
+
   ~Engine() {
+    cache.reset();  // stream-ordered frees need the stream
     if (g_decode) cudaGraphExecDestroy(g_decode);
     if (g_prefill) cudaGraphExecDestroy(g_prefill);
     if (g_prefill_cap) cudaGraphExecDestroy(g_prefill_cap);
@@ -437,7 +468,8 @@ struct Engine {
     spec = sp;
     device = dev;
     require((flags & ~static_cast<uint32_t>(RTA_MODEL_PACKET_HISTORY | RTA_MODEL_TOKEN_PREFILL |
-                                            RTA_MODEL_TC_PREFILL | RTA_MODEL_SPLIT_ACTIVATIONS)) == 0,
+                                            RTA_MODEL_TC_PREFILL | RTA_MODEL_SPLIT_ACTIVATIONS |
+                                            RTA_MODEL_CACHE)) == 0,
             "unknown model flags", RTA_E_ARG);
     split_decode = (flags & RTA_MODEL_SPLIT_ACTIVATIONS) != 0;
     token_prefill = (flags & RTA_MODEL_TOKEN_PREFILL) != 0;
@@ -447,6 +479,8 @@ struct Engine {
     nseq = sequences;
     na = nseq;
     if (tm) setup_team(tm, seq_starts);
+    require(!(flags & RTA_MODEL_CACHE) || (nseq == 1 && !tm), "the caches serve single-sequence handles",
+            RTA_E_ARG);
     require(spec.depth >= 1 && spec.depth <= 256, "depth must be 1..256", RTA_E_ARG);
     require(spec.hidden_size % 256 == 0 && spec.middle_size % 256 == 0, "hidden/middle must be multiples of 256",
             RTA_E_ARG);
@@ -677,11 +711,27 @@ struct Engine {
       freq[p] = std::pow(spec.rope_theta, -static_cast<float>(p) / static_cast<float>(spec.rotary_dim / 2u));
     inv_freq.alloc(hd / 2);
     RTA_CUDA(cudaMemcpyAsync(inv_freq.p, freq.data(), freq.size() * 4, cudaMemcpyHostToDevice, stream));
+    if (flags & RTA_MODEL_CACHE) open_caches();
     reset_sequence();
     capture();
   }
 
+  void open_caches() {
+    cache = std::make_unique<Caches>();
+    Caches& c = *cache;
+    c.slot_hash.alloc(static_cast<size_t>(std::max(1u, n_full)) * capacity * 8u);
+    c.cursor.alloc(1);
+    c.partial.alloc(static_cast<size_t>(kDigestBlocks) * 8u);
+    c.addresses.alloc((kMaxOut + 1ull) * 8u);
+    const size_t per_block = std::max(1u, n_full) * (packet_history ? 1ull : 2ull * spec.kv_heads);
+    c.segs.alloc((capacity / 16ull + 2ull) * per_block);
+    size_t free_b = 0, total_b = 0;
+    RTA_CUDA(cudaMemGetInfo(&free_b, &total_b));
+    c.budget = std::min<uint64_t>(8ull << 30, free_b / 4u);
+  }
+
   void reset_sequence() {
+    if (cache) cache->cursor.zero(stream);  // every history row is digested again
     ctrl.zero(stream);
     rec.zero(stream);
     conv.zero(stream);
@@ -1474,6 +1524,7 @@ struct Engine {
   // final-normed row of every position (states [n][D]) and, when layers is not
   // NULL, every layer's output row ([depth][n][D]).
   void prefill_capture(const uint32_t* ids, uint32_t n, const uint32_t st[2], float* states, float* layer_rows) {
+    invalidate_cache(true);  // layer capture recomputes the prompt outside the caches
     require(nseq == 1 && !team, "debug prefill serves single-sequence handles", RTA_E_STATE);
     require(n >= 1 && n <= capacity, "prefill length must be 1..capacity", RTA_E_ARG);
     require(states != nullptr, "debug prefill needs the state rows", RTA_E_ARG);
@@ -1564,6 +1615,419 @@ struct Engine {
     generate_batch(count, ids_out, n_out);
   }
 
+  // ------------------------------------------------------------ cache logic
+  // whole: the sequence bookkeeping is void (the state moved outside the
+  // caches); else only boundaries stop being saved / restored.
+  void invalidate_cache(bool whole) {
+    if (!cache) return;
+    cache->prefix_ok = false;
+    if (whole) {
+      cache->ready = false;
+      cache->address_ok = false;
+    }
+  }
+  bool is_stop(uint32_t t) const { return t == stops[0] || t == stops[1]; }
+  // generated tokens the device state has to consume (a trailing stop id has no step)
+  uint32_t consumable() const {
+    const auto& g = cache->gen;
+    return static_cast<uint32_t>(g.size()) - (!g.empty() && is_stop(g.back()) ? 1u : 0u);
+  }
+
+  // The state address of the live sequence into addresses[slot] (device).
+  void digest(uint32_t slot) {
+    Caches& c = *cache;
+    DigestArgs a;
+    a.words[0] = reinterpret_cast<const uint32_t*>(state.p);
+    a.count[0] = state.n;
+    a.words[1] = reinterpret_cast<const uint32_t*>(rec.p);
+    a.count[1] = n_rec ? rec.n : 0u;
+    a.words[2] = reinterpret_cast<const uint32_t*>(conv.p);
+    a.count[2] = n_rec ? conv.n : 0u;
+    a.n_full = n_full;
+    a.kvh = spec.kv_heads;
+    a.hd = spec.attention_head_dim;
+    a.capacity = capacity;
+    if (packet_history) {
+      a.packets = pring.p;
+      a.pbytes = pbytes;
+    } else {
+      a.kcache = kcache.p;
+      a.vcache = vcache.p;
+      a.layer_kv = static_cast<size_t>(spec.kv_heads) * capacity * spec.attention_head_dim * na;
+    }
+    a.slot_hash = c.slot_hash.p;
+    a.cursor = c.cursor.p;
+    a.pos_next = &ctrl.p->pos_next;
+    a.partial = c.partial.p;
+    a.out = c.addresses.p + slot * 8ull;
+    a.seed[0] = c.epoch;
+    a.seed[1] = capacity;
+    a.seed[2] = stops[0];
+    a.seed[3] = stops[1];
+    RTA_CUDA(launch_state_digest(a, stream));
+    ++c.info[RTA_CACHE_DIGESTS];
+  }
+  std::vector<Key256> read_addresses(uint32_t first, uint32_t n) {
+    std::vector<Key256> out(n);
+    if (n)
+      RTA_CUDA(cudaMemcpyAsync(out.data(), cache->addresses.p + first * 8ull, n * sizeof(Key256),
+                               cudaMemcpyDeviceToHost, stream));
+    RTA_CUDA(cudaStreamSynchronize(stream));
+    return out;
+  }
+
+  // History rows of every full layer, positions [b.first, b.first + b.count),
+  // between the ring and the block's own copy ([layer][K, V][kvh][count][hd]
+  // halves, or [layer][count][packet]).
+  size_t block_bytes(uint32_t count) const {
+    const size_t row = packet_history ? pbytes : 4ull * spec.kv_heads * spec.attention_head_dim;
+    return static_cast<size_t>(n_full) * count * row;
+  }
+  void block_segments(const HistoryBlock& b, bool to_ring, std::vector<CopySeg>& out, uint64_t& longest) {
+    const uint32_t hd = spec.attention_head_dim, kvh = spec.kv_heads;
+    uint8_t* mine = static_cast<uint8_t*>(b.rows.p);
+    auto push = [&](void* ring, uint8_t* own, uint64_t bytes) {
+      out.push_back(to_ring ? CopySeg{own, ring, bytes} : CopySeg{ring, own, bytes});
+      longest = std::max(longest, bytes);
+    };
+    for (uint32_t fi = 0; fi < n_full; ++fi) {
+      if (packet_history) {
+        const uint64_t bytes = static_cast<uint64_t>(b.count) * pbytes;
+        push(pring.p + (static_cast<size_t>(fi) * capacity + b.first) * pbytes, mine + fi * bytes, bytes);
+      } else {
+        const size_t layer_kv = static_cast<size_t>(kvh) * capacity * hd;
+        const uint64_t bytes = static_cast<uint64_t>(b.count) * hd * 2u;
+        for (uint32_t kv = 0; kv < 2; ++kv)
+          for (uint32_t h = 0; h < kvh; ++h)
+            push((kv ? vcache.p : kcache.p) + fi * layer_kv + (static_cast<size_t>(h) * capacity + b.first) * hd,
+                 mine + ((static_cast<size_t>(fi) * 2u + kv) * kvh + h) * bytes, bytes);
+      }
+    }
+  }
+  void run_segments(const std::vector<CopySeg>& segs, uint64_t longest) {
+    Caches& c = *cache;
+    for (size_t first = 0; first < segs.size(); first += c.segs.n) {
+      const size_t n = std::min(c.segs.n, segs.size() - first);
+      RTA_CUDA(cudaMemcpyAsync(c.segs.p, segs.data() + first, n * sizeof(CopySeg), cudaMemcpyHostToDevice, stream));
+      RTA_CUDA(launch_copy_segments(c.segs.p, static_cast<uint32_t>(n), longest, stream));
+    }
+  }
+
+  // Boundary e (ids = the live sequence): the state words, and the history of
+  // [0, n) in 16-position blocks, copied out of the ring only for blocks no
+  // other boundary holds already.
+  void save_boundary(HistoryEntry& e, const std::vector<Key256>& keys) {
+    Caches& c = *cache;
+    const size_t sb = state.n * 4u, rb = rec.n * 4u, cb = conv.n * 4u;
+    RTA_CUDA(e.snapshot.alloc(sb + rb + cb, stream));
+    uint8_t* d = static_cast<uint8_t*>(e.snapshot.p);
+    RTA_CUDA(cudaMemcpyAsync(d, state.p, sb, cudaMemcpyDeviceToDevice, stream));
+    RTA_CUDA(cudaMemcpyAsync(d + sb, rec.p, rb, cudaMemcpyDeviceToDevice, stream));
+    RTA_CUDA(cudaMemcpyAsync(d + sb + rb, conv.p, cb, cudaMemcpyDeviceToDevice, stream));
+    std::vector<CopySeg> segs;
+    uint64_t longest = 0;
+    const uint32_t n = static_cast<uint32_t>(e.ids.size());
+    e.blocks.clear();
+    if (n_full)
+      for (uint32_t first = 0; first < n; first += 16u) {
+        const uint32_t cnt = std::min(16u, n - first);
+        bool fresh = false;
+        auto b = c.index.block(keys[first + cnt], first, cnt, &fresh);
+        if (fresh) {
+          RTA_CUDA(b->rows.alloc(block_bytes(cnt), stream));
+          block_segments(*b, false, segs, longest);
+          b->ready = true;
+        }
+        e.blocks.push_back(std::move(b));
+      }
+    run_segments(segs, longest);
+    e.saved = true;
+  }
+  // Make boundary e the live state: its state words, its history blocks into
+  // the ring, and a control block that resumes at its length.
+  void attach(const HistoryEntry& e) {
+    Caches& c = *cache;
+    const size_t sb = state.n * 4u, rb = rec.n * 4u, cb = conv.n * 4u;
+    const uint8_t* d = static_cast<const uint8_t*>(e.snapshot.p);
+    RTA_CUDA(cudaMemcpyAsync(state.p, d, sb, cudaMemcpyDeviceToDevice, stream));
+    RTA_CUDA(cudaMemcpyAsync(rec.p, d + sb, rb, cudaMemcpyDeviceToDevice, stream));
+    RTA_CUDA(cudaMemcpyAsync(conv.p, d + sb + rb, cb, cudaMemcpyDeviceToDevice, stream));
+    std::vector<CopySeg> segs;
+    uint64_t longest = 0;
+    for (const auto& b : e.blocks) block_segments(*b, true, segs, longest);
+    run_segments(segs, longest);
+    const uint32_t n = static_cast<uint32_t>(e.ids.size());
+    std::memset(ctrl_host, 0, sizeof(Control));
+    ctrl_host[0].pos_next = n;
+    ctrl_host[0].pos_cur = n - 1u;
+    ctrl_host[0].stops[0] = stops[0];
+    ctrl_host[0].stops[1] = stops[1];
+    write_headers();
+    c.cursor.zero(stream);
+    c.attached = e.blocks;
+    read_control();
+  }
+  // Feed ids[from, to) to the state at position `from` through the prefill
+  // graphs, without the reset: chunks, or one position per replay (per_token,
+  // the decode step's own kernels without the readout).
+  void extend(const uint32_t* ids, uint32_t from, uint32_t to, bool per_token) {
+    require(from < to && to <= capacity, "cached extension must stay inside the ring", RTA_E_ARG);
+    RTA_CUDA(cudaMemcpyAsync(prompt.p + from, ids + from, (to - from) * 4ull, cudaMemcpyHostToDevice, stream));
+    std::memset(ctrl_host, 0, sizeof(Control));
+    ctrl_host[0].running = 1u;
+    ctrl_host[0].prompt_len = to;
+    ctrl_host[0].pos_next = from;
+    ctrl_host[0].pos_cur = from ? from - 1u : 0u;
+    ctrl_host[0].stops[0] = stops[0];
+    ctrl_host[0].stops[1] = stops[1];
+    write_headers();
+    if (chunked && g_chunk && !per_token)
+      for (uint32_t i = from; i < to; i += kChunk) RTA_CUDA(cudaGraphLaunch(g_chunk, stream));
+    else
+      for (uint32_t i = from; i < to; ++i) RTA_CUDA(cudaGraphLaunch(g_prefill, stream));
+    read_control();
+  }
+
+  // Worker ops 1 / 11 / 12 with the caches (Resident::prefill,
+  // optical_resident.cpp:635-699): restore the longest saved boundary that
+  // prefixes the prompt, compute the rest, save the prompt's end as a boundary
+  // (when anything was computed), and take the state address.
+  void prefill_cached(const uint32_t* ids, uint32_t n, const uint32_t st[2], uint32_t boundary) {
+    require(n >= 1 && n <= capacity, "prefill length must be 1..capacity", RTA_E_ARG);
+    require(boundary >= 1 && boundary <= n, "checkpoint boundary must lie in 1..n", RTA_E_ARG);
+    for (uint32_t i = 0; i < n; ++i) require(ids[i] < spec.vocabulary_size, "token id beyond the vocabulary", RTA_E_ARG);
+    Caches& c = *cache;
+    std::fill(c.info, c.info + RTA_CACHE_INFO_WORDS, 0ull);
+    c.info[RTA_CACHE_TREE_LEAF] = 0xffffffffull;
+    c.ready = c.prefix_ok = c.address_ok = false;
+    stops[0] = st ? st[0] : 0xffffffffu;
+    stops[1] = st ? st[1] : 0xffffffffu;
+    const auto t0 = std::chrono::steady_clock::now();
+    const std::vector<Key256> keys = prefix_identities(ids, n, c.epoch);
+    uint32_t lookups = 0;
+    std::shared_ptr<HistoryEntry> hit = c.index.find(ids, n, keys, 1u, &lookups);
+    c.ms[0] = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    const uint32_t reused = hit ? static_cast<uint32_t>(hit->ids.size()) : 0u;
+    const bool address_hit = hit && reused == n && hit->address_ready && hit->stops[0] == stops[0] &&
+                             hit->stops[1] == stops[1];
+    const uint32_t rows = n - reused;
+    std::shared_ptr<HistoryEntry> entry = rows ? c.index.reserve(ids, n, 1u, keys[n]) : nullptr;
+    Key256 address{};
+    try {
+      RTA_CUDA(cudaEventRecord(ev0, stream));
+      if (hit) {
+        attach(*hit);
+      } else {
+        reset_sequence();
+        c.attached.clear();
+      }
+      if (rows) extend(ids, reused, n, false);
+      if (entry) save_boundary(*entry, keys);
+      if (!address_hit) digest(0);
+      RTA_CUDA(cudaEventRecord(ev1, stream));
+      address = address_hit ? hit->address : read_addresses(0, 1)[0];
+    } catch (...) {
+      c.index.erase(entry);
+      throw;
+    }
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, ev0, ev1);
+    last_gpu_ms = ms;
+    HistoryEntry* at_end = entry ? entry.get() : (reused == n ? hit.get() : nullptr);
+    if (at_end) {
+      at_end->address = address;
+      at_end->address_ready = true;
+      at_end->stops[0] = stops[0];
+      at_end->stops[1] = stops[1];
+    }
+    c.prefix.assign(ids, ids + n);
+    c.gen.clear();
+    c.fwd = 0;
+    c.address = address;
+    c.ready = c.prefix_ok = c.address_ok = true;
+    const uint64_t held = c.index.evict(c.budget, entry.get(), hit.get());
+    c.info[RTA_CACHE_PREFILL_HIT] = hit ? 1u : 0u;
+    c.info[RTA_CACHE_REUSED_TOKENS] = reused;
+    c.info[RTA_CACHE_STABLE_TOKENS] = boundary;
+    c.info[RTA_CACHE_SNAPSHOT_KIND] = !hit ? 0u : reused == n ? 1u : reused == boundary ? 2u : 3u;
+    c.info[RTA_CACHE_SHARED_BLOCKS] = hit ? hit->blocks.size() : 0u;
+    c.info[RTA_CACHE_SAVED_BOUNDARIES] = entry ? 1u : 0u;
+    c.info[RTA_CACHE_BOUNDARIES] = c.index.size();
+    c.info[RTA_CACHE_LOOKUPS] = lookups;
+    c.info[RTA_CACHE_COMPUTED_TOKENS] = rows;
+    c.info[RTA_CACHE_EVICTIONS] = c.index.evictions;
+    c.info[RTA_CACHE_ADDRESS_HIT] = address_hit ? 1u : 0u;
+    c.info[RTA_CACHE_BYTES] = held;
+    c.info[RTA_CACHE_TREE_NODES] = c.tree.size();
+    c.info[RTA_CACHE_TREE_CAPACITY] = ReplyTree::kCapacity;
+  }
+
+  // Bring the device state level with every emitted token: from the longest
+  // saved boundary past it, if any, then one prefill step per token (the
+  // decode step's kernels, so the state is the one decoding would have left).
+  void materialize() {
+    Caches& c = *cache;
+    const uint32_t target = consumable();
+    if (c.fwd >= target) return;
+    const uint32_t n = static_cast<uint32_t>(c.prefix.size());
+    std::vector<uint32_t> seq(c.prefix);
+    seq.insert(seq.end(), c.gen.begin(), c.gen.begin() + target);
+    RTA_CUDA(cudaEventRecord(ev0, stream));
+    bool restored = false;
+    if (c.prefix_ok) {
+      const std::vector<Key256> keys = prefix_identities(seq.data(), seq.size(), c.epoch);
+      uint32_t lookups = 0;
+      std::shared_ptr<HistoryEntry> b = c.index.find(seq.data(), seq.size(), keys, n + c.fwd + 1u, &lookups);
+      if (b) {
+        attach(*b);
+        c.fwd = static_cast<uint32_t>(b->ids.size()) - n;
+        restored = true;
+      }
+    }
+    c.info[RTA_CACHE_RESTORED_TOKENS] = target - c.fwd;
+    c.info[RTA_CACHE_CHECKPOINT_RESTORED] = restored ? 1u : 0u;
+    if (c.fwd < target) extend(seq.data(), n + c.fwd, n + target, true);
+    RTA_CUDA(cudaEventRecord(ev1, stream));
+    RTA_CUDA(cudaEventSynchronize(ev1));
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, ev0, ev1);
+    c.ms[2] = ms;
+    c.fwd = target;
+  }
+
+  // Worker op 2 with the caches (Resident::generatePacket,
+  // optical_resident.cpp:770-853): follow the reply tree from the state
+  // address, then decode the rest with the address of every step's result and
+  // record those steps.  The tree serves positions inside the ring.
+  void generate_cached(uint32_t count, uint32_t* ids_out, uint32_t* n_out) {
+    require(count >= 1 && count <= kMaxOut, "generate count must be 1..4096", RTA_E_ARG);
+    Caches& c = *cache;
+    for (int k = RTA_CACHE_REPLAYED_TOKENS; k <= RTA_CACHE_CHECKPOINT_RESTORED; ++k) c.info[k] = 0u;
+    c.info[RTA_CACHE_TREE_LEAF] = 0xffffffffull;
+    c.info[RTA_CACHE_DIGESTS] = 0u;
+    c.ms[1] = c.ms[2] = 0.0;
+    std::vector<uint32_t> out;
+    out.reserve(count);
+    uint32_t p = static_cast<uint32_t>(c.prefix.size()) + consumable();
+    const bool tree = c.address_ok && static_cast<uint64_t>(p) + count <= capacity;
+    bool stopped = false;
+    uint32_t replayed = 0, queries = 0;
+    const auto t0 = std::chrono::steady_clock::now();
+    if (tree) {
+      Key256 key = c.address;
+      while (replayed < count) {
+        ++queries;
+        uint32_t slot = 0;
+        const ReplyTree::Node* nd = c.tree.find(key, p, &slot);
+        if (!nd) break;
+        out.push_back(nd->token);
+        c.gen.push_back(nd->token);
+        ++replayed;
+        c.info[RTA_CACHE_TREE_LEAF] = slot;
+        if (is_stop(nd->token)) {
+          stopped = true;
+          break;
+        }
+        key = nd->next;
+        ++p;
+      }
+      c.address = key;
+    }
+    c.ms[1] = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    double gpu = 0.0;
+    if (replayed < count && !stopped) {
+      materialize();
+      const uint32_t rest = count - replayed;
+      ctrl_host[0].running = 1u;
+      ctrl_host[0].n_out = 0u;
+      ctrl_host[0].stops[0] = stops[0];
+      ctrl_host[0].stops[1] = stops[1];
+      write_headers();
+      RTA_CUDA(cudaEventRecord(ev0, stream));
+      for (uint32_t i = 0; i < rest; ++i) {
+        RTA_CUDA(cudaGraphLaunch(g_decode, stream));
+        if (tree) digest(i + 1u);
+      }
+      RTA_CUDA(cudaEventRecord(ev1, stream));
+      read_control(rest);
+      float ms = 0.f;
+      cudaEventElapsedTime(&ms, ev0, ev1);
+      gpu = ms;
+      const uint32_t got = std::min(ctrl_host[0].n_out, rest);
+      const uint32_t* tok = ctrl_host[0].ids;
+      if (tree) {
+        const std::vector<Key256> addr = read_addresses(1u, got);
+        Key256 prev = c.address;
+        for (uint32_t i = 0; i < got; ++i) {
+          c.tree.record(prev, p + i, tok[i], addr[i]);
+          prev = addr[i];
+        }
+        c.address = prev;
+      } else {
+        c.address_ok = false;  // past the ring: the tree stays out until the next prefill
+      }
+      for (uint32_t i = 0; i < got; ++i) {
+        out.push_back(tok[i]);
+        c.gen.push_back(tok[i]);
+      }
+      c.fwd = consumable();
+    }
+    last_gpu_ms = gpu + c.ms[2];
+    c.info[RTA_CACHE_REPLAYED_TOKENS] = replayed;
+    c.info[RTA_CACHE_TREE_QUERIES] = queries;
+    c.info[RTA_CACHE_TREE_NODES] = c.tree.size();
+    c.info[RTA_CACHE_TREE_CAPACITY] = ReplyTree::kCapacity;
+    c.info[RTA_CACHE_BOUNDARIES] = c.index.size();
+    c.info[RTA_CACHE_EVICTIONS] = c.index.evictions;
+    if (ids_out) std::copy(out.begin(), out.end(), ids_out);
+    if (n_out) *n_out = static_cast<uint32_t>(out.size());
+  }
+
+  // Worker op 13 (Resident::finishHistory, optical_resident.cpp:743-759).
+  void finish_history(uint64_t* saved, uint64_t* tokens, uint64_t* boundaries) {
+    Caches& c = *cache;
+    c.info[RTA_CACHE_FINISH_SAVED] = c.info[RTA_CACHE_FINISH_TOKENS] = 0u;
+    const uint32_t n = static_cast<uint32_t>(c.prefix.size()), m = consumable();
+    if (c.ready && c.prefix_ok && !c.gen.empty() && c.fwd == m && n + m <= capacity) {
+      std::vector<uint32_t> ids(c.prefix);
+      ids.insert(ids.end(), c.gen.begin(), c.gen.begin() + m);
+      const uint32_t t = static_cast<uint32_t>(ids.size());
+      c.info[RTA_CACHE_FINISH_TOKENS] = t;
+      const std::vector<Key256> keys = prefix_identities(ids.data(), t, c.epoch);
+      std::shared_ptr<HistoryEntry> e = c.index.reserve(ids.data(), t, 2u, keys[t]);
+      if (e) {
+        try {
+          save_boundary(*e, keys);
+          RTA_CUDA(cudaStreamSynchronize(stream));
+        } catch (...) {
+          c.index.erase(e);
+          throw;
+        }
+        if (c.address_ok) {
+          e->address = c.address;
+          e->address_ready = true;
+          e->stops[0] = stops[0];
+          e->stops[1] = stops[1];
+        }
+        c.info[RTA_CACHE_FINISH_SAVED] = 1u;
+        c.info[RTA_CACHE_BYTES] = c.index.evict(c.budget, e.get(), nullptr);
+      }
+    }
+    c.info[RTA_CACHE_BOUNDARIES] = c.index.size();
+    c.info[RTA_CACHE_EVICTIONS] = c.index.evictions;
+    if (saved) *saved = c.info[RTA_CACHE_FINISH_SAVED];
+    if (tokens) *tokens = c.info[RTA_CACHE_FINISH_TOKENS];
+    if (boundaries) *boundaries = c.index.size();
+  }
+
+  // The address of the live state, level with every emitted token.
+  Key256 state_address() {
+    require(cache != nullptr, "the handle was opened without RTA_MODEL_CACHE", RTA_E_STATE);
+    if (cache->ready) materialize();
+    digest(0);
+    return read_addresses(0, 1)[0];
+  }
+
   // Worker op 14 (attentionCheck, resident_attention_runtime.inl:646-753): the
   // full-attention detector of one full layer over a supplied causal history.
   // K/V rows are packed into the reference's history packets (returned), the
@@ -1574,6 +2038,7 @@ struct Engine {
                        uint32_t rows, uint32_t count, uint32_t query_start, uint32_t history_start, uint32_t block,
                        float* out, float* phys, uint8_t* packets_out, uint32_t* receipts, uint32_t* n_records,
                        double* timing) {
+    invalidate_cache(false);
     const uint32_t H = spec.attention_heads, KVH = spec.kv_heads, hd = spec.attention_head_dim;
     require(!team, "diagnostics are served by single-GPU handles", RTA_E_STATE);
     require(layer < spec.depth && layers[layer]->full, "attention diagnostic needs a full-attention layer", RTA_E_ARG);
@@ -1730,6 +2195,7 @@ struct Engine {
   }
 
   void mlp(uint32_t layer, const float* x, uint32_t rows, float* y, float* a) {
+    invalidate_cache(false);  // diagnostics end prefix reuse (optical_resident.cpp:969, ops 4/5/6/14)
     require(!team, "diagnostics are served by single-GPU handles", RTA_E_STATE);
     require(layer < spec.depth, "layer out of range", RTA_E_ARG);
     require(rows >= 1 && rows <= 32, "MLP check supports 1..32 rows", RTA_E_ARG);
@@ -1803,6 +2269,7 @@ struct Engine {
   }
 
   void vocabulary(const float* hidden, float* logits, uint32_t* argmax, float* best) {
+    invalidate_cache(false);
     require(!team, "diagnostics are served by single-GPU handles", RTA_E_STATE);
     const uint32_t D = this->D(), V = spec.vocabulary_size;
     for (uint32_t i = 0; i < D; ++i) require(std::isfinite(hidden[i]), "vocabulary input must be finite", RTA_E_ARG);
@@ -1967,10 +2434,18 @@ rta_status rta_model_open_files_ex(const rta_model_spec* spec, const char* optic
 void rta_model_close(rta_model* m) { delete m; }
 
 rta_status rta_model_prefill(rta_model* m, const uint32_t* ids, uint32_t n, const uint32_t stops[2], double* gpu_ms) {
+  return rta_model_prefill_checkpoint(m, ids, n, stops, n, gpu_ms);
+}
+
+rta_status rta_model_prefill_checkpoint(rta_model* m, const uint32_t* ids, uint32_t n, const uint32_t stops[2],
+                                        uint32_t boundary, double* gpu_ms) {
   if (!m || !ids) return RTA_E_ARG;
   try {
     cudaSetDevice(m->engine.device);
-    m->engine.prefill(ids, n, stops);
+    if (m->engine.cache)
+      m->engine.prefill_cached(ids, n, stops, boundary);
+    else
+      m->engine.prefill(ids, n, stops);
     if (gpu_ms) *gpu_ms = m->engine.last_gpu_ms;
   } catch (const rta::Failure& f) {
     return rta::fail_model(f);
@@ -2007,7 +2482,10 @@ rta_status rta_model_generate(rta_model* m, uint32_t count, uint32_t* ids, uint3
   if (!m) return RTA_E_ARG;
   try {
     cudaSetDevice(m->engine.device);
-    m->engine.generate(count, ids, n_out);
+    if (m->engine.cache && m->engine.cache->ready)
+      m->engine.generate_cached(count, ids, n_out);
+    else
+      m->engine.generate(count, ids, n_out);
     if (gpu_ms) *gpu_ms = m->engine.last_gpu_ms;
   } catch (const rta::Failure& f) {
     return rta::fail_model(f);
@@ -2020,6 +2498,7 @@ rta_status rta_model_prefill_batch(rta_model* m, const uint32_t* ids, const uint
   if (!m || !ids || !lengths) return RTA_E_ARG;
   try {
     cudaSetDevice(m->engine.device);
+    m->engine.invalidate_cache(true);  // the batch calls move the state outside the caches
     m->engine.prefill_batch(ids, lengths, stride, stops);
     if (gpu_ms) *gpu_ms = m->engine.last_gpu_ms;
   } catch (const rta::Failure& f) {
@@ -2032,6 +2511,7 @@ rta_status rta_model_seed_history(rta_model* m, const uint32_t* lengths, uint64_
   if (!m || !lengths) return RTA_E_ARG;
   try {
     cudaSetDevice(m->engine.device);
+    m->engine.invalidate_cache(true);
     m->engine.seed_history(lengths, seed);
   } catch (const rta::Failure& f) {
     return rta::fail_model(f);
@@ -2043,6 +2523,7 @@ rta_status rta_model_generate_batch(rta_model* m, uint32_t count, uint32_t* ids,
   if (!m) return RTA_E_ARG;
   try {
     cudaSetDevice(m->engine.device);
+    m->engine.invalidate_cache(true);
     m->engine.generate_batch(count, ids, n_out);
     if (gpu_ms) *gpu_ms = m->engine.last_gpu_ms;
   } catch (const rta::Failure& f) {
@@ -2105,9 +2586,70 @@ rta_status rta_model_state(rta_model* m, float* state, uint32_t* position) {
   if (!m || !state) return RTA_E_ARG;
   try {
     cudaSetDevice(m->engine.device);
+    if (m->engine.cache && m->engine.cache->ready) m->engine.materialize();
     RTA_CUDA(cudaMemcpyAsync(state, m->engine.state.p, m->engine.D() * 4ull, cudaMemcpyDeviceToHost,
                              m->engine.stream));
     RTA_CUDA(cudaStreamSynchronize(m->engine.stream));
+    if (position) *position = m->engine.position;
+  } catch (const rta::Failure& f) {
+    return rta::fail_model(f);
+  }
+  return RTA_OK;
+}
+
+rta_status rta_model_cache_info(rta_model* m, uint64_t* out, size_t n, double* ms) {
+  if (!m || (!out && n)) return RTA_E_ARG;
+  if (!m->engine.cache) {
+    rta::g_model_error = "the handle was opened without RTA_MODEL_CACHE";
+    return RTA_E_STATE;
+  }
+  const auto& c = *m->engine.cache;
+  for (size_t i = 0; i < n && i < RTA_CACHE_INFO_WORDS; ++i) out[i] = c.info[i];
+  if (ms)
+    for (int i = 0; i < 3; ++i) ms[i] = c.ms[i];
+  return RTA_OK;
+}
+
+rta_status rta_model_finish_history(rta_model* m, uint64_t* saved, uint64_t* tokens, uint64_t* boundaries) {
+  if (!m) return RTA_E_ARG;
+  if (!m->engine.cache) {
+    rta::g_model_error = "the handle was opened without RTA_MODEL_CACHE";
+    return RTA_E_STATE;
+  }
+  try {
+    cudaSetDevice(m->engine.device);
+    m->engine.finish_history(saved, tokens, boundaries);
+  } catch (const rta::Failure& f) {
+    return rta::fail_model(f);
+  }
+  return RTA_OK;
+}
+
+rta_status rta_model_cache_limit(rta_model* m, uint64_t bytes) {
+  if (!m) return RTA_E_ARG;
+  if (!m->engine.cache) {
+    rta::g_model_error = "the handle was opened without RTA_MODEL_CACHE";
+    return RTA_E_STATE;
+  }
+  try {
+    cudaSetDevice(m->engine.device);
+    auto& c = *m->engine.cache;
+    c.budget = bytes;
+    c.info[RTA_CACHE_BYTES] = c.index.evict(bytes, nullptr, nullptr);
+    c.info[RTA_CACHE_BOUNDARIES] = c.index.size();
+    c.info[RTA_CACHE_EVICTIONS] = c.index.evictions;
+  } catch (const rta::Failure& f) {
+    return rta::fail_model(f);
+  }
+  return RTA_OK;
+}
+
+rta_status rta_model_state_address(rta_model* m, uint32_t address[8], uint32_t* position) {
+  if (!m || !address) return RTA_E_ARG;
+  try {
+    cudaSetDevice(m->engine.device);
+    const rta::Key256 k = m->engine.state_address();
+    for (int i = 0; i < 8; ++i) address[i] = k[i];
     if (position) *position = m->engine.position;
   } catch (const rta::Failure& f) {
     return rta::fail_model(f);

@@ -241,21 +241,16 @@ __global__ void __launch_bounds__(256) attn_prep_kernel(PrepParams p) {
 // RMS-normed layer input; 4-tap causal conv + SiLU; L2-normalised q, k; and the
 // gated delta rule s <- s*decay; r = k.s; s += k*(v - r)*beta; o = (q/sqrt(128)).s
 // on a [128 value x 128 key] fp32 state per head.  Grid (head, value slice,
-// sequence), ROWS value rows per CTA.
+// sequence), 16 value rows per CTA: a few sequences split each head's rows over
+// 8 CTAs for parallelism at one token (many sequences go to the persistent
+// gdn_batch_kernel below).
 //
 // Latency layout: the kernel is a short chain of dependent steps, so everything
 // that does not depend on the preceding kernels (this CTA's state rows, the
 // gate / norm / conv weights, the conv history) is requested before
-// griddepcontrol.wait -- state rows into registers; the gate and norm weights
-// into registers (16-row CTAs) or by bulk copies into shared memory together
-// with the hidden row after the wait (128-row CTAs, the batch case: 64 KB of
-// inputs per CTA in three copies instead of 64 dependent L2 loads per thread)
-// -- and the block reductions carry several values per barrier.  A few sequences split
-// each head's rows over 8 CTAs (16 rows: parallelism for one token); many
-// sequences give each (sequence, head) one CTA of all 128 rows, so the gates,
-// norms and convolutions (64 KB of L2 reads over x and the gate rows) are
-// computed once per head instead of once per slice.
-constexpr uint32_t kGdnRowsSmall = 16, kGdnRowsBatch = 128;
+// griddepcontrol.wait, into registers, and the block reductions carry several
+// values per barrier.
+constexpr uint32_t kGdnRowsSmall = 16;
 
 __device__ __forceinline__ float signed_product_sum(float a0, float a1, float a2, float a3, float b0, float b1,
                                                     float b2, float b3) {
@@ -295,16 +290,10 @@ __device__ __forceinline__ void block_sums(float (&v)[N], float* red) {
 
 constexpr uint32_t kGdnDPer = 16;  // hidden values per thread: hidden size <= 4096
 
-template <uint32_t ROWS>
-__global__ void __launch_bounds__(256, ROWS > 16u ? 2 : 1) gdn_kernel(GdnParams p) {
-  constexpr uint32_t kGdnRows = ROWS, kGdnRowsPerWarp = ROWS / 8u;
+__global__ void __launch_bounds__(256) gdn_kernel(GdnParams p) {
+  constexpr uint32_t kGdnRows = kGdnRowsSmall, kGdnRowsPerWarp = kGdnRows / 8u;
   __shared__ float red1[8], red2[16], red3[16];
   __shared__ float qn[128], kn[128], vv[kGdnRows];
-  // Many CTAs (ROWS > 16): the head's gate rows, the norm weight and the hidden
-  // row are staged by bulk copies, [wa D | wb D | norm D | x D] floats
-  extern __shared__ __align__(16) float gdn_stage[];
-  __shared__ __align__(8) uint64_t gdn_bar[2];
-  __shared__ int gdn_ok;
   const uint32_t h = blockIdx.x, slice = blockIdx.y, z = blockIdx.z, tid = threadIdx.x;
   const uint32_t HD = 128u, S = p.H * HD, K = p.KH * HD, kh = h % p.KH;
   const uint32_t warp = tid >> 5, lane = tid & 31u;
@@ -321,33 +310,17 @@ __global__ void __launch_bounds__(256, ROWS > 16u ? 2 : 1) gdn_kernel(GdnParams 
     s0[i] = *reinterpret_cast<const float2*>(row + 2 * lane);   // lane owns keys (2l, 2l+1) and
     s1[i] = *reinterpret_cast<const float2*>(row + 2 * lane + 64);  // (2l+64, 2l+65), as op 21
   }
-  // Few CTAs (one sequence): the gate weights and the norm weight of this
-  // thread's hidden values (c = tid + 256 i) are held in registers, read before
-  // the wait.  Many CTAs: they stay in memory (occupancy), prefetched to L2.
-  constexpr bool kHold = ROWS <= 16u;
-  constexpr uint32_t kPer = kHold ? kGdnDPer : 1u;
+  // The gate weights and the norm weight of this thread's hidden values
+  // (c = tid + 256 i) are held in registers, read before the wait.
+  constexpr uint32_t kPer = kGdnDPer;
   float nw[kPer], wa[kPer], wb[kPer], xr[kPer];
-  if constexpr (kHold) {
 #pragma unroll
-    for (uint32_t i = 0; i < kPer; ++i) {
-      const uint32_t c = tid + 256u * i;
-      const bool in = c < p.D;
-      nw[i] = in ? p.attn_norm[c] : 0.f;
-      wa[i] = in ? p.wa[static_cast<size_t>(h) * p.D + c] : 0.f;
-      wb[i] = in ? p.wb[static_cast<size_t>(h) * p.D + c] : 0.f;
-    }
-  } else {
-    if (tid == 0) {  // constant weights: requested before the wait
-      mbar_init(&gdn_bar[0], 1);
-      mbar_init(&gdn_bar[1], 1);
-      fence_mbar_init();
-      const uint32_t bytes = p.D * 4u;
-      mbar_expect_tx(&gdn_bar[0], 3u * bytes);
-      bulk_g2s(gdn_stage, p.wa + static_cast<size_t>(h) * p.D, bytes, &gdn_bar[0]);
-      bulk_g2s(gdn_stage + p.D, p.wb + static_cast<size_t>(h) * p.D, bytes, &gdn_bar[0]);
-      bulk_g2s(gdn_stage + 2u * p.D, p.attn_norm, bytes, &gdn_bar[0]);
-    }
-    __syncthreads();  // barriers initialised before anyone waits on them
+  for (uint32_t i = 0; i < kPer; ++i) {
+    const uint32_t c = tid + 256u * i;
+    const bool in = c < p.D;
+    nw[i] = in ? p.attn_norm[c] : 0.f;
+    wa[i] = in ? p.wa[static_cast<size_t>(h) * p.D + c] : 0.f;
+    wb[i] = in ? p.wb[static_cast<size_t>(h) * p.D + c] : 0.f;
   }
   // The conv history is double-buffered by position parity; the position is
   // written by this step's embed kernel, so both buffers are read here and the
@@ -378,28 +351,13 @@ __global__ void __launch_bounds__(256, ROWS > 16u ? 2 : 1) gdn_kernel(GdnParams 
   // use, so they share one round trip
   const uint32_t run = p.running ? p.running[z * p.ctrl_step] : 1u;
   const uint32_t posv = p.pos[z * p.ctrl_step];
-  if constexpr (kHold) {
 #pragma unroll
-    for (uint32_t i = 0; i < kPer; ++i) {
-      const uint32_t c = tid + 256u * i;
-      xr[i] = c < p.D ? x_seq[c] : 0.f;
-    }
-  } else if (tid == 0) {
-    mbar_expect_tx(&gdn_bar[1], p.D * 4u);
-    bulk_g2s(gdn_stage + 3u * p.D, x_seq, p.D * 4u, &gdn_bar[1]);
+  for (uint32_t i = 0; i < kPer; ++i) {
+    const uint32_t c = tid + 256u * i;
+    xr[i] = c < p.D ? x_seq[c] : 0.f;
   }
   const float raw_q = proj[tid < 128u ? kh * HD + tid : K + kh * HD + (tid - 128u)];
   const float raw_v = tid < kGdnRows ? proj[2u * K + h * HD + slice * kGdnRows + tid] : 0.f;
-  if constexpr (!kHold) {  // both copies land (bounded) before the CTA may leave
-    if (tid == 0) {
-      uint32_t* err = p.err ? p.err + static_cast<size_t>(z) * p.err_step : nullptr;
-      const bool a_ok = mbar_wait(&gdn_bar[0], 0u, err);
-      const bool b_ok = mbar_wait(&gdn_bar[1], 0u, err);
-      gdn_ok = a_ok && b_ok ? 1 : 0;
-    }
-    __syncthreads();
-    if (!gdn_ok) return;
-  }
   if (run == 0u) return;
   const uint32_t par = posv & 1u;
   float* next = conv_state + (par ^ 1u) * buf;
@@ -408,32 +366,18 @@ __global__ void __launch_bounds__(256, ROWS > 16u ? 2 : 1) gdn_kernel(GdnParams 
 
   // ---- op 18 gates: a, b = (rmsnorm(x) * attn_norm) . W_alpha[h], W_beta[h]
   float ss[1] = {0.f};
-  if constexpr (kHold) {
 #pragma unroll
-    for (uint32_t i = 0; i < kPer; ++i)
-      if (tid + 256u * i < p.D) ss[0] += xr[i] * xr[i];
-  } else {
-    const float* xs = gdn_stage + 3u * p.D;
-    for (uint32_t c = tid; c < p.D; c += 256u) ss[0] += xs[c] * xs[c];
-  }
+  for (uint32_t i = 0; i < kPer; ++i)
+    if (tid + 256u * i < p.D) ss[0] += xr[i] * xr[i];
   block_sums<1>(ss, red1);
   const float inv = rsqrtf(ss[0] / static_cast<float>(p.D) + p.eps);
   float ab[2] = {0.f, 0.f};
-  if constexpr (kHold) {
 #pragma unroll
-    for (uint32_t i = 0; i < kPer; ++i) {
-      if (tid + 256u * i >= p.D) continue;
-      const float xn = xr[i] * inv * nw[i];
-      ab[0] += xn * wa[i];
-      ab[1] += xn * wb[i];
-    }
-  } else {
-    const float *was = gdn_stage, *wbs = gdn_stage + p.D, *nws = gdn_stage + 2u * p.D, *xs = gdn_stage + 3u * p.D;
-    for (uint32_t c = tid; c < p.D; c += 256u) {
-      const float xn = xs[c] * inv * nws[c];
-      ab[0] += xn * was[c];
-      ab[1] += xn * wbs[c];
-    }
+  for (uint32_t i = 0; i < kPer; ++i) {
+    if (tid + 256u * i >= p.D) continue;
+    const float xn = xr[i] * inv * nw[i];
+    ab[0] += xn * wa[i];
+    ab[1] += xn * wb[i];
   }
 
   // ---- op 19: causal conv + SiLU (independent of the gates)
@@ -1022,7 +966,7 @@ cudaError_t launch_gdn(const GdnParams& p, cudaStream_t s, bool pdl) {
     cfg.numAttrs = 1;
     return cudaLaunchKernelExC(&cfg, reinterpret_cast<const void*>(gdn_batch_kernel), args);
   }
-  return launch_pdl(reinterpret_cast<const void*>(gdn_kernel<kGdnRowsSmall>),
+  return launch_pdl(reinterpret_cast<const void*>(gdn_kernel),
                     dim3(p.H, 128u / kGdnRowsSmall, p.nseq), dim3(256), args, s, pdl);
 }
 cudaError_t launch_gdn_chunk(const GdnChunkParams& p, cudaStream_t s, bool pdl) {

@@ -57,11 +57,23 @@ _SIGS = {
     "rta_model_vocabulary": (_I, [_P, _P, _P, ctypes.POINTER(_U32), ctypes.POINTER(ctypes.c_float)]),
     "rta_model_state": (_I, [_P, _P, ctypes.POINTER(_U32)]),
     "rta_model_resources": (_I, [_P, _P, _SZ]),
+    "rta_model_prefill_checkpoint": (_I, [_P, _P, _U32, _P, _U32, ctypes.POINTER(ctypes.c_double)]),
+    "rta_model_cache_info": (_I, [_P, _P, _SZ, _P]),
+    "rta_model_finish_history": (_I, [_P, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64),
+                                      ctypes.POINTER(ctypes.c_uint64)]),
+    "rta_model_cache_limit": (_I, [_P, ctypes.c_uint64]),
+    "rta_model_state_address": (_I, [_P, _P, ctypes.POINTER(_U32)]),
 }
 PACKET_HISTORY = 1  # RTA_MODEL_PACKET_HISTORY
 TOKEN_PREFILL = 2   # RTA_MODEL_TOKEN_PREFILL
 TC_PREFILL = 4      # RTA_MODEL_TC_PREFILL
 SPLIT_ACTIVATIONS = 8  # RTA_MODEL_SPLIT_ACTIVATIONS
+CACHE = 16             # RTA_MODEL_CACHE
+# RTA_CACHE_* counters (include/rta.h), in index order
+CACHE_INFO_NAMES = ("prefill_hit", "reused_tokens", "stable_tokens", "snapshot_kind", "shared_blocks",
+                    "saved_boundaries", "boundaries", "lookups", "computed_tokens", "evictions", "address_hit",
+                    "replayed_tokens", "tree_queries", "tree_nodes", "tree_capacity", "tree_leaf", "restored_tokens",
+                    "checkpoint_restored", "finish_saved", "finish_tokens", "bytes", "digests")
 PROFILE_KINDS = ("start", "readout", "embed", "qkv", "attention_prep", "attention", "o_proj", "in_proj",
                  "gated_delta", "out_proj", "gate_up", "down", "exchange")  # RTA_PROF_* (include/rta.h)
 RESOURCE_NAMES = ("payload_bytes", "derived_layer_bytes", "history_bytes", "recurrent_state_bytes", "capacity",
@@ -116,11 +128,12 @@ class ResidentModel:
     @classmethod
     def from_payloads(cls, spec: assets.Spec, params, matrices, basis, capacity: int, device: int | None = None,
                       sequences: int = 1, history: str = "fp16", token_prefill: bool = False,
-                      tc_prefill: bool = False, split_activations: bool = False):
+                      tc_prefill: bool = False, split_activations: bool = False, cache: bool = False):
         """history: "fp16" K/V rings, or "packet" (the reference's Q4_K/Q6_K history packets).
         token_prefill: prefill one position per step instead of 64-position chunks;
         tc_prefill: the chunks' products on the tensor cores (panel copies of the weights);
-        split_activations: batched decode products take x as two fp16 operands.
+        split_activations: batched decode products take x as two fp16 operands;
+        cache: prefix boundaries and the reply tree (single sequence; RTA_MODEL_CACHE).
         params: uint32 numpy; matrices/basis: uint8 numpy (host) or torch CUDA tensors (device).
         device: CUDA ordinal (default: the caller's current device)."""
         device = _current_device() if device is None else device
@@ -139,7 +152,8 @@ class ResidentModel:
         if history not in ("fp16", "packet"):
             raise ValueError("history must be 'fp16' or 'packet'")
         flags = ((PACKET_HISTORY if history == "packet" else 0) | (TOKEN_PREFILL if token_prefill else 0)
-                 | (TC_PREFILL if tc_prefill else 0) | (SPLIT_ACTIVATIONS if split_activations else 0))
+                 | (TC_PREFILL if tc_prefill else 0) | (SPLIT_ACTIVATIONS if split_activations else 0)
+                 | (CACHE if cache else 0))
         _check(lib.rta_model_open_ex(ctypes.byref(cs), _np_ptr(params), params.size, mp, mb, bp, bb, capacity,
                                      sequences, flags, device, ctypes.byref(h)))
         del mkeep, bkeep
@@ -212,7 +226,7 @@ class ResidentModel:
     @classmethod
     def synthetic(cls, spec: assets.Spec, seed: int = 0, capacity: int = 1024, device: int | None = None,
                   sequences: int = 1, history: str = "fp16", token_prefill: bool = False,
-                  tc_prefill: bool = False, split_activations: bool = False):
+                  tc_prefill: bool = False, split_activations: bool = False, cache: bool = False):
         """Random-init model of `spec` generated on the GPU (payloads in the exporter's layout)."""
         import torch
         device = _current_device() if device is None else device
@@ -220,7 +234,7 @@ class ResidentModel:
         layout = assets.plan(spec, seed)
         mats, basis = assets.generate_device(layout, seed)
         model = cls.from_payloads(spec, layout.params(), mats, basis, capacity, device, sequences, history,
-                                  token_prefill, tc_prefill, split_activations)
+                                  token_prefill, tc_prefill, split_activations, cache)
         model.layout = layout
         del mats, basis
         torch.cuda.empty_cache()
@@ -244,14 +258,44 @@ class ResidentModel:
         except Exception:
             pass
 
-    def prefill(self, ids, stops=()):
+    def prefill(self, ids, stops=(), checkpoint: int | None = None):
+        """checkpoint: the stable prefix of worker op 11 (default: the whole prompt)."""
         ids = np.ascontiguousarray(ids, np.uint32)
         st = (list(stops)[:2] + [0xFFFFFFFF] * 2)[:2]
         st = np.array(st, np.uint32)
         ms = ctypes.c_double(0)
-        _check(_lib_model().rta_model_prefill(self._h, _np_ptr(ids), ids.size, _np_ptr(st), ctypes.byref(ms)))
+        boundary = ids.size if checkpoint is None else int(checkpoint)
+        _check(_lib_model().rta_model_prefill_checkpoint(self._h, _np_ptr(ids), ids.size, _np_ptr(st), boundary,
+                                                         ctypes.byref(ms)))
         self.last_gpu_ms = ms.value
         return ms.value
+
+    # ------------------------------------------------------------ caches
+    def cache_info(self):
+        """Counters of the caches' last prefill / generate / finish_history (RTA_CACHE_*),
+        plus lookup_ms, tree_ms and restore_ms."""
+        out = np.zeros(len(CACHE_INFO_NAMES), np.uint64)
+        ms = np.zeros(3, np.float64)
+        _check(_lib_model().rta_model_cache_info(self._h, _np_ptr(out), out.size, _np_ptr(ms)))
+        info = dict(zip(CACHE_INFO_NAMES, map(int, out)))
+        info.update(lookup_ms=float(ms[0]), tree_ms=float(ms[1]), restore_ms=float(ms[2]))
+        return info
+
+    def finish_history(self):
+        """Save prompt + reply as a prefix boundary (worker op 13): (saved, tokens, boundaries)."""
+        a, b, c = ctypes.c_uint64(0), ctypes.c_uint64(0), ctypes.c_uint64(0)
+        _check(_lib_model().rta_model_finish_history(self._h, ctypes.byref(a), ctypes.byref(b), ctypes.byref(c)))
+        return int(a.value), int(b.value), int(c.value)
+
+    def cache_limit(self, nbytes: int):
+        _check(_lib_model().rta_model_cache_limit(self._h, int(nbytes)))
+
+    def state_address(self):
+        """The 256-bit address of the current decode state (8 uint32) and the position."""
+        out = np.zeros(8, np.uint32)
+        pos = ctypes.c_uint32(0)
+        _check(_lib_model().rta_model_state_address(self._h, _np_ptr(out), ctypes.byref(pos)))
+        return out, int(pos.value)
 
     def prefill_capture(self, ids, stops=(), layers: bool = False):
         """Debug prefill (worker op 1 with debug = 1): returns the final-normed residual

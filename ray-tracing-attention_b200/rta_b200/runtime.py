@@ -35,14 +35,14 @@ class WorkerError(RuntimeError):
 class WorkerClient:
     """One rta_worker process serving one model directory (model.json + payloads)."""
 
-    def __init__(self, directory, capacity: int = 300, attention_block: int = 128, worker=None):
+    def __init__(self, directory, capacity: int = 300, attention_block: int = 128, worker=None, cache: bool = True):
         directory = Path(directory)
         self.spec = assets.Spec.from_dict(json.loads((directory / "model.json").read_text())["model_spec"])
         self.capacity = capacity
         self.attention_block = attention_block
         env = dict(os.environ, RT_ATTENTION_BLOCK=str(attention_block))
         self._p = subprocess.Popen([str(worker or worker_path()), str(directory / "optical_model.bin"),
-                                    str(directory / "vocabulary.bin"), str(capacity)],
+                                    str(directory / "vocabulary.bin"), str(capacity), str(int(cache))],
                                    stdin=subprocess.PIPE, stdout=subprocess.PIPE, stderr=subprocess.PIPE, env=env)
         hello = self._read(20)
         magic, depth, blocks, middle, mode = struct.unpack("<5I", hello)
@@ -88,7 +88,13 @@ class WorkerClient:
         payload = self.request(1, ids.size, 0, ids.tobytes() + st.tobytes())
         timing = np.frombuffer(payload, "<f8", count=6)
         control = np.frombuffer(payload, "<u4", count=8, offset=48)
-        return dict(gpu_ms=float(timing[1]), wall_ms=float(timing[2]), control=control)
+        # history-cache counters after the batch and feature words (resident_runtime.py:134-147)
+        c = np.frombuffer(payload, "<u8", count=10, offset=80 + 32 + 16)
+        return dict(gpu_ms=float(timing[1]), wall_ms=float(timing[2]), control=control,
+                    cache_hit=bool(timing[4]), cached_prefix_tokens=int(timing[5]), stable_prefix_tokens=int(c[0]),
+                    snapshot_kind=int(c[1]), shared_blocks=int(c[2]), saved_boundaries=int(c[3]),
+                    boundaries=int(c[4]), computed_tokens=int(c[6]), address_hit=int(
+                        np.frombuffer(payload, "<u8", count=2, offset=80 + 32 + 16 + 64 + 8)[1]))
 
     def generate(self, count: int):
         """Op 2: one GenerationPacket (optical_resident.cpp:63-71)."""
@@ -96,7 +102,16 @@ class WorkerClient:
         control = np.frombuffer(payload, "<u4", count=8, offset=18 * 8)
         n = int(control[1])
         ids = np.frombuffer(payload, "<u4", count=64, offset=18 * 8 + 32)[:n].copy()
-        return dict(ids=ids, running=bool(control[2]), gpu_ms=float(np.frombuffer(payload, "<f8", count=1)[0]))
+        time = np.frombuffer(payload, "<f8", count=18)
+        cache = np.frombuffer(payload, "<u4", count=4, offset=18 * 8 + 32 + 256 + 20 + 32)
+        return dict(ids=ids, running=bool(control[2]), gpu_ms=float(time[0]), reply_cache_hit=bool(time[5]),
+                    cached_tokens=int(cache[0]), tree_queries=int(cache[1]), cache_nodes=int(cache[2]))
+
+    def finish_history(self):
+        """Op 13: (saved, tokens, boundaries)."""
+        payload = self.request(13, 0)
+        v = np.frombuffer(payload, "<u8", count=3)
+        return int(v[0]), int(v[1]), int(v[2])
 
     def mlp(self, x, layer: int = 0):
         x = np.ascontiguousarray(x, "<f4").reshape(-1, self.spec.hidden_size)

@@ -10,9 +10,11 @@
 //
 // Served operations: 0 quit, 1 prefill (debug 0, 1 = per-position and per-layer
 // rows, 2 = timing layout), 2 generate, 4 vocabulary, 6 mlp, 8 resources,
-// 9 stream, 10 grow (capacity), 11 / 12 checkpointed prefill (validated; no
-// history cache, so computed as op 1), 13 finish_history (nothing to save),
-// 14 full-attention diagnostic (dense receipts).  The attention history is kept
+// 9 stream, 10 grow (capacity), 11 / 12 checkpointed prefill, 13
+// finish_history, 14 full-attention diagnostic (dense receipts).  With the
+// `cache` argument on (argv[4], on by default as in the reference) the handle
+// keeps the prefix boundaries and the reply tree (RTA_MODEL_CACHE) and the
+// replies carry their counters.  The attention history is kept
 // in the reference's packet format.  Operations tied to the ray-traced geometry
 // and its statistics (5 codec, 7 aperture, 15 statistics) answer status 1, which
 // the runtime turns into RuntimeError.
@@ -127,6 +129,7 @@ struct Worker {
   uint32_t capacity = 300, position = 0;
   uint32_t stops[2] = {0xffffffffu, 0xffffffffu};
   uint32_t block = 128;  // RT_ATTENTION_BLOCK: receipt group size (128, 256 or 512)
+  bool cache = true;     // argv[4] (optical_resident.cpp:967: argc <= 4 || stoul(argv[4]) != 0)
 
   void check(rta_status st) {
     if (st != RTA_OK) throw std::runtime_error(rta_model_last_error());
@@ -134,7 +137,7 @@ struct Worker {
   void open() {
     // the reference's history format: Q4_K key / Q6_K value packets
     check(rta_model_open_files_ex(&spec, model_bin.c_str(), geometry_bin.c_str(), vocab_bin.c_str(), capacity, 1u,
-                                  RTA_MODEL_PACKET_HISTORY, 0, &model));
+                                  RTA_MODEL_PACKET_HISTORY | (cache ? RTA_MODEL_CACHE : 0u), 0, &model));
   }
 
   // ops 1 / 11 / 12 (Resident::prefill, optical_resident.cpp:609-712): ids[count] +
@@ -142,28 +145,35 @@ struct Worker {
   // -> 6 doubles + 8 control words [+ debug 1: final-normed rows [count][D] and
   // every layer's output rows [depth][count][D]] + 4 batch statistics [+ debug 2:
   // 6 phase timings] + the history-cache counters (prefill parser,
-  // resident_runtime.py:116-158).  The checkpoints mark where the reference's
-  // shared-history cache saves boundaries; this backend keeps no history cache,
-  // so they are validated and the prefix is computed in full, which is what the
-  // reference reports with its cache disabled (no stable prefix, no hit).
+  // resident_runtime.py:116-158).  The checkpoint (op 11), or the largest
+  // boundary of kind bit 1 (op 12), is the stable prefix the history cache
+  // reports; the prefix itself is saved at the prompt's end
+  // (optical_resident.cpp:616-622, :646-651).  A layer capture bypasses the
+  // caches, as in the reference.
   void prefill(uint32_t op, uint32_t count, uint32_t debug) {
     if (debug > 2u || !count || count > capacity) throw std::runtime_error("Invalid resident prefix");
     std::vector<uint32_t> ids, st;
     input(ids, count);
     input(st, 2);
+    uint32_t boundary = count;
     if (op == 11) {
-      std::vector<uint32_t> boundary;
-      input(boundary, 1);
-      if (!boundary[0] || boundary[0] > count) throw std::runtime_error("Invalid prefix word IDs or boundary");
+      std::vector<uint32_t> b;
+      input(b, 1);
+      if (!b[0] || b[0] > count) throw std::runtime_error("Invalid prefix word IDs or boundary");
+      boundary = b[0];
     } else if (op == 12) {
       std::vector<uint32_t> n;
       input(n, 1);
       if (n[0] > 4096u) throw std::runtime_error("Too many history boundaries");
       std::vector<uint32_t> marks;
       input(marks, 2ull * n[0]);
-      for (uint32_t i = 0; i < n[0]; ++i)
+      uint32_t stable = 0;
+      for (uint32_t i = 0; i < n[0]; ++i) {
         if (!marks[2 * i] || marks[2 * i] > count || !(marks[2 * i + 1] & 15u) || marks[2 * i + 1] > 15u)
           throw std::runtime_error("Invalid history boundary");
+        if (marks[2 * i + 1] & 1u) stable = std::max(stable, marks[2 * i]);
+      }
+      if (stable) boundary = stable;
     }
     for (uint32_t id : ids)
       if (id >= spec.vocabulary_size) throw std::runtime_error("Invalid prefix word IDs or boundary");
@@ -178,12 +188,18 @@ struct Worker {
       layers.resize(static_cast<size_t>(spec.depth) * count * D);
       check(rta_model_prefill_capture(model, ids.data(), count, stops, states.data(), layers.data(), &gpu));
     } else {
-      check(rta_model_prefill(model, ids.data(), count, stops, &gpu));
+      check(rta_model_prefill_checkpoint(model, ids.data(), count, stops, boundary, &gpu));
     }
     const double wall = std::chrono::duration<double, std::milli>(Clock::now() - t0).count();
     position = count;
+    uint64_t c[RTA_CACHE_INFO_WORDS] = {0};
+    double cms[3] = {0.0, 0.0, 0.0};
+    const bool cached = cache && debug != 1u;
+    if (cached) check(rta_model_cache_info(model, c, RTA_CACHE_INFO_WORDS, cms));
+    else c[RTA_CACHE_COMPUTED_TOKENS] = count;
     std::vector<char> out;
-    append<double>(out, {0.0, gpu, wall, wall, 0.0, 0.0});
+    append<double>(out, {0.0, gpu, wall, wall, static_cast<double>(c[RTA_CACHE_PREFILL_HIT]),
+                         static_cast<double>(c[RTA_CACHE_REUSED_TOKENS])});
     append<uint32_t>(out, {ids.back(), 0u, 1u, 0u, stops[0], stops[1], 0u, 0u});
     if (debug == 1u) {
       append(out, states.data(), states.size());
@@ -192,21 +208,24 @@ struct Worker {
     append<uint64_t>(out, {1ull, static_cast<uint64_t>(count), 0ull, static_cast<uint64_t>(count)});
     if (debug == 2u) append<double>(out, {0.0, 0.0, 0.0, 0.0, 0.0, 0.0});  // no ray-traced phases here
     append<uint64_t>(out, {0ull, 0ull});                                    // feature rows traced / reused
-    append<uint64_t>(out, {0ull, 0ull});                                    // stable prefix, snapshot kind
-    append<uint64_t>(out, {0ull, 0ull, 0ull, 0ull, static_cast<uint64_t>(count), 0ull});  // cache counters
-    append<double>(out, {0.0});                                             // cache lookup wall ms
-    append<uint64_t>(out, {0ull, 0ull});                                    // rebuilt tokens, address hit
+    append<uint64_t>(out, {c[RTA_CACHE_STABLE_TOKENS], c[RTA_CACHE_SNAPSHOT_KIND]});
+    append<uint64_t>(out, {c[RTA_CACHE_SHARED_BLOCKS], c[RTA_CACHE_SAVED_BOUNDARIES], c[RTA_CACHE_BOUNDARIES],
+                           c[RTA_CACHE_LOOKUPS], c[RTA_CACHE_COMPUTED_TOKENS], c[RTA_CACHE_EVICTIONS]});
+    append<double>(out, {cms[0]});                            // history lookup wall ms
+    append<uint64_t>(out, {0ull, c[RTA_CACHE_ADDRESS_HIT]});  // rebuilt tokens, address hit
     if (debug == 2u) append<double>(out, {0.0, 0.0});
     reply(0, out);
   }
 
-  // op 13 (finishHistory, optical_resident.cpp:743-759): saves the generated
-  // output as a cache boundary in the reference; without a history cache nothing
-  // is saved -> saved 0, tokens 0, cache size 0, wall ms.
+  // op 13 (finishHistory, optical_resident.cpp:743-759): the prompt plus the
+  // generated reply saved as a boundary -> saved, tokens, boundaries, wall ms
+  // (nothing is saved with the cache off).
   void finish_history() {
     const auto t0 = Clock::now();
+    uint64_t saved = 0, tokens = 0, boundaries = 0;
+    if (cache) check(rta_model_finish_history(model, &saved, &tokens, &boundaries));
     std::vector<char> out;
-    append<uint64_t>(out, {0ull, 0ull, 0ull});
+    append<uint64_t>(out, {saved, tokens, boundaries});
     append<double>(out, {std::chrono::duration<double, std::milli>(Clock::now() - t0).count()});
     reply(0, out);
   }
@@ -215,18 +234,30 @@ struct Worker {
   std::vector<char> packet(const std::vector<uint32_t>& ids, bool running, double gpu, double wall) {
     std::vector<char> out;
     const uint32_t n = static_cast<uint32_t>(std::min<size_t>(ids.size(), 64));
-    append<double>(out, {gpu, wall, 1.0, 1.0, 0.0, 0.0, static_cast<double>(position), 0.0, 0, 0, 0, 0, 0, 0, 0, 0,
-                         0, 0});
+    uint64_t c[RTA_CACHE_INFO_WORDS] = {0};
+    double cms[3] = {0.0, 0.0, 0.0};
+    if (cache) check(rta_model_cache_info(model, c, RTA_CACHE_INFO_WORDS, cms));
+    const uint32_t replayed = static_cast<uint32_t>(c[RTA_CACHE_REPLAYED_TOKENS]);
+    const bool all_cached = replayed > 0 && replayed == ids.size();
+    append<double>(out, {gpu, wall, 1.0, 1.0, 0.0, all_cached ? 1.0 : 0.0, static_cast<double>(position), 0.0, 0, 0,
+                         0, 0, 0, 0, 0, 0, 0, 0});
     append<uint32_t>(out, {n ? ids[n - 1] : 0u, n, running ? 1u : 0u, 0u, stops[0], stops[1], 0u, 0u});
     std::vector<uint32_t> id64(64, 0u);
     std::copy_n(ids.begin(), n, id64.begin());
     append(out, id64.data(), 64);
-    append<uint32_t>(out, {spec.middle_size * spec.depth, spec.middle_size * spec.depth, spec.vocabulary_size, 0u,
-                           0u});
-    append<double>(out, {0.0, 0.0, 0.0, 0.0});
-    append<uint32_t>(out, {0u, 0u, 0u, 0u});
-    append<double>(out, {0.0, 0.0, 0.0, 0.0, 0.0});
-    append<uint32_t>(out, {0u, 0u});
+    // rows through the MLPs: computed tokens but a final stop id (generatePacket's counts, :845-846)
+    const uint32_t fresh = static_cast<uint32_t>(ids.size()) - replayed;
+    const uint32_t computed = fresh - (!running && fresh > 0 ? 1u : 0u);
+    append<uint32_t>(out, {spec.middle_size * spec.depth * computed, spec.middle_size * spec.depth * computed,
+                           spec.vocabulary_size * computed, replayed,
+                           static_cast<uint32_t>(c[RTA_CACHE_TREE_LEAF])});
+    append<double>(out, {0.0, 0.0, 0.0, cms[1]});  // ray-query time by kind: history, vocabulary, mlp, cache
+    append<uint32_t>(out, {replayed, static_cast<uint32_t>(c[RTA_CACHE_TREE_QUERIES]),
+                           static_cast<uint32_t>(c[RTA_CACHE_TREE_NODES]),
+                           static_cast<uint32_t>(c[RTA_CACHE_TREE_CAPACITY])});
+    append<double>(out, {cms[1], cms[1], cms[2], static_cast<double>(c[RTA_CACHE_RESTORED_TOKENS]),
+                         static_cast<double>(c[RTA_CACHE_CHECKPOINT_RESTORED])});
+    append<uint32_t>(out, {replayed, 0u});  // candidates, rejected candidates
     append<uint64_t>(out, {0ull, 0ull});
     return out;
   }
@@ -388,6 +419,7 @@ int main(int argc, char** argv) {
                                                        : w.model_bin.find_last_of('/'));
     w.geometry_bin = (dir.empty() ? std::string(".") : dir) + "/geometry_weights.bin";
     w.capacity = argc > 3 ? static_cast<uint32_t>(std::stoul(argv[3])) : 300u;
+    w.cache = argc <= 4 || std::stoul(argv[4]) != 0;
     w.spec = read_spec(dir.empty() ? "." : dir);
     if (const char* b = std::getenv("RT_ATTENTION_BLOCK")) {
       w.block = static_cast<uint32_t>(std::strtoul(b, nullptr, 10));

@@ -8,8 +8,9 @@ cache, routing, aperture, word tile, feature tile, readout unroll, readout
 words, prefill batch, matrix rows) on a small synthetic model, and driven with
 the exact request bytes that ResidentRuntime's methods write for the session
 listed in SESSION (resident_runtime.py:110-392: prefill with and without
-checkpoints and layer capture, generate, stream, grow, finish_history, mlp,
-vocabulary, attention, resources, quit).  Every request and every reply byte is
+checkpoints and layer capture, a repeated prefill and its replayed reply (the
+worker runs with its caches on, as the runtime starts it), generate, stream,
+grow, finish_history, mlp, vocabulary, attention, resources, quit).  Every request and every reply byte is
 stored, with the model.json the runtime reads.  tests/test_runtime_replay.py
 then runs the unmodified ResidentRuntime against a replay of these bytes: it
 must write the same requests and parse every reply.
@@ -70,10 +71,14 @@ def requests(spec, x, stop_id):
     out = [
         ("prefill", req(1, 12, 0, x["prompt"].tobytes() + stops(())), 1),
         ("generate", req(2, 8, 0), 1),
+        # the same prompt again: a boundary hit, then the reply replayed from the reply tree
+        ("prefill_again", req(1, 12, 0, x["prompt"].tobytes() + stops(())), 1),
+        ("generate_replay", req(2, 8, 0), 1),
         ("stream", req(9, 4, 3), 4),
         ("prefill_checkpoint", req(11, 9, 0, x["prompt_ckpt"].tobytes() + stops((stop_id,)) + struct.pack("<I", 5)),
          1),
         ("generate_to_stop", req(2, 6, 0), 1),
+        ("finish_after_stop", req(13, 0), 1),
         ("prefill_boundaries", req(12, 7, 0, x["prompt_marks"].tobytes() + stops(()) +
                                    struct.pack("<I", 2) + struct.pack("<4I", 3, 1, 6, 2)), 1),
         ("prefill_layers", req(1, 6, 1, x["prompt_debug"].tobytes() + stops(())), 1),

@@ -140,17 +140,30 @@ def test_reference_runtime_parses_every_worker_reply(tmp_path):
 
     r = rt.prefill(x["prompt"])
     assert r["control"][4] == 0xFFFFFFFF and r["prefill_query_positions"] == 12
+    assert r["prefill_cache_hit"] is False and r["history_saved_boundaries"] == 1
+    assert r["prefill_computed_tokens"] == 12 and r["stable_prefix_tokens"] == 12
     gen = rt.generate(8)
     ids8 = np.frombuffer(reply_payload(names.index("generate")), "<u4", count=8, offset=176)
     assert np.array_equal(gen["ids"], ids8) and len(gen["ids"]) == 8 and rt.position == 20
+    assert gen["cached_tokens"] == 0 and gen["compute_tokens"] == 8 and gen["cache_nodes"] == 8
+    # the reference's cache check (benchmark_attention_receipts.py:130-150)
+    hit = rt.prefill(x["prompt"])
+    assert hit["prefill_cache_hit"] is True and hit["cached_prefix_tokens"] == 12
+    assert hit["history_address_hit"] == 1 and hit["prefill_computed_tokens"] == 0 and hit["prefill_snapshot_kind"] == 1
+    replay = rt.generate(8)
+    assert np.array_equal(replay["ids"], gen["ids"]) and replay["reply_cache_hit"] is True
+    assert replay["cached_tokens"] == 8 and replay["compute_tokens"] == 0 and replay["tree_cache_hits"] == 8
     stream = list(rt.stream_generate(4))
     assert [len(s["ids"]) for s in stream] == [1, 1, 1, 1] and rt.position == 24
+    assert stream[0]["cache_state_tokens"] == 8  # the replayed reply is computed before the stream goes on
     r = rt.prefill(x["prompt_ckpt"], stops=(stop_id,), checkpoint_tokens=5)
-    assert r["stable_prefix_tokens"] == 0 and r["prefill_cache_hit"] is False
+    assert r["stable_prefix_tokens"] == 5 and r["prefill_cache_hit"] is False
     gen = rt.generate(6)
     assert len(gen["ids"]) == 3 and int(gen["ids"][-1]) == stop_id and gen["control"][2] == 0
+    fh = rt.finish_history()  # prompt + reply, the stop id left out
+    assert fh["history_output_saved"] == 1 and fh["history_output_tokens"] == 9 + 2
     r = rt.prefill(x["prompt_marks"], checkpoint_boundaries=[(3, 1), (6, 2)])
-    assert r["prefill_computed_tokens"] == 7
+    assert r["prefill_computed_tokens"] == 7 and r["stable_prefix_tokens"] == 3
     r = rt.prefill(x["prompt_debug"], debug=True)
     assert r["state"].shape == (6, spec.hidden_size) and r["layers"].shape == (spec.depth, 6, spec.hidden_size)
     assert np.all(np.isfinite(r["state"])) and np.all(np.isfinite(r["layers"]))

@@ -70,3 +70,35 @@ def test_worker_serves_the_protocol_like_the_library(model_dir):
         res = w.resources()                    # the session survives an error reply
         assert res.size == 61 and res[38] == 128
     lib.close()
+
+
+def test_worker_caches_replay_a_reply(model_dir):
+    """The worker's cache argument (on by default, as ResidentRuntime starts it):
+    a repeated prompt restores its boundary and the reply is replayed from the
+    reply tree with the same ids; with the argument 0 nothing is cached."""
+    from rta_b200 import assets
+    from rta_b200.runtime import WorkerClient
+    spec, _params, _mats, _basis = assets.read_files(model_dir)
+    prompt = np.random.default_rng(32).integers(0, spec.vocabulary_size, 20)
+    with WorkerClient(model_dir, capacity=64) as w:
+        first = w.prefill(prompt)
+        assert not first["cache_hit"] and first["saved_boundaries"] == 1 and first["computed_tokens"] == 20
+        a = w.generate(10)
+        again = w.prefill(prompt)
+        assert again["cache_hit"] and again["cached_prefix_tokens"] == 20 and again["address_hit"] == 1
+        assert again["computed_tokens"] == 0
+        b = w.generate(10)
+        assert np.array_equal(a["ids"], b["ids"]) and b["reply_cache_hit"] and b["cached_tokens"] == 10
+        assert w.finish_history()[0] == 0  # the replayed reply has no computed state yet
+        c = w.generate(2)
+        assert not c["reply_cache_hit"] and c["cached_tokens"] == 0
+        saved, tokens, _ = w.finish_history()
+        assert saved == 1 and tokens == 20 + 12
+    with WorkerClient(model_dir, capacity=64, cache=False) as w:
+        w.prefill(prompt)
+        x = w.generate(10)
+        assert np.array_equal(x["ids"], a["ids"])
+        r = w.prefill(prompt)
+        assert not r["cache_hit"] and r["computed_tokens"] == 20
+        assert not w.generate(10)["reply_cache_hit"]
+        assert w.finish_history() == (0, 0, 0)
