@@ -14,6 +14,8 @@ Workloads (the benchmark configs, synthetic seeded inputs of the stated shapes):
   gemm      the tensor-core batched product alone (--rows --cols --batch --format)
   mlp_tp    the MLP split over the ranks (tensor parallel; --hidden --middle --batch)
   lmhead_tp config 3's readout split over the ranks (tensor parallel; --batch)
+  cache     the decode caches on config 4's model: prefill computed / restored /
+            extended, decode with state digests, the reply replayed (one GPU)
 At N > 1 (torchrun, one process per GPU, NCCL) every rank runs the same
 workload on its own GPU (replicas: the decode of one sequence does not shard),
 except ragged9b (sequences sharded) and the *_tp workloads (one job split over
@@ -1182,6 +1184,62 @@ def run_reference(args, world, rank):
                     "timed its CPU path: the C restatement of its shader math"}
 
 
+def run_cache(args):
+    """The decode caches (RTA_MODEL_CACHE) on config 4's model: a 512-position
+    prompt prefilled and 256 tokens decoded with a state digest after every
+    step (the reply tree records them), the same prompt prefilled again (its
+    boundary restored: state words and 32 history blocks), the 256 tokens replayed
+    from the reply tree, and a prompt that extends the boundary by 64 positions.
+    Every figure comes through the public API (ResidentModel -> C-ABI) with host
+    buffers; the value is the replayed reply's tokens per second of wall time.
+    The uncached handle of the same weights gives the decode rate without digests."""
+    from rta_b200 import assets
+    from rta_b200.model import ResidentModel
+    spec = assets.spec_2b()
+    seed, n, k = 20261201, args.prompt, 256
+    prompt = np.random.default_rng(seed).integers(0, spec.vocabulary_size, n)
+    c = ResidentModel.synthetic(spec, seed, capacity=2048, history=args.kv, cache=True)
+    u = ResidentModel.synthetic(spec, seed, capacity=2048, history=args.kv)
+    wall = lambda f: (lambda t0: (f(), (time.perf_counter() - t0) * 1e3))(time.perf_counter())
+    warm = np.random.default_rng(seed + 2).integers(0, spec.vocabulary_size, 64)  # shares no prefix
+    for _ in range(max(1, args.warmup - 2)):  # graphs, allocator pools, the reply tree's nodes
+        c.prefill(warm)
+        c.generate(8)
+    _, miss_ms = wall(lambda: c.prefill(prompt))
+    miss = c.cache_info()
+    first, _ = wall(lambda: c.generate(k))
+    decode_cached_ms = c.last_gpu_ms
+    u.prefill(prompt)
+    plain = u.generate(k)
+    decode_plain_ms = u.last_gpu_ms
+    _, hit_ms = wall(lambda: c.prefill(prompt))
+    hit = c.cache_info()
+    replay, replay_ms = wall(lambda: c.generate(k))
+    rep_info = c.cache_info()
+    ext = np.concatenate([prompt, np.random.default_rng(seed + 1).integers(0, spec.vocabulary_size, 64)])
+    _, ext_ms = wall(lambda: c.prefill(ext))
+    ext_info = c.cache_info()
+    same = bool(np.array_equal(first, plain) and np.array_equal(replay, first))
+    c.close()
+    u.close()
+    value = len(replay) / (replay_ms / 1e3)
+    return {"metric": "reply-tree replay tokens/s (2B shape, 512 prompt + 256 tokens, cache hit)", "value": value,
+            "unit": "tokens/s", "n_gpus": 1, "steps": 1, "warmup": args.warmup, "higher_is_better": True,
+            "dtype": "u32 (256-bit state keys)", "data": "synthetic (seeded random init, prompt ids)",
+            "config": {"workload": "config4_2b_cache_replay", "prompt": n, "tokens": k, "history": args.kv},
+            "tokens_identical_to_uncached": same, "replayed_tokens": rep_info["replayed_tokens"],
+            "prefill_computed_ms": miss_ms, "prefill_restored_ms": hit_ms,
+            "prefill_restored": {"reused": hit["reused_tokens"], "computed": hit["computed_tokens"],
+                                 "address_hit": hit["address_hit"], "blocks": hit["shared_blocks"]},
+            "prefill_extended_ms": ext_ms,
+            "prefill_extended": {"reused": ext_info["reused_tokens"], "computed": ext_info["computed_tokens"]},
+            "boundary_bytes": miss["bytes"],
+            "decode_tok_s_with_digests": k / (decode_cached_ms / 1e3),
+            "decode_tok_s_uncached": k / (decode_plain_ms / 1e3),
+            "digest_us_per_token": (decode_cached_ms - decode_plain_ms) / k * 1e3,
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 4 * k}}
+
+
 def run_reference_decode(args, world):
     """The 2B decode through the model oracle on all host cores: one model build,
     W warm-up tokens, then min(K, 16) timed tokens (a bounded sample)."""
@@ -1219,7 +1277,7 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="ragged9b")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["cache"], default="ragged9b")
     ap.add_argument("--history", type=int, default=32768)
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--min-seconds", type=float, default=1.0,
@@ -1247,6 +1305,15 @@ def main():
                     help="decode2b: prompt length before the timed tokens (short prompts keep profiler runs small)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.workload == "cache":
+        if args.impl == "reference":
+            line = {"impl": "reference", "unavailable": "the reference's caches live in its Vulkan ray-query worker "
+                                                        "(no graphics stack or RT cores on this box)"}
+        else:
+            line = run_cache(args)
+        if int(os.environ.get("RANK", "0")) == 0:
+            print(json.dumps(line), flush=True)
+        return
     if args.impl == "reference":
         rank = int(os.environ.get("RANK", "0"))
         world = int(os.environ.get("WORLD_SIZE", "1"))

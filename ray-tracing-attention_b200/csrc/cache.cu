@@ -95,33 +95,50 @@ __device__ __forceinline__ void history_range(const DigestArgs& a, uint32_t& lo,
   if (lo > hi || lo < window) lo = window;
 }
 
-// (1) one warp per (position, layer) row: the row digest of its slot
+// 32-bit words of one history row of one layer
+__host__ __device__ __forceinline__ uint32_t row_words(const DigestArgs& a) {
+  return a.packets ? a.pbytes / 4u : a.kvh * a.hd;  // fp16: K then V, kvh x hd halves each
+}
+
+// (1) one warp per (position, layer, 128-word chunk of the row): the chunk's
+// digest into its slot entry.  Four independent loads per lane, so a step's
+// few new rows spread over many warps instead of one dependent chain each.
 __global__ void __launch_bounds__(256) digest_rows_kernel(const DigestArgs a) {
   uint32_t lo, hi;
   history_range(a, lo, hi);
   const uint32_t lane = threadIdx.x & 31u;
-  const uint32_t items = (hi - lo) * a.n_full, warps = gridDim.x * 8u;
+  const uint32_t words = row_words(a), chunks = (words + kRowChunk - 1u) / kRowChunk;
+  const uint32_t per_row = a.n_full * chunks, items = (hi - lo) * per_row, warps = gridDim.x * 8u;
+  const uint32_t hw = a.hd / 2u, per = a.kvh * hw;  // fp16: 32-bit words of one K (or V) row
   for (uint32_t it = blockIdx.x * 8u + (threadIdx.x >> 5); it < items; it += warps) {
-    const uint32_t p = lo + it / a.n_full, layer = it % a.n_full, slot = p % a.capacity;
-    const uint32_t r = row_identity(layer, p);
-    Fold f;
-    f.clear();
-    if (a.packets) {
-      const uint32_t* row =
-          reinterpret_cast<const uint32_t*>(a.packets + (static_cast<size_t>(layer) * a.capacity + slot) * a.pbytes);
-      for (uint32_t j = lane; j < a.pbytes / 4u; j += 32u) f.absorb(row[j], j, r);
-    } else {
-      const uint32_t hw = a.hd / 2u, per = a.kvh * hw;  // 32-bit words of one K (or V) row
-      for (uint32_t j = lane; j < 2u * per; j += 32u) {
+    const uint32_t p = lo + it / per_row, rem = it % per_row, layer = rem / chunks, c = rem % chunks;
+    const uint32_t slot = p % a.capacity, r = row_identity(layer, p);
+    uint32_t v[kRowChunk / 32u];
+    bool in[kRowChunk / 32u];
+#pragma unroll
+    for (uint32_t u = 0; u < kRowChunk / 32u; ++u) {
+      const uint32_t j = c * kRowChunk + u * 32u + lane;
+      in[u] = j < words;
+      v[u] = 0u;
+      if (!in[u]) continue;
+      if (a.packets) {
+        v[u] = reinterpret_cast<const uint32_t*>(a.packets + (static_cast<size_t>(layer) * a.capacity + slot) *
+                                                             a.pbytes)[j];
+      } else {
         const uint32_t kv = j / per, jj = j % per, h = jj / hw, w = jj % hw;
         const __half* base =
             (kv ? a.vcache : a.kcache) + layer * a.layer_kv + (static_cast<size_t>(h) * a.capacity + slot) * a.hd;
-        f.absorb(reinterpret_cast<const uint32_t*>(base)[w], j, r);
+        v[u] = reinterpret_cast<const uint32_t*>(base)[w];
       }
     }
+    Fold f;
+    f.clear();
+#pragma unroll
+    for (uint32_t u = 0; u < kRowChunk / 32u; ++u)
+      if (in[u]) f.absorb(v[u], c * kRowChunk + u * 32u + lane, r);
     f.warp_fold();
     if (lane == 0) {
-      uint32_t* out = a.slot_hash + (static_cast<size_t>(layer) * a.capacity + slot) * 8u;
+      uint32_t* out = a.slot_hash + ((static_cast<size_t>(layer) * a.capacity + slot) * chunks + c) * 8u;
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         out[k] = f.x[k];
@@ -131,7 +148,9 @@ __global__ void __launch_bounds__(256) digest_rows_kernel(const DigestArgs a) {
   }
 }
 
-// (2) the state words and the live slots' row digests -> one partial per CTA
+// (2) the state words and the live slots' chunk digests -> one partial per
+// CTA.  Each thread keeps four 16-byte loads in flight before it hashes them
+// (the fold is memory-latency bound otherwise).
 __global__ void __launch_bounds__(256) digest_fold_kernel(const DigestArgs a) {
   __shared__ uint32_t sh[8][8];
   Fold f;
@@ -143,21 +162,37 @@ __global__ void __launch_bounds__(256) digest_fold_kernel(const DigestArgs a) {
     const uint32_t* w = a.words[s];
     const size_t n = a.count[s];
     const size_t n4 = (reinterpret_cast<uintptr_t>(w) & 15u) == 0 ? n / 4u : 0u;
-    for (size_t i = tid; i < n4; i += nth) {
-      const uint4 v = reinterpret_cast<const uint4*>(w)[i];
+    const uint4* w4 = reinterpret_cast<const uint4*>(w);
+    size_t i = tid;
+    for (; i + 3u * nth < n4; i += 4u * nth) {
+      uint4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = w4[i + u * nth];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint32_t at = base + static_cast<uint32_t>(4u * (i + u * nth));
+        f.absorb(v[u].x, at, kStateSeed);
+        f.absorb(v[u].y, at + 1u, kStateSeed);
+        f.absorb(v[u].z, at + 2u, kStateSeed);
+        f.absorb(v[u].w, at + 3u, kStateSeed);
+      }
+    }
+    for (; i < n4; i += nth) {
+      const uint4 v = w4[i];
       const uint32_t at = base + static_cast<uint32_t>(4u * i);
       f.absorb(v.x, at, kStateSeed);
       f.absorb(v.y, at + 1u, kStateSeed);
       f.absorb(v.z, at + 2u, kStateSeed);
       f.absorb(v.w, at + 3u, kStateSeed);
     }
-    for (size_t i = 4u * n4 + tid; i < n; i += nth) f.absorb(w[i], base + static_cast<uint32_t>(i), kStateSeed);
+    for (size_t j = 4u * n4 + tid; j < n; j += nth) f.absorb(w[j], base + static_cast<uint32_t>(j), kStateSeed);
     base += static_cast<uint32_t>(n);
   }
-  const uint32_t live = min(*a.pos_next, a.capacity), entries = a.n_full * live;
+  const uint32_t chunks = (row_words(a) + kRowChunk - 1u) / kRowChunk;
+  const uint32_t live = min(*a.pos_next, a.capacity), per_layer = live * chunks, entries = a.n_full * per_layer;
   for (size_t e = tid; e < entries; e += nth) {
-    const size_t layer = e / live, slot = e % live;
-    f.merge(a.slot_hash + (layer * a.capacity + slot) * 8u);
+    const size_t layer = e / per_layer, at = e % per_layer;  // (slot, chunk) entries are contiguous per layer
+    f.merge(a.slot_hash + (layer * a.capacity * chunks + at) * 8u);
   }
   f.block_fold(sh);
   if (threadIdx.x == 0)
@@ -177,14 +212,21 @@ __global__ void __launch_bounds__(256) digest_final_kernel(const DigestArgs a) {
   for (uint32_t b = threadIdx.x; b < kDigestBlocks; b += blockDim.x) f.merge(a.partial + b * 8u);
   f.block_fold(sh);
   if (threadIdx.x == 0) {
+    uint32_t* out = a.out;
+    if (a.slot) {
+      const uint32_t at = *a.slot;
+      *a.slot = at + 1u;
+      if (at >= a.slots) return;  // past the caller's buffer: nothing written, the cursor kept
+      out += at * 8u;
+    }
     const uint32_t pos = *a.pos_next;
     const uint32_t s = fmix32(pos ^ 0xA54FF53Au) ^ fmix32(a.seed[0] + 0x510E527Fu) ^
                        fmix32(a.seed[1] * 3u + 0x9B05688Cu) ^ fmix32(a.seed[2] ^ 0x1F83D9ABu) ^
                        fmix32(a.seed[3] + 0x5BE0CD19u);
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      a.out[k] = fmix32(f.x[k] ^ fmix32(s + static_cast<uint32_t>(k) * 0x9E3779B9u));
-      a.out[4 + k] = fmix32(f.a[k] ^ fmix32(s ^ static_cast<uint32_t>(k + 1) * 0x85EBCA77u));
+      out[k] = fmix32(f.x[k] ^ fmix32(s + static_cast<uint32_t>(k) * 0x9E3779B9u));
+      out[4 + k] = fmix32(f.a[k] ^ fmix32(s ^ static_cast<uint32_t>(k + 1) * 0x85EBCA77u));
     }
     *a.cursor = pos;
   }

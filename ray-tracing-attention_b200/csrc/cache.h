@@ -48,12 +48,14 @@ cudaError_t launch_copy_segments(const CopySeg* segs_device, uint32_t n, uint64_
 
 // The state address.  Three launches: (1) the history rows written since the
 // last digest (positions [*cursor, *pos_next), the live window at most) are
-// hashed into per-slot row digests; (2) every state word and the row digests
-// of the live slots are folded into per-CTA partial digests; (3) one CTA
+// hashed into per-slot digests of their 128-word chunks; (2) every state word
+// and the chunk digests of the live slots are folded into per-CTA partial
+// digests; (3) one CTA
 // combines them with the position and the seeds into out[8] and advances
 // *cursor.  Lanes 0-3 fold by XOR and lanes 4-7 by addition: both are
 // order-free, so the CTA split and the slot order do not matter.
-constexpr uint32_t kDigestBlocks = 296;
+constexpr uint32_t kDigestBlocks = 592;  // 4 CTAs of 256 threads per SM
+constexpr uint32_t kRowChunk = 128;      // history row words per chunk digest
 struct DigestArgs {
   const uint32_t* words[3] = {nullptr, nullptr, nullptr};  // state row, recurrent states, convolution states
   size_t count[3] = {0, 0, 0};                             // 32-bit words of each
@@ -62,11 +64,15 @@ struct DigestArgs {
   const uint8_t* packets = nullptr;  // packet rings [layer][capacity][pbytes]
   size_t layer_kv = 0;               // halves between two layers' K planes
   uint32_t n_full = 0, kvh = 0, hd = 0, capacity = 0, pbytes = 0;
-  uint32_t* slot_hash = nullptr;       // [n_full][capacity][8]
+  uint32_t* slot_hash = nullptr;       // [n_full][capacity][row chunks][8]
   uint32_t* cursor = nullptr;          // history positions digested so far (device word)
   const uint32_t* pos_next = nullptr;  // the control block's next position
   uint32_t* partial = nullptr;         // [kDigestBlocks][8]
-  uint32_t* out = nullptr;             // [8]
+  uint32_t* out = nullptr;             // [8], or [slots][8] with a slot counter
+  // Optional device counter: the address goes to out[*slot] and the counter
+  // advances (a graph that digests after every replay); `slots` bounds it.
+  uint32_t* slot = nullptr;
+  uint32_t slots = 0;
   uint32_t seed[4] = {0, 0, 0, 0};     // epoch, capacity, stop ids
 };
 cudaError_t launch_state_digest(const DigestArgs& a, cudaStream_t s);

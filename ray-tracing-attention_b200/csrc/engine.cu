@@ -227,10 +227,13 @@ struct Engine {
   struct Caches {
     HistoryIndex index;
     ReplyTree tree;
-    DevBuf<uint32_t> slot_hash;  // [n_full][capacity][8] row digests
+    DevBuf<uint32_t> slot_hash;  // [n_full][capacity][row chunks][8] history chunk digests
     DevBuf<uint32_t> cursor;     // [1] history positions digested so far
     DevBuf<uint32_t> partial;    // [kDigestBlocks][8]
     DevBuf<uint32_t> addresses;  // [kMaxOut + 1][8]: slot 0 the state now, slot i + 1 after step i
+    DevBuf<uint32_t> slot;       // [1] the digesting decode graph's next address slot
+    cudaGraphExec_t g_step = nullptr;  // one decode step and the digest of its result
+    uint32_t g_step_stops[2] = {0, 0};  // the stop ids g_step's digest was captured with
     DevBuf<CopySeg> segs;        // the copy list of one save / restore
     uint64_t budget = 0;
     uint32_t epoch = 0;
@@ -250,6 +253,7 @@ struct Engine {
   std::unique_ptr<Caches> cache;
 
   ~Engine() {
+    if (cache && cache->g_step) cudaGraphExecDestroy(cache->g_step);
     cache.reset();  // stream-ordered frees need the stream
     if (g_decode) cudaGraphExecDestroy(g_decode);
     if (g_prefill) cudaGraphExecDestroy(g_prefill);
@@ -719,10 +723,13 @@ struct Engine {
   void open_caches() {
     cache = std::make_unique<Caches>();
     Caches& c = *cache;
-    c.slot_hash.alloc(static_cast<size_t>(std::max(1u, n_full)) * capacity * 8u);
+    const uint32_t row_words = packet_history ? pbytes / 4u : spec.kv_heads * spec.attention_head_dim;
+    const uint32_t chunks = (row_words + kRowChunk - 1u) / kRowChunk;
+    c.slot_hash.alloc(static_cast<size_t>(std::max(1u, n_full)) * capacity * chunks * 8u);
     c.cursor.alloc(1);
     c.partial.alloc(static_cast<size_t>(kDigestBlocks) * 8u);
     c.addresses.alloc((kMaxOut + 1ull) * 8u);
+    c.slot.alloc(1);
     const size_t per_block = std::max(1u, n_full) * (packet_history ? 1ull : 2ull * spec.kv_heads);
     c.segs.alloc((capacity / 16ull + 2ull) * per_block);
     size_t free_b = 0, total_b = 0;
@@ -1634,7 +1641,9 @@ struct Engine {
   }
 
   // The state address of the live sequence into addresses[slot] (device).
-  void digest(uint32_t slot) {
+  void digest(uint32_t slot) { digest_at(cache->addresses.p + slot * 8ull, nullptr, 1u); }
+  // ... into out, or into out[*counter] (counter advanced, `slots` at most).
+  void digest_at(uint32_t* out, uint32_t* counter, uint32_t slots) {
     Caches& c = *cache;
     DigestArgs a;
     a.words[0] = reinterpret_cast<const uint32_t*>(state.p);
@@ -1659,13 +1668,37 @@ struct Engine {
     a.cursor = c.cursor.p;
     a.pos_next = &ctrl.p->pos_next;
     a.partial = c.partial.p;
-    a.out = c.addresses.p + slot * 8ull;
+    a.out = out;
+    a.slot = counter;
+    a.slots = slots;
     a.seed[0] = c.epoch;
     a.seed[1] = capacity;
     a.seed[2] = stops[0];
     a.seed[3] = stops[1];
     RTA_CUDA(launch_state_digest(a, stream));
     ++c.info[RTA_CACHE_DIGESTS];
+  }
+  // The decode step followed by the digest of its result into addresses[1 +
+  // *slot]: one graph per token while the reply tree records.
+  cudaGraphExec_t instantiate_digest_step() {
+    Caches& c = *cache;
+    cudaGraph_t graph = nullptr;
+    RTA_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeRelaxed));
+    try {
+      record_step(true, false);
+      digest_at(c.addresses.p + 8u, c.slot.p, kMaxOut);
+    } catch (...) {
+      cudaStreamEndCapture(stream, &graph);
+      if (graph) cudaGraphDestroy(graph);
+      throw;
+    }
+    RTA_CUDA(cudaStreamEndCapture(stream, &graph));
+    cudaGraphExec_t exec = nullptr;
+    const cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    RTA_CUDA(e);
+    --c.info[RTA_CACHE_DIGESTS];  // the capture launched nothing
+    return exec;
   }
   std::vector<Key256> read_addresses(uint32_t first, uint32_t n) {
     std::vector<Key256> out(n);
@@ -1943,12 +1976,22 @@ struct Engine {
       ctrl_host[0].stops[0] = stops[0];
       ctrl_host[0].stops[1] = stops[1];
       write_headers();
-      RTA_CUDA(cudaEventRecord(ev0, stream));
-      for (uint32_t i = 0; i < rest; ++i) {
-        RTA_CUDA(cudaGraphLaunch(g_decode, stream));
-        if (tree) digest(i + 1u);
+      if (tree) {
+        if (c.g_step && (c.g_step_stops[0] != stops[0] || c.g_step_stops[1] != stops[1])) {
+          cudaGraphExecDestroy(c.g_step);  // the stop ids are part of the address
+          c.g_step = nullptr;
+        }
+        if (!c.g_step) {
+          c.g_step = instantiate_digest_step();
+          c.g_step_stops[0] = stops[0];
+          c.g_step_stops[1] = stops[1];
+        }
+        RTA_CUDA(cudaMemsetAsync(c.slot.p, 0, 4, stream));
       }
+      RTA_CUDA(cudaEventRecord(ev0, stream));
+      for (uint32_t i = 0; i < rest; ++i) RTA_CUDA(cudaGraphLaunch(tree ? c.g_step : g_decode, stream));
       RTA_CUDA(cudaEventRecord(ev1, stream));
+      if (tree) c.info[RTA_CACHE_DIGESTS] += rest;
       read_control(rest);
       float ms = 0.f;
       cudaEventElapsedTime(&ms, ev0, ev1);
