@@ -32,12 +32,13 @@ namespace {
 
 constexpr int kWarps = 4;
 constexpr int kThreads = 128;
-constexpr int kTile = 16;      // positions per stage
-constexpr int kStages = 8;     // two per warp (one long history: all splits resident at once)
-constexpr int kStagesMany = 4;  // one per warp, three CTAs per SM (several waves of splits)
+constexpr int kTileMany = 16;   // positions per stage, several waves of splits
+constexpr int kTileOne = 16;    // positions per stage, one wave (32 measured slower: 37.1 vs 34.6 us at L 32768)
+constexpr int kStages = 12;     // one wave of splits (a long history): a ring shared by kWarpsOne warps
+constexpr int kWarpsOne = 8;
+constexpr int kStagesMany = 4;  // several waves of splits: one per warp of kWarps, three CTAs per SM
 constexpr int kHD = 256;       // head dimension handled by this kernel
 constexpr int kRowBytes = kHD * 2 + 16;
-constexpr int kStageBytes = 2 * kTile * kRowBytes;  // K rows then V rows
 constexpr int kGroup = 4;      // query heads per KV head (GQA 16/4)
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
@@ -78,22 +79,33 @@ __device__ __forceinline__ uint32_t used_splits(const AttnParams& p, uint32_t n,
   return want < 1u ? 1u : want > nsplit ? nsplit : want;
 }
 
-// STAGES (a multiple of kWarps: warp w owns stages w, w + 4, ...): 8 when the
-// splits fit in one wave of CTAs, 4 when they take several waves, so that three
-// CTAs share an SM and overlap each other's stage waits.
-template <int STAGES>
-__global__ void __launch_bounds__(kThreads) attention_split_kernel(const AttnParams p) {
-  static_assert(STAGES % kWarps == 0, "stages are owned by warps");
-  constexpr int kStages = STAGES;
+// WARPS x 32 threads and a ring of STAGES stages of TILE positions (16 or
+// 32: one or two 16-row MMA blocks).  Warp w takes tiles w, w + WARPS, ...;
+// tile t lands in stage t % STAGES, and the warp that consumes tile t issues
+// tile t + STAGES into the stage it frees, so the ring stays full whichever
+// warp is ahead.  One wave of CTAs (a long history): eight warps over twelve
+// 16-position stages (198 KB in flight per SM, two warps per scheduler);
+// several waves (many sequences): four warps over four 16-position stages and
+// three CTAs per SM.  Softmax in base 2: the scores carry log2(e) / sqrt(d), the
+// split records' maxima go out in natural units.
+template <int WARPS, int STAGES, int TILE>
+__global__ void __launch_bounds__(WARPS * 32) attention_split_kernel(const AttnParams p) {
+  static_assert(STAGES <= 16 && (TILE == 16 || TILE == 32), "16 barriers at most; one or two row blocks");
+  constexpr int kStages = STAGES, kWarps = WARPS, kThreads = WARPS * 32, kTile = TILE, kNB = TILE / 16;
+  constexpr int kStageBytes = 2 * kTile * kRowBytes;  // K rows then V rows
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
-  __half* pbuf = reinterpret_cast<__half*>(smem + kStages * kStageBytes + 128);  // [warp][8 cols][16 pos]
+  uint32_t* issued = reinterpret_cast<uint32_t*>(smem + kStages * kStageBytes + 128);  // copies per stage
+  __half* pbuf = reinterpret_cast<__half*>(smem + kStages * kStageBytes + 256);  // [warp][8 cols][TILE pos]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t g = static_cast<uint32_t>(lane) >> 2, t4 = static_cast<uint32_t>(lane) & 3u;
   const uint32_t split = blockIdx.x, kv = blockIdx.y, z = blockIdx.z;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) mbar_init(&bars[s], 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&bars[s], 1);
+      issued[s] = 0u;
+    }
     fence_mbar_init();
   }
   __syncthreads();
@@ -119,18 +131,28 @@ __global__ void __launch_bounds__(kThreads) attention_split_kernel(const AttnPar
   auto issue = [&](uint32_t tile) {  // called by one full warp
     const uint32_t s = tile % kStages;
     uint8_t* st = smem + s * kStageBytes;
-    if (lane == 0) mbar_expect_tx(&bars[s], 2u * kTile * kHD * 2u);
+    if (lane == 0) {
+      mbar_expect_tx(&bars[s], 2u * kTile * kHD * 2u);
+      __threadfence_block();
+      atomicAdd(&issued[s], 1u);  // the consumer's go-ahead (see the main loop)
+    }
     __syncwarp();
-    const uint32_t row = static_cast<uint32_t>(lane) & 15u;
-    uint32_t pos = first + tile * kTile + row;
-    if (pos >= last) pos = last - 1u;  // finite filler for masked rows
-    const size_t at = static_cast<size_t>(pos % p.capacity) * p.pos_stride;
-    const __half* src = lane < 16 ? kbase + at : vbase + at;
-    uint8_t* dst = st + (lane < 16 ? 0 : kTile * kRowBytes) + row * kRowBytes;
-    bulk_g2s(dst, src, kHD * 2u, &bars[s]);
+    // one row copy per lane and kind: 16-position tiles split the lanes
+    // between K and V rows, 32-position tiles give each lane its K and V row
+#pragma unroll
+    for (int c = 0; c < kNB; ++c) {
+      const uint32_t row = kTile == 32 ? static_cast<uint32_t>(lane) : static_cast<uint32_t>(lane) & 15u;
+      const bool is_v = kTile == 32 ? c == 1 : lane >= 16;
+      uint32_t pos = first + tile * kTile + row;
+      if (pos >= last) pos = last - 1u;  // finite filler for masked rows
+      const size_t at = static_cast<size_t>(pos % p.capacity) * p.pos_stride;
+      const __half* src = is_v ? vbase + at : kbase + at;
+      uint8_t* dst = st + (is_v ? kTile * kRowBytes : 0) + row * kRowBytes;
+      bulk_g2s(dst, src, kHD * 2u, &bars[s]);
+    }
   };
-  // warp w owns tiles w, w+4, w+8, ... and stages (tile % 8)
-  for (uint32_t tile = warp; tile < ntiles && tile < static_cast<uint32_t>(warp + kStages); tile += kWarps) issue(tile);
+  // the ring's first tiles: tile t < STAGES by warp t % WARPS
+  for (uint32_t tile = warp; tile < ntiles && tile < static_cast<uint32_t>(kStages); tile += kWarps) issue(tile);
 
   // Query fragments (B operand, "col" layout): column g<4 -> hi(q[head g]),
   // g>=4 -> lo residual of head g-4; k = dim.
@@ -152,111 +174,150 @@ __global__ void __launch_bounds__(kThreads) attention_split_kernel(const AttnPar
     }
   }
 
-  const float inv_scale = 1.0f / sqrtf(static_cast<float>(kHD));
+  constexpr float kLog2e = 1.4426950408889634f;
+  const float inv_scale = kLog2e / sqrtf(static_cast<float>(kHD));  // scores in log2 units
   float o[16][4];
 #pragma unroll
   for (int mt = 0; mt < 16; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
   float m_run[2] = {-INFINITY, -INFINITY}, z_run[2] = {0.f, 0.f};
   bool failed = false;
-  uint32_t failed_tile = 0;
   __half* pw = pbuf + warp * 8 * kTile;
 
   for (uint32_t tile = warp; tile < ntiles; tile += kWarps) {
     const uint32_t s = tile % kStages;
+    if (kStages != kWarps) {
+      // Shared ring (a stage serves several warps): the stage's barrier may
+      // still be a phase short of this tile (the tile before it in the stage
+      // not consumed yet), and a parity wait cannot tell phase k from k + 2.
+      // Wait (boundedly) until this tile's copy has been issued, then for its
+      // phase.  With one stage per warp the warp itself orders the phases.
+      const uint32_t need = tile / kStages + 1u;
+      const uint64_t start = globaltimer();
+      for (uint32_t spin = 0; *reinterpret_cast<volatile uint32_t*>(&issued[s]) < need; ++spin) {
+        if ((spin & 63u) == 63u && globaltimer() - start > RTA_WAIT_NS) {
+          if (p.err) atomicOr(p.err, RTA_DEVERR_TIMEOUT);
+          failed = true;
+          break;
+        }
+        __nanosleep(32);
+      }
+      if (failed) break;
+    }
     if (!mbar_wait(&bars[s], (tile / kStages) & 1u, p.err)) {
       failed = true;
-      failed_tile = tile;
       break;
     }
     const uint32_t st = smem_u32(smem + s * kStageBytes);
-    // S^T[pos][col] = K[pos] . Q[col]
-    // four independent accumulators break the 16-deep MMA dependency chain
-    float sp[4][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    // S^T[pos][col] = K[pos] . Q[col], one 16-row block per b; four
+    // independent accumulators per block break the 16-deep MMA chain
+    float sc[kNB][4];
 #pragma unroll
-    for (int kk = 0; kk < 16; ++kk) {
-      uint32_t a0, a1, a2, a3;
-      const uint32_t addr = st + (lane & 15) * kRowBytes + (kk * 16 + (lane >> 4) * 8) * 2;
-      ldsm_x4(addr, a0, a1, a2, a3);
-      mma_f16(sp[kk & 3], a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
+    for (int b = 0; b < kNB; ++b) {
+      float sp[4][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+      for (int kk = 0; kk < 16; ++kk) {
+        uint32_t a0, a1, a2, a3;
+        const uint32_t addr = st + (b * 16 + (lane & 15)) * kRowBytes + (kk * 16 + (lane >> 4) * 8) * 2;
+        ldsm_x4(addr, a0, a1, a2, a3);
+        mma_f16(sp[kk & 3], a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
+      }
+      // hi + lo columns -> full score; lanes t4 and t4^2 end up with the same values.
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float sacc = (sp[0][i] + sp[1][i]) + (sp[2][i] + sp[3][i]);
+        sc[b][i] = (sacc + __shfl_xor_sync(0xffffffffu, sacc, 2)) * inv_scale;
+      }
+      const uint32_t pos0 = tile * kTile + b * 16 + g, pos1 = pos0 + 8u;
+      if (pos0 >= count) sc[b][0] = sc[b][1] = -INFINITY;
+      if (pos1 >= count) sc[b][2] = sc[b][3] = -INFINITY;
     }
-    float sacc[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) sacc[i] = (sp[0][i] + sp[1][i]) + (sp[2][i] + sp[3][i]);
-    // hi + lo columns -> full score; lanes t4 and t4^2 end up with the same values.
-    float sc[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) sc[i] = (sacc[i] + __shfl_xor_sync(0xffffffffu, sacc[i], 2)) * inv_scale;
-    const uint32_t pos0 = tile * kTile + g, pos1 = pos0 + 8u;
-    if (pos0 >= count) sc[0] = sc[1] = -INFINITY;
-    if (pos1 >= count) sc[2] = sc[3] = -INFINITY;
-    float pr[4];
+    float pr[kNB][4], rescale[2];
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {  // the two heads of this lane: 2*(t4&1)+hh
-      float mx = fmaxf(sc[hh], sc[2 + hh]);
+      float mx = -INFINITY;
+#pragma unroll
+      for (int b = 0; b < kNB; ++b) mx = fmaxf(mx, fmaxf(sc[b][hh], sc[b][2 + hh]));
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
       const float m_new = fmaxf(m_run[hh], mx);
-      const float scale = m_new == -INFINITY ? 1.f : expf(m_run[hh] - m_new);
-      const float p0 = m_new == -INFINITY ? 0.f : expf(sc[hh] - m_new);
-      const float p1 = m_new == -INFINITY ? 0.f : expf(sc[2 + hh] - m_new);
-      float ps = p0 + p1;
+      const float scale = m_new == -INFINITY ? 1.f : exp2f(m_run[hh] - m_new);
+      float ps = 0.f;
+#pragma unroll
+      for (int b = 0; b < kNB; ++b) {
+        const float p0 = m_new == -INFINITY ? 0.f : exp2f(sc[b][hh] - m_new);
+        const float p1 = m_new == -INFINITY ? 0.f : exp2f(sc[b][2 + hh] - m_new);
+        ps += p0 + p1;
+        pr[b][hh] = p0;
+        pr[b][2 + hh] = p1;
+      }
       ps += __shfl_xor_sync(0xffffffffu, ps, 4);
       ps += __shfl_xor_sync(0xffffffffu, ps, 8);
       ps += __shfl_xor_sync(0xffffffffu, ps, 16);
       z_run[hh] = z_run[hh] * scale + ps;
       m_run[hh] = m_new;
+      rescale[hh] = scale;
+    }
+    // the value accumulators follow a new maximum; a scale of exactly 1 (the
+    // maximum did not move, the common case) changes nothing and is skipped
+    if (__any_sync(0xffffffffu, (rescale[0] != 1.f) | (rescale[1] != 1.f))) {
 #pragma unroll
       for (int mt = 0; mt < 16; ++mt) {
-        o[mt][hh] *= scale;
-        o[mt][2 + hh] *= scale;
+        o[mt][0] *= rescale[0];
+        o[mt][2] *= rescale[0];
+        o[mt][1] *= rescale[1];
+        o[mt][3] *= rescale[1];
       }
-      pr[hh] = p0;
-      pr[2 + hh] = p1;
     }
     // P (split hi/lo) -> shared [col][pos] for the B operand of P*V.
     {
       const uint32_t hA = 2u * (t4 & 1u);
       const bool hi = t4 < 2u;
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const uint32_t col = (hi ? 0u : 4u) + hA + hh;
+      for (int b = 0; b < kNB; ++b)
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
-          const float pv = pr[2 * r + hh];
-          const __half ph = __float2half_rn(pv);
-          pw[col * kTile + g + 8u * r] = hi ? ph : __float2half_rn(pv - __half2float(ph));
+        for (int hh = 0; hh < 2; ++hh) {
+          const uint32_t col = (hi ? 0u : 4u) + hA + hh;
+#pragma unroll
+          for (int r = 0; r < 2; ++r) {
+            const float pv = pr[b][2 * r + hh];
+            const __half ph = __float2half_rn(pv);
+            pw[col * kTile + b * 16 + g + 8u * r] = hi ? ph : __float2half_rn(pv - __half2float(ph));
+          }
         }
-      }
     }
     __syncwarp();
-    const uint32_t pb0 = *reinterpret_cast<const uint32_t*>(pw + g * kTile + 2u * t4);
-    const uint32_t pb1 = *reinterpret_cast<const uint32_t*>(pw + g * kTile + 2u * t4 + 8u);
     const uint32_t vst = st + kTile * kRowBytes;
 #pragma unroll
-    for (int mt = 0; mt < 16; ++mt) {
-      uint32_t a0, a1, a2, a3;
-      const uint32_t mi = static_cast<uint32_t>(lane) >> 3, rr = static_cast<uint32_t>(lane) & 7u;
-      const uint32_t prow = rr + ((mi >> 1) << 3), dcol = mt * 16 + (mi & 1u) * 8;
-      ldsm_x4_t(vst + prow * kRowBytes + dcol * 2, a0, a1, a2, a3);
-      mma_f16(o[mt], a0, a1, a2, a3, pb0, pb1);
+    for (int b = 0; b < kNB; ++b) {
+      const uint32_t pb0 = *reinterpret_cast<const uint32_t*>(pw + g * kTile + b * 16 + 2u * t4);
+      const uint32_t pb1 = *reinterpret_cast<const uint32_t*>(pw + g * kTile + b * 16 + 2u * t4 + 8u);
+#pragma unroll
+      for (int mt = 0; mt < 16; ++mt) {
+        uint32_t a0, a1, a2, a3;
+        const uint32_t mi = static_cast<uint32_t>(lane) >> 3, rr = static_cast<uint32_t>(lane) & 7u;
+        const uint32_t prow = b * 16 + rr + ((mi >> 1) << 3), dcol = mt * 16 + (mi & 1u) * 8;
+        ldsm_x4_t(vst + prow * kRowBytes + dcol * 2, a0, a1, a2, a3);
+        mma_f16(o[mt], a0, a1, a2, a3, pb0, pb1);
+      }
     }
     __syncwarp();
     if (tile + kStages < ntiles) issue(tile + kStages);
   }
 
-  // ---- combine the four warps of this CTA through shared memory ----------
+  // ---- combine the warps of this CTA through shared memory ----------------
   const size_t rec = (static_cast<size_t>(z) * p.kvh + kv) * gridDim.x + split;  // record index
   if (__syncthreads_or(failed ? 1 : 0)) {
     // A stage never arrived: publish an empty record (the host sees the
-    // timeout bit).  The warp that gave up still owns the copies it issued
-    // and has not consumed (tiles failed_tile, +kWarps, ... below
-    // failed_tile + kStages): wait for them once more, boundedly, so that no
-    // bulk copy lands in shared memory after this CTA has left the SM.
-    if (failed && lane == 0)
-      for (uint32_t u = failed_tile; u < ntiles && u < failed_tile + kStages; u += kWarps)
-        (void)mbar_wait(&bars[u % kStages], (u / kStages) & 1u, nullptr);
-    __syncwarp();
+    // timeout bit).  Copies issued into the ring and not consumed may still be
+    // in flight: wait once more, boundedly, for the last copy into every stage,
+    // so that no bulk copy lands in shared memory after this CTA has left the SM.
+    if (threadIdx.x == 0)
+      for (int s2 = 0; s2 < kStages; ++s2) {
+        const uint32_t n_issued = issued[s2];
+        if (n_issued) (void)mbar_wait(&bars[s2], (n_issued - 1u) & 1u, nullptr);
+      }
+    __syncthreads();
     for (uint32_t i = threadIdx.x; i < kGroup * kHD; i += kThreads) {
       p.part_o[(rec * kGroup + i / kHD) * kHD + i % kHD] = 0.f;
       if (i % kHD == 0) {
@@ -295,13 +356,13 @@ __global__ void __launch_bounds__(kThreads) attention_split_kernel(const AttnPar
     float zs = 0.f, os = 0.f;
     if (m != -INFINITY)
       for (int w = 0; w < kWarps; ++w) {
-        const float e = cm[w * 4 + h] == -INFINITY ? 0.f : expf(cm[w * 4 + h] - m);
+        const float e = cm[w * 4 + h] == -INFINITY ? 0.f : exp2f(cm[w * 4 + h] - m);
         zs += cz[w * 4 + h] * e;
         os += (co[(w * 8 + h) * kHD + d] + co[(w * 8 + 4 + h) * kHD + d]) * e;
       }
     p.part_o[(rec * kGroup + h) * kHD + d] = os;
     if (d == 0) {
-      p.part_m[rec * kGroup + h] = m;
+      p.part_m[rec * kGroup + h] = m * (1.0f / kLog2e);  // natural units, as the merge expects
       p.part_z[rec * kGroup + h] = zs;
     }
   }
@@ -515,13 +576,19 @@ __global__ void __launch_bounds__(kThreads) attention_packet_split_kernel(const 
 
 // Merge the split records of every (sequence, head): m = max m_s,
 // Z = sum Z_s e^(m_s-m), U = sum U_s e^(m_s-m), out = U/max(Z,1e-30)*gate.
-// The split maxima and the weights e^(m_s-m) are formed once per CTA (one
-// split per thread), so only the value rows are walked per output dimension,
-// with several loads in flight.
+// Every load goes out in one round: each thread's split maxima and sums, and
+// each warp's first kMergeRows value rows (warp w takes splits w, w+8, ...;
+// lane l holds dimensions 8l..8l+7); the weights e^(m_s-m) follow once the
+// maxima are in, and the eight warps' partial rows are added in warp order.
+// Launched with programmatic dependent launch: its CTAs are resident and
+// waiting when the split grid finishes.
 constexpr uint32_t kMaxMergeSplits = 1024;
+constexpr uint32_t kMergeWarps = kHD / 32u;
+constexpr uint32_t kMergeRows = 8;  // value rows per warp requested before the weights are known
 __global__ void __launch_bounds__(kHD) attention_merge_kernel(const AttnParams p, uint32_t nsplit) {
   __shared__ float es[kMaxMergeSplits];
-  __shared__ float red[kHD / 32];
+  __shared__ float red[kMergeWarps];
+  __shared__ __align__(16) float rows[kMergeWarps][kHD];
   pdl_wait();
   pdl_launch_dependents();
   const uint32_t head = blockIdx.x, z = blockIdx.y, d = threadIdx.x;
@@ -534,11 +601,30 @@ __global__ void __launch_bounds__(kHD) attention_merge_kernel(const AttnParams p
     window(p, z, t, lo, n);
     nsplit = used_splits(p, n, nsplit);
   }
-  float mloc = -INFINITY;
-  for (uint32_t s = d; s < nsplit; s += kHD) {
-    const float ms = p.part_m[(rec0 + s) * kGroup + h];
-    es[s] = ms;
-    mloc = fmaxf(mloc, ms);
+  constexpr uint32_t kOwn = kMaxMergeSplits / kHD;
+  float mloc = -INFINITY, zown[kOwn];
+#pragma unroll
+  for (uint32_t i = 0; i < kOwn; ++i) {
+    const uint32_t s = d + i * kHD;
+    zown[i] = 0.f;
+    if (s < nsplit) {
+      const float ms = p.part_m[(rec0 + s) * kGroup + h];
+      zown[i] = p.part_z[(rec0 + s) * kGroup + h];
+      es[s] = ms;
+      mloc = fmaxf(mloc, ms);
+    }
+  }
+  const float* po = p.part_o + (rec0 * kGroup + h) * kHD + 8u * lane;
+  constexpr size_t kRecStride = static_cast<size_t>(kGroup) * kHD;  // floats between two splits' rows
+  float4 va[kMergeRows], vb[kMergeRows];
+#pragma unroll
+  for (uint32_t j = 0; j < kMergeRows; ++j) {
+    const uint32_t s = warp + j * kMergeWarps;
+    va[j] = vb[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (s < nsplit) {
+      va[j] = *reinterpret_cast<const float4*>(po + s * kRecStride);
+      vb[j] = *reinterpret_cast<const float4*>(po + s * kRecStride + 4u);
+    }
   }
 #pragma unroll
   for (int o = 16; o >= 1; o >>= 1) mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, o));
@@ -546,30 +632,53 @@ __global__ void __launch_bounds__(kHD) attention_merge_kernel(const AttnParams p
   __syncthreads();
   float m = red[0];
 #pragma unroll
-  for (uint32_t w = 1; w < kHD / 32u; ++w) m = fmaxf(m, red[w]);
+  for (uint32_t w = 1; w < kMergeWarps; ++w) m = fmaxf(m, red[w]);
   if (run == 0u) return;
   float zloc = 0.f;
-  for (uint32_t s = d; s < nsplit; s += kHD) {  // this thread's own entries of es
-    const float ms = es[s];
-    const float e = (ms == -INFINITY || m == -INFINITY) ? 0.f : expf(ms - m);
-    es[s] = e;
-    if (e != 0.f) zloc += p.part_z[(rec0 + s) * kGroup + h] * e;
+#pragma unroll
+  for (uint32_t i = 0; i < kOwn; ++i) {  // this thread's own entries of es
+    const uint32_t s = d + i * kHD;
+    if (s < nsplit) {
+      const float ms = es[s];
+      const float e = (ms == -INFINITY || m == -INFINITY) ? 0.f : expf(ms - m);
+      es[s] = e;
+      if (e != 0.f) zloc += zown[i] * e;
+    }
   }
 #pragma unroll
   for (int o = 16; o >= 1; o >>= 1) zloc += __shfl_xor_sync(0xffffffffu, zloc, o);
   __syncthreads();  // maxima read by every thread before red is reused; weights visible
   if (lane == 0) red[warp] = zloc;
-  __syncthreads();
-  float zs = 0.f;
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  auto add_row = [&](const float4& a, const float4& b, float e) {
+    if (e != 0.f) {
+      acc[0] += a.x * e;
+      acc[1] += a.y * e;
+      acc[2] += a.z * e;
+      acc[3] += a.w * e;
+      acc[4] += b.x * e;
+      acc[5] += b.y * e;
+      acc[6] += b.z * e;
+      acc[7] += b.w * e;
+    }
+  };
 #pragma unroll
-  for (uint32_t w = 0; w < kHD / 32u; ++w) zs += red[w];
-  float os = 0.f;
-  const float* po = p.part_o + (rec0 * kGroup + h) * kHD + d;
-#pragma unroll 8
-  for (uint32_t s = 0; s < nsplit; ++s) {  // every record below nsplit is written (empty ones as zeros)
-    const float e = es[s];
-    const float ov = po[static_cast<size_t>(s) * kGroup * kHD];  // unconditional: the loads go out together
-    os += e != 0.f ? ov * e : 0.f;
+  for (uint32_t j = 0; j < kMergeRows; ++j) {
+    const uint32_t s = warp + j * kMergeWarps;
+    if (s < nsplit) add_row(va[j], vb[j], es[s]);
+  }
+#pragma unroll 4
+  for (uint32_t s = warp + kMergeRows * kMergeWarps; s < nsplit; s += kMergeWarps)  // long split lists
+    add_row(*reinterpret_cast<const float4*>(po + s * kRecStride),
+            *reinterpret_cast<const float4*>(po + s * kRecStride + 4u), es[s]);
+  *reinterpret_cast<float4*>(&rows[warp][8u * lane]) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+  *reinterpret_cast<float4*>(&rows[warp][8u * lane + 4u]) = make_float4(acc[4], acc[5], acc[6], acc[7]);
+  __syncthreads();
+  float zs = 0.f, os = 0.f;
+#pragma unroll
+  for (uint32_t w = 0; w < kMergeWarps; ++w) {
+    zs += red[w];
+    os += rows[w][d];
   }
   float v = os / fmaxf(zs, 1e-30f);
   if (p.gate) v *= detector_sigmoid(p.gate[static_cast<size_t>(z) * p.gate_seq_stride + static_cast<size_t>(head) * kHD + d]);
@@ -585,7 +694,9 @@ __global__ void __launch_bounds__(kHD) attention_merge_kernel(const AttnParams p
 
 }  // namespace
 
-size_t attention_smem_bytes(int stages) { return stages * kStageBytes + 128 + kWarps * 8 * kTile * 2; }
+size_t attention_smem_bytes(int stages, int warps, int tile) {
+  return static_cast<size_t>(stages) * 2 * tile * kRowBytes + 256 + warps * 8 * tile * 2;
+}
 
 cudaError_t launch_attention_merge(const AttnParams& p, uint32_t nsplit, uint32_t nseq, bool pdl, cudaStream_t s) {
   cudaLaunchAttribute attr[1];
@@ -604,6 +715,7 @@ cudaError_t launch_attention(const AttnParams& p, uint32_t nsplit, uint32_t nseq
   if (p.hd != kHD || p.heads != p.kvh * kGroup || !p.q || !p.out || !p.part_m || !p.part_z || !p.part_o ||
       nsplit == 0 || nsplit > kMaxMergeSplits || nseq == 0 || p.capacity == 0)
     return cudaErrorInvalidValue;
+  if (reinterpret_cast<uintptr_t>(p.part_o) % 16u) return cudaErrorMisalignedAddress;  // the merge reads float4 rows
   if (p.packets) {  // the reference's packet history
     if (p.packet_stride != packet_bytes(p.kvh) || p.packet_stride % 8 || p.packet_seq_stride % 8 ||
         reinterpret_cast<uintptr_t>(p.packets) % 8)
@@ -619,7 +731,7 @@ cudaError_t launch_attention(const AttnParams& p, uint32_t nsplit, uint32_t nseq
     cfg.numAttrs = 1;
     const cudaError_t e = cudaLaunchKernelEx(&cfg, attention_packet_split_kernel, p);
     if (e != cudaSuccess) return e;
-    return launch_attention_merge(p, nsplit, nseq, pdl, s);
+    return launch_attention_merge(p, nsplit, nseq, true, s);
   }
   if (!p.k || !p.v) return cudaErrorInvalidValue;
   if (reinterpret_cast<uintptr_t>(p.k) % 16 || reinterpret_cast<uintptr_t>(p.v) % 16 || p.pos_stride % 8 ||
@@ -641,11 +753,13 @@ cudaError_t launch_attention(const AttnParams& p, uint32_t nsplit, uint32_t nseq
     std::lock_guard<std::mutex> lock(setup_mutex);
     sms = sms_of[dev].load(std::memory_order_relaxed);
     if (sms == 0) {
-      e = cudaFuncSetAttribute(attention_split_kernel<kStages>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(attention_smem_bytes(kStages)));
+      e = cudaFuncSetAttribute(attention_split_kernel<kWarpsOne, kStages, kTileOne>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(attention_smem_bytes(kStages, kWarpsOne, kTileOne)));
       if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(attention_split_kernel<kStagesMany>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(attention_smem_bytes(kStagesMany)));
+        e = cudaFuncSetAttribute(attention_split_kernel<kWarps, kStagesMany, kTileMany>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(attention_smem_bytes(kStagesMany, kWarps, kTileMany)));
       if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
       if (e != cudaSuccess) return e;
       if (sms <= 0) return cudaErrorInvalidDevice;
@@ -653,21 +767,22 @@ cudaError_t launch_attention(const AttnParams& p, uint32_t nsplit, uint32_t nseq
     }
   }
   const bool many = static_cast<uint64_t>(nsplit) * p.kvh * nseq > static_cast<uint64_t>(sms);
-  const size_t smem = attention_smem_bytes(many ? kStagesMany : kStages);
+  const size_t smem = many ? attention_smem_bytes(kStagesMany, kWarps, kTileMany)
+                            : attention_smem_bytes(kStages, kWarpsOne, kTileOne);
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(nsplit, p.kvh, nseq);
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(many ? kThreads : kWarpsOne * 32);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = many ? cudaLaunchKernelEx(&cfg, attention_split_kernel<kStagesMany>, p)
-           : cudaLaunchKernelEx(&cfg, attention_split_kernel<kStages>, p);
+  e = many ? cudaLaunchKernelEx(&cfg, attention_split_kernel<kWarps, kStagesMany, kTileMany>, p)
+           : cudaLaunchKernelEx(&cfg, attention_split_kernel<kWarpsOne, kStages, kTileOne>, p);
   if (e != cudaSuccess) return e;
-  return launch_attention_merge(p, nsplit, nseq, pdl, s);
+  return launch_attention_merge(p, nsplit, nseq, true, s);  // resident early, waits for the split grid
 }
 
 uint32_t attention_default_splits(uint32_t history, uint32_t kvh, int sms) {

@@ -48,7 +48,7 @@ struct AttnParams {
   uint32_t split_by_length = 0;
 };
 
-size_t attention_smem_bytes(int stages);
+size_t attention_smem_bytes(int stages, int warps, int tile);
 cudaError_t launch_attention(const AttnParams& p, uint32_t nsplit, uint32_t nseq, bool pdl, cudaStream_t s);
 uint32_t attention_default_splits(uint32_t history, uint32_t kvh, int sms);
 

@@ -367,7 +367,9 @@ rta_status rta_attention_decode_f16(const float* q, const void* k, const void* v
   p.out_seq_stride = static_cast<size_t>(heads) * head_dim;
   p.phys = phys;
   p.err = reinterpret_cast<uint32_t*>(ws);
-  p.part_m = reinterpret_cast<float*>(ws + kErrBytes);
+  // split records from the first 16-byte boundary past the error word (the
+  // workspace size carries 64 bytes of slack): the merge reads float4 rows
+  p.part_m = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(ws + kErrBytes) + 15u) & ~uintptr_t{15});
   p.part_z = p.part_m + recs;
   p.part_o = p.part_z + recs;
   cudaStream_t s = as_stream(stream);

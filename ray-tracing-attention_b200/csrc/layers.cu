@@ -251,6 +251,7 @@ __global__ void __launch_bounds__(256) attn_prep_kernel(PrepParams p) {
 // griddepcontrol.wait, into registers, and the block reductions carry several
 // values per barrier.
 constexpr uint32_t kGdnRowsSmall = 16;
+constexpr uint32_t kGdnPersistentUnits = 64;  // (head, sequence) units from which gdn_batch_kernel runs
 
 __device__ __forceinline__ float signed_product_sum(float a0, float a1, float a2, float a3, float b0, float b1,
                                                     float b2, float b3) {
@@ -938,7 +939,11 @@ cudaError_t launch_gdn(const GdnParams& p, cudaStream_t s, bool pdl) {
   void* args[] = {const_cast<GdnParams*>(&p)};
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  if (p.H * p.nseq >= 2u * static_cast<uint32_t>(sms)) {  // enough (head, sequence) units for every SM
+  // From 64 (head, sequence) units on, one persistent CTA per SM walks them: the
+  // 16-row CTAs re-read the gate rows, the norm weight and the hidden row in all
+  // eight slices of a head (64 KB each at the 9B shape: 134 MB of L2 reads per
+  // layer at 8 sequences), and below one unit per SM the empty CTAs just leave.
+  if (p.H * p.nseq >= kGdnPersistentUnits) {
     // bulk copies of whole states: 16-byte aligned, and each state row block contiguous
     if ((reinterpret_cast<uintptr_t>(p.rec) % 16u) || (p.rec_seq * 4u) % 16u || (reinterpret_cast<uintptr_t>(p.conv_w) % 16u))
       return cudaErrorMisalignedAddress;

@@ -4,10 +4,10 @@ ray_tracing/native/shaders/resident_math.comp:131-148).
 
 Both head layouts of the benchmark shapes are covered: 16 state heads over 16
 key heads at hidden 2048 (2B) and 32 state heads over 16 key heads at hidden
-4096 (9B), at batch 1 (16-row CTAs, eight per head) and at batches that fill
-the GPU with (head, sequence) units (one persistent CTA per SM walking a range
-of units, whole states staged by bulk copies; at 40 sequences the ranges cross
-head boundaries).  Three
+4096 (9B), at batch 1 (16-row CTAs, eight per head) and at batches of 64
+(head, sequence) units and more (one persistent CTA per SM walking a range of
+units, whole states staged by bulk copies; fewer units than SMs leave CTAs
+without work; at 40 sequences the ranges cross head boundaries).  Three
 consecutive positions run, so both conv-history buffers are read and written.
 Bars: detector output and recurrent state within 1e-3 relative L2 of the oracle
 after every step; the rolled convolution taps are copies and must be exact.
@@ -37,7 +37,7 @@ def _inputs(rng, B, D, H, KH):
 
 
 @pytest.mark.parametrize("D,H,KH,B", [(2048, 16, 16, 1), (4096, 32, 16, 1), (4096, 32, 16, 16), (2048, 16, 16, 24),
-                                     (4096, 32, 16, 40)])
+                                     (4096, 32, 16, 40), (4096, 32, 16, 2), (4096, 32, 16, 8), (2048, 16, 16, 4)])
 def test_gated_delta_matches_oracle(D, H, KH, B):
     import torch
     from rta_b200 import ops
