@@ -622,7 +622,7 @@ __global__ void __launch_bounds__(256, 1) gdn_batch_kernel(GdnParams p) {
           }
         const float* sst = gst + stage * kGdnStateFloats;
         float* st = p.rec + z * p.rec_seq + static_cast<size_t>(h) * HD * HD;
-#pragma unroll 1
+#pragma unroll  // the four passes' chains interleave (255 registers, no spills; 82.2 -> 79.8 us per 9B layer)
         for (uint32_t pass = 0; pass < 4u; ++pass) {
           const uint32_t r = warp * 16u + 4u * pass + grp;
           float s[16];
