@@ -192,16 +192,18 @@ __global__ void __launch_bounds__(WARPS * 32) attention_split_kernel(const AttnP
       // Wait (boundedly) until this tile's copy has been issued, then for its
       // phase.  With one stage per warp the warp itself orders the phases.
       const uint32_t need = tile / kStages + 1u;
-      const uint64_t start = globaltimer();
-      for (uint32_t spin = 0; *reinterpret_cast<volatile uint32_t*>(&issued[s]) < need; ++spin) {
-        if ((spin & 63u) == 63u && globaltimer() - start > RTA_WAIT_NS) {
-          if (p.err) atomicOr(p.err, RTA_DEVERR_TIMEOUT);
-          failed = true;
-          break;
+      if (*reinterpret_cast<volatile uint32_t*>(&issued[s]) < need) {  // rare: the clock is read only here
+        const uint64_t start = globaltimer();
+        for (uint32_t spin = 0; *reinterpret_cast<volatile uint32_t*>(&issued[s]) < need; ++spin) {
+          if ((spin & 63u) == 63u && globaltimer() - start > RTA_WAIT_NS) {
+            if (p.err) atomicOr(p.err, RTA_DEVERR_TIMEOUT);
+            failed = true;
+            break;
+          }
+          __nanosleep(32);
         }
-        __nanosleep(32);
+        if (failed) break;
       }
-      if (failed) break;
     }
     if (!mbar_wait(&bars[s], (tile / kStages) & 1u, p.err)) {
       failed = true;
