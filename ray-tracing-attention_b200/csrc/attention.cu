@@ -579,18 +579,21 @@ __global__ void __launch_bounds__(kThreads) attention_packet_split_kernel(const 
 // Merge the split records of every (sequence, head): m = max m_s,
 // Z = sum Z_s e^(m_s-m), U = sum U_s e^(m_s-m), out = U/max(Z,1e-30)*gate.
 // Every load goes out in one round: each thread's split maxima and sums, and
-// each warp's first kMergeRows value rows (warp w takes splits w, w+8, ...;
-// lane l holds dimensions 8l..8l+7); the weights e^(m_s-m) follow once the
-// maxima are in, and the eight warps' partial rows are added in warp order.
+// the value rows -- with at most eight splits (many sequences) each thread
+// takes its own dimension of every row; with more (one long history) warp w
+// takes splits w, w+8, ... (its first kMergeRows of them at once; lane l holds
+// dimensions 8l..8l+7) and the eight warps' partial rows are added in warp
+// order.  The weights e^(m_s-m) follow once the maxima are in.
 // Launched with programmatic dependent launch: its CTAs are resident and
 // waiting when the split grid finishes.
 constexpr uint32_t kMaxMergeSplits = 1024;
 constexpr uint32_t kMergeWarps = kHD / 32u;
 constexpr uint32_t kMergeRows = 8;  // value rows per warp requested before the weights are known
+template <bool FEW>  // FEW: at most kMergeWarps splits in the launch (the path is fixed at compile time: registers)
 __global__ void __launch_bounds__(kHD) attention_merge_kernel(const AttnParams p, uint32_t nsplit) {
   __shared__ float es[kMaxMergeSplits];
   __shared__ float red[kMergeWarps];
-  __shared__ __align__(16) float rows[kMergeWarps][kHD];
+  __shared__ __align__(16) float rows[FEW ? 1 : kMergeWarps][kHD];
   pdl_wait();
   pdl_launch_dependents();
   const uint32_t head = blockIdx.x, z = blockIdx.y, d = threadIdx.x;
@@ -618,14 +621,21 @@ __global__ void __launch_bounds__(kHD) attention_merge_kernel(const AttnParams p
   }
   const float* po = p.part_o + (rec0 * kGroup + h) * kHD + 8u * lane;
   constexpr size_t kRecStride = static_cast<size_t>(kGroup) * kHD;  // floats between two splits' rows
-  float4 va[kMergeRows], vb[kMergeRows];
+  float ov[FEW ? kMergeWarps : 1];                         // few splits: dimension d of every row
+  float4 va[FEW ? 1 : kMergeRows], vb[FEW ? 1 : kMergeRows];  // otherwise: this warp's first rows
+  if constexpr (FEW) {
+    const float* pd = p.part_o + (rec0 * kGroup + h) * kHD + d;
 #pragma unroll
-  for (uint32_t j = 0; j < kMergeRows; ++j) {
-    const uint32_t s = warp + j * kMergeWarps;
-    va[j] = vb[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (s < nsplit) {
-      va[j] = *reinterpret_cast<const float4*>(po + s * kRecStride);
-      vb[j] = *reinterpret_cast<const float4*>(po + s * kRecStride + 4u);
+    for (uint32_t j = 0; j < kMergeWarps; ++j) ov[j] = j < nsplit ? pd[j * kRecStride] : 0.f;
+  } else {
+#pragma unroll
+    for (uint32_t j = 0; j < (FEW ? 1u : kMergeRows); ++j) {
+      const uint32_t s = warp + j * kMergeWarps;
+      va[j] = vb[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (s < nsplit) {
+        va[j] = *reinterpret_cast<const float4*>(po + s * kRecStride);
+        vb[j] = *reinterpret_cast<const float4*>(po + s * kRecStride + 4u);
+      }
     }
   }
 #pragma unroll
@@ -651,37 +661,44 @@ __global__ void __launch_bounds__(kHD) attention_merge_kernel(const AttnParams p
   for (int o = 16; o >= 1; o >>= 1) zloc += __shfl_xor_sync(0xffffffffu, zloc, o);
   __syncthreads();  // maxima read by every thread before red is reused; weights visible
   if (lane == 0) red[warp] = zloc;
-  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  auto add_row = [&](const float4& a, const float4& b, float e) {
-    if (e != 0.f) {
-      acc[0] += a.x * e;
-      acc[1] += a.y * e;
-      acc[2] += a.z * e;
-      acc[3] += a.w * e;
-      acc[4] += b.x * e;
-      acc[5] += b.y * e;
-      acc[6] += b.z * e;
-      acc[7] += b.w * e;
+  float os = 0.f;
+  if constexpr (FEW) {
+#pragma unroll
+    for (uint32_t j = 0; j < kMergeWarps; ++j)
+      if (j < nsplit && es[j] != 0.f) os += ov[j] * es[j];
+    __syncthreads();  // the sums in red
+  } else {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    auto add_row = [&](const float4& a, const float4& b, float e) {
+      if (e != 0.f) {
+        acc[0] += a.x * e;
+        acc[1] += a.y * e;
+        acc[2] += a.z * e;
+        acc[3] += a.w * e;
+        acc[4] += b.x * e;
+        acc[5] += b.y * e;
+        acc[6] += b.z * e;
+        acc[7] += b.w * e;
+      }
+    };
+#pragma unroll
+    for (uint32_t j = 0; j < (FEW ? 1u : kMergeRows); ++j) {
+      const uint32_t s = warp + j * kMergeWarps;
+      if (s < nsplit) add_row(va[j], vb[j], es[s]);
     }
-  };
-#pragma unroll
-  for (uint32_t j = 0; j < kMergeRows; ++j) {
-    const uint32_t s = warp + j * kMergeWarps;
-    if (s < nsplit) add_row(va[j], vb[j], es[s]);
-  }
 #pragma unroll 4
-  for (uint32_t s = warp + kMergeRows * kMergeWarps; s < nsplit; s += kMergeWarps)  // long split lists
-    add_row(*reinterpret_cast<const float4*>(po + s * kRecStride),
-            *reinterpret_cast<const float4*>(po + s * kRecStride + 4u), es[s]);
-  *reinterpret_cast<float4*>(&rows[warp][8u * lane]) = make_float4(acc[0], acc[1], acc[2], acc[3]);
-  *reinterpret_cast<float4*>(&rows[warp][8u * lane + 4u]) = make_float4(acc[4], acc[5], acc[6], acc[7]);
-  __syncthreads();
-  float zs = 0.f, os = 0.f;
+    for (uint32_t s = warp + (FEW ? 1u : kMergeRows) * kMergeWarps; s < nsplit; s += kMergeWarps)  // long lists
+      add_row(*reinterpret_cast<const float4*>(po + s * kRecStride),
+              *reinterpret_cast<const float4*>(po + s * kRecStride + 4u), es[s]);
+    *reinterpret_cast<float4*>(&rows[FEW ? 0 : warp][8u * lane]) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    *reinterpret_cast<float4*>(&rows[FEW ? 0 : warp][8u * lane + 4u]) = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    __syncthreads();
 #pragma unroll
-  for (uint32_t w = 0; w < kMergeWarps; ++w) {
-    zs += red[w];
-    os += rows[w][d];
+    for (uint32_t w = 0; w < (FEW ? 1u : kMergeWarps); ++w) os += rows[w][d];
   }
+  float zs = 0.f;
+#pragma unroll
+  for (uint32_t w = 0; w < kMergeWarps; ++w) zs += red[w];
   float v = os / fmaxf(zs, 1e-30f);
   if (p.gate) v *= detector_sigmoid(p.gate[static_cast<size_t>(z) * p.gate_seq_stride + static_cast<size_t>(head) * kHD + d]);
   uint32_t od = d;
@@ -710,7 +727,8 @@ cudaError_t launch_attention_merge(const AttnParams& p, uint32_t nsplit, uint32_
   cfg.stream = s;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, attention_merge_kernel, p, nsplit);
+  return nsplit <= kMergeWarps ? cudaLaunchKernelEx(&cfg, attention_merge_kernel<true>, p, nsplit)
+                               : cudaLaunchKernelEx(&cfg, attention_merge_kernel<false>, p, nsplit);
 }
 
 cudaError_t launch_attention(const AttnParams& p, uint32_t nsplit, uint32_t nseq, bool pdl, cudaStream_t s) {
