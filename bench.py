@@ -769,7 +769,17 @@ def run_ragged(args, world, rank, local):
     shards = sharding.shard_sequences(lengths, world)
     mine = lengths[shards[rank]]
     capacity = (int(lengths.max()) + 256 + 255) // 256 * 256
-    tp = world > 1 and not args.no_tp
+    # N > 1: sequence sharding while every rank keeps 16+ sequences (all its
+    # products on the tensor cores, no exchange: 12215 vs 11520 tokens/s for the
+    # hybrid at N = 2), the hybrid below that (8 sequences per rank: the hybrid
+    # 11489, sequence sharding 7401 at N = 8, where sharded ranks fall to the
+    # batched GEMV over the full weights); --tp / --no-tp force one or the other
+    if args.tp:
+        tp = world > 1
+    elif args.no_tp:
+        tp = False
+    else:
+        tp = world > 1 and min(len(sh) for sh in shards) < 16
     team = None
     if tp:
         # hybrid: every rank keeps the residual rows of all 64 sequences (its shard
@@ -1285,6 +1295,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-tp", action="store_true",
                     help="ragged9b at N > 1: shard by sequence only (weights replicated, no exchanges)")
+    ap.add_argument("--tp", action="store_true",
+                    help="ragged9b at N > 1: the tensor-parallel hybrid whatever the sequences per rank "
+                         "(default: the hybrid only below 16 sequences per rank)")
     ap.add_argument("--no-other-configs", action="store_true",
                     help="ragged9b at N=1: skip the compact lines of benchmark configs 1-4")
     ap.add_argument("--batch", type=int, default=1,
