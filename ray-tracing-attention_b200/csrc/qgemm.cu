@@ -34,13 +34,17 @@
 //     = qh bytes 128 + 32h + 16part .. +15; then scales [row 128][16 int8],
 //     then d [row 128][fp16].
 //
-// Work order: K slices as wide as the activation slots (4 block columns at
-// N = 64), within a slice every 128-row tile, within a tile the slice's block
-// columns.  One persistent CTA per SM (608 threads) takes an equal contiguous
-// range of that order (whole tiles when an argmax needs whole sums), so the
-// activations of a slice are copied into shared memory once per CTA and stay
-// there while the CTA walks the slice's tiles; a unit (one tile's run of block
-// columns) ends in a partial sum that lands atomically.
+// Work order: tile by tile, within a tile every block column (K slices of
+// `width` block columns are supported; every launch now takes the whole K).
+// One persistent CTA per SM (608 threads) takes an equal contiguous range of
+// that order (whole tiles when an argmax needs whole sums), and the
+// activation block columns stream through the slots (slot = block column %
+// slots, prefetched ahead of the MMAs); a unit (one tile's run of block
+// columns inside the range) ends in a partial sum that lands atomically, so a
+// CTA emits about 1 + tiles/CTAs partial sums.  (Slices as narrow as the slots,
+// with the activations resident while a CTA walks a slice's tiles, emitted 2-4x
+// more partial sums, 128 x N fp32 atomics each, and measured slower: 9007 vs
+// 9247 tokens/s in the 9B ragged decode.)
 //   warp 0      bulk-copies the range's weight panels, one per block column,
 //               from kernel start (weights do not depend on earlier kernels)
 //   warp 18     bulk-copies an activation block column into its slot (block
@@ -1100,11 +1104,10 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const uint32_t nmat = a.w1 ? 2u : 1u, ntiles = nmat * (a.rows / tc::kTileRows), KB = a.cols / 256u;
   // Work split.  Without an argmax every CTA takes an equal contiguous range of
-  // the panels in slice-major order (slices as wide as the activation slots,
-  // so the activations of a slice are copied once per CTA and stay resident
-  // while it walks the slice's tiles); partial sums land atomically (residual
-  // products add into y, stores into rows the prep kernel zeroes).  The argmax
-  // needs whole sums: whole tiles per CTA, activations streamed through the slots.
+  // the panels in tile-major order, activations streamed through the slots;
+  // partial sums land atomically (residual products add into y, stores into
+  // rows the prep kernel zeroes).  The argmax needs whole sums: whole tiles per
+  // CTA.
   const bool whole = a.argmax != nullptr || !a.y;
   const uint32_t total = ntiles * KB;
   const uint32_t grid = whole ? (ntiles < static_cast<uint32_t>(sms) ? ntiles : static_cast<uint32_t>(sms))
@@ -1144,7 +1147,7 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
     p.KB = a.cols / 256u;
     p.ntiles = ntiles;
     p.slots = 4u * 64u / pr.N;
-    p.width = whole ? KB : p.slots;
+    p.width = KB;
     p.total = total;
     p.whole_tiles = whole ? 1u : 0u;
     p.split = a.split ? 1u : 0u;
