@@ -29,6 +29,9 @@
 //    load sits inside a loop.
 #include "rta_internal.h"
 
+#include <atomic>
+#include <mutex>
+
 namespace rta {
 namespace {
 
@@ -1260,34 +1263,48 @@ cudaError_t launch_t(const GemvArgs& a, Params p, cudaStream_t s) {
   const uint32_t smem = smem_bytes<FMT, TILED>(a.cols, p.batch, &p);
   // One-time kernel setup and occupancy per (kernel instance, smem size): these
   // queries cost microseconds and must stay off the per-launch path
-  // (function attributes are per device: index the cache by device ordinal).
-  static int max_smem_set[64] = {0};
-  static uint32_t cached_smem[8] = {0};
-  static int cached_grid[8] = {0};
-  static int sms = 0;
+  // (function attributes are per device: index the flags by device ordinal).
+  // Host threads may make their first calls at the same time: the setup and
+  // the cache fills run under a lock, and each entry is published with release
+  // order (an SM count, or an occupancy after its shared-memory size), so the
+  // lock-free reads never see half an entry.
+  static std::mutex setup_mutex;
+  static std::atomic<int> sms_of[64];
+  static std::atomic<uint32_t> cached_smem[8];
+  static std::atomic<int> cached_grid[8];
   cudaError_t e = cudaSuccess;
   int dev = 0;
-  cudaGetDevice(&dev);
+  e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if (!max_smem_set[dev]) {
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    if (e != cudaSuccess) return e;
-    max_smem_set[dev] = 1;
+  int sms = sms_of[dev].load(std::memory_order_acquire);
+  if (sms == 0) {
+    std::lock_guard<std::mutex> lock(setup_mutex);
+    sms = sms_of[dev].load(std::memory_order_relaxed);
+    if (sms == 0) {
+      e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+      if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      if (e != cudaSuccess) return e;
+      if (sms <= 0) return cudaErrorInvalidDevice;
+      sms_of[dev].store(sms, std::memory_order_release);
+    }
   }
   if (smem > 227u * 1024u) return cudaErrorInvalidConfiguration;
   int per_sm = 0;
   for (int i = 0; i < 8; ++i)
-    if (cached_smem[i] == smem) per_sm = cached_grid[i];
+    if (cached_smem[i].load(std::memory_order_acquire) == smem) per_sm = cached_grid[i].load(std::memory_order_relaxed);
   if (per_sm == 0) {
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, smem);
     if (e != cudaSuccess) return e;
     if (per_sm < 1) return cudaErrorInvalidConfiguration;
-    for (int i = 0; i < 8; ++i)
-      if (cached_smem[i] == 0) {
-        cached_smem[i] = smem;
-        cached_grid[i] = per_sm;
-        break;
+    std::lock_guard<std::mutex> lock(setup_mutex);
+    bool held = false;
+    for (int i = 0; i < 8 && !held; ++i) held = cached_smem[i].load(std::memory_order_relaxed) == smem;
+    for (int i = 0; i < 8 && !held; ++i)
+      if (cached_smem[i].load(std::memory_order_relaxed) == 0) {
+        cached_grid[i].store(per_sm, std::memory_order_relaxed);
+        cached_smem[i].store(smem, std::memory_order_release);
+        held = true;
       }
   }
   const uint32_t tiles = a.rows / kTileRows;

@@ -64,8 +64,10 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 #include <cstring>
+#include <mutex>
 
 #include "rta_device.cuh"
 #include "rta_internal.h"
@@ -1029,15 +1031,21 @@ cudaError_t launch_n(const tc::Params& p0, const tc::Prep& pr, uint32_t grid, bo
   uint32_t smem = p.off_misc + 16u + 8u * static_cast<uint32_t>(N);
   smem = smem < tc::kMinSmem ? tc::kMinSmem : smem;
   auto kernel = tc::tc_gemm_kernel<FMT, N>;
-  static int attr_done[64] = {0};
+  // once per (kernel, device), under a lock: host threads may make their first
+  // calls at the same time; the flag is published with release order
+  static std::mutex attr_mutex;
+  static std::atomic<int> attr_done[64];
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if (!attr_done[dev]) {
-    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    if (e != cudaSuccess) return e;
-    attr_done[dev] = 1;
+  if (!attr_done[dev].load(std::memory_order_acquire)) {
+    std::lock_guard<std::mutex> lock(attr_mutex);
+    if (!attr_done[dev].load(std::memory_order_relaxed)) {
+      e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+      if (e != cudaSuccess) return e;
+      attr_done[dev].store(1, std::memory_order_release);
+    }
   }
   if (smem > 227u * 1024u) return cudaErrorInvalidConfiguration;
   cudaLaunchAttribute attr[1];
