@@ -750,6 +750,23 @@ def ragged_step_bytes(spec, layout, lengths, capacity, tp_world: int = 1, all_se
     return weights + emb + kv + rec
 
 
+def ragged_uses_hybrid(world: int, shard_sizes, force_tp: bool = False, force_no_tp: bool = False) -> bool:
+    """Config 5's multi-GPU mode: sequence sharding while every rank keeps 16 or
+    more sequences (all its products on the tensor cores, no exchange: 12215 vs
+    11520 tokens/s for the hybrid at N = 2, 14720 vs 13333 at N = 4), the
+    tensor-parallel hybrid below that (8 sequences per rank: the hybrid 11489,
+    sequence sharding 7401 at N = 8, where sharded ranks fall to the batched GEMV
+    over the full weights).  --tp / --no-tp force one or the other; one GPU never
+    takes the hybrid."""
+    if world <= 1:
+        return False
+    if force_tp:
+        return True
+    if force_no_tp:
+        return False
+    return min(shard_sizes) < 16
+
+
 def run_ragged(args, world, rank, local):
     """Config 5 on `world` GPUs: every rank decodes its shard of the 64 sequences;
     `value` = 64 tokens per step / the slowest rank's step time (CUDA events around
@@ -769,17 +786,7 @@ def run_ragged(args, world, rank, local):
     shards = sharding.shard_sequences(lengths, world)
     mine = lengths[shards[rank]]
     capacity = (int(lengths.max()) + 256 + 255) // 256 * 256
-    # N > 1: sequence sharding while every rank keeps 16+ sequences (all its
-    # products on the tensor cores, no exchange: 12215 vs 11520 tokens/s for the
-    # hybrid at N = 2), the hybrid below that (8 sequences per rank: the hybrid
-    # 11489, sequence sharding 7401 at N = 8, where sharded ranks fall to the
-    # batched GEMV over the full weights); --tp / --no-tp force one or the other
-    if args.tp:
-        tp = world > 1
-    elif args.no_tp:
-        tp = False
-    else:
-        tp = world > 1 and min(len(sh) for sh in shards) < 16
+    tp = ragged_uses_hybrid(world, [len(sh) for sh in shards], args.tp, args.no_tp)
     team = None
     if tp:
         # hybrid: every rank keeps the residual rows of all 64 sequences (its shard
