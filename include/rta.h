@@ -16,6 +16,10 @@
  *     (op 4), mlp (op 6), attention (op 14), resources (op 8), grow (op 10).
  *     Host buffers in, host buffers out; a handle is single-threaded.
  *
+ * Host threads may call the operators, and use different handles, at the same
+ * time: each kernel's one-time set-up on a device (shared-memory limits,
+ * occupancy) is synchronised, so first calls that arrive together are safe.
+ *
  * Every function returns an rta_status and never aborts the process.
  * Format codes are the exporter's (ray_tracing/compiler/export.py:12):
  * 0 F32, 1 F16, 30 BF16, 12 Q4_K, 14 Q6_K.
